@@ -1,0 +1,450 @@
+#!/usr/bin/env python
+"""Benchmark of the SSD chunked-scan forward (and the decode state update) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1|c2|c4]
+
+One JSON line on stdout (rank 0). A "step" is one SSD forward over one batch of
+the workload (default: BASELINE config 1, 8 x 2048 tokens, H24 P64 N128 cs256,
+bf16 with D + z). Multi-GPU (torchrun, one process per GPU): every rank runs its
+own batch of the same shape from its own seed (the scan has no cross-row or
+cross-head exchange), so scaling is weak and ``value`` = all ranks' tokens / the
+slowest rank's device time.
+
+Timing: CUDA events on the launching stream around each step, L2 flushed
+(256 MiB write) between steps outside the events, barrier + synchronize on both
+sides of the timed loop, max over ranks. ``e2e`` repeats the measurement through
+the public op (``SSDScanFn``) with pinned host inputs copied in and ``y``/``h_last``
+copied out inside the timed region. ``--impl reference`` times the CPU
+restatement of the reference's five stages (``oracle/``) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+INF = float("inf")
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=["c1", "c2", "c4"], default="c1")
+    ap.add_argument("--kernel-impl", choices=["auto", "tc", "simt"], default="auto")
+    ap.add_argument("--no-ssu", action="store_true", help="skip the decode (config 3) measurement")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- distributed
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        backend = "nccl" if torch.cuda.is_available() and args.impl == "ours" else "gloo"
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the timed loop runs."""
+
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            bus = torch.cuda.get_device_properties(device_index).pci_bus_id
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", bus], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        self.t0 = self.t1 = None
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "note": "nvidia-smi unavailable"}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = []
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                ts = time.mktime(time.strptime(parts[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                rows.append((ts, float(parts[1]), float(parts[2]), parts[4:8]))
+            except ValueError:
+                continue
+        window = [r for r in rows if self.t0 is not None and self.t0 - 1 <= r[0] <= (self.t1 or r[0]) + 1] or rows
+        if not window:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        reasons = sorted({self.REASONS[i] for r in window for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[1] for r in window), "sm_max_mhz": max(r[2] for r in window),
+                "reasons": reasons, "samples": len(window)}
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_baseline(cfg, seconds: float, max_steps=None):
+    """Time the fp32 CPU restatement of the reference's five stages (oracle/ssd_ref.py)
+    on one batch row of the workload, repeated until ``seconds`` of work; returns
+    tokens/s with all host threads."""
+    from oracle import ssd_ref
+    from selective_attention_b200 import workloads
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rows = 1
+    seqlen = cfg.seqlen if not cfg.varlen else 4096
+    inp = workloads.make_ssd_inputs(cfg, seed=1, batch=rows, seqlen=seqlen, varlen=False)
+    f = lambda t: None if t is None else t.float()  # noqa: E731
+
+    def step():
+        y, h = ssd_ref.ssd_scan_forward(f(inp["u"]), inp["A"], f(inp["B"]), f(inp["C"]), inp["delta_raw"], None,
+                                        None, None, cfg.chunk)
+        ssd_ref.gate_epilogue(y, inp["u"], inp["D"], inp["z"])
+
+    step()  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if (max_steps and n >= max_steps) or (not max_steps and el >= seconds):
+            break
+    tok = n * rows * seqlen
+    return {"value": tok / el, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} x ({rows} row x {seqlen} tokens, H{cfg.nheads} P{cfg.headdim} N{cfg.dstate} "
+                      f"cs{cfg.chunk}) fp32 oracle stage-by-stage restatement, {el:.1f} s",
+            "cpu": _cpu_model()}
+
+
+def _cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def run_reference_arm(args, rank, world):
+    from selective_attention_b200 import workloads
+
+    cfg = workloads.CONFIGS[args.config]
+    if rank != 0:
+        return
+    # Size the per-step sample so W + K steps fit in about two minutes.
+    from oracle import ssd_ref  # noqa: F401  (import cost outside the timing)
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    probe = cpu_baseline(cfg, seconds=0.0, max_steps=1)
+    per_step_tokens_s = probe["value"]
+    seqlen = cfg.seqlen if not cfg.varlen else 4096
+    t_row = seqlen / per_step_tokens_s
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    heads = max(1, min(cfg.nheads, int(cfg.nheads * budget / max(t_row, 1e-9))))
+    sub = workloads.SSDConfig(**{**cfg.__dict__, "nheads": heads, "ngroups": 1 if cfg.ngroups < 2 else
+                                 max(1, min(cfg.ngroups, heads // max(1, cfg.nheads // cfg.ngroups)))})
+    res_w = cpu_baseline(sub, seconds=0.0, max_steps=max(1, args.warmup))
+    del res_w
+    t0 = time.perf_counter()
+    res = cpu_baseline(sub, seconds=0.0, max_steps=max(1, args.steps))
+    el = time.perf_counter() - t0
+    scale = heads / cfg.nheads  # a sampled token carries heads/H of a full token's work
+    value = res["value"] * scale
+    line = {
+        "impl": "reference", "metric": "SSD chunked-scan fwd tokens/s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * el / max(1, args.steps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{cfg.name} sampled on host cores", "heads_per_sample": heads},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": res["cores"], "kind": "port",
+                         "sample": res["sample"] + f"; scaled by {heads}/{cfg.nheads} heads",
+                         "cpu": res.get("cpu")},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def main():
+    args = parse()
+    rank, world, local = dist_setup(args)
+    try:
+        if args.impl == "reference":
+            run_reference_arm(args, rank, world)
+            return
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+def time_steps(fn, steps, flush_buf, stream):
+    """Sum of per-step CUDA-event durations (ms); L2 flushed before each step, untimed."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for s, e in evs:
+        flush_buf.fill_(1)
+        s.record(stream)
+        fn()
+        e.record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def run_ours(args, rank, world, local):
+    import selective_attention_b200 as sab
+    from selective_attention_b200 import kernels, workloads
+
+    dev = torch.device("cuda", local)
+    cfg = workloads.CONFIGS[args.config]
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except (OSError, ValueError):
+        pass
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+
+    inp = workloads.make_ssd_inputs(cfg, seed=1 + rank, device=dev, gen_device="cuda")
+    T = cfg.tokens
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    cu = inp["cu_seqlens"]
+    nseq = None if cu is None else cu.numel() - 1
+    y = torch.empty(cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, dtype=inp["u"].dtype, device=dev)
+    h_last = torch.empty(nseq or cfg.batch, cfg.nheads, cfg.headdim, cfg.dstate, dtype=torch.float32, device=dev)
+    p, keep, _ = kernels.ssd_scan_params(inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None, None,
+                                         cfg.chunk, True, (0.0, INF), inp["D"], inp["z"], cu, args.kernel_impl)
+    ws = torch.empty(kernels.workspace_size(p), dtype=torch.uint8, device=dev)
+    tc = kernels.uses_tensor_cores(p)
+    stage_ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for e in stage_ev:
+        e.record(stream)  # materialise the handles
+    ev_handles = [e.cuda_event for e in stage_ev]
+
+    def step(events=None):
+        kernels.ssd_scan_forward(inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None, None,
+                                 cfg.chunk, True, (0.0, INF), True, inp["D"], inp["z"], cu, args.kernel_impl,
+                                 out=(y, h_last), workspace=ws, events=events)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    sab.check_device_error(dev)
+
+    clocks = ClockSampler(local)
+    time.sleep(1.0)  # let the sampler start before the timed loop
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.mark_start()
+    per_step = time_steps(step, args.steps, flush, stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks.mark_end()
+    ms_total = max_over_ranks(sum(per_step), world)
+    ms_step = ms_total / args.steps
+    value = world * T / (ms_total / 1e3 / args.steps)
+
+    # per-stage times (separate pass, same flushing) for the roofline
+    n_stage = min(args.steps, 50)
+    st = [[0.0] * 5 for _ in range(n_stage)]
+    for i in range(n_stage):
+        flush.fill_(1)
+        step(events=ev_handles)
+        torch.cuda.synchronize()
+        for j in range(5):
+            st[i][j] = stage_ev[j].elapsed_time(stage_ev[j + 1])
+    stage_ms = [statistics.median(r[j] for r in st) for j in range(5)]
+    clk = clocks.stop()
+    sab.check_device_error(dev)
+
+    # algorithmic bytes of the dominant kernel (chunk_scan with bmm fused, D/z epilogue)
+    sx = inp["u"].element_size()
+    b, L, H, P, N, G = cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, cfg.dstate, cfg.ngroups
+    nck = (T + cfg.chunk - 1) // cfg.chunk + (nseq or 0) if cu is not None else b * math.ceil(L / cfg.chunk)
+    s_prev = 2 if tc else 4
+    scan_bytes = (T * H * P * (sx + sx + y.element_size()) + 2 * T * G * N * sx + 8 * T * H
+                  + s_prev * nck * H * P * N)
+    state_bytes = T * H * P * sx + T * G * N * sx + 8 * T * H + 4 * nck * H * P * N
+    pass_bytes = 4 * nck * H * P * N + s_prev * nck * H * P * N + 4 * (nseq or b) * H * P * N + 4 * nck * H
+    cums_bytes = 4 * T * H + 8 * nck * H * cfg.chunk
+    names = ["chunk_cumsum", "chunk_state", "state_passing", "bmm_chunk", "chunk_scan"]
+    bytes_ = [cums_bytes, state_bytes, pass_bytes, 0, scan_bytes]
+    stages = {}
+    for n_, ms_, by in zip(names, stage_ms, bytes_):
+        if n_ == "bmm_chunk" and tc:
+            continue
+        gbs = by / (ms_ / 1e3) / 1e9 if ms_ > 0 else None
+        stages[n_] = {"us": ms_ * 1e3, "alg_bytes": by, "gbs": gbs, "frac": (gbs / hbm_peak) if gbs else None}
+    dom = max(stages, key=lambda k: stages[k]["us"])
+    traffic = _traffic_from_profiles(dom, cfg.name)
+    roof = {"kernel": dom, "bound": "hbm", "achieved": stages[dom]["gbs"], "peak": hbm_peak, "unit": "GB/s",
+            "frac": stages[dom]["frac"], "traffic": traffic, "peak_source": peak_src,
+            "alg_bytes_per_launch": stages[dom]["alg_bytes"], "us_per_launch": stages[dom]["us"]}
+    fused_min = workloads.ssd_algorithmic_bytes(cfg, y_bytes=y.element_size(), nseq=nseq)
+    whole = {"alg_min_bytes": fused_min, "gbs": fused_min / (ms_step / 1e3) / 1e9,
+             "frac_of_fused_roof": fused_min / (ms_step / 1e3) / 1e9 / hbm_peak}
+
+    line = {
+        "metric": "SSD chunked-scan fwd tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if sx == 2 else "f32", "data": "synthetic",
+        "config": {"workload": _workload_name(cfg), "global_batch": cfg.batch * world, "seq_len": cfg.seqlen,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "path": "tcgen05" if tc else "cuda-core", "l2": "flushed between timed steps (256 MiB write)"},
+        "roofline": roof, "stages": stages, "whole_step": whole, "clocks": clk,
+        "gpu_launches": args.steps * ((4 if tc else 5) + (1 if cu is not None else 0)),
+    }
+    if not args.no_e2e:
+        line["e2e"] = e2e_measure(args, cfg, inp, dev, world, flush)
+    if not args.no_ssu:
+        line["ssu"] = ssu_measure(args, dev, flush, hbm_peak, world)
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def _workload_name(cfg):
+    extra = "+D" if cfg.D else ""
+    extra += "+z" if cfg.z else ""
+    shape = f"{cfg.tokens} packed tokens" if cfg.varlen else f"{cfg.batch}x{cfg.seqlen}"
+    return (f"{cfg.name}: SSD fwd {cfg.dtype} {shape} H{cfg.nheads} P{cfg.headdim} N{cfg.dstate} "
+            f"G{cfg.ngroups} cs{cfg.chunk} {extra}").strip()
+
+
+def _traffic_from_profiles(kernel, cfg_name):
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        d = json.load(open(path))
+        return d.get(cfg_name, {}).get(kernel)
+    except (OSError, ValueError):
+        return None
+
+
+def e2e_measure(args, cfg, inp, dev, world, flush):
+    """Same metric through SSDScanFn with pinned host inputs and outputs."""
+    import selective_attention_b200 as sab
+
+    names = ["u", "B", "C", "delta_raw", "z"]
+    host = {k: inp[k].cpu().pin_memory() for k in names if inp[k] is not None}
+    dev_in = {k: torch.empty_like(inp[k]) for k in host}
+    small = {k: inp[k] for k in ("A", "D")}
+    cu = inp["cu_seqlens"]
+    y_h = torch.empty(cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, dtype=inp["u"].dtype).pin_memory()
+    nrow = cfg.batch if cu is None else cu.numel() - 1
+    h_h = torch.empty(nrow, cfg.nheads, cfg.headdim, cfg.dstate, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for k, t in host.items():
+            dev_in[k].copy_(t, non_blocking=True)
+        y, h = sab.SSDScanFn.apply(dev_in["u"], small["A"], dev_in["B"], dev_in["C"], dev_in["delta_raw"], None,
+                                   None, None, cfg.chunk, True, (0.0, INF), True, small["D"], dev_in.get("z"), cu)
+        y_h.copy_(y, non_blocking=True)
+        h_h.copy_(h, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    steps = max(5, min(args.steps, 50))
+    barrier(world)
+    per = time_steps(step, steps, flush, stream)
+    barrier(world)
+    ms = max_over_ranks(sum(per), world) / steps
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = y_h.numel() * y_h.element_size() + h_h.numel() * h_h.element_size()
+    return {"value": world * cfg.tokens / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": ms, "steps": steps,
+            "note": "pinned host -> device inputs, SSDScanFn, device -> pinned host y and h_last, per step"}
+
+
+def ssu_measure(args, dev, flush, hbm_peak, world):
+    """Decode state update: achieved HBM GB/s on the algorithmic bytes."""
+    from selective_attention_b200 import kernels, workloads
+
+    cfg = workloads.SSU_CONFIGS["c3"]
+    inp = workloads.make_ssu_inputs(cfg, seed=2, device=dev, gen_device="cuda")
+    y = torch.empty_like(inp["u"])
+    h = inp["h"]
+
+    def step():
+        kernels.ssu_forward(inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], inp["delta_bias"], h, True,
+                            (0.0, INF), inp["D"], inp["z"], y=y)
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    steps = max(10, min(args.steps, 200))
+    per = time_steps(step, steps, flush, torch.cuda.current_stream(dev))
+    us = statistics.median(per) * 1e3
+    by = workloads.ssu_algorithmic_bytes(cfg)
+    gbs = by / (us / 1e6) / 1e9
+    return {"config": "c3: decode b256 H80 P64 N128 G1, fp32 state in place, bf16 x/B/C/z, D+z",
+            "us_per_step": us, "alg_bytes": by, "gbs": gbs, "peak_gbs": hbm_peak, "frac": gbs / hbm_peak,
+            "steps": steps, "timing": "median of per-step CUDA events, L2 flushed between steps"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+/*
+ * ssd_b200.h - C ABI of the B200 (sm_100a) SSD chunked-scan forward and the
+ * single-token selective state update (SSU).
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t
+ * (passed as void*), launches asynchronously on that stream and returns an
+ * ssd_status_t. Nothing here allocates device memory: the fused SSD forward
+ * takes a caller-provided workspace sized by ssd_scan_fwd_workspace_size().
+ * Tensors are dense row-major ("contiguous") in the shapes given below.
+ *
+ * Reference interfaces replaced (nmquan1503/selective-attention, paths under
+ * src/selective_attention/):
+ *   ssd_scan_fwd           <- triton_kernels/ssd_scan/forward.py:223 ssd_scan_forward
+ *                             (called from ops/ssd_scan.py:70 SSDScanFn.forward)
+ *   ssd_chunk_cumsum_fwd   <- triton_kernels/ssd_scan/forward.py:14  chunk_cumsum_forward
+ *   ssd_chunk_state_fwd    <- triton_kernels/ssd_scan/forward.py:62  chunk_state_forward
+ *   ssd_state_passing_fwd  <- triton_kernels/ssd_scan/forward.py:102 state_passing_forward
+ *   ssd_bmm_chunk_fwd      <- triton_kernels/ssd_scan/forward.py:139 bmm_chunk_forward
+ *   ssd_chunk_scan_fwd     <- triton_kernels/ssd_scan/forward.py:175 chunk_scan_forward
+ *   ssu_fwd                <- triton_kernels/ssu/forward.py:7 ssu_forward
+ *                             (called from ops/ssu.py:61 SSUFn.forward)
+ * The reference crosses host->device only at Triton launches; these functions are
+ * the same crossing for a C caller.
+ */
+#ifndef SSD_B200_H
+#define SSD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  SSD_OK = 0,
+  SSD_ERR_INVALID_ARGUMENT = 1, /* bad size, null pointer, unsupported combination */
+  SSD_ERR_UNSUPPORTED_DTYPE = 2,
+  SSD_ERR_WORKSPACE_TOO_SMALL = 3,
+  SSD_ERR_CUDA = 4,             /* a CUDA runtime call failed (launch, attribute, ...) */
+  SSD_ERR_DEVICE_TIMEOUT = 5,   /* a kernel gave up on a bounded wait (see ssd_b200_device_error) */
+  SSD_ERR_NO_TENSOR_MAP = 6     /* the driver's tensor-map encoder could not be obtained */
+} ssd_status_t;
+
+typedef enum { SSD_F32 = 0, SSD_BF16 = 1, SSD_F16 = 2 } ssd_dtype_t;
+
+typedef enum {
+  SSD_IMPL_AUTO = 0,   /* tensor-core path when the shape/dtype allow it, else CUDA-core path */
+  SSD_IMPL_TC = 1,     /* tcgen05 + TMA kernels (bf16/fp16, headdim 64, dstate 128, chunk 256) */
+  SSD_IMPL_SIMT = 2    /* CUDA-core FFMA kernels (any dtype; fp32-exact accumulation) */
+} ssd_impl_t;
+
+/*
+ * One parameter block for the SSD entry points. Fields an entry point does not
+ * use are ignored. Shapes (b = batch, L = seqlen, H = nheads, P = headdim,
+ * N = dstate, G = ngroups, cs = chunk_size, nc = ceil(L/cs)):
+ *
+ *   u          (b, L, H, P)   x_dtype          A          (H,)          fp32
+ *   B, C       (b, L, G, N)   x_dtype          delta_raw  (b, L, H)     dt_dtype
+ *   delta_bias (H,) fp32 or NULL               h_init     (b, H, P, N)  fp32 or NULL
+ *   length     (b,) int64 or NULL (= L)        D          (H*P,) fp32 or NULL
+ *   z          (b, L, H*P)    x_dtype or NULL  y          (b, L, H, P)  y_dtype
+ *   h_last     (b, H, P, N)   fp32
+ *
+ * Packed variable-length mode (an extension; the reference only has padded rows
+ * plus `length`): nseq > 0, b must be 1, L is the total token count and
+ * cu_seqlens holds nseq+1 offsets (int32 or int64 per cu_dtype). Each sequence is
+ * scanned as its own row with zero (or h_init[i]) initial state, exactly as the
+ * reference computes a right-padded row with length = seqlen; h_last and h_init are
+ * (nseq, H, P, N). `length` must be NULL in this mode.
+ *
+ * Stage buffers (chunk-major, k = b*nc + c in padded mode):
+ *   dt, cum    (b, nc, H, cs) fp32   -- the reference's (b, H, nc, cs) with H and nc swapped
+ *   states     (b, nc, H, P, N) fp32 -- same as the reference
+ *   CB         (b, nc, G, cs, cs) fp32 -- same as the reference
+ */
+typedef struct ssd_params {
+  int64_t batch, seqlen, nheads, headdim, dstate, ngroups, chunk_size;
+  int64_t nseq;
+  int32_t x_dtype, dt_dtype, y_dtype, cu_dtype; /* cu_dtype: 32 or 64 */
+  int32_t use_delta_softplus;
+  float delta_min, delta_max;
+  int32_t impl;
+  const void* u;
+  const float* A;
+  const void* B;
+  const void* C;
+  const void* delta_raw;
+  const float* delta_bias;
+  const float* h_init;
+  const int64_t* length;
+  const float* D;
+  const void* z;
+  const void* cu_seqlens;
+  void* y;
+  float* h_last;
+  float* dt;
+  float* cum;
+  float* states;
+  float* CB;
+  void* workspace;
+  size_t workspace_bytes;
+  /* Optional cudaEvent_t handles recorded on the stream by ssd_scan_fwd: [0] before
+     the first stage, then after chunk_cumsum [1], chunk_state [2], state_passing [3],
+     bmm_chunk [4] (same point as [3] when bmm is fused) and chunk_scan [5]. NULL
+     entries are skipped. */
+  void* events[6];
+} ssd_params;
+
+/* Library version string and the status text of a code. */
+const char* ssd_b200_version(void);
+const char* ssd_b200_status_string(int status);
+
+/*
+ * Device-side error flag: kernels set it (instead of trapping) when a bounded
+ * wait gives up. Synchronizes `stream`, returns the flag (0 = none) and clears it.
+ */
+int ssd_b200_device_error(void* stream);
+
+/* Whether `p` would take the tensor-core path under SSD_IMPL_AUTO (1) or not (0). */
+int ssd_scan_uses_tensor_cores(const ssd_params* p);
+
+/* Bytes of workspace ssd_scan_fwd needs for `p` (sizes, dtypes, impl, nseq). */
+size_t ssd_scan_fwd_workspace_size(const ssd_params* p);
+
+/*
+ * Fused SSD forward: chunk_cumsum -> chunk_state -> state_passing -> chunk_scan
+ * (bmm_chunk fused into chunk_scan on the tensor-core path), with the optional
+ * D-skip and z-gate epilogue y = (y + D*u) * silu(z) of modules/ssm.py:145-150.
+ * Writes y and h_last. Uses p->workspace (>= ssd_scan_fwd_workspace_size(p)).
+ */
+int ssd_scan_fwd(const ssd_params* p, void* stream);
+
+/* Stage entry points (padded mode only). Each reads/writes the stage buffers. */
+int ssd_chunk_cumsum_fwd(const ssd_params* p, void* stream);     /* -> dt, cum */
+int ssd_chunk_state_fwd(const ssd_params* p, void* stream);      /* u, B, dt, cum -> states */
+int ssd_state_passing_fwd(const ssd_params* p, void* stream);    /* states (in place), cum, h_init -> h_last */
+int ssd_bmm_chunk_fwd(const ssd_params* p, void* stream);        /* B, C -> CB (lower-triangular tiles) */
+int ssd_chunk_scan_fwd(const ssd_params* p, void* stream);       /* u, dt, cum, C, states, CB, D, z -> y */
+
+/*
+ * Selective state update, one token (triton_kernels/ssu/forward.py:7):
+ *   dt = clamp(softplus?(delta_raw + delta_bias)), h <- h*exp(A*dt) + (B*dt) x u,
+ *   y = h . C, then optionally y = (y + D*u) * silu(z).
+ * u (b,H,P) x_dtype; A (H,) fp32; B, C (b,G,N) x_dtype; delta_raw (b,H) dt_dtype;
+ * delta_bias (H,) fp32 or NULL; h (b,H,P,N) h_dtype, updated in place;
+ * D (H*P,) fp32 or NULL; z (b,H*P) x_dtype or NULL; y (b,H,P) y_dtype.
+ */
+int ssu_fwd(const void* u, const float* A, const void* B, const void* C,
+            const void* delta_raw, const float* delta_bias, void* h, void* y,
+            const float* D, const void* z,
+            int64_t batch, int64_t nheads, int64_t headdim, int64_t dstate, int64_t ngroups,
+            int32_t x_dtype, int32_t dt_dtype, int32_t h_dtype, int32_t y_dtype,
+            int32_t use_delta_softplus, float delta_min, float delta_max, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SSD_B200_H */

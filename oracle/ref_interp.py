@@ -1,0 +1,54 @@
+"""Run the reference's own Triton kernels on CPU under the Triton interpreter.
+
+TEST INFRASTRUCTURE ONLY: used by ``tests/golden/make_golden.py`` to produce the
+committed golden vectors. It needs the reference checkout (``SA_REFERENCE_SRC`` or
+the default mount) and therefore never runs on a GPU box; nothing in the product,
+the GPU tests or ``bench.py`` imports it.
+
+Recipe:
+- ``TRITON_INTERPRET=1`` must be set before ``triton`` is first imported;
+- each autotuned forward kernel is pinned to one config (its last), so the
+  autotuner does not try to benchmark (which needs a GPU driver);
+- ``length`` is always passed explicitly, since the reference's default allocates
+  on ``"cuda"`` (``ops/ssd_scan.py:67-68``).
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+DEFAULT_SRC = os.environ.get("SA_REFERENCE_SRC", "/root/reference/src")
+
+_loaded = None
+
+
+def load():
+    """Import the reference package in interpreter mode; returns a namespace dict."""
+    global _loaded
+    if _loaded is not None:
+        return _loaded
+    if "triton" in sys.modules and os.environ.get("TRITON_INTERPRET") != "1":
+        raise RuntimeError("triton was imported before TRITON_INTERPRET=1 could be set")
+    os.environ["TRITON_INTERPRET"] = "1"
+    if not os.path.isdir(DEFAULT_SRC):
+        raise FileNotFoundError(f"reference sources not found at {DEFAULT_SRC}")
+    if DEFAULT_SRC not in sys.path:
+        sys.path.insert(0, DEFAULT_SRC)
+    import selective_attention.triton_kernels.ssd_scan.forward_kernel as fk  # noqa: E402
+    for name in ("chunk_cumsum_forward_kernel", "chunk_state_forward_kernel",
+                 "state_passing_forward_kernel", "bmm_chunk_forward_kernel",
+                 "chunk_scan_forward_kernel"):
+        k = getattr(fk, name)
+        k.configs = [k.configs[-1]]
+    from selective_attention.ops import SSDScanFn, SSUFn
+    from selective_attention.triton_kernels.ssd_scan import forward as fwd
+    _loaded = {
+        "SSDScanFn": SSDScanFn,
+        "SSUFn": SSUFn,
+        "chunk_cumsum_forward": fwd.chunk_cumsum_forward,
+        "chunk_state_forward": fwd.chunk_state_forward,
+        "state_passing_forward": fwd.state_passing_forward,
+        "bmm_chunk_forward": fwd.bmm_chunk_forward,
+        "chunk_scan_forward": fwd.chunk_scan_forward,
+    }
+    return _loaded

@@ -1,0 +1,28 @@
+"""B200-native SSD chunked-scan forward and selective state update.
+
+Public surface (mirrors the reference's ``selective_attention.ops`` and
+``selective_attention.triton_kernels``):
+
+- ``SSDScanFn`` / ``SSUFn``: drop-in ops with the reference's signatures.
+- ``kernels``: stage-level host functions (``chunk_cumsum_forward`` ... ``ssd_scan_forward``,
+  ``ssu_forward``) over the C ABI of ``libssd_b200.so`` (``include/ssd_b200.h``).
+- ``shim.install()``: make an installed reference package use these kernels.
+- ``check_device_error()``: surface a kernel's bounded-wait timeout as ``RuntimeError``.
+"""
+from ._lib import check_device_error, device_error
+from .ops import SSDScanFn, SSUFn
+from .kernels import (
+    bmm_chunk_forward,
+    chunk_cumsum_forward,
+    chunk_scan_forward,
+    chunk_state_forward,
+    ssd_scan_forward,
+    ssu_forward,
+    state_passing_forward,
+)
+
+__all__ = [
+    "SSDScanFn", "SSUFn", "ssd_scan_forward", "ssu_forward", "chunk_cumsum_forward",
+    "chunk_state_forward", "state_passing_forward", "bmm_chunk_forward", "chunk_scan_forward",
+    "check_device_error", "device_error",
+]

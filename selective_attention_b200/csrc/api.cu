@@ -1,0 +1,326 @@
+// api.cu - the C ABI declared in include/ssd_b200.h: argument checks, workspace
+// layout, stage dispatch between the tensor-core and CUDA-core kernels.
+#include <cstring>
+
+#include "kernels.h"
+
+using namespace ssdb200;
+
+namespace {
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t v) { return (v + kAlign - 1) & ~(kAlign - 1); }
+
+bool dtype_ok(int d) { return d == SSD_F32 || d == SSD_BF16 || d == SSD_F16; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct Geometry {
+  int b, H, P, N, G, cs;
+  long long L, T;
+  int nc;        // padded: chunks per row
+  int nchunks;   // grid extent over chunks
+  int nrows;     // rows (padded batch) or sequences (packed)
+  bool packed;
+};
+
+int geometry(const ssd_params* p, Geometry& g) {
+  if (!p) return SSD_ERR_INVALID_ARGUMENT;
+  if (p->batch <= 0 || p->seqlen <= 0 || p->nheads <= 0 || p->headdim <= 0 || p->dstate <= 0 ||
+      p->ngroups <= 0 || p->chunk_size <= 0)
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (p->nheads % p->ngroups != 0) return SSD_ERR_INVALID_ARGUMENT;
+  if (p->chunk_size > 256) return SSD_ERR_INVALID_ARGUMENT;  // chunk_cumsum: <= 8 tokens per lane
+  if ((p->headdim * p->dstate) % 4 != 0) return SSD_ERR_INVALID_ARGUMENT;
+  g.b = (int)p->batch;
+  g.H = (int)p->nheads;
+  g.P = (int)p->headdim;
+  g.N = (int)p->dstate;
+  g.G = (int)p->ngroups;
+  g.cs = (int)p->chunk_size;
+  g.L = p->seqlen;
+  g.T = p->batch * p->seqlen;
+  g.packed = p->nseq > 0;
+  if (g.T > (1ll << 31) - 1) return SSD_ERR_INVALID_ARGUMENT;  // TMA coordinates are 32-bit
+  if (g.packed) {
+    if (p->batch != 1 || p->length || !p->cu_seqlens) return SSD_ERR_INVALID_ARGUMENT;
+    if (p->cu_dtype != 32 && p->cu_dtype != 64) return SSD_ERR_INVALID_ARGUMENT;
+    g.nc = 0;
+    g.nrows = (int)p->nseq;
+    g.nchunks = (int)((g.T + g.cs - 1) / g.cs + p->nseq);
+  } else {
+    g.nc = (int)((g.L + g.cs - 1) / g.cs);
+    g.nrows = g.b;
+    g.nchunks = g.b * g.nc;
+  }
+  return SSD_OK;
+}
+
+// The CUDA-core chunk_state stages 32 tokens of x*w and B in shared memory.
+bool simt_fits(const Geometry& g) { return 32ll * (g.P + g.N) * 4 <= 200 * 1024; }
+
+bool use_tc(const ssd_params* p, const Geometry& g) {
+  if (p->impl == SSD_IMPL_SIMT) return false;
+  return tc_supported(p->x_dtype, g.P, g.N, g.cs);
+}
+
+struct Workspace {
+  float* dt;
+  float* cum;
+  float* states;
+  void* prev16;
+  float* CB;
+  ChunkEntry* table;
+  int2* rows;
+  int* count;
+  size_t bytes;
+};
+
+Workspace carve(const ssd_params* p, const Geometry& g, bool tc, uint8_t* base) {
+  Workspace w{};
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* ptr = base ? base + off : nullptr;
+    off += align_up(n);
+    return ptr;
+  };
+  const size_t nk = (size_t)g.nchunks;
+  w.dt = (float*)take(nk * g.H * g.cs * sizeof(float));
+  w.cum = (float*)take(nk * g.H * g.cs * sizeof(float));
+  w.states = (float*)take(nk * g.H * (size_t)g.P * g.N * sizeof(float));
+  if (tc) w.prev16 = take(nk * g.H * (size_t)g.P * g.N * 2);
+  else w.CB = (float*)take(nk * g.G * (size_t)g.cs * g.cs * sizeof(float));
+  if (g.packed) {
+    w.table = (ChunkEntry*)take(nk * sizeof(ChunkEntry));
+    w.rows = (int2*)take((size_t)g.nrows * sizeof(int2));
+    w.count = (int*)take(sizeof(int));
+  }
+  (void)p;
+  w.bytes = off;
+  return w;
+}
+
+LaunchCtx make_ctx(const ssd_params* p, const Geometry& g, cudaStream_t s, const Workspace* w) {
+  LaunchCtx c{};
+  c.stream = s;
+  c.cm.packed = g.packed ? 1 : 0;
+  c.cm.cs = g.cs;
+  c.cm.nc = g.nc;
+  c.cm.L = g.L;
+  c.cm.length = reinterpret_cast<const long long*>(p->length);
+  if (g.packed && w) {
+    c.cm.table = w->table;
+    c.cm.count = w->count;
+    c.cm.rows = w->rows;
+  }
+  c.nchunks_max = g.nchunks;
+  c.nrows = g.nrows;
+  c.H = g.H;
+  c.P = g.P;
+  c.N = g.N;
+  c.G = g.G;
+  c.cs = g.cs;
+  c.T = g.T;
+  c.use_sp = p->use_delta_softplus ? 1 : 0;
+  c.dmin = p->delta_min;
+  c.dmax = p->delta_max;
+  return c;
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? SSD_OK : SSD_ERR_CUDA; }
+
+int check_common_inputs(const ssd_params* p, bool need_y) {
+  if (!dtype_ok(p->x_dtype) || !dtype_ok(p->dt_dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  if (need_y && !dtype_ok(p->y_dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  return SSD_OK;
+}
+
+void record(const ssd_params* p, int i, cudaStream_t s) {
+  if (p->events[i]) cudaEventRecord(reinterpret_cast<cudaEvent_t>(p->events[i]), s);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ssd_b200_version(void) { return "ssd_b200 0.1.0 sm_100a"; }
+
+const char* ssd_b200_status_string(int status) {
+  switch (status) {
+    case SSD_OK: return "ok";
+    case SSD_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case SSD_ERR_UNSUPPORTED_DTYPE: return "unsupported dtype";
+    case SSD_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case SSD_ERR_CUDA: return "CUDA runtime error";
+    case SSD_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+    case SSD_ERR_NO_TENSOR_MAP: return "tensor-map encoder unavailable";
+  }
+  return "unknown status";
+}
+
+int ssd_b200_device_error(void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned int a = fetch_error_simt(s);
+  const unsigned int b = fetch_error_tc(s);
+  const unsigned int c = fetch_error_ssu(s);
+  return (int)(a ? a : (b ? b : c));
+}
+
+int ssd_scan_uses_tensor_cores(const ssd_params* p) {
+  Geometry g;
+  if (geometry(p, g) != SSD_OK) return 0;
+  return use_tc(p, g) ? 1 : 0;
+}
+
+size_t ssd_scan_fwd_workspace_size(const ssd_params* p) {
+  Geometry g;
+  if (geometry(p, g) != SSD_OK) return 0;
+  return carve(p, g, use_tc(p, g), nullptr).bytes;
+}
+
+int ssd_scan_fwd(const ssd_params* p, void* stream) {
+  Geometry g;
+  int st = geometry(p, g);
+  if (st) return st;
+  if ((st = check_common_inputs(p, true))) return st;
+  if (!p->u || !p->A || !p->B || !p->C || !p->delta_raw || !p->y || !p->h_last || !p->workspace)
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (p->impl == SSD_IMPL_TC && !tc_supported(p->x_dtype, g.P, g.N, g.cs)) return SSD_ERR_INVALID_ARGUMENT;
+  const bool tc = use_tc(p, g);
+  if (!tc && !simt_fits(g)) return SSD_ERR_INVALID_ARGUMENT;
+  if (tc && p->y_dtype != SSD_F32 && p->y_dtype != p->x_dtype) return SSD_ERR_UNSUPPORTED_DTYPE;
+  if (!aligned16(p->h_last) || (p->h_init && !aligned16(p->h_init))) return SSD_ERR_INVALID_ARGUMENT;
+  if (tc && (!aligned16(p->u) || !aligned16(p->B) || !aligned16(p->C) || !aligned16(p->y) ||
+             (p->z && !aligned16(p->z))))
+    return SSD_ERR_INVALID_ARGUMENT;
+  Workspace w = carve(p, g, tc, reinterpret_cast<uint8_t*>(p->workspace));
+  if (p->workspace_bytes < w.bytes) return SSD_ERR_WORKSPACE_TOO_SMALL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  LaunchCtx c = make_ctx(p, g, s, &w);
+  record(p, 0, s);
+  if (g.packed) {
+    st = cuda_status(launch_build_chunk_table(s, p->cu_seqlens, p->cu_dtype == 64, (int)p->nseq, g.cs, w.table,
+                                              w.rows, w.count));
+    if (st) return st;
+  }
+  if ((st = cuda_status(launch_chunk_cumsum(c, p->dt_dtype, p->A, p->delta_raw, p->delta_bias, w.dt, w.cum))))
+    return st;
+  record(p, 1, s);
+  int tms = 0;
+  if (tc) {
+    cudaError_t e = launch_tc_chunk_state(c, p->x_dtype, p->u, p->B, w.dt, w.cum, w.states, &tms);
+    if (tms) return SSD_ERR_NO_TENSOR_MAP;
+    if ((st = cuda_status(e))) return st;
+    record(p, 2, s);
+    if ((st = cuda_status(launch_state_passing(c, w.states, w.prev16, p->x_dtype, w.cum, p->h_init, p->h_last))))
+      return st;
+    record(p, 3, s);
+    record(p, 4, s);
+    e = launch_tc_chunk_scan(c, p->x_dtype, p->y_dtype, p->u, w.dt, w.cum, p->B, p->C, w.prev16, p->D, p->z, p->y,
+                             &tms);
+    if (tms) return SSD_ERR_NO_TENSOR_MAP;
+    if ((st = cuda_status(e))) return st;
+    record(p, 5, s);
+  } else {
+    if ((st = cuda_status(launch_simt_chunk_state(c, p->x_dtype, p->u, p->B, w.dt, w.cum, w.states)))) return st;
+    record(p, 2, s);
+    if ((st = cuda_status(launch_state_passing(c, w.states, nullptr, SSD_F32, w.cum, p->h_init, p->h_last))))
+      return st;
+    record(p, 3, s);
+    if ((st = cuda_status(launch_simt_bmm_chunk(c, p->x_dtype, p->B, p->C, w.CB)))) return st;
+    record(p, 4, s);
+    if ((st = cuda_status(launch_simt_chunk_scan(c, p->x_dtype, p->y_dtype, p->u, w.dt, w.cum, p->C, w.states,
+                                                 w.CB, p->D, p->z, p->y))))
+      return st;
+    record(p, 5, s);
+  }
+  return SSD_OK;
+}
+
+// ------------------------------------------------------------- stage entries
+static int stage_prologue(const ssd_params* p, Geometry& g) {
+  int st = geometry(p, g);
+  if (st) return st;
+  if (g.packed) return SSD_ERR_INVALID_ARGUMENT;
+  return SSD_OK;
+}
+
+int ssd_chunk_cumsum_fwd(const ssd_params* p, void* stream) {
+  Geometry g;
+  int st = stage_prologue(p, g);
+  if (st) return st;
+  if (!dtype_ok(p->dt_dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  if (!p->A || !p->delta_raw || !p->dt || !p->cum) return SSD_ERR_INVALID_ARGUMENT;
+  LaunchCtx c = make_ctx(p, g, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  return cuda_status(launch_chunk_cumsum(c, p->dt_dtype, p->A, p->delta_raw, p->delta_bias, p->dt, p->cum));
+}
+
+int ssd_chunk_state_fwd(const ssd_params* p, void* stream) {
+  Geometry g;
+  int st = stage_prologue(p, g);
+  if (st) return st;
+  if ((st = check_common_inputs(p, false))) return st;
+  if (!p->u || !p->B || !p->dt || !p->cum || !p->states) return SSD_ERR_INVALID_ARGUMENT;
+  LaunchCtx c = make_ctx(p, g, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  if (use_tc(p, g)) {
+    if (!aligned16(p->u) || !aligned16(p->B)) return SSD_ERR_INVALID_ARGUMENT;
+    int tms = 0;
+    cudaError_t e = launch_tc_chunk_state(c, p->x_dtype, p->u, p->B, p->dt, p->cum, p->states, &tms);
+    if (tms) return SSD_ERR_NO_TENSOR_MAP;
+    return cuda_status(e);
+  }
+  if (p->impl == SSD_IMPL_TC || !simt_fits(g)) return SSD_ERR_INVALID_ARGUMENT;
+  return cuda_status(launch_simt_chunk_state(c, p->x_dtype, p->u, p->B, p->dt, p->cum, p->states));
+}
+
+int ssd_state_passing_fwd(const ssd_params* p, void* stream) {
+  Geometry g;
+  int st = stage_prologue(p, g);
+  if (st) return st;
+  if (!p->states || !p->cum || !p->h_last) return SSD_ERR_INVALID_ARGUMENT;
+  if (!aligned16(p->states) || !aligned16(p->h_last) || (p->h_init && !aligned16(p->h_init)))
+    return SSD_ERR_INVALID_ARGUMENT;
+  LaunchCtx c = make_ctx(p, g, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  return cuda_status(launch_state_passing(c, p->states, nullptr, SSD_F32, p->cum, p->h_init, p->h_last));
+}
+
+int ssd_bmm_chunk_fwd(const ssd_params* p, void* stream) {
+  Geometry g;
+  int st = stage_prologue(p, g);
+  if (st) return st;
+  if (!dtype_ok(p->x_dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  if (!p->B || !p->C || !p->CB) return SSD_ERR_INVALID_ARGUMENT;
+  LaunchCtx c = make_ctx(p, g, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  return cuda_status(launch_simt_bmm_chunk(c, p->x_dtype, p->B, p->C, p->CB));
+}
+
+int ssd_chunk_scan_fwd(const ssd_params* p, void* stream) {
+  Geometry g;
+  int st = stage_prologue(p, g);
+  if (st) return st;
+  if ((st = check_common_inputs(p, true))) return st;
+  if (!p->u || !p->C || !p->dt || !p->cum || !p->states || !p->CB || !p->y) return SSD_ERR_INVALID_ARGUMENT;
+  LaunchCtx c = make_ctx(p, g, reinterpret_cast<cudaStream_t>(stream), nullptr);
+  return cuda_status(launch_simt_chunk_scan(c, p->x_dtype, p->y_dtype, p->u, p->dt, p->cum, p->C, p->states, p->CB,
+                                            p->D, p->z, p->y));
+}
+
+// ------------------------------------------------------------- SSU
+int ssu_fwd(const void* u, const float* A, const void* B, const void* C, const void* delta_raw,
+            const float* delta_bias, void* h, void* y, const float* D, const void* z, int64_t batch,
+            int64_t nheads, int64_t headdim, int64_t dstate, int64_t ngroups, int32_t x_dtype, int32_t dt_dtype,
+            int32_t h_dtype, int32_t y_dtype, int32_t use_delta_softplus, float delta_min, float delta_max,
+            void* stream) {
+  if (!u || !A || !B || !C || !delta_raw || !h || !y) return SSD_ERR_INVALID_ARGUMENT;
+  if (batch <= 0 || nheads <= 0 || headdim <= 0 || dstate <= 0 || ngroups <= 0) return SSD_ERR_INVALID_ARGUMENT;
+  if (nheads % ngroups != 0 || dstate > 1024) return SSD_ERR_INVALID_ARGUMENT;
+  if (batch * nheads > 0x7fffffffll) return SSD_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(x_dtype) || !dtype_ok(dt_dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  if (h_dtype != SSD_F32 && h_dtype != SSD_BF16) return SSD_ERR_UNSUPPORTED_DTYPE;
+  if (y_dtype != x_dtype) return SSD_ERR_UNSUPPORTED_DTYPE;
+  return cuda_status(launch_ssu(u, A, B, C, delta_raw, delta_bias, h, y, D, z, (int)batch, (int)nheads,
+                                (int)headdim, (int)dstate, (int)ngroups, x_dtype, dt_dtype, h_dtype, y_dtype,
+                                use_delta_softplus, delta_min, delta_max, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,54 @@
+// kernels.h - host-side launch interface between the C ABI (api.cu) and the
+// kernel translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+
+namespace ssdb200 {
+
+struct LaunchCtx {
+  cudaStream_t stream;
+  ChunkMap cm;
+  int nchunks_max;  // grid extent over chunks (exact in padded mode, an upper bound in packed mode)
+  int nrows;        // batch rows (padded) or sequences (packed)
+  int H, P, N, G, cs;
+  long long T;      // total tokens (b * L)
+  int use_sp;
+  float dmin, dmax;
+};
+
+// ssd_simt.cu
+cudaError_t launch_chunk_cumsum(const LaunchCtx& c, int dt_dtype, const float* A, const void* delta_raw,
+                                const float* delta_bias, float* dt, float* cum);
+cudaError_t launch_state_passing(const LaunchCtx& c, float* states, void* prev16, int prev_dtype,
+                                 const float* cum, const float* h_init, float* h_last);
+cudaError_t launch_build_chunk_table(cudaStream_t s, const void* cu, int cu64, int nseq, int cs, ChunkEntry* table,
+                                     int2* rows, int* count);
+cudaError_t launch_simt_chunk_state(const LaunchCtx& c, int x_dtype, const void* u, const void* B,
+                                    const float* dt, const float* cum, float* states);
+cudaError_t launch_simt_bmm_chunk(const LaunchCtx& c, int x_dtype, const void* B, const void* C, float* CB);
+cudaError_t launch_simt_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, const void* u, const float* dt,
+                                   const float* cum, const void* C, const float* prev, const float* CB,
+                                   const float* D, const void* z, void* y);
+unsigned int fetch_error_simt(cudaStream_t s);
+
+// ssd_tc.cu (tcgen05 + TMA; bf16/fp16 inputs, P = 64, N = 128, cs = 256; prev16 in the input type)
+bool tc_supported(int x_dtype, int P, int N, int cs);
+cudaError_t launch_tc_chunk_state(const LaunchCtx& c, int x_dtype, const void* u, const void* B, const float* dt,
+                                  const float* cum, float* states, int* tmap_status);
+cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, const void* u, const float* dt,
+                                 const float* cum, const void* B, const void* C, const void* prev16,
+                                 const float* D, const void* z, void* y, int* tmap_status);
+unsigned int fetch_error_tc(cudaStream_t s);
+
+// ssu.cu
+cudaError_t launch_ssu(const void* u, const float* A, const void* B, const void* C, const void* delta_raw,
+                       const float* delta_bias, void* h, void* y, const float* D, const void* z, int b, int H,
+                       int P, int N, int G, int x_dtype, int dt_dtype, int h_dtype, int y_dtype, int use_sp,
+                       float dmin, float dmax, cudaStream_t stream);
+unsigned int fetch_error_ssu(cudaStream_t s);
+
+}  // namespace ssdb200

@@ -1,0 +1,447 @@
+// ssd_simt.cu - bandwidth kernels shared by both SSD paths (chunk_cumsum,
+// state_passing, packed chunk table) and the CUDA-core (FFMA) versions of
+// chunk_state, bmm_chunk and chunk_scan used for fp32 inputs and for shapes the
+// tensor-core kernels do not cover.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ssdb200 {
+
+// ===========================================================================
+// chunk_cumsum: ssd_scan/forward_kernel.py:19-87.
+// One CTA per (chunk, 32-head slice). The (cs x 32) slice of delta_raw is read
+// coalesced into shared memory, transformed (bias, softplus, clamp, length mask),
+// then each warp scans whole heads: 8 tokens per lane sequentially, lane totals
+// with a shuffle scan. Writes dt and cum, both (nchunks, H, cs).
+// ===========================================================================
+template <typename DT>
+__global__ void __launch_bounds__(256) chunk_cumsum_kernel(
+    const float* __restrict__ A, const DT* __restrict__ delta_raw, const float* __restrict__ delta_bias,
+    float* __restrict__ dt_out, float* __restrict__ cum_out, ChunkMap cm, int H, int use_sp,
+    float dmin, float dmax) {
+  __shared__ float tile[256][33];
+  const int k = blockIdx.x;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int cs = cm.cs;
+  const int h0 = blockIdx.y * 32;
+  const int nh = min(32, H - h0);
+  const int tid = threadIdx.x;
+  for (int idx = tid; idx < cs * 32; idx += 256) {
+    const int t = idx >> 5, hh = idx & 31;
+    float v = 0.f;
+    if (t < ci.vlim && hh < nh) {
+      float d = Ld<DT>::f(delta_raw + (ci.tok0 + t) * (long long)H + h0 + hh);
+      if (delta_bias) d += delta_bias[h0 + hh];
+      v = dt_transform(d, use_sp, dmin, dmax);
+    }
+    tile[t][hh] = v;
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  const int E = (cs + 31) >> 5;  // tokens per lane (<= 8)
+  for (int hh = warp; hh < nh; hh += 8) {
+    const float a = A[h0 + hh];
+    float vals[8];
+    float run = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int t = lane * E + e;
+      float v = (e < E && t < cs) ? tile[t][hh] * a : 0.f;
+      run += v;
+      vals[e] = run;
+    }
+    // inclusive scan of lane totals
+    float incl = run;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      float o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    const float excl = incl - run;
+    const long long base = ((long long)k * H + h0 + hh) * cs;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int t = lane * E + e;
+      if (e < E && t < cs) {
+        dt_out[base + t] = tile[t][hh];
+        cum_out[base + t] = excl + vals[e];
+      }
+    }
+  }
+}
+
+// ===========================================================================
+// state_passing: ssd_scan/forward_kernel.py:202-250.
+// One thread per 4 consecutive state elements of one (row, head); walks the row's
+// chunks in order: out[c] = prev; prev = exp(cum_last[c]) * prev + S[c].
+// P16 = float: prev states overwrite S in place (fp32), as the reference does.
+// P16 = bf16/fp16: prev states go to a separate 16-bit buffer (the tensor-core
+// chunk_scan operand, in the input's type) and S is left untouched.
+// ===========================================================================
+template <typename P16>
+__global__ void __launch_bounds__(256) state_passing_kernel(
+    float* __restrict__ states, P16* __restrict__ prev16, const float* __restrict__ cum,
+    const float* __restrict__ h_init, float* __restrict__ h_last, ChunkMap cm, int H, int PN) {
+  constexpr bool kSeparate = sizeof(P16) == 2;
+  const int row = blockIdx.z, h = blockIdx.y;
+  const int e0 = (blockIdx.x * 256 + threadIdx.x) * 4;
+  if (e0 >= PN) return;
+  int first, count;
+  if (cm.packed) {
+    int2 r = cm.rows[row];
+    first = r.x;
+    count = r.y;
+  } else {
+    first = row * cm.nc;
+    count = cm.nc;
+  }
+  const int cs = cm.cs;
+  float4 prev = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (h_init) prev = *reinterpret_cast<const float4*>(h_init + ((long long)row * H + h) * PN + e0);
+  float4 nxt = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (count > 0) nxt = *reinterpret_cast<const float4*>(states + ((long long)first * H + h) * PN + e0);
+  for (int c = 0; c < count; ++c) {
+    const long long kk = first + c;
+    const float4 s = nxt;
+    if (c + 1 < count) nxt = *reinterpret_cast<const float4*>(states + ((kk + 1) * H + h) * PN + e0);
+    const long long off = (kk * H + h) * PN + e0;
+    if constexpr (kSeparate) {
+      uint2 pk;
+      pk.x = pack2<P16>(prev.x, prev.y);
+      pk.y = pack2<P16>(prev.z, prev.w);
+      *reinterpret_cast<uint2*>(prev16 + off) = pk;
+    } else {
+      *reinterpret_cast<float4*>(states + off) = prev;
+    }
+    const float sc = expf(cum[(kk * H + h) * cs + cs - 1]);
+    prev.x = sc * prev.x + s.x;
+    prev.y = sc * prev.y + s.y;
+    prev.z = sc * prev.z + s.z;
+    prev.w = sc * prev.w + s.w;
+  }
+  *reinterpret_cast<float4*>(h_last + ((long long)row * H + h) * PN + e0) = prev;
+}
+
+// ===========================================================================
+// Packed mode: chunk table from cu_seqlens (one CTA). Sequence i of length len
+// gets ceil(len/cs) chunks starting at token cu[i]; rows[i] = {first, count}.
+// ===========================================================================
+template <typename IT>
+__global__ void __launch_bounds__(1024) build_chunk_table_kernel(const IT* __restrict__ cu, int nseq, int cs,
+                                                                 ChunkEntry* __restrict__ table,
+                                                                 int2* __restrict__ rows, int* __restrict__ count) {
+  __shared__ int warp_sums[32];
+  __shared__ int running_s;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) running_s = 0;
+  __syncthreads();
+  for (int base = 0; base < nseq; base += 1024) {
+    const int i = base + tid;
+    long long start = 0, len = 0;
+    int n = 0;
+    if (i < nseq) {
+      start = (long long)cu[i];
+      len = (long long)cu[i + 1] - start;
+      if (len < 0) len = 0;
+      n = (int)((len + cs - 1) / cs);
+    }
+    int incl = n;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_sums[lane];
+      int wi = w;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        int o = __shfl_up_sync(0xffffffffu, wi, off);
+        if (lane >= off) wi += o;
+      }
+      warp_sums[lane] = wi - w;  // exclusive prefix of warp totals
+    }
+    __syncthreads();
+    const int running = running_s;
+    const int first = running + warp_sums[warp] + incl - n;
+    if (i < nseq) {
+      rows[i] = make_int2(first, n);
+      for (int c = 0; c < n; ++c) {
+        ChunkEntry e;
+        e.row = i;
+        e.c = c;
+        e.tok0 = start + (long long)c * cs;
+        long long rem = len - (long long)c * cs;
+        e.lim = (int)(rem < cs ? rem : cs);
+        e.pad = 0;
+        table[first + c] = e;
+      }
+    }
+    __syncthreads();
+    if (tid == 1023) running_s = first + n;
+    __syncthreads();
+  }
+  if (tid == 0) *count = running_s;
+}
+
+// ===========================================================================
+// CUDA-core chunk_state: ssd_scan/forward_kernel.py:107-185.
+// CTA = (4096-output slice of P*N, head, chunk); 16 outputs per thread.
+// Token tiles of 32 are staged in shared memory as x*w and B.
+// ===========================================================================
+template <typename T>
+__global__ void __launch_bounds__(256) simt_chunk_state_kernel(
+    const T* __restrict__ u, const T* __restrict__ Bm, const float* __restrict__ dt,
+    const float* __restrict__ cum, float* __restrict__ states, ChunkMap cm, int H, int G, int P, int N) {
+  extern __shared__ float sm[];
+  const int k = blockIdx.z, h = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int cs = cm.cs, hpg = H / G, g = h / hpg;
+  float* xs = sm;            // [32][P]
+  float* bs = sm + 32 * P;   // [32][N]
+  const int tid = threadIdx.x;
+  const int PN = P * N;
+  int pp[16], nn[16];
+  const int o0 = blockIdx.x * 4096 + tid * 16;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    int o = o0 + i;
+    if (o >= PN) o = PN - 1;
+    pp[i] = o / N;
+    nn[i] = o - pp[i] * N;
+  }
+  float acc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+  const float* dtk = dt + ((long long)k * H + h) * cs;
+  const float* cmk = cum + ((long long)k * H + h) * cs;
+  const float clast = cmk[cs - 1];
+  for (int l0 = 0; l0 < ci.lim; l0 += 32) {
+    for (int idx = tid; idx < 32 * P; idx += 256) {
+      const int l = idx / P, p = idx - l * P;
+      float v = 0.f;
+      if (l0 + l < ci.lim) {
+        const float w = expf(fminf(clast - cmk[l0 + l], 0.f)) * dtk[l0 + l];
+        v = Ld<T>::f(u + ((ci.tok0 + l0 + l) * H + h) * (long long)P + p) * w;
+      }
+      xs[idx] = v;
+    }
+    for (int idx = tid; idx < 32 * N; idx += 256) {
+      const int l = idx / N, n = idx - l * N;
+      float v = 0.f;
+      if (l0 + l < ci.lim) v = Ld<T>::f(Bm + ((ci.tok0 + l0 + l) * G + g) * (long long)N + n);
+      bs[idx] = v;
+    }
+    __syncthreads();
+    const int lmax = min(32, ci.lim - l0);
+    for (int l = 0; l < lmax; ++l) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = fmaf(xs[l * P + pp[i]], bs[l * N + nn[i]], acc[i]);
+    }
+    __syncthreads();
+  }
+  float* out = states + ((long long)k * H + h) * PN;
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (o0 + i < PN) out[o0 + i] = acc[i];
+}
+
+// ===========================================================================
+// CUDA-core bmm_chunk: ssd_scan/forward_kernel.py:270-328.
+// CB[k,g,l,s] = sum_n C[l,n] B[s,n] for l,s < lim (zero outside), written for the
+// whole cs x cs block (the reference writes only the lower tiles when causal).
+// ===========================================================================
+template <typename T>
+__global__ void __launch_bounds__(256) simt_bmm_chunk_kernel(const T* __restrict__ Bm, const T* __restrict__ Cm,
+                                                             float* __restrict__ CB, ChunkMap cm, int G, int N) {
+  const int k = blockIdx.z, g = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int cs = cm.cs;
+  const int o0 = blockIdx.x * 4096 + threadIdx.x * 16;
+  float* out = CB + ((long long)k * G + g) * cs * cs;
+  for (int i = 0; i < 16; ++i) {
+    const int o = o0 + i;
+    if (o >= cs * cs) break;
+    const int l = o / cs, s = o - l * cs;
+    float acc = 0.f;
+    if (l < ci.lim && s < ci.lim) {
+      const T* cr = Cm + ((ci.tok0 + l) * G + g) * (long long)N;
+      const T* br = Bm + ((ci.tok0 + s) * G + g) * (long long)N;
+      for (int n = 0; n < N; ++n) acc = fmaf(Ld<T>::f(cr + n), Ld<T>::f(br + n), acc);
+    }
+    out[o] = acc;
+  }
+}
+
+// ===========================================================================
+// CUDA-core chunk_scan: ssd_scan/forward_kernel.py:350-455, plus the D/z epilogue
+// of modules/ssm.py:145-150. 16 outputs (l, p) per thread.
+//   y = exp(cum_l) * sum_n C[l,n] prev[p,n]
+//     + sum_{s<=l, s<lim} CB[l,s] exp(min(cum_l - cum_s, 0)) dt_s u[s,p]
+// ===========================================================================
+template <typename T, typename YT>
+__global__ void __launch_bounds__(256) simt_chunk_scan_kernel(
+    const T* __restrict__ u, const float* __restrict__ dt, const float* __restrict__ cum,
+    const T* __restrict__ Cm, const float* __restrict__ prev, const float* __restrict__ CB,
+    const float* __restrict__ D, const T* __restrict__ z, YT* __restrict__ y, ChunkMap cm, int H, int G,
+    int P, int N) {
+  const int k = blockIdx.z, h = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int cs = cm.cs, hpg = H / G, g = h / hpg;
+  const float* dtk = dt + ((long long)k * H + h) * cs;
+  const float* cmk = cum + ((long long)k * H + h) * cs;
+  const float* hp = prev + ((long long)k * H + h) * (long long)P * N;
+  const float* cbk = CB + ((long long)k * G + g) * cs * cs;
+  const int o0 = blockIdx.x * 4096 + threadIdx.x * 16;
+  for (int i = 0; i < 16; ++i) {
+    const int o = o0 + i;
+    if (o >= cs * P) break;
+    const int l = o / P, p = o - l * P;
+    if (l >= ci.lim) continue;
+    const long long tok = ci.tok0 + l;
+    const float cl = cmk[l];
+    float acc = 0.f;
+    const T* cr = Cm + (tok * G + g) * (long long)N;
+    for (int n = 0; n < N; ++n) acc = fmaf(Ld<T>::f(cr + n), hp[p * N + n], acc);
+    acc *= expf(cl);
+    const int smax = min(l, ci.lim - 1);
+    for (int s = 0; s <= smax; ++s) {
+      const float m = cbk[l * cs + s] * expf(fminf(cl - cmk[s], 0.f)) * dtk[s];
+      acc = fmaf(m, Ld<T>::f(u + ((ci.tok0 + s) * H + h) * (long long)P + p), acc);
+    }
+    const long long yo = (tok * H + h) * (long long)P + p;
+    if (D) acc = fmaf(D[h * P + p], Ld<T>::f(u + yo), acc);
+    if (z) acc *= silu(Ld<T>::f(z + yo));
+    y[yo] = from_f32<YT>(acc);
+  }
+}
+
+// ===========================================================================
+// Host launchers
+// ===========================================================================
+template <typename DT>
+static cudaError_t launch_cumsum_t(const LaunchCtx& c, const float* A, const void* dr, const float* bias,
+                                   float* dt, float* cum) {
+  dim3 grid(c.nchunks_max, (unsigned)((c.H + 31) / 32));
+  chunk_cumsum_kernel<DT><<<grid, 256, 0, c.stream>>>(A, (const DT*)dr, bias, dt, cum, c.cm, c.H, c.use_sp,
+                                                      c.dmin, c.dmax);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_chunk_cumsum(const LaunchCtx& c, int dt_dtype, const float* A, const void* delta_raw,
+                                const float* delta_bias, float* dt, float* cum) {
+  switch (dt_dtype) {
+    case SSD_F32: return launch_cumsum_t<float>(c, A, delta_raw, delta_bias, dt, cum);
+    case SSD_BF16: return launch_cumsum_t<__nv_bfloat16>(c, A, delta_raw, delta_bias, dt, cum);
+    case SSD_F16: return launch_cumsum_t<__half>(c, A, delta_raw, delta_bias, dt, cum);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_state_passing(const LaunchCtx& c, float* states, void* prev16, int prev_dtype,
+                                 const float* cum, const float* h_init, float* h_last) {
+  const int PN = c.P * c.N;
+  dim3 grid((unsigned)((PN / 4 + 255) / 256), (unsigned)c.H, (unsigned)c.nrows);
+  if (prev16 && prev_dtype == SSD_BF16)
+    state_passing_kernel<__nv_bfloat16><<<grid, 256, 0, c.stream>>>(states, (__nv_bfloat16*)prev16, cum, h_init,
+                                                                     h_last, c.cm, c.H, PN);
+  else if (prev16 && prev_dtype == SSD_F16)
+    state_passing_kernel<__half><<<grid, 256, 0, c.stream>>>(states, (__half*)prev16, cum, h_init, h_last, c.cm,
+                                                             c.H, PN);
+  else
+    state_passing_kernel<float><<<grid, 256, 0, c.stream>>>(states, nullptr, cum, h_init, h_last, c.cm, c.H, PN);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_build_chunk_table(cudaStream_t s, const void* cu, int cu64, int nseq, int cs, ChunkEntry* table,
+                                     int2* rows, int* count) {
+  if (cu64)
+    build_chunk_table_kernel<long long><<<1, 1024, 0, s>>>((const long long*)cu, nseq, cs, table, rows, count);
+  else
+    build_chunk_table_kernel<int><<<1, 1024, 0, s>>>((const int*)cu, nseq, cs, table, rows, count);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t simt_state_t(const LaunchCtx& c, const void* u, const void* B, const float* dt,
+                                const float* cum, float* states) {
+  const int PN = c.P * c.N;
+  dim3 grid((unsigned)((PN + 4095) / 4096), (unsigned)c.H, (unsigned)c.nchunks_max);
+  size_t sm = (size_t)32 * (c.P + c.N) * sizeof(float);
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(simt_chunk_state_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sm);
+    if (e != cudaSuccess) return e;
+  }
+  simt_chunk_state_kernel<T><<<grid, 256, sm, c.stream>>>((const T*)u, (const T*)B, dt, cum, states, c.cm, c.H,
+                                                          c.G, c.P, c.N);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_simt_chunk_state(const LaunchCtx& c, int x_dtype, const void* u, const void* B,
+                                    const float* dt, const float* cum, float* states) {
+  switch (x_dtype) {
+    case SSD_F32: return simt_state_t<float>(c, u, B, dt, cum, states);
+    case SSD_BF16: return simt_state_t<__nv_bfloat16>(c, u, B, dt, cum, states);
+    case SSD_F16: return simt_state_t<__half>(c, u, B, dt, cum, states);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename T>
+static cudaError_t simt_bmm_t(const LaunchCtx& c, const void* B, const void* C, float* CB) {
+  dim3 grid((unsigned)((c.cs * c.cs + 4095) / 4096), (unsigned)c.G, (unsigned)c.nchunks_max);
+  simt_bmm_chunk_kernel<T><<<grid, 256, 0, c.stream>>>((const T*)B, (const T*)C, CB, c.cm, c.G, c.N);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_simt_bmm_chunk(const LaunchCtx& c, int x_dtype, const void* B, const void* C, float* CB) {
+  switch (x_dtype) {
+    case SSD_F32: return simt_bmm_t<float>(c, B, C, CB);
+    case SSD_BF16: return simt_bmm_t<__nv_bfloat16>(c, B, C, CB);
+    case SSD_F16: return simt_bmm_t<__half>(c, B, C, CB);
+  }
+  return cudaErrorInvalidValue;
+}
+
+template <typename T, typename YT>
+static cudaError_t simt_scan_t(const LaunchCtx& c, const void* u, const float* dt, const float* cum, const void* C,
+                               const float* prev, const float* CB, const float* D, const void* z, void* y) {
+  dim3 grid((unsigned)((c.cs * c.P + 4095) / 4096), (unsigned)c.H, (unsigned)c.nchunks_max);
+  simt_chunk_scan_kernel<T, YT><<<grid, 256, 0, c.stream>>>((const T*)u, dt, cum, (const T*)C, prev, CB, D,
+                                                            (const T*)z, (YT*)y, c.cm, c.H, c.G, c.P, c.N);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t simt_scan_y(const LaunchCtx& c, int y_dtype, const void* u, const float* dt, const float* cum,
+                               const void* C, const float* prev, const float* CB, const float* D, const void* z,
+                               void* y) {
+  switch (y_dtype) {
+    case SSD_F32: return simt_scan_t<T, float>(c, u, dt, cum, C, prev, CB, D, z, y);
+    case SSD_BF16: return simt_scan_t<T, __nv_bfloat16>(c, u, dt, cum, C, prev, CB, D, z, y);
+    case SSD_F16: return simt_scan_t<T, __half>(c, u, dt, cum, C, prev, CB, D, z, y);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_simt_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, const void* u, const float* dt,
+                                   const float* cum, const void* C, const float* prev, const float* CB,
+                                   const float* D, const void* z, void* y) {
+  switch (x_dtype) {
+    case SSD_F32: return simt_scan_y<float>(c, y_dtype, u, dt, cum, C, prev, CB, D, z, y);
+    case SSD_BF16: return simt_scan_y<__nv_bfloat16>(c, y_dtype, u, dt, cum, C, prev, CB, D, z, y);
+    case SSD_F16: return simt_scan_y<__half>(c, y_dtype, u, dt, cum, C, prev, CB, D, z, y);
+  }
+  return cudaErrorInvalidValue;
+}
+
+SSDB200_DEFINE_ERROR_FETCH(fetch_error_simt)
+
+}  // namespace ssdb200

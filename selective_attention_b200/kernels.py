@@ -1,0 +1,261 @@
+"""Host functions over the C ABI, mirroring ``triton_kernels`` of the reference.
+
+Names, argument order and return layouts follow
+``triton_kernels/ssd_scan/forward.py`` (``chunk_cumsum_forward`` :14,
+``chunk_state_forward`` :62, ``state_passing_forward`` :102, ``bmm_chunk_forward`` :139,
+``chunk_scan_forward`` :175, ``ssd_scan_forward`` :223) and ``triton_kernels/ssu/forward.py``
+(``ssu_forward`` :7). Every launch goes on the current torch stream of the inputs'
+device; nothing synchronizes.
+
+Internal layout note: the CUDA kernels keep ``delta`` / ``decay_cumsum`` chunk-major,
+``(b, nc, H, cs)``; the functions here return them as ``(b, H, nc, cs)`` views, the
+reference's layout, and accept either.
+"""
+from __future__ import annotations
+
+import math
+from ctypes import byref, c_void_p
+from typing import Optional, Sequence, Tuple
+
+import torch
+
+from . import _lib
+from .utils import check_cuda, to_contiguous
+
+INF = float("inf")
+
+
+def _params(**kw) -> _lib.SSDParams:
+    p = _lib.SSDParams()
+    p.delta_min, p.delta_max = 0.0, INF
+    p.use_delta_softplus = 1
+    p.cu_dtype = 64
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+def _chunk_major(t: torch.Tensor) -> torch.Tensor:
+    """(b, H, nc, cs) reference layout -> contiguous (b, nc, H, cs) kernel layout."""
+    return t.permute(0, 2, 1, 3).contiguous()
+
+
+def _stream(dev) -> c_void_p:
+    return c_void_p(_lib.stream_handle(dev))
+
+
+def chunk_cumsum_forward(A, delta_raw, delta_bias, length, chunk_size, use_delta_softplus=True,
+                         delta_limit: Tuple[float, float] = (0.0, INF)):
+    """Returns ``(decay_cumsum, delta)``, each ``(b, H, nc, cs)`` fp32 (views)."""
+    b, L, H = delta_raw.shape
+    dev = check_cuda([A, delta_raw, delta_bias, length], ["A", "delta_raw", "delta_bias", "length"])
+    nc = math.ceil(L / chunk_size)
+    A = to_contiguous(A.float())
+    delta_raw = to_contiguous(delta_raw)
+    delta_bias = None if delta_bias is None else to_contiguous(delta_bias.float())
+    length = None if length is None else to_contiguous(length.to(torch.int64))
+    dt = torch.empty(b, nc, H, chunk_size, device=dev, dtype=torch.float32)
+    cum = torch.empty_like(dt)
+    p = _params(batch=b, seqlen=L, nheads=H, headdim=1, dstate=4, ngroups=1, chunk_size=chunk_size,
+                dt_dtype=_lib.dtype_code(delta_raw.dtype, "delta_raw"),
+                use_delta_softplus=int(bool(use_delta_softplus)),
+                delta_min=float(delta_limit[0]), delta_max=float(delta_limit[1]),
+                A=_lib.ptr(A), delta_raw=_lib.ptr(delta_raw), delta_bias=_lib.ptr(delta_bias),
+                length=_lib.ptr(length), dt=_lib.ptr(dt), cum=_lib.ptr(cum))
+    _lib.check(_lib.lib().ssd_chunk_cumsum_fwd(byref(p), _stream(dev)), "chunk_cumsum_forward")
+    return cum.permute(0, 2, 1, 3), dt.permute(0, 2, 1, 3)
+
+
+def chunk_state_forward(u, B, delta, decay_cumsum, impl: str = "auto"):
+    """Per-chunk states ``(b, nc, H, P, N)`` fp32."""
+    b, L, H, P = u.shape
+    G, N = B.shape[2], B.shape[3]
+    nc, cs = delta.shape[2], delta.shape[3]
+    dev = check_cuda([u, B, delta, decay_cumsum], ["u", "B", "delta", "decay_cumsum"])
+    u, B = to_contiguous(u), to_contiguous(B)
+    if B.dtype != u.dtype:
+        raise ValueError(f"[B] dtype {B.dtype} differs from u's {u.dtype}")
+    dt, cum = _chunk_major(delta.float()), _chunk_major(decay_cumsum.float())
+    states = torch.empty(b, nc, H, P, N, device=dev, dtype=torch.float32)
+    p = _params(batch=b, seqlen=L, nheads=H, headdim=P, dstate=N, ngroups=G, chunk_size=cs,
+                x_dtype=_lib.dtype_code(u.dtype, "u"), impl=_lib.IMPLS[impl],
+                u=_lib.ptr(u), B=_lib.ptr(B), dt=_lib.ptr(dt), cum=_lib.ptr(cum), states=_lib.ptr(states))
+    _lib.check(_lib.lib().ssd_chunk_state_fwd(byref(p), _stream(dev)), "chunk_state_forward")
+    return states
+
+
+def state_passing_forward(h, h_init, decay_last):
+    """``h``: ``(b, nc, H, P*N)`` per-chunk states, overwritten in place with the
+    states entering each chunk; returns ``(h, h_last)`` like the reference."""
+    b, nc, H, PN = h.shape
+    dev = check_cuda([h, h_init, decay_last], ["h", "h_init", "decay_last"])
+    if h.dtype != torch.float32 or not h.is_contiguous():
+        raise ValueError("[h] expected a contiguous float32 tensor (updated in place)")
+    h_init = None if h_init is None else to_contiguous(h_init.float())
+    # decay_last (b, H, nc) is presented to the kernel as a cumsum with chunk_size 1.
+    last = decay_last.float().permute(0, 2, 1).contiguous()  # (b, nc, H)
+    h_last = torch.empty(b, H, PN, device=dev, dtype=torch.float32)
+    p = _params(batch=b, seqlen=nc, nheads=H, headdim=1, dstate=PN, ngroups=1, chunk_size=1,
+                states=_lib.ptr(h), cum=_lib.ptr(last), h_init=_lib.ptr(h_init), h_last=_lib.ptr(h_last))
+    _lib.check(_lib.lib().ssd_state_passing_fwd(byref(p), _stream(dev)), "state_passing_forward")
+    return h, h_last
+
+
+def bmm_chunk_forward(B, C, chunk_size, is_causal=False):
+    """``CB = C B^T`` per chunk and group, ``(b, nc, G, cs, cs)`` fp32; rows/columns
+    past ``seq_len`` are zero. (Written for every tile regardless of ``is_causal``.)"""
+    b, L, G, N = B.shape
+    dev = check_cuda([B, C], ["B", "C"])
+    B, C = to_contiguous(B), to_contiguous(C)
+    nc = math.ceil(L / chunk_size)
+    CB = torch.empty(b, nc, G, chunk_size, chunk_size, device=dev, dtype=torch.float32)
+    p = _params(batch=b, seqlen=L, nheads=G, headdim=1, dstate=N, ngroups=G, chunk_size=chunk_size,
+                x_dtype=_lib.dtype_code(B.dtype, "B"), B=_lib.ptr(B), C=_lib.ptr(C), CB=_lib.ptr(CB))
+    # headdim*dstate must be a multiple of 4 for the geometry check; bmm ignores headdim.
+    p.headdim = 4
+    _lib.check(_lib.lib().ssd_bmm_chunk_fwd(byref(p), _stream(dev)), "bmm_chunk_forward")
+    return CB
+
+
+def chunk_scan_forward(u, delta, decay_cumsum, C, h, CB, D=None, z=None, out_dtype=torch.float32):
+    """``y (b, L, H, P)``; ``h`` holds the states entering each chunk (fp32)."""
+    b, L, H, P = u.shape
+    G, N = C.shape[2], C.shape[3]
+    nc, cs = delta.shape[2], delta.shape[3]
+    dev = check_cuda([u, delta, decay_cumsum, C, h, CB, D, z], ["u", "delta", "decay_cumsum", "C", "h", "CB", "D", "z"])
+    u, C = to_contiguous(u), to_contiguous(C)
+    h, CB = to_contiguous(h.float()), to_contiguous(CB.float())
+    dt, cum = _chunk_major(delta.float()), _chunk_major(decay_cumsum.float())
+    D = None if D is None else to_contiguous(D.float())
+    z = None if z is None else to_contiguous(z.to(u.dtype))
+    y = torch.empty(b, L, H, P, device=dev, dtype=out_dtype)
+    p = _params(batch=b, seqlen=L, nheads=H, headdim=P, dstate=N, ngroups=G, chunk_size=cs,
+                x_dtype=_lib.dtype_code(u.dtype, "u"), dt_dtype=0, y_dtype=_lib.dtype_code(out_dtype, "y"),
+                u=_lib.ptr(u), C=_lib.ptr(C), dt=_lib.ptr(dt), cum=_lib.ptr(cum), states=_lib.ptr(h),
+                CB=_lib.ptr(CB), D=_lib.ptr(D), z=_lib.ptr(z), y=_lib.ptr(y))
+    _lib.check(_lib.lib().ssd_chunk_scan_fwd(byref(p), _stream(dev)), "chunk_scan_forward")
+    return y
+
+
+def ssd_scan_params(u, A, B, C, delta_raw, delta_bias=None, h_init=None, length=None, chunk_size=256,
+                    use_delta_softplus=True, delta_limit=(0.0, INF), D=None, z=None, cu_seqlens=None,
+                    impl: str = "auto", y_dtype: Optional[torch.dtype] = None):
+    """Build the ``ssd_params`` block for ``ssd_scan_fwd`` (no outputs or workspace yet).
+
+    Returns ``(params, keep)``; ``keep`` holds the converted tensors the pointers refer to.
+    """
+    b, L, H, P = u.shape
+    G, N = B.shape[2], B.shape[3]
+    A = to_contiguous(A.float())
+    delta_bias = None if delta_bias is None else to_contiguous(delta_bias.float())
+    h_init = None if h_init is None else to_contiguous(h_init.float())
+    length = None if length is None else to_contiguous(length.to(torch.int64))
+    D = None if D is None else to_contiguous(D.float())
+    if z is not None:
+        if z.dtype != u.dtype:
+            raise ValueError(f"[z] dtype {z.dtype} differs from u's {u.dtype}")
+        z = to_contiguous(z)
+    if y_dtype is None:
+        y_dtype = u.dtype if (D is not None or z is not None) else torch.float32
+    nseq = 0
+    cu_dtype = 64
+    if cu_seqlens is not None:
+        if cu_seqlens.dtype not in (torch.int32, torch.int64):
+            raise ValueError("[cu_seqlens] expected int32 or int64")
+        cu_seqlens = to_contiguous(cu_seqlens)
+        nseq = cu_seqlens.numel() - 1
+        cu_dtype = 64 if cu_seqlens.dtype == torch.int64 else 32
+    p = _params(batch=b, seqlen=L, nheads=H, headdim=P, dstate=N, ngroups=G, chunk_size=int(chunk_size),
+                nseq=nseq, x_dtype=_lib.dtype_code(u.dtype, "u"),
+                dt_dtype=_lib.dtype_code(delta_raw.dtype, "delta_raw"), y_dtype=_lib.dtype_code(y_dtype, "y"),
+                cu_dtype=cu_dtype, use_delta_softplus=int(bool(use_delta_softplus)),
+                delta_min=float(delta_limit[0]), delta_max=float(delta_limit[1]), impl=_lib.IMPLS[impl],
+                u=_lib.ptr(u), A=_lib.ptr(A), B=_lib.ptr(B), C=_lib.ptr(C), delta_raw=_lib.ptr(delta_raw),
+                delta_bias=_lib.ptr(delta_bias), h_init=_lib.ptr(h_init), length=_lib.ptr(length),
+                D=_lib.ptr(D), z=_lib.ptr(z), cu_seqlens=_lib.ptr(cu_seqlens))
+    keep = (u, A, B, C, delta_raw, delta_bias, h_init, length, D, z, cu_seqlens)
+    return p, keep, y_dtype
+
+
+def workspace_size(params) -> int:
+    return int(_lib.lib().ssd_scan_fwd_workspace_size(byref(params)))
+
+
+def uses_tensor_cores(params) -> bool:
+    return bool(_lib.lib().ssd_scan_uses_tensor_cores(byref(params)))
+
+
+def ssd_scan_forward(u, A, B, C, delta_raw, delta_bias=None, h_init=None, length=None, chunk_size=256,
+                     use_delta_softplus=True, delta_limit=(0.0, INF), is_causal=True, D=None, z=None,
+                     cu_seqlens=None, impl: str = "auto", out: Optional[Sequence[torch.Tensor]] = None,
+                     workspace: Optional[torch.Tensor] = None, events=None):
+    """Fused SSD forward. Returns ``(y, h_last)``.
+
+    ``y`` is fp32 (the reference contract, ``forward.py:200``) unless ``D`` or ``z``
+    is given, in which case the epilogue ``(y + D*u) * silu(z)`` is applied and
+    ``y`` has ``u``'s dtype. ``is_causal`` does not change the result (the reference
+    hardcodes causal chunk_scan, ``forward.py:213``). With ``cu_seqlens`` (packed
+    mode, b = 1) ``h_last`` is ``(nseq, H, P, N)``.
+    """
+    b, L, H, P = u.shape
+    N = B.shape[3]
+    dev = check_cuda([u, A, B, C, delta_raw, delta_bias, h_init, length, D, z, cu_seqlens],
+                     ["u", "A", "B", "C", "delta_raw", "delta_bias", "h_init", "length", "D", "z", "cu_seqlens"])
+    u, B, C, delta_raw = to_contiguous(u), to_contiguous(B), to_contiguous(C), to_contiguous(delta_raw)
+    for t, n in ((B, "B"), (C, "C")):
+        if t.dtype != u.dtype:
+            raise ValueError(f"[{n}] dtype {t.dtype} differs from u's {u.dtype}")
+    p, keep, y_dtype = ssd_scan_params(u, A, B, C, delta_raw, delta_bias, h_init, length, chunk_size,
+                                       use_delta_softplus, delta_limit, D, z, cu_seqlens, impl)
+    nrows = b if cu_seqlens is None else cu_seqlens.numel() - 1
+    if out is None:
+        y = torch.empty(b, L, H, P, device=dev, dtype=y_dtype)
+        h_last = torch.empty(nrows, H, P, N, device=dev, dtype=torch.float32)
+    else:
+        y, h_last = out
+    need = workspace_size(p)
+    if need == 0:
+        raise ValueError("invalid SSD geometry (sizes, heads/groups, chunk_size <= 256)")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=dev, dtype=torch.uint8)
+    p.y, p.h_last = _lib.ptr(y), _lib.ptr(h_last)
+    p.workspace, p.workspace_bytes = _lib.ptr(workspace), workspace.numel()
+    if events is not None:
+        for i, e in enumerate(events):
+            p.events[i] = None if e is None else e
+    _lib.check(_lib.lib().ssd_scan_fwd(byref(p), _stream(dev)), "ssd_scan_forward")
+    del keep
+    return y, h_last
+
+
+def ssu_forward(u, A, B, C, delta_raw, delta_bias, h, use_delta_softplus=True, delta_limit=(0.0, INF),
+                D=None, z=None, y=None):
+    """One-token state update; ``h`` is updated in place. Returns ``(y, h)`` with ``y``
+    in ``u``'s dtype (``ssu/forward.py:34``)."""
+    b, H, P = u.shape
+    G, N = B.shape[1], B.shape[2]
+    dev = check_cuda([u, A, B, C, delta_raw, delta_bias, h, D, z],
+                     ["u", "A", "B", "C", "delta_raw", "delta_bias", "h", "D", "z"])
+    u, B, C, delta_raw = to_contiguous(u), to_contiguous(B), to_contiguous(C), to_contiguous(delta_raw)
+    for t, n in ((B, "B"), (C, "C")):
+        if t.dtype != u.dtype:
+            raise ValueError(f"[{n}] dtype {t.dtype} differs from u's {u.dtype}")
+    A = to_contiguous(A.float())
+    delta_bias = None if delta_bias is None else to_contiguous(delta_bias.float())
+    D = None if D is None else to_contiguous(D.float())
+    if z is not None:
+        if z.dtype != u.dtype:
+            raise ValueError(f"[z] dtype {z.dtype} differs from u's {u.dtype}")
+        z = to_contiguous(z)
+    if h.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError(f"[h] unsupported state dtype {h.dtype}; expected float32 or bfloat16")
+    if y is None:
+        y = torch.empty_like(u)
+    st = _lib.lib().ssu_fwd(
+        _lib.ptr(u), _lib.ptr(A), _lib.ptr(B), _lib.ptr(C), _lib.ptr(delta_raw), _lib.ptr(delta_bias),
+        _lib.ptr(h), _lib.ptr(y), _lib.ptr(D), _lib.ptr(z), b, H, P, N, G,
+        _lib.dtype_code(u.dtype, "u"), _lib.dtype_code(delta_raw.dtype, "delta_raw"),
+        _lib.dtype_code(h.dtype, "h"), _lib.dtype_code(y.dtype, "y"), int(bool(use_delta_softplus)),
+        float(delta_limit[0]), float(delta_limit[1]), _stream(dev))
+    _lib.check(st, "ssu_forward")
+    return y, h
