@@ -99,7 +99,8 @@ class ClockSampler:
     def __init__(self, device_index: int):
         self.proc = None
         try:
-            bus = torch.cuda.get_device_properties(device_index).pci_bus_id
+            pr = torch.cuda.get_device_properties(device_index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
                  "-i", bus], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
@@ -333,8 +334,10 @@ def run_ours(args, rank, world, local):
     bytes_ = [cums_bytes, state_bytes, pass_bytes, 0, scan_bytes]
     stages = {}
     for n_, ms_, by in zip(names, stage_ms, bytes_):
-        if n_ == "bmm_chunk" and tc:
-            continue
+        if tc and n_ in ("bmm_chunk", "chunk_cumsum"):
+            continue  # fused: cumsum into chunk_state, bmm into chunk_scan
+        if tc and n_ == "chunk_state":
+            by += cums_bytes
         gbs = by / (ms_ / 1e3) / 1e9 if ms_ > 0 else None
         stages[n_] = {"us": ms_ * 1e3, "alg_bytes": by, "gbs": gbs, "frac": (gbs / hbm_peak) if gbs else None}
     dom = max(stages, key=lambda k: stages[k]["us"])

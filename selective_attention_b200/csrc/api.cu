@@ -203,12 +203,12 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
                                               w.rows, w.count));
     if (st) return st;
   }
-  if ((st = cuda_status(launch_chunk_cumsum(c, p->dt_dtype, p->A, p->delta_raw, p->delta_bias, w.dt, w.cum))))
-    return st;
-  record(p, 1, s);
   int tms = 0;
   if (tc) {
-    cudaError_t e = launch_tc_chunk_state(c, p->x_dtype, p->u, p->B, w.dt, w.cum, w.states, &tms);
+    // chunk_cumsum is fused into the tensor-core chunk_state (events [1] and [2] coincide).
+    record(p, 1, s);
+    cudaError_t e = launch_tc_chunk_state(c, p->x_dtype, p->dt_dtype, p->u, p->B, p->A, p->delta_raw,
+                                          p->delta_bias, w.dt, w.cum, w.states, &tms);
     if (tms) return SSD_ERR_NO_TENSOR_MAP;
     if ((st = cuda_status(e))) return st;
     record(p, 2, s);
@@ -216,12 +216,15 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
       return st;
     record(p, 3, s);
     record(p, 4, s);
-    e = launch_tc_chunk_scan(c, p->x_dtype, p->y_dtype, p->u, w.dt, w.cum, p->B, p->C, w.prev16, p->D, p->z, p->y,
-                             &tms);
+    e = launch_tc_chunk_scan(c, p->x_dtype, p->y_dtype, p->u, p->A, w.dt, w.cum, p->B, p->C, w.prev16, p->D, p->z,
+                             p->y, &tms);
     if (tms) return SSD_ERR_NO_TENSOR_MAP;
     if ((st = cuda_status(e))) return st;
     record(p, 5, s);
   } else {
+    if ((st = cuda_status(launch_chunk_cumsum(c, p->dt_dtype, p->A, p->delta_raw, p->delta_bias, w.dt, w.cum))))
+      return st;
+    record(p, 1, s);
     if ((st = cuda_status(launch_simt_chunk_state(c, p->x_dtype, p->u, p->B, w.dt, w.cum, w.states)))) return st;
     record(p, 2, s);
     if ((st = cuda_status(launch_state_passing(c, w.states, nullptr, SSD_F32, w.cum, p->h_init, p->h_last))))
@@ -265,7 +268,8 @@ int ssd_chunk_state_fwd(const ssd_params* p, void* stream) {
   if (use_tc(p, g)) {
     if (!aligned16(p->u) || !aligned16(p->B)) return SSD_ERR_INVALID_ARGUMENT;
     int tms = 0;
-    cudaError_t e = launch_tc_chunk_state(c, p->x_dtype, p->u, p->B, p->dt, p->cum, p->states, &tms);
+    cudaError_t e = launch_tc_chunk_state(c, p->x_dtype, SSD_F32, p->u, p->B, nullptr, nullptr, nullptr, p->dt,
+                                          p->cum, p->states, &tms);
     if (tms) return SSD_ERR_NO_TENSOR_MAP;
     return cuda_status(e);
   }

@@ -75,6 +75,8 @@ __device__ __forceinline__ float dt_transform(float d, int use_softplus, float d
 }
 
 __device__ __forceinline__ float silu(float z) { return z / (1.0f + expf(-z)); }
+// Same function through the fast intrinsics, for epilogues that round to 16 bits.
+__device__ __forceinline__ float silu_fast(float z) { return __fdividef(z, 1.0f + __expf(-z)); }
 
 // ---------------------------------------------------------------------------
 // Chunk map: chunk k of the scan -> (row, chunk-in-row, first token, limits).

@@ -37,10 +37,12 @@ unsigned int fetch_error_simt(cudaStream_t s);
 
 // ssd_tc.cu (tcgen05 + TMA; bf16/fp16 inputs, P = 64, N = 128, cs = 256; prev16 in the input type)
 bool tc_supported(int x_dtype, int P, int N, int cs);
-cudaError_t launch_tc_chunk_state(const LaunchCtx& c, int x_dtype, const void* u, const void* B, const float* dt,
-                                  const float* cum, float* states, int* tmap_status);
-cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, const void* u, const float* dt,
-                                 const float* cum, const void* B, const void* C, const void* prev16,
+// delta_raw == NULL: dt / cum are inputs; otherwise chunk_cumsum is fused in and they are written.
+cudaError_t launch_tc_chunk_state(const LaunchCtx& c, int x_dtype, int dt_dtype, const void* u, const void* B,
+                                  const float* A, const void* delta_raw, const float* delta_bias, float* dt,
+                                  float* cum, float* states, int* tmap_status);
+cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, const void* u, const float* A,
+                                 const float* dt, const float* cum, const void* B, const void* C, const void* prev16,
                                  const float* D, const void* z, void* y, int* tmap_status);
 unsigned int fetch_error_tc(cudaStream_t s);
 

@@ -9,64 +9,52 @@ namespace ssdb200 {
 
 // ===========================================================================
 // chunk_cumsum: ssd_scan/forward_kernel.py:19-87.
-// One CTA per (chunk, 32-head slice). The (cs x 32) slice of delta_raw is read
-// coalesced into shared memory, transformed (bias, softplus, clamp, length mask),
-// then each warp scans whole heads: 8 tokens per lane sequentially, lane totals
-// with a shuffle scan. Writes dt and cum, both (nchunks, H, cs).
+// One warp per (chunk, head): lane i owns tokens [i*E, i*E + E), E = ceil(cs/32),
+// loads and transforms them (bias, softplus, clamp, length mask), scans them
+// sequentially and adds the exclusive shuffle scan of the lane totals. Writes dt
+// and cum, both (nchunks, H, cs).
 // ===========================================================================
 template <typename DT>
 __global__ void __launch_bounds__(256) chunk_cumsum_kernel(
     const float* __restrict__ A, const DT* __restrict__ delta_raw, const float* __restrict__ delta_bias,
     float* __restrict__ dt_out, float* __restrict__ cum_out, ChunkMap cm, int H, int use_sp,
     float dmin, float dmax) {
-  __shared__ float tile[256][33];
   const int k = blockIdx.x;
   ChunkInfo ci;
   if (!chunk_info(cm, k, ci)) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y * 8 + warp;
+  if (h >= H) return;
   const int cs = cm.cs;
-  const int h0 = blockIdx.y * 32;
-  const int nh = min(32, H - h0);
-  const int tid = threadIdx.x;
-  for (int idx = tid; idx < cs * 32; idx += 256) {
-    const int t = idx >> 5, hh = idx & 31;
-    float v = 0.f;
-    if (t < ci.vlim && hh < nh) {
-      float d = Ld<DT>::f(delta_raw + (ci.tok0 + t) * (long long)H + h0 + hh);
-      if (delta_bias) d += delta_bias[h0 + hh];
-      v = dt_transform(d, use_sp, dmin, dmax);
-    }
-    tile[t][hh] = v;
-  }
-  __syncthreads();
-  const int warp = tid >> 5, lane = tid & 31;
   const int E = (cs + 31) >> 5;  // tokens per lane (<= 8)
-  for (int hh = warp; hh < nh; hh += 8) {
-    const float a = A[h0 + hh];
-    float vals[8];
-    float run = 0.f;
+  const float a = A[h];
+  const float bias = delta_bias ? delta_bias[h] : 0.f;
+  float dv[8], vals[8];
+  float run = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int t = lane * E + e;
-      float v = (e < E && t < cs) ? tile[t][hh] * a : 0.f;
-      run += v;
-      vals[e] = run;
-    }
-    // inclusive scan of lane totals
-    float incl = run;
+  for (int e = 0; e < 8; ++e) {
+    const int t = lane * E + e;
+    float v = 0.f;
+    if (e < E && t < ci.vlim)
+      v = dt_transform(Ld<DT>::f(delta_raw + (ci.tok0 + t) * (long long)H + h) + bias, use_sp, dmin, dmax);
+    dv[e] = v;
+    run += v * a;
+    vals[e] = run;
+  }
+  float incl = run;
 #pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      float o = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += o;
-    }
-    const float excl = incl - run;
-    const long long base = ((long long)k * H + h0 + hh) * cs;
+  for (int off = 1; off < 32; off <<= 1) {
+    const float o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  const float excl = incl - run;
+  const long long base = ((long long)k * H + h) * cs;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int t = lane * E + e;
-      if (e < E && t < cs) {
-        dt_out[base + t] = tile[t][hh];
-        cum_out[base + t] = excl + vals[e];
-      }
+  for (int e = 0; e < 8; ++e) {
+    const int t = lane * E + e;
+    if (e < E && t < cs) {
+      dt_out[base + t] = dv[e];
+      cum_out[base + t] = excl + vals[e];
     }
   }
 }
@@ -328,7 +316,7 @@ __global__ void __launch_bounds__(256) simt_chunk_scan_kernel(
 template <typename DT>
 static cudaError_t launch_cumsum_t(const LaunchCtx& c, const float* A, const void* dr, const float* bias,
                                    float* dt, float* cum) {
-  dim3 grid(c.nchunks_max, (unsigned)((c.H + 31) / 32));
+  dim3 grid(c.nchunks_max, (unsigned)((c.H + 7) / 8));
   chunk_cumsum_kernel<DT><<<grid, 256, 0, c.stream>>>(A, (const DT*)dr, bias, dt, cum, c.cm, c.H, c.use_sp,
                                                       c.dmin, c.dmax);
   return cudaGetLastError();

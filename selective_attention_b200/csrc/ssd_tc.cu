@@ -1,23 +1,31 @@
-// ssd_tc.cu - tensor-core (tcgen05 + TMA) chunk_state and chunk_scan for 16-bit
-// inputs with headdim 64, dstate 128, chunk 256.
+// ssd_tc.cu - tensor-core (tcgen05 + TMA) SSD stages for 16-bit inputs with
+// headdim 64, dstate 128, chunk 256.
 //
-// chunk_state (ssd_scan/forward_kernel.py:107-185), one CTA per (head, chunk):
-//   S^T[n, p] = sum_l B[l, n] * (x[l, p] * w_l),  w_l = exp(min(cum_last - cum_l, 0)) * dt_l
-//   M = 128 (dstate), N = 64 (headdim), K = 256 tokens, both operands MN-major
-//   (token rows of 128 B as TMA lands them); x is scaled by w_l in shared memory.
+// chunk_state (ssd_scan/forward_kernel.py:19-87 chunk_cumsum fused with :107-185),
+// one CTA (4 warps) per (head, chunk), ~52 KB of shared memory (4 CTAs per SM):
+//   dt, cum for the chunk's 256 tokens (shuffle scan), written for chunk_scan and
+//   state_passing; then in two 128-token phases
+//   S^T[n, p] += sum_l B[l, n] * (x[l, p] * w_l),  w_l = exp(min(cum_last - cum_l, 0)) * dt_l
+//   M = 128 (dstate), N = 64 (headdim), K = 128 tokens per phase; both operands
+//   MN-major (token rows of 128 B as TMA lands them); x is scaled by w_l in place.
 //
 // chunk_scan (ssd_scan/forward_kernel.py:350-455 with bmm_chunk :270-328 fused),
-// one CTA per (128-row half of a chunk, head, chunk):
-//   MMA1  CB[l, s]   = C[l, :] . B[s, :]            M 128, N 128|256, K 128 (K-major)
-//   CB -> registers: M[l, s] = CB * exp(min(cum_l - cum_s, 0)) * dt_s  (s <= l, s < lim)
-//         -> bf16/fp16, written back over the B tile in the K-major layout
-//   MMA3  Yoff[l, p] = C[l, :] . prev[p, :]         M 128, N 64, K 128 (K-major)
-//   MMA2  Yin[l, p]  = sum_s M[l, s] x[s, p]         M 128, N 64, K 128|256 (x MN-major)
+// one CTA (8 warps) per (128-row half m of a chunk, head, chunk), ~100 KB of shared
+// memory (2 CTAs per SM). Rows l of half m see tokens s in [0, 128(m+1)), taken in
+// 128-token phases j = 0..m that reuse one B/x buffer:
+//   MMA1  CB_j[l, s]  = C[l, :] . B[s, :]          M 128, N 128, K 128 (K-major)
+//   CB_j -> M_j[l, s] = CB * decay(l, s) * dt_s  (bf16/fp16, K-major, over the B tile)
+//   MMA2  Yin[l, p]  += sum_s M_j[l, s] x[s, p]    M 128, N 64, K 128 (x MN-major)
+//   MMA3  Yoff[l, p]  = C[l, :] . prev[p, :]        M 128, N 64, K 128 (phase 0)
 //   y = exp(cum_l) * Yoff + Yin (+ D x) (* silu z)
+// decay(l, s) = exp(min(cum_l - cum_s, 0)) with s <= l. In an off-diagonal phase
+// (j < m, every s < l) it is evaluated as exp(cum_l - cum_r) * exp(cum_r - cum_s)
+// with r = 128j + 127, both factors <= 1, whenever cum is non-increasing (A <= 0
+// and dt >= 0: then min(., 0) is the identity); otherwise element by element.
 //
-// All shared-memory tiles use the 128-byte swizzle; TMEM accumulators are fp32.
-// Every mbarrier wait is bounded (sm100::mbar_wait) and a kernel that gives up
-// records a site code in the error flag and returns after releasing TMEM.
+// All tiles use the 128-byte swizzle; accumulators are fp32 in TMEM. Every mbarrier
+// wait is bounded: a CTA that gives up records a site code in the error flag and
+// returns after its copies/MMAs get a last bounded wait and TMEM is released.
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -44,39 +52,56 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// ---------------------------------------------------------------------------
-// chunk_state
-// ---------------------------------------------------------------------------
-constexpr int kStateSmem = 65536 + 32768 + 1024 + 64 + 1024;
+// Scale the 16-byte chunk (8 elements of T16) by w.
+template <typename T16>
+__device__ __forceinline__ uint4 scale8(uint4 a, float w) {
+  float2 f;
+  uint4 v;
+  f = unpack2<T16>(a.x); v.x = pack2<T16>(f.x * w, f.y * w);
+  f = unpack2<T16>(a.y); v.y = pack2<T16>(f.x * w, f.y * w);
+  f = unpack2<T16>(a.z); v.z = pack2<T16>(f.x * w, f.y * w);
+  f = unpack2<T16>(a.w); v.w = pack2<T16>(f.x * w, f.y * w);
+  return v;
+}
 
-template <bool BF16>
-__global__ void __launch_bounds__(128, 1) tc_chunk_state_kernel(const __grid_constant__ CUtensorMap tm_x,
-                                                                const __grid_constant__ CUtensorMap tm_b,
-                                                                const float* __restrict__ dt,
-                                                                const float* __restrict__ cum,
-                                                                float* __restrict__ states, ChunkMap cm, int H,
-                                                                int hpg) {
+// ===========================================================================
+// chunk_state (+ chunk_cumsum)
+// ===========================================================================
+constexpr int kStateSmem = 32768 + 16384 + 1024 + 1024 + 64 + 64 + 1024;
+
+// FUSE: compute dt / cum from delta_raw and write them; otherwise read them.
+template <bool BF16, typename DT, bool FUSE>
+__global__ void __launch_bounds__(128) tc_chunk_state_kernel(
+    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_b,
+    const float* __restrict__ A, const DT* __restrict__ delta_raw, const float* __restrict__ delta_bias,
+    float* __restrict__ dt_io, float* __restrict__ cum_io, float* __restrict__ states, ChunkMap cm, int H,
+    int hpg, int use_sp, float dmin, float dmax) {
   using T16 = typename T16Of<BF16>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* sB = smem;            // 2 x (256 rows x 128 B): dstate halves
-  uint8_t* sX = smem + 65536;    // 256 rows x 128 B
-  float* sW = reinterpret_cast<float*>(smem + 98304);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 98304 + 1024);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  uint8_t* sB = smem;            // 2 x (128 rows x 128 B): dstate halves, one 128-token phase
+  uint8_t* sX = smem + 32768;    // 128 rows x 128 B
+  float* sW = reinterpret_cast<float*>(smem + 49152);
+  float* sCum = sW + 256;
+  float* sWarp = sCum + 256;     // 4 warp totals
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sWarp + 16);  // tma0, tma1, mma0, mma1
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 4);
 
   const int h = blockIdx.x, k = blockIdx.y;
   ChunkInfo ci;
   if (!chunk_info(cm, k, ci)) return;
   const int g = h / hpg;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t bar_tma = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
+  uint32_t bar[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) bar[i] = smem_u32(&bars[i]);
+  const bool two_phases = ci.lim > 128;
 
   if (tid == 0) {
     prefetch_tmap(&tm_x);
     prefetch_tmap(&tm_b);
-    mbar_init(bar_tma, 1);
-    mbar_init(bar_mma, 1);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) mbar_init(bar[i], 1);
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), 64);
@@ -84,59 +109,110 @@ __global__ void __launch_bounds__(128, 1) tc_chunk_state_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  const int t0 = (int)ci.tok0;
 
   if (tid == 0) {
-    mbar_expect_tx(bar_tma, 3u * 32768u);
-    const int t0 = (int)ci.tok0;
-    tma_load_3d(smem_u32(sX), &tm_x, 0, h, t0, bar_tma);
-    tma_load_3d(smem_u32(sB), &tm_b, 0, g, t0, bar_tma);
-    tma_load_3d(smem_u32(sB + 32768), &tm_b, 64, g, t0, bar_tma);
+    mbar_expect_tx(bar[0], 49152u);
+    tma_load_3d(smem_u32(sX), &tm_x, 0, h, t0, bar[0]);
+    tma_load_3d(smem_u32(sB), &tm_b, 0, g, t0, bar[0]);
+    tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, g, t0, bar[0]);
   }
-  const float* dtk = dt + ((long long)k * H + h) * 256;
-  const float* cmk = cum + ((long long)k * H + h) * 256;
-  const float clast = cmk[255];
-  for (int l = tid; l < 256; l += 128) {
-    float w = 0.f;
-    if (l < ci.lim) w = __expf(fminf(clast - cmk[l], 0.f)) * dtk[l];
-    sW[l] = w;
+
+  // ---- chunk_cumsum for (k, h): tokens 2*tid, 2*tid+1 ----
+  const long long io = ((long long)k * H + h) * 256 + 2 * tid;
+  float d[2], cum0, cum1;
+  if constexpr (FUSE) {
+    const float a = A[h];
+    const float bias = delta_bias ? delta_bias[h] : 0.f;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int l = 2 * tid + e;
+      d[e] = 0.f;
+      if (l < ci.vlim)
+        d[e] = dt_transform(Ld<DT>::f(delta_raw + (ci.tok0 + l) * (long long)H + h) + bias, use_sp, dmin, dmax);
+    }
+    const float c0 = d[0] * a;
+    const float tot = c0 + d[1] * a;
+    float incl = tot;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    if (lane == 31) sWarp[warp] = incl;
+    __syncthreads();
+    float wbase = 0.f;
+    for (int w = 0; w < warp; ++w) wbase += sWarp[w];
+    const float excl = wbase + incl - tot;
+    cum0 = excl + c0;
+    cum1 = excl + tot;
+    *reinterpret_cast<float2*>(dt_io + io) = make_float2(d[0], d[1]);
+    *reinterpret_cast<float2*>(cum_io + io) = make_float2(cum0, cum1);
+  } else {
+    const float2 dv = *reinterpret_cast<const float2*>(dt_io + io);
+    const float2 cv = *reinterpret_cast<const float2*>(cum_io + io);
+    d[0] = dv.x;
+    d[1] = dv.y;
+    cum0 = cv.x;
+    cum1 = cv.y;
+  }
+  sCum[2 * tid] = cum0;
+  sCum[2 * tid + 1] = cum1;
+  __syncthreads();
+  {
+    const float clast = sCum[255];
+    sW[2 * tid] = (2 * tid < ci.lim) ? __expf(fminf(clast - cum0, 0.f)) * d[0] : 0.f;
+    sW[2 * tid + 1] = (2 * tid + 1 < ci.lim) ? __expf(fminf(clast - cum1, 0.f)) * d[1] : 0.f;
   }
   __syncthreads();
-  bool tma_ok = mbar_wait(bar_tma, 0, kSiteStateTma);
-  if (tma_ok) {
-    // x rows scaled by w_l in place; rows past `lim` become exact zeros.
-    for (int q = tid; q < 2048; q += 128) {
-      uint4* pch = reinterpret_cast<uint4*>(sX + q * 16);
-      const int l = q >> 3;
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (l < ci.lim) {
+
+  const uint32_t idesc = idesc_f16(128, 64, BF16, /*a_mn=*/true, /*b_mn=*/true);
+  bool ok = true;
+  bool pend_tma = true, pend_mma = false;
+  int cur_mma_bar = 2;
+  for (int ph = 0; ph < (two_phases ? 2 : 1); ++ph) {
+    bool w_ok = mbar_wait(bar[ph], 0, kSiteStateTma);
+    if (w_ok) {
+      // x rows scaled by w_l in place (rows past `lim` have w = 0 and become exact zeros).
+      for (int q = tid; q < 1024; q += 128) {
+        uint4* pch = reinterpret_cast<uint4*>(sX + q * 16);
+        const int l = ph * 128 + (q >> 3);
         const float w = sW[l];
-        uint4 a = *pch;
-        float2 f;
-        f = unpack2<T16>(a.x); v.x = pack2<T16>(f.x * w, f.y * w);
-        f = unpack2<T16>(a.y); v.y = pack2<T16>(f.x * w, f.y * w);
-        f = unpack2<T16>(a.z); v.z = pack2<T16>(f.x * w, f.y * w);
-        f = unpack2<T16>(a.w); v.w = pack2<T16>(f.x * w, f.y * w);
+        *pch = (w == 0.f) ? make_uint4(0u, 0u, 0u, 0u) : scale8<T16>(*pch, w);
       }
-      *pch = v;
     }
-  }
-  fence_proxy_async_smem();
-  const bool ok = __syncthreads_and(tma_ok) != 0;
-  if (ok && tid == 0) {
-    tc_fence_after();
-    const uint32_t idesc = idesc_f16(128, 64, BF16, /*a_mn=*/true, /*b_mn=*/true);
-    const uint32_t a0 = smem_u32(sB), b0 = smem_u32(sX);
+    fence_proxy_async_smem();
+    ok = __syncthreads_and(w_ok) != 0;
+    if (!ok) break;
+    pend_tma = false;
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(sB), b0 = smem_u32(sX);
 #pragma unroll
-    for (int ks = 0; ks < 16; ++ks) {
-      const uint64_t ad = sdesc_sw128(a0 + ks * 2048, 32768, 1024);
-      const uint64_t bd = sdesc_sw128(b0 + ks * 2048, 16, 1024);
-      umma_f16(tmem, ad, bd, idesc, ks > 0 ? 1u : 0u);
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t ad = sdesc_sw128(a0 + ks * 2048, 16384, 1024);
+        const uint64_t bd = sdesc_sw128(b0 + ks * 2048, 16, 1024);
+        umma_f16(tmem, ad, bd, idesc, (ph > 0 || ks > 0) ? 1u : 0u);
+      }
+      umma_commit(bar[2 + ph]);
     }
-    umma_commit(bar_mma);
+    pend_mma = true;
+    cur_mma_bar = 2 + ph;
+    if (ph == 0 && two_phases) {
+      // The second phase reuses the buffers: wait for this phase's MMAs first.
+      if (tid == 0) {
+        if (mbar_wait(bar[2], 0, kSiteStateMma)) {
+          mbar_expect_tx(bar[1], 49152u);
+          tma_load_3d(smem_u32(sX), &tm_x, 0, h, t0 + 128, bar[1]);
+          tma_load_3d(smem_u32(sB), &tm_b, 0, g, t0 + 128, bar[1]);
+          tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, g, t0 + 128, bar[1]);
+        }
+      }
+      pend_tma = true;
+    }
   }
-  __syncwarp();
   bool mma_ok = false;
-  if (ok) mma_ok = mbar_wait(bar_mma, 0, kSiteStateMma);
+  if (ok) mma_ok = mbar_wait(bar[cur_mma_bar], 0, kSiteStateMma);
   tc_fence_after();
   if (ok && __syncthreads_and(mma_ok)) {
     const int n = warp * 32 + lane;
@@ -150,56 +226,69 @@ __global__ void __launch_bounds__(128, 1) tc_chunk_state_kernel(const __grid_con
       for (int j = 0; j < 32; ++j) out[(half * 32 + j) * 128 + n] = __uint_as_float(r[j]);
     }
   } else if (tid == 0) {
-    // Give in-flight copies / MMAs a last bounded chance to land before exit.
-    if (!tma_ok) mbar_wait(bar_tma, 0, kSiteStateTma);
-    if (ok && !mma_ok) mbar_wait(bar_mma, 0, kSiteStateMma);
+    // Let in-flight copies / MMAs land (bounded) before the CTA exits.
+    if (pend_tma) mbar_wait(bar[two_phases ? 1 : 0], 0, kSiteStateTma);
+    if (pend_mma) mbar_wait(bar[cur_mma_bar], 0, kSiteStateMma);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 64);
 }
 
-// ---------------------------------------------------------------------------
+// ===========================================================================
 // chunk_scan (+ bmm_chunk)
-// ---------------------------------------------------------------------------
-constexpr int kScanSmem = 32768 + 65536 + 32768 + 16384 + 2048 + 64 + 1024;
+// ===========================================================================
+constexpr int kScanTileBytes = 32768 + 32768 + 16384 + 16384;
+constexpr int kScanSmem = kScanTileBytes + 2048 + 512 + 256 + 256 + 1024;
 
 template <bool BF16, typename YT>
-__global__ void __launch_bounds__(128, 1) tc_chunk_scan_kernel(
+__global__ void __launch_bounds__(256) tc_chunk_scan_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c,
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_h,
-    const float* __restrict__ dt, const float* __restrict__ cum, const float* __restrict__ D,
-    const typename T16Of<BF16>::type* __restrict__ z, YT* __restrict__ y, ChunkMap cm, int H, int hpg) {
+    const float* __restrict__ A, const float* __restrict__ dt, const float* __restrict__ cum,
+    const float* __restrict__ D, const typename T16Of<BF16>::type* __restrict__ z, YT* __restrict__ y, ChunkMap cm,
+    int H, int hpg, int dt_nonneg) {
   using T16 = typename T16Of<BF16>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sC = smem;              // 2 x (128 rows x 128 B): dstate halves of C rows [128m, 128m+128)
-  uint8_t* sB = smem + 32768;      // 2 x (S rows x 128 B): dstate halves of B rows [0, S); later M tiles
-  uint8_t* sX = smem + 98304;      // S rows x 128 B: x rows [0, S)
-  uint8_t* sH = smem + 131072;     // 2 x (64 rows x 128 B): dstate halves of prev[p, :]
-  float* sDt = reinterpret_cast<float*>(smem + 147456);
+  uint8_t* sB = smem + 32768;      // 2 x (128 rows x 128 B): B rows of the phase; then M (2 s-blocks of 64)
+  uint8_t* sX = smem + 65536;      // 128 rows x 128 B: x rows of the phase
+  uint8_t* sH = smem + 81920;      // 2 x (64 rows x 128 B): dstate halves of prev[p, :]
+  float* sDt = reinterpret_cast<float*>(smem + kScanTileBytes);
   float* sCum = sDt + 256;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 147456 + 2048);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3);
+  float* sColf = sCum + 256;       // 128
+  float* sD = sColf + 128;         // 64
+  int* sBlkOk = reinterpret_cast<int*>(sD + 64);  // 4 (+4 pad)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sBlkOk + 8);  // tma[2], m1[2], m2[2]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 6);
 
   const int m = blockIdx.x & 1, h = blockIdx.x >> 1, k = blockIdx.y;
   ChunkInfo ci;
   if (!chunk_info(cm, k, ci)) return;
   const int lbase = 128 * m;
   if (lbase >= ci.lim) return;  // no token of this half belongs to the row
-  const int S = 128 * (m + 1);
   const int g = h / hpg;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t bar_tma = smem_u32(&bars[0]), bar_m1 = smem_u32(&bars[1]), bar_m2 = smem_u32(&bars[2]);
+  const int quad = warp & 3, ch = warp >> 2;  // TMEM lane quadrant, column half
+  const int r = quad * 32 + lane;             // row within the half
+  const int l = lbase + r;                    // row within the chunk
+  uint32_t bt[2], b1[2], b2[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    bt[i] = smem_u32(&bars[i]);
+    b1[i] = smem_u32(&bars[2 + i]);
+    b2[i] = smem_u32(&bars[4 + i]);
+  }
+  const uint32_t T_CB = 0, T_YIN = 128, T_YOFF = 192;
 
   if (tid == 0) {
     prefetch_tmap(&tm_x);
     prefetch_tmap(&tm_c);
     prefetch_tmap(&tm_b);
     prefetch_tmap(&tm_h);
-    mbar_init(bar_tma, 1);
-    mbar_init(bar_m1, 1);
-    mbar_init(bar_m2, 1);
+#pragma unroll
+    for (int i = 0; i < 6; ++i) mbar_init(smem_u32(&bars[i]), 1);
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
@@ -207,185 +296,252 @@ __global__ void __launch_bounds__(128, 1) tc_chunk_scan_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  const uint32_t tq = tmem + ((uint32_t)(quad * 32) << 16);  // this warp's lane quadrant
+  const int t0 = (int)ci.tok0;
 
   if (tid == 0) {
-    const uint32_t bytes = 32768u + (uint32_t)S * 256u + (uint32_t)S * 128u + 16384u;
-    mbar_expect_tx(bar_tma, bytes);
-    const int t0 = (int)ci.tok0;
-    tma_load_3d(smem_u32(sC), &tm_c, 0, g, t0 + lbase, bar_tma);
-    tma_load_3d(smem_u32(sC + 16384), &tm_c, 64, g, t0 + lbase, bar_tma);
-    for (int rb = 0; rb <= m; ++rb) {
-      tma_load_3d(smem_u32(sB + rb * 16384), &tm_b, 0, g, t0 + 128 * rb, bar_tma);
-      tma_load_3d(smem_u32(sB + S * 128 + rb * 16384), &tm_b, 64, g, t0 + 128 * rb, bar_tma);
-      tma_load_3d(smem_u32(sX + rb * 16384), &tm_x, 0, h, t0 + 128 * rb, bar_tma);
-    }
-    tma_load_3d(smem_u32(sH), &tm_h, 0, 0, k * H + h, bar_tma);
-    tma_load_3d(smem_u32(sH + 8192), &tm_h, 64, 0, k * H + h, bar_tma);
+    mbar_expect_tx(bt[0], 32768u + 16384u + 32768u + 16384u);
+    tma_load_3d(smem_u32(sC), &tm_c, 0, g, t0 + lbase, bt[0]);
+    tma_load_3d(smem_u32(sC + 16384), &tm_c, 64, g, t0 + lbase, bt[0]);
+    tma_load_3d(smem_u32(sH), &tm_h, 0, 0, k * H + h, bt[0]);
+    tma_load_3d(smem_u32(sH + 8192), &tm_h, 64, 0, k * H + h, bt[0]);
+    tma_load_3d(smem_u32(sB), &tm_b, 0, g, t0, bt[0]);
+    tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, g, t0, bt[0]);
+    tma_load_3d(smem_u32(sX), &tm_x, 0, h, t0, bt[0]);
   }
   {
     const float* dtk = dt + ((long long)k * H + h) * 256;
     const float* cmk = cum + ((long long)k * H + h) * 256;
-    for (int i = tid; i < 256; i += 128) {
-      sDt[i] = dtk[i];
-      sCum[i] = cmk[i];
-    }
+    sDt[tid] = dtk[tid];
+    sCum[tid] = cmk[tid];
+    if (tid < 64) sD[tid] = D ? D[h * 64 + tid] : 0.f;
   }
+  // cum non-increasing => min(cum_l - cum_s, 0) = cum_l - cum_s for s <= l
+  const bool mono = dt_nonneg && (A[h] <= 0.f);
   __syncthreads();
-  const bool tma_ok = mbar_wait(bar_tma, 0, kSiteScanTma);
-  const bool ok0 = __syncthreads_and(tma_ok) != 0;
-
-  if (ok0 && tid == 0) {
-    tc_fence_after();
-    const uint32_t id1 = idesc_f16(128, S, BF16, false, false);
-    const uint32_t c0 = smem_u32(sC), b0 = smem_u32(sB);
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t j = ks >> 2, kk = (ks & 3) * 32;
-      const uint64_t ad = sdesc_sw128(c0 + j * 16384 + kk, 16, 1024);
-      const uint64_t bd = sdesc_sw128(b0 + j * (uint32_t)S * 128 + kk, 16, 1024);
-      umma_f16(tmem, ad, bd, id1, ks > 0 ? 1u : 0u);
-    }
-    umma_commit(bar_m1);
-  }
-  __syncwarp();
-  bool m1_ok = false;
-  if (ok0) m1_ok = mbar_wait(bar_m1, 0, kSiteScanMma1);
-  tc_fence_after();
-  const bool ok1 = ok0 && (__syncthreads_and(m1_ok) != 0);
-
-  const int r = warp * 32 + lane;  // row inside this half
-  const int l = lbase + r;         // row inside the chunk
   const float cl = sCum[l];
-  if (ok1) {
-    // x rows past `lim` -> exact zeros, so they cannot leak into Yin.
-    for (int q = tid; q < S * 8; q += 128) {
-      const int s = q >> 3;
-      if (s >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
-    }
-    const int warp_lmax = lbase + warp * 32 + 31;
-    for (int cb = 0; cb < S / 32; ++cb) {
-      const int s0 = cb * 32;
-      uint32_t v[32];
-      const bool any = s0 <= warp_lmax;  // warp-uniform
-      if (any) {
-        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + s0, v);
-        tmem_wait_ld();
-      }
-      uint32_t pk[16];
+
+  bool ok = true;
+  bool pend_tma = true, pend_m1 = false, pend_m2 = false;
+  int last_m1 = 0, last_m2 = 0;
+  const uint32_t id_kk64 = idesc_f16(128, 64, BF16, false, false);
+  const uint32_t id_kk128 = idesc_f16(128, 128, BF16, false, false);
+  const uint32_t id_km64 = idesc_f16(128, 64, BF16, false, true);
+  for (int j = 0; j <= m; ++j) {
+    const bool w_ok = mbar_wait(bt[j], 0, kSiteScanTma);
+    ok = __syncthreads_and(w_ok) != 0;
+    if (!ok) break;
+    pend_tma = false;
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t c0 = smem_u32(sC), b0 = smem_u32(sB), h0 = smem_u32(sH);
 #pragma unroll
-      for (int jj = 0; jj < 16; ++jj) {
-        const int sa = s0 + 2 * jj, sb2 = sa + 1;
-        float a = 0.f, b = 0.f;
-        if (any && sa <= l && sa < ci.lim) a = __uint_as_float(v[2 * jj]) * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
-        if (any && sb2 <= l && sb2 < ci.lim) b = __uint_as_float(v[2 * jj + 1]) * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
-        pk[jj] = pack2<T16>(a, b);
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
+        umma_f16(tmem + T_CB, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
+                 sdesc_sw128(b0 + hf * 16384 + kk, 16, 1024), id_kk128, ks > 0 ? 1u : 0u);
       }
-      uint8_t* base = sB + (s0 >> 6) * 16384;
-      const uint32_t c16 = (s0 & 63) >> 3;
+      if (j == 0) {
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
+          umma_f16(tmem + T_YOFF, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
+                   sdesc_sw128(h0 + hf * 8192 + kk, 16, 1024), id_kk64, ks > 0 ? 1u : 0u);
+        }
+      }
+      umma_commit(b1[j]);
+    }
+    pend_m1 = true;
+    last_m1 = j;
+    const int sbase = 128 * j;  // first token of this phase
+    // Column factors exp(cum_r - cum_s) * dt_s with r the last token of the 32-token
+    // block holding s (<= dt_s when cum is non-increasing), and per-block flags:
+    // a diagonal tile may use the factored form only if its row factor
+    // exp(cum_l - cum_r) <= exp(cum_first - cum_r) stays far from overflow.
+    if (tid < 128) {
+      const int s = sbase + tid;
+      const float cr = sCum[sbase + (tid | 31)];
+      sColf[tid] = mono ? __expf(cr - sCum[s]) * sDt[s] : 0.f;
+      if ((tid & 31) == 0) sBlkOk[tid >> 5] = mono && (sCum[s] - cr <= 80.f);
+    }
+    // x rows past `lim` -> exact zeros (they then cannot leak into Yin)
+    for (int q = tid; q < 1024; q += 256)
+      if (sbase + (q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
+    const bool m1_ok = mbar_wait(b1[j], 0, kSiteScanMma1);
+    tc_fence_after();
+    ok = __syncthreads_and(m1_ok) != 0;  // also publishes sColf
+    if (!ok) break;
+    pend_m1 = false;
+    // ---- CB_j (TMEM) -> M_j (smem, K-major over the B tile) ----
+    // This warp covers rows [wr0, wr0 + 32) and 32-column blocks cb = ch, ch + 2.
+    const int wr0 = lbase + quad * 32;
+    uint32_t v[2][32];
+    int kind[2];  // 0: above the diagonal (zeros), 1: factored, 2: element by element
+#pragma unroll
+    for (int cbi = 0; cbi < 2; ++cbi) {
+      const int cb = 2 * cbi + ch;
+      const int s0 = sbase + cb * 32;
+      if (s0 > wr0 + 31) {
+        kind[cbi] = 0;
+      } else {
+        const bool diag = s0 + 31 >= wr0;  // blocks are aligned, so this is the 32x32 diagonal tile
+        kind[cbi] = (diag ? sBlkOk[cb] : mono) ? 1 : 2;
+        tmem_ld32(tq + T_CB + cb * 32, v[cbi]);
+      }
+    }
+    tmem_wait_ld();
+#pragma unroll
+    for (int cbi = 0; cbi < 2; ++cbi) {
+      const int cb = 2 * cbi + ch;
+      const int s0 = sbase + cb * 32;
+      uint32_t pk[16];
+      if (kind[cbi] == 0) {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) pk[jj] = 0u;
+      } else if (kind[cbi] == 1) {
+        const float rowf = __expf(cl - sCum[s0 + 31]);
+        const float4* cf = reinterpret_cast<const float4*>(sColf + cb * 32);
+        const bool diag = s0 + 31 >= wr0;
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4) {
+          const float4 c4 = cf[q4];
+          float x0 = __uint_as_float(v[cbi][4 * q4]) * rowf * c4.x;
+          float x1 = __uint_as_float(v[cbi][4 * q4 + 1]) * rowf * c4.y;
+          float x2 = __uint_as_float(v[cbi][4 * q4 + 2]) * rowf * c4.z;
+          float x3 = __uint_as_float(v[cbi][4 * q4 + 3]) * rowf * c4.w;
+          if (diag) {
+            const int sa = s0 + 4 * q4;
+            x0 = sa <= l ? x0 : 0.f;
+            x1 = sa + 1 <= l ? x1 : 0.f;
+            x2 = sa + 2 <= l ? x2 : 0.f;
+            x3 = sa + 3 <= l ? x3 : 0.f;
+          }
+          pk[2 * q4] = pack2<T16>(x0, x1);
+          pk[2 * q4 + 1] = pack2<T16>(x2, x3);
+        }
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int sa = s0 + 2 * jj, sb2 = sa + 1;
+          float x0 = 0.f, x1 = 0.f;
+          if (sa <= l && sa < ci.lim)
+            x0 = __uint_as_float(v[cbi][2 * jj]) * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
+          if (sb2 <= l && sb2 < ci.lim)
+            x1 = __uint_as_float(v[cbi][2 * jj + 1]) * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
+          pk[jj] = pack2<T16>(x0, x1);
+        }
+      }
+      uint8_t* base = sB + (cb >> 1) * 16384;
+      const uint32_t c16 = (cb & 1) * 4;
 #pragma unroll
       for (int q = 0; q < 4; ++q)
         *reinterpret_cast<uint4*>(base + sw128_off(r, c16 + q)) =
             make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
     }
-  }
-  fence_proxy_async_smem();
-  tc_fence_before();
-  const bool ok2 = ok1 && (__syncthreads_and(ok1) != 0);
-  if (ok2 && tid == 0) {
-    tc_fence_after();
-    const uint32_t c0 = smem_u32(sC), h0 = smem_u32(sH), m0 = smem_u32(sB), x0 = smem_u32(sX);
-    const uint32_t id3 = idesc_f16(128, 64, BF16, false, false);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t m0 = smem_u32(sB), x0 = smem_u32(sX);
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t j = ks >> 2, kk = (ks & 3) * 32;
-      const uint64_t ad = sdesc_sw128(c0 + j * 16384 + kk, 16, 1024);
-      const uint64_t bd = sdesc_sw128(h0 + j * 8192 + kk, 16, 1024);
-      umma_f16(tmem, ad, bd, id3, ks > 0 ? 1u : 0u);
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t sb = ks >> 2, kk = (ks & 3) * 32;
+        umma_f16(tmem + T_YIN, sdesc_sw128(m0 + sb * 16384 + kk, 16, 1024), sdesc_sw128(x0 + ks * 2048, 16, 1024),
+                 id_km64, (j > 0 || ks > 0) ? 1u : 0u);
+      }
+      umma_commit(b2[j]);
     }
-    const uint32_t id2 = idesc_f16(128, 64, BF16, false, true);
-    for (int ks = 0; ks < S / 16; ++ks) {
-      const uint32_t sb = ks >> 2, kk = (ks & 3) * 32;
-      const uint64_t ad = sdesc_sw128(m0 + sb * 16384 + kk, 16, 1024);
-      const uint64_t bd = sdesc_sw128(x0 + ks * 2048, 16, 1024);
-      umma_f16(tmem + 64, ad, bd, id2, ks > 0 ? 1u : 0u);
+    pend_m2 = true;
+    last_m2 = j;
+    if (j < m) {
+      // next phase reuses the B/x buffers: wait for this phase's MMA2 first
+      if (tid == 0 && mbar_wait(b2[j], 0, kSiteScanMma2)) {
+        mbar_expect_tx(bt[j + 1], 32768u + 16384u);
+        const int tn = t0 + 128 * (j + 1);
+        tma_load_3d(smem_u32(sB), &tm_b, 0, g, tn, bt[j + 1]);
+        tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, g, tn, bt[j + 1]);
+        tma_load_3d(smem_u32(sX), &tm_x, 0, h, tn, bt[j + 1]);
+      }
+      pend_tma = true;
     }
-    umma_commit(bar_m2);
   }
-  __syncwarp();
+
+  // ---- epilogue: y = exp(cum_l) * Yoff + Yin (+ D x) (* silu z) ----
+  const long long tok = ci.tok0 + l;
+  const bool valid = l < ci.lim;
+  const long long yrow = (tok * H + h) * 64 + ch * 32;
+  uint4 zv[4];
+  if (z && valid) {
+    const uint4* zp = reinterpret_cast<const uint4*>(z + yrow);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) zv[q] = zp[q];
+  }
   bool m2_ok = false;
-  if (ok2) m2_ok = mbar_wait(bar_m2, 0, kSiteScanMma2);
+  if (ok) m2_ok = mbar_wait(b2[m], 0, kSiteScanMma2);
   tc_fence_after();
-  const bool ok3 = ok2 && (__syncthreads_and(m2_ok) != 0);
-  if (ok3) {
-    const float el = __expf(cl);
-    const long long tok = ci.tok0 + l;
-    const bool valid = l < ci.lim;
-    const long long yrow = (tok * H + h) * 64;
+  if (ok && __syncthreads_and(m2_ok)) {
+    uint32_t ro[32], ri[32];
+    tmem_ld32(tq + T_YOFF + ch * 32, ro);
+    tmem_ld32(tq + T_YIN + ch * 32, ri);
+    tmem_wait_ld();
+    if (valid) {
+      const float el = __expf(cl);
+      float o[32];
 #pragma unroll
-    for (int pc = 0; pc < 2; ++pc) {
-      uint32_t ro[32], ri[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + pc * 32, ro);
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + 64 + pc * 32, ri);
-      tmem_wait_ld();
-      if (valid) {
-        float o[32];
+      for (int jj = 0; jj < 32; ++jj) o[jj] = fmaf(el, __uint_as_float(ro[jj]), __uint_as_float(ri[jj]));
+      if (D) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) o[j] = fmaf(el, __uint_as_float(ro[j]), __uint_as_float(ri[j]));
-        if (D) {
+        for (int q = 0; q < 4; ++q) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(sX + sw128_off(r, ch * 4 + q));
+          const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 xv = *reinterpret_cast<const uint4*>(sX + sw128_off(l, pc * 4 + q));
-            const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = unpack2<T16>(w4[e]);
-              const int p = pc * 32 + q * 8 + 2 * e;
-              o[q * 8 + 2 * e] = fmaf(D[h * 64 + p], f.x, o[q * 8 + 2 * e]);
-              o[q * 8 + 2 * e + 1] = fmaf(D[h * 64 + p + 1], f.y, o[q * 8 + 2 * e + 1]);
-            }
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack2<T16>(w4[e]);
+            const int pi = q * 8 + 2 * e;
+            o[pi] = fmaf(sD[ch * 32 + pi], f.x, o[pi]);
+            o[pi + 1] = fmaf(sD[ch * 32 + pi + 1], f.y, o[pi + 1]);
           }
-        }
-        if (z) {
-          const uint4* zp = reinterpret_cast<const uint4*>(z + yrow + pc * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 zv = zp[q];
-            const uint32_t w4[4] = {zv.x, zv.y, zv.z, zv.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = unpack2<T16>(w4[e]);
-              o[q * 8 + 2 * e] *= silu(f.x);
-              o[q * 8 + 2 * e + 1] *= silu(f.y);
-            }
-          }
-        }
-        if constexpr (sizeof(YT) == 4) {
-          float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow + pc * 32);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-        } else {
-          uint4* yp = reinterpret_cast<uint4*>(y + yrow + pc * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            yp[q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
-                               pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
         }
       }
+      if (z) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t w4[4] = {zv[q].x, zv[q].y, zv[q].z, zv[q].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack2<T16>(w4[e]);
+            o[q * 8 + 2 * e] *= silu_fast(f.x);
+            o[q * 8 + 2 * e + 1] *= silu_fast(f.y);
+          }
+        }
+      }
+      if constexpr (sizeof(YT) == 4) {
+        float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+      } else {
+        uint4* yp = reinterpret_cast<uint4*>(y + yrow);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          yp[q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
+                             pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
+      }
     }
-  }
-  if (!ok3 && tid == 0) {
-    if (!tma_ok) mbar_wait(bar_tma, 0, kSiteScanTma);
-    if (ok0 && !m1_ok) mbar_wait(bar_m1, 0, kSiteScanMma1);
-    if (ok2 && !m2_ok) mbar_wait(bar_m2, 0, kSiteScanMma2);
+  } else if (tid == 0) {
+    // Let in-flight copies / MMAs land (bounded) before the CTA exits.
+    if (pend_tma) mbar_wait(bt[m], 0, kSiteScanTma);
+    if (pend_m1) mbar_wait(b1[last_m1], 0, kSiteScanMma1);
+    if (pend_m2) mbar_wait(b2[last_m2], 0, kSiteScanMma2);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
-// ---------------------------------------------------------------------------
+// ===========================================================================
 // Host side: tensor maps and launches
-// ---------------------------------------------------------------------------
+// ===========================================================================
 static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static bool tried = false;
@@ -419,44 +575,64 @@ bool tc_supported(int x_dtype, int P, int N, int cs) {
   return (x_dtype == SSD_BF16 || x_dtype == SSD_F16) && P == 64 && N == 128 && cs == 256;
 }
 
-cudaError_t launch_tc_chunk_state(const LaunchCtx& c, int x_dtype, const void* u, const void* B, const float* dt,
-                                  const float* cum, float* states, int* tmap_status) {
+template <bool BF16, typename DT, bool FUSE>
+static cudaError_t tc_state_launch(const LaunchCtx& c, const CUtensorMap& mx, const CUtensorMap& mb, const float* A,
+                                   const void* dr, const float* bias, float* dt, float* cum, float* states) {
+  auto kern = tc_chunk_state_kernel<BF16, DT, FUSE>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kStateSmem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)c.H, (unsigned)c.nchunks_max);
+  kern<<<grid, 128, kStateSmem, c.stream>>>(mx, mb, A, (const DT*)dr, bias, dt, cum, states, c.cm, c.H, c.H / c.G,
+                                            c.use_sp, c.dmin, c.dmax);
+  return cudaGetLastError();
+}
+
+template <bool BF16>
+static cudaError_t tc_state_dt(const LaunchCtx& c, int dt_dtype, const CUtensorMap& mx, const CUtensorMap& mb,
+                               const float* A, const void* dr, const float* bias, float* dt, float* cum,
+                               float* states) {
+  if (!dr) return tc_state_launch<BF16, float, false>(c, mx, mb, A, dr, bias, dt, cum, states);
+  switch (dt_dtype) {
+    case SSD_F32: return tc_state_launch<BF16, float, true>(c, mx, mb, A, dr, bias, dt, cum, states);
+    case SSD_BF16: return tc_state_launch<BF16, __nv_bfloat16, true>(c, mx, mb, A, dr, bias, dt, cum, states);
+    case SSD_F16: return tc_state_launch<BF16, __half, true>(c, mx, mb, A, dr, bias, dt, cum, states);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// delta_raw == NULL: dt / cum are inputs; otherwise they are computed (chunk_cumsum fused) and written.
+cudaError_t launch_tc_chunk_state(const LaunchCtx& c, int x_dtype, int dt_dtype, const void* u, const void* B,
+                                  const float* A, const void* delta_raw, const float* delta_bias, float* dt,
+                                  float* cum, float* states, int* tmap_status) {
   const bool bf16 = x_dtype == SSD_BF16;
   CUtensorMap mx, mb;
-  if (!make_map_3d(&mx, u, bf16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 256) ||
-      !make_map_3d(&mb, B, bf16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 256)) {
+  if (!make_map_3d(&mx, u, bf16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&mb, B, bf16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128)) {
     *tmap_status = 1;
     return cudaErrorInvalidValue;
   }
   *tmap_status = 0;
-  dim3 grid((unsigned)c.H, (unsigned)c.nchunks_max);
-  const int hpg = c.H / c.G;
-  if (bf16) {
-    cudaFuncSetAttribute(tc_chunk_state_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStateSmem);
-    tc_chunk_state_kernel<true><<<grid, 128, kStateSmem, c.stream>>>(mx, mb, dt, cum, states, c.cm, c.H, hpg);
-  } else {
-    cudaFuncSetAttribute(tc_chunk_state_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kStateSmem);
-    tc_chunk_state_kernel<false><<<grid, 128, kStateSmem, c.stream>>>(mx, mb, dt, cum, states, c.cm, c.H, hpg);
-  }
-  return cudaGetLastError();
+  if (bf16) return tc_state_dt<true>(c, dt_dtype, mx, mb, A, delta_raw, delta_bias, dt, cum, states);
+  return tc_state_dt<false>(c, dt_dtype, mx, mb, A, delta_raw, delta_bias, dt, cum, states);
 }
 
 template <bool BF16, typename YT>
 static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, const CUtensorMap& mc,
-                                  const CUtensorMap& mb, const CUtensorMap& mh, const float* dt, const float* cum,
-                                  const float* D, const void* z, void* y) {
+                                  const CUtensorMap& mb, const CUtensorMap& mh, const float* A, const float* dt,
+                                  const float* cum, const float* D, const void* z, void* y) {
   auto kern = tc_chunk_scan_kernel<BF16, YT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem);
   if (e != cudaSuccess) return e;
+  const int dt_nonneg = (c.dmax >= 0.f) && (c.use_sp || c.dmin >= 0.f);
   dim3 grid((unsigned)(2 * c.H), (unsigned)c.nchunks_max);
-  kern<<<grid, 128, kScanSmem, c.stream>>>(mx, mc, mb, mh, dt, cum, D,
+  kern<<<grid, 256, kScanSmem, c.stream>>>(mx, mc, mb, mh, A, dt, cum, D,
                                            reinterpret_cast<const typename T16Of<BF16>::type*>(z),
-                                           reinterpret_cast<YT*>(y), c.cm, c.H, c.H / c.G);
+                                           reinterpret_cast<YT*>(y), c.cm, c.H, c.H / c.G, dt_nonneg);
   return cudaGetLastError();
 }
 
-cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, const void* u, const float* dt,
-                                 const float* cum, const void* B, const void* C, const void* prev16,
+cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, const void* u, const float* A,
+                                 const float* dt, const float* cum, const void* B, const void* C, const void* prev16,
                                  const float* D, const void* z, void* y, int* tmap_status) {
   const bool bf16 = x_dtype == SSD_BF16;
   CUtensorMap mx, mc, mb, mh;
@@ -472,12 +648,12 @@ cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, c
   }
   *tmap_status = 0;
   if (y_dtype == SSD_F32) {
-    if (bf16) return tc_scan_launch<true, float>(c, mx, mc, mb, mh, dt, cum, D, z, y);
-    return tc_scan_launch<false, float>(c, mx, mc, mb, mh, dt, cum, D, z, y);
+    if (bf16) return tc_scan_launch<true, float>(c, mx, mc, mb, mh, A, dt, cum, D, z, y);
+    return tc_scan_launch<false, float>(c, mx, mc, mb, mh, A, dt, cum, D, z, y);
   }
   if (y_dtype == x_dtype) {
-    if (bf16) return tc_scan_launch<true, __nv_bfloat16>(c, mx, mc, mb, mh, dt, cum, D, z, y);
-    return tc_scan_launch<false, __half>(c, mx, mc, mb, mh, dt, cum, D, z, y);
+    if (bf16) return tc_scan_launch<true, __nv_bfloat16>(c, mx, mc, mb, mh, A, dt, cum, D, z, y);
+    return tc_scan_launch<false, __half>(c, mx, mc, mb, mh, A, dt, cum, D, z, y);
   }
   return cudaErrorInvalidValue;
 }

@@ -182,6 +182,31 @@ def test_c2_varlen_full_size_vs_oracle():
         assert_bf16_close(h[s:s + 1], hs, f"c2 seq {s} h_last")
 
 
+@pytest.mark.parametrize("impl", ["tc", "simt"])
+def test_decay_edge_cases_vs_oracle(impl):
+    """A head with A > 0 (the min(., 0) clamps of forward_kernel.py:178,438 are active),
+    a head with a very fast decay (dt ~ 1, |A| up to 16: the factored decay would overflow
+    on diagonal tiles, so the element-by-element form must be used), plus two ordinary heads."""
+    import selective_attention_b200 as sab
+
+    inp = _c_inputs("c1", seed=7, batch=2, seqlen=520, nheads=4)
+    A = inp["A"].clone()
+    A[1] = 0.05
+    A[2] = -16.0
+    db = torch.zeros(4)
+    db[2] = 4.0
+    length = torch.tensor([520, 300])
+    y, h = sab.SSDScanFn.apply(dev(inp["u"]), dev(A), dev(inp["B"]), dev(inp["C"]), dev(inp["delta_raw"]), dev(db),
+                               None, dev(length), 256, True, (0.0, INF), True, dev(inp["D"]), dev(inp["z"]), None,
+                               impl)
+    sab.check_device_error()
+    y_ref, h_ref = ssd_ref.ssd_scan_forward(inp["u"].float(), A, inp["B"].float(), inp["C"].float(),
+                                            inp["delta_raw"], db, None, length, 256)
+    y_ref = ssd_ref.gate_epilogue(y_ref, inp["u"], inp["D"], inp["z"])
+    assert_bf16_close(y, y_ref, f"{impl} y")
+    assert_bf16_close(h, h_ref, f"{impl} h_last")
+
+
 def test_tc_and_simt_agree():
     """Both device paths on the same bf16 inputs (two chunks, ragged length)."""
     import selective_attention_b200 as sab
