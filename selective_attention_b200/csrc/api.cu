@@ -191,7 +191,7 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
   if (tc && p->y_dtype != SSD_F32 && p->y_dtype != p->x_dtype) return SSD_ERR_UNSUPPORTED_DTYPE;
   if (!aligned16(p->h_last) || (p->h_init && !aligned16(p->h_init))) return SSD_ERR_INVALID_ARGUMENT;
   if (tc && (!aligned16(p->u) || !aligned16(p->B) || !aligned16(p->C) || !aligned16(p->y) ||
-             (p->z && !aligned16(p->z))))
+             (p->z && !aligned16(p->z)) || (p->D && !aligned16(p->D))))
     return SSD_ERR_INVALID_ARGUMENT;
   Workspace w = carve(p, g, tc, reinterpret_cast<uint8_t*>(p->workspace));
   if (p->workspace_bytes < w.bytes) return SSD_ERR_WORKSPACE_TOO_SMALL;

@@ -42,6 +42,8 @@ enum : unsigned int {
   kSiteScanTma = 0x201,
   kSiteScanMma1 = 0x202,
   kSiteScanMma2 = 0x203,
+  kSiteScanConv = 0x204,
+  kSiteScanEpi = 0x205,
 };
 
 template <bool BF16> struct T16Of;
@@ -236,307 +238,395 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
 }
 
 // ===========================================================================
-// chunk_scan (+ bmm_chunk)
+// chunk_scan (+ bmm_chunk): persistent and warp-specialised
 // ===========================================================================
-constexpr int kScanTileBytes = 32768 + 32768 + 16384 + 16384;
-constexpr int kScanSmem = kScanTileBytes + 2048 + 512 + 256 + 256 + 1024;
+// Work items are (chunk k, head h, half m); an item is m + 1 jobs, job j covering
+// source tokens [128j, 128j + 128) for the rows of half m. One CTA per SM walks
+// items blockIdx.x, blockIdx.x + gridDim.x, ... with three roles:
+//   warp 0 (one lane)  TMA producer: per job, C rows of the half, B and x rows of
+//                      the job, prev[k, h] (job 0), dt / cum (and D) into a stage
+//                      of a 2-deep shared-memory ring;
+//   warp 1 (one lane)  MMA issuer: MMA1 CB = C B^T into the stage's TMEM slot
+//                      (+ MMA3 Yoff = C prev^T for job 0), then - one job behind -
+//                      MMA2 Yin += M x once the compute warps have written M;
+//   warps 2..9         compute: CB -> M conversion per job, epilogue per item.
+// TMEM: CB slots [0,128) and [128,256) per stage; Yin/Yoff slots at 256 + 128*(item&1).
+// Every wait is bounded; a role that gives up records the site, raises the CTA's
+// abort flag and leaves its loop; the others then give up at their next wait.
+constexpr int kScanStageBytes = 98304;  // sC 32K | sB 32K | sX 16K | sH 16K
+constexpr int kScanSmallBytes = 3072;   // dt 1K | cum 1K | D 256 | colf 512 | flags
+constexpr int kScanThreads = 320;
+constexpr int kScanSmem = 2 * kScanStageBytes + 2 * kScanSmallBytes + 256 + 1024;
+
+// Item `it` -> (chunk, head, half); false if the half holds no token of the row.
+__device__ __forceinline__ bool scan_item(const ChunkMap& cm, int it, int H, ChunkInfo& ci, int& k, int& h,
+                                          int& m) {
+  k = it / (2 * H);
+  const int rem = it - k * 2 * H;
+  h = rem >> 1;
+  m = 1 - (rem & 1);  // the heavier half of a (chunk, head) first
+  if (!chunk_info(cm, k, ci)) return false;
+  return 128 * m < ci.lim;
+}
 
 template <bool BF16, typename YT>
-__global__ void __launch_bounds__(256) tc_chunk_scan_kernel(
+__global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c,
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_h,
     const float* __restrict__ A, const float* __restrict__ dt, const float* __restrict__ cum,
     const float* __restrict__ D, const typename T16Of<BF16>::type* __restrict__ z, YT* __restrict__ y, ChunkMap cm,
-    int H, int hpg, int dt_nonneg) {
+    int H, int hpg, int dt_nonneg, int n_items) {
   using T16 = typename T16Of<BF16>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* sC = smem;              // 2 x (128 rows x 128 B): dstate halves of C rows [128m, 128m+128)
-  uint8_t* sB = smem + 32768;      // 2 x (128 rows x 128 B): B rows of the phase; then M (2 s-blocks of 64)
-  uint8_t* sX = smem + 65536;      // 128 rows x 128 B: x rows of the phase
-  uint8_t* sH = smem + 81920;      // 2 x (64 rows x 128 B): dstate halves of prev[p, :]
-  float* sDt = reinterpret_cast<float*>(smem + kScanTileBytes);
-  float* sCum = sDt + 256;
-  float* sColf = sCum + 256;       // 128
-  float* sD = sColf + 128;         // 64
-  int* sBlkOk = reinterpret_cast<int*>(sD + 64);  // 4 (+4 pad)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sBlkOk + 8);  // tma[2], m1[2], m2[2]
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 6);
+  uint8_t* small0 = smem + 2 * kScanStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(small0 + 2 * kScanSmallBytes);
+  // full[2] cbfull[2] mfull[2] jobdone[2] epidone[2]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  auto stage = [&](int s) { return smem + s * kScanStageBytes; };
+  auto small = [&](int s) { return reinterpret_cast<float*>(small0 + s * kScanSmallBytes); };
+  // small stage layout (floats): dt [0,256) cum [256,512) D [512,576) colf [576,704) flags [704,708)
 
-  const int m = blockIdx.x & 1, h = blockIdx.x >> 1, k = blockIdx.y;
-  ChunkInfo ci;
-  if (!chunk_info(cm, k, ci)) return;
-  const int lbase = 128 * m;
-  if (lbase >= ci.lim) return;  // no token of this half belongs to the row
-  const int g = h / hpg;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int quad = warp & 3, ch = warp >> 2;  // TMEM lane quadrant, column half
-  const int r = quad * 32 + lane;             // row within the half
-  const int l = lbase + r;                    // row within the chunk
-  uint32_t bt[2], b1[2], b2[2];
-#pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    bt[i] = smem_u32(&bars[i]);
-    b1[i] = smem_u32(&bars[2 + i]);
-    b2[i] = smem_u32(&bars[4 + i]);
-  }
-  const uint32_t T_CB = 0, T_YIN = 128, T_YOFF = 192;
-
   if (tid == 0) {
     prefetch_tmap(&tm_x);
     prefetch_tmap(&tm_c);
     prefetch_tmap(&tm_b);
     prefetch_tmap(&tm_h);
-#pragma unroll
-    for (int i = 0; i < 6; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(0 + s), 1);  // full: producer's expect_tx
+      mbar_init(bar(2 + s), 1);  // cbfull: MMA commit
+      mbar_init(bar(4 + s), 8);  // mfull: one arrive per compute warp
+      mbar_init(bar(6 + s), 1);  // jobdone: MMA commit
+      mbar_init(bar(8 + s), 8);  // epidone (per Y slot): one arrive per compute warp
+    }
+    *s_abort = 0;
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
+  if (warp == 1) tmem_alloc(smem_u32(tslot), 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tq = tmem + ((uint32_t)(quad * 32) << 16);  // this warp's lane quadrant
-  const int t0 = (int)ci.tok0;
 
-  if (tid == 0) {
-    mbar_expect_tx(bt[0], 32768u + 16384u + 32768u + 16384u);
-    tma_load_3d(smem_u32(sC), &tm_c, 0, g, t0 + lbase, bt[0]);
-    tma_load_3d(smem_u32(sC + 16384), &tm_c, 64, g, t0 + lbase, bt[0]);
-    tma_load_3d(smem_u32(sH), &tm_h, 0, 0, k * H + h, bt[0]);
-    tma_load_3d(smem_u32(sH + 8192), &tm_h, 64, 0, k * H + h, bt[0]);
-    tma_load_3d(smem_u32(sB), &tm_b, 0, g, t0, bt[0]);
-    tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, g, t0, bt[0]);
-    tma_load_3d(smem_u32(sX), &tm_x, 0, h, t0, bt[0]);
-  }
-  {
-    const float* dtk = dt + ((long long)k * H + h) * 256;
-    const float* cmk = cum + ((long long)k * H + h) * 256;
-    sDt[tid] = dtk[tid];
-    sCum[tid] = cmk[tid];
-    if (tid < 64) sD[tid] = D ? D[h * 64 + tid] : 0.f;
-  }
-  // cum non-increasing => min(cum_l - cum_s, 0) = cum_l - cum_s for s <= l
-  const bool mono = dt_nonneg && (A[h] <= 0.f);
-  __syncthreads();
-  const float cl = sCum[l];
-
-  bool ok = true;
-  bool pend_tma = true, pend_m1 = false, pend_m2 = false;
-  int last_m1 = 0, last_m2 = 0;
-  const uint32_t id_kk64 = idesc_f16(128, 64, BF16, false, false);
-  const uint32_t id_kk128 = idesc_f16(128, 128, BF16, false, false);
-  const uint32_t id_km64 = idesc_f16(128, 64, BF16, false, true);
-  for (int j = 0; j <= m; ++j) {
-    const bool w_ok = mbar_wait(bt[j], 0, kSiteScanTma);
-    ok = __syncthreads_and(w_ok) != 0;
-    if (!ok) break;
-    pend_tma = false;
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t c0 = smem_u32(sC), b0 = smem_u32(sB), h0 = smem_u32(sH);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
-        umma_f16(tmem + T_CB, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
-                 sdesc_sw128(b0 + hf * 16384 + kk, 16, 1024), id_kk128, ks > 0 ? 1u : 0u);
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int J = 0, nI = 0;
+      int last_item[2] = {-1, -1};
+      bool issued[2] = {false, false};
+      int last_J[2] = {0, 0};
+      for (int it = blockIdx.x; it < n_items && !*s_abort; it += gridDim.x) {
+        ChunkInfo ci;
+        int k, h, m;
+        if (!scan_item(cm, it, H, ci, k, h, m)) continue;
+        const int g = h / hpg, t0 = (int)ci.tok0;
+        bool fail = false;
+        for (int j = 0; j <= m; ++j) {
+          const int s = J & 1;
+          if (J >= 2) {
+            if (!mbar_wait(bar(6 + s), ((J - 2) >> 1) & 1, kSiteScanMma2)) { fail = true; break; }
+            if (last_item[s] >= 0 &&
+                !mbar_wait(bar(8 + (last_item[s] & 1)), (last_item[s] >> 1) & 1, kSiteScanEpi)) {
+              fail = true;
+              break;
+            }
+          }
+          uint8_t* st = stage(s);
+          float* sm = small(s);
+          const bool withD = (j == m) && D != nullptr;
+          const uint32_t bytes = 32768u + 32768u + 16384u + (j == 0 ? 16384u : 0u) + 2048u + (withD ? 256u : 0u);
+          const uint32_t fb = bar(0 + s);
+          mbar_expect_tx(fb, bytes);
+          tma_load_3d(smem_u32(st), &tm_c, 0, g, t0 + 128 * m, fb);
+          tma_load_3d(smem_u32(st + 16384), &tm_c, 64, g, t0 + 128 * m, fb);
+          tma_load_3d(smem_u32(st + 32768), &tm_b, 0, g, t0 + 128 * j, fb);
+          tma_load_3d(smem_u32(st + 49152), &tm_b, 64, g, t0 + 128 * j, fb);
+          tma_load_3d(smem_u32(st + 65536), &tm_x, 0, h, t0 + 128 * j, fb);
+          if (j == 0) {
+            tma_load_3d(smem_u32(st + 81920), &tm_h, 0, 0, k * H + h, fb);
+            tma_load_3d(smem_u32(st + 90112), &tm_h, 64, 0, k * H + h, fb);
+          }
+          bulk_load(smem_u32(sm), dt + ((long long)k * H + h) * 256, 1024u, fb);
+          bulk_load(smem_u32(sm + 256), cum + ((long long)k * H + h) * 256, 1024u, fb);
+          if (withD) bulk_load(smem_u32(sm + 512), D + h * 64, 256u, fb);
+          issued[s] = true;
+          last_J[s] = J;
+          last_item[s] = (j == m) ? nI : -1;
+          ++J;
+        }
+        if (fail) {
+          *s_abort = 1;
+          break;
+        }
+        ++nI;
       }
-      if (j == 0) {
+      // No copy may still be in flight when the CTA exits.
+      for (int s = 0; s < 2; ++s)
+        if (issued[s]) mbar_wait(bar(0 + s), (last_J[s] >> 1) & 1, kSiteScanTma);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_cb = idesc_f16(128, 128, BF16, false, false);
+      const uint32_t id_off = idesc_f16(128, 64, BF16, false, false);
+      const uint32_t id_in = idesc_f16(128, 64, BF16, false, true);
+      int J = 0, nI = 0;
+      bool have_prev = false, fail = false, committed = false;
+      int pv_s = 0, pv_J = 0, pv_slot = 0, pv_j = 0, last_commit_s = 0, last_commit_J = 0;
+      auto mma2 = [&]() -> bool {
+        if (!mbar_wait(bar(4 + pv_s), (pv_J >> 1) & 1, kSiteScanConv)) return false;
+        tc_fence_after();
+        const uint32_t m0 = smem_u32(stage(pv_s) + 32768), x0 = smem_u32(stage(pv_s) + 65536);
+        const uint32_t yin = tmem + 256 + 128 * pv_slot;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
-          umma_f16(tmem + T_YOFF, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
-                   sdesc_sw128(h0 + hf * 8192 + kk, 16, 1024), id_kk64, ks > 0 ? 1u : 0u);
+          const uint32_t sb = ks >> 2, kk = (ks & 3) * 32;
+          umma_f16(yin, sdesc_sw128(m0 + sb * 16384 + kk, 16, 1024), sdesc_sw128(x0 + ks * 2048, 16, 1024), id_in,
+                   (pv_j > 0 || ks > 0) ? 1u : 0u);
         }
-      }
-      umma_commit(b1[j]);
-    }
-    pend_m1 = true;
-    last_m1 = j;
-    const int sbase = 128 * j;  // first token of this phase
-    // Column factors exp(cum_r - cum_s) * dt_s with r the last token of the 32-token
-    // block holding s (<= dt_s when cum is non-increasing), and per-block flags:
-    // a diagonal tile may use the factored form only if its row factor
-    // exp(cum_l - cum_r) <= exp(cum_first - cum_r) stays far from overflow.
-    if (tid < 128) {
-      const int s = sbase + tid;
-      const float cr = sCum[sbase + (tid | 31)];
-      sColf[tid] = mono ? __expf(cr - sCum[s]) * sDt[s] : 0.f;
-      if ((tid & 31) == 0) sBlkOk[tid >> 5] = mono && (sCum[s] - cr <= 80.f);
-    }
-    // x rows past `lim` -> exact zeros (they then cannot leak into Yin)
-    for (int q = tid; q < 1024; q += 256)
-      if (sbase + (q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
-    const bool m1_ok = mbar_wait(b1[j], 0, kSiteScanMma1);
-    tc_fence_after();
-    ok = __syncthreads_and(m1_ok) != 0;  // also publishes sColf
-    if (!ok) break;
-    pend_m1 = false;
-    // ---- CB_j (TMEM) -> M_j (smem, K-major over the B tile) ----
-    // This warp covers rows [wr0, wr0 + 32) and 32-column blocks cb = ch, ch + 2.
-    const int wr0 = lbase + quad * 32;
-    uint32_t v[2][32];
-    int kind[2];  // 0: above the diagonal (zeros), 1: factored, 2: element by element
-#pragma unroll
-    for (int cbi = 0; cbi < 2; ++cbi) {
-      const int cb = 2 * cbi + ch;
-      const int s0 = sbase + cb * 32;
-      if (s0 > wr0 + 31) {
-        kind[cbi] = 0;
-      } else {
-        const bool diag = s0 + 31 >= wr0;  // blocks are aligned, so this is the 32x32 diagonal tile
-        kind[cbi] = (diag ? sBlkOk[cb] : mono) ? 1 : 2;
-        tmem_ld32(tq + T_CB + cb * 32, v[cbi]);
-      }
-    }
-    tmem_wait_ld();
-#pragma unroll
-    for (int cbi = 0; cbi < 2; ++cbi) {
-      const int cb = 2 * cbi + ch;
-      const int s0 = sbase + cb * 32;
-      uint32_t pk[16];
-      if (kind[cbi] == 0) {
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) pk[jj] = 0u;
-      } else if (kind[cbi] == 1) {
-        const float rowf = __expf(cl - sCum[s0 + 31]);
-        const float4* cf = reinterpret_cast<const float4*>(sColf + cb * 32);
-        const bool diag = s0 + 31 >= wr0;
-#pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4) {
-          const float4 c4 = cf[q4];
-          float x0 = __uint_as_float(v[cbi][4 * q4]) * rowf * c4.x;
-          float x1 = __uint_as_float(v[cbi][4 * q4 + 1]) * rowf * c4.y;
-          float x2 = __uint_as_float(v[cbi][4 * q4 + 2]) * rowf * c4.z;
-          float x3 = __uint_as_float(v[cbi][4 * q4 + 3]) * rowf * c4.w;
-          if (diag) {
-            const int sa = s0 + 4 * q4;
-            x0 = sa <= l ? x0 : 0.f;
-            x1 = sa + 1 <= l ? x1 : 0.f;
-            x2 = sa + 2 <= l ? x2 : 0.f;
-            x3 = sa + 3 <= l ? x3 : 0.f;
+        umma_commit(bar(6 + pv_s));
+        committed = true;
+        last_commit_s = pv_s;
+        last_commit_J = pv_J;
+        return true;
+      };
+      for (int it = blockIdx.x; it < n_items && !fail && !*s_abort; it += gridDim.x) {
+        ChunkInfo ci;
+        int k, h, m;
+        if (!scan_item(cm, it, H, ci, k, h, m)) continue;
+        const int slot = nI & 1;
+        for (int j = 0; j <= m; ++j) {
+          const int s = J & 1;
+          if (!mbar_wait(bar(0 + s), (J >> 1) & 1, kSiteScanTma)) { fail = true; break; }
+          if (j == 0 && nI >= 2 && !mbar_wait(bar(8 + slot), ((nI - 2) >> 1) & 1, kSiteScanEpi)) {
+            fail = true;
+            break;
           }
-          pk[2 * q4] = pack2<T16>(x0, x1);
-          pk[2 * q4 + 1] = pack2<T16>(x2, x3);
+          tc_fence_after();
+          const uint32_t c0 = smem_u32(stage(s)), b0 = smem_u32(stage(s) + 32768), h0 = smem_u32(stage(s) + 81920);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
+            umma_f16(tmem + 128 * s, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
+                     sdesc_sw128(b0 + hf * 16384 + kk, 16, 1024), id_cb, ks > 0 ? 1u : 0u);
+          }
+          if (j == 0) {
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+              const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
+              umma_f16(tmem + 256 + 128 * slot + 64, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
+                       sdesc_sw128(h0 + hf * 8192 + kk, 16, 1024), id_off, ks > 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(bar(2 + s));
+          if (have_prev && !mma2()) { fail = true; break; }
+          have_prev = true;
+          pv_s = s;
+          pv_J = J;
+          pv_slot = slot;
+          pv_j = j;
+          ++J;
         }
-      } else {
-#pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int sa = s0 + 2 * jj, sb2 = sa + 1;
-          float x0 = 0.f, x1 = 0.f;
-          if (sa <= l && sa < ci.lim)
-            x0 = __uint_as_float(v[cbi][2 * jj]) * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
-          if (sb2 <= l && sb2 < ci.lim)
-            x1 = __uint_as_float(v[cbi][2 * jj + 1]) * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
-          pk[jj] = pack2<T16>(x0, x1);
+        ++nI;
+      }
+      if (!fail && have_prev && !mma2()) fail = true;
+      if (fail) *s_abort = 1;
+      // All MMAs must be complete before TMEM is released.
+      if (committed) mbar_wait(bar(6 + last_commit_s), (last_commit_J >> 1) & 1, kSiteScanMma2);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const int ctid = tid - 64;
+    const int quad = warp & 3, ch = (warp - 2) >> 2;
+    const int r = quad * 32 + lane;
+    int J = 0, nI = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+      ChunkInfo ci;
+      int k, h, m;
+      if (!scan_item(cm, it, H, ci, k, h, m)) continue;
+      const int lbase = 128 * m, l = lbase + r, slot = nI & 1, wr0 = lbase + quad * 32;
+      const bool mono = dt_nonneg && (A[h] <= 0.f);
+      bool fail = false;
+      for (int j = 0; j <= m; ++j) {
+        const int s = J & 1, par = (J >> 1) & 1, sbase = 128 * j;
+        uint8_t* st = stage(s);
+        uint8_t* sB = st + 32768;
+        uint8_t* sX = st + 65536;
+        float* sm = small(s);
+        const float* sDt = sm;
+        const float* sCum = sm + 256;
+        float* sColf = sm + 576;
+        int* sBlkOk = reinterpret_cast<int*>(sm + 704);
+        bool ok = mbar_wait(bar(0 + s), par, kSiteScanTma);
+        if (!named_bar_and(1, 256, ok && !*s_abort)) { fail = true; break; }
+        if (ctid < 128) {
+          const int sl = sbase + ctid;
+          const float cr = sCum[sbase + (ctid | 31)];
+          sColf[ctid] = mono ? __expf(cr - sCum[sl]) * sDt[sl] : 0.f;
+          if ((ctid & 31) == 0) sBlkOk[ctid >> 5] = mono && (sCum[sl] - cr <= 80.f);
         }
-      }
-      uint8_t* base = sB + (cb >> 1) * 16384;
-      const uint32_t c16 = (cb & 1) * 4;
+        // x rows past `lim` -> exact zeros, so they cannot leak into Yin
+        for (int q = ctid; q < 1024; q += 256)
+          if (sbase + (q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
+        ok = mbar_wait(bar(2 + s), par, kSiteScanMma1);
+        tc_fence_after();
+        if (!named_bar_and(1, 256, ok)) { fail = true; break; }  // also publishes colf / flags
+        const float cl = sCum[l];
+        // ---- CB (TMEM) -> M (K-major over the B tile) ----
+        const uint32_t tq = tmem + ((uint32_t)(quad * 32) << 16) + 128 * s;
+        uint32_t v[2][32];
+        int kind[2];  // 0: above the diagonal, 1: factored, 2: element by element
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        *reinterpret_cast<uint4*>(base + sw128_off(r, c16 + q)) =
-            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t m0 = smem_u32(sB), x0 = smem_u32(sX);
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t sb = ks >> 2, kk = (ks & 3) * 32;
-        umma_f16(tmem + T_YIN, sdesc_sw128(m0 + sb * 16384 + kk, 16, 1024), sdesc_sw128(x0 + ks * 2048, 16, 1024),
-                 id_km64, (j > 0 || ks > 0) ? 1u : 0u);
-      }
-      umma_commit(b2[j]);
-    }
-    pend_m2 = true;
-    last_m2 = j;
-    if (j < m) {
-      // next phase reuses the B/x buffers: wait for this phase's MMA2 first
-      if (tid == 0 && mbar_wait(b2[j], 0, kSiteScanMma2)) {
-        mbar_expect_tx(bt[j + 1], 32768u + 16384u);
-        const int tn = t0 + 128 * (j + 1);
-        tma_load_3d(smem_u32(sB), &tm_b, 0, g, tn, bt[j + 1]);
-        tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, g, tn, bt[j + 1]);
-        tma_load_3d(smem_u32(sX), &tm_x, 0, h, tn, bt[j + 1]);
-      }
-      pend_tma = true;
-    }
-  }
-
-  // ---- epilogue: y = exp(cum_l) * Yoff + Yin (+ D x) (* silu z) ----
-  const long long tok = ci.tok0 + l;
-  const bool valid = l < ci.lim;
-  const long long yrow = (tok * H + h) * 64 + ch * 32;
-  uint4 zv[4];
-  if (z && valid) {
-    const uint4* zp = reinterpret_cast<const uint4*>(z + yrow);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) zv[q] = zp[q];
-  }
-  bool m2_ok = false;
-  if (ok) m2_ok = mbar_wait(b2[m], 0, kSiteScanMma2);
-  tc_fence_after();
-  if (ok && __syncthreads_and(m2_ok)) {
-    uint32_t ro[32], ri[32];
-    tmem_ld32(tq + T_YOFF + ch * 32, ro);
-    tmem_ld32(tq + T_YIN + ch * 32, ri);
-    tmem_wait_ld();
-    if (valid) {
-      const float el = __expf(cl);
-      float o[32];
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) o[jj] = fmaf(el, __uint_as_float(ro[jj]), __uint_as_float(ri[jj]));
-      if (D) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 xv = *reinterpret_cast<const uint4*>(sX + sw128_off(r, ch * 4 + q));
-          const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = unpack2<T16>(w4[e]);
-            const int pi = q * 8 + 2 * e;
-            o[pi] = fmaf(sD[ch * 32 + pi], f.x, o[pi]);
-            o[pi + 1] = fmaf(sD[ch * 32 + pi + 1], f.y, o[pi + 1]);
+        for (int cbi = 0; cbi < 2; ++cbi) {
+          const int cb = 2 * cbi + ch;
+          const int s0 = sbase + cb * 32;
+          if (s0 > wr0 + 31) {
+            kind[cbi] = 0;
+          } else {
+            const bool diag = s0 + 31 >= wr0;
+            kind[cbi] = (diag ? sBlkOk[cb] : mono) ? 1 : 2;
+            tmem_ld32(tq + cb * 32, v[cbi]);
           }
         }
-      }
-      if (z) {
+        tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint32_t w4[4] = {zv[q].x, zv[q].y, zv[q].z, zv[q].w};
+        for (int cbi = 0; cbi < 2; ++cbi) {
+          const int cb = 2 * cbi + ch;
+          const int s0 = sbase + cb * 32;
+          uint32_t pk[16];
+          if (kind[cbi] == 0) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = unpack2<T16>(w4[e]);
-            o[q * 8 + 2 * e] *= silu_fast(f.x);
-            o[q * 8 + 2 * e + 1] *= silu_fast(f.y);
+            for (int jj = 0; jj < 16; ++jj) pk[jj] = 0u;
+          } else if (kind[cbi] == 1) {
+            const float rowf = __expf(cl - sCum[s0 + 31]);
+            const float4* cf = reinterpret_cast<const float4*>(sColf + cb * 32);
+            const bool diag = s0 + 31 >= wr0;
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4) {
+              const float4 c4 = cf[q4];
+              float x0 = __uint_as_float(v[cbi][4 * q4]) * rowf * c4.x;
+              float x1 = __uint_as_float(v[cbi][4 * q4 + 1]) * rowf * c4.y;
+              float x2 = __uint_as_float(v[cbi][4 * q4 + 2]) * rowf * c4.z;
+              float x3 = __uint_as_float(v[cbi][4 * q4 + 3]) * rowf * c4.w;
+              if (diag) {
+                const int sa = s0 + 4 * q4;
+                x0 = sa <= l ? x0 : 0.f;
+                x1 = sa + 1 <= l ? x1 : 0.f;
+                x2 = sa + 2 <= l ? x2 : 0.f;
+                x3 = sa + 3 <= l ? x3 : 0.f;
+              }
+              pk[2 * q4] = pack2<T16>(x0, x1);
+              pk[2 * q4 + 1] = pack2<T16>(x2, x3);
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int sa = s0 + 2 * jj, sb2 = sa + 1;
+              float x0 = 0.f, x1 = 0.f;
+              if (sa <= l && sa < ci.lim)
+                x0 = __uint_as_float(v[cbi][2 * jj]) * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
+              if (sb2 <= l && sb2 < ci.lim)
+                x1 = __uint_as_float(v[cbi][2 * jj + 1]) * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
+              pk[jj] = pack2<T16>(x0, x1);
+            }
           }
+          uint8_t* base = sB + (cb >> 1) * 16384;
+          const uint32_t c16 = (cb & 1) * 4;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(base + sw128_off(r, c16 + q)) =
+                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
-      }
-      if constexpr (sizeof(YT) == 4) {
-        float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(4 + s));
+        if (j == m) {
+          // ---- epilogue: y = exp(cum_l) Yoff + Yin (+ D x) (* silu z) ----
+          const long long tok = ci.tok0 + l;
+          const bool valid = l < ci.lim;
+          const long long yrow = (tok * H + h) * 64 + ch * 32;
+          uint4 zv[4];
+          if (z && valid) {
+            const uint4* zp = reinterpret_cast<const uint4*>(z + yrow);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-      } else {
-        uint4* yp = reinterpret_cast<uint4*>(y + yrow);
+            for (int q = 0; q < 4; ++q) zv[q] = zp[q];
+          }
+          ok = mbar_wait(bar(6 + s), par, kSiteScanMma2);
+          tc_fence_after();
+          if (!named_bar_and(1, 256, ok)) { fail = true; break; }
+          const uint32_t ty = tmem + ((uint32_t)(quad * 32) << 16) + 256 + 128 * slot;
+          uint32_t ri[32], ro[32];
+          tmem_ld32(ty + ch * 32, ri);
+          tmem_ld32(ty + 64 + ch * 32, ro);
+          tmem_wait_ld();
+          tc_fence_before();
+          if (valid) {
+            const float el = __expf(cl);
+            float o[32];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          yp[q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
-                             pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
+            for (int jj = 0; jj < 32; ++jj) o[jj] = fmaf(el, __uint_as_float(ro[jj]), __uint_as_float(ri[jj]));
+            if (D) {
+              const float* sD = sm + 512 + ch * 32;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint4 xv = *reinterpret_cast<const uint4*>(sX + sw128_off(r, ch * 4 + q));
+                const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = unpack2<T16>(w4[e]);
+                  const int pi = q * 8 + 2 * e;
+                  o[pi] = fmaf(sD[pi], f.x, o[pi]);
+                  o[pi + 1] = fmaf(sD[pi + 1], f.y, o[pi + 1]);
+                }
+              }
+            }
+            if (z) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint32_t w4[4] = {zv[q].x, zv[q].y, zv[q].z, zv[q].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 f = unpack2<T16>(w4[e]);
+                  const float h0 = 0.5f * f.x, h1 = 0.5f * f.y;
+                  o[q * 8 + 2 * e] *= fmaf(h0, tanh_approx(h0), h0);
+                  o[q * 8 + 2 * e + 1] *= fmaf(h1, tanh_approx(h1), h1);
+                }
+              }
+            }
+            if constexpr (sizeof(YT) == 4) {
+              float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            } else {
+              uint4* yp = reinterpret_cast<uint4*>(y + yrow);
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                yp[q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
+                                   pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
+            }
+          }
+          // Y slot (TMEM) and stage (x tile, D) are free once every compute warp is here.
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(8 + slot));
+        }
+        ++J;
       }
+      if (fail) {
+        *s_abort = 1;
+        break;
+      }
+      ++nI;
     }
-  } else if (tid == 0) {
-    // Let in-flight copies / MMAs land (bounded) before the CTA exits.
-    if (pend_tma) mbar_wait(bt[m], 0, kSiteScanTma);
-    if (pend_m1) mbar_wait(b1[last_m1], 0, kSiteScanMma1);
-    if (pend_m2) mbar_wait(b2[last_m2], 0, kSiteScanMma2);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
+  if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
 // ===========================================================================
@@ -624,10 +714,15 @@ static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, con
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem);
   if (e != cudaSuccess) return e;
   const int dt_nonneg = (c.dmax >= 0.f) && (c.use_sp || c.dmin >= 0.f);
-  dim3 grid((unsigned)(2 * c.H), (unsigned)c.nchunks_max);
-  kern<<<grid, 256, kScanSmem, c.stream>>>(mx, mc, mb, mh, A, dt, cum, D,
-                                           reinterpret_cast<const typename T16Of<BF16>::type*>(z),
-                                           reinterpret_cast<YT*>(y), c.cm, c.H, c.H / c.G, dt_nonneg);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long items = 2ll * c.H * c.nchunks_max;
+  if (items > 0x7fffffffll) return cudaErrorInvalidValue;
+  const int grid = (int)(items < sms ? items : sms);  // persistent: one CTA per SM
+  kern<<<grid, kScanThreads, kScanSmem, c.stream>>>(mx, mc, mb, mh, A, dt, cum, D,
+                                                    reinterpret_cast<const typename T16Of<BF16>::type*>(z),
+                                                    reinterpret_cast<YT*>(y), c.cm, c.H, c.H / c.G, dt_nonneg,
+                                                    (int)items);
   return cudaGetLastError();
 }
 

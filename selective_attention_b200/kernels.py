@@ -40,6 +40,12 @@ def _chunk_major(t: torch.Tensor) -> torch.Tensor:
     return t.permute(0, 2, 1, 3).contiguous()
 
 
+def _aligned16(t: torch.Tensor) -> torch.Tensor:
+    """The tensor-core path moves tiles with TMA / bulk copies, which need 16-byte
+    aligned base addresses; an offset view is copied into a fresh allocation."""
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def _stream(dev) -> c_void_p:
     return c_void_p(_lib.stream_handle(dev))
 
@@ -150,11 +156,12 @@ def ssd_scan_params(u, A, B, C, delta_raw, delta_bias=None, h_init=None, length=
     delta_bias = None if delta_bias is None else to_contiguous(delta_bias.float())
     h_init = None if h_init is None else to_contiguous(h_init.float())
     length = None if length is None else to_contiguous(length.to(torch.int64))
-    D = None if D is None else to_contiguous(D.float())
+    D = None if D is None else _aligned16(to_contiguous(D.float()))
     if z is not None:
         if z.dtype != u.dtype:
             raise ValueError(f"[z] dtype {z.dtype} differs from u's {u.dtype}")
-        z = to_contiguous(z)
+        z = _aligned16(to_contiguous(z))
+    u, B, C = _aligned16(u), _aligned16(B), _aligned16(C)
     if y_dtype is None:
         y_dtype = u.dtype if (D is not None or z is not None) else torch.float32
     nseq = 0
