@@ -9,19 +9,19 @@
 //   M = 128 (dstate), N = 64 (headdim), K = 128 tokens per phase; both operands
 //   MN-major (token rows of 128 B as TMA lands them); x is scaled by w_l in place.
 //
-// chunk_scan (ssd_scan/forward_kernel.py:350-455 with bmm_chunk :270-328 fused),
-// one CTA (8 warps) per (128-row half m of a chunk, head, chunk), ~100 KB of shared
-// memory (2 CTAs per SM). Rows l of half m see tokens s in [0, 128(m+1)), taken in
-// 128-token phases j = 0..m that reuse one B/x buffer:
+// chunk_scan (ssd_scan/forward_kernel.py:350-455 with bmm_chunk :270-328 fused):
+// persistent and warp-specialised (one CTA per SM, see tc_chunk_scan_kernel). For
+// the 128 rows l of half m of a chunk and 128-token source blocks j = 0..m:
 //   MMA1  CB_j[l, s]  = C[l, :] . B[s, :]          M 128, N 128, K 128 (K-major)
 //   CB_j -> M_j[l, s] = CB * decay(l, s) * dt_s  (bf16/fp16, K-major, over the B tile)
 //   MMA2  Yin[l, p]  += sum_s M_j[l, s] x[s, p]    M 128, N 64, K 128 (x MN-major)
-//   MMA3  Yoff[l, p]  = C[l, :] . prev[p, :]        M 128, N 64, K 128 (phase 0)
+//   MMA3  Yoff[l, p]  = C[l, :] . prev[p, :]        M 128, N 64, K 128 (block 0)
 //   y = exp(cum_l) * Yoff + Yin (+ D x) (* silu z)
-// decay(l, s) = exp(min(cum_l - cum_s, 0)) with s <= l. In an off-diagonal phase
-// (j < m, every s < l) it is evaluated as exp(cum_l - cum_r) * exp(cum_r - cum_s)
-// with r = 128j + 127, both factors <= 1, whenever cum is non-increasing (A <= 0
-// and dt >= 0: then min(., 0) is the identity); otherwise element by element.
+// decay(l, s) = exp(min(cum_l - cum_s, 0)) with s <= l. Per 32x32 tile it is
+// evaluated as exp(cum_l - cum_r) * exp(cum_r - cum_s), r the tile's last column,
+// whenever cum is non-increasing (A <= 0 and dt >= 0, so min(., 0) is the identity)
+// and, on diagonal tiles, the tile's own decay is below 80 (no overflow); otherwise
+// element by element.
 //
 // All tiles use the 128-byte swizzle; accumulators are fp32 in TMEM. Every mbarrier
 // wait is bounded: a CTA that gives up records a site code in the error flag and
@@ -249,13 +249,13 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
 //   warp 1 (one lane)  MMA issuer: MMA1 CB = C B^T into the stage's TMEM slot
 //                      (+ MMA3 Yoff = C prev^T for job 0), then - one job behind -
 //                      MMA2 Yin += M x once the compute warps have written M;
-//   warps 2..9         compute: CB -> M conversion per job, epilogue per item.
+//   warps 2..17        compute: CB -> M conversion per job, epilogue per item.
 // TMEM: CB slots [0,128) and [128,256) per stage; Yin/Yoff slots at 256 + 128*(item&1).
 // Every wait is bounded; a role that gives up records the site, raises the CTA's
 // abort flag and leaves its loop; the others then give up at their next wait.
 constexpr int kScanStageBytes = 98304;  // sC 32K | sB 32K | sX 16K | sH 16K
 constexpr int kScanSmallBytes = 3072;   // dt 1K | cum 1K | D 256 | colf 512 | flags
-constexpr int kScanThreads = 320;
+constexpr int kScanThreads = 576;  // warp 0 TMA, warp 1 MMA, warps 2..17 compute
 constexpr int kScanSmem = 2 * kScanStageBytes + 2 * kScanSmallBytes + 256 + 1024;
 
 // Item `it` -> (chunk, head, half); false if the half holds no token of the row.
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   auto stage = [&](int s) { return smem + s * kScanStageBytes; };
   auto small = [&](int s) { return reinterpret_cast<float*>(small0 + s * kScanSmallBytes); };
-  // small stage layout (floats): dt [0,256) cum [256,512) D [512,576) colf [576,704) flags [704,708)
+  // small stage layout (floats): dt [0,256) cum [256,512) D [512,576) colf [576,704) flags [704,708) A_h [708]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -298,9 +298,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(0 + s), 1);  // full: producer's expect_tx
       mbar_init(bar(2 + s), 1);  // cbfull: MMA commit
-      mbar_init(bar(4 + s), 8);  // mfull: one arrive per compute warp
+      mbar_init(bar(4 + s), 16);  // mfull: one arrive per compute warp
       mbar_init(bar(6 + s), 1);  // jobdone: MMA commit
-      mbar_init(bar(8 + s), 8);  // epidone (per Y slot): one arrive per compute warp
+      mbar_init(bar(8 + s), 16);  // epidone (per Y slot): one arrive per compute warp
     }
     *s_abort = 0;
     fence_mbar_init();
@@ -339,6 +339,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           const bool withD = (j == m) && D != nullptr;
           const uint32_t bytes = 32768u + 32768u + 16384u + (j == 0 ? 16384u : 0u) + 2048u + (withD ? 256u : 0u);
           const uint32_t fb = bar(0 + s);
+          sm[708] = A[h];  // published to the compute warps by the arrive below (release)
           mbar_expect_tx(fb, bytes);
           tma_load_3d(smem_u32(st), &tm_c, 0, g, t0 + 128 * m, fb);
           tma_load_3d(smem_u32(st + 16384), &tm_c, 64, g, t0 + 128 * m, fb);
@@ -441,8 +442,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     __syncwarp();
   } else {
     // ------------------------------------------------------------ compute warps
+    // 16 warps: TMEM lane quadrant quad = warp % 4 (rows 32*quad ..), column group
+    // cg = (warp - 2) / 4: the 32-column block cg of CB in the conversion and the
+    // 16 output columns [16*cg, 16*cg + 16) in the epilogue.
     const int ctid = tid - 64;
-    const int quad = warp & 3, ch = (warp - 2) >> 2;
+    const int quad = warp & 3, cg = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     int J = 0, nI = 0;
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
@@ -450,7 +454,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       int k, h, m;
       if (!scan_item(cm, it, H, ci, k, h, m)) continue;
       const int lbase = 128 * m, l = lbase + r, slot = nI & 1, wr0 = lbase + quad * 32;
-      const bool mono = dt_nonneg && (A[h] <= 0.f);
       bool fail = false;
       for (int j = 0; j <= m; ++j) {
         const int s = J & 1, par = (J >> 1) & 1, sbase = 128 * j;
@@ -463,76 +466,69 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         float* sColf = sm + 576;
         int* sBlkOk = reinterpret_cast<int*>(sm + 704);
         bool ok = mbar_wait(bar(0 + s), par, kSiteScanTma);
-        if (!named_bar_and(1, 256, ok && !*s_abort)) { fail = true; break; }
+        if (!named_bar_and(1, 512, ok && !*s_abort)) { fail = true; break; }
+        // cum non-increasing (A <= 0 and dt >= 0) => min(cum_l - cum_s, 0) = cum_l - cum_s
+        const bool mono = dt_nonneg && (sm[708] <= 0.f);
         if (ctid < 128) {
           const int sl = sbase + ctid;
           const float cr = sCum[sbase + (ctid | 31)];
           sColf[ctid] = mono ? __expf(cr - sCum[sl]) * sDt[sl] : 0.f;
           if ((ctid & 31) == 0) sBlkOk[ctid >> 5] = mono && (sCum[sl] - cr <= 80.f);
         }
-        // x rows past `lim` -> exact zeros, so they cannot leak into Yin
-        for (int q = ctid; q < 1024; q += 256)
-          if (sbase + (q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
+        if (sbase + 128 > ci.lim) {
+          // x rows past `lim` -> exact zeros, so they cannot leak into Yin
+          for (int q = ctid; q < 1024; q += 512)
+            if (sbase + (q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
         ok = mbar_wait(bar(2 + s), par, kSiteScanMma1);
         tc_fence_after();
-        if (!named_bar_and(1, 256, ok)) { fail = true; break; }  // also publishes colf / flags
+        if (!named_bar_and(1, 512, ok)) { fail = true; break; }  // also publishes colf / flags
         const float cl = sCum[l];
-        // ---- CB (TMEM) -> M (K-major over the B tile) ----
-        const uint32_t tq = tmem + ((uint32_t)(quad * 32) << 16) + 128 * s;
-        uint32_t v[2][32];
-        int kind[2];  // 0: above the diagonal, 1: factored, 2: element by element
-#pragma unroll
-        for (int cbi = 0; cbi < 2; ++cbi) {
-          const int cb = 2 * cbi + ch;
-          const int s0 = sbase + cb * 32;
-          if (s0 > wr0 + 31) {
-            kind[cbi] = 0;
-          } else {
-            const bool diag = s0 + 31 >= wr0;
-            kind[cbi] = (diag ? sBlkOk[cb] : mono) ? 1 : 2;
-            tmem_ld32(tq + cb * 32, v[cbi]);
-          }
-        }
-        tmem_wait_ld();
-#pragma unroll
-        for (int cbi = 0; cbi < 2; ++cbi) {
-          const int cb = 2 * cbi + ch;
+        // ---- CB (TMEM) -> M (K-major over the B tile): block cg, rows of this quadrant ----
+        {
+          const int cb = cg;
           const int s0 = sbase + cb * 32;
           uint32_t pk[16];
-          if (kind[cbi] == 0) {
+          if (s0 > wr0 + 31) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) pk[jj] = 0u;
-          } else if (kind[cbi] == 1) {
-            const float rowf = __expf(cl - sCum[s0 + 31]);
-            const float4* cf = reinterpret_cast<const float4*>(sColf + cb * 32);
-            const bool diag = s0 + 31 >= wr0;
-#pragma unroll
-            for (int q4 = 0; q4 < 8; ++q4) {
-              const float4 c4 = cf[q4];
-              float x0 = __uint_as_float(v[cbi][4 * q4]) * rowf * c4.x;
-              float x1 = __uint_as_float(v[cbi][4 * q4 + 1]) * rowf * c4.y;
-              float x2 = __uint_as_float(v[cbi][4 * q4 + 2]) * rowf * c4.z;
-              float x3 = __uint_as_float(v[cbi][4 * q4 + 3]) * rowf * c4.w;
-              if (diag) {
-                const int sa = s0 + 4 * q4;
-                x0 = sa <= l ? x0 : 0.f;
-                x1 = sa + 1 <= l ? x1 : 0.f;
-                x2 = sa + 2 <= l ? x2 : 0.f;
-                x3 = sa + 3 <= l ? x3 : 0.f;
-              }
-              pk[2 * q4] = pack2<T16>(x0, x1);
-              pk[2 * q4 + 1] = pack2<T16>(x2, x3);
-            }
           } else {
+            const bool diag = s0 + 31 >= wr0;  // blocks are aligned: the 32x32 diagonal tile
+            const bool fac = diag ? (sBlkOk[cb] != 0) : mono;
+            uint32_t v[32];
+            tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + 128 * s + cb * 32, v);
+            tmem_wait_ld();
+            if (fac) {
+              const float rowf = __expf(cl - sCum[s0 + 31]);
+              const float4* cf = reinterpret_cast<const float4*>(sColf + cb * 32);
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const int sa = s0 + 2 * jj, sb2 = sa + 1;
-              float x0 = 0.f, x1 = 0.f;
-              if (sa <= l && sa < ci.lim)
-                x0 = __uint_as_float(v[cbi][2 * jj]) * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
-              if (sb2 <= l && sb2 < ci.lim)
-                x1 = __uint_as_float(v[cbi][2 * jj + 1]) * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
-              pk[jj] = pack2<T16>(x0, x1);
+              for (int q4 = 0; q4 < 8; ++q4) {
+                const float4 c4 = cf[q4];
+                float x0 = __uint_as_float(v[4 * q4]) * rowf * c4.x;
+                float x1 = __uint_as_float(v[4 * q4 + 1]) * rowf * c4.y;
+                float x2 = __uint_as_float(v[4 * q4 + 2]) * rowf * c4.z;
+                float x3 = __uint_as_float(v[4 * q4 + 3]) * rowf * c4.w;
+                if (diag) {
+                  const int sa = s0 + 4 * q4;
+                  x0 = sa <= l ? x0 : 0.f;
+                  x1 = sa + 1 <= l ? x1 : 0.f;
+                  x2 = sa + 2 <= l ? x2 : 0.f;
+                  x3 = sa + 3 <= l ? x3 : 0.f;
+                }
+                pk[2 * q4] = pack2<T16>(x0, x1);
+                pk[2 * q4 + 1] = pack2<T16>(x2, x3);
+              }
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) {
+                const int sa = s0 + 2 * jj, sb2 = sa + 1;
+                float x0 = 0.f, x1 = 0.f;
+                if (sa <= l && sa < ci.lim)
+                  x0 = __uint_as_float(v[2 * jj]) * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
+                if (sb2 <= l && sb2 < ci.lim)
+                  x1 = __uint_as_float(v[2 * jj + 1]) * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
+                pk[jj] = pack2<T16>(x0, x1);
+              }
             }
           }
           uint8_t* base = sB + (cb >> 1) * 16384;
@@ -547,53 +543,63 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(4 + s));
         if (j == m) {
-          // ---- epilogue: y = exp(cum_l) Yoff + Yin (+ D x) (* silu z) ----
+          // ---- epilogue: y = exp(cum_l) Yoff + Yin (+ D x) (* silu z), columns [16cg, 16cg+16) ----
           const long long tok = ci.tok0 + l;
           const bool valid = l < ci.lim;
-          const long long yrow = (tok * H + h) * 64 + ch * 32;
-          uint4 zv[4];
+          const long long yrow = (tok * H + h) * 64 + cg * 16;
+          uint4 zv[2];
           if (z && valid) {
             const uint4* zp = reinterpret_cast<const uint4*>(z + yrow);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) zv[q] = zp[q];
+            zv[0] = zp[0];
+            zv[1] = zp[1];
           }
           ok = mbar_wait(bar(6 + s), par, kSiteScanMma2);
           tc_fence_after();
-          if (!named_bar_and(1, 256, ok)) { fail = true; break; }
+          if (!named_bar_and(1, 512, ok)) { fail = true; break; }
           const uint32_t ty = tmem + ((uint32_t)(quad * 32) << 16) + 256 + 128 * slot;
-          uint32_t ri[32], ro[32];
-          tmem_ld32(ty + ch * 32, ri);
-          tmem_ld32(ty + 64 + ch * 32, ro);
+          uint32_t ri[16], ro[16];
+          tmem_ld16(ty + cg * 16, ri);
+          tmem_ld16(ty + 64 + cg * 16, ro);
           tmem_wait_ld();
           tc_fence_before();
           if (valid) {
             const float el = __expf(cl);
-            float o[32];
+            float o[16];
 #pragma unroll
-            for (int jj = 0; jj < 32; ++jj) o[jj] = fmaf(el, __uint_as_float(ro[jj]), __uint_as_float(ri[jj]));
+            for (int jj = 0; jj < 16; ++jj) o[jj] = fmaf(el, __uint_as_float(ro[jj]), __uint_as_float(ri[jj]));
             if (D) {
-              const float* sD = sm + 512 + ch * 32;
+              const float4* sD4 = reinterpret_cast<const float4*>(sm + 512 + cg * 16);
+              float dd[16];
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
-                const uint4 xv = *reinterpret_cast<const uint4*>(sX + sw128_off(r, ch * 4 + q));
+                const float4 d4 = sD4[q];
+                dd[4 * q] = d4.x;
+                dd[4 * q + 1] = d4.y;
+                dd[4 * q + 2] = d4.z;
+                dd[4 * q + 3] = d4.w;
+              }
+#pragma unroll
+              for (int q = 0; q < 2; ++q) {
+                const uint4 xv = *reinterpret_cast<const uint4*>(sX + sw128_off(r, cg * 2 + q));
                 const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const float2 f = unpack2<T16>(w4[e]);
                   const int pi = q * 8 + 2 * e;
-                  o[pi] = fmaf(sD[pi], f.x, o[pi]);
-                  o[pi + 1] = fmaf(sD[pi + 1], f.y, o[pi + 1]);
+                  o[pi] = fmaf(dd[pi], f.x, o[pi]);
+                  o[pi + 1] = fmaf(dd[pi + 1], f.y, o[pi + 1]);
                 }
               }
             }
             if (z) {
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
+              for (int q = 0; q < 2; ++q) {
                 const uint32_t w4[4] = {zv[q].x, zv[q].y, zv[q].z, zv[q].w};
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const float2 f = unpack2<T16>(w4[e]);
                   const float h0 = 0.5f * f.x, h1 = 0.5f * f.y;
+                  // silu(z) = z * sigmoid(z) = h + h * tanh(h), h = z / 2
                   o[q * 8 + 2 * e] *= fmaf(h0, tanh_approx(h0), h0);
                   o[q * 8 + 2 * e + 1] *= fmaf(h1, tanh_approx(h1), h1);
                 }
@@ -602,11 +608,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
             if constexpr (sizeof(YT) == 4) {
               float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow);
 #pragma unroll
-              for (int q = 0; q < 8; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+              for (int q = 0; q < 4; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
             } else {
               uint4* yp = reinterpret_cast<uint4*>(y + yrow);
 #pragma unroll
-              for (int q = 0; q < 4; ++q)
+              for (int q = 0; q < 2; ++q)
                 yp[q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
                                    pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
             }
