@@ -238,35 +238,50 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
 }
 
 // ===========================================================================
-// chunk_scan (+ bmm_chunk): persistent and warp-specialised
+// chunk_scan (+ bmm_chunk): persistent, warp-specialised, CB shared across heads
 // ===========================================================================
-// Work items are (chunk k, head h, half m); an item is m + 1 jobs, job j covering
-// source tokens [128j, 128j + 128) for the rows of half m. One CTA per SM walks
-// items blockIdx.x, blockIdx.x + gridDim.x, ... with three roles:
-//   warp 0 (one lane)  TMA producer: per job, C rows of the half, B and x rows of
-//                      the job, prev[k, h] (job 0), dt / cum (and D) into a stage
-//                      of a 2-deep shared-memory ring;
-//   warp 1 (one lane)  MMA issuer: MMA1 CB = C B^T into the stage's TMEM slot
-//                      (+ MMA3 Yoff = C prev^T for job 0), then - one job behind -
-//                      MMA2 Yin += M x once the compute warps have written M;
-//   warps 2..17        compute: CB -> M conversion per job, epilogue per item.
-// TMEM: CB slots [0,128) and [128,256) per stage; Yin/Yoff slots at 256 + 128*(item&1).
-// Every wait is bounded; a role that gives up records the site, raises the CTA's
-// abort flag and leaves its loop; the others then give up at their next wait.
-constexpr int kScanStageBytes = 98304;  // sC 32K | sB 32K | sX 16K | sH 16K
-constexpr int kScanSmallBytes = 3072;   // dt 1K | cum 1K | D 256 | colf 512 | flags
-constexpr int kScanThreads = 576;  // warp 0 TMA, warp 1 MMA, warps 2..17 compute
-constexpr int kScanSmem = 2 * kScanStageBytes + 2 * kScanSmallBytes + 256 + 1024;
+// Work items are (chunk k, half m, group g, block of up to HB heads of the group).
+// Per item, C rows of the half and B rows [0, 128(m+1)) are loaded once and
+// CB_j = C B_j^T (j = 0..m, 128 source tokens each) is computed once into TMEM;
+// then, head by head, only x, prev, dt, cum and D are loaded, and
+//   M_j[l, s] = CB_j[l, s] * decay_h(l, s) * dt_s   (written to TMEM, 16-bit)
+//   Yin      += M_j x_j      (A from TMEM)    Yoff = C prev^T    (per head)
+//   y = exp(cum_l) Yoff + Yin (+ D x) (* silu z)
+// Roles (one CTA per SM, items blockIdx.x, blockIdx.x + gridDim.x, ...):
+//   warp 0 (one lane)  TMA producer: item tiles (C, B) single-buffered, head tiles
+//                      (x, prev, dt, cum, D) in a 2-deep ring;
+//   warp 1 (one lane)  MMA issuer;
+//   warps 2..17        compute: CB -> M conversion (warp: one 32-column block of a
+//                      32-row quadrant), then the head's epilogue (16 output columns).
+// TMEM columns: CB_0 [0,128) CB_1 [128,256) M buffers [256,320) [320,384)
+//               Yin [384,448) Yoff [448,512).
+// Barriers that a role may lag behind are kept per ring slot, so a waiter is never
+// two phases behind the barrier it polls. Every wait is bounded; a role that gives
+// up records the site, raises the CTA's abort flag and leaves its loop.
+constexpr int kScanHeadStageBytes = 32768 + 16384;  // x rows [0, 256) | prev
+constexpr int kScanSmallBytes = 4096;                // dt 1K | cum 1K | D 256 | colf 1K | flags | A
+constexpr int kScanThreads = 576;                    // warp 0 TMA, warp 1 MMA, warps 2..17 compute
+constexpr int kScanSmem = 32768 + 65536 + 2 * kScanHeadStageBytes + 2 * kScanSmallBytes + 256 + 1024;
 
-// Item `it` -> (chunk, head, half); false if the half holds no token of the row.
-__device__ __forceinline__ bool scan_item(const ChunkMap& cm, int it, int H, ChunkInfo& ci, int& k, int& h,
-                                          int& m) {
-  k = it / (2 * H);
-  const int rem = it - k * 2 * H;
-  h = rem >> 1;
-  m = 1 - (rem & 1);  // the heavier half of a (chunk, head) first
-  if (!chunk_info(cm, k, ci)) return false;
-  return 128 * m < ci.lim;
+struct ScanItem {
+  int k, m, g, h0, nh;  // chunk, half, group, first head, heads in the block
+};
+
+// Item `it` -> ScanItem; false if the half holds no token of the row.
+__device__ __forceinline__ bool scan_item(const ChunkMap& cm, int it, int G, int hpg, int HB, ScanItem& si,
+                                          ChunkInfo& ci) {
+  const int nhb = (hpg + HB - 1) / HB;
+  int rem = it;
+  const int hbi = rem % nhb;
+  rem /= nhb;
+  si.g = rem % G;
+  rem /= G;
+  si.m = 1 - (rem & 1);  // the heavier half of a chunk first
+  si.k = rem >> 1;
+  si.h0 = si.g * hpg + hbi * HB;
+  si.nh = min(HB, hpg - hbi * HB);
+  if (!chunk_info(cm, si.k, ci)) return false;
+  return 128 * si.m < ci.lim;
 }
 
 template <bool BF16, typename YT>
@@ -275,19 +290,25 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_h,
     const float* __restrict__ A, const float* __restrict__ dt, const float* __restrict__ cum,
     const float* __restrict__ D, const typename T16Of<BF16>::type* __restrict__ z, YT* __restrict__ y, ChunkMap cm,
-    int H, int hpg, int dt_nonneg, int n_items) {
+    int H, int G, int HB, int dt_nonneg, int n_items) {
   using T16 = typename T16Of<BF16>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* small0 = smem + 2 * kScanStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(small0 + 2 * kScanSmallBytes);
-  // full[2] cbfull[2] mfull[2] jobdone[2] epidone[2]
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint8_t* sC = smem;           // 2 x (128 rows x 128 B): dstate halves of the half's C rows
+  uint8_t* sB = smem + 32768;   // per job j: 2 x (128 rows x 128 B) at 32768 * j
+  auto hstage = [&](int s) { return smem + 98304 + s * kScanHeadStageBytes; };  // x [0,32K) prev [32K,48K)
+  auto small = [&](int s) {
+    return reinterpret_cast<float*>(smem + 98304 + 2 * kScanHeadStageBytes + s * kScanSmallBytes);
+  };
+  // small layout (floats): dt [0,256) cum [256,512) D [512,576) colf [576,832) flags [832,840) A_h [840]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 98304 + 2 * kScanHeadStageBytes + 2 * kScanSmallBytes);
+  enum { ITEM_FULL = 0, CB_FULL, C_FREE, CB_FREE, HEAD_FULL0, HEAD_FULL1, EPI0, EPI1, MFULL0, MFULL1, M2DONE0,
+         M2DONE1, NBARS };
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  auto stage = [&](int s) { return smem + s * kScanStageBytes; };
-  auto small = [&](int s) { return reinterpret_cast<float*>(small0 + s * kScanSmallBytes); };
-  // small stage layout (floats): dt [0,256) cum [256,512) D [512,576) colf [576,704) flags [704,708) A_h [708]
+  const int hpg = H / G;
+  const uint32_t T_M = 256, T_YIN = 384, T_YOFF = 448;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -295,12 +316,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     prefetch_tmap(&tm_c);
     prefetch_tmap(&tm_b);
     prefetch_tmap(&tm_h);
+    mbar_init(bar(ITEM_FULL), 1);
+    mbar_init(bar(CB_FULL), 1);
+    mbar_init(bar(C_FREE), 1);
+    mbar_init(bar(CB_FREE), 16);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(0 + s), 1);  // full: producer's expect_tx
-      mbar_init(bar(2 + s), 1);  // cbfull: MMA commit
-      mbar_init(bar(4 + s), 16);  // mfull: one arrive per compute warp
-      mbar_init(bar(6 + s), 1);  // jobdone: MMA commit
-      mbar_init(bar(8 + s), 16);  // epidone (per Y slot): one arrive per compute warp
+      mbar_init(bar(HEAD_FULL0 + s), 1);
+      mbar_init(bar(EPI0 + s), 16);
+      mbar_init(bar(MFULL0 + s), 16);
+      mbar_init(bar(M2DONE0 + s), 1);
     }
     *s_abort = 0;
     fence_mbar_init();
@@ -314,59 +338,56 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int J = 0, nI = 0;
-      int last_item[2] = {-1, -1};
-      bool issued[2] = {false, false};
-      int last_J[2] = {0, 0};
-      for (int it = blockIdx.x; it < n_items && !*s_abort; it += gridDim.x) {
+      int I = 0, Hc = 0;
+      bool fail = false;
+      for (int it = blockIdx.x; it < n_items && !fail && !*s_abort; it += gridDim.x) {
+        ScanItem si;
         ChunkInfo ci;
-        int k, h, m;
-        if (!scan_item(cm, it, H, ci, k, h, m)) continue;
-        const int g = h / hpg, t0 = (int)ci.tok0;
-        bool fail = false;
-        for (int j = 0; j <= m; ++j) {
-          const int s = J & 1;
-          if (J >= 2) {
-            if (!mbar_wait(bar(6 + s), ((J - 2) >> 1) & 1, kSiteScanMma2)) { fail = true; break; }
-            if (last_item[s] >= 0 &&
-                !mbar_wait(bar(8 + (last_item[s] & 1)), (last_item[s] >> 1) & 1, kSiteScanEpi)) {
-              fail = true;
-              break;
-            }
+        if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
+        const int t0 = (int)ci.tok0, S = 128 * (si.m + 1);
+        if (I > 0) {
+          // B tiles free once the previous item's MMA1 completed; C once its last MMA3 did.
+          if (!mbar_wait(bar(CB_FULL), (I - 1) & 1, kSiteScanMma1) ||
+              !mbar_wait(bar(C_FREE), (I - 1) & 1, kSiteScanMma1)) {
+            fail = true;
+            break;
           }
-          uint8_t* st = stage(s);
-          float* sm = small(s);
-          const bool withD = (j == m) && D != nullptr;
-          const uint32_t bytes = 32768u + 32768u + 16384u + (j == 0 ? 16384u : 0u) + 2048u + (withD ? 256u : 0u);
-          const uint32_t fb = bar(0 + s);
-          sm[708] = A[h];  // published to the compute warps by the arrive below (release)
-          mbar_expect_tx(fb, bytes);
-          tma_load_3d(smem_u32(st), &tm_c, 0, g, t0 + 128 * m, fb);
-          tma_load_3d(smem_u32(st + 16384), &tm_c, 64, g, t0 + 128 * m, fb);
-          tma_load_3d(smem_u32(st + 32768), &tm_b, 0, g, t0 + 128 * j, fb);
-          tma_load_3d(smem_u32(st + 49152), &tm_b, 64, g, t0 + 128 * j, fb);
-          tma_load_3d(smem_u32(st + 65536), &tm_x, 0, h, t0 + 128 * j, fb);
-          if (j == 0) {
-            tma_load_3d(smem_u32(st + 81920), &tm_h, 0, 0, k * H + h, fb);
-            tma_load_3d(smem_u32(st + 90112), &tm_h, 64, 0, k * H + h, fb);
+        }
+        mbar_expect_tx(bar(ITEM_FULL), 32768u + (uint32_t)S * 256u);
+        tma_load_3d(smem_u32(sC), &tm_c, 0, si.g, t0 + 128 * si.m, bar(ITEM_FULL));
+        tma_load_3d(smem_u32(sC + 16384), &tm_c, 64, si.g, t0 + 128 * si.m, bar(ITEM_FULL));
+        for (int j = 0; j <= si.m; ++j) {
+          tma_load_3d(smem_u32(sB + 32768 * j), &tm_b, 0, si.g, t0 + 128 * j, bar(ITEM_FULL));
+          tma_load_3d(smem_u32(sB + 32768 * j + 16384), &tm_b, 64, si.g, t0 + 128 * j, bar(ITEM_FULL));
+        }
+        for (int i = 0; i < si.nh; ++i) {
+          const int h = si.h0 + i, hs = Hc & 1;
+          if (Hc >= 2 && !mbar_wait(bar(EPI0 + hs), ((Hc - 2) >> 1) & 1, kSiteScanEpi)) {
+            fail = true;
+            break;
           }
-          bulk_load(smem_u32(sm), dt + ((long long)k * H + h) * 256, 1024u, fb);
-          bulk_load(smem_u32(sm + 256), cum + ((long long)k * H + h) * 256, 1024u, fb);
-          if (withD) bulk_load(smem_u32(sm + 512), D + h * 64, 256u, fb);
-          issued[s] = true;
-          last_J[s] = J;
-          last_item[s] = (j == m) ? nI : -1;
-          ++J;
+          uint8_t* st = hstage(hs);
+          float* sm = small(hs);
+          const uint32_t fb = bar(HEAD_FULL0 + hs);
+          sm[840] = A[h];  // published by the arrive below (release)
+          mbar_expect_tx(fb, (uint32_t)S * 128u + 16384u + 2048u + (D ? 256u : 0u));
+          for (int j = 0; j <= si.m; ++j) tma_load_3d(smem_u32(st + 16384 * j), &tm_x, 0, h, t0 + 128 * j, fb);
+          tma_load_3d(smem_u32(st + 32768), &tm_h, 0, 0, si.k * H + h, fb);
+          tma_load_3d(smem_u32(st + 40960), &tm_h, 64, 0, si.k * H + h, fb);
+          bulk_load(smem_u32(sm), dt + ((long long)si.k * H + h) * 256, 1024u, fb);
+          bulk_load(smem_u32(sm + 256), cum + ((long long)si.k * H + h) * 256, 1024u, fb);
+          if (D) bulk_load(smem_u32(sm + 512), D + h * 64, 256u, fb);
+          ++Hc;
         }
-        if (fail) {
-          *s_abort = 1;
-          break;
-        }
-        ++nI;
+        ++I;
       }
+      if (fail) *s_abort = 1;
       // No copy may still be in flight when the CTA exits.
-      for (int s = 0; s < 2; ++s)
-        if (issued[s]) mbar_wait(bar(0 + s), (last_J[s] >> 1) & 1, kSiteScanTma);
+      if (I > 0) mbar_wait(bar(ITEM_FULL), (I - 1) & 1, kSiteScanTma);
+      for (int d = 1; d <= 2 && d <= Hc; ++d) {
+        const int hc = Hc - d;
+        mbar_wait(bar(HEAD_FULL0 + (hc & 1)), (hc >> 1) & 1, kSiteScanTma);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -375,132 +396,133 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       const uint32_t id_cb = idesc_f16(128, 128, BF16, false, false);
       const uint32_t id_off = idesc_f16(128, 64, BF16, false, false);
       const uint32_t id_in = idesc_f16(128, 64, BF16, false, true);
-      int J = 0, nI = 0;
-      bool have_prev = false, fail = false, committed = false;
-      int pv_s = 0, pv_J = 0, pv_slot = 0, pv_j = 0, last_commit_s = 0, last_commit_J = 0;
-      auto mma2 = [&]() -> bool {
-        if (!mbar_wait(bar(4 + pv_s), (pv_J >> 1) & 1, kSiteScanConv)) return false;
-        tc_fence_after();
-        const uint32_t m0 = smem_u32(stage(pv_s) + 32768), x0 = smem_u32(stage(pv_s) + 65536);
-        const uint32_t yin = tmem + 256 + 128 * pv_slot;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t sb = ks >> 2, kk = (ks & 3) * 32;
-          umma_f16(yin, sdesc_sw128(m0 + sb * 16384 + kk, 16, 1024), sdesc_sw128(x0 + ks * 2048, 16, 1024), id_in,
-                   (pv_j > 0 || ks > 0) ? 1u : 0u);
-        }
-        umma_commit(bar(6 + pv_s));
-        committed = true;
-        last_commit_s = pv_s;
-        last_commit_J = pv_J;
-        return true;
-      };
+      int I = 0, Hc = 0, Jc = 0;
+      bool fail = false;
+      int last_bar = -1, last_par = 0;
       for (int it = blockIdx.x; it < n_items && !fail && !*s_abort; it += gridDim.x) {
+        ScanItem si;
         ChunkInfo ci;
-        int k, h, m;
-        if (!scan_item(cm, it, H, ci, k, h, m)) continue;
-        const int slot = nI & 1;
-        for (int j = 0; j <= m; ++j) {
-          const int s = J & 1;
-          if (!mbar_wait(bar(0 + s), (J >> 1) & 1, kSiteScanTma)) { fail = true; break; }
-          if (j == 0 && nI >= 2 && !mbar_wait(bar(8 + slot), ((nI - 2) >> 1) & 1, kSiteScanEpi)) {
+        if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
+        if (!mbar_wait(bar(ITEM_FULL), I & 1, kSiteScanTma) ||
+            (I > 0 && !mbar_wait(bar(CB_FREE), (I - 1) & 1, kSiteScanConv))) {
+          fail = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t c0 = smem_u32(sC);
+        for (int j = 0; j <= si.m; ++j) {
+          const uint32_t b0 = smem_u32(sB + 32768 * j);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
+            umma_f16(tmem + 128 * j, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
+                     sdesc_sw128(b0 + hf * 16384 + kk, 16, 1024), id_cb, ks > 0 ? 1u : 0u);
+          }
+        }
+        umma_commit(bar(CB_FULL));
+        for (int i = 0; i < si.nh && !fail; ++i) {
+          const int hs = Hc & 1;
+          if (!mbar_wait(bar(HEAD_FULL0 + hs), (Hc >> 1) & 1, kSiteScanTma) ||
+              (Hc >= 1 && !mbar_wait(bar(EPI0 + ((Hc - 1) & 1)), ((Hc - 1) >> 1) & 1, kSiteScanEpi))) {
             fail = true;
             break;
           }
           tc_fence_after();
-          const uint32_t c0 = smem_u32(stage(s)), b0 = smem_u32(stage(s) + 32768), h0 = smem_u32(stage(s) + 81920);
+          const uint32_t h0 = smem_u32(hstage(hs) + 32768), x0 = smem_u32(hstage(hs));
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
-            umma_f16(tmem + 128 * s, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
-                     sdesc_sw128(b0 + hf * 16384 + kk, 16, 1024), id_cb, ks > 0 ? 1u : 0u);
+            umma_f16(tmem + T_YOFF, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
+                     sdesc_sw128(h0 + hf * 8192 + kk, 16, 1024), id_off, ks > 0 ? 1u : 0u);
           }
-          if (j == 0) {
-#pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-              const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
-              umma_f16(tmem + 256 + 128 * slot + 64, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
-                       sdesc_sw128(h0 + hf * 8192 + kk, 16, 1024), id_off, ks > 0 ? 1u : 0u);
+          if (i == si.nh - 1) umma_commit(bar(C_FREE));
+          for (int j = 0; j <= si.m; ++j) {
+            const int mb = Jc & 1;
+            if (!mbar_wait(bar(MFULL0 + mb), (Jc >> 1) & 1, kSiteScanConv)) {
+              fail = true;
+              break;
             }
+            tc_fence_after();
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+              umma_f16_ts(tmem + T_YIN, tmem + T_M + 64 * mb + 8 * ks,
+                          sdesc_sw128(x0 + 16384 * j + ks * 2048, 16, 1024), id_in, (j > 0 || ks > 0) ? 1u : 0u);
+            umma_commit(bar(M2DONE0 + mb));
+            last_bar = M2DONE0 + mb;
+            last_par = (Jc >> 1) & 1;
+            ++Jc;
           }
-          umma_commit(bar(2 + s));
-          if (have_prev && !mma2()) { fail = true; break; }
-          have_prev = true;
-          pv_s = s;
-          pv_J = J;
-          pv_slot = slot;
-          pv_j = j;
-          ++J;
+          ++Hc;
         }
-        ++nI;
+        ++I;
       }
-      if (!fail && have_prev && !mma2()) fail = true;
       if (fail) *s_abort = 1;
       // All MMAs must be complete before TMEM is released.
-      if (committed) mbar_wait(bar(6 + last_commit_s), (last_commit_J >> 1) & 1, kSiteScanMma2);
+      if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, kSiteScanMma2);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ compute warps
-    // 16 warps: TMEM lane quadrant quad = warp % 4 (rows 32*quad ..), column group
-    // cg = (warp - 2) / 4: the 32-column block cg of CB in the conversion and the
-    // 16 output columns [16*cg, 16*cg + 16) in the epilogue.
     const int ctid = tid - 64;
     const int quad = warp & 3, cg = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
-    int J = 0, nI = 0;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const uint32_t tlane = (uint32_t)(quad * 32) << 16;
+    int I = 0, Hc = 0, Jc = 0;
+    bool fail = false;
+    for (int it = blockIdx.x; it < n_items && !fail; it += gridDim.x) {
+      ScanItem si;
       ChunkInfo ci;
-      int k, h, m;
-      if (!scan_item(cm, it, H, ci, k, h, m)) continue;
-      const int lbase = 128 * m, l = lbase + r, slot = nI & 1, wr0 = lbase + quad * 32;
-      bool fail = false;
-      for (int j = 0; j <= m; ++j) {
-        const int s = J & 1, par = (J >> 1) & 1, sbase = 128 * j;
-        uint8_t* st = stage(s);
-        uint8_t* sB = st + 32768;
-        uint8_t* sX = st + 65536;
-        float* sm = small(s);
+      if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
+      const int m = si.m, lbase = 128 * m, l = lbase + r, wr0 = lbase + quad * 32, S = 128 * (m + 1);
+      bool ok = mbar_wait(bar(CB_FULL), I & 1, kSiteScanMma1);
+      tc_fence_after();
+      if (!named_bar_and(1, 512, ok && !*s_abort)) { fail = true; break; }
+      for (int i = 0; i < si.nh; ++i) {
+        const int h = si.h0 + i, hs = Hc & 1;
+        uint8_t* sX = hstage(hs);
+        float* sm = small(hs);
         const float* sDt = sm;
         const float* sCum = sm + 256;
         float* sColf = sm + 576;
-        int* sBlkOk = reinterpret_cast<int*>(sm + 704);
-        bool ok = mbar_wait(bar(0 + s), par, kSiteScanTma);
-        if (!named_bar_and(1, 512, ok && !*s_abort)) { fail = true; break; }
+        int* sBlkOk = reinterpret_cast<int*>(sm + 832);
+        ok = mbar_wait(bar(HEAD_FULL0 + hs), (Hc >> 1) & 1, kSiteScanTma);
+        if (!named_bar_and(1, 512, ok)) { fail = true; break; }
         // cum non-increasing (A <= 0 and dt >= 0) => min(cum_l - cum_s, 0) = cum_l - cum_s
-        const bool mono = dt_nonneg && (sm[708] <= 0.f);
-        if (ctid < 128) {
-          const int sl = sbase + ctid;
-          const float cr = sCum[sbase + (ctid | 31)];
-          sColf[ctid] = mono ? __expf(cr - sCum[sl]) * sDt[sl] : 0.f;
-          if ((ctid & 31) == 0) sBlkOk[ctid >> 5] = mono && (sCum[sl] - cr <= 80.f);
+        const bool mono = dt_nonneg && (sm[840] <= 0.f);
+        if (ctid < S) {
+          const float cr = sCum[ctid | 31];
+          sColf[ctid] = mono ? __expf(cr - sCum[ctid]) * sDt[ctid] : 0.f;
+          if ((ctid & 31) == 0) sBlkOk[ctid >> 5] = mono && (sCum[ctid] - cr <= 80.f);
         }
-        if (sbase + 128 > ci.lim) {
+        if (S > ci.lim) {
           // x rows past `lim` -> exact zeros, so they cannot leak into Yin
-          for (int q = ctid; q < 1024; q += 512)
-            if (sbase + (q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
+          for (int q = ctid; q < S * 8; q += 512)
+            if ((q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
-        ok = mbar_wait(bar(2 + s), par, kSiteScanMma1);
-        tc_fence_after();
-        if (!named_bar_and(1, 512, ok)) { fail = true; break; }  // also publishes colf / flags
+        if (!named_bar_and(1, 512, true)) { fail = true; break; }  // publishes colf / flags
         const float cl = sCum[l];
-        // ---- CB (TMEM) -> M (K-major over the B tile): block cg, rows of this quadrant ----
-        {
-          const int cb = cg;
-          const int s0 = sbase + cb * 32;
+        for (int j = 0; j <= m; ++j) {
+          const int mb = Jc & 1;
+          if (Jc >= 2) {
+            ok = mbar_wait(bar(M2DONE0 + mb), ((Jc - 2) >> 1) & 1, kSiteScanMma2);
+            if (!named_bar_and(1, 512, ok)) { fail = true; break; }
+            tc_fence_after();
+          }
+          // ---- CB_j block cg, rows of this quadrant -> M (16-bit, TMEM) ----
+          const int s0 = 128 * j + cg * 32;
           uint32_t pk[16];
           if (s0 > wr0 + 31) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) pk[jj] = 0u;
           } else {
             const bool diag = s0 + 31 >= wr0;  // blocks are aligned: the 32x32 diagonal tile
-            const bool fac = diag ? (sBlkOk[cb] != 0) : mono;
+            const bool fac = diag ? (sBlkOk[s0 >> 5] != 0) : mono;
             uint32_t v[32];
-            tmem_ld32(tmem + ((uint32_t)(quad * 32) << 16) + 128 * s + cb * 32, v);
+            tmem_ld32(tmem + tlane + 128 * j + cg * 32, v);
             tmem_wait_ld();
             if (fac) {
               const float rowf = __expf(cl - sCum[s0 + 31]);
-              const float4* cf = reinterpret_cast<const float4*>(sColf + cb * 32);
+              const float4* cf = reinterpret_cast<const float4*>(sColf + s0);
 #pragma unroll
               for (int q4 = 0; q4 < 8; ++q4) {
                 const float4 c4 = cf[q4];
@@ -531,104 +553,102 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
               }
             }
           }
-          uint8_t* base = sB + (cb >> 1) * 16384;
-          const uint32_t c16 = (cb & 1) * 4;
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(base + sw128_off(r, c16 + q)) =
-                make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-        }
-        fence_proxy_async_smem();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(4 + s));
-        if (j == m) {
-          // ---- epilogue: y = exp(cum_l) Yoff + Yin (+ D x) (* silu z), columns [16cg, 16cg+16) ----
-          const long long tok = ci.tok0 + l;
-          const bool valid = l < ci.lim;
-          const long long yrow = (tok * H + h) * 64 + cg * 16;
-          uint4 zv[2];
-          if (z && valid) {
-            const uint4* zp = reinterpret_cast<const uint4*>(z + yrow);
-            zv[0] = zp[0];
-            zv[1] = zp[1];
-          }
-          ok = mbar_wait(bar(6 + s), par, kSiteScanMma2);
-          tc_fence_after();
-          if (!named_bar_and(1, 512, ok)) { fail = true; break; }
-          const uint32_t ty = tmem + ((uint32_t)(quad * 32) << 16) + 256 + 128 * slot;
-          uint32_t ri[16], ro[16];
-          tmem_ld16(ty + cg * 16, ri);
-          tmem_ld16(ty + 64 + cg * 16, ro);
-          tmem_wait_ld();
+          tmem_st16(tmem + tlane + T_M + 64 * mb + 16 * cg, pk);
+          tmem_wait_st();
+          fence_proxy_async_smem();  // sX zero-fill (first job) visible to MMA2
           tc_fence_before();
-          if (valid) {
-            const float el = __expf(cl);
-            float o[16];
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(MFULL0 + mb));
+          ++Jc;
+        }
+        if (fail) break;
+        if (i == si.nh - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(CB_FREE));  // this item's CB is no longer read
+        }
+        // ---- epilogue: y = exp(cum_l) Yoff + Yin (+ D x) (* silu z), columns [16cg, 16cg+16) ----
+        const long long tok = ci.tok0 + l;
+        const bool valid = l < ci.lim;
+        const long long yrow = (tok * H + h) * 64 + cg * 16;
+        uint4 zv[2];
+        if (z && valid) {
+          const uint4* zp = reinterpret_cast<const uint4*>(z + yrow);
+          zv[0] = zp[0];
+          zv[1] = zp[1];
+        }
+        const int jl = Jc - 1;
+        ok = mbar_wait(bar(M2DONE0 + (jl & 1)), (jl >> 1) & 1, kSiteScanMma2);
+        tc_fence_after();
+        if (!named_bar_and(1, 512, ok)) { fail = true; break; }
+        uint32_t ri[16], ro[16];
+        tmem_ld16(tmem + tlane + T_YIN + cg * 16, ri);
+        tmem_ld16(tmem + tlane + T_YOFF + cg * 16, ro);
+        tmem_wait_ld();
+        tc_fence_before();
+        if (valid) {
+          const float el = __expf(cl);
+          float o[16];
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) o[jj] = fmaf(el, __uint_as_float(ro[jj]), __uint_as_float(ri[jj]));
-            if (D) {
-              const float4* sD4 = reinterpret_cast<const float4*>(sm + 512 + cg * 16);
-              float dd[16];
+          for (int jj = 0; jj < 16; ++jj) o[jj] = fmaf(el, __uint_as_float(ro[jj]), __uint_as_float(ri[jj]));
+          if (D) {
+            const float4* sD4 = reinterpret_cast<const float4*>(sm + 512 + cg * 16);
+            float dd[16];
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const float4 d4 = sD4[q];
-                dd[4 * q] = d4.x;
-                dd[4 * q + 1] = d4.y;
-                dd[4 * q + 2] = d4.z;
-                dd[4 * q + 3] = d4.w;
-              }
-#pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                const uint4 xv = *reinterpret_cast<const uint4*>(sX + sw128_off(r, cg * 2 + q));
-                const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 f = unpack2<T16>(w4[e]);
-                  const int pi = q * 8 + 2 * e;
-                  o[pi] = fmaf(dd[pi], f.x, o[pi]);
-                  o[pi + 1] = fmaf(dd[pi + 1], f.y, o[pi + 1]);
-                }
-              }
+            for (int q = 0; q < 4; ++q) {
+              const float4 d4 = sD4[q];
+              dd[4 * q] = d4.x;
+              dd[4 * q + 1] = d4.y;
+              dd[4 * q + 2] = d4.z;
+              dd[4 * q + 3] = d4.w;
             }
-            if (z) {
+            const uint8_t* xr = sX + 16384 * m;  // x rows of this half
 #pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                const uint32_t w4[4] = {zv[q].x, zv[q].y, zv[q].z, zv[q].w};
+            for (int q = 0; q < 2; ++q) {
+              const uint4 xv = *reinterpret_cast<const uint4*>(xr + sw128_off(r, cg * 2 + q));
+              const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 f = unpack2<T16>(w4[e]);
-                  const float h0 = 0.5f * f.x, h1 = 0.5f * f.y;
-                  // silu(z) = z * sigmoid(z) = h + h * tanh(h), h = z / 2
-                  o[q * 8 + 2 * e] *= fmaf(h0, tanh_approx(h0), h0);
-                  o[q * 8 + 2 * e + 1] *= fmaf(h1, tanh_approx(h1), h1);
-                }
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = unpack2<T16>(w4[e]);
+                const int pi = q * 8 + 2 * e;
+                o[pi] = fmaf(dd[pi], f.x, o[pi]);
+                o[pi + 1] = fmaf(dd[pi + 1], f.y, o[pi + 1]);
               }
-            }
-            if constexpr (sizeof(YT) == 4) {
-              float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow);
-#pragma unroll
-              for (int q = 0; q < 4; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
-            } else {
-              uint4* yp = reinterpret_cast<uint4*>(y + yrow);
-#pragma unroll
-              for (int q = 0; q < 2; ++q)
-                yp[q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
-                                   pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
             }
           }
-          // Y slot (TMEM) and stage (x tile, D) are free once every compute warp is here.
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(8 + slot));
+          if (z) {
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              const uint32_t w4[4] = {zv[q].x, zv[q].y, zv[q].z, zv[q].w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = unpack2<T16>(w4[e]);
+                const float h0 = 0.5f * f.x, h1 = 0.5f * f.y;
+                // silu(z) = z * sigmoid(z) = h + h * tanh(h), h = z / 2
+                o[q * 8 + 2 * e] *= fmaf(h0, tanh_approx(h0), h0);
+                o[q * 8 + 2 * e + 1] *= fmaf(h1, tanh_approx(h1), h1);
+              }
+            }
+          }
+          if constexpr (sizeof(YT) == 4) {
+            float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+          } else {
+            uint4* yp = reinterpret_cast<uint4*>(y + yrow);
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+              yp[q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
+                                 pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
+          }
         }
-        ++J;
+        // Y (TMEM) and the head stage (x tile, D, dt, cum) are free once every compute warp is here.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(EPI0 + hs));
+        ++Hc;
       }
-      if (fail) {
-        *s_abort = 1;
-        break;
-      }
-      ++nI;
+      ++I;
     }
+    if (fail) *s_abort = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -722,12 +742,18 @@ static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, con
   const int dt_nonneg = (c.dmax >= 0.f) && (c.use_sp || c.dmin >= 0.f);
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long items = 2ll * c.H * c.nchunks_max;
+  // Heads per item: up to 8 share one CB; fewer when that leaves too few items
+  // to keep every SM busy (about four items per CTA).
+  const int hpg = c.H / c.G;
+  int hb = hpg < 8 ? hpg : 8;
+  auto n_items = [&](int b) { return 2ll * c.nchunks_max * c.G * ((hpg + b - 1) / b); };
+  while (hb > 1 && n_items(hb) < 4ll * sms) hb = (hb + 1) / 2;
+  const long long items = n_items(hb);
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
   const int grid = (int)(items < sms ? items : sms);  // persistent: one CTA per SM
   kern<<<grid, kScanThreads, kScanSmem, c.stream>>>(mx, mc, mb, mh, A, dt, cum, D,
                                                     reinterpret_cast<const typename T16Of<BF16>::type*>(z),
-                                                    reinterpret_cast<YT*>(y), c.cm, c.H, c.H / c.G, dt_nonneg,
+                                                    reinterpret_cast<YT*>(y), c.cm, c.H, c.G, hb, dt_nonneg,
                                                     (int)items);
   return cudaGetLastError();
 }
