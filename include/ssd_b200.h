@@ -39,7 +39,8 @@ typedef enum {
   SSD_ERR_WORKSPACE_TOO_SMALL = 3,
   SSD_ERR_CUDA = 4,             /* a CUDA runtime call failed (launch, attribute, ...) */
   SSD_ERR_DEVICE_TIMEOUT = 5,   /* a kernel gave up on a bounded wait (see ssd_b200_device_error) */
-  SSD_ERR_NO_TENSOR_MAP = 6     /* the driver's tensor-map encoder could not be obtained */
+  SSD_ERR_NO_TENSOR_MAP = 6,    /* the driver's tensor-map encoder could not be obtained */
+  SSD_ERR_SCRATCH_LIMIT = 7     /* ssd_scan_fwd_noalloc: needs more than its fixed scratch */
 } ssd_status_t;
 
 typedef enum { SSD_F32 = 0, SSD_BF16 = 1, SSD_F16 = 2 } ssd_dtype_t;
@@ -130,6 +131,26 @@ size_t ssd_scan_fwd_workspace_size(const ssd_params* p);
  * Writes y and h_last. Uses p->workspace (>= ssd_scan_fwd_workspace_size(p)).
  */
 int ssd_scan_fwd(const ssd_params* p, void* stream);
+
+/*
+ * ssd_scan_fwd without a caller workspace and without any allocation. It has no
+ * counterpart in the reference (whose forward allocates its intermediates through
+ * torch on every call). It is for callers that cannot allocate device memory when
+ * they run the scan, e.g. a host whose device memory is fully reserved by another
+ * runtime's pool, or a hot path that must not block on an allocation's device-wide
+ * synchronisation. The library holds a fixed scratch array of
+ * SSD_NOALLOC_SCRATCH_BYTES on every GPU that loads it, until the process exits;
+ * p->workspace and p->workspace_bytes are ignored. A problem whose
+ * ssd_scan_fwd_workspace_size() exceeds the array returns SSD_ERR_SCRATCH_LIMIT
+ * (the tensor-core path needs about 50 KB per chunk and head: b=2, L=2048, H=32 fits;
+ * b=8, L=2048, H=24, at 78 MB, does not).
+ * The first call on a device resolves the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture. All calls
+ * share the array: calls that overlap on the GPU (other streams or host threads)
+ * race on it. Nothing in it needs to start at zero.
+ */
+#define SSD_NOALLOC_SCRATCH_BYTES (32u << 20)
+int ssd_scan_fwd_noalloc(const ssd_params* p, void* stream);
 
 /* Stage entry points (padded mode only). Each reads/writes the stage buffers. */
 int ssd_chunk_cumsum_fwd(const ssd_params* p, void* stream);     /* -> dt, cum */

@@ -18,6 +18,7 @@ SSD_OK = 0
 SSD_ERR_INVALID_ARGUMENT = 1
 SSD_ERR_UNSUPPORTED_DTYPE = 2
 SSD_ERR_WORKSPACE_TOO_SMALL = 3
+SSD_ERR_SCRATCH_LIMIT = 7
 
 IMPL_AUTO, IMPL_TC, IMPL_SIMT = 0, 1, 2
 IMPLS = {"auto": IMPL_AUTO, "tc": IMPL_TC, "simt": IMPL_SIMT}
@@ -32,6 +33,7 @@ EXPORTS = {
     "ssd_scan_uses_tensor_cores": (c_int, [c_void_p]),
     "ssd_scan_fwd_workspace_size": (c_size_t, [c_void_p]),
     "ssd_scan_fwd": (c_int, [c_void_p, c_void_p]),
+    "ssd_scan_fwd_noalloc": (c_int, [c_void_p, c_void_p]),
     "ssd_chunk_cumsum_fwd": (c_int, [c_void_p, c_void_p]),
     "ssd_chunk_state_fwd": (c_int, [c_void_p, c_void_p]),
     "ssd_state_passing_fwd": (c_int, [c_void_p, c_void_p]),

@@ -154,6 +154,7 @@ const char* ssd_b200_status_string(int status) {
     case SSD_ERR_CUDA: return "CUDA runtime error";
     case SSD_ERR_DEVICE_TIMEOUT: return "device wait timed out";
     case SSD_ERR_NO_TENSOR_MAP: return "tensor-map encoder unavailable";
+    case SSD_ERR_SCRATCH_LIMIT: return "problem needs more scratch than ssd_scan_fwd_noalloc holds";
   }
   return "unknown status";
 }
