@@ -261,7 +261,9 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
 constexpr int kScanHeadStageBytes = 32768 + 16384;  // x rows [0, 256) | prev
 constexpr int kScanSmallBytes = 4096;                // dt 1K | cum 1K | D 256 | colf 1K | flags | A
 constexpr int kScanThreads = 576;                    // warp 0 TMA, warp 1 MMA, warps 2..17 compute
-constexpr int kScanSmem = 32768 + 65536 + 2 * kScanHeadStageBytes + 2 * kScanSmallBytes + 256 + 1024;
+constexpr int kScanMaxHeads = 1024;  // A[0:H) staged in shared memory
+constexpr int kScanSmem =
+    32768 + 65536 + 2 * kScanHeadStageBytes + 2 * kScanSmallBytes + 256 + 4 * kScanMaxHeads + 1024;
 
 struct ScanItem {
   int k, m, g, h0, nh;  // chunk, half, group, first head, heads in the block
@@ -300,12 +302,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
   auto small = [&](int s) {
     return reinterpret_cast<float*>(smem + 98304 + 2 * kScanHeadStageBytes + s * kScanSmallBytes);
   };
-  // small layout (floats): dt [0,256) cum [256,512) D [512,576) colf [576,832) flags [832,840) A_h [840]
+  // small layout (floats): dt [0,256) cum [256,512) D [512,576) colf [576,832) flags [832,840)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 98304 + 2 * kScanHeadStageBytes + 2 * kScanSmallBytes);
   enum { ITEM_FULL = 0, CB_FULL, C_FREE, CB_FREE, HEAD_FULL0, HEAD_FULL1, EPI0, EPI1, MFULL0, MFULL1, M2DONE0,
          M2DONE1, NBARS };
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
+  float* sA = reinterpret_cast<float*>(smem + 98304 + 2 * kScanHeadStageBytes + 2 * kScanSmallBytes + 256);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int hpg = H / G;
   const uint32_t T_M = 256, T_YIN = 384, T_YOFF = 448;
@@ -329,6 +332,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     *s_abort = 0;
     fence_mbar_init();
   }
+  for (int i = tid; i < H; i += kScanThreads) sA[i] = A[i];
   if (warp == 1) tmem_alloc(smem_u32(tslot), 512);
   tc_fence_before();
   __syncthreads();
@@ -369,7 +373,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           uint8_t* st = hstage(hs);
           float* sm = small(hs);
           const uint32_t fb = bar(HEAD_FULL0 + hs);
-          sm[840] = A[h];  // published by the arrive below (release)
           mbar_expect_tx(fb, (uint32_t)S * 128u + 16384u + 2048u + (D ? 256u : 0u));
           for (int j = 0; j <= si.m; ++j) tma_load_3d(smem_u32(st + 16384 * j), &tm_x, 0, h, t0 + 128 * j, fb);
           tma_load_3d(smem_u32(st + 32768), &tm_h, 0, 0, si.k * H + h, fb);
@@ -488,7 +491,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         ok = mbar_wait(bar(HEAD_FULL0 + hs), (Hc >> 1) & 1, kSiteScanTma);
         if (!named_bar_and(1, 512, ok)) { fail = true; break; }
         // cum non-increasing (A <= 0 and dt >= 0) => min(cum_l - cum_s, 0) = cum_l - cum_s
-        const bool mono = dt_nonneg && (sm[840] <= 0.f);
+        const bool mono = dt_nonneg && (sA[h] <= 0.f);
         if (ctid < S) {
           const float cr = sCum[ctid | 31];
           sColf[ctid] = mono ? __expf(cr - sCum[ctid]) * sDt[ctid] : 0.f;
@@ -736,6 +739,7 @@ template <bool BF16, typename YT>
 static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, const CUtensorMap& mc,
                                   const CUtensorMap& mb, const CUtensorMap& mh, const float* A, const float* dt,
                                   const float* cum, const float* D, const void* z, void* y) {
+  if (c.H > kScanMaxHeads) return cudaErrorInvalidValue;
   auto kern = tc_chunk_scan_kernel<BF16, YT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem);
   if (e != cudaSuccess) return e;
