@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c1|c2|c4]
 
 One JSON line on stdout (rank 0). A "step" is one SSD forward over one batch of
-the workload (default: BASELINE config 1, 8 x 2048 tokens, H24 P64 N128 cs256,
+the workload (default: benchmark config c1, 8 x 2048 tokens, H24 P64 N128 cs256,
 bf16 with D + z). Multi-GPU (torchrun, one process per GPU): every rank runs its
 own batch of the same shape from its own seed (the scan has no cross-row or
 cross-head exchange), so scaling is weak and ``value`` = all ranks' tokens / the
@@ -44,7 +44,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=["c1", "c2", "c4"], default="c1")
-    ap.add_argument("--kernel-impl", choices=["auto", "tc", "simt"], default="auto")
+    ap.add_argument("--kernel-impl", choices=["auto", "tc", "tc_staged", "simt"], default="auto")
     ap.add_argument("--no-ssu", action="store_true", help="skip the decode (config 3) measurement")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
@@ -279,6 +279,7 @@ def run_ours(args, rank, world, local):
                                          cfg.chunk, True, (0.0, INF), inp["D"], inp["z"], cu, args.kernel_impl)
     ws = torch.empty(kernels.workspace_size(p), dtype=torch.uint8, device=dev)
     tc = kernels.uses_tensor_cores(p)
+    path = kernels.scan_path(p)
     stage_ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
     for e in stage_ev:
         e.record(stream)  # materialise the handles
@@ -330,12 +331,20 @@ def run_ours(args, rank, world, local):
     state_bytes = T * H * P * sx + T * G * N * sx + 8 * T * H + 4 * nck * H * P * N
     pass_bytes = 4 * nck * H * P * N + s_prev * nck * H * P * N + 4 * (nseq or b) * H * P * N + 4 * nck * H
     cums_bytes = 4 * T * H + 8 * nck * H * cfg.chunk
+    # fused chunk_state + state_passing: x, B, raw dt in; dt, cum, prev16, h_last out
+    sp_bytes = (T * H * P * sx + T * G * N * sx + 4 * T * H + 8 * nck * H * cfg.chunk + 2 * nck * H * P * N
+                + 4 * (nseq or b) * H * P * N)
     names = ["chunk_cumsum", "chunk_state", "state_passing", "bmm_chunk", "chunk_scan"]
     bytes_ = [cums_bytes, state_bytes, pass_bytes, 0, scan_bytes]
+    if path == "tc_fused":
+        names[2] = "chunk_state+state_passing"
+        bytes_[2] = sp_bytes
     stages = {}
     for n_, ms_, by in zip(names, stage_ms, bytes_):
         if tc and n_ in ("bmm_chunk", "chunk_cumsum"):
             continue  # fused: cumsum into chunk_state, bmm into chunk_scan
+        if path == "tc_fused" and n_ == "chunk_state":
+            continue  # fused into the chain kernel timed as stage [2, 3)
         if tc and n_ == "chunk_state":
             by += cums_bytes
         gbs = by / (ms_ / 1e3) / 1e9 if ms_ > 0 else None
@@ -355,9 +364,10 @@ def run_ours(args, rank, world, local):
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if sx == 2 else "f32", "data": "synthetic",
         "config": {"workload": _workload_name(cfg), "global_batch": cfg.batch * world, "seq_len": cfg.seqlen,
                    "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "path": "tcgen05" if tc else "cuda-core", "l2": "flushed between timed steps (256 MiB write)"},
+                   "path": {"tc_fused": "tcgen05, chunk_state+state_passing fused", "tc_staged": "tcgen05",
+                            "simt": "cuda-core"}[path], "l2": "flushed between timed steps (256 MiB write)"},
         "roofline": roof, "stages": stages, "whole_step": whole, "clocks": clk,
-        "gpu_launches": args.steps * ((4 if tc else 5) + (1 if cu is not None else 0)),
+        "gpu_launches": args.steps * ({"tc_fused": 2, "tc_staged": 3, "simt": 5}[path] + (1 if cu is not None else 0)),
     }
     if not args.no_e2e:
         line["e2e"] = e2e_measure(args, cfg, inp, dev, world, flush)
@@ -424,7 +434,7 @@ def e2e_measure(args, cfg, inp, dev, world, flush):
 
 
 def ssu_measure(args, dev, flush, hbm_peak, world):
-    """Decode state update: achieved HBM GB/s on the algorithmic bytes."""
+    """Decode state update, benchmark config c3: achieved HBM GB/s on the algorithmic bytes."""
     from selective_attention_b200 import kernels, workloads
 
     cfg = workloads.SSU_CONFIGS["c3"]

@@ -46,10 +46,17 @@ typedef enum {
 typedef enum { SSD_F32 = 0, SSD_BF16 = 1, SSD_F16 = 2 } ssd_dtype_t;
 
 typedef enum {
-  SSD_IMPL_AUTO = 0,   /* tensor-core path when the shape/dtype allow it, else CUDA-core path */
-  SSD_IMPL_TC = 1,     /* tcgen05 + TMA kernels (bf16/fp16, headdim 64, dstate 128, chunk 256) */
-  SSD_IMPL_SIMT = 2    /* CUDA-core FFMA kernels (any dtype; fp32-exact accumulation) */
+  SSD_IMPL_AUTO = 0,   /* tensor-core path when the shape/dtype allow it, else CUDA-core path;
+                          on the tensor-core path chunk_state and state_passing are fused when
+                          there are at least SSD_FUSED_MIN_CHAINS (row, head) chains */
+  SSD_IMPL_TC = 1,     /* tcgen05 + TMA kernels (bf16/fp16, headdim 64, dstate 128, chunk 256),
+                          chunk_state and state_passing fused (one CTA per (row, head) chain) */
+  SSD_IMPL_SIMT = 2,   /* CUDA-core FFMA kernels (any dtype; fp32-exact accumulation) */
+  SSD_IMPL_TC_STAGED = 3 /* tensor-core kernels with chunk_state and state_passing as separate
+                            launches and fp32 chunk states in the workspace */
 } ssd_impl_t;
+
+#define SSD_FUSED_MIN_CHAINS 128
 
 /*
  * One parameter block for the SSD entry points. Fields an entry point does not
@@ -120,6 +127,12 @@ int ssd_b200_device_error(void* stream);
 
 /* Whether `p` would take the tensor-core path under SSD_IMPL_AUTO (1) or not (0). */
 int ssd_scan_uses_tensor_cores(const ssd_params* p);
+
+/* The kernel chain ssd_scan_fwd runs for `p` (its impl field included): 0 CUDA-core
+ * stages, 1 tensor-core stages with chunk_state and state_passing as separate launches,
+ * 2 tensor-core with chunk_state and state_passing fused; -1 for an invalid geometry.
+ * No reference counterpart (host-side query). */
+int ssd_scan_path(const ssd_params* p);
 
 /* Bytes of workspace ssd_scan_fwd needs for `p` (sizes, dtypes, impl, nseq). */
 size_t ssd_scan_fwd_workspace_size(const ssd_params* p);

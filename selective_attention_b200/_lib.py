@@ -20,8 +20,9 @@ SSD_ERR_UNSUPPORTED_DTYPE = 2
 SSD_ERR_WORKSPACE_TOO_SMALL = 3
 SSD_ERR_SCRATCH_LIMIT = 7
 
-IMPL_AUTO, IMPL_TC, IMPL_SIMT = 0, 1, 2
-IMPLS = {"auto": IMPL_AUTO, "tc": IMPL_TC, "simt": IMPL_SIMT}
+IMPL_AUTO, IMPL_TC, IMPL_SIMT, IMPL_TC_STAGED = 0, 1, 2, 3
+IMPLS = {"auto": IMPL_AUTO, "tc": IMPL_TC, "simt": IMPL_SIMT, "tc_staged": IMPL_TC_STAGED}
+FUSED_MIN_CHAINS = 128  # SSD_FUSED_MIN_CHAINS
 
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
@@ -31,6 +32,7 @@ EXPORTS = {
     "ssd_b200_status_string": (ctypes.c_char_p, [c_int]),
     "ssd_b200_device_error": (c_int, [c_void_p]),
     "ssd_scan_uses_tensor_cores": (c_int, [c_void_p]),
+    "ssd_scan_path": (c_int, [c_void_p]),
     "ssd_scan_fwd_workspace_size": (c_size_t, [c_void_p]),
     "ssd_scan_fwd": (c_int, [c_void_p, c_void_p]),
     "ssd_scan_fwd_noalloc": (c_int, [c_void_p, c_void_p]),

@@ -64,6 +64,14 @@ bool use_tc(const ssd_params* p, const Geometry& g) {
   return tc_supported(p->x_dtype, g.P, g.N, g.cs);
 }
 
+// Tensor-core path with chunk_state and state_passing fused (one CTA per (row, head)
+// chain): always under SSD_IMPL_TC, under AUTO when there are enough chains to fill
+// the GPU.
+bool use_fused(const ssd_params* p, const Geometry& g) {
+  if (!use_tc(p, g) || p->impl == SSD_IMPL_TC_STAGED) return false;
+  return p->impl == SSD_IMPL_TC || (long long)g.nrows * g.H >= SSD_FUSED_MIN_CHAINS;
+}
+
 struct Workspace {
   float* dt;
   float* cum;
@@ -76,7 +84,7 @@ struct Workspace {
   size_t bytes;
 };
 
-Workspace carve(const ssd_params* p, const Geometry& g, bool tc, uint8_t* base) {
+Workspace carve(const ssd_params* p, const Geometry& g, bool tc, bool fused, uint8_t* base) {
   Workspace w{};
   size_t off = 0;
   auto take = [&](size_t n) {
@@ -87,7 +95,7 @@ Workspace carve(const ssd_params* p, const Geometry& g, bool tc, uint8_t* base) 
   const size_t nk = (size_t)g.nchunks;
   w.dt = (float*)take(nk * g.H * g.cs * sizeof(float));
   w.cum = (float*)take(nk * g.H * g.cs * sizeof(float));
-  w.states = (float*)take(nk * g.H * (size_t)g.P * g.N * sizeof(float));
+  if (!fused) w.states = (float*)take(nk * g.H * (size_t)g.P * g.N * sizeof(float));
   if (tc) w.prev16 = take(nk * g.H * (size_t)g.P * g.N * 2);
   else w.CB = (float*)take(nk * g.G * (size_t)g.cs * g.cs * sizeof(float));
   if (g.packed) {
@@ -173,10 +181,17 @@ int ssd_scan_uses_tensor_cores(const ssd_params* p) {
   return use_tc(p, g) ? 1 : 0;
 }
 
+int ssd_scan_path(const ssd_params* p) {
+  Geometry g;
+  if (geometry(p, g) != SSD_OK) return -1;
+  if (use_fused(p, g)) return 2;
+  return use_tc(p, g) ? 1 : 0;
+}
+
 size_t ssd_scan_fwd_workspace_size(const ssd_params* p) {
   Geometry g;
   if (geometry(p, g) != SSD_OK) return 0;
-  return carve(p, g, use_tc(p, g), nullptr).bytes;
+  return carve(p, g, use_tc(p, g), use_fused(p, g), nullptr).bytes;
 }
 
 int ssd_scan_fwd(const ssd_params* p, void* stream) {
@@ -186,7 +201,8 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
   if ((st = check_common_inputs(p, true))) return st;
   if (!p->u || !p->A || !p->B || !p->C || !p->delta_raw || !p->y || !p->h_last || !p->workspace)
     return SSD_ERR_INVALID_ARGUMENT;
-  if (p->impl == SSD_IMPL_TC && !tc_supported(p->x_dtype, g.P, g.N, g.cs)) return SSD_ERR_INVALID_ARGUMENT;
+  const bool want_tc = p->impl == SSD_IMPL_TC || p->impl == SSD_IMPL_TC_STAGED;
+  if (want_tc && !tc_supported(p->x_dtype, g.P, g.N, g.cs)) return SSD_ERR_INVALID_ARGUMENT;
   const bool tc = use_tc(p, g);
   if (!tc && !simt_fits(g)) return SSD_ERR_INVALID_ARGUMENT;
   if (tc && p->y_dtype != SSD_F32 && p->y_dtype != p->x_dtype) return SSD_ERR_UNSUPPORTED_DTYPE;
@@ -194,7 +210,8 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
   if (tc && (!aligned16(p->u) || !aligned16(p->B) || !aligned16(p->C) || !aligned16(p->y) ||
              (p->z && !aligned16(p->z)) || (p->D && !aligned16(p->D))))
     return SSD_ERR_INVALID_ARGUMENT;
-  Workspace w = carve(p, g, tc, reinterpret_cast<uint8_t*>(p->workspace));
+  const bool fused = use_fused(p, g);
+  Workspace w = carve(p, g, tc, fused, reinterpret_cast<uint8_t*>(p->workspace));
   if (p->workspace_bytes < w.bytes) return SSD_ERR_WORKSPACE_TOO_SMALL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   LaunchCtx c = make_ctx(p, g, s, &w);
@@ -205,7 +222,22 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
     if (st) return st;
   }
   int tms = 0;
-  if (tc) {
+  if (fused) {
+    // chunk_cumsum, chunk_state and state_passing in one kernel (events [1]..[3] coincide).
+    record(p, 1, s);
+    record(p, 2, s);
+    cudaError_t e = launch_tc_state_pass(c, p->x_dtype, p->dt_dtype, p->u, p->B, p->A, p->delta_raw,
+                                         p->delta_bias, w.dt, w.cum, w.prev16, p->h_init, p->h_last, &tms);
+    if (tms) return SSD_ERR_NO_TENSOR_MAP;
+    if ((st = cuda_status(e))) return st;
+    record(p, 3, s);
+    record(p, 4, s);
+    e = launch_tc_chunk_scan(c, p->x_dtype, p->y_dtype, p->u, p->A, w.dt, w.cum, p->B, p->C, w.prev16, p->D, p->z,
+                             p->y, &tms);
+    if (tms) return SSD_ERR_NO_TENSOR_MAP;
+    if ((st = cuda_status(e))) return st;
+    record(p, 5, s);
+  } else if (tc) {
     // chunk_cumsum is fused into the tensor-core chunk_state (events [1] and [2] coincide).
     record(p, 1, s);
     cudaError_t e = launch_tc_chunk_state(c, p->x_dtype, p->dt_dtype, p->u, p->B, p->A, p->delta_raw,
@@ -274,7 +306,7 @@ int ssd_chunk_state_fwd(const ssd_params* p, void* stream) {
     if (tms) return SSD_ERR_NO_TENSOR_MAP;
     return cuda_status(e);
   }
-  if (p->impl == SSD_IMPL_TC || !simt_fits(g)) return SSD_ERR_INVALID_ARGUMENT;
+  if (p->impl == SSD_IMPL_TC || p->impl == SSD_IMPL_TC_STAGED || !simt_fits(g)) return SSD_ERR_INVALID_ARGUMENT;
   return cuda_status(launch_simt_chunk_state(c, p->x_dtype, p->u, p->B, p->dt, p->cum, p->states));
 }
 

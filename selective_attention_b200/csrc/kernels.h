@@ -41,6 +41,11 @@ bool tc_supported(int x_dtype, int P, int N, int cs);
 cudaError_t launch_tc_chunk_state(const LaunchCtx& c, int x_dtype, int dt_dtype, const void* u, const void* B,
                                   const float* A, const void* delta_raw, const float* delta_bias, float* dt,
                                   float* cum, float* states, int* tmap_status);
+// chunk_cumsum + chunk_state + state_passing in one kernel, one CTA per (row, head)
+// chain: writes dt, cum, prev16 and h_last; the fp32 chunk states stay on chip.
+cudaError_t launch_tc_state_pass(const LaunchCtx& c, int x_dtype, int dt_dtype, const void* u, const void* B,
+                                 const float* A, const void* delta_raw, const float* delta_bias, float* dt,
+                                 float* cum, void* prev16, const float* h_init, float* h_last, int* tmap_status);
 cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, const void* u, const float* A,
                                  const float* dt, const float* cum, const void* B, const void* C, const void* prev16,
                                  const float* D, const void* z, void* y, int* tmap_status);

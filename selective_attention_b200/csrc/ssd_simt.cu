@@ -63,15 +63,11 @@ __global__ void __launch_bounds__(256) chunk_cumsum_kernel(
 // state_passing: ssd_scan/forward_kernel.py:202-250.
 // One thread per 4 consecutive state elements of one (row, head); walks the row's
 // chunks in order: out[c] = prev; prev = exp(cum_last[c]) * prev + S[c].
-// P16 = float: prev states overwrite S in place (fp32), as the reference does.
-// P16 = bf16/fp16: prev states go to a separate 16-bit buffer (the tensor-core
-// chunk_scan operand, in the input's type) and S is left untouched.
+// Prev states overwrite S in place (fp32), as the reference does.
 // ===========================================================================
-template <typename P16>
-__global__ void __launch_bounds__(256) state_passing_kernel(
-    float* __restrict__ states, P16* __restrict__ prev16, const float* __restrict__ cum,
-    const float* __restrict__ h_init, float* __restrict__ h_last, ChunkMap cm, int H, int PN) {
-  constexpr bool kSeparate = sizeof(P16) == 2;
+__global__ void __launch_bounds__(256) state_passing_kernel(float* __restrict__ states, const float* __restrict__ cum,
+                                                           const float* __restrict__ h_init,
+                                                           float* __restrict__ h_last, ChunkMap cm, int H, int PN) {
   const int row = blockIdx.z, h = blockIdx.y;
   const int e0 = (blockIdx.x * 256 + threadIdx.x) * 4;
   if (e0 >= PN) return;
@@ -94,14 +90,7 @@ __global__ void __launch_bounds__(256) state_passing_kernel(
     const float4 s = nxt;
     if (c + 1 < count) nxt = *reinterpret_cast<const float4*>(states + ((kk + 1) * H + h) * PN + e0);
     const long long off = (kk * H + h) * PN + e0;
-    if constexpr (kSeparate) {
-      uint2 pk;
-      pk.x = pack2<P16>(prev.x, prev.y);
-      pk.y = pack2<P16>(prev.z, prev.w);
-      *reinterpret_cast<uint2*>(prev16 + off) = pk;
-    } else {
-      *reinterpret_cast<float4*>(states + off) = prev;
-    }
+    *reinterpret_cast<float4*>(states + off) = prev;
     const float sc = expf(cum[(kk * H + h) * cs + cs - 1]);
     prev.x = sc * prev.x + s.x;
     prev.y = sc * prev.y + s.y;
@@ -109,6 +98,66 @@ __global__ void __launch_bounds__(256) state_passing_kernel(
     prev.w = sc * prev.w + s.w;
   }
   *reinterpret_cast<float4*>(h_last + ((long long)row * H + h) * PN + e0) = prev;
+}
+
+// ===========================================================================
+// state_passing for the tensor-core chunk_scan (P = 64, N = 128): the same
+// recurrence, but the prev states go to a separate buffer in the input's 16-bit
+// type laid out [chunk][head][n][p] (p contiguous), and S is left untouched.
+// One CTA per (32 dstate rows, head, row); thread (n, p pairs) reads S coalesced
+// along n and the tile is transposed through shared memory for 16-byte stores.
+// ===========================================================================
+template <typename P16>
+__global__ void __launch_bounds__(256) state_passing16_kernel(
+    const float* __restrict__ states, P16* __restrict__ prev16, const float* __restrict__ cum,
+    const float* __restrict__ h_init, float* __restrict__ h_last, ChunkMap cm, int H) {
+  constexpr int P = 64, N = 128, PN = P * N;
+  __shared__ uint32_t sT[32 * 33];  // [n][p pair], padded rows
+  const int row = blockIdx.z, h = blockIdx.y, n0 = blockIdx.x * 32;
+  const int tid = threadIdx.x, nl = tid & 31, pr = tid >> 5;
+  int first, count;
+  if (cm.packed) {
+    const int2 r = cm.rows[row];
+    first = r.x;
+    count = r.y;
+  } else {
+    first = row * cm.nc;
+    count = cm.nc;
+  }
+  // thread's elements: n = n0 + nl, p = 2 (pr + 8 i) + e, i < 4, e < 2
+  float prev[8];
+  const long long hoff = ((long long)row * H + h) * PN + n0 + nl;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) prev[2 * i + e] = h_init ? h_init[hoff + (2 * (pr + 8 * i) + e) * N] : 0.f;
+  const int orow = tid >> 3, oq = tid & 7;  // read-out: row n0 + orow, p [8 oq, 8 oq + 8)
+  for (int c = 0; c < count; ++c) {
+    const long long kk = first + c;
+    const long long soff = (kk * H + h) * PN + n0 + nl;
+    float s[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) s[2 * i + e] = states[soff + (2 * (pr + 8 * i) + e) * N];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sT[nl * 33 + pr + 8 * i] = pack2<P16>(prev[2 * i], prev[2 * i + 1]);
+    __syncthreads();
+    uint4 v;
+    v.x = sT[orow * 33 + 4 * oq];
+    v.y = sT[orow * 33 + 4 * oq + 1];
+    v.z = sT[orow * 33 + 4 * oq + 2];
+    v.w = sT[orow * 33 + 4 * oq + 3];
+    *reinterpret_cast<uint4*>(prev16 + (kk * H + h) * PN + (long long)(n0 + orow) * P + 8 * oq) = v;
+    __syncthreads();
+    const float sc = expf(cum[(kk * H + h) * cm.cs + cm.cs - 1]);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) prev[j] = sc * prev[j] + s[j];
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) h_last[hoff + (2 * (pr + 8 * i) + e) * N] = prev[2 * i + e];
 }
 
 // ===========================================================================
@@ -335,15 +384,21 @@ cudaError_t launch_chunk_cumsum(const LaunchCtx& c, int dt_dtype, const float* A
 cudaError_t launch_state_passing(const LaunchCtx& c, float* states, void* prev16, int prev_dtype,
                                  const float* cum, const float* h_init, float* h_last) {
   const int PN = c.P * c.N;
+  if (prev16) {
+    if (c.P != 64 || c.N != 128) return cudaErrorInvalidValue;
+    dim3 g16(4u, (unsigned)c.H, (unsigned)c.nrows);
+    if (prev_dtype == SSD_BF16)
+      state_passing16_kernel<__nv_bfloat16><<<g16, 256, 0, c.stream>>>(states, (__nv_bfloat16*)prev16, cum, h_init,
+                                                                       h_last, c.cm, c.H);
+    else if (prev_dtype == SSD_F16)
+      state_passing16_kernel<__half><<<g16, 256, 0, c.stream>>>(states, (__half*)prev16, cum, h_init, h_last, c.cm,
+                                                                c.H);
+    else
+      return cudaErrorInvalidValue;
+    return cudaGetLastError();
+  }
   dim3 grid((unsigned)((PN / 4 + 255) / 256), (unsigned)c.H, (unsigned)c.nrows);
-  if (prev16 && prev_dtype == SSD_BF16)
-    state_passing_kernel<__nv_bfloat16><<<grid, 256, 0, c.stream>>>(states, (__nv_bfloat16*)prev16, cum, h_init,
-                                                                     h_last, c.cm, c.H, PN);
-  else if (prev16 && prev_dtype == SSD_F16)
-    state_passing_kernel<__half><<<grid, 256, 0, c.stream>>>(states, (__half*)prev16, cum, h_init, h_last, c.cm,
-                                                             c.H, PN);
-  else
-    state_passing_kernel<float><<<grid, 256, 0, c.stream>>>(states, nullptr, cum, h_init, h_last, c.cm, c.H, PN);
+  state_passing_kernel<<<grid, 256, 0, c.stream>>>(states, cum, h_init, h_last, c.cm, c.H, PN);
   return cudaGetLastError();
 }
 

@@ -15,7 +15,8 @@
 //   MMA1  CB_j[l, s]  = C[l, :] . B[s, :]          M 128, N 128, K 128 (K-major)
 //   CB_j -> M_j[l, s] = CB * decay(l, s) * dt_s  (bf16/fp16, K-major, over the B tile)
 //   MMA2  Yin[l, p]  += sum_s M_j[l, s] x[s, p]    M 128, N 64, K 128 (x MN-major)
-//   MMA3  Yoff[l, p]  = C[l, :] . prev[p, :]        M 128, N 64, K 128 (block 0)
+//   MMA3  Yoff[l, p]  = C[l, :] . prev[:, p]        M 128, N 64, K 128 (prev16 stored
+//                                                    [n][p], read MN-major)
 //   y = exp(cum_l) * Yoff + Yin (+ D x) (* silu z)
 // decay(l, s) = exp(min(cum_l - cum_s, 0)) with s <= l. Per 32x32 tile it is
 // evaluated as exp(cum_l - cum_r) * exp(cum_r - cum_s), r the tile's last column,
@@ -54,7 +55,7 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// Scale the 16-byte chunk (8 elements of T16) by w.
+// Scale the 16-byte chunk (8 elements of T16) by w (fp32 products, one rounding).
 template <typename T16>
 __device__ __forceinline__ uint4 scale8(uint4 a, float w) {
   float2 f;
@@ -64,6 +65,18 @@ __device__ __forceinline__ uint4 scale8(uint4 a, float w) {
   f = unpack2<T16>(a.z); v.z = pack2<T16>(f.x * w, f.y * w);
   f = unpack2<T16>(a.w); v.w = pack2<T16>(f.x * w, f.y * w);
   return v;
+}
+
+// Scale 8 elements by w2 = (w, w) in the 16-bit type itself (bf16x2 / f16x2
+// multiplies: w and each product are rounded to the 16-bit type).
+template <typename T16> __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t w2);
+template <> __device__ __forceinline__ uint32_t mul2<__nv_bfloat16>(uint32_t a, uint32_t w2) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&w2));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+template <typename T16>
+__device__ __forceinline__ uint4 scale8_packed(uint4 a, uint32_t w2) {
+  return make_uint4(mul2<T16>(a.x, w2), mul2<T16>(a.y, w2), mul2<T16>(a.z, w2), mul2<T16>(a.w, w2));
 }
 
 // ===========================================================================
@@ -238,6 +251,333 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
 }
 
 // ===========================================================================
+// chunk_state + state_passing: one (row, head pair) chain per CTA
+// ===========================================================================
+// The CTA walks the row's chunks in order for two heads of one group. Per chunk
+// it computes dt / cum (forward_kernel.py:20-105), the chunk states
+// S_k = sum_l B_l^T (x_l w_l) of both heads with one N = 128 MMA per 16 tokens
+// (:108-200; the B tile is loaded once for the pair) and folds S_k into the
+// running states, which live in registers (:203-258):
+//   prev_0 = h_init (or 0),  prev_{k+1} = exp(cum_last_k) prev_k + S_k,  h_last = prev_count.
+// prev_k is written in the input's 16-bit type for chunk_scan; the fp32 chunk
+// states never reach memory.
+// Roles: warp 0 (one lane) TMA producer of 64-token stages (B: two dstate
+// halves, x of each head) in a kSpStages-deep ring; warp 1 (one lane) MMA
+// issuer, accumulating chunk k in TMEM columns [128 (k & 1), +128) (head i at
+// +64 i); warps 2..5 (head 0) and 6..9 (head 1): dt / cum, x scaling and the
+// state update, thread = dstate row n (its TMEM lane). With an odd number of
+// heads per group the last CTA has one head; its second warp group only
+// releases the stages.
+// Ordering without extra barriers: a head group folds chunk k-1 after it
+// released chunk k's stages, and MMA(k+1) into the same accumulator waits for
+// chunk k+1's first stage, which both groups release after that fold.
+constexpr int kSpStages = 6;
+constexpr int kSpStageBytes = 16384 + 2 * 8192;  // B [64 tokens x 2 halves x 128 B] | x head 0 | x head 1
+constexpr int kSpThreads = 320;
+constexpr int kSpSmem = kSpStages * kSpStageBytes + 2048 + 64 + 256 + 1024;
+
+enum : unsigned int {
+  kSiteSpTma = 0x111,
+  kSiteSpScaled = 0x112,
+  kSiteSpMma = 0x113,
+};
+
+template <bool BF16, typename DT>
+__global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
+    const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_b,
+    const float* __restrict__ A, const DT* __restrict__ delta_raw, const float* __restrict__ delta_bias,
+    float* __restrict__ dt_out, float* __restrict__ cum_out, typename T16Of<BF16>::type* __restrict__ prev16,
+    const float* __restrict__ h_init, float* __restrict__ h_last, ChunkMap cm, int H, int hpg, int use_sp,
+    float dmin, float dmax) {
+  using T16 = typename T16Of<BF16>::type;
+  constexpr int NST = kSpStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  auto sBst = [&](int s) { return smem + s * kSpStageBytes; };
+  auto sXst = [&](int s, int i) { return smem + s * kSpStageBytes + 16384 + 8192 * i; };
+  float* sW = reinterpret_cast<float*>(smem + NST * kSpStageBytes);  // [head][256] token weights
+  float* sWarp = sW + 512;                                             // [head][4] warp totals
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sWarp + 16);
+  // FULL[NST] SCALED[NST] EMPTY[NST] ACC[2]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3 * NST + 2);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int FULL = 0, SCALED = NST, EMPTY = 2 * NST, ACC = 3 * NST;
+
+  // blockIdx.x -> (row, group, head pair of the group)
+  const int npairs = (hpg + 1) >> 1;
+  const int G = H / hpg;
+  int rem = blockIdx.x;
+  const int pair = rem % npairs;
+  rem /= npairs;
+  const int g = rem % G;
+  const int row = rem / G;
+  const int h0 = g * hpg + 2 * pair;
+  const int nh = min(2, hpg - 2 * pair);
+  int first, count;
+  if (cm.packed) {
+    const int2 r = cm.rows[row];
+    first = r.x;
+    count = r.y;
+  } else {
+    first = row * cm.nc;
+    count = cm.nc;
+  }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_b);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(bar(FULL + s), 1);
+      mbar_init(bar(SCALED + s), 8);
+      mbar_init(bar(EMPTY + s), 1);
+    }
+    mbar_init(bar(ACC), 1);
+    mbar_init(bar(ACC + 1), 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tslot), 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int r = 0;
+      bool fail = false;
+      const uint32_t bytes = 16384u + 8192u * (uint32_t)nh;
+      for (int k = 0; k < count && !fail && !*s_abort; ++k) {
+        ChunkInfo ci;
+        chunk_info(cm, first + k, ci);
+        const int nst = (ci.lim + 63) >> 6, t0 = (int)ci.tok0;
+        for (int s = 0; s < nst; ++s, ++r) {
+          const int slot = r % NST;
+          if (r >= NST && !mbar_wait(bar(EMPTY + slot), ((r / NST) - 1) & 1, kSiteSpMma)) {
+            fail = true;
+            break;
+          }
+          const uint32_t fb = bar(FULL + slot);
+          mbar_expect_tx(fb, bytes);
+          tma_load_3d(smem_u32(sBst(slot)), &tm_b, 0, g, t0 + 64 * s, fb);
+          tma_load_3d(smem_u32(sBst(slot) + 8192), &tm_b, 64, g, t0 + 64 * s, fb);
+          for (int i = 0; i < nh; ++i) tma_load_3d(smem_u32(sXst(slot, i)), &tm_x, 0, h0 + i, t0 + 64 * s, fb);
+        }
+      }
+      if (fail) *s_abort = 1;
+      // No copy may still be in flight when the CTA exits.
+      for (int d = 1; d <= NST && d <= r; ++d) {
+        const int rr = r - d;
+        mbar_wait(bar(FULL + rr % NST), (rr / NST) & 1, kSiteSpTma);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(128, 64 * nh, BF16, /*a_mn=*/true, /*b_mn=*/true);
+      int r = 0, last_bar = -1, last_par = 0;
+      bool fail = false;
+      for (int k = 0; k < count && !fail && !*s_abort; ++k) {
+        ChunkInfo ci;
+        chunk_info(cm, first + k, ci);
+        const int nst = (ci.lim + 63) >> 6;
+        const uint32_t acc = tmem + 128 * (k & 1);
+        for (int s = 0; s < nst; ++s, ++r) {
+          const int slot = r % NST;
+          if (!mbar_wait(bar(SCALED + slot), (r / NST) & 1, kSiteSpScaled)) {
+            fail = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sBst(slot)), b0 = smem_u32(sXst(slot, 0));
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            umma_f16(acc, sdesc_sw128(a0 + ks * 2048, 8192, 1024), sdesc_sw128(b0 + ks * 2048, 8192, 1024), idesc,
+                     (s > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(bar(EMPTY + slot));
+          last_bar = EMPTY + slot;
+          last_par = (r / NST) & 1;
+        }
+        if (fail) break;
+        umma_commit(bar(ACC + (k & 1)));
+      }
+      if (fail) *s_abort = 1;
+      // All MMAs must be complete before TMEM is released.
+      if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, kSiteSpMma);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ head groups
+    const int hg = (warp - 2) >> 2;   // head of the pair
+    const bool active = hg < nh;
+    const int bar_id = 1 + hg;
+    const int ctid = tid - 64 - 128 * hg, cw = (warp - 2) & 3;
+    const int quad = warp & 3, n = quad * 32 + lane;
+    const uint32_t tlane = (uint32_t)(quad * 32) << 16;
+    const int h = h0 + (active ? hg : 0);
+    const float a = A[h];
+    const float bias = delta_bias ? delta_bias[h] : 0.f;
+    const long long PN = 64 * 128;
+    float* sWh = sW + 256 * hg;
+    float* sWarph = sWarp + 4 * hg;
+    float prev[64];
+    if (h_init && active) {
+      const float* hi = h_init + ((long long)row * H + h) * PN + n;
+#pragma unroll
+      for (int p = 0; p < 64; ++p) prev[p] = hi[p * 128];
+    } else {
+#pragma unroll
+      for (int p = 0; p < 64; ++p) prev[p] = 0.f;
+    }
+    // Raw delta of tokens 2 ctid, 2 ctid + 1 of chunk k (loaded one chunk ahead).
+    auto load_raw = [&](int k, float& r0, float& r1) {
+      r0 = r1 = 0.f;
+      if (k >= count || !active) return;
+      ChunkInfo ci;
+      chunk_info(cm, first + k, ci);
+      const DT* dr = delta_raw + (ci.tok0 + 2 * ctid) * (long long)H + h;
+      if (2 * ctid < ci.vlim) r0 = Ld<DT>::f(dr);
+      if (2 * ctid + 1 < ci.vlim) r1 = Ld<DT>::f(dr + H);
+    };
+    // prev16 row n of a chunk: 64 contiguous p values, eight 16-byte stores.
+    auto store_prev16 = [&](T16* dst) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        d4[q] = make_uint4(pack2<T16>(prev[8 * q], prev[8 * q + 1]), pack2<T16>(prev[8 * q + 2], prev[8 * q + 3]),
+                           pack2<T16>(prev[8 * q + 4], prev[8 * q + 5]), pack2<T16>(prev[8 * q + 6], prev[8 * q + 7]));
+    };
+    bool wfail = false;  // this warp gave up on a wait; the group learns it at its next barrier
+    // Fold the finished chunk j: prev = exp(cum_last_j) prev + S_j, then store.
+    auto fold = [&](int j, float el) -> bool {
+      bool ok = !wfail && mbar_wait(bar(ACC + (j & 1)), (j >> 1) & 1, kSiteSpMma);
+      tc_fence_after();
+      if (!named_bar_and(bar_id, 128, ok && !*s_abort)) return false;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v[32];
+        tmem_ld32(tmem + tlane + 128 * (j & 1) + 64 * hg + 32 * half, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q = 0; q < 32; ++q) prev[32 * half + q] = fmaf(el, prev[32 * half + q], __uint_as_float(v[q]));
+      }
+      tc_fence_before();
+      if (j + 1 < count) {
+        store_prev16(prev16 + ((long long)(first + j + 1) * H + h) * PN + n * 64);
+      } else {
+        float* dst = h_last + ((long long)row * H + h) * PN + n;
+#pragma unroll
+        for (int p = 0; p < 64; ++p) dst[p * 128] = prev[p];
+      }
+      return true;
+    };
+    bool fail = false;
+    if (active) {
+      if (count == 0) {
+        float* dst = h_last + ((long long)row * H + h) * PN + n;
+#pragma unroll
+        for (int p = 0; p < 64; ++p) dst[p * 128] = prev[p];
+      } else {
+        store_prev16(prev16 + ((long long)first * H + h) * PN + n * 64);
+      }
+    }
+    float raw0, raw1;
+    load_raw(0, raw0, raw1);
+    float el_prev = 1.f;
+    int r = 0;
+    for (int k = 0; k < count && !fail; ++k) {
+      ChunkInfo ci;
+      chunk_info(cm, first + k, ci);
+      const long long kk = first + k;
+      const int nst = (ci.lim + 63) >> 6;
+      // ---- dt / cum of the chunk (shuffle scan over 128 threads x 2 tokens) ----
+      float d0 = 0.f, d1 = 0.f, c0 = 0.f, tot = 0.f, incl = 0.f, cl = 0.f;
+      if (active) {
+        d0 = 2 * ctid < ci.vlim ? dt_transform(raw0 + bias, use_sp, dmin, dmax) : 0.f;
+        d1 = 2 * ctid + 1 < ci.vlim ? dt_transform(raw1 + bias, use_sp, dmin, dmax) : 0.f;
+        load_raw(k + 1, raw0, raw1);
+        c0 = d0 * a;
+        tot = c0 + d1 * a;
+        incl = tot;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const float o = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += o;
+        }
+        if (lane == 31) sWarph[cw] = incl;
+      }
+      // Every barrier of the group ANDs the warps' wait results, so all of them
+      // leave together when one gave up.
+      if (!named_bar_and(bar_id, 128, !wfail && !*s_abort)) {
+        fail = true;
+        break;
+      }
+      if (active) {
+        float wbase = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const float t = sWarph[w];
+          wbase += w < cw ? t : 0.f;
+          cl += t;
+        }
+        const float excl = wbase + incl - tot;
+        const float cum0 = excl + c0, cum1 = excl + tot;
+        const long long io = (kk * H + h) * 256 + 2 * ctid;
+        *reinterpret_cast<float2*>(dt_out + io) = make_float2(d0, d1);
+        *reinterpret_cast<float2*>(cum_out + io) = make_float2(cum0, cum1);
+        sWh[2 * ctid] = 2 * ctid < ci.lim ? __expf(fminf(cl - cum0, 0.f)) * d0 : 0.f;
+        sWh[2 * ctid + 1] = 2 * ctid + 1 < ci.lim ? __expf(fminf(cl - cum1, 0.f)) * d1 : 0.f;
+      }
+      named_bar_sync(bar_id, 128);
+      // ---- x rows scaled by w_l in place (rows past `lim` become exact zeros) ----
+      // Warps go through the stages independently; a warp that gave up stops
+      // releasing stages and the group leaves at its next barrier.
+      for (int s = 0; s < nst; ++s, ++r) {
+        const int slot = r % NST;
+        if (!wfail) {
+          const bool ok = mbar_wait(bar(FULL + slot), (r / NST) & 1, kSiteSpTma);
+          wfail = !__all_sync(0xffffffffu, ok);
+        }
+        if (wfail) continue;
+        if (active) {
+          uint8_t* sx = sXst(slot, hg);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int q = cw * 32 + lane + 128 * i;
+            uint4* pch = reinterpret_cast<uint4*>(sx + q * 16);
+            const float w = sWh[64 * s + (q >> 3)];
+            if constexpr (BF16) {
+              const __nv_bfloat162 w2 = __float2bfloat162_rn(w);
+              *pch = (w == 0.f) ? make_uint4(0u, 0u, 0u, 0u)
+                                : scale8_packed<T16>(*pch, *reinterpret_cast<const uint32_t*>(&w2));
+            } else {
+              *pch = (w == 0.f) ? make_uint4(0u, 0u, 0u, 0u) : scale8<T16>(*pch, w);
+            }
+          }
+          fence_proxy_async_smem();
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(SCALED + slot));
+      }
+      // ---- fold the previous chunk while this chunk's MMAs run ----
+      if (active && k > 0 && !fold(k - 1, el_prev)) {
+        fail = true;
+        break;
+      }
+      el_prev = expf(cl);
+    }
+    if (active && !fail && count > 0 && !fold(count - 1, el_prev)) fail = true;
+    if (fail || wfail) *s_abort = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 256);
+}
+
+// ===========================================================================
 // chunk_scan (+ bmm_chunk): persistent, warp-specialised, CB shared across heads
 // ===========================================================================
 // Work items are (chunk k, half m, group g, block of up to HB heads of the group).
@@ -376,7 +716,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           mbar_expect_tx(fb, (uint32_t)S * 128u + 16384u + 2048u + (D ? 256u : 0u));
           for (int j = 0; j <= si.m; ++j) tma_load_3d(smem_u32(st + 16384 * j), &tm_x, 0, h, t0 + 128 * j, fb);
           tma_load_3d(smem_u32(st + 32768), &tm_h, 0, 0, si.k * H + h, fb);
-          tma_load_3d(smem_u32(st + 40960), &tm_h, 64, 0, si.k * H + h, fb);
           bulk_load(smem_u32(sm), dt + ((long long)si.k * H + h) * 256, 1024u, fb);
           bulk_load(smem_u32(sm + 256), cum + ((long long)si.k * H + h) * 256, 1024u, fb);
           if (D) bulk_load(smem_u32(sm + 512), D + h * 64, 256u, fb);
@@ -397,7 +736,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t id_cb = idesc_f16(128, 128, BF16, false, false);
-      const uint32_t id_off = idesc_f16(128, 64, BF16, false, false);
+      const uint32_t id_off = idesc_f16(128, 64, BF16, false, /*b_mn=*/true);
       const uint32_t id_in = idesc_f16(128, 64, BF16, false, true);
       int I = 0, Hc = 0, Jc = 0;
       bool fail = false;
@@ -436,7 +775,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           for (int ks = 0; ks < 8; ++ks) {
             const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
             umma_f16(tmem + T_YOFF, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
-                     sdesc_sw128(h0 + hf * 8192 + kk, 16, 1024), id_off, ks > 0 ? 1u : 0u);
+                     sdesc_sw128(h0 + ks * 2048, 16, 1024), id_off, ks > 0 ? 1u : 0u);
           }
           if (i == si.nh - 1) umma_commit(bar(C_FREE));
           for (int j = 0; j <= si.m; ++j) {
@@ -735,6 +1074,52 @@ cudaError_t launch_tc_chunk_state(const LaunchCtx& c, int x_dtype, int dt_dtype,
   return tc_state_dt<false>(c, dt_dtype, mx, mb, A, delta_raw, delta_bias, dt, cum, states);
 }
 
+template <bool BF16, typename DT>
+static cudaError_t tc_state_pass_launch(const LaunchCtx& c, const CUtensorMap& mx, const CUtensorMap& mb,
+                                        const float* A, const void* dr, const float* bias, float* dt, float* cum,
+                                        void* prev16, const float* h_init, float* h_last) {
+  auto kern = tc_state_pass_kernel<BF16, DT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSpSmem);
+  if (e != cudaSuccess) return e;
+  const int hpg = c.H / c.G;
+  const long long chains = (long long)c.nrows * c.G * ((hpg + 1) / 2);  // (row, head pair)
+  if (chains <= 0 || chains > 0x7fffffffll) return cudaErrorInvalidValue;
+  kern<<<(unsigned)chains, kSpThreads, kSpSmem, c.stream>>>(
+      mx, mb, A, (const DT*)dr, bias, dt, cum, reinterpret_cast<typename T16Of<BF16>::type*>(prev16), h_init,
+      h_last, c.cm, c.H, c.H / c.G, c.use_sp, c.dmin, c.dmax);
+  return cudaGetLastError();
+}
+
+template <bool BF16>
+static cudaError_t tc_state_pass_dt(const LaunchCtx& c, int dt_dtype, const CUtensorMap& mx, const CUtensorMap& mb,
+                                    const float* A, const void* dr, const float* bias, float* dt, float* cum,
+                                    void* prev16, const float* h_init, float* h_last) {
+  switch (dt_dtype) {
+    case SSD_F32: return tc_state_pass_launch<BF16, float>(c, mx, mb, A, dr, bias, dt, cum, prev16, h_init, h_last);
+    case SSD_BF16:
+      return tc_state_pass_launch<BF16, __nv_bfloat16>(c, mx, mb, A, dr, bias, dt, cum, prev16, h_init, h_last);
+    case SSD_F16: return tc_state_pass_launch<BF16, __half>(c, mx, mb, A, dr, bias, dt, cum, prev16, h_init, h_last);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_tc_state_pass(const LaunchCtx& c, int x_dtype, int dt_dtype, const void* u, const void* B,
+                                 const float* A, const void* delta_raw, const float* delta_bias, float* dt,
+                                 float* cum, void* prev16, const float* h_init, float* h_last, int* tmap_status) {
+  const bool bf16 = x_dtype == SSD_BF16;
+  CUtensorMap mx, mb;
+  if (!make_map_3d(&mx, u, bf16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 64) ||
+      !make_map_3d(&mb, B, bf16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 64)) {
+    *tmap_status = 1;
+    return cudaErrorInvalidValue;
+  }
+  *tmap_status = 0;
+  if (!delta_raw) return cudaErrorInvalidValue;
+  if (bf16) return tc_state_pass_dt<true>(c, dt_dtype, mx, mb, A, delta_raw, delta_bias, dt, cum, prev16, h_init,
+                                          h_last);
+  return tc_state_pass_dt<false>(c, dt_dtype, mx, mb, A, delta_raw, delta_bias, dt, cum, prev16, h_init, h_last);
+}
+
 template <bool BF16, typename YT>
 static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, const CUtensorMap& mc,
                                   const CUtensorMap& mb, const CUtensorMap& mh, const float* A, const float* dt,
@@ -767,13 +1152,14 @@ cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, c
                                  const float* D, const void* z, void* y, int* tmap_status) {
   const bool bf16 = x_dtype == SSD_BF16;
   CUtensorMap mx, mc, mb, mh;
-  // prev16 holds the previous-chunk states in the input's 16-bit type, so every
+  // prev16 holds the previous-chunk states in the input's 16-bit type, [chunk][head][n][p]
+  // (p contiguous: the MN-major B operand of MMA3), so every
   // MMA of the kernel has operands of one type.
   const uint64_t nch = (uint64_t)c.nchunks_max;
   if (!make_map_3d(&mx, u, bf16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
       !make_map_3d(&mc, C, bf16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128) ||
       !make_map_3d(&mb, B, bf16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128) ||
-      !make_map_3d(&mh, prev16, bf16, 128, 64, nch * (uint64_t)c.H, 64, 64, 1)) {
+      !make_map_3d(&mh, prev16, bf16, 64, 128, nch * (uint64_t)c.H, 64, 128, 1)) {
     *tmap_status = 1;
     return cudaErrorInvalidValue;
   }

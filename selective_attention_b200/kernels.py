@@ -192,6 +192,18 @@ def uses_tensor_cores(params) -> bool:
     return bool(_lib.lib().ssd_scan_uses_tensor_cores(byref(params)))
 
 
+SCAN_PATHS = {0: "simt", 1: "tc_staged", 2: "tc_fused"}
+
+
+def scan_path(params) -> str:
+    """Kernel chain of ``ssd_scan_fwd`` for these parameters: "simt", "tc_staged" or
+    "tc_fused" (chunk_state and state_passing in one kernel)."""
+    code = _lib.lib().ssd_scan_path(byref(params))
+    if code < 0:
+        raise ValueError("invalid SSD geometry")
+    return SCAN_PATHS[code]
+
+
 def ssd_scan_forward(u, A, B, C, delta_raw, delta_bias=None, h_init=None, length=None, chunk_size=256,
                      use_delta_softplus=True, delta_limit=(0.0, INF), is_causal=True, D=None, z=None,
                      cu_seqlens=None, impl: str = "auto", out: Optional[Sequence[torch.Tensor]] = None,

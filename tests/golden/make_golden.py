@@ -76,7 +76,7 @@ def save(name, **kw):
 
 
 def main():
-    # c0: fp32 2x256, H4 P32 N16 G1 cs64, D, with every stage output.
+    # c0: fp32 2x256, H4 P32 N16 G1 cs64, D (benchmark config c0), with every stage output.
     inp = gen(0, 2, 256, 4, 32, 16, 1)
     length = torch.tensor([256, 256])
     out = run_ssd(inp, length, 64, stages=True)

@@ -55,6 +55,20 @@ def test_params_struct_layout_matches_c():
         assert getattr(_lib.SSDParams, f).offset == off, f
 
 
+def test_header_constants_match_the_binding():
+    from selective_attention_b200 import _lib
+
+    src = open(HEADER).read()
+    consts = dict(re.findall(r"^\s*(SSD_[A-Z_]+)\s*=\s*(\d+)", src, flags=re.M))
+    assert int(consts["SSD_IMPL_AUTO"]) == _lib.IMPL_AUTO
+    assert int(consts["SSD_IMPL_TC"]) == _lib.IMPL_TC
+    assert int(consts["SSD_IMPL_SIMT"]) == _lib.IMPL_SIMT
+    assert int(consts["SSD_IMPL_TC_STAGED"]) == _lib.IMPL_TC_STAGED
+    assert int(consts["SSD_ERR_SCRATCH_LIMIT"]) == _lib.SSD_ERR_SCRATCH_LIMIT
+    m = re.search(r"#define\s+SSD_FUSED_MIN_CHAINS\s+(\d+)", src)
+    assert m and int(m.group(1)) == _lib.FUSED_MIN_CHAINS
+
+
 def _params(**kw):
     from selective_attention_b200 import kernels
 
@@ -72,8 +86,16 @@ def test_workspace_and_dispatch_queries_are_host_only():
     assert L.ssd_scan_uses_tensor_cores(ctypes.byref(p)) == 1
     ws = L.ssd_scan_fwd_workspace_size(ctypes.byref(p))
     nk, H = 8 * 8, 24
-    expect = 2 * nk * H * 256 * 4 + nk * H * 64 * 128 * 4 + nk * H * 64 * 128 * 2
+    # 192 (row, head) chains: chunk_state and state_passing fused, no fp32 chunk states
+    expect = 2 * nk * H * 256 * 4 + nk * H * 64 * 128 * 2
     assert ws == expect
+    staged = _params(impl=_lib.IMPL_TC_STAGED)
+    assert L.ssd_scan_fwd_workspace_size(ctypes.byref(staged)) == expect + nk * H * 64 * 128 * 4
+    few = _params(batch=4)  # 96 chains < SSD_FUSED_MIN_CHAINS: staged under AUTO, fused under TC
+    nk4 = 4 * 8
+    base4 = 2 * nk4 * H * 256 * 4 + nk4 * H * 64 * 128 * 2
+    assert L.ssd_scan_fwd_workspace_size(ctypes.byref(few)) == base4 + nk4 * H * 64 * 128 * 4
+    assert L.ssd_scan_fwd_workspace_size(ctypes.byref(_params(batch=4, impl=_lib.IMPL_TC))) == base4
     p32 = _params(x_dtype=0)
     assert L.ssd_scan_uses_tensor_cores(ctypes.byref(p32)) == 0
     assert L.ssd_scan_fwd_workspace_size(ctypes.byref(_params(nheads=24, ngroups=5))) == 0  # H % G != 0

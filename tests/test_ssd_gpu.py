@@ -30,10 +30,19 @@ def run_case(g, impl, D=None, z=None):
     return y, h
 
 
-@pytest.mark.parametrize("impl", ["auto", "simt"])
+TC_IMPLS = ["tc", "tc_staged"]  # chunk_state + state_passing fused / as separate launches
+
+
+def skip_tc_for_fp32(g, impl):
+    if impl in TC_IMPLS and g["inputs"]["u"].dtype == torch.float32:
+        pytest.skip("the tensor-core kernels take 16-bit inputs")
+
+
+@pytest.mark.parametrize("impl", ["auto", "simt"] + TC_IMPLS)
 @pytest.mark.parametrize("case", SSD_CASES)
 def test_ssd_matches_reference_golden(case, impl):
     g = load_golden(case)
+    skip_tc_for_fp32(g, impl)
     y, h = run_case(g, impl)
     assert y.dtype == torch.float32 and h.dtype == torch.float32
     close = assert_close_for(g["inputs"]["u"].dtype)
@@ -52,11 +61,12 @@ def test_tensor_core_path_is_taken_for_bf16(case):
     assert kernels.uses_tensor_cores(p)
 
 
-@pytest.mark.parametrize("impl", ["auto", "simt"])
+@pytest.mark.parametrize("impl", ["auto", "simt"] + TC_IMPLS)
 @pytest.mark.parametrize("case", ["ssd_bf16_c1slice", "ssd_bf16_groups", "ssd_c0_fp32"])
 def test_ssd_fused_gate_epilogue(case, impl):
     """(y + D*u) * silu(z) fused in the scan epilogue, vs modules/ssm.py:145-150 on the golden y."""
     g = load_golden(case)
+    skip_tc_for_fp32(g, impl)
     i = g["inputs"]
     D, z = i["D"], i["z"]
     y, h = run_case(g, impl, D=D, z=z)
@@ -66,7 +76,7 @@ def test_ssd_fused_gate_epilogue(case, impl):
     assert_close_for(i["u"].dtype)(h, g["h_last"], f"{case}/{impl} h_last")
 
 
-@pytest.mark.parametrize("impl", ["auto", "simt"])
+@pytest.mark.parametrize("impl", ["auto", "simt"] + TC_IMPLS)
 def test_ssd_varlen_matches_padded_reference(impl):
     import selective_attention_b200 as sab
 
@@ -127,9 +137,9 @@ def _c_inputs(name, seed=0, **over):
     return workloads.make_ssd_inputs(workloads.CONFIGS[name], seed=seed, **over)
 
 
-@pytest.mark.parametrize("impl", ["auto", "simt"])
+@pytest.mark.parametrize("impl", ["auto", "simt", "tc_staged"])
 def test_c1_full_size_vs_oracle(impl):
-    """BASELINE config 1 at full size (8 x 2048, H24 P64 N128, cs256, D + z)."""
+    """Benchmark config c1 at full size (8 x 2048, H24 P64 N128, cs256, D + z)."""
     import selective_attention_b200 as sab
 
     inp = _c_inputs("c1")
@@ -144,7 +154,8 @@ def test_c1_full_size_vs_oracle(impl):
     assert_bf16_close(h, h_ref, "c1 h_last")
 
 
-def test_c4_shape_groups_partial_chunks_vs_oracle():
+@pytest.mark.parametrize("impl", TC_IMPLS)
+def test_c4_shape_groups_partial_chunks_vs_oracle(impl):
     """c4 head/group shape (H16 over G8, 2 heads per group) with ragged rows and h_init."""
     import selective_attention_b200 as sab
 
@@ -152,7 +163,7 @@ def test_c4_shape_groups_partial_chunks_vs_oracle():
     length = torch.tensor([1000, 613])
     y, h = sab.SSDScanFn.apply(dev(inp["u"]), dev(inp["A"]), dev(inp["B"]), dev(inp["C"]), dev(inp["delta_raw"]),
                                dev(inp["delta_bias"]), dev(inp["h_init"]), dev(length), 256, True, (0.0, INF), True,
-                               dev(inp["D"]), dev(inp["z"]))
+                               dev(inp["D"]), dev(inp["z"]), None, impl)
     sab.check_device_error()
     y_ref, h_ref = ssd_ref.ssd_scan_forward(inp["u"].float(), inp["A"], inp["B"].float(), inp["C"].float(),
                                             inp["delta_raw"], inp["delta_bias"], inp["h_init"], length, 256)
@@ -161,15 +172,17 @@ def test_c4_shape_groups_partial_chunks_vs_oracle():
     assert_bf16_close(h, h_ref, "c4-shape h_last")
 
 
-def test_c2_varlen_full_size_vs_oracle():
-    """32768 packed tokens, lengths U[128, 4096], H80, D + z."""
+@pytest.mark.parametrize("impl", ["auto", "tc_staged"])
+def test_c2_varlen_full_size_vs_oracle(impl):
+    """Benchmark config c2: 32768 packed tokens, lengths U[128, 4096], H80, D + z."""
     import selective_attention_b200 as sab
 
     inp = _c_inputs("c2")
     cu = inp["cu_seqlens"]
     assert int(cu[-1]) == 32768
     y, h = sab.SSDScanFn.apply(dev(inp["u"]), dev(inp["A"]), dev(inp["B"]), dev(inp["C"]), dev(inp["delta_raw"]),
-                               None, None, None, 256, True, (0.0, INF), True, dev(inp["D"]), dev(inp["z"]), dev(cu))
+                               None, None, None, 256, True, (0.0, INF), True, dev(inp["D"]), dev(inp["z"]), dev(cu),
+                               impl)
     sab.check_device_error()
     # oracle on the first three sequences and the last one (each sequence is independent)
     idx = [0, 1, 2, cu.numel() - 2]
@@ -182,7 +195,7 @@ def test_c2_varlen_full_size_vs_oracle():
         assert_bf16_close(h[s:s + 1], hs, f"c2 seq {s} h_last")
 
 
-@pytest.mark.parametrize("impl", ["tc", "simt"])
+@pytest.mark.parametrize("impl", ["simt"] + TC_IMPLS)
 def test_decay_edge_cases_vs_oracle(impl):
     """A head with A > 0 (the min(., 0) clamps of forward_kernel.py:178,438 are active),
     a head with a very fast decay (dt ~ 1, |A| up to 16: the factored decay would overflow
@@ -214,13 +227,14 @@ def test_tc_and_simt_agree():
     inp = _c_inputs("c1", seed=5, batch=3, seqlen=700)
     length = torch.tensor([700, 513, 1])
     outs = {}
-    for impl in ("tc", "simt"):
+    for impl in ("tc", "tc_staged", "simt"):
         outs[impl] = sab.SSDScanFn.apply(dev(inp["u"]), dev(inp["A"]), dev(inp["B"]), dev(inp["C"]),
                                          dev(inp["delta_raw"]), None, None, dev(length), 256, True, (0.0, INF), True,
                                          dev(inp["D"]), dev(inp["z"]), None, impl)
     sab.check_device_error()
-    assert_bf16_close(outs["tc"][0], outs["simt"][0].float(), "tc vs simt y")
-    assert_bf16_close(outs["tc"][1], outs["simt"][1], "tc vs simt h_last")
+    for impl in TC_IMPLS:
+        assert_bf16_close(outs[impl][0], outs["simt"][0].float(), f"{impl} vs simt y")
+        assert_bf16_close(outs[impl][1], outs["simt"][1], f"{impl} vs simt h_last")
 
 
 def test_prefill_then_decode_matches_full_scan():

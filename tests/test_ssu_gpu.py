@@ -91,7 +91,7 @@ def test_ssu_bf16_state():
 
 
 def test_ssu_c3_full_size_vs_oracle():
-    """b256 H80 P64 N128, fp32 state in place, bf16 x/B/C/z, dt_bias, D + z."""
+    """Benchmark config c3: b256 H80 P64 N128, fp32 state in place, bf16 x/B/C/z, dt_bias, D + z."""
     import selective_attention_b200 as sab
     from selective_attention_b200 import workloads
 

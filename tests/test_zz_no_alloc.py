@@ -71,7 +71,7 @@ def test_noalloc_rejects_problems_beyond_its_scratch():
     from selective_attention_b200 import _lib, kernels
 
     L = _lib.lib()
-    p = kernels._params(batch=8, seqlen=2048, nheads=24, headdim=64, dstate=128, ngroups=1, chunk_size=256,
+    p = kernels._params(batch=16, seqlen=2048, nheads=24, headdim=64, dstate=128, ngroups=1, chunk_size=256,
                         x_dtype=1, dt_dtype=0, y_dtype=1)
     assert L.ssd_scan_fwd_workspace_size(ctypes.byref(p)) > (32 << 20)
     st = L.ssd_scan_fwd_noalloc(ctypes.byref(p), None)
