@@ -74,6 +74,10 @@ template <> __device__ __forceinline__ uint32_t mul2<__nv_bfloat16>(uint32_t a, 
   __nv_bfloat162 r = __hmul2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&w2));
   return *reinterpret_cast<uint32_t*>(&r);
 }
+template <> __device__ __forceinline__ uint32_t mul2<__half>(uint32_t a, uint32_t w2) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&w2));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
 template <typename T16>
 __device__ __forceinline__ uint4 scale8_packed(uint4 a, uint32_t w2) {
   return make_uint4(mul2<T16>(a.x, w2), mul2<T16>(a.y, w2), mul2<T16>(a.z, w2), mul2<T16>(a.w, w2));
@@ -581,29 +585,44 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
 // chunk_scan (+ bmm_chunk): persistent, warp-specialised, CB shared across heads
 // ===========================================================================
 // Work items are (chunk k, half m, group g, block of up to HB heads of the group).
-// Per item, C rows of the half and B rows [0, 128(m+1)) are loaded once and
-// CB_j = C B_j^T (j = 0..m, 128 source tokens each) is computed once into TMEM;
-// then, head by head, only x, prev, dt, cum and D are loaded, and
-//   M_j[l, s] = CB_j[l, s] * decay_h(l, s) * dt_s   (written to TMEM, 16-bit)
-//   Yin      += M_j x_j      (A from TMEM)    Yoff = C prev^T    (per head)
-//   y = exp(cum_l) Yoff + Yin (+ D x) (* silu z)
+// Per item, C rows of the half and B rows [0, 128(m+1)) are loaded once,
+// CB_j = C B_j^T (j = 0..m, 128 source tokens each) is computed once into TMEM
+// and rounded there to the input's 16-bit type; then, head by head, only x, prev,
+// z, dt, cum and D are loaded.
+// The decay is factored per 32-row block R (rows [32R, 32R+32) of the chunk):
+//   exp(cum_l - cum_s) = exp(cum_l - cum_{32R}) * exp(cum_{32R} - cum_s)
+// Both factors are <= 1 for s < 32R when cum is non-increasing (A <= 0, dt >= 0);
+// inside the diagonal 32x32 tile the second one is bounded by the tile's own decay,
+// which must stay below kScanFacMaxDecay. For such "factored" row blocks
+//   M'_j[l, s] = CB_j[l, s] * g_R[s],  g_R[s] = exp(cum_{32R} - cum_s) dt_s  (s <= l)
+// is one packed 16-bit multiply per pair of elements, and the row factor
+// exp(cum_l - cum_{32R}) is applied to Yin in the epilogue. Other row blocks get the
+// exact M_j[l, s] = CB_j[l, s] exp(min(cum_l - cum_s, 0)) dt_s and row factor 1.
+//   Yin  += M'_j x_j   (A from TMEM)    Yoff = C prev     (per head)
+//   y = exp(cum_l) Yoff + rowf_l Yin (+ D x) (* silu z)
 // Roles (one CTA per SM, items blockIdx.x, blockIdx.x + gridDim.x, ...):
 //   warp 0 (one lane)  TMA producer: item tiles (C, B) single-buffered, head tiles
-//                      (x, prev, dt, cum, D) in a 2-deep ring;
+//                      (x, prev, dt, cum, D) in a 2-deep ring, z tile one head ahead;
 //   warp 1 (one lane)  MMA issuer;
-//   warps 2..17        compute: CB -> M conversion (warp: one 32-column block of a
-//                      32-row quadrant), then the head's epilogue (16 output columns).
-// TMEM columns: CB_0 [0,128) CB_1 [128,256) M buffers [256,320) [320,384)
-//               Yin [384,448) Yoff [448,512).
+//   warps 2..17        compute: CB_j -> M'_j conversion (warp: one 32-column block of
+//                      a 32-row quadrant), then the head's epilogue (16 output columns).
+// TMEM columns: CB_0 [0,128) CB_1 [128,256) (fp32 from MMA1; 16-bit in the first
+//               64 columns of each after the per-item rounding), M buffers
+//               [256,320) [320,384), Yin [384,448), Yoff [448,512).
 // Barriers that a role may lag behind are kept per ring slot, so a waiter is never
 // two phases behind the barrier it polls. Every wait is bounded; a role that gives
 // up records the site, raises the CTA's abort flag and leaves its loop.
 constexpr int kScanHeadStageBytes = 32768 + 16384;  // x rows [0, 256) | prev
-constexpr int kScanSmallBytes = 4096;                // dt 1K | cum 1K | D 256 | colf 1K | flags | A
-constexpr int kScanThreads = 576;                    // warp 0 TMA, warp 1 MMA, warps 2..17 compute
-constexpr int kScanMaxHeads = 1024;  // A[0:H) staged in shared memory
-constexpr int kScanSmem =
-    32768 + 65536 + 2 * kScanHeadStageBytes + 2 * kScanSmallBytes + 256 + 4 * kScanMaxHeads + 1024;
+constexpr int kScanSmallBytes = 5120;  // words: dt [0,256) cum [256,512) D [512,576) flags [576,580) g [640,1152)
+constexpr int kScanThreads = 576;      // warp 0 TMA, warp 1 MMA, warps 2..17 compute
+constexpr int kScanMaxHeads = 1024;    // A[0:H) staged in shared memory
+constexpr int kScanZOff = 32768 + 65536 + 2 * kScanHeadStageBytes;  // z rows of the half (16 KB)
+constexpr int kScanSmallOff = kScanZOff + 16384;
+constexpr int kScanBarOff = kScanSmallOff + 2 * kScanSmallBytes;
+constexpr int kScanSmem = kScanBarOff + 256 + 4 * kScanMaxHeads + 1024;
+// Largest decay inside a diagonal 32x32 tile for which the factored form is used:
+// g_R reaches exp(decay) * dt, which must fit the 16-bit type with a wide margin.
+__device__ __forceinline__ float scan_fac_max_decay(bool bf16) { return bf16 ? 60.f : 8.f; }
 
 struct ScanItem {
   int k, m, g, h0, nh;  // chunk, half, group, first head, heads in the block
@@ -630,25 +649,23 @@ template <bool BF16, typename YT>
 __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c,
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_h,
-    const float* __restrict__ A, const float* __restrict__ dt, const float* __restrict__ cum,
-    const float* __restrict__ D, const typename T16Of<BF16>::type* __restrict__ z, YT* __restrict__ y, ChunkMap cm,
-    int H, int G, int HB, int dt_nonneg, int n_items) {
+    const __grid_constant__ CUtensorMap tm_z, const float* __restrict__ A, const float* __restrict__ dt,
+    const float* __restrict__ cum, const float* __restrict__ D, int has_z, YT* __restrict__ y, ChunkMap cm, int H,
+    int G, int HB, int dt_nonneg, int n_items) {
   using T16 = typename T16Of<BF16>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sC = smem;           // 2 x (128 rows x 128 B): dstate halves of the half's C rows
   uint8_t* sB = smem + 32768;   // per job j: 2 x (128 rows x 128 B) at 32768 * j
   auto hstage = [&](int s) { return smem + 98304 + s * kScanHeadStageBytes; };  // x [0,32K) prev [32K,48K)
-  auto small = [&](int s) {
-    return reinterpret_cast<float*>(smem + 98304 + 2 * kScanHeadStageBytes + s * kScanSmallBytes);
-  };
-  // small layout (floats): dt [0,256) cum [256,512) D [512,576) colf [576,832) flags [832,840)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 98304 + 2 * kScanHeadStageBytes + 2 * kScanSmallBytes);
-  enum { ITEM_FULL = 0, CB_FULL, C_FREE, CB_FREE, HEAD_FULL0, HEAD_FULL1, EPI0, EPI1, MFULL0, MFULL1, M2DONE0,
-         M2DONE1, NBARS };
+  uint8_t* sZ = smem + kScanZOff;
+  auto small = [&](int s) { return reinterpret_cast<float*>(smem + kScanSmallOff + s * kScanSmallBytes); };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kScanBarOff);
+  enum { ITEM_FULL = 0, CB_FULL, C_FREE, CB_FREE, YOFF_DONE, Z_FULL, HEAD_FULL0, HEAD_FULL1, EPI0, EPI1, MFULL0,
+         MFULL1, M2DONE0, M2DONE1, NBARS };
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
-  float* sA = reinterpret_cast<float*>(smem + 98304 + 2 * kScanHeadStageBytes + 2 * kScanSmallBytes + 256);
+  float* sA = reinterpret_cast<float*>(smem + kScanBarOff + 256);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int hpg = H / G;
   const uint32_t T_M = 256, T_YIN = 384, T_YOFF = 448;
@@ -659,10 +676,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     prefetch_tmap(&tm_c);
     prefetch_tmap(&tm_b);
     prefetch_tmap(&tm_h);
+    if (has_z) prefetch_tmap(&tm_z);
     mbar_init(bar(ITEM_FULL), 1);
     mbar_init(bar(CB_FULL), 1);
     mbar_init(bar(C_FREE), 1);
     mbar_init(bar(CB_FREE), 16);
+    mbar_init(bar(YOFF_DONE), 1);
+    mbar_init(bar(Z_FULL), 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(bar(HEAD_FULL0 + s), 1);
       mbar_init(bar(EPI0 + s), 16);
@@ -719,6 +739,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           bulk_load(smem_u32(sm), dt + ((long long)si.k * H + h) * 256, 1024u, fb);
           bulk_load(smem_u32(sm + 256), cum + ((long long)si.k * H + h) * 256, 1024u, fb);
           if (D) bulk_load(smem_u32(sm + 512), D + h * 64, 256u, fb);
+          if (has_z) {
+            // The z tile is single-buffered: free once the previous head's epilogue is done.
+            if (Hc >= 1 && !mbar_wait(bar(EPI0 + ((Hc - 1) & 1)), ((Hc - 1) >> 1) & 1, kSiteScanEpi)) {
+              fail = true;
+              break;
+            }
+            mbar_expect_tx(bar(Z_FULL), 16384u);
+            tma_load_3d(smem_u32(sZ), &tm_z, 0, h, t0 + 128 * si.m, bar(Z_FULL));
+          }
           ++Hc;
         }
         ++I;
@@ -730,6 +759,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         const int hc = Hc - d;
         mbar_wait(bar(HEAD_FULL0 + (hc & 1)), (hc >> 1) & 1, kSiteScanTma);
       }
+      if (has_z && Hc > 0) mbar_wait(bar(Z_FULL), (Hc - 1) & 1, kSiteScanTma);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -777,6 +807,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
             umma_f16(tmem + T_YOFF, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
                      sdesc_sw128(h0 + ks * 2048, 16, 1024), id_off, ks > 0 ? 1u : 0u);
           }
+          umma_commit(bar(YOFF_DONE));
           if (i == si.nh - 1) umma_commit(bar(C_FREE));
           for (int j = 0; j <= si.m; ++j) {
             const int mb = Jc & 1;
@@ -809,89 +840,121 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     const int quad = warp & 3, cg = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const uint32_t tlane = (uint32_t)(quad * 32) << 16;
+    const float fac_max = scan_fac_max_decay(BF16);
     int I = 0, Hc = 0, Jc = 0;
-    bool fail = false;
+    // Warps wait on the mbarriers independently; a warp that gives up (wfail) stops
+    // releasing work, and all warps leave together at the next named barrier, which
+    // ANDs the flags (fail).
+    bool fail = false, wfail = false;
+    auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
+      if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
+      return !wfail;
+    };
     for (int it = blockIdx.x; it < n_items && !fail; it += gridDim.x) {
       ScanItem si;
       ChunkInfo ci;
       if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
-      const int m = si.m, lbase = 128 * m, l = lbase + r, wr0 = lbase + quad * 32, S = 128 * (m + 1);
-      bool ok = mbar_wait(bar(CB_FULL), I & 1, kSiteScanMma1);
+      const int m = si.m, l = 128 * m + r, R = 4 * m + quad, S = 128 * (m + 1);
+      warp_wait(bar(CB_FULL), I & 1, kSiteScanMma1);
       tc_fence_after();
-      if (!named_bar_and(1, 512, ok && !*s_abort)) { fail = true; break; }
+      if (!named_bar_and(1, 512, !wfail && !*s_abort)) { fail = true; break; }
+      // ---- CB_j (fp32) -> 16-bit, into the first 64 columns of CB_j's own region ----
+      for (int j = 0; j <= m; ++j) {
+        uint32_t hv[16];
+        {
+          uint32_t v[32];
+          tmem_ld32(tmem + tlane + 128 * j + 32 * cg, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 16; ++q) hv[q] = pack2<T16>(__uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1]));
+        }
+        tc_fence_before();
+        named_bar_sync(1, 512);  // every warp has read its fp32 block before any is overwritten
+        tc_fence_after();
+        tmem_st16(tmem + tlane + 128 * j + 16 * cg, hv);
+        tmem_wait_st();
+      }
       for (int i = 0; i < si.nh; ++i) {
         const int h = si.h0 + i, hs = Hc & 1;
         uint8_t* sX = hstage(hs);
         float* sm = small(hs);
         const float* sDt = sm;
         const float* sCum = sm + 256;
-        float* sColf = sm + 576;
-        int* sBlkOk = reinterpret_cast<int*>(sm + 832);
-        ok = mbar_wait(bar(HEAD_FULL0 + hs), (Hc >> 1) & 1, kSiteScanTma);
-        if (!named_bar_and(1, 512, ok)) { fail = true; break; }
+        int* sFlag = reinterpret_cast<int*>(sm + 576);
+        uint32_t* sG = reinterpret_cast<uint32_t*>(sm + 640);  // [row block of the half][pair of s]
+        warp_wait(bar(HEAD_FULL0 + hs), (Hc >> 1) & 1, kSiteScanTma);
         // cum non-increasing (A <= 0 and dt >= 0) => min(cum_l - cum_s, 0) = cum_l - cum_s
         const bool mono = dt_nonneg && (sA[h] <= 0.f);
-        if (ctid < S) {
-          const float cr = sCum[ctid | 31];
-          sColf[ctid] = mono ? __expf(cr - sCum[ctid]) * sDt[ctid] : 0.f;
-          if ((ctid & 31) == 0) sBlkOk[ctid >> 5] = mono && (sCum[ctid] - cr <= 80.f);
+        {
+          const int rb = 4 * m + (ctid >> 7), s2 = 2 * (ctid & 127);
+          uint32_t gv = 0u;
+          if (mono && s2 < 32 * (rb + 1)) {
+            const float cr = sCum[32 * rb];
+            const float g0 = s2 < ci.lim ? __expf(cr - sCum[s2]) * sDt[s2] : 0.f;
+            const float g1 = s2 + 1 < ci.lim ? __expf(cr - sCum[s2 + 1]) * sDt[s2 + 1] : 0.f;
+            gv = pack2<T16>(g0, g1);
+          }
+          sG[ctid] = gv;
+          if (ctid < 4) {
+            const int rr = 4 * m + ctid;
+            sFlag[ctid] = mono && (sCum[32 * rr] - sCum[32 * rr + 31] <= fac_max);
+          }
         }
         if (S > ci.lim) {
           // x rows past `lim` -> exact zeros, so they cannot leak into Yin
           for (int q = ctid; q < S * 8; q += 512)
             if ((q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
-        if (!named_bar_and(1, 512, true)) { fail = true; break; }  // publishes colf / flags
+        if (!named_bar_and(1, 512, !wfail && !*s_abort)) { fail = true; break; }  // publishes g / flags
         const float cl = sCum[l];
+        const bool fR = sFlag[quad] != 0;
         for (int j = 0; j <= m; ++j) {
           const int mb = Jc & 1;
           if (Jc >= 2) {
-            ok = mbar_wait(bar(M2DONE0 + mb), ((Jc - 2) >> 1) & 1, kSiteScanMma2);
-            if (!named_bar_and(1, 512, ok)) { fail = true; break; }
+            warp_wait(bar(M2DONE0 + mb), ((Jc - 2) >> 1) & 1, kSiteScanMma2);
             tc_fence_after();
           }
-          // ---- CB_j block cg, rows of this quadrant -> M (16-bit, TMEM) ----
+          if (wfail) {
+            ++Jc;
+            continue;
+          }
+          // ---- 16-bit CB_j block cg, rows of this quadrant -> M'_j (TMEM) ----
           const int s0 = 128 * j + cg * 32;
           uint32_t pk[16];
-          if (s0 > wr0 + 31) {
+          if (s0 > 32 * R + 31) {
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) pk[jj] = 0u;
+            for (int q = 0; q < 16; ++q) pk[q] = 0u;
           } else {
-            const bool diag = s0 + 31 >= wr0;  // blocks are aligned: the 32x32 diagonal tile
-            const bool fac = diag ? (sBlkOk[s0 >> 5] != 0) : mono;
-            uint32_t v[32];
-            tmem_ld32(tmem + tlane + 128 * j + cg * 32, v);
+            uint32_t cb[16];
+            tmem_ld16(tmem + tlane + 128 * j + 16 * cg, cb);
             tmem_wait_ld();
-            if (fac) {
-              const float rowf = __expf(cl - sCum[s0 + 31]);
-              const float4* cf = reinterpret_cast<const float4*>(sColf + s0);
+            if (fR) {
+              const uint4* gp = reinterpret_cast<const uint4*>(sG + quad * 128 + (s0 >> 1));
 #pragma unroll
-              for (int q4 = 0; q4 < 8; ++q4) {
-                const float4 c4 = cf[q4];
-                float x0 = __uint_as_float(v[4 * q4]) * rowf * c4.x;
-                float x1 = __uint_as_float(v[4 * q4 + 1]) * rowf * c4.y;
-                float x2 = __uint_as_float(v[4 * q4 + 2]) * rowf * c4.z;
-                float x3 = __uint_as_float(v[4 * q4 + 3]) * rowf * c4.w;
-                if (diag) {
-                  const int sa = s0 + 4 * q4;
-                  x0 = sa <= l ? x0 : 0.f;
-                  x1 = sa + 1 <= l ? x1 : 0.f;
-                  x2 = sa + 2 <= l ? x2 : 0.f;
-                  x3 = sa + 3 <= l ? x3 : 0.f;
+              for (int q4 = 0; q4 < 4; ++q4) {
+                const uint4 g4 = gp[q4];
+                pk[4 * q4] = mul2<T16>(cb[4 * q4], g4.x);
+                pk[4 * q4 + 1] = mul2<T16>(cb[4 * q4 + 1], g4.y);
+                pk[4 * q4 + 2] = mul2<T16>(cb[4 * q4 + 2], g4.z);
+                pk[4 * q4 + 3] = mul2<T16>(cb[4 * q4 + 3], g4.w);
+              }
+              if (s0 == 32 * R) {
+                // diagonal tile: column c of the tile is kept when c <= lane
+#pragma unroll
+                for (int q = 0; q < 16; ++q) {
+                  const uint32_t keep = (2 * q + 1 <= lane) ? 0xffffffffu : ((2 * q <= lane) ? 0x0000ffffu : 0u);
+                  pk[q] &= keep;
                 }
-                pk[2 * q4] = pack2<T16>(x0, x1);
-                pk[2 * q4 + 1] = pack2<T16>(x2, x3);
               }
             } else {
 #pragma unroll
-              for (int jj = 0; jj < 16; ++jj) {
-                const int sa = s0 + 2 * jj, sb2 = sa + 1;
+              for (int q = 0; q < 16; ++q) {
+                const float2 c2 = unpack2<T16>(cb[q]);
+                const int sa = s0 + 2 * q, sb2 = sa + 1;
                 float x0 = 0.f, x1 = 0.f;
-                if (sa <= l && sa < ci.lim)
-                  x0 = __uint_as_float(v[2 * jj]) * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
-                if (sb2 <= l && sb2 < ci.lim)
-                  x1 = __uint_as_float(v[2 * jj + 1]) * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
-                pk[jj] = pack2<T16>(x0, x1);
+                if (sa <= l && sa < ci.lim) x0 = c2.x * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
+                if (sb2 <= l && sb2 < ci.lim) x1 = c2.y * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
+                pk[q] = pack2<T16>(x0, x1);
               }
             }
           }
@@ -903,64 +966,68 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           if (lane == 0) mbar_arrive(bar(MFULL0 + mb));
           ++Jc;
         }
-        if (fail) break;
-        if (i == si.nh - 1) {
+        if (i == si.nh - 1 && !wfail) {
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(CB_FREE));  // this item's CB is no longer read
         }
-        // ---- epilogue: y = exp(cum_l) Yoff + Yin (+ D x) (* silu z), columns [16cg, 16cg+16) ----
-        const long long tok = ci.tok0 + l;
+        // ---- epilogue: y = (exp(cum_l) Yoff + rowf_l Yin + D x) * silu(z), columns [16cg, 16cg+16) ----
+        // The Yoff and D x parts need only MMA3 (issued first for the head), so they
+        // run before the wait for the last MMA2.
         const bool valid = l < ci.lim;
-        const long long yrow = (tok * H + h) * 64 + cg * 16;
-        uint4 zv[2];
-        if (z && valid) {
-          const uint4* zp = reinterpret_cast<const uint4*>(z + yrow);
-          zv[0] = zp[0];
-          zv[1] = zp[1];
-        }
-        const int jl = Jc - 1;
-        ok = mbar_wait(bar(M2DONE0 + (jl & 1)), (jl >> 1) & 1, kSiteScanMma2);
+        const long long yrow = ((ci.tok0 + l) * H + h) * 64 + cg * 16;
+        warp_wait(bar(YOFF_DONE), Hc & 1, kSiteScanMma2);
         tc_fence_after();
-        if (!named_bar_and(1, 512, ok)) { fail = true; break; }
-        uint32_t ri[16], ro[16];
+        if (wfail) {
+          ++Hc;
+          continue;
+        }
+        float o[16];
+        {
+          uint32_t ro[16];
+          tmem_ld16(tmem + tlane + T_YOFF + cg * 16, ro);
+          tmem_wait_ld();
+          const float el = __expf(cl);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) o[jj] = el * __uint_as_float(ro[jj]);
+        }
+        if (D) {
+          const float4* sD4 = reinterpret_cast<const float4*>(sm + 512 + cg * 16);
+          const uint8_t* xr = sX + 16384 * m;  // x rows of this half
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const uint4 xv = *reinterpret_cast<const uint4*>(xr + sw128_off(r, cg * 2 + q));
+            const float4 da = sD4[2 * q], db = sD4[2 * q + 1];
+            const float dq[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+            const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = unpack2<T16>(w4[e]);
+              o[q * 8 + 2 * e] = fmaf(dq[2 * e], f.x, o[q * 8 + 2 * e]);
+              o[q * 8 + 2 * e + 1] = fmaf(dq[2 * e + 1], f.y, o[q * 8 + 2 * e + 1]);
+            }
+          }
+        }
+        const float rowf = fR ? __expf(cl - sCum[32 * R]) : 1.f;
+        const int jl = Jc - 1;
+        warp_wait(bar(M2DONE0 + (jl & 1)), (jl >> 1) & 1, kSiteScanMma2);
+        if (has_z) warp_wait(bar(Z_FULL), Hc & 1, kSiteScanTma);
+        tc_fence_after();
+        if (wfail) {
+          ++Hc;
+          continue;
+        }
+        uint32_t ri[16];
         tmem_ld16(tmem + tlane + T_YIN + cg * 16, ri);
-        tmem_ld16(tmem + tlane + T_YOFF + cg * 16, ro);
         tmem_wait_ld();
         tc_fence_before();
         if (valid) {
-          const float el = __expf(cl);
-          float o[16];
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) o[jj] = fmaf(el, __uint_as_float(ro[jj]), __uint_as_float(ri[jj]));
-          if (D) {
-            const float4* sD4 = reinterpret_cast<const float4*>(sm + 512 + cg * 16);
-            float dd[16];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float4 d4 = sD4[q];
-              dd[4 * q] = d4.x;
-              dd[4 * q + 1] = d4.y;
-              dd[4 * q + 2] = d4.z;
-              dd[4 * q + 3] = d4.w;
-            }
-            const uint8_t* xr = sX + 16384 * m;  // x rows of this half
+          for (int jj = 0; jj < 16; ++jj) o[jj] = fmaf(rowf, __uint_as_float(ri[jj]), o[jj]);
+          if (has_z) {
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
-              const uint4 xv = *reinterpret_cast<const uint4*>(xr + sw128_off(r, cg * 2 + q));
-              const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 f = unpack2<T16>(w4[e]);
-                const int pi = q * 8 + 2 * e;
-                o[pi] = fmaf(dd[pi], f.x, o[pi]);
-                o[pi + 1] = fmaf(dd[pi + 1], f.y, o[pi + 1]);
-              }
-            }
-          }
-          if (z) {
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              const uint32_t w4[4] = {zv[q].x, zv[q].y, zv[q].z, zv[q].w};
+              const uint4 zv = *reinterpret_cast<const uint4*>(sZ + sw128_off(r, cg * 2 + q));
+              const uint32_t w4[4] = {zv.x, zv.y, zv.z, zv.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const float2 f = unpack2<T16>(w4[e]);
@@ -983,14 +1050,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
                                  pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
           }
         }
-        // Y (TMEM) and the head stage (x tile, D, dt, cum) are free once every compute warp is here.
+        // Y (TMEM), the head stage (x, D, dt, cum, g) and the z tile are free once
+        // every compute warp is here.
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(EPI0 + hs));
         ++Hc;
       }
       ++I;
     }
-    if (fail) *s_abort = 1;
+    if (fail || wfail) *s_abort = 1;
   }
   tc_fence_before();
   __syncthreads();
@@ -1122,8 +1190,8 @@ cudaError_t launch_tc_state_pass(const LaunchCtx& c, int x_dtype, int dt_dtype, 
 
 template <bool BF16, typename YT>
 static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, const CUtensorMap& mc,
-                                  const CUtensorMap& mb, const CUtensorMap& mh, const float* A, const float* dt,
-                                  const float* cum, const float* D, const void* z, void* y) {
+                                  const CUtensorMap& mb, const CUtensorMap& mh, const CUtensorMap& mz, int has_z,
+                                  const float* A, const float* dt, const float* cum, const float* D, void* y) {
   if (c.H > kScanMaxHeads) return cudaErrorInvalidValue;
   auto kern = tc_chunk_scan_kernel<BF16, YT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kScanSmem);
@@ -1140,8 +1208,7 @@ static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, con
   const long long items = n_items(hb);
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
   const int grid = (int)(items < sms ? items : sms);  // persistent: one CTA per SM
-  kern<<<grid, kScanThreads, kScanSmem, c.stream>>>(mx, mc, mb, mh, A, dt, cum, D,
-                                                    reinterpret_cast<const typename T16Of<BF16>::type*>(z),
+  kern<<<grid, kScanThreads, kScanSmem, c.stream>>>(mx, mc, mb, mh, mz, A, dt, cum, D, has_z,
                                                     reinterpret_cast<YT*>(y), c.cm, c.H, c.G, hb, dt_nonneg,
                                                     (int)items);
   return cudaGetLastError();
@@ -1151,7 +1218,7 @@ cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, c
                                  const float* dt, const float* cum, const void* B, const void* C, const void* prev16,
                                  const float* D, const void* z, void* y, int* tmap_status) {
   const bool bf16 = x_dtype == SSD_BF16;
-  CUtensorMap mx, mc, mb, mh;
+  CUtensorMap mx, mc, mb, mh, mz;
   // prev16 holds the previous-chunk states in the input's 16-bit type, [chunk][head][n][p]
   // (p contiguous: the MN-major B operand of MMA3), so every
   // MMA of the kernel has operands of one type.
@@ -1163,14 +1230,20 @@ cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, c
     *tmap_status = 1;
     return cudaErrorInvalidValue;
   }
+  // z (same layout as u) is loaded one 128-row half at a time.
+  const int has_z = z != nullptr;
+  if (!make_map_3d(&mz, has_z ? z : u, bf16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128)) {
+    *tmap_status = 1;
+    return cudaErrorInvalidValue;
+  }
   *tmap_status = 0;
   if (y_dtype == SSD_F32) {
-    if (bf16) return tc_scan_launch<true, float>(c, mx, mc, mb, mh, A, dt, cum, D, z, y);
-    return tc_scan_launch<false, float>(c, mx, mc, mb, mh, A, dt, cum, D, z, y);
+    if (bf16) return tc_scan_launch<true, float>(c, mx, mc, mb, mh, mz, has_z, A, dt, cum, D, y);
+    return tc_scan_launch<false, float>(c, mx, mc, mb, mh, mz, has_z, A, dt, cum, D, y);
   }
   if (y_dtype == x_dtype) {
-    if (bf16) return tc_scan_launch<true, __nv_bfloat16>(c, mx, mc, mb, mh, A, dt, cum, D, z, y);
-    return tc_scan_launch<false, __half>(c, mx, mc, mb, mh, A, dt, cum, D, z, y);
+    if (bf16) return tc_scan_launch<true, __nv_bfloat16>(c, mx, mc, mb, mh, mz, has_z, A, dt, cum, D, y);
+    return tc_scan_launch<false, __half>(c, mx, mc, mb, mh, mz, has_z, A, dt, cum, D, y);
   }
   return cudaErrorInvalidValue;
 }
