@@ -64,7 +64,8 @@ def dist_setup(args):
         backend = "nccl" if torch.cuda.is_available() and args.impl == "ours" else "gloo"
         if torch.cuda.is_available():
             torch.cuda.set_device(local)
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+        kw = {"device_id": torch.device("cuda", local)} if backend == "nccl" else {}
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
     elif torch.cuda.is_available():
         torch.cuda.set_device(local)
     return rank, world, local
