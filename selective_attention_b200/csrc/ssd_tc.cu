@@ -265,25 +265,29 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
 //   prev_0 = h_init (or 0),  prev_{k+1} = exp(cum_last_k) prev_k + S_k,  h_last = prev_count.
 // prev_k is written in the input's 16-bit type for chunk_scan; the fp32 chunk
 // states never reach memory.
-// Roles: warp 0 (one lane) TMA producer of 64-token stages (B: two dstate
-// halves, x of each head) in a kSpStages-deep ring; warp 1 (one lane) MMA
-// issuer, accumulating chunk k in TMEM columns [128 (k & 1), +128) (head i at
-// +64 i); warps 2..5 (head 0) and 6..9 (head 1): dt / cum, x scaling and the
-// state update, thread = dstate row n (its TMEM lane). With an odd number of
-// heads per group the last CTA has one head; its second warp group only
+// Roles: warp 0 (one lane) TMA producer of 128-token stages (B: two dstate
+// halves, x of each head) in a kSpStages-deep ring; warp 1 (one lane) MMA issuer,
+// accumulating chunk k in TMEM columns [128 (k & 1), +128) (head i at +64 i);
+// warps 10 and 11 compute dt, cum and the token weights w of heads 0 and 1 one
+// chunk ahead into a double buffer; warps 2..5 (head 0) and 6..9 (head 1) scale x by w and
+// fold the chunk states, thread = dstate row n (its TMEM lane). With an odd number
+// of heads per group the last CTA has one head; its second warp group only
 // releases the stages.
 // Ordering without extra barriers: a head group folds chunk k-1 after it
 // released chunk k's stages, and MMA(k+1) into the same accumulator waits for
 // chunk k+1's first stage, which both groups release after that fold.
-constexpr int kSpStages = 6;
-constexpr int kSpStageBytes = 16384 + 2 * 8192;  // B [64 tokens x 2 halves x 128 B] | x head 0 | x head 1
-constexpr int kSpThreads = 320;
-constexpr int kSpSmem = kSpStages * kSpStageBytes + 2048 + 64 + 256 + 1024;
+constexpr int kSpStages = 3;
+constexpr int kSpStageBytes = 32768 + 2 * 16384;  // B [128 tokens x 2 halves x 128 B] | x head 0 | x head 1
+constexpr int kSpThreads = 384;                    // 2 role warps, 8 head-group warps, 2 prep warps
+constexpr int kSpWBufs = 3;  // w / exp(cum_last) buffers: the prep warps run up to two chunks ahead
+// ring | w [buffer][2 heads][256] | exp(cum_last) [buffer][2] | barriers, TMEM slot, abort flag
+constexpr int kSpSmem = kSpStages * kSpStageBytes + kSpWBufs * 2048 + 32 + 256 + 1024;
 
 enum : unsigned int {
   kSiteSpTma = 0x111,
   kSiteSpScaled = 0x112,
   kSiteSpMma = 0x113,
+  kSiteSpPrep = 0x114,
 };
 
 template <bool BF16, typename DT>
@@ -298,15 +302,16 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   auto sBst = [&](int s) { return smem + s * kSpStageBytes; };
-  auto sXst = [&](int s, int i) { return smem + s * kSpStageBytes + 16384 + 8192 * i; };
-  float* sW = reinterpret_cast<float*>(smem + NST * kSpStageBytes);  // [head][256] token weights
-  float* sWarp = sW + 512;                                             // [head][4] warp totals
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sWarp + 16);
-  // FULL[NST] SCALED[NST] EMPTY[NST] ACC[2]
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3 * NST + 2);
+  auto sXst = [&](int s, int i) { return smem + s * kSpStageBytes + 32768 + 16384 * i; };
+  constexpr int NW = kSpWBufs;
+  float* sW = reinterpret_cast<float*>(smem + NST * kSpStageBytes);  // [buffer][head][256] token weights
+  float* sEl = sW + 512 * NW;                                          // [buffer][head] exp(cum_last)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sEl + 8);
+  // FULL[NST] SCALED[NST] EMPTY[NST] ACC[2] W_READY[NW] W_FREE[NW]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3 * NST + 2 + 2 * NW);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const int FULL = 0, SCALED = NST, EMPTY = 2 * NST, ACC = 3 * NST;
+  const int FULL = 0, SCALED = NST, EMPTY = 2 * NST, ACC = 3 * NST, W_READY = 3 * NST + 2, W_FREE = W_READY + NW;
 
   // blockIdx.x -> (row, group, head pair of the group)
   const int npairs = (hpg + 1) >> 1;
@@ -338,6 +343,10 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
     }
     mbar_init(bar(ACC), 1);
     mbar_init(bar(ACC + 1), 1);
+    for (int b = 0; b < NW; ++b) {
+      mbar_init(bar(W_READY + b), 2);
+      mbar_init(bar(W_FREE + b), 8);
+    }
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -352,11 +361,11 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
     if (lane == 0) {
       int r = 0;
       bool fail = false;
-      const uint32_t bytes = 16384u + 8192u * (uint32_t)nh;
+      const uint32_t bytes = 32768u + 16384u * (uint32_t)nh;
       for (int k = 0; k < count && !fail && !*s_abort; ++k) {
         ChunkInfo ci;
         chunk_info(cm, first + k, ci);
-        const int nst = (ci.lim + 63) >> 6, t0 = (int)ci.tok0;
+        const int nst = (ci.lim + 127) >> 7, t0 = (int)ci.tok0;
         for (int s = 0; s < nst; ++s, ++r) {
           const int slot = r % NST;
           if (r >= NST && !mbar_wait(bar(EMPTY + slot), ((r / NST) - 1) & 1, kSiteSpMma)) {
@@ -365,9 +374,9 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
           }
           const uint32_t fb = bar(FULL + slot);
           mbar_expect_tx(fb, bytes);
-          tma_load_3d(smem_u32(sBst(slot)), &tm_b, 0, g, t0 + 64 * s, fb);
-          tma_load_3d(smem_u32(sBst(slot) + 8192), &tm_b, 64, g, t0 + 64 * s, fb);
-          for (int i = 0; i < nh; ++i) tma_load_3d(smem_u32(sXst(slot, i)), &tm_x, 0, h0 + i, t0 + 64 * s, fb);
+          tma_load_3d(smem_u32(sBst(slot)), &tm_b, 0, g, t0 + 128 * s, fb);
+          tma_load_3d(smem_u32(sBst(slot) + 16384), &tm_b, 64, g, t0 + 128 * s, fb);
+          for (int i = 0; i < nh; ++i) tma_load_3d(smem_u32(sXst(slot, i)), &tm_x, 0, h0 + i, t0 + 128 * s, fb);
         }
       }
       if (fail) *s_abort = 1;
@@ -387,7 +396,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       for (int k = 0; k < count && !fail && !*s_abort; ++k) {
         ChunkInfo ci;
         chunk_info(cm, first + k, ci);
-        const int nst = (ci.lim + 63) >> 6;
+        const int nst = (ci.lim + 127) >> 7;
         const uint32_t acc = tmem + 128 * (k & 1);
         for (int s = 0; s < nst; ++s, ++r) {
           const int slot = r % NST;
@@ -398,9 +407,9 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
           tc_fence_after();
           const uint32_t a0 = smem_u32(sBst(slot)), b0 = smem_u32(sXst(slot, 0));
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            umma_f16(acc, sdesc_sw128(a0 + ks * 2048, 8192, 1024), sdesc_sw128(b0 + ks * 2048, 8192, 1024), idesc,
-                     (s > 0 || ks > 0) ? 1u : 0u);
+          for (int ks = 0; ks < 8; ++ks)
+            umma_f16(acc, sdesc_sw128(a0 + ks * 2048, 16384, 1024), sdesc_sw128(b0 + ks * 2048, 16384, 1024),
+                     idesc, (s > 0 || ks > 0) ? 1u : 0u);
           umma_commit(bar(EMPTY + slot));
           last_bar = EMPTY + slot;
           last_par = (r / NST) & 1;
@@ -413,20 +422,85 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, kSiteSpMma);
     }
     __syncwarp();
+  } else if (warp >= 10) {
+    // ------------------------------------------------------------ dt / cum / w, one chunk ahead
+    // warp 10 + hl serves head hl; lane: tokens [8 lane, 8 lane + 8) of the chunk.
+    // Raw dt of the next chunk is loaded while this one is processed.
+    const int hl = warp - 10, tb = 8 * lane;
+    const bool act = hl < nh;
+    const int h = h0 + (act ? hl : 0);
+    const float a = A[h];
+    const float bias = delta_bias ? delta_bias[h] : 0.f;
+    auto load_raw = [&](int k, float (&rv)[8]) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) rv[e] = 0.f;
+      if (k >= count || !act) return;
+      ChunkInfo ci;
+      chunk_info(cm, first + k, ci);
+      const DT* dr = delta_raw + (ci.tok0 + tb) * (long long)H + h;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (tb + e < ci.vlim) rv[e] = Ld<DT>::f(dr + (long long)e * H);
+    };
+    float raw[8];
+    load_raw(0, raw);
+    bool fail = false;
+    for (int k = 0; k < count && !fail; ++k) {
+      const int buf = k % NW;
+      ChunkInfo ci;
+      chunk_info(cm, first + k, ci);
+      float d[8], c[8];
+      float run = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        d[e] = (act && tb + e < ci.vlim) ? dt_transform(raw[e] + bias, use_sp, dmin, dmax) : 0.f;
+        run += d[e] * a;
+        c[e] = run;
+      }
+      load_raw(k + 1, raw);
+      float incl = run;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const float o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      const float base = incl - run;
+      const float cl = __shfl_sync(0xffffffffu, incl, 31);
+      if (k >= NW && !__all_sync(0xffffffffu, mbar_wait(bar(W_FREE + buf), ((k - NW) / NW) & 1, kSiteSpPrep))) {
+        fail = true;
+        break;
+      }
+      if (act) {
+        const long long io = ((first + k) * (long long)H + h) * 256 + tb;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          *reinterpret_cast<float4*>(dt_out + io + 4 * q) =
+              make_float4(d[4 * q], d[4 * q + 1], d[4 * q + 2], d[4 * q + 3]);
+          *reinterpret_cast<float4*>(cum_out + io + 4 * q) =
+              make_float4(base + c[4 * q], base + c[4 * q + 1], base + c[4 * q + 2], base + c[4 * q + 3]);
+        }
+        float* w = sW + 512 * buf + 256 * hl + tb;
+        float wv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) wv[e] = tb + e < ci.lim ? __expf(fminf(cl - (base + c[e]), 0.f)) * d[e] : 0.f;
+        reinterpret_cast<float4*>(w)[0] = make_float4(wv[0], wv[1], wv[2], wv[3]);
+        reinterpret_cast<float4*>(w)[1] = make_float4(wv[4], wv[5], wv[6], wv[7]);
+        if (lane == 0) sEl[2 * buf + hl] = expf(cl);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(W_READY + buf));
+    }
+    if (fail) *s_abort = 1;
   } else {
     // ------------------------------------------------------------ head groups
     const int hg = (warp - 2) >> 2;   // head of the pair
     const bool active = hg < nh;
     const int bar_id = 1 + hg;
-    const int ctid = tid - 64 - 128 * hg, cw = (warp - 2) & 3;
+    const int cw = (warp - 2) & 3;
     const int quad = warp & 3, n = quad * 32 + lane;
     const uint32_t tlane = (uint32_t)(quad * 32) << 16;
     const int h = h0 + (active ? hg : 0);
-    const float a = A[h];
-    const float bias = delta_bias ? delta_bias[h] : 0.f;
     const long long PN = 64 * 128;
-    float* sWh = sW + 256 * hg;
-    float* sWarph = sWarp + 4 * hg;
     float prev[64];
     if (h_init && active) {
       const float* hi = h_init + ((long long)row * H + h) * PN + n;
@@ -436,16 +510,6 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
 #pragma unroll
       for (int p = 0; p < 64; ++p) prev[p] = 0.f;
     }
-    // Raw delta of tokens 2 ctid, 2 ctid + 1 of chunk k (loaded one chunk ahead).
-    auto load_raw = [&](int k, float& r0, float& r1) {
-      r0 = r1 = 0.f;
-      if (k >= count || !active) return;
-      ChunkInfo ci;
-      chunk_info(cm, first + k, ci);
-      const DT* dr = delta_raw + (ci.tok0 + 2 * ctid) * (long long)H + h;
-      if (2 * ctid < ci.vlim) r0 = Ld<DT>::f(dr);
-      if (2 * ctid + 1 < ci.vlim) r1 = Ld<DT>::f(dr + H);
-    };
     // prev16 row n of a chunk: 64 contiguous p values, eight 16-byte stores.
     auto store_prev16 = [&](T16* dst) {
       uint4* d4 = reinterpret_cast<uint4*>(dst);
@@ -454,12 +518,19 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         d4[q] = make_uint4(pack2<T16>(prev[8 * q], prev[8 * q + 1]), pack2<T16>(prev[8 * q + 2], prev[8 * q + 3]),
                            pack2<T16>(prev[8 * q + 4], prev[8 * q + 5]), pack2<T16>(prev[8 * q + 6], prev[8 * q + 7]));
     };
-    bool wfail = false;  // this warp gave up on a wait; the group learns it at its next barrier
+    // Warps wait independently; a warp that gives up stops releasing work and the
+    // group leaves at its next barrier, which ANDs the flags.
+    bool wfail = false;
+    auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
+      if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
+      return !wfail;
+    };
     // Fold the finished chunk j: prev = exp(cum_last_j) prev + S_j, then store.
-    auto fold = [&](int j, float el) -> bool {
-      bool ok = !wfail && mbar_wait(bar(ACC + (j & 1)), (j >> 1) & 1, kSiteSpMma);
+    auto fold = [&](int j) -> bool {
+      warp_wait(bar(ACC + (j & 1)), (j >> 1) & 1, kSiteSpMma);
       tc_fence_after();
-      if (!named_bar_and(bar_id, 128, ok && !*s_abort)) return false;
+      if (!named_bar_and(bar_id, 128, !wfail && !*s_abort)) return false;
+      const float el = sEl[2 * (j % NW) + hg];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t v[32];
@@ -469,6 +540,8 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         for (int q = 0; q < 32; ++q) prev[32 * half + q] = fmaf(el, prev[32 * half + q], __uint_as_float(v[q]));
       }
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(W_FREE + j % NW));  // w / exp(cum_last) of chunk j no longer read
       if (j + 1 < count) {
         store_prev16(prev16 + ((long long)(first + j + 1) * H + h) * PN + n * 64);
       } else {
@@ -488,92 +561,61 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         store_prev16(prev16 + ((long long)first * H + h) * PN + n * 64);
       }
     }
-    float raw0, raw1;
-    load_raw(0, raw0, raw1);
-    float el_prev = 1.f;
     int r = 0;
     for (int k = 0; k < count && !fail; ++k) {
       ChunkInfo ci;
       chunk_info(cm, first + k, ci);
-      const long long kk = first + k;
-      const int nst = (ci.lim + 63) >> 6;
-      // ---- dt / cum of the chunk (shuffle scan over 128 threads x 2 tokens) ----
-      float d0 = 0.f, d1 = 0.f, c0 = 0.f, tot = 0.f, incl = 0.f, cl = 0.f;
-      if (active) {
-        d0 = 2 * ctid < ci.vlim ? dt_transform(raw0 + bias, use_sp, dmin, dmax) : 0.f;
-        d1 = 2 * ctid + 1 < ci.vlim ? dt_transform(raw1 + bias, use_sp, dmin, dmax) : 0.f;
-        load_raw(k + 1, raw0, raw1);
-        c0 = d0 * a;
-        tot = c0 + d1 * a;
-        incl = tot;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const float o = __shfl_up_sync(0xffffffffu, incl, off);
-          if (lane >= off) incl += o;
-        }
-        if (lane == 31) sWarph[cw] = incl;
-      }
-      // Every barrier of the group ANDs the warps' wait results, so all of them
-      // leave together when one gave up.
-      if (!named_bar_and(bar_id, 128, !wfail && !*s_abort)) {
-        fail = true;
-        break;
-      }
-      if (active) {
-        float wbase = 0.f;
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          const float t = sWarph[w];
-          wbase += w < cw ? t : 0.f;
-          cl += t;
-        }
-        const float excl = wbase + incl - tot;
-        const float cum0 = excl + c0, cum1 = excl + tot;
-        const long long io = (kk * H + h) * 256 + 2 * ctid;
-        *reinterpret_cast<float2*>(dt_out + io) = make_float2(d0, d1);
-        *reinterpret_cast<float2*>(cum_out + io) = make_float2(cum0, cum1);
-        sWh[2 * ctid] = 2 * ctid < ci.lim ? __expf(fminf(cl - cum0, 0.f)) * d0 : 0.f;
-        sWh[2 * ctid + 1] = 2 * ctid + 1 < ci.lim ? __expf(fminf(cl - cum1, 0.f)) * d1 : 0.f;
-      }
-      named_bar_sync(bar_id, 128);
+      const int nst = (ci.lim + 127) >> 7, buf = k % NW;
+      warp_wait(bar(W_READY + buf), (k / NW) & 1, kSiteSpPrep);
+      const float* wh = sW + 512 * buf + 256 * hg;
       // ---- x rows scaled by w_l in place (rows past `lim` become exact zeros) ----
-      // Warps go through the stages independently; a warp that gave up stops
-      // releasing stages and the group leaves at its next barrier.
       for (int s = 0; s < nst; ++s, ++r) {
         const int slot = r % NST;
-        if (!wfail) {
-          const bool ok = mbar_wait(bar(FULL + slot), (r / NST) & 1, kSiteSpTma);
-          wfail = !__all_sync(0xffffffffu, ok);
-        }
+        warp_wait(bar(FULL + slot), (r / NST) & 1, kSiteSpTma);
         if (wfail) continue;
         if (active) {
-          uint8_t* sx = sXst(slot, hg);
+          uint4* sx = reinterpret_cast<uint4*>(sXst(slot, hg)) + cw * 32 + lane;
+          // All loads first: stores through the same shared-memory pointers would
+          // otherwise order each chunk's load behind the previous chunk's store.
+          uint4 xv[8];
+          float wv[8];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int q = cw * 32 + lane + 128 * i;
-            uint4* pch = reinterpret_cast<uint4*>(sx + q * 16);
-            const float w = sWh[64 * s + (q >> 3)];
+          for (int i = 0; i < 8; ++i) {
+            xv[i] = sx[128 * i];
+            wv[i] = wh[128 * s + ((cw * 32 + lane + 128 * i) >> 3)];
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            uint4 o4;
             if constexpr (BF16) {
-              const __nv_bfloat162 w2 = __float2bfloat162_rn(w);
-              *pch = (w == 0.f) ? make_uint4(0u, 0u, 0u, 0u)
-                                : scale8_packed<T16>(*pch, *reinterpret_cast<const uint32_t*>(&w2));
+              const __nv_bfloat162 w2 = __float2bfloat162_rn(wv[i]);
+              o4 = scale8_packed<T16>(xv[i], *reinterpret_cast<const uint32_t*>(&w2));
             } else {
-              *pch = (w == 0.f) ? make_uint4(0u, 0u, 0u, 0u) : scale8<T16>(*pch, w);
+              o4 = scale8<T16>(xv[i], wv[i]);
             }
+            sx[128 * i] = (wv[i] == 0.f) ? make_uint4(0u, 0u, 0u, 0u) : o4;
           }
           fence_proxy_async_smem();
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(SCALED + slot));
       }
+      if (!active) {
+        // the group of a missing second head only releases stages (and w buffers)
+        if (!wfail) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(W_FREE + buf));
+        }
+        if (!named_bar_and(bar_id, 128, !wfail && !*s_abort)) fail = true;
+        continue;
+      }
       // ---- fold the previous chunk while this chunk's MMAs run ----
-      if (active && k > 0 && !fold(k - 1, el_prev)) {
+      if (k > 0 && !fold(k - 1)) {
         fail = true;
         break;
       }
-      el_prev = expf(cl);
     }
-    if (active && !fail && count > 0 && !fold(count - 1, el_prev)) fail = true;
+    if (active && !fail && count > 0 && !fold(count - 1)) fail = true;
     if (fail || wfail) *s_abort = 1;
   }
   tc_fence_before();
@@ -925,14 +967,20 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
 #pragma unroll
             for (int q = 0; q < 16; ++q) pk[q] = 0u;
           } else {
+            // g pairs before the TMEM load: the wait below is a compiler memory barrier.
+            uint4 g4v[4];
+            if (fR) {
+              const uint4* gp = reinterpret_cast<const uint4*>(sG + quad * 128 + (s0 >> 1));
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4) g4v[q4] = gp[q4];
+            }
             uint32_t cb[16];
             tmem_ld16(tmem + tlane + 128 * j + 16 * cg, cb);
             tmem_wait_ld();
             if (fR) {
-              const uint4* gp = reinterpret_cast<const uint4*>(sG + quad * 128 + (s0 >> 1));
 #pragma unroll
               for (int q4 = 0; q4 < 4; ++q4) {
-                const uint4 g4 = gp[q4];
+                const uint4 g4 = g4v[q4];
                 pk[4 * q4] = mul2<T16>(cb[4 * q4], g4.x);
                 pk[4 * q4 + 1] = mul2<T16>(cb[4 * q4 + 1], g4.y);
                 pk[4 * q4 + 2] = mul2<T16>(cb[4 * q4 + 2], g4.z);
@@ -975,6 +1023,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         // run before the wait for the last MMA2.
         const bool valid = l < ci.lim;
         const long long yrow = ((ci.tok0 + l) * H + h) * 64 + cg * 16;
+        const float rowf = fR ? __expf(cl - sCum[32 * R]) : 1.f;
         warp_wait(bar(YOFF_DONE), Hc & 1, kSiteScanMma2);
         tc_fence_after();
         if (wfail) {
@@ -992,10 +1041,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         }
         if (D) {
           const float4* sD4 = reinterpret_cast<const float4*>(sm + 512 + cg * 16);
-          const uint8_t* xr = sX + 16384 * m;  // x rows of this half
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
-            const uint4 xv = *reinterpret_cast<const uint4*>(xr + sw128_off(r, cg * 2 + q));
+            const uint4 xv = *reinterpret_cast<const uint4*>(sX + 16384 * m + sw128_off(r, cg * 2 + q));
             const float4 da = sD4[2 * q], db = sD4[2 * q + 1];
             const float dq[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
             const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
@@ -1007,10 +1055,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
             }
           }
         }
-        const float rowf = fR ? __expf(cl - sCum[32 * R]) : 1.f;
+        uint4 zv0 = make_uint4(0u, 0u, 0u, 0u), zv1 = zv0;
+        if (has_z && warp_wait(bar(Z_FULL), Hc & 1, kSiteScanTma)) {
+          zv0 = *reinterpret_cast<const uint4*>(sZ + sw128_off(r, cg * 2));
+          zv1 = *reinterpret_cast<const uint4*>(sZ + sw128_off(r, cg * 2 + 1));
+        }
         const int jl = Jc - 1;
         warp_wait(bar(M2DONE0 + (jl & 1)), (jl >> 1) & 1, kSiteScanMma2);
-        if (has_z) warp_wait(bar(Z_FULL), Hc & 1, kSiteScanTma);
         tc_fence_after();
         if (wfail) {
           ++Hc;
@@ -1026,7 +1077,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           if (has_z) {
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
-              const uint4 zv = *reinterpret_cast<const uint4*>(sZ + sw128_off(r, cg * 2 + q));
+              const uint4 zv = q ? zv1 : zv0;
               const uint32_t w4[4] = {zv.x, zv.y, zv.z, zv.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
@@ -1176,8 +1227,8 @@ cudaError_t launch_tc_state_pass(const LaunchCtx& c, int x_dtype, int dt_dtype, 
                                  float* cum, void* prev16, const float* h_init, float* h_last, int* tmap_status) {
   const bool bf16 = x_dtype == SSD_BF16;
   CUtensorMap mx, mb;
-  if (!make_map_3d(&mx, u, bf16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 64) ||
-      !make_map_3d(&mb, B, bf16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 64)) {
+  if (!make_map_3d(&mx, u, bf16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&mb, B, bf16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128)) {
     *tmap_status = 1;
     return cudaErrorInvalidValue;
   }
