@@ -13,8 +13,9 @@ slowest rank's device time.
 Timing: CUDA events on the launching stream around each step, L2 flushed
 (256 MiB write) between steps outside the events, barrier + synchronize on both
 sides of the timed loop, max over ranks. ``e2e`` repeats the measurement through
-the public op (``SSDScanFn``) with pinned host inputs copied in and ``y``/``h_last``
-copied out inside the timed region. ``--impl reference`` times the CPU
+the public API with pinned host inputs copied in and ``y``/``h_last`` copied out
+inside the timed region: ``HostStreamScan`` (row slices whose copies overlap the
+scan) for padded batches, ``SSDScanFn`` with explicit copies for packed ones. ``--impl reference`` times the CPU
 restatement of the reference's five stages (``oracle/``) on the host cores instead.
 """
 from __future__ import annotations
@@ -398,7 +399,9 @@ def _traffic_from_profiles(kernel, cfg_name):
 
 
 def e2e_measure(args, cfg, inp, dev, world, flush):
-    """Same metric through SSDScanFn with pinned host inputs and outputs."""
+    """Same metric through the public API with pinned host inputs and outputs: the
+    streaming entry ``HostStreamScan`` (row slices, copies overlapped with the scan) for
+    padded batches, ``SSDScanFn`` with explicit copies for packed ones."""
     import selective_attention_b200 as sab
 
     names = ["u", "B", "C", "delta_raw", "z"]
@@ -410,8 +413,14 @@ def e2e_measure(args, cfg, inp, dev, world, flush):
     nrow = cfg.batch if cu is None else cu.numel() - 1
     h_h = torch.empty(nrow, cfg.nheads, cfg.headdim, cfg.dstate, dtype=torch.float32).pin_memory()
     stream = torch.cuda.current_stream(dev)
+    scanner = sab.HostStreamScan(dev, slices=8, streams=2) if cu is None else None
+    A_h, D_h = small["A"].cpu(), small["D"].cpu()
 
     def step():
+        if scanner is not None:
+            scanner(host["u"], A_h, host["B"], host["C"], host["delta_raw"], None, None, None, cfg.chunk, True,
+                    (0.0, INF), D_h, host.get("z"), out=(y_h, h_h))
+            return
         for k, t in host.items():
             dev_in[k].copy_(t, non_blocking=True)
         y, h = sab.SSDScanFn.apply(dev_in["u"], small["A"], dev_in["B"], dev_in["C"], dev_in["delta_raw"], None,
@@ -431,7 +440,8 @@ def e2e_measure(args, cfg, inp, dev, world, flush):
     d2h = y_h.numel() * y_h.element_size() + h_h.numel() * h_h.element_size()
     return {"value": world * cfg.tokens / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms, "steps": steps,
-            "note": "pinned host -> device inputs, SSDScanFn, device -> pinned host y and h_last, per step"}
+            "note": ("pinned host -> device inputs, scan, device -> pinned host y and h_last, per step; "
+                     + ("HostStreamScan, 8 row slices on 2 streams" if scanner is not None else "SSDScanFn"))}
 
 
 def ssu_measure(args, dev, flush, hbm_peak, world):

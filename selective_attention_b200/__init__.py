@@ -6,11 +6,14 @@ Public surface (mirrors the reference's ``selective_attention.ops`` and
 - ``SSDScanFn`` / ``SSUFn``: drop-in ops with the reference's signatures.
 - ``kernels``: stage-level host functions (``chunk_cumsum_forward`` ... ``ssd_scan_forward``,
   ``ssu_forward``) over the C ABI of ``libssd_b200.so`` (``include/ssd_b200.h``).
+- ``HostStreamScan``: the SSD forward on inputs in pinned host memory, with the copies
+  of row slices overlapped with the scan (no reference counterpart).
 - ``shim.install()``: make an installed reference package use these kernels.
 - ``check_device_error()``: surface a kernel's bounded-wait timeout as ``RuntimeError``.
 """
 from ._lib import check_device_error, device_error
 from .ops import SSDScanFn, SSUFn
+from .streaming import HostStreamScan
 from .kernels import (
     bmm_chunk_forward,
     chunk_cumsum_forward,
@@ -22,7 +25,7 @@ from .kernels import (
 )
 
 __all__ = [
-    "SSDScanFn", "SSUFn", "ssd_scan_forward", "ssu_forward", "chunk_cumsum_forward",
+    "SSDScanFn", "SSUFn", "HostStreamScan", "ssd_scan_forward", "ssu_forward", "chunk_cumsum_forward",
     "chunk_state_forward", "state_passing_forward", "bmm_chunk_forward", "chunk_scan_forward",
     "check_device_error", "device_error",
 ]

@@ -1250,12 +1250,12 @@ static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, con
   const int dt_nonneg = (c.dmax >= 0.f) && (c.use_sp || c.dmin >= 0.f);
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // Heads per item: up to 8 share one CB; fewer when that leaves too few items
-  // to keep every SM busy (about four items per CTA).
+  // Heads per item: up to 8 share one CB (its load, MMA and rounding are paid once
+  // per item); fewer when that leaves under two items per CTA.
   const int hpg = c.H / c.G;
   int hb = hpg < 8 ? hpg : 8;
   auto n_items = [&](int b) { return 2ll * c.nchunks_max * c.G * ((hpg + b - 1) / b); };
-  while (hb > 1 && n_items(hb) < 4ll * sms) hb = (hb + 1) / 2;
+  while (hb > 1 && n_items(hb) < 2ll * sms) hb = (hb + 1) / 2;
   const long long items = n_items(hb);
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
   const int grid = (int)(items < sms ? items : sms);  // persistent: one CTA per SM

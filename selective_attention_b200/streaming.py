@@ -1,0 +1,134 @@
+"""SSD forward on inputs that live in (pinned) host memory.
+
+``HostStreamScan`` runs ``ssd_scan_forward`` over a padded batch whose tensors are in
+host memory: the batch is cut into row slices and each slice goes host -> device,
+through the scan and back on one of two CUDA streams, so the copies of one slice
+overlap the scan and the copy back of its neighbours. Rows are independent in the
+scan, so the result equals one ``ssd_scan_forward`` over the whole batch (the kernel
+chain chosen per slice may differ, with the same tolerance as between chains).
+
+There is no reference counterpart: the reference takes device tensors only. This is
+the entry for callers whose data is not resident on the GPU.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Sequence
+
+import torch
+
+from . import kernels
+
+INF = float("inf")
+
+
+class HostStreamScan:
+    """Reusable host -> device -> host streaming SSD forward for one problem shape.
+
+    Device buffers for two slices (one per stream) and the per-slice workspaces are
+    allocated on first use and kept, so repeated calls allocate nothing on the device.
+    """
+
+    def __init__(self, device=None, slices: int = 4, streams: int = 2):
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.slices = max(1, int(slices))
+        self.nstreams = max(1, int(streams))
+        self._key = None
+        self._bufs = None
+        self._streams = [torch.cuda.Stream(self.device) for _ in range(self.nstreams)]
+
+    def _buffers(self, key, rows, L, H, P, G, N, dtypes, have):
+        if self._key == key:
+            return self._bufs
+        dev = self.device
+        bufs = []
+        for _ in range(self.nstreams):
+            b = {
+                "u": torch.empty(rows, L, H, P, device=dev, dtype=dtypes["u"]),
+                "B": torch.empty(rows, L, G, N, device=dev, dtype=dtypes["u"]),
+                "C": torch.empty(rows, L, G, N, device=dev, dtype=dtypes["u"]),
+                "delta_raw": torch.empty(rows, L, H, device=dev, dtype=dtypes["delta_raw"]),
+                "y": torch.empty(rows, L, H, P, device=dev, dtype=dtypes["y"]),
+                "h_last": torch.empty(rows, H, P, N, device=dev, dtype=torch.float32),
+            }
+            if have["z"]:
+                b["z"] = torch.empty((rows,) + have["z"], device=dev, dtype=dtypes["u"])
+            if have["h_init"]:
+                b["h_init"] = torch.empty(rows, H, P, N, device=dev, dtype=torch.float32)
+            if have["length"]:
+                b["length"] = torch.empty(rows, device=dev, dtype=torch.int64)
+            b["workspace"] = torch.empty(0, device=dev, dtype=torch.uint8)
+            bufs.append(b)
+        self._key, self._bufs = key, bufs
+        return bufs
+
+    def __call__(self, u, A, B, C, delta_raw, delta_bias=None, h_init=None, length=None, chunk_size=256,
+                 use_delta_softplus=True, delta_limit=(0.0, INF), D=None, z=None, impl: str = "auto",
+                 out: Optional[Sequence[torch.Tensor]] = None):
+        """Same arguments and results as ``ssd_scan_forward`` (padded rows only), with
+        u, B, C, delta_raw, z, h_init and length in host memory; results land in host
+        memory (``out`` or new pinned tensors). A, D and delta_bias may be on either side.
+        Returns once the work is queued; synchronize the current stream before reading."""
+        if u.dim() != 4 or B.dim() != 4 or C.dim() != 4 or delta_raw.dim() != 3:
+            raise ValueError("expected u (b, L, H, P), B and C (b, L, G, N), delta_raw (b, L, H)")
+        for t, n in ((u, "u"), (B, "B"), (C, "C"), (delta_raw, "delta_raw"), (z, "z"), (h_init, "h_init"),
+                     (length, "length")):
+            if t is not None and t.is_cuda:
+                raise ValueError(f"[{n}] HostStreamScan takes host tensors; use ssd_scan_forward for device ones")
+        b, L, H, P = u.shape
+        G, N = B.shape[2], B.shape[3]
+        dev = self.device
+        y_dtype = u.dtype if (D is not None or z is not None) else torch.float32
+        if out is None:
+            y_h = torch.empty(b, L, H, P, dtype=y_dtype).pin_memory()
+            h_h = torch.empty(b, H, P, N, dtype=torch.float32).pin_memory()
+        else:
+            y_h, h_h = out
+        small = {}
+        for n, t in (("A", A), ("D", D), ("delta_bias", delta_bias)):
+            small[n] = None if t is None else t.to(dev, dtype=torch.float32, non_blocking=True)
+        rows = math.ceil(b / self.slices)
+        # z keeps its own trailing shape: (L, H, P) or the SSM layer's (L, H * P)
+        have = {"z": None if z is None else tuple(z.shape[1:]), "h_init": h_init is not None,
+                "length": length is not None}
+        key = (rows, L, H, P, G, N, u.dtype, delta_raw.dtype, y_dtype, have["z"], have["h_init"], have["length"])
+        bufs = self._buffers(key, rows, L, H, P, G, N, {"u": u.dtype, "delta_raw": delta_raw.dtype, "y": y_dtype},
+                             have)
+        cur = torch.cuda.current_stream(dev)
+        start = torch.cuda.Event()
+        start.record(cur)
+        for s in self._streams:
+            s.wait_event(start)
+        for i, r0 in enumerate(range(0, b, rows)):
+            r1 = min(b, r0 + rows)
+            n = r1 - r0
+            s = self._streams[i % self.nstreams]
+            d = bufs[i % self.nstreams]
+            with torch.cuda.stream(s):
+                dv = {}
+                for name, t in (("u", u), ("B", B), ("C", C), ("delta_raw", delta_raw), ("z", z), ("h_init", h_init),
+                                ("length", length)):
+                    if t is None:
+                        dv[name] = None
+                        continue
+                    dv[name] = d[name][:n]
+                    dv[name].copy_(t[r0:r1], non_blocking=True)
+                y_d, h_d = d["y"][:n], d["h_last"][:n]
+                p, keep, _ = kernels.ssd_scan_params(dv["u"], small["A"], dv["B"], dv["C"], dv["delta_raw"],
+                                                     small["delta_bias"], dv["h_init"], dv["length"], chunk_size,
+                                                     use_delta_softplus, delta_limit, small["D"], dv["z"], None, impl)
+                need = kernels.workspace_size(p)
+                if d["workspace"].numel() < need:
+                    d["workspace"] = torch.empty(need, device=dev, dtype=torch.uint8)
+                kernels.ssd_scan_forward(dv["u"], small["A"], dv["B"], dv["C"], dv["delta_raw"], small["delta_bias"],
+                                         dv["h_init"], dv["length"], chunk_size, use_delta_softplus, delta_limit,
+                                         True, small["D"], dv["z"], None, impl, out=(y_d, h_d),
+                                         workspace=d["workspace"])
+                y_h[r0:r1].copy_(y_d, non_blocking=True)
+                h_h[r0:r1].copy_(h_d, non_blocking=True)
+                del keep
+        for s in self._streams:
+            done = torch.cuda.Event()
+            done.record(s)
+            cur.wait_event(done)
+        return y_h, h_h

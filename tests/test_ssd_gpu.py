@@ -288,3 +288,28 @@ def test_backward_raises():
     y, _ = sab.SSDScanFn.apply(u, dev(i["A"]), dev(i["B"]), dev(i["C"]), dev(i["delta_raw"]), None, None, None, 64)
     with pytest.raises(NotImplementedError):
         y.sum().backward()
+
+
+@pytest.mark.parametrize("slices", [1, 3])
+def test_host_stream_scan_matches_device_scan(slices):
+    """HostStreamScan (host inputs, row slices on two streams) == ssd_scan_forward on the device."""
+    import selective_attention_b200 as sab
+    from selective_attention_b200 import kernels
+
+    inp = _c_inputs("c1", seed=9, batch=5, seqlen=600, nheads=8, h_init=True, delta_bias=True)
+    length = torch.tensor([600, 512, 333, 1, 600])
+    host = {k: inp[k].pin_memory() for k in ("u", "B", "C", "delta_raw", "z", "h_init")}
+    scan = sab.HostStreamScan(slices=slices, streams=2)
+    for _ in range(2):  # second call reuses the device buffers
+        y, h = scan(host["u"], inp["A"], host["B"], host["C"], host["delta_raw"], inp["delta_bias"], host["h_init"],
+                    length, 256, True, (0.0, INF), inp["D"], host["z"])
+        torch.cuda.synchronize()
+        sab.check_device_error()
+        assert not y.is_cuda and not h.is_cuda
+        y_ref, h_ref = kernels.ssd_scan_forward(dev(inp["u"]), dev(inp["A"]), dev(inp["B"]), dev(inp["C"]),
+                                                dev(inp["delta_raw"]), dev(inp["delta_bias"]), dev(inp["h_init"]),
+                                                dev(length), 256, True, (0.0, INF), True, dev(inp["D"]), dev(inp["z"]))
+        assert_bf16_close(y.float(), y_ref.float().cpu(), f"stream scan y ({slices} slices)")
+        assert_bf16_close(h, h_ref.cpu(), f"stream scan h_last ({slices} slices)")
+    with pytest.raises(ValueError):
+        scan(dev(inp["u"]), inp["A"], host["B"], host["C"], host["delta_raw"])
