@@ -313,3 +313,52 @@ def test_host_stream_scan_matches_device_scan(slices):
         assert_bf16_close(h, h_ref.cpu(), f"stream scan h_last ({slices} slices)")
     with pytest.raises(ValueError):
         scan(dev(inp["u"]), inp["A"], host["B"], host["C"], host["delta_raw"])
+
+
+@pytest.mark.parametrize("impl", TC_IMPLS)
+def test_packed_edge_lengths_odd_heads_per_group(impl):
+    """Packed rows of lengths 1, 0, 63, 129, 256, 300, 17 with 3 heads per group (the
+    fused kernel's last head pair holds one head), h_init per sequence, D and z, against
+    the padded oracle (each sequence its own row with length = seqlen)."""
+    import selective_attention_b200 as sab
+
+    g = torch.Generator().manual_seed(31)
+    lens = [1, 0, 63, 129, 256, 300, 17]
+    T, H, P, N, G = sum(lens), 6, 64, 128, 2
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    u = torch.randn(1, T, H, P, generator=g).bfloat16()
+    B = (torch.randn(1, T, G, N, generator=g) / math.sqrt(N)).bfloat16()
+    C = (torch.randn(1, T, G, N, generator=g) / math.sqrt(N)).bfloat16()
+    dr = torch.randn(1, T, H, generator=g) - 4.0
+    A = -torch.exp(torch.rand(H, generator=g) * math.log(16.0))
+    db = 0.1 * torch.randn(H, generator=g)
+    h0 = 0.1 * torch.randn(len(lens), H, P, N, generator=g)
+    D = torch.randn(H * P, generator=g)
+    z = torch.randn(1, T, H, P, generator=g).bfloat16()
+    y, h = sab.SSDScanFn.apply(dev(u), dev(A), dev(B), dev(C), dev(dr), dev(db), dev(h0), None, 256, True,
+                               (0.0, INF), True, dev(D), dev(z), dev(cu), impl)
+    sab.check_device_error()
+    y_ref, h_ref = ssd_ref.ssd_scan_varlen(u.float(), A, B.float(), C.float(), dr, db, cu, 256, h_init=h0)
+    y_ref = ssd_ref.gate_epilogue(y_ref, u, D, z)
+    assert_bf16_close(y, y_ref, f"packed edge y ({impl})")
+    assert_bf16_close(h, h_ref, f"packed edge h_last ({impl})")
+
+
+@pytest.mark.parametrize("impl", TC_IMPLS)
+def test_padded_odd_heads_per_group_ragged(impl):
+    """Padded rows with 3 heads per group, ragged lengths and h_init (fused kernel's
+    single-head pair on the padded path)."""
+    import selective_attention_b200 as sab
+
+    inp = _c_inputs("c4", seed=13, batch=3, seqlen=700, nheads=6, h_init=True, delta_bias=True)
+    length = torch.tensor([700, 129, 0])
+    y, h = sab.SSDScanFn.apply(dev(inp["u"]), dev(inp["A"]), dev(inp["B"][:, :, :2]), dev(inp["C"][:, :, :2]),
+                               dev(inp["delta_raw"]), dev(inp["delta_bias"]), dev(inp["h_init"]), dev(length), 256,
+                               True, (0.0, INF), True, dev(inp["D"]), dev(inp["z"]), None, impl)
+    sab.check_device_error()
+    y_ref, h_ref = ssd_ref.ssd_scan_forward(inp["u"].float(), inp["A"], inp["B"][:, :, :2].float(),
+                                            inp["C"][:, :, :2].float(), inp["delta_raw"], inp["delta_bias"],
+                                            inp["h_init"], length, 256)
+    y_ref = ssd_ref.gate_epilogue(y_ref, inp["u"], inp["D"], inp["z"])
+    assert_bf16_close(y, y_ref, f"odd heads y ({impl})")
+    assert_bf16_close(h, h_ref, f"odd heads h_last ({impl})")
