@@ -33,28 +33,28 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
 }
-// The suspend-time hint lets a waiting thread sleep (up to the hint, in ns) instead
-// of spinning, so waiting warps do not take issue slots from working ones; the
-// thread resumes as soon as the phase completes.
-constexpr uint32_t kSuspendHintNs = 200000;
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+// Non-blocking test of the phase with the given parity.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "r"(bar), "r"(parity)
       : "memory");
   return ok != 0;
 }
 // Bounded wait for the phase with the given parity to complete. Returns false
 // (after recording `site` in the error flag) if it did not complete in time.
+// The pipeline hand-offs are short, so the wait polls with test_wait (it sees the
+// phase flip sooner than a suspended try_wait is woken); the clock check every
+// eighth poll also spaces the polls out.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int site) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1; it < kWaitMaxPolls; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_test_wait(bar, parity)) return true;
     if ((it & 7u) == 0u && globaltimer_ns() - t0 > kWaitTimeoutNs) break;
   }
   record_error(site);

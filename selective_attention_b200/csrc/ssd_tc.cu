@@ -630,7 +630,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
 // Per item, C rows of the half and B rows [0, 128(m+1)) are loaded once,
 // CB_j = C B_j^T (j = 0..m, 128 source tokens each) is computed once into TMEM
 // and rounded there to the input's 16-bit type; then, head by head, only x, prev,
-// z, dt, cum and D are loaded.
+// z, dt and cum are loaded (the epilogue reads D from global memory).
 // The decay is factored per 32-row block R (rows [32R, 32R+32) of the chunk):
 //   exp(cum_l - cum_s) = exp(cum_l - cum_{32R}) * exp(cum_{32R} - cum_s)
 // Both factors are <= 1 for s < 32R when cum is non-increasing (A <= 0, dt >= 0);
@@ -643,24 +643,31 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
 //   Yin  += M'_j x_j   (A from TMEM)    Yoff = C prev     (per head)
 //   y = exp(cum_l) Yoff + rowf_l Yin (+ D x) (* silu z)
 // Roles (one CTA per SM, items blockIdx.x, blockIdx.x + gridDim.x, ...):
-//   warp 0 (one lane)  TMA producer: item tiles (C, B) single-buffered, head tiles
-//                      (x, prev, dt, cum, D) in a 2-deep ring, z tile one head ahead;
+//   warp 0 (one lane)  TMA producer: C per item, B one 128-token block at a time,
+//                      head stages (x, prev, dt, cum) in a 3-deep ring; z of a head
+//                      goes into its stage's prev tile once MMA3 has read prev;
 //   warp 1 (one lane)  MMA issuer;
-//   warps 2..17        compute: CB_j -> M'_j conversion (warp: one 32-column block of
-//                      a 32-row quadrant), then the head's epilogue (16 output columns).
-// TMEM columns: CB_0 [0,128) CB_1 [128,256) (fp32 from MMA1; 16-bit in the first
-//               64 columns of each after the per-item rounding), M buffers
-//               [256,320) [320,384), Yin [384,448), Yoff [448,512).
+//   warps 2..9         conversion: CB_j landing (fp32) -> 16 bits per item, then per
+//                      head the g table and CB_j -> M'_j (warp: two 32-column blocks
+//                      of a 32-row quadrant);
+//   warps 10..17       epilogue of the previous head (32 output columns per warp),
+//                      so conversion of head i+1 overlaps the epilogue of head i.
+// TMEM columns: 16-bit CB_0 [0,64) CB_1 [64,128); Y buffer 1 (Yin, Yoff) [128,256),
+//               also MMA1's fp32 landing zone at an item's start; M buffers [256,320)
+//               [320,384); Y buffer 0 [384,512). Heads alternate Y buffers.
+// The epilogue warps copy a head's x, z and cum rows into registers first and release
+// the stage; the stage is reloaded once that release and the head's MMAs are done.
 // Barriers that a role may lag behind are kept per ring slot, so a waiter is never
 // two phases behind the barrier it polls. Every wait is bounded; a role that gives
 // up records the site, raises the CTA's abort flag and leaves its loop.
-constexpr int kScanHeadStageBytes = 32768 + 16384;  // x rows [0, 256) | prev
-constexpr int kScanSmallBytes = 5120;  // words: dt [0,256) cum [256,512) D [512,576) flags [576,580) g [640,1152)
-constexpr int kScanThreads = 576;      // warp 0 TMA, warp 1 MMA, warps 2..17 compute
+constexpr int kScanHeadStageBytes = 32768 + 16384;  // x rows [0, 256) | prev, later z
+constexpr int kScanStages = 3;                       // head stages in flight
+constexpr int kScanSmallBytes = 4224;  // words: dt [0,256) cum [256,512) flags [512,516) g [520,1032)
+constexpr int kScanThreads = 576;      // warp 0 TMA, warp 1 MMA, warps 2..9 conversion, 10..17 epilogue
 constexpr int kScanMaxHeads = 1024;    // A[0:H) staged in shared memory
-constexpr int kScanZOff = 32768 + 65536 + 2 * kScanHeadStageBytes;  // z rows of the half (16 KB)
-constexpr int kScanSmallOff = kScanZOff + 16384;
-constexpr int kScanBarOff = kScanSmallOff + 2 * kScanSmallBytes;
+// C 32 KB | B (one 128-token block) 32 KB | head stages | small stages | barriers | A
+constexpr int kScanSmallOff = 65536 + kScanStages * kScanHeadStageBytes;
+constexpr int kScanBarOff = kScanSmallOff + kScanStages * kScanSmallBytes;
 constexpr int kScanSmem = kScanBarOff + 256 + 4 * kScanMaxHeads + 1024;
 // Largest decay inside a diagonal 32x32 tile for which the factored form is used:
 // g_R reaches exp(decay) * dt, which must fit the 16-bit type with a wide margin.
@@ -697,20 +704,30 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
   using T16 = typename T16Of<BF16>::type;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
+  constexpr int NS = kScanStages;
   uint8_t* sC = smem;           // 2 x (128 rows x 128 B): dstate halves of the half's C rows
-  uint8_t* sB = smem + 32768;   // per job j: 2 x (128 rows x 128 B) at 32768 * j
-  auto hstage = [&](int s) { return smem + 98304 + s * kScanHeadStageBytes; };  // x [0,32K) prev [32K,48K)
-  uint8_t* sZ = smem + kScanZOff;
+  uint8_t* sB = smem + 32768;   // B rows of one 128-token block j: 2 x (128 rows x 128 B)
+  // head stage: x rows [0, 256) | prev, then the z rows of the half once MMA3 has read prev
+  auto hstage = [&](int s) { return smem + 65536 + s * kScanHeadStageBytes; };
   auto small = [&](int s) { return reinterpret_cast<float*>(smem + kScanSmallOff + s * kScanSmallBytes); };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kScanBarOff);
-  enum { ITEM_FULL = 0, CB_FULL, C_FREE, CB_FREE, YOFF_DONE, Z_FULL, HEAD_FULL0, HEAD_FULL1, EPI0, EPI1, MFULL0,
-         MFULL1, M2DONE0, M2DONE1, NBARS };
+  // per stage (NS each): HEAD_FULL, STAGE_FREE, STAGE_MMA, YOFF, Z_FULL
+  enum {
+    ITEM_FULL = 0, BJ_FULL, B_FREE, C_FREE, CBS_FULL, CBS_FREE, MFULL0, MFULL1, M2DONE0, M2DONE1, YFULL0, YFULL1,
+    YFREE0, YFREE1, HEAD_FULL0, STAGE_FREE0 = HEAD_FULL0 + NS, STAGE_MMA0 = STAGE_FREE0 + NS,
+    YOFF0 = STAGE_MMA0 + NS, Z_FULL0 = YOFF0 + NS, NBARS = Z_FULL0 + NS
+  };
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
   float* sA = reinterpret_cast<float*>(smem + kScanBarOff + 256);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
   const int hpg = H / G;
-  const uint32_t T_M = 256, T_YIN = 384, T_YOFF = 448;
+  // TMEM: 16-bit CB_0 [0,64) CB_1 [64,128); Y buffer 1 [128,256) (Yin, Yoff), also the
+  // fp32 landing zone of MMA1 at an item's start; M buffers [256,320) [320,384);
+  // Y buffer 0 [384,512).
+  const uint32_t T_SCR = 128, T_M = 256;
+  auto t_yin = [&](int yb) { return yb ? 128u : 384u; };
+  auto t_yoff = [&](int yb) { return yb ? 192u : 448u; };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -720,16 +737,23 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     prefetch_tmap(&tm_h);
     if (has_z) prefetch_tmap(&tm_z);
     mbar_init(bar(ITEM_FULL), 1);
-    mbar_init(bar(CB_FULL), 1);
+    mbar_init(bar(BJ_FULL), 1);
+    mbar_init(bar(B_FREE), 1);
     mbar_init(bar(C_FREE), 1);
-    mbar_init(bar(CB_FREE), 16);
-    mbar_init(bar(YOFF_DONE), 1);
-    mbar_init(bar(Z_FULL), 1);
-    for (int s = 0; s < 2; ++s) {
+    mbar_init(bar(CBS_FULL), 1);
+    mbar_init(bar(CBS_FREE), 8);
+    for (int s = 0; s < NS; ++s) {
       mbar_init(bar(HEAD_FULL0 + s), 1);
-      mbar_init(bar(EPI0 + s), 16);
-      mbar_init(bar(MFULL0 + s), 16);
+      mbar_init(bar(STAGE_FREE0 + s), 8);
+      mbar_init(bar(STAGE_MMA0 + s), 1);
+      mbar_init(bar(YOFF0 + s), 1);
+      mbar_init(bar(Z_FULL0 + s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(MFULL0 + s), 8);
       mbar_init(bar(M2DONE0 + s), 1);
+      mbar_init(bar(YFULL0 + s), 1);
+      mbar_init(bar(YFREE0 + s), 8);
     }
     *s_abort = 0;
     fence_mbar_init();
@@ -744,64 +768,90 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int I = 0, Hc = 0;
+      int I = 0, Hc = 0, zc = 0, Bc = 0, Bj = 0;  // items, heads, z loads, MMA1 jobs, B_1 landings
       bool fail = false;
+      int zh = 0, zt = 0;  // head and first token of the previous head's half
+      // z rows of head zc go into its stage's prev tile once its MMA3 has read prev.
+      auto load_z = [&]() -> bool {
+        const int s = zc % NS;
+        if (!mbar_wait(bar(YOFF0 + s), (zc / NS) & 1, kSiteScanMma2)) return false;
+        mbar_expect_tx(bar(Z_FULL0 + s), 16384u);
+        tma_load_3d(smem_u32(hstage(s) + 32768), &tm_z, 0, zh, zt, bar(Z_FULL0 + s));
+        ++zc;
+        return true;
+      };
       for (int it = blockIdx.x; it < n_items && !fail && !*s_abort; it += gridDim.x) {
         ScanItem si;
         ChunkInfo ci;
         if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
         const int t0 = (int)ci.tok0, S = 128 * (si.m + 1);
-        if (I > 0) {
-          // B tiles free once the previous item's MMA1 completed; C once its last MMA3 did.
-          if (!mbar_wait(bar(CB_FULL), (I - 1) & 1, kSiteScanMma1) ||
-              !mbar_wait(bar(C_FREE), (I - 1) & 1, kSiteScanMma1)) {
-            fail = true;
-            break;
-          }
+        // C free once the previous item's last MMA3 completed; the B buffer once the
+        // previous MMA1 did.
+        if ((I > 0 && !mbar_wait(bar(C_FREE), (I - 1) & 1, kSiteScanMma1)) ||
+            (Bc > 0 && !mbar_wait(bar(B_FREE), (Bc - 1) & 1, kSiteScanMma1))) {
+          fail = true;
+          break;
         }
-        mbar_expect_tx(bar(ITEM_FULL), 32768u + (uint32_t)S * 256u);
+        mbar_expect_tx(bar(ITEM_FULL), 65536u);
         tma_load_3d(smem_u32(sC), &tm_c, 0, si.g, t0 + 128 * si.m, bar(ITEM_FULL));
         tma_load_3d(smem_u32(sC + 16384), &tm_c, 64, si.g, t0 + 128 * si.m, bar(ITEM_FULL));
-        for (int j = 0; j <= si.m; ++j) {
-          tma_load_3d(smem_u32(sB + 32768 * j), &tm_b, 0, si.g, t0 + 128 * j, bar(ITEM_FULL));
-          tma_load_3d(smem_u32(sB + 32768 * j + 16384), &tm_b, 64, si.g, t0 + 128 * j, bar(ITEM_FULL));
-        }
+        tma_load_3d(smem_u32(sB), &tm_b, 0, si.g, t0, bar(ITEM_FULL));
+        tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, si.g, t0, bar(ITEM_FULL));
+        ++Bc;
         for (int i = 0; i < si.nh; ++i) {
-          const int h = si.h0 + i, hs = Hc & 1;
-          if (Hc >= 2 && !mbar_wait(bar(EPI0 + hs), ((Hc - 2) >> 1) & 1, kSiteScanEpi)) {
+          const int h = si.h0 + i, hs = Hc % NS;
+          // The stage is free once the epilogue of the head NS back copied what it
+          // needs and that head's MMAs completed.
+          if (Hc >= NS && (!mbar_wait(bar(STAGE_FREE0 + hs), ((Hc - NS) / NS) & 1, kSiteScanEpi) ||
+                           !mbar_wait(bar(STAGE_MMA0 + hs), ((Hc - NS) / NS) & 1, kSiteScanMma2))) {
             fail = true;
             break;
           }
           uint8_t* st = hstage(hs);
           float* sm = small(hs);
           const uint32_t fb = bar(HEAD_FULL0 + hs);
-          mbar_expect_tx(fb, (uint32_t)S * 128u + 16384u + 2048u + (D ? 256u : 0u));
+          mbar_expect_tx(fb, (uint32_t)S * 128u + 16384u + 2048u);
           for (int j = 0; j <= si.m; ++j) tma_load_3d(smem_u32(st + 16384 * j), &tm_x, 0, h, t0 + 128 * j, fb);
           tma_load_3d(smem_u32(st + 32768), &tm_h, 0, 0, si.k * H + h, fb);
           bulk_load(smem_u32(sm), dt + ((long long)si.k * H + h) * 256, 1024u, fb);
           bulk_load(smem_u32(sm + 256), cum + ((long long)si.k * H + h) * 256, 1024u, fb);
-          if (D) bulk_load(smem_u32(sm + 512), D + h * 64, 256u, fb);
-          if (has_z) {
-            // The z tile is single-buffered: free once the previous head's epilogue is done.
-            if (Hc >= 1 && !mbar_wait(bar(EPI0 + ((Hc - 1) & 1)), ((Hc - 1) >> 1) & 1, kSiteScanEpi)) {
+          // z of the previous head first: MMA1 of this item may wait for that head's
+          // epilogue, which needs its z, before B's block 1 can be loaded.
+          if (has_z && Hc >= 1 && !load_z()) {
+            fail = true;
+            break;
+          }
+          if (i == 0 && si.m == 1) {
+            // B rows of block 1 once MMA1 of block 0 has read the buffer
+            if (!mbar_wait(bar(B_FREE), (Bc - 1) & 1, kSiteScanMma1)) {
               fail = true;
               break;
             }
-            mbar_expect_tx(bar(Z_FULL), 16384u);
-            tma_load_3d(smem_u32(sZ), &tm_z, 0, h, t0 + 128 * si.m, bar(Z_FULL));
+            mbar_expect_tx(bar(BJ_FULL), 32768u);
+            tma_load_3d(smem_u32(sB), &tm_b, 0, si.g, t0 + 128, bar(BJ_FULL));
+            tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, si.g, t0 + 128, bar(BJ_FULL));
+            ++Bc;
+            ++Bj;
           }
+          zh = h;
+          zt = t0 + 128 * si.m;
           ++Hc;
         }
         ++I;
       }
+      if (!fail && !*s_abort && has_z && Hc > 0 && !load_z()) fail = true;
       if (fail) *s_abort = 1;
       // No copy may still be in flight when the CTA exits.
       if (I > 0) mbar_wait(bar(ITEM_FULL), (I - 1) & 1, kSiteScanTma);
-      for (int d = 1; d <= 2 && d <= Hc; ++d) {
+      if (Bj > 0) mbar_wait(bar(BJ_FULL), (Bj - 1) & 1, kSiteScanTma);
+      for (int d = 1; d <= NS && d <= Hc; ++d) {
         const int hc = Hc - d;
-        mbar_wait(bar(HEAD_FULL0 + (hc & 1)), (hc >> 1) & 1, kSiteScanTma);
+        mbar_wait(bar(HEAD_FULL0 + hc % NS), (hc / NS) & 1, kSiteScanTma);
       }
-      if (has_z && Hc > 0) mbar_wait(bar(Z_FULL), (Hc - 1) & 1, kSiteScanTma);
+      for (int d = 1; d <= NS && d <= zc; ++d) {
+        const int hc = zc - d;
+        mbar_wait(bar(Z_FULL0 + hc % NS), (hc / NS) & 1, kSiteScanTma);
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -810,34 +860,51 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       const uint32_t id_cb = idesc_f16(128, 128, BF16, false, false);
       const uint32_t id_off = idesc_f16(128, 64, BF16, false, /*b_mn=*/true);
       const uint32_t id_in = idesc_f16(128, 64, BF16, false, true);
-      int I = 0, Hc = 0, Jc = 0;
+      int I = 0, Hc = 0, Jc = 0, Sc = 0, Bj = 0;  // items, heads, M-buffer jobs, CB landings, B_1 landings
       bool fail = false;
       int last_bar = -1, last_par = 0;
       for (int it = blockIdx.x; it < n_items && !fail && !*s_abort; it += gridDim.x) {
         ScanItem si;
         ChunkInfo ci;
         if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
-        if (!mbar_wait(bar(ITEM_FULL), I & 1, kSiteScanTma) ||
-            (I > 0 && !mbar_wait(bar(CB_FREE), (I - 1) & 1, kSiteScanConv))) {
+        if (!mbar_wait(bar(ITEM_FULL), I & 1, kSiteScanTma)) {
           fail = true;
           break;
         }
-        tc_fence_after();
         const uint32_t c0 = smem_u32(sC);
-        for (int j = 0; j <= si.m; ++j) {
-          const uint32_t b0 = smem_u32(sB + 32768 * j);
+        for (int j = 0; j <= si.m && !fail; ++j) {
+          // The landing zone is Y buffer 1: free once the epilogue of the last head
+          // that used it loaded it, and once the previous CB_j landing was converted.
+          const int y1 = Hc / 2;  // heads so far that used Y buffer 1 (odd head counters)
+          if ((y1 > 0 && !mbar_wait(bar(YFREE1), (y1 - 1) & 1, kSiteScanEpi)) ||
+              (Sc > 0 && !mbar_wait(bar(CBS_FREE), (Sc - 1) & 1, kSiteScanConv)) ||
+              (j == 1 && !mbar_wait(bar(BJ_FULL), Bj & 1, kSiteScanTma))) {
+            fail = true;
+            break;
+          }
+          if (j == 1) ++Bj;
+          tc_fence_after();
+          const uint32_t b0 = smem_u32(sB);
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
-            umma_f16(tmem + 128 * j, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
+            umma_f16(tmem + T_SCR, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
                      sdesc_sw128(b0 + hf * 16384 + kk, 16, 1024), id_cb, ks > 0 ? 1u : 0u);
           }
+          umma_commit(bar(CBS_FULL));
+          umma_commit(bar(B_FREE));
+          ++Sc;
         }
-        umma_commit(bar(CB_FULL));
+        if (fail) break;
+        // Head MMAs may write Y buffer 1 only after the last landing was converted.
+        if (!mbar_wait(bar(CBS_FREE), (Sc - 1) & 1, kSiteScanConv)) {
+          fail = true;
+          break;
+        }
         for (int i = 0; i < si.nh && !fail; ++i) {
-          const int hs = Hc & 1;
-          if (!mbar_wait(bar(HEAD_FULL0 + hs), (Hc >> 1) & 1, kSiteScanTma) ||
-              (Hc >= 1 && !mbar_wait(bar(EPI0 + ((Hc - 1) & 1)), ((Hc - 1) >> 1) & 1, kSiteScanEpi))) {
+          const int hs = Hc % NS, yb = Hc & 1;
+          if (!mbar_wait(bar(HEAD_FULL0 + hs), (Hc / NS) & 1, kSiteScanTma) ||
+              (Hc >= 2 && !mbar_wait(bar(YFREE0 + yb), ((Hc - 2) >> 1) & 1, kSiteScanEpi))) {
             fail = true;
             break;
           }
@@ -846,10 +913,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
-            umma_f16(tmem + T_YOFF, sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
+            umma_f16(tmem + t_yoff(yb), sdesc_sw128(c0 + hf * 16384 + kk, 16, 1024),
                      sdesc_sw128(h0 + ks * 2048, 16, 1024), id_off, ks > 0 ? 1u : 0u);
           }
-          umma_commit(bar(YOFF_DONE));
+          umma_commit(bar(YOFF0 + hs));
           if (i == si.nh - 1) umma_commit(bar(C_FREE));
           for (int j = 0; j <= si.m; ++j) {
             const int mb = Jc & 1;
@@ -860,13 +927,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
             tc_fence_after();
 #pragma unroll
             for (int ks = 0; ks < 8; ++ks)
-              umma_f16_ts(tmem + T_YIN, tmem + T_M + 64 * mb + 8 * ks,
+              umma_f16_ts(tmem + t_yin(yb), tmem + T_M + 64 * mb + 8 * ks,
                           sdesc_sw128(x0 + 16384 * j + ks * 2048, 16, 1024), id_in, (j > 0 || ks > 0) ? 1u : 0u);
             umma_commit(bar(M2DONE0 + mb));
-            last_bar = M2DONE0 + mb;
-            last_par = (Jc >> 1) & 1;
             ++Jc;
           }
+          if (fail) break;
+          umma_commit(bar(YFULL0 + yb));
+          umma_commit(bar(STAGE_MMA0 + hs));
+          last_bar = STAGE_MMA0 + hs;
+          last_par = (Hc / NS) & 1;
           ++Hc;
         }
         ++I;
@@ -874,19 +944,18 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       if (fail) *s_abort = 1;
       // All MMAs must be complete before TMEM is released.
       if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, kSiteScanMma2);
+      else if (Sc > 0) mbar_wait(bar(CBS_FULL), (Sc - 1) & 1, kSiteScanMma1);
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------ compute warps
-    const int ctid = tid - 64;
-    const int quad = warp & 3, cg = (warp - 2) >> 2;
+  } else if (warp < 10) {
+    // ------------------------------------------------------------ conversion warps (2..9)
+    // warp (quad, cc): rows of TMEM quadrant quad, column blocks cg = 2 cc, 2 cc + 1 (32 each)
+    const int ct = tid - 64;  // 0..255
+    const int quad = warp & 3, cc = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const uint32_t tlane = (uint32_t)(quad * 32) << 16;
     const float fac_max = scan_fac_max_decay(BF16);
-    int I = 0, Hc = 0, Jc = 0;
-    // Warps wait on the mbarriers independently; a warp that gives up (wfail) stops
-    // releasing work, and all warps leave together at the next named barrier, which
-    // ANDs the flags (fail).
+    int I = 0, Hc = 0, Jc = 0, Sc = 0;
     bool fail = false, wfail = false;
     auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
       if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
@@ -897,57 +966,61 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       ChunkInfo ci;
       if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
       const int m = si.m, l = 128 * m + r, R = 4 * m + quad, S = 128 * (m + 1);
-      warp_wait(bar(CB_FULL), I & 1, kSiteScanMma1);
-      tc_fence_after();
-      if (!named_bar_and(1, 512, !wfail && !*s_abort)) { fail = true; break; }
-      // ---- CB_j (fp32) -> 16-bit, into the first 64 columns of CB_j's own region ----
-      for (int j = 0; j <= m; ++j) {
-        uint32_t hv[16];
-        {
-          uint32_t v[32];
-          tmem_ld32(tmem + tlane + 128 * j + 32 * cg, v);
+      // ---- CB_j (fp32, landing zone) -> 16-bit CB_j at [64 j, 64 j + 64) ----
+      for (int j = 0; j <= m; ++j, ++Sc) {
+        warp_wait(bar(CBS_FULL), Sc & 1, kSiteScanMma1);
+        tc_fence_after();
+        if (wfail) continue;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int cg = 2 * cc + t;
+          uint32_t v[32], hv[16];
+          tmem_ld32(tmem + tlane + T_SCR + 32 * cg, v);
           tmem_wait_ld();
 #pragma unroll
           for (int q = 0; q < 16; ++q) hv[q] = pack2<T16>(__uint_as_float(v[2 * q]), __uint_as_float(v[2 * q + 1]));
+          tmem_st16(tmem + tlane + 64 * j + 16 * cg, hv);
         }
-        tc_fence_before();
-        named_bar_sync(1, 512);  // every warp has read its fp32 block before any is overwritten
-        tc_fence_after();
-        tmem_st16(tmem + tlane + 128 * j + 16 * cg, hv);
         tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(CBS_FREE));
       }
       for (int i = 0; i < si.nh; ++i) {
-        const int h = si.h0 + i, hs = Hc & 1;
+        const int h = si.h0 + i, hs = Hc % NS;
         uint8_t* sX = hstage(hs);
         float* sm = small(hs);
         const float* sDt = sm;
         const float* sCum = sm + 256;
-        int* sFlag = reinterpret_cast<int*>(sm + 576);
-        uint32_t* sG = reinterpret_cast<uint32_t*>(sm + 640);  // [row block of the half][pair of s]
-        warp_wait(bar(HEAD_FULL0 + hs), (Hc >> 1) & 1, kSiteScanTma);
-        // cum non-increasing (A <= 0 and dt >= 0) => min(cum_l - cum_s, 0) = cum_l - cum_s
+        int* sFlag = reinterpret_cast<int*>(sm + 512);
+        uint32_t* sG = reinterpret_cast<uint32_t*>(sm + 520);  // [row block of the half][pair of s]
+        warp_wait(bar(HEAD_FULL0 + hs), (Hc / NS) & 1, kSiteScanTma);
         const bool mono = dt_nonneg && (sA[h] <= 0.f);
-        {
-          const int rb = 4 * m + (ctid >> 7), s2 = 2 * (ctid & 127);
-          uint32_t gv = 0u;
-          if (mono && s2 < 32 * (rb + 1)) {
-            const float cr = sCum[32 * rb];
-            const float g0 = s2 < ci.lim ? __expf(cr - sCum[s2]) * sDt[s2] : 0.f;
-            const float g1 = s2 + 1 < ci.lim ? __expf(cr - sCum[s2 + 1]) * sDt[s2 + 1] : 0.f;
-            gv = pack2<T16>(g0, g1);
+        if (!wfail) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int idx = ct + 256 * e;
+            const int rb = 4 * m + (idx >> 7), s2 = 2 * (idx & 127);
+            uint32_t gv = 0u;
+            if (mono && s2 < 32 * (rb + 1)) {
+              const float cr = sCum[32 * rb];
+              const float g0 = s2 < ci.lim ? __expf(cr - sCum[s2]) * sDt[s2] : 0.f;
+              const float g1 = s2 + 1 < ci.lim ? __expf(cr - sCum[s2 + 1]) * sDt[s2 + 1] : 0.f;
+              gv = pack2<T16>(g0, g1);
+            }
+            sG[idx] = gv;
           }
-          sG[ctid] = gv;
-          if (ctid < 4) {
-            const int rr = 4 * m + ctid;
-            sFlag[ctid] = mono && (sCum[32 * rr] - sCum[32 * rr + 31] <= fac_max);
+          if (ct < 4) {
+            const int rr = 4 * m + ct;
+            sFlag[ct] = mono && (sCum[32 * rr] - sCum[32 * rr + 31] <= fac_max);
+          }
+          if (S > ci.lim) {
+            // x rows past `lim` -> exact zeros, so they cannot leak into Yin
+            for (int q = ct; q < S * 8; q += 256)
+              if ((q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
           }
         }
-        if (S > ci.lim) {
-          // x rows past `lim` -> exact zeros, so they cannot leak into Yin
-          for (int q = ctid; q < S * 8; q += 512)
-            if ((q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
-        }
-        if (!named_bar_and(1, 512, !wfail && !*s_abort)) { fail = true; break; }  // publishes g / flags
+        if (!named_bar_and(1, 256, !wfail && !*s_abort)) { fail = true; break; }  // publishes g / flags
         const float cl = sCum[l];
         const bool fR = sFlag[quad] != 0;
         for (int j = 0; j <= m; ++j) {
@@ -960,53 +1033,56 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
             ++Jc;
             continue;
           }
-          // ---- 16-bit CB_j block cg, rows of this quadrant -> M'_j (TMEM) ----
-          const int s0 = 128 * j + cg * 32;
-          uint32_t pk[16];
-          if (s0 > 32 * R + 31) {
 #pragma unroll
-            for (int q = 0; q < 16; ++q) pk[q] = 0u;
-          } else {
-            // g pairs before the TMEM load: the wait below is a compiler memory barrier.
-            uint4 g4v[4];
-            if (fR) {
-              const uint4* gp = reinterpret_cast<const uint4*>(sG + quad * 128 + (s0 >> 1));
+          for (int t = 0; t < 2; ++t) {
+            const int cg = 2 * cc + t;
+            // ---- 16-bit CB_j block cg, rows of this quadrant -> M'_j (TMEM) ----
+            const int s0 = 128 * j + cg * 32;
+            uint32_t pk[16];
+            if (s0 > 32 * R + 31) {
 #pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4) g4v[q4] = gp[q4];
-            }
-            uint32_t cb[16];
-            tmem_ld16(tmem + tlane + 128 * j + 16 * cg, cb);
-            tmem_wait_ld();
-            if (fR) {
+              for (int q = 0; q < 16; ++q) pk[q] = 0u;
+            } else {
+              uint4 g4v[4];
+              if (fR) {
+                const uint4* gp = reinterpret_cast<const uint4*>(sG + quad * 128 + (s0 >> 1));
 #pragma unroll
-              for (int q4 = 0; q4 < 4; ++q4) {
-                const uint4 g4 = g4v[q4];
-                pk[4 * q4] = mul2<T16>(cb[4 * q4], g4.x);
-                pk[4 * q4 + 1] = mul2<T16>(cb[4 * q4 + 1], g4.y);
-                pk[4 * q4 + 2] = mul2<T16>(cb[4 * q4 + 2], g4.z);
-                pk[4 * q4 + 3] = mul2<T16>(cb[4 * q4 + 3], g4.w);
+                for (int q4 = 0; q4 < 4; ++q4) g4v[q4] = gp[q4];
               }
-              if (s0 == 32 * R) {
-                // diagonal tile: column c of the tile is kept when c <= lane
+              uint32_t cb[16];
+              tmem_ld16(tmem + tlane + 64 * j + 16 * cg, cb);
+              tmem_wait_ld();
+              if (fR) {
+#pragma unroll
+                for (int q4 = 0; q4 < 4; ++q4) {
+                  const uint4 g4 = g4v[q4];
+                  pk[4 * q4] = mul2<T16>(cb[4 * q4], g4.x);
+                  pk[4 * q4 + 1] = mul2<T16>(cb[4 * q4 + 1], g4.y);
+                  pk[4 * q4 + 2] = mul2<T16>(cb[4 * q4 + 2], g4.z);
+                  pk[4 * q4 + 3] = mul2<T16>(cb[4 * q4 + 3], g4.w);
+                }
+                if (s0 == 32 * R) {
+                  // diagonal tile: column c of the tile is kept when c <= lane
+#pragma unroll
+                  for (int q = 0; q < 16; ++q) {
+                    const uint32_t keep = (2 * q + 1 <= lane) ? 0xffffffffu : ((2 * q <= lane) ? 0x0000ffffu : 0u);
+                    pk[q] &= keep;
+                  }
+                }
+              } else {
 #pragma unroll
                 for (int q = 0; q < 16; ++q) {
-                  const uint32_t keep = (2 * q + 1 <= lane) ? 0xffffffffu : ((2 * q <= lane) ? 0x0000ffffu : 0u);
-                  pk[q] &= keep;
+                  const float2 c2 = unpack2<T16>(cb[q]);
+                  const int sa = s0 + 2 * q, sb2 = sa + 1;
+                  float x0 = 0.f, x1 = 0.f;
+                  if (sa <= l && sa < ci.lim) x0 = c2.x * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
+                  if (sb2 <= l && sb2 < ci.lim) x1 = c2.y * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
+                  pk[q] = pack2<T16>(x0, x1);
                 }
               }
-            } else {
-#pragma unroll
-              for (int q = 0; q < 16; ++q) {
-                const float2 c2 = unpack2<T16>(cb[q]);
-                const int sa = s0 + 2 * q, sb2 = sa + 1;
-                float x0 = 0.f, x1 = 0.f;
-                if (sa <= l && sa < ci.lim) x0 = c2.x * __expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
-                if (sb2 <= l && sb2 < ci.lim) x1 = c2.y * __expf(fminf(cl - sCum[sb2], 0.f)) * sDt[sb2];
-                pk[q] = pack2<T16>(x0, x1);
-              }
             }
+            tmem_st16(tmem + tlane + T_M + 64 * mb + 16 * cg, pk);
           }
-          tmem_st16(tmem + tlane + T_M + 64 * mb + 16 * cg, pk);
           tmem_wait_st();
           fence_proxy_async_smem();  // sX zero-fill (first job) visible to MMA2
           tc_fence_before();
@@ -1014,71 +1090,96 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           if (lane == 0) mbar_arrive(bar(MFULL0 + mb));
           ++Jc;
         }
-        if (i == si.nh - 1 && !wfail) {
+        ++Hc;
+      }
+      ++I;
+    }
+    if (fail || wfail) *s_abort = 1;
+  } else {
+    // ------------------------------------------------------------ epilogue warps (10..17)
+    // warp (quad, ce): rows of TMEM quadrant quad, output columns [32 ce, 32 ce + 32).
+    // y = (exp(cum_l) Yoff + rowf_l Yin + D x) * silu(z)
+    const int quad = warp & 3, ce = (warp - 10) >> 2;
+    const int r = quad * 32 + lane;
+    const uint32_t tlane = (uint32_t)(quad * 32) << 16;
+    const float fac_max = scan_fac_max_decay(BF16);
+    int Hc = 0;
+    bool fail = false, wfail = false;
+    auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
+      if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
+      return !wfail;
+    };
+    for (int it = blockIdx.x; it < n_items && !fail; it += gridDim.x) {
+      ScanItem si;
+      ChunkInfo ci;
+      if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
+      const int m = si.m, l = 128 * m + r, R = 4 * m + quad;
+      for (int i = 0; i < si.nh; ++i, ++Hc) {
+        const int h = si.h0 + i, hs = Hc % NS, yb = Hc & 1;
+        const uint8_t* sX = hstage(hs);
+        const float* sCum = small(hs) + 256;
+        // Copy what this epilogue reads from the head stage, then release the stage.
+        warp_wait(bar(HEAD_FULL0 + hs), (Hc / NS) & 1, kSiteScanTma);
+        if (has_z) warp_wait(bar(Z_FULL0 + hs), (Hc / NS) & 1, kSiteScanTma);
+        uint4 xv[4], zv[4];
+        float cl = 0.f, rowf = 1.f;
+        if (!wfail) {
+          const bool mono = dt_nonneg && (sA[h] <= 0.f);
+          cl = sCum[l];
+          const bool fR = mono && (sCum[32 * R] - sCum[32 * R + 31] <= fac_max);
+          rowf = fR ? __expf(cl - sCum[32 * R]) : 1.f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            xv[q] = *reinterpret_cast<const uint4*>(sX + 16384 * m + sw128_off(r, 4 * ce + q));
+            zv[q] = has_z ? *reinterpret_cast<const uint4*>(sX + 32768 + sw128_off(r, 4 * ce + q))
+                          : make_uint4(0u, 0u, 0u, 0u);
+          }
           __syncwarp();
-          if (lane == 0) mbar_arrive(bar(CB_FREE));  // this item's CB is no longer read
+          if (lane == 0) mbar_arrive(bar(STAGE_FREE0 + hs));
         }
-        // ---- epilogue: y = (exp(cum_l) Yoff + rowf_l Yin + D x) * silu(z), columns [16cg, 16cg+16) ----
-        // The Yoff and D x parts need only MMA3 (issued first for the head), so they
-        // run before the wait for the last MMA2.
-        const bool valid = l < ci.lim;
-        const long long yrow = ((ci.tok0 + l) * H + h) * 64 + cg * 16;
-        const float rowf = fR ? __expf(cl - sCum[32 * R]) : 1.f;
-        warp_wait(bar(YOFF_DONE), Hc & 1, kSiteScanMma2);
+        warp_wait(bar(YFULL0 + yb), (Hc >> 1) & 1, kSiteScanMma2);
         tc_fence_after();
-        if (wfail) {
-          ++Hc;
-          continue;
-        }
-        float o[16];
-        {
-          uint32_t ro[16];
-          tmem_ld16(tmem + tlane + T_YOFF + cg * 16, ro);
+        if (wfail) continue;
+        const bool valid = l < ci.lim;
+        const long long yrow = ((ci.tok0 + l) * H + h) * 64 + ce * 32;
+        const float el = __expf(cl);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t ri[16], ro[16];
+          tmem_ld16(tmem + tlane + t_yin(yb) + 32 * ce + 16 * hf, ri);
+          tmem_ld16(tmem + tlane + t_yoff(yb) + 32 * ce + 16 * hf, ro);
           tmem_wait_ld();
-          const float el = __expf(cl);
+          if (hf == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(YFREE0 + yb));  // Y may be overwritten by head Hc + 2
+          }
+          if (!valid) continue;
+          float o[16];
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) o[jj] = el * __uint_as_float(ro[jj]);
-        }
-        if (D) {
-          const float4* sD4 = reinterpret_cast<const float4*>(sm + 512 + cg * 16);
+          for (int jj = 0; jj < 16; ++jj)
+            o[jj] = fmaf(el, __uint_as_float(ro[jj]), rowf * __uint_as_float(ri[jj]));
+          if (D) {
+            const float4* d4 = reinterpret_cast<const float4*>(D + h * 64 + ce * 32 + 16 * hf);
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const uint4 xv = *reinterpret_cast<const uint4*>(sX + 16384 * m + sw128_off(r, cg * 2 + q));
-            const float4 da = sD4[2 * q], db = sD4[2 * q + 1];
-            const float dq[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
-            const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
+            for (int q = 0; q < 2; ++q) {
+              const uint4 xq = xv[2 * hf + q];
+              const float4 da = __ldg(d4 + 2 * q), db = __ldg(d4 + 2 * q + 1);
+              const float dq[8] = {da.x, da.y, da.z, da.w, db.x, db.y, db.z, db.w};
+              const uint32_t w4[4] = {xq.x, xq.y, xq.z, xq.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = unpack2<T16>(w4[e]);
-              o[q * 8 + 2 * e] = fmaf(dq[2 * e], f.x, o[q * 8 + 2 * e]);
-              o[q * 8 + 2 * e + 1] = fmaf(dq[2 * e + 1], f.y, o[q * 8 + 2 * e + 1]);
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = unpack2<T16>(w4[e]);
+                o[q * 8 + 2 * e] = fmaf(dq[2 * e], f.x, o[q * 8 + 2 * e]);
+                o[q * 8 + 2 * e + 1] = fmaf(dq[2 * e + 1], f.y, o[q * 8 + 2 * e + 1]);
+              }
             }
           }
-        }
-        uint4 zv0 = make_uint4(0u, 0u, 0u, 0u), zv1 = zv0;
-        if (has_z && warp_wait(bar(Z_FULL), Hc & 1, kSiteScanTma)) {
-          zv0 = *reinterpret_cast<const uint4*>(sZ + sw128_off(r, cg * 2));
-          zv1 = *reinterpret_cast<const uint4*>(sZ + sw128_off(r, cg * 2 + 1));
-        }
-        const int jl = Jc - 1;
-        warp_wait(bar(M2DONE0 + (jl & 1)), (jl >> 1) & 1, kSiteScanMma2);
-        tc_fence_after();
-        if (wfail) {
-          ++Hc;
-          continue;
-        }
-        uint32_t ri[16];
-        tmem_ld16(tmem + tlane + T_YIN + cg * 16, ri);
-        tmem_wait_ld();
-        tc_fence_before();
-        if (valid) {
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) o[jj] = fmaf(rowf, __uint_as_float(ri[jj]), o[jj]);
           if (has_z) {
 #pragma unroll
             for (int q = 0; q < 2; ++q) {
-              const uint4 zv = q ? zv1 : zv0;
-              const uint32_t w4[4] = {zv.x, zv.y, zv.z, zv.w};
+              const uint4 zq = zv[2 * hf + q];
+              const uint32_t w4[4] = {zq.x, zq.y, zq.z, zq.w};
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 const float2 f = unpack2<T16>(w4[e]);
@@ -1090,24 +1191,18 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
             }
           }
           if constexpr (sizeof(YT) == 4) {
-            float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow);
+            float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow + 16 * hf);
 #pragma unroll
             for (int q = 0; q < 4; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
           } else {
-            uint4* yp = reinterpret_cast<uint4*>(y + yrow);
+            uint4* yp = reinterpret_cast<uint4*>(y + yrow + 16 * hf);
 #pragma unroll
             for (int q = 0; q < 2; ++q)
               yp[q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
                                  pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
           }
         }
-        // Y (TMEM), the head stage (x, D, dt, cum, g) and the z tile are free once
-        // every compute warp is here.
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(EPI0 + hs));
-        ++Hc;
       }
-      ++I;
     }
     if (fail || wfail) *s_abort = 1;
   }
