@@ -510,13 +510,36 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
 #pragma unroll
       for (int p = 0; p < 64; ++p) prev[p] = 0.f;
     }
-    // prev16 row n of a chunk: 64 contiguous p values, eight 16-byte stores.
-    auto store_prev16 = [&](T16* dst) {
-      uint4* d4 = reinterpret_cast<uint4*>(dst);
+    // prev16 of a chunk, row n = 64 contiguous p values (128 bytes). The 16-byte pieces
+    // of eight neighbouring rows are transposed across each group of 8 lanes, so that
+    // every store instruction writes four whole 128-byte rows instead of 32 scattered
+    // 16-byte pieces.
+    const int li = lane & 7, rbase = quad * 32 + (lane & ~7);
+    auto store_prev16 = [&](T16* chunk_base) {
+      uint4 d[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q)
-        d4[q] = make_uint4(pack2<T16>(prev[8 * q], prev[8 * q + 1]), pack2<T16>(prev[8 * q + 2], prev[8 * q + 3]),
-                           pack2<T16>(prev[8 * q + 4], prev[8 * q + 5]), pack2<T16>(prev[8 * q + 6], prev[8 * q + 7]));
+        d[q] = make_uint4(pack2<T16>(prev[8 * q], prev[8 * q + 1]), pack2<T16>(prev[8 * q + 2], prev[8 * q + 3]),
+                          pack2<T16>(prev[8 * q + 4], prev[8 * q + 5]), pack2<T16>(prev[8 * q + 6], prev[8 * q + 7]));
+#pragma unroll
+      for (int msk = 4; msk >= 1; msk >>= 1) {
+        const bool upper = (li & msk) != 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (q & msk) continue;
+          uint4 snd = upper ? d[q] : d[q | msk];
+          uint4 rcv;
+          rcv.x = __shfl_xor_sync(0xffffffffu, snd.x, msk);
+          rcv.y = __shfl_xor_sync(0xffffffffu, snd.y, msk);
+          rcv.z = __shfl_xor_sync(0xffffffffu, snd.z, msk);
+          rcv.w = __shfl_xor_sync(0xffffffffu, snd.w, msk);
+          if (upper) d[q] = rcv; else d[q | msk] = rcv;
+        }
+      }
+      // lane (group, li) now holds piece li of rows rbase + 0..7
+      uint4* d4 = reinterpret_cast<uint4*>(chunk_base) + rbase * 8 + li;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d4[8 * j] = d[j];
     };
     // Warps wait independently; a warp that gives up stops releasing work and the
     // group leaves at its next barrier, which ANDs the flags.
@@ -543,7 +566,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(W_FREE + j % NW));  // w / exp(cum_last) of chunk j no longer read
       if (j + 1 < count) {
-        store_prev16(prev16 + ((long long)(first + j + 1) * H + h) * PN + n * 64);
+        store_prev16(prev16 + ((long long)(first + j + 1) * H + h) * PN);
       } else {
         float* dst = h_last + ((long long)row * H + h) * PN + n;
 #pragma unroll
@@ -558,7 +581,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
 #pragma unroll
         for (int p = 0; p < 64; ++p) dst[p * 128] = prev[p];
       } else {
-        store_prev16(prev16 + ((long long)first * H + h) * PN + n * 64);
+        store_prev16(prev16 + ((long long)first * H + h) * PN);
       }
     }
     int r = 0;
@@ -997,30 +1020,30 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         warp_wait(bar(HEAD_FULL0 + hs), (Hc / NS) & 1, kSiteScanTma);
         const bool mono = dt_nonneg && (sA[h] <= 0.f);
         if (!wfail) {
+          // The two warps of a quadrant compute the g pairs of their own row block R
+          // and meet at a barrier of their own, so the quadrants run decoupled.
+          const int tq = cc * 32 + lane;
+          const float cr = sCum[32 * R];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int idx = ct + 256 * e;
-            const int rb = 4 * m + (idx >> 7), s2 = 2 * (idx & 127);
+            const int pidx = tq + 64 * e, s2 = 2 * pidx;
             uint32_t gv = 0u;
-            if (mono && s2 < 32 * (rb + 1)) {
-              const float cr = sCum[32 * rb];
+            if (mono && s2 < 32 * (R + 1)) {
               const float g0 = s2 < ci.lim ? __expf(cr - sCum[s2]) * sDt[s2] : 0.f;
               const float g1 = s2 + 1 < ci.lim ? __expf(cr - sCum[s2 + 1]) * sDt[s2 + 1] : 0.f;
               gv = pack2<T16>(g0, g1);
             }
-            sG[idx] = gv;
+            sG[quad * 128 + pidx] = gv;
           }
-          if (ct < 4) {
-            const int rr = 4 * m + ct;
-            sFlag[ct] = mono && (sCum[32 * rr] - sCum[32 * rr + 31] <= fac_max);
-          }
+          if (tq == 0) sFlag[quad] = mono && (cr - sCum[32 * R + 31] <= fac_max);
           if (S > ci.lim) {
             // x rows past `lim` -> exact zeros, so they cannot leak into Yin
             for (int q = ct; q < S * 8; q += 256)
               if ((q >> 3) >= ci.lim) *reinterpret_cast<uint4*>(sX + q * 16) = make_uint4(0u, 0u, 0u, 0u);
           }
         }
-        if (!named_bar_and(1, 256, !wfail && !*s_abort)) { fail = true; break; }  // publishes g / flags
+        // publishes this quadrant's g pairs and flag
+        if (!named_bar_and(2 + quad, 64, !wfail && !*s_abort)) { fail = true; break; }
         const float cl = sCum[l];
         const bool fR = sFlag[quad] != 0;
         for (int j = 0; j <= m; ++j) {
