@@ -83,6 +83,29 @@ __device__ __forceinline__ uint4 scale8_packed(uint4 a, uint32_t w2) {
   return make_uint4(mul2<T16>(a.x, w2), mul2<T16>(a.y, w2), mul2<T16>(a.z, w2), mul2<T16>(a.w, w2));
 }
 
+// Transpose NP x NP 16-byte pieces across each group of NP lanes: lane li of a
+// group enters with pieces 0..NP-1 of "its" row and leaves with piece li of the
+// group's rows 0..NP-1. Rows held one per lane become whole-row stores: store j
+// of the group then writes row j contiguously.
+template <int NP>
+__device__ __forceinline__ void lane_transpose(uint4 (&d)[NP], int li) {
+#pragma unroll
+  for (int msk = NP / 2; msk >= 1; msk >>= 1) {
+    const bool upper = (li & msk) != 0;
+#pragma unroll
+    for (int q = 0; q < NP; ++q) {
+      if (q & msk) continue;
+      const uint4 snd = upper ? d[q] : d[q | msk];
+      uint4 rcv;
+      rcv.x = __shfl_xor_sync(0xffffffffu, snd.x, msk);
+      rcv.y = __shfl_xor_sync(0xffffffffu, snd.y, msk);
+      rcv.z = __shfl_xor_sync(0xffffffffu, snd.z, msk);
+      rcv.w = __shfl_xor_sync(0xffffffffu, snd.w, msk);
+      if (upper) d[q] = rcv; else d[q | msk] = rcv;
+    }
+  }
+}
+
 // ===========================================================================
 // chunk_state (+ chunk_cumsum)
 // ===========================================================================
@@ -510,10 +533,9 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
 #pragma unroll
       for (int p = 0; p < 64; ++p) prev[p] = 0.f;
     }
-    // prev16 of a chunk, row n = 64 contiguous p values (128 bytes). The 16-byte pieces
-    // of eight neighbouring rows are transposed across each group of 8 lanes, so that
-    // every store instruction writes four whole 128-byte rows instead of 32 scattered
-    // 16-byte pieces.
+    // prev16 of a chunk, row n = 64 contiguous p values (128 bytes), transposed across
+    // each group of 8 lanes so that every store instruction writes four whole rows
+    // instead of 32 scattered 16-byte pieces.
     const int li = lane & 7, rbase = quad * 32 + (lane & ~7);
     auto store_prev16 = [&](T16* chunk_base) {
       uint4 d[8];
@@ -521,21 +543,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       for (int q = 0; q < 8; ++q)
         d[q] = make_uint4(pack2<T16>(prev[8 * q], prev[8 * q + 1]), pack2<T16>(prev[8 * q + 2], prev[8 * q + 3]),
                           pack2<T16>(prev[8 * q + 4], prev[8 * q + 5]), pack2<T16>(prev[8 * q + 6], prev[8 * q + 7]));
-#pragma unroll
-      for (int msk = 4; msk >= 1; msk >>= 1) {
-        const bool upper = (li & msk) != 0;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          if (q & msk) continue;
-          uint4 snd = upper ? d[q] : d[q | msk];
-          uint4 rcv;
-          rcv.x = __shfl_xor_sync(0xffffffffu, snd.x, msk);
-          rcv.y = __shfl_xor_sync(0xffffffffu, snd.y, msk);
-          rcv.z = __shfl_xor_sync(0xffffffffu, snd.z, msk);
-          rcv.w = __shfl_xor_sync(0xffffffffu, snd.w, msk);
-          if (upper) d[q] = rcv; else d[q | msk] = rcv;
-        }
-      }
+      lane_transpose<8>(d, li);
       // lane (group, li) now holds piece li of rows rbase + 0..7
       uint4* d4 = reinterpret_cast<uint4*>(chunk_base) + rbase * 8 + li;
 #pragma unroll
@@ -1163,9 +1171,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         warp_wait(bar(YFULL0 + yb), (Hc >> 1) & 1, kSiteScanMma2);
         tc_fence_after();
         if (wfail) continue;
-        const bool valid = l < ci.lim;
-        const long long yrow = ((ci.tok0 + l) * H + h) * 64 + ce * 32;
         const float el = __expf(cl);
+        // y pieces of this lane's row: 32 columns in 16-byte pieces (4 for 16-bit y, 8 for fp32)
+        constexpr int NPC = sizeof(YT) == 4 ? 8 : 4;
+        uint4 pc[NPC];
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           uint32_t ri[16], ro[16];
@@ -1177,7 +1186,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
             __syncwarp();
             if (lane == 0) mbar_arrive(bar(YFREE0 + yb));  // Y may be overwritten by head Hc + 2
           }
-          if (!valid) continue;
           float o[16];
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj)
@@ -1214,15 +1222,27 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
             }
           }
           if constexpr (sizeof(YT) == 4) {
-            float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + yrow + 16 * hf);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) yp[q] = make_float4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
+            for (int q = 0; q < 4; ++q)
+              pc[4 * hf + q] = make_uint4(__float_as_uint(o[4 * q]), __float_as_uint(o[4 * q + 1]),
+                                          __float_as_uint(o[4 * q + 2]), __float_as_uint(o[4 * q + 3]));
           } else {
-            uint4* yp = reinterpret_cast<uint4*>(y + yrow + 16 * hf);
 #pragma unroll
             for (int q = 0; q < 2; ++q)
-              yp[q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
-                                 pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
+              pc[2 * hf + q] = make_uint4(pack2<YT>(o[8 * q], o[8 * q + 1]), pack2<YT>(o[8 * q + 2], o[8 * q + 3]),
+                                          pack2<YT>(o[8 * q + 4], o[8 * q + 5]), pack2<YT>(o[8 * q + 6], o[8 * q + 7]));
+          }
+        }
+        // Rows are transposed across groups of NPC lanes: each store writes whole 64- or
+        // 128-byte row segments instead of 32 scattered 16-byte pieces.
+        const int li = lane & (NPC - 1), lr0 = 128 * m + quad * 32 + (lane & ~(NPC - 1));
+        lane_transpose<NPC>(pc, li);
+#pragma unroll
+        for (int j = 0; j < NPC; ++j) {
+          const int lj = lr0 + j;
+          if (lj < ci.lim) {
+            const long long yo = ((ci.tok0 + lj) * H + h) * 64 + ce * 32;
+            reinterpret_cast<uint4*>(y + yo)[li] = pc[j];
           }
         }
       }
