@@ -448,7 +448,8 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
   } else if (warp >= 10) {
     // ------------------------------------------------------------ dt / cum / w, one chunk ahead
     // warp 10 + hl serves head hl; lane: tokens [8 lane, 8 lane + 8) of the chunk.
-    // Raw dt of the next chunk is loaded while this one is processed.
+    // Raw dt is loaded two chunks ahead (two register sets used in turn), so the
+    // latency of these strided loads stays off the chain.
     const int hl = warp - 10, tb = 8 * lane;
     const bool act = hl < nh;
     const int h = h0 + (act ? hl : 0);
@@ -465,10 +466,8 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       for (int e = 0; e < 8; ++e)
         if (tb + e < ci.vlim) rv[e] = Ld<DT>::f(dr + (long long)e * H);
     };
-    float raw[8];
-    load_raw(0, raw);
-    bool fail = false;
-    for (int k = 0; k < count && !fail; ++k) {
+    // One chunk: dt / cum to global memory, w / exp(cum_last) into buffer k % NW.
+    auto prep = [&](int k, float (&raw)[8]) -> bool {
       const int buf = k % NW;
       ChunkInfo ci;
       chunk_info(cm, first + k, ci);
@@ -480,7 +479,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         run += d[e] * a;
         c[e] = run;
       }
-      load_raw(k + 1, raw);
+      load_raw(k + 2, raw);
       float incl = run;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -489,10 +488,8 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       }
       const float base = incl - run;
       const float cl = __shfl_sync(0xffffffffu, incl, 31);
-      if (k >= NW && !__all_sync(0xffffffffu, mbar_wait(bar(W_FREE + buf), ((k - NW) / NW) & 1, kSiteSpPrep))) {
-        fail = true;
-        break;
-      }
+      if (k >= NW && !__all_sync(0xffffffffu, mbar_wait(bar(W_FREE + buf), ((k - NW) / NW) & 1, kSiteSpPrep)))
+        return false;
       if (act) {
         const long long io = ((first + k) * (long long)H + h) * 256 + tb;
 #pragma unroll
@@ -512,6 +509,14 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(W_READY + buf));
+      return true;
+    };
+    float rawA[8], rawB[8];
+    load_raw(0, rawA);
+    load_raw(1, rawB);
+    bool fail = false;
+    for (int k = 0; k < count && !fail; k += 2) {
+      if (!prep(k, rawA) || (k + 1 < count && !prep(k + 1, rawB))) fail = true;
     }
     if (fail) *s_abort = 1;
   } else {
