@@ -680,8 +680,10 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
 //   y = exp(cum_l) Yoff + rowf_l Yin (+ D x) (* silu z)
 // Roles (one CTA per SM, items blockIdx.x, blockIdx.x + gridDim.x, ...):
 //   warp 0 (one lane)  TMA producer: C per item, B one 128-token block at a time,
-//                      head stages (x, prev, dt, cum) in a 3-deep ring; z of a head
-//                      goes into its stage's prev tile once MMA3 has read prev;
+//                      head stages (x, prev, dt, cum) in a 3-deep ring; z of a
+//                      first-half head comes with them (into the x rows [128, 256)
+//                      that half does not use), z of a second-half head goes into its
+//                      stage's prev tile once MMA3 has read prev;
 //   warp 1 (one lane)  MMA issuer;
 //   warps 2..9         conversion: CB_j landing (fp32) -> 16 bits per item, then per
 //                      head the g table and CB_j -> M'_j (warp: two 32-column blocks
@@ -696,7 +698,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
 // Barriers that a role may lag behind are kept per ring slot, so a waiter is never
 // two phases behind the barrier it polls. Every wait is bounded; a role that gives
 // up records the site, raises the CTA's abort flag and leaves its loop.
-constexpr int kScanHeadStageBytes = 32768 + 16384;  // x rows [0, 256) | prev, later z
+constexpr int kScanHeadStageBytes = 32768 + 16384;  // x rows [0, 256) (m = 0: [0, 128) | z) | prev (m = 1: later z)
 constexpr int kScanStages = 3;                       // head stages in flight
 constexpr int kScanSmallBytes = 4224;  // words: dt [0,256) cum [256,512) flags [512,516) g [520,1032)
 constexpr int kScanThreads = 576;      // warp 0 TMA, warp 1 MMA, warps 2..9 conversion, 10..17 epilogue
@@ -804,16 +806,19 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int I = 0, Hc = 0, zc = 0, Bc = 0, Bj = 0;  // items, heads, z loads, MMA1 jobs, B_1 landings
+      int I = 0, Hc = 0, zc = 0, Bc = 0, Bj = 0;  // items, heads, z phases started, MMA1 jobs, B_1 landings
       bool fail = false;
-      int zh = 0, zt = 0;  // head and first token of the previous head's half
-      // z rows of head zc go into its stage's prev tile once its MMA3 has read prev.
+      int zpend = -1, zh = 0, zt = 0;  // head counter, head and first token of a pending z load
+      // z rows of a second-half head go into its stage's prev tile once its MMA3 has
+      // read prev. (A first-half head's z comes with its main loads, into the x rows
+      // [128, 256) that the first half does not use.)
       auto load_z = [&]() -> bool {
-        const int s = zc % NS;
-        if (!mbar_wait(bar(YOFF0 + s), (zc / NS) & 1, kSiteScanMma2)) return false;
+        const int s = zpend % NS;
+        if (!mbar_wait(bar(YOFF0 + s), (zpend / NS) & 1, kSiteScanMma2)) return false;
         mbar_expect_tx(bar(Z_FULL0 + s), 16384u);
         tma_load_3d(smem_u32(hstage(s) + 32768), &tm_z, 0, zh, zt, bar(Z_FULL0 + s));
         ++zc;
+        zpend = -1;
         return true;
       };
       for (int it = blockIdx.x; it < n_items && !fail && !*s_abort; it += gridDim.x) {
@@ -846,16 +851,27 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           uint8_t* st = hstage(hs);
           float* sm = small(hs);
           const uint32_t fb = bar(HEAD_FULL0 + hs);
-          mbar_expect_tx(fb, (uint32_t)S * 128u + 16384u + 2048u);
+          const bool z_now = has_z && si.m == 0;
+          mbar_expect_tx(fb, (uint32_t)S * 128u + 16384u + 2048u + (z_now ? 16384u : 0u));
           for (int j = 0; j <= si.m; ++j) tma_load_3d(smem_u32(st + 16384 * j), &tm_x, 0, h, t0 + 128 * j, fb);
           tma_load_3d(smem_u32(st + 32768), &tm_h, 0, 0, si.k * H + h, fb);
           bulk_load(smem_u32(sm), dt + ((long long)si.k * H + h) * 256, 1024u, fb);
           bulk_load(smem_u32(sm + 256), cum + ((long long)si.k * H + h) * 256, 1024u, fb);
+          if (z_now) tma_load_3d(smem_u32(st + 16384), &tm_z, 0, h, t0, fb);
           // z of the previous head first: MMA1 of this item may wait for that head's
           // epilogue, which needs its z, before B's block 1 can be loaded.
-          if (has_z && Hc >= 1 && !load_z()) {
+          if (zpend >= 0 && !load_z()) {
             fail = true;
             break;
+          }
+          if (z_now) {
+            // the z tile arrives with HEAD_FULL; complete this head's Z_FULL phase
+            mbar_arrive(bar(Z_FULL0 + hs));
+            ++zc;
+          } else if (has_z) {
+            zpend = Hc;
+            zh = h;
+            zt = t0 + 128;
           }
           if (i == 0 && si.m == 1) {
             // B rows of block 1 once MMA1 of block 0 has read the buffer
@@ -869,13 +885,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
             ++Bc;
             ++Bj;
           }
-          zh = h;
-          zt = t0 + 128 * si.m;
           ++Hc;
         }
         ++I;
       }
-      if (!fail && !*s_abort && has_z && Hc > 0 && !load_z()) fail = true;
+      if (!fail && !*s_abort && zpend >= 0 && !load_z()) fail = true;
       if (fail) *s_abort = 1;
       // No copy may still be in flight when the CTA exits.
       if (I > 0) mbar_wait(bar(ITEM_FULL), (I - 1) & 1, kSiteScanTma);
@@ -1167,7 +1181,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             xv[q] = *reinterpret_cast<const uint4*>(sX + 16384 * m + sw128_off(r, 4 * ce + q));
-            zv[q] = has_z ? *reinterpret_cast<const uint4*>(sX + 32768 + sw128_off(r, 4 * ce + q))
+            zv[q] = has_z ? *reinterpret_cast<const uint4*>(sX + (m ? 32768 : 16384) + sw128_off(r, 4 * ce + q))
                           : make_uint4(0u, 0u, 0u, 0u);
           }
           __syncwarp();
