@@ -57,8 +57,10 @@ template <> __device__ __forceinline__ uint32_t pack2<__half>(float a, float b) 
   return *reinterpret_cast<uint32_t*>(&v);
 }
 template <typename T> __device__ __forceinline__ float2 unpack2(uint32_t w);
+// bf16 is the upper half of an fp32 word: widening is an exact bit move (integer
+// pipe), which keeps the transcendental / conversion pipe free for tanh and exp.
 template <> __device__ __forceinline__ float2 unpack2<__nv_bfloat16>(uint32_t w) {
-  return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w));
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 template <> __device__ __forceinline__ float2 unpack2<__half>(uint32_t w) {
   return __half22float2(*reinterpret_cast<__half2*>(&w));
