@@ -284,24 +284,29 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
 // it computes dt / cum (forward_kernel.py:20-105), the chunk states
 // S_k = sum_l B_l^T (x_l w_l) of both heads with one N = 128 MMA per 16 tokens
 // (:108-200; the B tile is loaded once for the pair) and folds S_k into the
-// running states, which live in registers (:203-258):
+// running states, which live in TMEM in fp32 (:203-258):
 //   prev_0 = h_init (or 0),  prev_{k+1} = exp(cum_last_k) prev_k + S_k,  h_last = prev_count.
 // prev_k is written in the input's 16-bit type for chunk_scan; the fp32 chunk
 // states never reach memory.
-// Roles: warp 0 (one lane) TMA producer of 128-token stages (B: two dstate
-// halves, x of each head) in a kSpStages-deep ring; warp 1 (one lane) MMA issuer,
-// accumulating chunk k in TMEM columns [128 (k & 1), +128) (head i at +64 i);
-// warps 10 and 11 compute dt, cum and the token weights w of heads 0 and 1 one
-// chunk ahead into a double buffer; warps 2..5 (head 0) and 6..9 (head 1) scale x by w and
-// fold the chunk states, thread = dstate row n (its TMEM lane). With an odd number
-// of heads per group the last CTA has one head; its second warp group only
-// releases the stages.
-// Ordering without extra barriers: a head group folds chunk k-1 after it
-// released chunk k's stages, and MMA(k+1) into the same accumulator waits for
-// chunk k+1's first stage, which both groups release after that fold.
+// Roles (22 warps):
+//   warp 0 (one lane)   TMA producer of 128-token stages (B: two dstate halves, x of
+//                       each head) in a kSpStages-deep ring;
+//   warp 1 (one lane)   MMA issuer: chunk k accumulates in TMEM columns
+//                       [128 (k & 1), +128) (head i at +64 i);
+//   warps 2..5          dt, cum and token weights w, up to kSpWBufs chunks ahead:
+//                       warp 2 + 2 i + e serves head i on the chunks of parity e (a chunk's
+//                       dt does not depend on the previous chunk, so two warps a head
+//                       double the rate of this step);
+//   warps 6..13         scale the x rows of each stage by w in place (4 warps a head);
+//   warps 14..21        fold: prev (TMEM columns [256 + 64 i, +64)) = exp(cum_last) prev
+//                       + S_k, then store prev in 16 bits; thread = dstate row n (its
+//                       TMEM lane), 4 warps a head.
+// Scaling the next chunk overlaps the fold of the previous one. With an odd number
+// of heads per group the last CTA has one head; the second head's scale and fold
+// warps then only keep the barrier phases.
 constexpr int kSpStages = 3;
 constexpr int kSpStageBytes = 32768 + 2 * 16384;  // B [128 tokens x 2 halves x 128 B] | x head 0 | x head 1
-constexpr int kSpThreads = 384;                    // 2 role warps, 8 head-group warps, 2 prep warps
+constexpr int kSpThreads = 704;                    // 22 warps
 constexpr int kSpWBufs = 3;  // w / exp(cum_last) buffers: the prep warps run up to two chunks ahead
 // ring | w [buffer][2 heads][256] | exp(cum_last) [buffer][2] | barriers, TMEM slot, abort flag
 constexpr int kSpSmem = kSpStages * kSpStageBytes + kSpWBufs * 2048 + 32 + 256 + 1024;
@@ -311,6 +316,7 @@ enum : unsigned int {
   kSiteSpScaled = 0x112,
   kSiteSpMma = 0x113,
   kSiteSpPrep = 0x114,
+  kSiteSpFold = 0x115,
 };
 
 template <bool BF16, typename DT>
@@ -330,11 +336,13 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
   float* sW = reinterpret_cast<float*>(smem + NST * kSpStageBytes);  // [buffer][head][256] token weights
   float* sEl = sW + 512 * NW;                                          // [buffer][head] exp(cum_last)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sEl + 8);
-  // FULL[NST] SCALED[NST] EMPTY[NST] ACC[2] W_READY[NW] W_FREE[NW]
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3 * NST + 2 + 2 * NW);
+  // FULL[NST] SCALED[NST] EMPTY[NST] ACC_FULL[2] ACC_FREE[2] W_READY[NW] W_FREE[NW]
+  constexpr int FULL = 0, SCALED = NST, EMPTY = 2 * NST, ACC_FULL = 3 * NST, ACC_FREE = ACC_FULL + 2,
+                W_READY = ACC_FREE + 2, W_FREE = W_READY + NW, NBARS = W_FREE + NW;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const int FULL = 0, SCALED = NST, EMPTY = 2 * NST, ACC = 3 * NST, W_READY = 3 * NST + 2, W_FREE = W_READY + NW;
+  constexpr uint32_t T_PREV = 256;  // running states: TMEM columns [256, 384)
 
   // blockIdx.x -> (row, group, head pair of the group)
   const int npairs = (hpg + 1) >> 1;
@@ -364,20 +372,30 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       mbar_init(bar(SCALED + s), 8);
       mbar_init(bar(EMPTY + s), 1);
     }
-    mbar_init(bar(ACC), 1);
-    mbar_init(bar(ACC + 1), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(ACC_FULL + b), 1);
+      mbar_init(bar(ACC_FREE + b), 8);
+    }
     for (int b = 0; b < NW; ++b) {
       mbar_init(bar(W_READY + b), 2);
-      mbar_init(bar(W_FREE + b), 8);
+      mbar_init(bar(W_FREE + b), 16);  // 8 scale + 8 fold warps
     }
     *s_abort = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(smem_u32(tslot), 256);
+  if (warp == 1) tmem_alloc(smem_u32(tslot), 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+
+  // Warps wait independently; a warp that gives up stops releasing work and raises
+  // the abort flag, so the others leave at their next check or bounded wait.
+  bool wfail = false;
+  auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
+    if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
+    return !wfail;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -421,6 +439,11 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         chunk_info(cm, first + k, ci);
         const int nst = (ci.lim + 127) >> 7;
         const uint32_t acc = tmem + 128 * (k & 1);
+        // the fold of chunk k - 2 must have read this accumulator
+        if (k >= 2 && !mbar_wait(bar(ACC_FREE + (k & 1)), ((k - 2) >> 1) & 1, kSiteSpFold)) {
+          fail = true;
+          break;
+        }
         for (int s = 0; s < nst; ++s, ++r) {
           const int slot = r % NST;
           if (!mbar_wait(bar(SCALED + slot), (r / NST) & 1, kSiteSpScaled)) {
@@ -438,19 +461,20 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
           last_par = (r / NST) & 1;
         }
         if (fail) break;
-        umma_commit(bar(ACC + (k & 1)));
+        umma_commit(bar(ACC_FULL + (k & 1)));
       }
       if (fail) *s_abort = 1;
       // All MMAs must be complete before TMEM is released.
       if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, kSiteSpMma);
     }
     __syncwarp();
-  } else if (warp >= 10) {
-    // ------------------------------------------------------------ dt / cum / w, one chunk ahead
-    // warp 10 + hl serves head hl; lane: tokens [8 lane, 8 lane + 8) of the chunk.
-    // Raw dt is loaded two chunks ahead (two register sets used in turn), so the
-    // latency of these strided loads stays off the chain.
-    const int hl = warp - 10, tb = 8 * lane;
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ dt / cum / w, ahead of the chain
+    // warp 2 + 2 hl + par serves head hl on chunks par, par + 2, ...; lane: tokens
+    // [8 lane, 8 lane + 8) of the chunk. Raw dt is loaded two chunks (of this warp)
+    // ahead, in two register sets used in turn, so the latency of these strided loads
+    // stays off the chain.
+    const int hl = (warp - 2) >> 1, par = (warp - 2) & 1, tb = 8 * lane;
     const bool act = hl < nh;
     const int h = h0 + (act ? hl : 0);
     const float a = A[h];
@@ -479,7 +503,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         run += d[e] * a;
         c[e] = run;
       }
-      load_raw(k + 2, raw);
+      load_raw(k + 4, raw);
       float incl = run;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -488,8 +512,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       }
       const float base = incl - run;
       const float cl = __shfl_sync(0xffffffffu, incl, 31);
-      if (k >= NW && !__all_sync(0xffffffffu, mbar_wait(bar(W_FREE + buf), ((k - NW) / NW) & 1, kSiteSpPrep)))
-        return false;
+      if (k >= NW && !warp_wait(bar(W_FREE + buf), ((k - NW) / NW) & 1, kSiteSpPrep)) return false;
       if (act) {
         const long long io = ((first + k) * (long long)H + h) * 256 + tb;
 #pragma unroll
@@ -512,103 +535,27 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       return true;
     };
     float rawA[8], rawB[8];
-    load_raw(0, rawA);
-    load_raw(1, rawB);
-    bool fail = false;
-    for (int k = 0; k < count && !fail; k += 2) {
-      if (!prep(k, rawA) || (k + 1 < count && !prep(k + 1, rawB))) fail = true;
+    load_raw(par, rawA);
+    load_raw(par + 2, rawB);
+    for (int k = par; k < count && !*s_abort; k += 4) {
+      if (!prep(k, rawA) || (k + 2 < count && !prep(k + 2, rawB))) break;
     }
-    if (fail) *s_abort = 1;
-  } else {
-    // ------------------------------------------------------------ head groups
-    const int hg = (warp - 2) >> 2;   // head of the pair
+    if (wfail) *s_abort = 1;
+  } else if (warp < 14) {
+    // ------------------------------------------------------------ scale x by w (in place)
+    const int hg = (warp - 6) >> 2, cw = (warp - 6) & 3;
     const bool active = hg < nh;
-    const int bar_id = 1 + hg;
-    const int cw = (warp - 2) & 3;
-    const int quad = warp & 3, n = quad * 32 + lane;
-    const uint32_t tlane = (uint32_t)(quad * 32) << 16;
-    const int h = h0 + (active ? hg : 0);
-    const long long PN = 64 * 128;
-    float prev[64];
-    if (h_init && active) {
-      const float* hi = h_init + ((long long)row * H + h) * PN + n;
-#pragma unroll
-      for (int p = 0; p < 64; ++p) prev[p] = hi[p * 128];
-    } else {
-#pragma unroll
-      for (int p = 0; p < 64; ++p) prev[p] = 0.f;
-    }
-    // prev16 of a chunk, row n = 64 contiguous p values (128 bytes), transposed across
-    // each group of 8 lanes so that every store instruction writes four whole rows
-    // instead of 32 scattered 16-byte pieces.
-    const int li = lane & 7, rbase = quad * 32 + (lane & ~7);
-    auto store_prev16 = [&](T16* chunk_base) {
-      uint4 d[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        d[q] = make_uint4(pack2<T16>(prev[8 * q], prev[8 * q + 1]), pack2<T16>(prev[8 * q + 2], prev[8 * q + 3]),
-                          pack2<T16>(prev[8 * q + 4], prev[8 * q + 5]), pack2<T16>(prev[8 * q + 6], prev[8 * q + 7]));
-      lane_transpose<8>(d, li);
-      // lane (group, li) now holds piece li of rows rbase + 0..7
-      uint4* d4 = reinterpret_cast<uint4*>(chunk_base) + rbase * 8 + li;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) d4[8 * j] = d[j];
-    };
-    // Warps wait independently; a warp that gives up stops releasing work and the
-    // group leaves at its next barrier, which ANDs the flags.
-    bool wfail = false;
-    auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
-      if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
-      return !wfail;
-    };
-    // Fold the finished chunk j: prev = exp(cum_last_j) prev + S_j, then store.
-    auto fold = [&](int j) -> bool {
-      warp_wait(bar(ACC + (j & 1)), (j >> 1) & 1, kSiteSpMma);
-      tc_fence_after();
-      if (!named_bar_and(bar_id, 128, !wfail && !*s_abort)) return false;
-      const float el = sEl[2 * (j % NW) + hg];
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t v[32];
-        tmem_ld32(tmem + tlane + 128 * (j & 1) + 64 * hg + 32 * half, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int q = 0; q < 32; ++q) prev[32 * half + q] = fmaf(el, prev[32 * half + q], __uint_as_float(v[q]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(W_FREE + j % NW));  // w / exp(cum_last) of chunk j no longer read
-      if (j + 1 < count) {
-        store_prev16(prev16 + ((long long)(first + j + 1) * H + h) * PN);
-      } else {
-        float* dst = h_last + ((long long)row * H + h) * PN + n;
-#pragma unroll
-        for (int p = 0; p < 64; ++p) dst[p * 128] = prev[p];
-      }
-      return true;
-    };
-    bool fail = false;
-    if (active) {
-      if (count == 0) {
-        float* dst = h_last + ((long long)row * H + h) * PN + n;
-#pragma unroll
-        for (int p = 0; p < 64; ++p) dst[p * 128] = prev[p];
-      } else {
-        store_prev16(prev16 + ((long long)first * H + h) * PN);
-      }
-    }
     int r = 0;
-    for (int k = 0; k < count && !fail; ++k) {
+    for (int k = 0; k < count && !wfail && !*s_abort; ++k) {
       ChunkInfo ci;
       chunk_info(cm, first + k, ci);
       const int nst = (ci.lim + 127) >> 7, buf = k % NW;
-      warp_wait(bar(W_READY + buf), (k / NW) & 1, kSiteSpPrep);
+      if (!warp_wait(bar(W_READY + buf), (k / NW) & 1, kSiteSpPrep)) break;
       const float* wh = sW + 512 * buf + 256 * hg;
-      // ---- x rows scaled by w_l in place (rows past `lim` become exact zeros) ----
+      // rows past `lim` become exact zeros (their w is 0)
       for (int s = 0; s < nst; ++s, ++r) {
         const int slot = r % NST;
-        warp_wait(bar(FULL + slot), (r / NST) & 1, kSiteSpTma);
-        if (wfail) continue;
+        if (!warp_wait(bar(FULL + slot), (r / NST) & 1, kSiteSpTma)) break;
         if (active) {
           uint4* sx = reinterpret_cast<uint4*>(sXst(slot, hg)) + cw * 32 + lane;
           // All loads first: stores through the same shared-memory pointers would
@@ -636,27 +583,106 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(SCALED + slot));
       }
-      if (!active) {
-        // the group of a missing second head only releases stages (and w buffers)
-        if (!wfail) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(W_FREE + buf));
+      if (wfail) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(W_FREE + buf));  // w of chunk k no longer read
+    }
+    if (wfail) *s_abort = 1;
+  } else {
+    // ------------------------------------------------------------ fold into the running states
+    const int hg = (warp - 14) >> 2;  // head of the pair
+    const bool active = hg < nh;
+    const int quad = warp & 3, n = quad * 32 + lane;
+    const uint32_t tlane = (uint32_t)(quad * 32) << 16;
+    const uint32_t tprev = tmem + tlane + T_PREV + 64 * hg;
+    const int h = h0 + (active ? hg : 0);
+    const long long PN = 64 * 128;
+    const int li = lane & 7, rbase = quad * 32 + (lane & ~7);
+    // prev16 row n of a chunk = 64 contiguous p values (128 bytes), transposed across
+    // each group of 8 lanes so that every store instruction writes four whole rows.
+    auto store_prev16 = [&](uint4 (&d)[8], T16* chunk_base) {
+      lane_transpose<8>(d, li);
+      uint4* d4 = reinterpret_cast<uint4*>(chunk_base) + rbase * 8 + li;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d4[8 * j] = d[j];
+    };
+    auto pack8 = [&](const uint32_t (&v)[16], int off) {
+      return make_uint4(pack2<T16>(__uint_as_float(v[off]), __uint_as_float(v[off + 1])),
+                        pack2<T16>(__uint_as_float(v[off + 2]), __uint_as_float(v[off + 3])),
+                        pack2<T16>(__uint_as_float(v[off + 4]), __uint_as_float(v[off + 5])),
+                        pack2<T16>(__uint_as_float(v[off + 6]), __uint_as_float(v[off + 7])));
+    };
+    // prev_0 = h_init (or 0) into TMEM and, as 16 bits, for the first chunk.
+    if (active) {
+      const float* hi = h_init ? h_init + ((long long)row * H + h) * PN + n : nullptr;
+      uint4 d[8];
+#pragma unroll
+      for (int qt = 0; qt < 4; ++qt) {
+        uint32_t v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(hi ? hi[(16 * qt + i) * 128] : 0.f);
+        if (count == 0) {
+          float* dst = h_last + ((long long)row * H + h) * PN + n;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) dst[(16 * qt + i) * 128] = __uint_as_float(v[i]);
+        } else {
+          tmem_st16(tprev + 16 * qt, v);
+          d[2 * qt] = pack8(v, 0);
+          d[2 * qt + 1] = pack8(v, 8);
         }
-        if (!named_bar_and(bar_id, 128, !wfail && !*s_abort)) fail = true;
-        continue;
       }
-      // ---- fold the previous chunk while this chunk's MMAs run ----
-      if (k > 0 && !fold(k - 1)) {
-        fail = true;
-        break;
+      if (count > 0) {
+        tmem_wait_st();
+        store_prev16(d, prev16 + ((long long)first * H + h) * PN);
       }
     }
-    if (active && !fail && count > 0 && !fold(count - 1)) fail = true;
-    if (fail || wfail) *s_abort = 1;
+    for (int j = 0; j < count && !*s_abort; ++j) {
+      const int buf = j % NW;
+      if (!warp_wait(bar(ACC_FULL + (j & 1)), (j >> 1) & 1, kSiteSpMma) ||
+          !warp_wait(bar(W_READY + buf), (j / NW) & 1, kSiteSpPrep))
+        break;
+      tc_fence_after();
+      const float el = sEl[2 * buf + hg];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(W_FREE + buf));  // exp(cum_last) of chunk j read
+      const bool last = j + 1 == count;
+      uint4 d[8];
+      if (active) {
+        const uint32_t acc = tmem + tlane + 128 * (j & 1) + 64 * hg;
+        float* dst = h_last + ((long long)row * H + h) * PN + n;
+#pragma unroll
+        for (int qt = 0; qt < 4; ++qt) {
+          uint32_t a[16], pv[16];
+          tmem_ld16(acc + 16 * qt, a);
+          tmem_ld16(tprev + 16 * qt, pv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            a[i] = __float_as_uint(fmaf(el, __uint_as_float(pv[i]), __uint_as_float(a[i])));
+          if (last) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) dst[(16 * qt + i) * 128] = __uint_as_float(a[i]);
+          } else {
+            tmem_st16(tprev + 16 * qt, a);
+            d[2 * qt] = pack8(a, 0);
+            d[2 * qt + 1] = pack8(a, 8);
+          }
+        }
+      }
+      // this chunk's accumulator is read: MMA(j + 2) may overwrite it
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(ACC_FREE + (j & 1)));
+      if (active && !last) {
+        tmem_wait_st();
+        store_prev16(d, prev16 + ((long long)(first + j + 1) * H + h) * PN);
+      }
+    }
+    if (wfail) *s_abort = 1;
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc(tmem, 256);
+  if (warp == 1) tmem_dealloc(tmem, 512);
 }
 
 // ===========================================================================
