@@ -398,6 +398,9 @@ def _traffic_from_profiles(kernel, cfg_name):
         return None
 
 
+E2E_SLICES = 4
+
+
 def e2e_measure(args, cfg, inp, dev, world, flush):
     """Same metric through the public API with pinned host inputs and outputs: the
     streaming entry ``HostStreamScan`` (row slices, copies overlapped with the scan) for
@@ -413,7 +416,7 @@ def e2e_measure(args, cfg, inp, dev, world, flush):
     nrow = cfg.batch if cu is None else cu.numel() - 1
     h_h = torch.empty(nrow, cfg.nheads, cfg.headdim, cfg.dstate, dtype=torch.float32).pin_memory()
     stream = torch.cuda.current_stream(dev)
-    scanner = sab.HostStreamScan(dev, slices=8, streams=2) if cu is None else None
+    scanner = sab.HostStreamScan(dev, slices=E2E_SLICES, in_flight=3) if cu is None else None
     A_h, D_h = small["A"].cpu(), small["D"].cpu()
 
     def step():
@@ -441,7 +444,8 @@ def e2e_measure(args, cfg, inp, dev, world, flush):
     return {"value": world * cfg.tokens / (ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "ms_per_step": ms, "steps": steps,
             "note": ("pinned host -> device inputs, scan, device -> pinned host y and h_last, per step; "
-                     + ("HostStreamScan, 8 row slices on 2 streams" if scanner is not None else "SSDScanFn"))}
+                     + (f"HostStreamScan, {E2E_SLICES} row slices, copy-in / scan / copy-out streams"
+                        if scanner is not None else "SSDScanFn"))}
 
 
 def ssu_measure(args, dev, flush, hbm_peak, world):

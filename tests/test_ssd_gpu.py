@@ -292,14 +292,15 @@ def test_backward_raises():
 
 @pytest.mark.parametrize("slices", [1, 3])
 def test_host_stream_scan_matches_device_scan(slices):
-    """HostStreamScan (host inputs, row slices on two streams) == ssd_scan_forward on the device."""
+    """HostStreamScan (host inputs, row slices through the copy-in / scan / copy-out
+    pipeline, buffer sets reused) == ssd_scan_forward on the device."""
     import selective_attention_b200 as sab
     from selective_attention_b200 import kernels
 
     inp = _c_inputs("c1", seed=9, batch=5, seqlen=600, nheads=8, h_init=True, delta_bias=True)
     length = torch.tensor([600, 512, 333, 1, 600])
     host = {k: inp[k].pin_memory() for k in ("u", "B", "C", "delta_raw", "z", "h_init")}
-    scan = sab.HostStreamScan(slices=slices, streams=2)
+    scan = sab.HostStreamScan(slices=slices, in_flight=2)
     for _ in range(2):  # second call reuses the device buffers
         y, h = scan(host["u"], inp["A"], host["B"], host["C"], host["delta_raw"], inp["delta_bias"], host["h_init"],
                     length, 256, True, (0.0, INF), inp["D"], host["z"])
