@@ -363,3 +363,23 @@ def test_padded_odd_heads_per_group_ragged(impl):
     y_ref = ssd_ref.gate_epilogue(y_ref, inp["u"], inp["D"], inp["z"])
     assert_bf16_close(y, y_ref, f"odd heads y ({impl})")
     assert_bf16_close(h, h_ref, f"odd heads h_last ({impl})")
+
+
+@pytest.mark.parametrize("impl", TC_IMPLS)
+def test_repeated_runs_are_bit_identical(impl):
+    """Every kernel of the chain is deterministic (no atomics, fixed MMA order), so
+    repeated runs on the same inputs must agree bit for bit. A missing wait between the
+    warp roles shows up here as rare differing runs long before it breaks a tolerance
+    (c2: packed ragged rows, 10 head blocks, many item boundaries per CTA)."""
+    from selective_attention_b200 import kernels, workloads
+
+    inp = workloads.make_ssd_inputs(workloads.CONFIGS["c2"], seed=0, device=torch.device("cuda"), gen_device="cuda")
+    args = (inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None, None, 256, True, (0.0, INF), True,
+            inp["D"], inp["z"], inp["cu_seqlens"])
+    y0, h0 = kernels.ssd_scan_forward(*args, impl=impl)
+    differ = 0
+    for _ in range(40):
+        y, h = kernels.ssd_scan_forward(*args, impl=impl)
+        differ += int(not (torch.equal(y, y0) and torch.equal(h, h0)))
+    torch.cuda.synchronize()
+    assert differ == 0, f"{differ} of 40 runs differ from the first"
