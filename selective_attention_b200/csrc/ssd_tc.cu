@@ -292,13 +292,14 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
 //   warp 0 (one lane)   TMA producer of 128-token stages (B: two dstate halves, x of
 //                       each head) in a kSpStages-deep ring;
 //   warp 1 (one lane)   MMA issuer: chunk k accumulates in TMEM columns
-//                       [128 (k & 1), +128) (head i at +64 i);
+//                       [128 (k % 3), +128) (head i at +64 i); three accumulators let
+//                       the MMAs run up to three chunks ahead of the fold;
 //   warps 2..5          dt, cum and token weights w, up to kSpWBufs chunks ahead:
 //                       warp 2 + 2 i + e serves head i on the chunks of parity e (a chunk's
 //                       dt does not depend on the previous chunk, so two warps a head
 //                       double the rate of this step);
 //   warps 6..13         scale the x rows of each stage by w in place (4 warps a head);
-//   warps 14..21        fold: prev (TMEM columns [256 + 64 i, +64)) = exp(cum_last) prev
+//   warps 14..21        fold: prev (TMEM columns [384 + 64 i, +64)) = exp(cum_last) prev
 //                       + S_k, then store prev in 16 bits; thread = dstate row n (its
 //                       TMEM lane), 4 warps a head.
 // Scaling the next chunk overlaps the fold of the previous one. With an odd number
@@ -307,7 +308,8 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
 constexpr int kSpStages = 3;
 constexpr int kSpStageBytes = 32768 + 2 * 16384;  // B [128 tokens x 2 halves x 128 B] | x head 0 | x head 1
 constexpr int kSpThreads = 704;                    // 22 warps
-constexpr int kSpWBufs = 3;  // w / exp(cum_last) buffers: the prep warps run up to two chunks ahead
+constexpr int kSpWBufs = 3;
+constexpr int kSpAccs = 3;  // chunk-state accumulators in TMEM  // w / exp(cum_last) buffers: the prep warps run up to two chunks ahead
 // ring | w [buffer][2 heads][256] | exp(cum_last) [buffer][2] | barriers, TMEM slot, abort flag
 constexpr int kSpSmem = kSpStages * kSpStageBytes + kSpWBufs * 2048 + 32 + 256 + 1024;
 
@@ -336,13 +338,16 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
   float* sW = reinterpret_cast<float*>(smem + NST * kSpStageBytes);  // [buffer][head][256] token weights
   float* sEl = sW + 512 * NW;                                          // [buffer][head] exp(cum_last)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sEl + 8);
-  // FULL[NST] SCALED[NST] EMPTY[NST] ACC_FULL[2] ACC_FREE[2] W_READY[NW] W_FREE[NW]
-  constexpr int FULL = 0, SCALED = NST, EMPTY = 2 * NST, ACC_FULL = 3 * NST, ACC_FREE = ACC_FULL + 2,
-                W_READY = ACC_FREE + 2, W_FREE = W_READY + NW, NBARS = W_FREE + NW;
+  // FULL[NST] SCALED[NST] EMPTY[NST] ACC_FULL[NA] ACC_FREE[NA] W_READY[NW] W_FREE[NW]
+  constexpr int NA = kSpAccs;
+  constexpr int FULL = 0, SCALED = NST, EMPTY = 2 * NST, ACC_FULL = 3 * NST, ACC_FREE = ACC_FULL + NA,
+                W_READY = ACC_FREE + NA, W_FREE = W_READY + NW, NBARS = W_FREE + NW;
+  static_assert(NBARS * 8 + 8 <= 256, "barrier area");
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  constexpr uint32_t T_PREV = 256;  // running states: TMEM columns [256, 384)
+  constexpr uint32_t T_PREV = 128 * NA;  // running states: TMEM columns [384, 512)
+  static_assert(128 * NA + 128 <= 512, "TMEM columns");
 
   // blockIdx.x -> (row, group, head pair of the group)
   const int npairs = (hpg + 1) >> 1;
@@ -372,7 +377,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       mbar_init(bar(SCALED + s), 8);
       mbar_init(bar(EMPTY + s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NA; ++b) {
       mbar_init(bar(ACC_FULL + b), 1);
       mbar_init(bar(ACC_FREE + b), 8);
     }
@@ -438,9 +443,9 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         ChunkInfo ci;
         chunk_info(cm, first + k, ci);
         const int nst = (ci.lim + 127) >> 7;
-        const uint32_t acc = tmem + 128 * (k & 1);
+        const uint32_t acc = tmem + 128 * (k % NA);
         // the fold of chunk k - 2 must have read this accumulator
-        if (k >= 2 && !mbar_wait(bar(ACC_FREE + (k & 1)), ((k - 2) >> 1) & 1, kSiteSpFold)) {
+        if (k >= NA && !mbar_wait(bar(ACC_FREE + k % NA), ((k - NA) / NA) & 1, kSiteSpFold)) {
           fail = true;
           break;
         }
@@ -461,7 +466,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
           last_par = (r / NST) & 1;
         }
         if (fail) break;
-        umma_commit(bar(ACC_FULL + (k & 1)));
+        umma_commit(bar(ACC_FULL + k % NA));
       }
       if (fail) *s_abort = 1;
       // All MMAs must be complete before TMEM is released.
@@ -638,7 +643,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
     }
     for (int j = 0; j < count && !*s_abort; ++j) {
       const int buf = j % NW;
-      if (!warp_wait(bar(ACC_FULL + (j & 1)), (j >> 1) & 1, kSiteSpMma) ||
+      if (!warp_wait(bar(ACC_FULL + j % NA), (j / NA) & 1, kSiteSpMma) ||
           !warp_wait(bar(W_READY + buf), (j / NW) & 1, kSiteSpPrep))
         break;
       tc_fence_after();
@@ -648,7 +653,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       const bool last = j + 1 == count;
       uint4 d[8];
       if (active) {
-        const uint32_t acc = tmem + tlane + 128 * (j & 1) + 64 * hg;
+        const uint32_t acc = tmem + tlane + 128 * (j % NA) + 64 * hg;
         float* dst = h_last + ((long long)row * H + h) * PN + n;
 #pragma unroll
         for (int qt = 0; qt < 4; ++qt) {
@@ -669,10 +674,10 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
           }
         }
       }
-      // this chunk's accumulator is read: MMA(j + 2) may overwrite it
+      // this chunk's accumulator is read: MMA(j + kSpAccs) may overwrite it
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(bar(ACC_FREE + (j & 1)));
+      if (lane == 0) mbar_arrive(bar(ACC_FREE + j % NA));
       if (active && !last) {
         tmem_wait_st();
         store_prev16(d, prev16 + ((long long)(first + j + 1) * H + h) * PN);
