@@ -763,6 +763,14 @@ __device__ __forceinline__ bool scan_item(const ChunkMap& cm, int it, int G, int
   return 128 * si.m < ci.lim;
 }
 
+// The j-th item of CTA b: rows of gridDim.x items taken in snake order (b, then
+// 2 grid - 1 - b, ...). Items alternate a chunk's heavier second half and its first
+// half, so a plain grid stride with an even grid would hand every CTA the same kind.
+__device__ __forceinline__ int scan_item_of(int j) {
+  const int b = (j & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
+  return j * (int)gridDim.x + b;
+}
+
 template <bool BF16, typename YT>
 __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c,
@@ -852,7 +860,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         zpend = -1;
         return true;
       };
-      for (int it = blockIdx.x; it < n_items && !fail && !*s_abort; it += gridDim.x) {
+      for (int jt = 0, it = scan_item_of(0); it < n_items && !fail && !*s_abort; it = scan_item_of(++jt)) {
         ScanItem si;
         ChunkInfo ci;
         if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
@@ -944,7 +952,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       int I = 0, Hc = 0, Jc = 0, Sc = 0, Bj = 0;  // items, heads, M-buffer jobs, CB landings, B_1 landings
       bool fail = false;
       int last_bar = -1, last_par = 0;
-      for (int it = blockIdx.x; it < n_items && !fail && !*s_abort; it += gridDim.x) {
+      for (int jt = 0, it = scan_item_of(0); it < n_items && !fail && !*s_abort; it = scan_item_of(++jt)) {
         ScanItem si;
         ChunkInfo ci;
         if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
@@ -1042,7 +1050,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
       return !wfail;
     };
-    for (int it = blockIdx.x; it < n_items && !fail; it += gridDim.x) {
+    for (int jt = 0, it = scan_item_of(0); it < n_items && !fail; it = scan_item_of(++jt)) {
       ScanItem si;
       ChunkInfo ci;
       if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
@@ -1190,7 +1198,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
       return !wfail;
     };
-    for (int it = blockIdx.x; it < n_items && !fail; it += gridDim.x) {
+    for (int jt = 0, it = scan_item_of(0); it < n_items && !fail; it = scan_item_of(++jt)) {
       ScanItem si;
       ChunkInfo ci;
       if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
@@ -1438,12 +1446,31 @@ static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, con
   const int dt_nonneg = (c.dmax >= 0.f) && (c.use_sp || c.dmin >= 0.f);
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // Heads per item: up to 8 share one CB (its load, MMA and rounding are paid once
-  // per item); fewer when that leaves under two items per CTA.
+  // Heads per item: the heads of an item share one CB (its load, MMA and rounding).
+  // Up to 8, fewer when that leaves under two items per CTA. An item's start costs about
+  // two heads' time on the CTA; with many rounds of items per CTA the pipeline hides it,
+  // but with few rounds (small batches) it does not, and then the block size with the
+  // smallest estimated makespan, rounds x (2 + heads per item), is taken.
   const int hpg = c.H / c.G;
-  int hb = hpg < 8 ? hpg : 8;
   auto n_items = [&](int b) { return 2ll * c.nchunks_max * c.G * ((hpg + b - 1) / b); };
+  auto makespan = [&](int b) {
+    const long long it = n_items(b), g = it < sms ? it : sms;
+    return ((it + g - 1) / g) * (2ll + b);
+  };
+  int hb = hpg < 8 ? hpg : 8;
   while (hb > 1 && n_items(hb) < 2ll * sms) hb = (hb + 1) / 2;
+  if ((n_items(hb) + sms - 1) / sms <= 4) {
+    long long best = makespan(hb);
+    const int b0 = hb;
+    for (int b = b0 + 1; b <= hpg && b <= kScanMaxHeads; ++b) {
+      if ((hpg + b - 1) / b == (hpg + b - 2) / (b - 1)) continue;  // same block count as b - 1
+      const long long cost = makespan(b);
+      if (cost <= best) {
+        best = cost;
+        hb = b;
+      }
+    }
+  }
   const long long items = n_items(hb);
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
   const int grid = (int)(items < sms ? items : sms);  // persistent: one CTA per SM
