@@ -19,6 +19,9 @@
  *   ssd_chunk_scan_fwd     <- triton_kernels/ssd_scan/forward.py:175 chunk_scan_forward
  *   ssu_fwd                <- triton_kernels/ssu/forward.py:7 ssu_forward
  *                             (called from ops/ssu.py:61 SSUFn.forward)
+ *   ssm_conv_prefill       <- modules/ssm.py:112-134 (SiLU, depthwise causal conv1d,
+ *                             split into x, B, C) and inference/ssm_cache.py:10-36
+ *                             SSMCache.build_conv_ctx
  * The reference crosses host->device only at Triton launches; these functions are
  * the same crossing for a C caller.
  */
@@ -186,6 +189,22 @@ int ssu_fwd(const void* u, const float* A, const void* B, const void* C,
             int64_t batch, int64_t nheads, int64_t headdim, int64_t dstate, int64_t ngroups,
             int32_t x_dtype, int32_t dt_dtype, int32_t h_dtype, int32_t y_dtype,
             int32_t use_delta_softplus, float delta_min, float delta_max, void* stream);
+
+/*
+ * SSM prefill front end between the input projection and the scan
+ * (modules/ssm.py:112-134, inference/ssm_cache.py:10-36):
+ *   out = bias + depthwise causal conv_K( silu(hbc) )   (silu rounded to `dtype` first),
+ *   x, B, C = out[..., :inner], out[..., inner:inner+gn], out[..., inner+gn:],
+ *   conv_ctx[b, c, k] = hbc[b, len_b - K + k, c] (0 outside [0, len_b)), len_b = lengths[b] or L.
+ * hbc (b, L, inner + 2*gn) with token stride row_stride (elements; the channels are
+ * contiguous), dtype; weight (inner+2*gn, K) fp32; bias (inner+2*gn,) fp32 or NULL;
+ * x (b, L, inner), B and C (b, L, gn) dtype; conv_ctx (b, inner+2*gn, K) dtype or NULL;
+ * lengths (b,) int64 or NULL. 1 <= K <= 8.
+ */
+int ssm_conv_prefill(const void* hbc, int64_t row_stride, const float* weight, const float* bias,
+                     void* x, void* B, void* C, void* conv_ctx, const int64_t* lengths,
+                     int64_t batch, int64_t seqlen, int64_t inner, int64_t gn, int64_t kernel_size,
+                     int32_t dtype, void* stream);
 
 #ifdef __cplusplus
 }

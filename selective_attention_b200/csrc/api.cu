@@ -360,4 +360,18 @@ int ssu_fwd(const void* u, const float* A, const void* B, const void* C, const v
                                 use_delta_softplus, delta_min, delta_max, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int ssm_conv_prefill(const void* hbc, int64_t row_stride, const float* weight, const float* bias, void* x, void* B,
+                     void* C, void* conv_ctx, const int64_t* lengths, int64_t batch, int64_t seqlen, int64_t inner,
+                     int64_t gn, int64_t kernel_size, int32_t dtype, void* stream) {
+  if (!hbc || !weight || !x || !B || !C) return SSD_ERR_INVALID_ARGUMENT;
+  if (batch <= 0 || seqlen <= 0 || inner <= 0 || gn <= 0 || kernel_size < 1 || kernel_size > 8)
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (row_stride < inner + 2 * gn) return SSD_ERR_INVALID_ARGUMENT;
+  if (batch > 65535 || seqlen > 0x7fffffffll || inner + 2 * gn > 0x7fffffffll) return SSD_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  return cuda_status(launch_ssm_conv_prefill(hbc, (long long)row_stride, weight, bias, x, B, C, conv_ctx, lengths,
+                                             (int)batch, (int)seqlen, (int)inner, (int)gn, (int)kernel_size, dtype,
+                                             reinterpret_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

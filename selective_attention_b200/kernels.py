@@ -278,3 +278,46 @@ def ssu_forward(u, A, B, C, delta_raw, delta_bias, h, use_delta_softplus=True, d
         float(delta_limit[0]), float(delta_limit[1]), _stream(dev))
     _lib.check(st, "ssu_forward")
     return y, h
+
+
+def ssm_conv_prefill(hBC, conv_weight, conv_bias, inner_dim, gn, lengths=None, build_ctx=False, out=None):
+    """SSM prefill front end (``modules/ssm.py:112-134``): ``silu`` then the depthwise causal
+    conv over the sequence, split into ``x`` (b, L, inner_dim), ``B`` and ``C`` (b, L, gn),
+    in ``hBC``'s dtype; with ``build_ctx`` also the decode cache ``conv_ctx`` (b, conv_dim, K)
+    of ``SSMCache.build_conv_ctx`` (``inference/ssm_cache.py:10-36``), the last K inputs
+    before each row's length (zeros where missing).
+
+    ``hBC`` is (b, L, conv_dim) with contiguous channels and any token stride, e.g. the
+    first ``conv_dim`` columns of the input projection's output. ``conv_weight`` is the
+    depthwise ``nn.Conv1d`` weight (conv_dim, 1, K) or (conv_dim, K); ``conv_bias``
+    (conv_dim,) or None. Returns ``(x, B, C, conv_ctx or None)``."""
+    if hBC.dim() != 3:
+        raise ValueError(f"[hBC] expected (batch, seq_len, conv_dim), got {tuple(hBC.shape)}")
+    b, L, conv_dim = hBC.shape
+    if conv_dim != inner_dim + 2 * gn:
+        raise ValueError(f"[hBC] conv_dim {conv_dim} != inner_dim + 2 * gn = {inner_dim + 2 * gn}")
+    w = conv_weight.reshape(conv_weight.shape[0], -1)
+    if w.shape[0] != conv_dim or not 1 <= w.shape[1] <= 8:
+        raise ValueError(f"[conv_weight] expected (conv_dim, 1, K) with K <= 8, got {tuple(conv_weight.shape)}")
+    K = w.shape[1]
+    dev = check_cuda([hBC, conv_weight, conv_bias, lengths], ["hBC", "conv_weight", "conv_bias", "lengths"])
+    if hBC.stride(2) != 1:
+        hBC = hBC.contiguous()
+    if hBC.stride(0) != L * hBC.stride(1):
+        hBC = hBC.contiguous()  # rows of one batch entry must follow each other at the token stride
+    w = to_contiguous(w.float())
+    bias = None if conv_bias is None else to_contiguous(conv_bias.float())
+    if lengths is not None:
+        lengths = to_contiguous(lengths.to(torch.int64))
+    if out is None:
+        x = torch.empty(b, L, inner_dim, dtype=hBC.dtype, device=hBC.device)
+        Bo = torch.empty(b, L, gn, dtype=hBC.dtype, device=hBC.device)
+        Co = torch.empty(b, L, gn, dtype=hBC.dtype, device=hBC.device)
+    else:
+        x, Bo, Co = out
+    ctx = torch.empty(b, conv_dim, K, dtype=hBC.dtype, device=hBC.device) if build_ctx else None
+    st = _lib.lib().ssm_conv_prefill(
+        _lib.ptr(hBC), hBC.stride(1), _lib.ptr(w), _lib.ptr(bias), _lib.ptr(x), _lib.ptr(Bo), _lib.ptr(Co),
+        _lib.ptr(ctx), _lib.ptr(lengths), b, L, inner_dim, gn, K, _lib.dtype_code(hBC.dtype, "hBC"), _stream(dev))
+    _lib.check(st, "ssm_conv_prefill")
+    return x, Bo, Co, ctx
