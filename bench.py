@@ -520,7 +520,44 @@ def ssu_measure(args, dev, flush, hbm_peak, world):
     gbs = by / (us / 1e6) / 1e9
     return {"config": "c3: decode b256 H80 P64 N128 G1, fp32 state in place, bf16 x/B/C/z, D+z",
             "us_per_step": us, "alg_bytes": by, "gbs": gbs, "peak_gbs": hbm_peak, "frac": gbs / hbm_peak,
-            "steps": steps, "timing": "median of per-step CUDA events, L2 flushed between steps"}
+            "steps": steps, "timing": "median of per-step CUDA events, L2 flushed between steps",
+            "front": decode_front_measure(args, dev, flush, cfg)}
+
+
+def decode_front_measure(args, dev, flush, cfg):
+    """The decode step's front end before the SSU at config 3's widths (conv cache update,
+    SiLU, weighted sum, split; K 4): one launch through the C ABI, arguments prepared once
+    (the kernel is a few microseconds, below the Python wrapper's own cost)."""
+    from selective_attention_b200 import _lib, kernels
+
+    b, inner, gn, K = cfg.batch, cfg.nheads * cfg.headdim, cfg.ngroups * cfg.dstate, 4
+    conv_dim = inner + 2 * gn
+    g = torch.Generator(device=dev).manual_seed(3)
+    proj = torch.randn(b, conv_dim + inner + cfg.nheads, device=dev, generator=g).to(torch.bfloat16)
+    ctx = torch.randn(b, conv_dim, K, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(conv_dim, K, device=dev, generator=g) * 0.5).contiguous()
+    bias = torch.randn(conv_dim, device=dev, generator=g) * 0.1
+    x = torch.empty(b, inner, device=dev, dtype=torch.bfloat16)
+    Bo = torch.empty(b, gn, device=dev, dtype=torch.bfloat16)
+    Co = torch.empty(b, gn, device=dev, dtype=torch.bfloat16)
+    kernels.ssm_conv_decode(proj[:, :conv_dim], ctx, w, bias, inner, gn, out=(x, Bo, Co))
+    fn = _lib.lib().ssm_conv_decode
+    cargs = (_lib.ptr(proj), proj.stride(0), _lib.ptr(ctx), _lib.ptr(w), _lib.ptr(bias), _lib.ptr(x), _lib.ptr(Bo),
+             _lib.ptr(Co), b, inner, gn, K, _lib.dtype_code(torch.bfloat16, "hBC"),
+             torch.cuda.current_stream(dev).cuda_stream)
+
+    def step():
+        _lib.check(fn(*cargs), "ssm_conv_decode")
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    per = time_steps(step, max(10, min(args.steps, 200)), flush, torch.cuda.current_stream(dev))
+    us = statistics.median(per) * 1e3
+    by = b * conv_dim * (2 * 2 * K + 2 + 2) + conv_dim * (K + 1) * 4  # cache r/w, input, output, weights
+    return {"config": f"b{b} conv_dim {conv_dim} (x {inner} + B {gn} + C {gn}) K{K} bf16, cache in place",
+            "us_per_step": us, "alg_bytes": by, "gbs": by / (us / 1e6) / 1e9,
+            "note": "replaces the reference's cache roll, silu, product, sum, bias add and split (6 torch launches)"}
 
 
 if __name__ == "__main__":

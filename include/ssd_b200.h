@@ -22,6 +22,9 @@
  *   ssm_conv_prefill       <- modules/ssm.py:112-134 (SiLU, depthwise causal conv1d,
  *                             split into x, B, C) and inference/ssm_cache.py:10-36
  *                             SSMCache.build_conv_ctx
+ *   ssm_conv_decode        <- modules/ssm.py:173-186 (decode step: cache update, SiLU,
+ *                             weighted sum, split) and inference/ssm_cache.py:38-43
+ *                             SSMCache.update
  * The reference crosses host->device only at Triton launches; these functions are
  * the same crossing for a C caller.
  */
@@ -205,6 +208,19 @@ int ssm_conv_prefill(const void* hbc, int64_t row_stride, const float* weight, c
                      void* x, void* B, void* C, void* conv_ctx, const int64_t* lengths,
                      int64_t batch, int64_t seqlen, int64_t inner, int64_t gn, int64_t kernel_size,
                      int32_t dtype, void* stream);
+
+/*
+ * SSM decode-step front end (modules/ssm.py:173-186, inference/ssm_cache.py:38-43): per
+ * channel c of row b, conv_ctx[b, c, :] is shifted left by one and hbc_new[b, c] appended
+ * (in place), then out = sum_k w[c,k] silu(conv_ctx[b,c,k]) + bias[c] with the reference's
+ * roundings to `dtype` (silu, each product, the sum, the bias add), split into
+ * x (b, inner), B and C (b, gn). hbc_new (b, inner + 2*gn) with row stride row_stride
+ * (elements), dtype; conv_ctx (b, inner + 2*gn, K) dtype, updated in place; weight
+ * (inner+2*gn, K) fp32; bias (inner+2*gn,) fp32 or NULL. 1 <= K <= 8.
+ */
+int ssm_conv_decode(const void* hbc_new, int64_t row_stride, void* conv_ctx, const float* weight, const float* bias,
+                    void* x, void* B, void* C, int64_t batch, int64_t inner, int64_t gn, int64_t kernel_size,
+                    int32_t dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -51,3 +51,27 @@ def prefill_front(hBC: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.
     out = out[:, :, :L].transpose(1, 2)                          # ssm.py:126-127
     x, B, C = torch.split(out, [inner, gn, gn], dim=-1)          # ssm.py:129-134
     return x, B, C, ctx
+
+
+def update_conv_ctx(ctx: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """SSMCache.update (inference/ssm_cache.py:38-43): shift left by one, append x."""
+    out = torch.roll(ctx, shifts=-1, dims=-1)
+    out[:, :, -1] = x
+    return out
+
+
+def decode_front(hBC: torch.Tensor, ctx: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], inner: int,
+                 gn: int):
+    """One decode step's front end (modules/ssm.py:173-186) with torch ops on tensors of
+    hBC's dtype, as the reference runs them: the cache update, silu of the whole window,
+    the product with the conv weight, the sum over the window and the bias add, then the
+    split. Returns x (b, inner), B, C (b, gn) and the updated cache."""
+    dt = hBC.dtype
+    new_ctx = update_conv_ctx(ctx, hBC)                               # ssm.py:173-174
+    s = F.silu(new_ctx)                                               # :175
+    w = weight.reshape(weight.shape[0], -1).to(dt)
+    out = (s * w).sum(dim=-1)                                         # :176
+    if bias is not None:
+        out = out + bias.to(dt)
+    x, B, C = torch.split(out, [inner, gn, gn], dim=-1)              # :177-184
+    return x, B, C, new_ctx

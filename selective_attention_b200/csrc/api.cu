@@ -374,4 +374,16 @@ int ssm_conv_prefill(const void* hbc, int64_t row_stride, const float* weight, c
                                              reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int ssm_conv_decode(const void* hbc_new, int64_t row_stride, void* conv_ctx, const float* weight, const float* bias,
+                    void* x, void* B, void* C, int64_t batch, int64_t inner, int64_t gn, int64_t kernel_size,
+                    int32_t dtype, void* stream) {
+  if (!hbc_new || !conv_ctx || !weight || !x || !B || !C) return SSD_ERR_INVALID_ARGUMENT;
+  if (batch <= 0 || inner <= 0 || gn <= 0 || kernel_size < 1 || kernel_size > 8) return SSD_ERR_INVALID_ARGUMENT;
+  if (row_stride < inner + 2 * gn || batch * (inner + 2 * gn) > 0x7fffffffffll) return SSD_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  return cuda_status(launch_ssm_conv_decode(hbc_new, (long long)row_stride, conv_ctx, weight, bias, x, B, C,
+                                            (int)batch, (int)inner, (int)gn, (int)kernel_size, dtype,
+                                            reinterpret_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

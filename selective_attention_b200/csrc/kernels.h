@@ -55,6 +55,9 @@ unsigned int fetch_error_tc(cudaStream_t s);
 cudaError_t launch_ssm_conv_prefill(const void* hbc, long long row_stride, const float* w, const float* bias,
                                     void* x, void* Bo, void* Co, void* ctx, const int64_t* lengths, int b, int L,
                                     int inner, int gn, int K, int dtype, cudaStream_t s);
+cudaError_t launch_ssm_conv_decode(const void* hnew, long long row_stride, void* ctx, const float* w,
+                                   const float* bias, void* x, void* Bo, void* Co, int b, int inner, int gn, int K,
+                                   int dtype, cudaStream_t s);
 cudaError_t launch_ssu(const void* u, const float* A, const void* B, const void* C, const void* delta_raw,
                        const float* delta_bias, void* h, void* y, const float* D, const void* z, int b, int H,
                        int P, int N, int G, int x_dtype, int dt_dtype, int h_dtype, int y_dtype, int use_sp,

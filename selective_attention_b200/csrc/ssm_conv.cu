@@ -389,6 +389,73 @@ static cudaError_t conv_launch_t(const void* hbc, long long rs, const float* w, 
   return cudaGetLastError();
 }
 
+// Decode step (modules/ssm.py:173-186 with inference/ssm_cache.py:38-43): per channel the
+// cache window is shifted left by one and the new input appended (in place), then
+//   out = round(round(sum_k round(w[c,k] silu(ctx[c,k]))) + bias[c])
+// with every round() to the activation type, as the reference's torch ops on tensors of
+// that type round (silu, the product, the sum, the bias add; identities for fp32), and
+// out split into x (b, inner), B, C (b, gn). One thread per (row, channel).
+template <typename T>
+__global__ void ssm_conv_decode_kernel(const T* __restrict__ hnew, long long row_stride, T* __restrict__ ctx,
+                                       const float* __restrict__ w, const float* __restrict__ bias,
+                                       T* __restrict__ x, T* __restrict__ Bo, T* __restrict__ Co, int B, int inner,
+                                       int gn, int K) {
+  const int conv_dim = inner + 2 * gn;
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)B * conv_dim) return;
+  const int b = (int)(i / conv_dim), c = (int)(i % conv_dim);
+  T* cp = ctx + i * K;
+  T win[8];
+  const T xn = hnew[(long long)b * row_stride + c];
+  float acc = 0.f;
+  if (sizeof(T) == 2 && K == 4 && (reinterpret_cast<uintptr_t>(ctx) & 7) == 0) {
+    // the window of a channel is 8 bytes: one load, one store
+    uint2 q = *reinterpret_cast<const uint2*>(cp);
+    const T* o = reinterpret_cast<const T*>(&q);
+    win[0] = o[1]; win[1] = o[2]; win[2] = o[3]; win[3] = xn;
+    *reinterpret_cast<uint2*>(cp) = *reinterpret_cast<const uint2*>(win);
+  } else {
+    for (int k = 0; k + 1 < K; ++k) win[k] = cp[k + 1];
+    win[K - 1] = xn;
+    for (int k = 0; k < K; ++k) cp[k] = win[k];
+  }
+  for (int k = 0; k < K; ++k) {
+    const float v = to_f32(win[k]);
+    acc += round_to<T>(w[(long long)c * K + k] * silu_t<T>(v));
+  }
+  float o = round_to<T>(acc);
+  if (bias) o = o + round_to<T>(bias[c]);
+  const T ov = from_f32<T>(o);
+  if (c < inner) x[(long long)b * inner + c] = ov;
+  else if (c < inner + gn) Bo[(long long)b * gn + (c - inner)] = ov;
+  else Co[(long long)b * gn + (c - inner - gn)] = ov;
+}
+
+cudaError_t launch_ssm_conv_decode(const void* hnew, long long row_stride, void* ctx, const float* w,
+                                   const float* bias, void* x, void* Bo, void* Co, int b, int inner, int gn, int K,
+                                   int dtype, cudaStream_t s) {
+  const long long n = (long long)b * (inner + 2 * gn);
+  const unsigned grid = (unsigned)((n + 255) / 256);
+  switch (dtype) {
+    case SSD_F32:
+      ssm_conv_decode_kernel<float><<<grid, 256, 0, s>>>((const float*)hnew, row_stride, (float*)ctx, w, bias,
+                                                         (float*)x, (float*)Bo, (float*)Co, b, inner, gn, K);
+      break;
+    case SSD_BF16:
+      ssm_conv_decode_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+          (const __nv_bfloat16*)hnew, row_stride, (__nv_bfloat16*)ctx, w, bias, (__nv_bfloat16*)x,
+          (__nv_bfloat16*)Bo, (__nv_bfloat16*)Co, b, inner, gn, K);
+      break;
+    case SSD_F16:
+      ssm_conv_decode_kernel<__half><<<grid, 256, 0, s>>>((const __half*)hnew, row_stride, (__half*)ctx, w, bias,
+                                                          (__half*)x, (__half*)Bo, (__half*)Co, b, inner, gn, K);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_ssm_conv_prefill(const void* hbc, long long row_stride, const float* w, const float* bias,
                                     void* x, void* Bo, void* Co, void* ctx, const int64_t* lengths, int b, int L,
                                     int inner, int gn, int K, int dtype, cudaStream_t s) {

@@ -321,3 +321,40 @@ def ssm_conv_prefill(hBC, conv_weight, conv_bias, inner_dim, gn, lengths=None, b
         _lib.ptr(ctx), _lib.ptr(lengths), b, L, inner_dim, gn, K, _lib.dtype_code(hBC.dtype, "hBC"), _stream(dev))
     _lib.check(st, "ssm_conv_prefill")
     return x, Bo, Co, ctx
+
+
+def ssm_conv_decode(hBC, conv_ctx, conv_weight, conv_bias, inner_dim, gn, out=None):
+    """SSM decode-step front end (``modules/ssm.py:173-186``): ``SSMCache.update``
+    (``inference/ssm_cache.py:38-43``, the cache window shifted left by one with ``hBC``
+    appended, in place in ``conv_ctx``), then ``(silu(conv_ctx) * weight).sum(-1) + bias``
+    with the reference's roundings to ``hBC``'s dtype, split into ``x`` (b, inner_dim),
+    ``B`` and ``C`` (b, gn). ``hBC`` (b, conv_dim) may be a slice of the projection output
+    (contiguous channels, any row stride); ``conv_ctx`` (b, conv_dim, K) contiguous, in
+    ``hBC``'s dtype. Returns ``(x, B, C)``."""
+    if hBC.dim() != 2:
+        raise ValueError(f"[hBC] expected (batch, conv_dim), got {tuple(hBC.shape)}")
+    b, conv_dim = hBC.shape
+    if conv_dim != inner_dim + 2 * gn:
+        raise ValueError(f"[hBC] conv_dim {conv_dim} != inner_dim + 2 * gn = {inner_dim + 2 * gn}")
+    w = conv_weight.reshape(conv_weight.shape[0], -1)
+    K = w.shape[1]
+    if w.shape[0] != conv_dim or not 1 <= K <= 8:
+        raise ValueError(f"[conv_weight] expected (conv_dim, 1, K) with K <= 8, got {tuple(conv_weight.shape)}")
+    if conv_ctx.shape != (b, conv_dim, K) or conv_ctx.dtype != hBC.dtype or not conv_ctx.is_contiguous():
+        raise ValueError(f"[conv_ctx] expected a contiguous {(b, conv_dim, K)} tensor of {hBC.dtype}")
+    dev = check_cuda([hBC, conv_ctx, conv_weight, conv_bias], ["hBC", "conv_ctx", "conv_weight", "conv_bias"])
+    if hBC.stride(1) != 1:
+        hBC = hBC.contiguous()
+    w = to_contiguous(w.float())
+    bias = None if conv_bias is None else to_contiguous(conv_bias.float())
+    if out is None:
+        x = torch.empty(b, inner_dim, dtype=hBC.dtype, device=hBC.device)
+        Bo = torch.empty(b, gn, dtype=hBC.dtype, device=hBC.device)
+        Co = torch.empty(b, gn, dtype=hBC.dtype, device=hBC.device)
+    else:
+        x, Bo, Co = out
+    st = _lib.lib().ssm_conv_decode(
+        _lib.ptr(hBC), hBC.stride(0), _lib.ptr(conv_ctx), _lib.ptr(w), _lib.ptr(bias), _lib.ptr(x), _lib.ptr(Bo),
+        _lib.ptr(Co), b, inner_dim, gn, K, _lib.dtype_code(hBC.dtype, "hBC"), _stream(dev))
+    _lib.check(st, "ssm_conv_decode")
+    return x, Bo, Co

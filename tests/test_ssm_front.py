@@ -97,3 +97,78 @@ def test_errors_before_launch():
         kernels.ssm_conv_prefill(hBC, torch.randn(20, 1, 4, device="cuda"), None, 10, 4)  # 10 + 8 != 20
     with pytest.raises(ValueError):
         kernels.ssm_conv_prefill(hBC, torch.randn(20, 1, 9, device="cuda"), None, 12, 4)  # K > 8
+
+
+DECODE_CASES = ["ssm_decode_fp32", "ssm_decode_bf16"]
+
+
+@pytest.mark.parametrize("case", DECODE_CASES)
+def test_decode_oracle_matches_reference_golden(case):
+    g = load_golden(case)
+    ctx = g["ctx0"].clone()
+    for hBC, o in zip(g["hBC"], g["out"]):
+        x, B, C, ctx = ssm_front_ref.decode_front(hBC, ctx, g["weight"], g["bias"], g["inner"], g["gn"])
+        close = assert_close_for(hBC.dtype)
+        close(x.float(), o["x"].float(), f"{case} x")
+        close(B.float(), o["B"].float(), f"{case} B")
+        close(C.float(), o["C"].float(), f"{case} C")
+        assert torch.equal(ctx, o["conv_ctx"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", DECODE_CASES)
+def test_decode_kernel_matches_reference_golden(case):
+    """Two steps in a row: the cache is updated in place and carried to the next step."""
+    from selective_attention_b200 import kernels
+
+    g = load_golden(case)
+    ctx = g["ctx0"].cuda().contiguous()
+    for hBC, o in zip(g["hBC"], g["out"]):
+        x, B, C = kernels.ssm_conv_decode(hBC.cuda(), ctx, g["weight"].cuda(), g["bias"].cuda(), g["inner"], g["gn"])
+        torch.cuda.synchronize()
+        close = assert_close_for(hBC.dtype)
+        close(x.float(), o["x"].float(), f"{case} x")
+        close(B.float(), o["B"].float(), f"{case} B")
+        close(C.float(), o["C"].float(), f"{case} C")
+        assert torch.equal(ctx.cpu(), o["conv_ctx"])
+
+
+@pytest.mark.gpu
+def test_decode_step_front_end_then_ssu_vs_oracle():
+    """A whole decode step of the SSM layer below the projections: the front end reads a
+    slice of a projection-shaped row, its x/B/C feed the SSU with D and the z gate
+    (modules/ssm.py:162-202), against the oracle composition."""
+    import math
+
+    from selective_attention_b200 import kernels
+    from oracle import ssd_ref
+
+    g = torch.Generator().manual_seed(11)
+    b, H, P, N, G, K = 5, 8, 64, 128, 1, 4
+    inner, gn = H * P, G * N
+    conv_dim = inner + 2 * gn
+    proj = torch.randn(b, conv_dim + inner + H, generator=g).to(torch.bfloat16)
+    hBC, z, dr = proj[:, :conv_dim], proj[:, conv_dim:conv_dim + inner], proj[:, conv_dim + inner:].float() - 4.0
+    ctx0 = torch.randn(b, conv_dim, K, generator=g).to(torch.bfloat16)
+    w = (torch.randn(conv_dim, 1, K, generator=g) * 0.5).to(torch.bfloat16)
+    bias = (torch.randn(conv_dim, generator=g) * 0.1).to(torch.bfloat16)
+    A = -torch.exp(torch.rand(H, generator=g) * math.log(16.0))
+    db = 0.1 * torch.randn(H, generator=g)
+    D = torch.randn(inner, generator=g)
+    h0 = 0.1 * torch.randn(b, H, P, N, generator=g)
+
+    ctx = ctx0.cuda().contiguous()
+    x, B, C = kernels.ssm_conv_decode(proj.cuda()[:, :conv_dim], ctx, w.cuda(), bias.cuda(), inner, gn)
+    h = h0.cuda().contiguous()
+    y, _ = kernels.ssu_forward(x.view(b, H, P), A.cuda(), B.view(b, G, N), C.view(b, G, N), dr.cuda(), db.cuda(), h,
+                               True, (0.0, float("inf")), D.cuda(), z.cuda().contiguous())
+    torch.cuda.synchronize()
+
+    xr, Br, Cr, ctxr = ssm_front_ref.decode_front(hBC, ctx0, w, bias, inner, gn)
+    yr, hr = ssd_ref.ssu_forward(xr.view(b, H, P).float(), A, Br.view(b, G, N).float(), Cr.view(b, G, N).float(),
+                                 dr, db, h0)
+    yr = ssd_ref.gate_epilogue(yr.reshape(b, 1, H, P), xr.view(b, 1, H, P), D, z.reshape(b, 1, inner)).view(b, H, P)
+    assert torch.equal(ctx.cpu(), ctxr)
+    assert_bf16_close(x.float(), xr.float(), "front x")
+    assert_bf16_close(y.float(), yr, "decode y")
+    assert_bf16_close(h, hr, "decode h")
