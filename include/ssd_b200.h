@@ -12,6 +12,8 @@
  * src/selective_attention/):
  *   ssd_scan_fwd           <- triton_kernels/ssd_scan/forward.py:223 ssd_scan_forward
  *                             (called from ops/ssd_scan.py:70 SSDScanFn.forward)
+ *   ssd_scan_bwd           <- triton_kernels/ssd_scan/backward.py:467 ssd_scan_backward
+ *                             (called from ops/ssd_scan.py:91 SSDScanFn.backward)
  *   ssd_chunk_cumsum_fwd   <- triton_kernels/ssd_scan/forward.py:14  chunk_cumsum_forward
  *   ssd_chunk_state_fwd    <- triton_kernels/ssd_scan/forward.py:62  chunk_state_forward
  *   ssd_state_passing_fwd  <- triton_kernels/ssd_scan/forward.py:102 state_passing_forward
@@ -177,6 +179,42 @@ int ssd_chunk_state_fwd(const ssd_params* p, void* stream);      /* u, B, dt, cu
 int ssd_state_passing_fwd(const ssd_params* p, void* stream);    /* states (in place), cum, h_init -> h_last */
 int ssd_bmm_chunk_fwd(const ssd_params* p, void* stream);        /* B, C -> CB (lower-triangular tiles) */
 int ssd_chunk_scan_fwd(const ssd_params* p, void* stream);       /* u, dt, cum, C, states, CB, D, z -> y */
+
+/*
+ * Gradients of the SSD scan (triton_kernels/ssd_scan/backward.py:467-555): the
+ * forward intermediates are recomputed, then the reference's stages run with the
+ * same maths and masking (rows at or past `length` get no gradient and their y_grad
+ * is ignored; clamped dt gets zero gradient; softplus gets sigmoid below 20).
+ * Inputs come from an ssd_params block that describes the forward call (u, A, B,
+ * C, delta_raw, delta_bias, h_init, length or cu_seqlens, chunk size, dt options;
+ * D, z and y are ignored) plus:
+ *   y_grad       (b, L, H, P)  y_grad_dtype (fp32 or x_dtype)
+ *   h_last_grad  (b, H, P, N)  fp32, or NULL for zero
+ * and writes
+ *   u_grad (b, L, H, P) x_dtype;  A_grad (H,) fp32;  B_grad, C_grad (b, L, G, N) fp32;
+ *   delta_raw_grad (b, L, H) dt_dtype;  delta_bias_grad (H,) fp32 (required iff
+ *   delta_bias is given);  h_init_grad (b, H, P, N) fp32 (required iff h_init is given)
+ * (the reference's output dtypes: backward.py:90,144,200,254,439-441). Supported shapes:
+ * headdim <= 64, dstate <= 128, both multiples of 4; chunk_size a multiple of 32 up
+ * to 256. Uses p->workspace (>= ssd_scan_bwd_workspace_size(p)); p->events, when
+ * set, are recorded before the first stage [0], after the state recompute [1], the
+ * state passes and CB [2], the state-side products [3], the intra-chunk products [4].
+ */
+typedef struct ssd_bwd_params {
+  const void* y_grad;
+  int32_t y_grad_dtype;
+  const float* h_last_grad;
+  void* u_grad;
+  float* A_grad;
+  float* B_grad;
+  float* C_grad;
+  void* delta_raw_grad;
+  float* delta_bias_grad;
+  float* h_init_grad;
+} ssd_bwd_params;
+
+size_t ssd_scan_bwd_workspace_size(const ssd_params* p);
+int ssd_scan_bwd(const ssd_params* p, const ssd_bwd_params* g, void* stream);
 
 /*
  * Selective state update, one token (triton_kernels/ssu/forward.py:7):

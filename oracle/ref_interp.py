@@ -52,3 +52,43 @@ def load():
         "chunk_scan_forward": fwd.chunk_scan_forward,
     }
     return _loaded
+
+
+_loaded_bwd = None
+
+
+def load_backward():
+    """Also pin the reference's backward kernels; returns ``ssd_scan_backward``.
+
+    Three host wrappers of the backward size their head splits from
+    ``torch.cuda.get_device_properties(device).multi_processor_count``
+    (``triton_kernels/ssd_scan/backward.py:197,251,301``), which has no CPU answer:
+    while this loader is in use it reports a 148-SM device for CPU tensors. The
+    split count only changes the order of the reference's fp32 sums.
+    """
+    global _loaded_bwd
+    if _loaded_bwd is not None:
+        return _loaded_bwd
+    ns = load()
+    import types
+
+    import torch
+    import selective_attention.triton_kernels.ssd_scan.backward_kernel as bk
+    for name in ("chunk_scan_backward_h_kernel", "state_passing_backward_kernel",
+                 "chunk_scan_chunk_state_backward_u_kernel", "chunk_state_backward_B_kernel",
+                 "chunk_scan_backward_C_grad_kernel", "chunk_scan_backward_CB_kernel",
+                 "bmm_chunk_backward_kernel", "chunk_scan_backward_decay_cumsum_kernel",
+                 "chunk_cumsum_backward_kernel"):
+        k = getattr(bk, name)
+        k.configs = [k.configs[-1]]
+    real = torch.cuda.get_device_properties
+
+    def props(device=None):
+        if device is None or torch.device(device).type == "cpu":
+            return types.SimpleNamespace(multi_processor_count=148)
+        return real(device)
+
+    torch.cuda.get_device_properties = props
+    from selective_attention.triton_kernels.ssd_scan import backward as bwd
+    _loaded_bwd = dict(ns, ssd_scan_backward=bwd.ssd_scan_backward)
+    return _loaded_bwd

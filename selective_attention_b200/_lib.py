@@ -36,6 +36,8 @@ EXPORTS = {
     "ssd_scan_fwd_workspace_size": (c_size_t, [c_void_p]),
     "ssd_scan_fwd": (c_int, [c_void_p, c_void_p]),
     "ssd_scan_fwd_noalloc": (c_int, [c_void_p, c_void_p]),
+    "ssd_scan_bwd_workspace_size": (c_size_t, [c_void_p]),
+    "ssd_scan_bwd": (c_int, [c_void_p, c_void_p, c_void_p]),
     "ssd_chunk_cumsum_fwd": (c_int, [c_void_p, c_void_p]),
     "ssd_chunk_state_fwd": (c_int, [c_void_p, c_void_p]),
     "ssd_state_passing_fwd": (c_int, [c_void_p, c_void_p]),
@@ -60,6 +62,16 @@ class SSDParams(ctypes.Structure):
         ("cu_seqlens", c_void_p), ("y", c_void_p), ("h_last", c_void_p), ("dt", c_void_p), ("cum", c_void_p),
         ("states", c_void_p), ("CB", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
         ("events", c_void_p * 6),
+    ]
+
+
+class SSDBwdParams(ctypes.Structure):
+    """Mirror of ``ssd_bwd_params`` in include/ssd_b200.h."""
+
+    _fields_ = [
+        ("y_grad", c_void_p), ("y_grad_dtype", c_int32), ("h_last_grad", c_void_p), ("u_grad", c_void_p),
+        ("A_grad", c_void_p), ("B_grad", c_void_p), ("C_grad", c_void_p), ("delta_raw_grad", c_void_p),
+        ("delta_bias_grad", c_void_p), ("h_init_grad", c_void_p),
     ]
 
 

@@ -273,6 +273,111 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
   return SSD_OK;
 }
 
+// ------------------------------------------------------------- backward
+namespace {
+
+size_t carve_bwd(const Geometry& g, uint8_t* base, BwdArgs* a, ChunkEntry** table, int2** rows, int** count) {
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* ptr = base ? base + off : nullptr;
+    off += align_up(n);
+    return reinterpret_cast<float*>(ptr);
+  };
+  const size_t nk = (size_t)g.nchunks, H = (size_t)g.H, PN = (size_t)g.P * g.N, cs = (size_t)g.cs;
+  BwdArgs dummy{};
+  BwdArgs& w = a ? *a : dummy;
+  w.dt = take(nk * H * cs * 4);
+  w.cum = take(nk * H * cs * 4);
+  w.states = take(nk * H * PN * 4);
+  w.hg = take(nk * H * PN * 4);
+  w.CB = take(nk * g.G * cs * cs * 4);
+  w.CBg = take(nk * g.G * cs * cs * 4);
+  w.accS = take(nk * H * cs * g.P * 4);
+  w.gC = take(nk * H * cs * 4);
+  w.dl_part = take(nk * H * bwd_dl_slices(g.P, g.N) * 4);
+  w.A_part = take(nk * H * 4);
+  w.bias_part = take(nk * H * 4);
+  ChunkEntry* t = nullptr;
+  int2* r = nullptr;
+  int* c = nullptr;
+  if (g.packed) {
+    t = reinterpret_cast<ChunkEntry*>(take(nk * sizeof(ChunkEntry)));
+    r = reinterpret_cast<int2*>(take((size_t)g.nrows * sizeof(int2)));
+    c = reinterpret_cast<int*>(take(sizeof(int)));
+  }
+  if (table) *table = t;
+  if (rows) *rows = r;
+  if (count) *count = c;
+  return off;
+}
+
+}  // namespace
+
+extern "C" size_t ssd_scan_bwd_workspace_size(const ssd_params* p) {
+  Geometry g;
+  if (geometry(p, g) != SSD_OK || !bwd_supported(g.P, g.N, g.cs)) return 0;
+  return carve_bwd(g, nullptr, nullptr, nullptr, nullptr, nullptr);
+}
+
+extern "C" int ssd_scan_bwd(const ssd_params* p, const ssd_bwd_params* gr, void* stream) {
+  Geometry g;
+  int st = geometry(p, g);
+  if (st) return st;
+  if (!gr) return SSD_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(p->x_dtype) || !dtype_ok(p->dt_dtype) || !dtype_ok(gr->y_grad_dtype))
+    return SSD_ERR_UNSUPPORTED_DTYPE;
+  if (!bwd_supported(g.P, g.N, g.cs)) return SSD_ERR_INVALID_ARGUMENT;
+  if (!p->u || !p->A || !p->B || !p->C || !p->delta_raw || !p->workspace || !gr->y_grad || !gr->u_grad ||
+      !gr->A_grad || !gr->B_grad || !gr->C_grad || !gr->delta_raw_grad)
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (!p->delta_bias != !gr->delta_bias_grad || !p->h_init != !gr->h_init_grad) return SSD_ERR_INVALID_ARGUMENT;
+  if (!aligned16(gr->B_grad) || !aligned16(gr->C_grad) || (p->h_init && !aligned16(p->h_init)) ||
+      (gr->h_init_grad && !aligned16(gr->h_init_grad)) || (gr->h_last_grad && !aligned16(gr->h_last_grad)))
+    return SSD_ERR_INVALID_ARGUMENT;
+  if ((long long)g.nchunks > 65535 || g.H > 65535 || g.nrows > 65535) return SSD_ERR_INVALID_ARGUMENT;
+  BwdArgs a{};
+  ChunkEntry* table;
+  int2* rows;
+  int* count;
+  const size_t need = carve_bwd(g, reinterpret_cast<uint8_t*>(p->workspace), &a, &table, &rows, &count);
+  if (p->workspace_bytes < need) return SSD_ERR_WORKSPACE_TOO_SMALL;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  Workspace w{};
+  w.table = table;
+  w.rows = rows;
+  w.count = count;
+  LaunchCtx c = make_ctx(p, g, s, &w);
+  record(p, 0, s);
+  if (g.packed) {
+    st = cuda_status(launch_build_chunk_table(s, p->cu_seqlens, p->cu_dtype == 64, (int)p->nseq, g.cs, table, rows,
+                                              count));
+    if (st) return st;
+  }
+  a.x_dtype = p->x_dtype;
+  a.dt_dtype = p->dt_dtype;
+  a.y_dtype = gr->y_grad_dtype;
+  a.u = p->u;
+  a.A = p->A;
+  a.B = p->B;
+  a.C = p->C;
+  a.delta_raw = p->delta_raw;
+  a.delta_bias = p->delta_bias;
+  a.h_init = p->h_init;
+  a.y_grad = gr->y_grad;
+  a.h_last_grad = gr->h_last_grad;
+  a.u_grad = gr->u_grad;
+  a.A_grad = gr->A_grad;
+  a.B_grad = gr->B_grad;
+  a.C_grad = gr->C_grad;
+  a.delta_raw_grad = gr->delta_raw_grad;
+  a.delta_bias_grad = gr->delta_bias_grad;
+  a.h_init_grad = gr->h_init_grad;
+  for (int i = 0; i < 6; ++i) a.ev[i] = reinterpret_cast<cudaEvent_t>(p->events[i]);
+  if ((st = cuda_status(launch_ssd_bwd(c, a)))) return st;
+  record(p, 5, s);
+  return SSD_OK;
+}
+
 // ------------------------------------------------------------- stage entries
 static int stage_prologue(const ssd_params* p, Geometry& g) {
   int st = geometry(p, g);

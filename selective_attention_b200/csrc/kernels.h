@@ -35,6 +35,33 @@ cudaError_t launch_simt_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype,
                                    const float* D, const void* z, void* y);
 unsigned int fetch_error_simt(cudaStream_t s);
 
+// ssd_bwd.cu (CUDA-core backward; P <= 64, N <= 128, chunk 32..256 in steps of 32)
+struct BwdArgs {
+  int x_dtype, dt_dtype, y_dtype;
+  const void* u;
+  const float* A;
+  const void* B;
+  const void* C;
+  const void* delta_raw;
+  const float* delta_bias;
+  const float* h_init;
+  const void* y_grad;
+  const float* h_last_grad;
+  void* u_grad;
+  float* A_grad;
+  float* B_grad;
+  float* C_grad;
+  void* delta_raw_grad;
+  float* delta_bias_grad;
+  float* h_init_grad;
+  // workspace
+  float *dt, *cum, *states, *hg, *CB, *CBg, *accS, *gC, *dl_part, *A_part, *bias_part;
+  cudaEvent_t ev[6];
+};
+bool bwd_supported(int P, int N, int cs);
+size_t bwd_dl_slices(int P, int N);
+cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a);
+
 // ssd_tc.cu (tcgen05 + TMA; bf16/fp16 inputs, P = 64, N = 128, cs = 256; prev16 in the input type)
 bool tc_supported(int x_dtype, int P, int N, int cs);
 // delta_raw == NULL: dt / cum are inputs; otherwise chunk_cumsum is fused in and they are written.

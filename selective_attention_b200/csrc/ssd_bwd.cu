@@ -1,0 +1,902 @@
+// ssd_bwd.cu - SSD chunked-scan backward (triton_kernels/ssd_scan/backward.py:467-555).
+//
+// The reference recomputes the forward intermediates and runs nine kernels with
+// fp32 intermediates in HBM. Here the same maths runs as six CUDA-core kernels
+// (fp32 FFMA, operands staged in shared memory, register-tiled), with the work of
+// several reference kernels merged where they share operands:
+//   bwd_chunk_states   chunk states S (forward recompute) and the intra-chunk state
+//                      gradient sum_l y_grad exp(cum) C, one pass over the chunk
+//   bwd_state_pass     forward recurrence (S -> prev states, in place) and the
+//                      reverse recurrence (state gradients, decay_last gradient,
+//                      h_init gradient) in one kernel per (row, head, 1024 elements)
+//   bwd_cb             CB = C B^T for the lower tiles of each chunk
+//   bwd_state_grad     the state-side products: B h_grad^T (for u_grad), u h_grad
+//                      (B_grad), y_grad prev (C_grad) and the C-side decay gradient
+//   bwd_intra          the intra-chunk products: CB^T y_grad (u_grad), y_grad u^T
+//                      (CB_grad), the intra-chunk and B-side decay gradients, and
+//                      the dt transform's backward (delta_raw_grad, A / bias partials)
+//   bwd_bmm            CB_grad^T C into B_grad and CB_grad B into C_grad
+// Group sums over heads (B_grad, C_grad, CB_grad) are fp32 atomic adds in L2.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace ssdb200 {
+namespace {
+
+__device__ __forceinline__ float ld_any(const void* p, long long i, int dt) {
+  if (dt == SSD_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  if (dt == SSD_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return static_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void st_any(void* p, long long i, int dt, float v) {
+  if (dt == SSD_BF16) static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else if (dt == SSD_F16) static_cast<__half*>(p)[i] = __float2half_rn(v);
+  else static_cast<float*>(p)[i] = v;
+}
+
+__device__ __forceinline__ float4 lds4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+__device__ __forceinline__ float comp(const float4& v, int q) {
+  return q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
+}
+
+__device__ __forceinline__ float dot4(const float4& a, const float4& b, float acc) {
+  acc = fmaf(a.x, b.x, acc);
+  acc = fmaf(a.y, b.y, acc);
+  acc = fmaf(a.z, b.z, acc);
+  return fmaf(a.w, b.w, acc);
+}
+
+// Sum over the 16 lanes of a half warp (lanes sharing tid >> 4).
+__device__ __forceinline__ float half_warp_sum(float v) {
+#pragma unroll
+  for (int off = 1; off < 16; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Exclusive prefix sum over a 256-thread block (one value per thread); `tmp` holds
+// 8 floats of shared memory. Also returns the block total.
+__device__ __forceinline__ float block_excl_scan(float v, float* tmp, float& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float x = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const float y = __shfl_up_sync(0xffffffffu, x, off);
+    if (lane >= off) x += y;
+  }
+  if (lane == 31) tmp[warp] = x;
+  __syncthreads();
+  float before = 0.f, all = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const float t = tmp[w];
+    if (w < warp) before += t;
+    all += t;
+  }
+  __syncthreads();
+  total = all;
+  return before + x - v;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* tmp) {
+  float total;
+  block_excl_scan(v, tmp, total);
+  return total;
+}
+
+constexpr int kLT = 32;        // token rows per tile
+constexpr int kPmax = 64, kNmax = 128, kCSmax = 256;
+constexpr int kLDT = kLT + 4;  // [feature][token] tiles
+constexpr int kLDN = kNmax + 4;
+constexpr int kLDP = kPmax + 4;
+
+// ===========================================================================
+// bwd_chunk_states: per (chunk, head)
+//   S[p,n]  = sum_{l<lim} u[l,p] exp(min(cum_last - cum_l, 0)) dt_l B[l,n]
+//             (chunk_state forward, backward.py:487)
+//   HG[p,n] = sum_{l<len} y_grad[l,p] exp(cum_l) C[l,n]   (backward_kernel.py:23-93)
+// Thread (tp, tn) owns p = tp + 16 i (i < 4), n = tn + 16 j (j < 8) of both.
+// ===========================================================================
+__global__ void __launch_bounds__(256) bwd_chunk_states_kernel(
+    const void* __restrict__ u, const void* __restrict__ Bm, const void* __restrict__ Cm,
+    const void* __restrict__ yg, const float* __restrict__ dt, const float* __restrict__ cum,
+    float* __restrict__ states, float* __restrict__ hg, ChunkMap cm, int H, int G, int P, int N, int xdt,
+    int ydt) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int h = blockIdx.x, k = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int cs = cm.cs, g = h / (H / G), tid = threadIdx.x;
+  float* xw = sm;                   // [kPmax][kLDT]
+  float* ye = xw + kPmax * kLDT;    // [kPmax][kLDT]
+  float* bt = ye + kPmax * kLDT;    // [kNmax][kLDT]
+  float* ct = bt + kNmax * kLDT;    // [kNmax][kLDT]
+  float* dts = ct + kNmax * kLDT;   // [kCSmax]
+  float* cms = dts + kCSmax;        // [kCSmax]
+  const long long kh = (long long)k * H + h;
+  for (int i = tid; i < cs; i += 256) {
+    dts[i] = dt[kh * cs + i];
+    cms[i] = cum[kh * cs + i];
+  }
+  __syncthreads();
+  const float clast = cms[cs - 1];
+  const int tp = tid >> 4, tn = tid & 15;
+  int pr[4], nr[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) pr[i] = min(tp + 16 * i, P - 1) * kLDT;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) nr[j] = min(tn + 16 * j, N - 1) * kLDT;
+  float aS[4][8], aH[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) aS[i][j] = aH[i][j] = 0.f;
+
+  for (int l0 = 0; l0 < ci.lim; l0 += kLT) {
+    __syncthreads();
+    for (int idx = tid; idx < kLT * P; idx += 256) {
+      const int l = idx / P, p = idx - l * P, t = l0 + l;
+      float xv = 0.f, yv = 0.f;
+      if (t < ci.lim) {
+        const long long off = ((ci.tok0 + t) * H + h) * (long long)P + p;
+        xv = ld_any(u, off, xdt) * (expf(fminf(clast - cms[t], 0.f)) * dts[t]);
+        if (t < ci.vlim) yv = ld_any(yg, off, ydt) * expf(cms[t]);
+      }
+      xw[p * kLDT + l] = xv;
+      ye[p * kLDT + l] = yv;
+    }
+    for (int idx = tid; idx < kLT * N; idx += 256) {
+      const int l = idx / N, n = idx - l * N, t = l0 + l;
+      float bv = 0.f, cv = 0.f;
+      if (t < ci.lim) {
+        const long long off = ((ci.tok0 + t) * G + g) * (long long)N + n;
+        bv = ld_any(Bm, off, xdt);
+        if (t < ci.vlim) cv = ld_any(Cm, off, xdt);
+      }
+      bt[n * kLDT + l] = bv;
+      ct[n * kLDT + l] = cv;
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int l = 0; l < kLT; l += 4) {
+      float4 a[4], b[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = lds4(xw + pr[i] + l);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b[j] = lds4(bt + nr[j] + l);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) aS[i][j] = dot4(a[i], b[j], aS[i][j]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = lds4(ye + pr[i] + l);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) b[j] = lds4(ct + nr[j] + l);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) aH[i][j] = dot4(a[i], b[j], aH[i][j]);
+    }
+  }
+  const long long base = kh * P * N;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int p = tp + 16 * i;
+    if (p >= P) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int n = tn + 16 * j;
+      if (n < N) {
+        states[base + p * N + n] = aS[i][j];
+        hg[base + p * N + n] = aH[i][j];
+      }
+    }
+  }
+}
+
+// ===========================================================================
+// bwd_state_pass: per (row, head, 1024 state elements), 4 elements per thread.
+// Forward (forward_kernel.py:244-249): states[c] <- prev; prev = exp(cl_c) prev + S_c.
+// Reverse (backward_kernel.py:144-157), g = gradient of the state leaving chunk c:
+//   dlast_c = sum(prev_c * g) * exp(cl_c)   (per-CTA partial, summed by bwd_intra)
+//   hg[c] <- g;  g = exp(cl_c) g + hg_intra[c];   h_init_grad = g after chunk 0.
+// ===========================================================================
+__global__ void __launch_bounds__(256) bwd_state_pass_kernel(
+    float* __restrict__ states, float* __restrict__ hg, const float* __restrict__ cum,
+    const float* __restrict__ h_init, const float* __restrict__ h_last_grad, float* __restrict__ h_init_grad,
+    float* __restrict__ dl_part, ChunkMap cm, int H, int PN) {
+  __shared__ float tmp[8];
+  const int row = blockIdx.z, h = blockIdx.y, nsl = gridDim.x;
+  const int e0 = (blockIdx.x * 256 + threadIdx.x) * 4;
+  const bool act = e0 < PN;
+  int first, count;
+  if (cm.packed) {
+    const int2 r = cm.rows[row];
+    first = r.x;
+    count = r.y;
+  } else {
+    first = row * cm.nc;
+    count = cm.nc;
+  }
+  const int cs = cm.cs;
+  const long long hoff = ((long long)row * H + h) * PN + e0;
+  float4 prev = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (h_init && act) prev = *reinterpret_cast<const float4*>(h_init + hoff);
+  for (int c = 0; c < count; ++c) {
+    const long long kk = first + c;
+    const long long off = (kk * H + h) * PN + e0;
+    const float sc = expf(cum[(kk * H + h) * cs + cs - 1]);
+    if (act) {
+      const float4 s = *reinterpret_cast<const float4*>(states + off);
+      *reinterpret_cast<float4*>(states + off) = prev;
+      prev.x = fmaf(sc, prev.x, s.x);
+      prev.y = fmaf(sc, prev.y, s.y);
+      prev.z = fmaf(sc, prev.z, s.z);
+      prev.w = fmaf(sc, prev.w, s.w);
+    }
+  }
+  float4 gr = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (h_last_grad && act) gr = *reinterpret_cast<const float4*>(h_last_grad + hoff);
+  for (int c = count - 1; c >= 0; --c) {
+    const long long kk = first + c;
+    const long long off = (kk * H + h) * PN + e0;
+    const float sc = expf(cum[(kk * H + h) * cs + cs - 1]);
+    float part = 0.f;
+    float4 hgi = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (act) {
+      const float4 pv = *reinterpret_cast<const float4*>(states + off);
+      part = dot4(pv, gr, 0.f);
+      hgi = *reinterpret_cast<const float4*>(hg + off);
+      *reinterpret_cast<float4*>(hg + off) = gr;
+    }
+    const float tot = block_sum(part, tmp);
+    if (threadIdx.x == 0) dl_part[(kk * H + h) * nsl + blockIdx.x] = tot * sc;
+    gr.x = fmaf(sc, gr.x, hgi.x);
+    gr.y = fmaf(sc, gr.y, hgi.y);
+    gr.z = fmaf(sc, gr.z, hgi.z);
+    gr.w = fmaf(sc, gr.w, hgi.w);
+  }
+  if (h_init_grad && act) *reinterpret_cast<float4*>(h_init_grad + hoff) = gr;
+}
+
+// ===========================================================================
+// bwd_cb: CB[l,s] = sum_n C[l,n] B[s,n] (forward_kernel.py:270-328) for the lower
+// 64x64 tiles of each chunk; rows / columns past seq_len are zero.
+// ===========================================================================
+__global__ void __launch_bounds__(256) bwd_cb_kernel(const void* __restrict__ Bm, const void* __restrict__ Cm,
+                                                     float* __restrict__ CB, ChunkMap cm, int G, int N, int xdt) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int k = blockIdx.z, g = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  int t = blockIdx.x, ti = 0;
+  while (t > ti) {
+    t -= ti + 1;
+    ++ti;
+  }
+  const int tj = t, cs = cm.cs, l0 = ti * 64, s0 = tj * 64, tid = threadIdx.x;
+  float* cS = sm;               // [64][kLDN]
+  float* bS = sm + 64 * kLDN;   // [64][kLDN]
+  for (int idx = tid; idx < 64 * N; idx += 256) {
+    const int r = idx / N, n = idx - r * N;
+    const int l = l0 + r, s = s0 + r;
+    cS[r * kLDN + n] = l < ci.lim ? ld_any(Cm, ((ci.tok0 + l) * G + g) * (long long)N + n, xdt) : 0.f;
+    bS[r * kLDN + n] = s < ci.lim ? ld_any(Bm, ((ci.tok0 + s) * G + g) * (long long)N + n, xdt) : 0.f;
+  }
+  __syncthreads();
+  const int ty = tid >> 4, tx = tid & 15;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int n = 0; n < N; n += 4) {
+    float4 a[4], b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = lds4(cS + (ty + 16 * i) * kLDN + n);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) b[j] = lds4(bS + (tx + 16 * j) * kLDN + n);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = dot4(a[i], b[j], acc[i][j]);
+  }
+  float* out = CB + ((long long)k * G + g) * cs * cs;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int l = l0 + ty + 16 * i;
+    if (l >= cs) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int s = s0 + tx + 16 * j;
+      if (s < cs) out[l * cs + s] = acc[i][j];
+    }
+  }
+}
+
+// ===========================================================================
+// bwd_state_grad: per (chunk, head), 32-token row tiles. With scale_l =
+// exp(min(cum_last - cum_l, 0)):
+//   accS[l,p] = scale_l sum_n B[l,n] hg[p,n]             (backward_kernel.py:255-262)
+//   B_grad[l,:] += scale_l dt_l sum_p u[l,p] hg[p,:]       (:402-415)
+//   C_grad[l,:] += exp(cum_l) sum_p y_grad[l,p] prev[p,:]  (:522-533)
+//   gC[l] = sum_n (that C_grad row) C[l,n]                 (:537-538)
+// accS goes to a scratch buffer for bwd_intra; rows at or past `length` are zero.
+// ===========================================================================
+__global__ void __launch_bounds__(256) bwd_state_grad_kernel(
+    const void* __restrict__ u, const void* __restrict__ Bm, const void* __restrict__ Cm,
+    const void* __restrict__ yg, const float* __restrict__ dt, const float* __restrict__ cum,
+    const float* __restrict__ prev, const float* __restrict__ hg, float* __restrict__ accS_out,
+    float* __restrict__ Bgrad, float* __restrict__ Cgrad, float* __restrict__ gC_out, ChunkMap cm, int H, int G,
+    int P, int N, int xdt, int ydt) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int h = blockIdx.x, k = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int cs = cm.cs, g = h / (H / G), tid = threadIdx.x;
+  float* hgS = sm;                  // [kPmax][kLDN]
+  float* pvS = hgS + kPmax * kLDN;  // [kPmax][kLDN]
+  float* bt = pvS + kPmax * kLDN;   // [kLT][kLDN]
+  float* ct = bt + kLT * kLDN;      // [kLT][kLDN]
+  float* uw = ct + kLT * kLDN;      // [kLT][kLDP]
+  float* ye = uw + kLT * kLDP;      // [kLT][kLDP]
+  float* dts = ye + kLT * kLDP;     // [kCSmax]
+  float* cms = dts + kCSmax;        // [kCSmax]
+  const long long kh = (long long)k * H + h;
+  const float* hgk = hg + kh * P * N;
+  const float* pvk = prev + kh * P * N;
+  for (int idx = tid * 4; idx < P * N; idx += 1024) {
+    const int p = idx / N, n = idx - p * N;
+    *reinterpret_cast<float4*>(hgS + p * kLDN + n) = *reinterpret_cast<const float4*>(hgk + idx);
+    *reinterpret_cast<float4*>(pvS + p * kLDN + n) = *reinterpret_cast<const float4*>(pvk + idx);
+  }
+  for (int i = tid; i < cs; i += 256) {
+    dts[i] = dt[kh * cs + i];
+    cms[i] = cum[kh * cs + i];
+  }
+  __syncthreads();
+  const float clast = cms[cs - 1];
+  const int vl = ci.vlim;
+  const int tl = tid >> 4, tq = tid & 15;
+  int prow[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) prow[j] = min(tq + 16 * j, P - 1) * kLDN;
+
+  for (int l0 = 0; l0 < ci.lim; l0 += kLT) {
+    __syncthreads();
+    for (int idx = tid; idx < kLT * N; idx += 256) {
+      const int l = idx / N, n = idx - l * N, t = l0 + l;
+      float bv = 0.f, cv = 0.f;
+      if (t < vl) {
+        const long long off = ((ci.tok0 + t) * G + g) * (long long)N + n;
+        bv = ld_any(Bm, off, xdt);
+        cv = ld_any(Cm, off, xdt);
+      }
+      bt[l * kLDN + n] = bv;
+      ct[l * kLDN + n] = cv;
+    }
+    for (int idx = tid; idx < kLT * P; idx += 256) {
+      const int l = idx / P, p = idx - l * P, t = l0 + l;
+      float uv = 0.f, yv = 0.f;
+      if (t < vl) {
+        const long long off = ((ci.tok0 + t) * H + h) * (long long)P + p;
+        uv = ld_any(u, off, xdt) * (expf(fminf(clast - cms[t], 0.f)) * dts[t]);
+        yv = ld_any(yg, off, ydt) * expf(cms[t]);
+      }
+      uw[l * kLDP + p] = uv;
+      ye[l * kLDP + p] = yv;
+    }
+    __syncthreads();
+
+    // accS: rows l = tl + 16 i, columns p = tq + 16 j
+    float aS[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) aS[i][j] = 0.f;
+    for (int n = 0; n < N; n += 4) {
+      float4 a[2], b[4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) a[i] = lds4(bt + (tl + 16 * i) * kLDN + n);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = lds4(hgS + prow[j] + n);
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) aS[i][j] = dot4(a[i], b[j], aS[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int l = l0 + tl + 16 * i;
+      if (l >= cs) continue;
+      const float sc = l < vl ? expf(fminf(clast - cms[l], 0.f)) : 0.f;
+      float* o = accS_out + (kh * cs + l) * P;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int p = tq + 16 * j;
+        if (p < P) o[p] = aS[i][j] * sc;
+      }
+    }
+
+    // B_grad / C_grad rows: l = tl + 16 i, columns n = 4 tq + 64 jj + (0..3)
+    float bA[2][8], cA[2][8];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) bA[i][j] = cA[i][j] = 0.f;
+    for (int p = 0; p < P; p += 4) {
+      float4 au[2], ay[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        au[i] = lds4(uw + (tl + 16 * i) * kLDP + p);
+        ay[i] = lds4(ye + (tl + 16 * i) * kLDP + p);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float* hr = hgS + (p + q) * kLDN + 4 * tq;
+        const float* vr = pvS + (p + q) * kLDN + 4 * tq;
+        const float4 h0 = lds4(hr), h1 = lds4(hr + 64), v0 = lds4(vr), v1 = lds4(vr + 64);
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float a = comp(au[i], q), y = comp(ay[i], q);
+          bA[i][0] = fmaf(a, h0.x, bA[i][0]);
+          bA[i][1] = fmaf(a, h0.y, bA[i][1]);
+          bA[i][2] = fmaf(a, h0.z, bA[i][2]);
+          bA[i][3] = fmaf(a, h0.w, bA[i][3]);
+          bA[i][4] = fmaf(a, h1.x, bA[i][4]);
+          bA[i][5] = fmaf(a, h1.y, bA[i][5]);
+          bA[i][6] = fmaf(a, h1.z, bA[i][6]);
+          bA[i][7] = fmaf(a, h1.w, bA[i][7]);
+          cA[i][0] = fmaf(y, v0.x, cA[i][0]);
+          cA[i][1] = fmaf(y, v0.y, cA[i][1]);
+          cA[i][2] = fmaf(y, v0.z, cA[i][2]);
+          cA[i][3] = fmaf(y, v0.w, cA[i][3]);
+          cA[i][4] = fmaf(y, v1.x, cA[i][4]);
+          cA[i][5] = fmaf(y, v1.y, cA[i][5]);
+          cA[i][6] = fmaf(y, v1.z, cA[i][6]);
+          cA[i][7] = fmaf(y, v1.w, cA[i][7]);
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int lr = tl + 16 * i, l = l0 + lr;
+      float gsum = 0.f;
+      if (l < vl) {
+        const long long row = ((ci.tok0 + l) * G + g) * (long long)N;
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int n0 = 4 * tq + 64 * jj;
+          if (n0 < N) {
+            atomicAdd(reinterpret_cast<float4*>(Bgrad + row + n0),
+                      make_float4(bA[i][4 * jj], bA[i][4 * jj + 1], bA[i][4 * jj + 2], bA[i][4 * jj + 3]));
+            atomicAdd(reinterpret_cast<float4*>(Cgrad + row + n0),
+                      make_float4(cA[i][4 * jj], cA[i][4 * jj + 1], cA[i][4 * jj + 2], cA[i][4 * jj + 3]));
+            const float4 cr = lds4(ct + lr * kLDN + n0);
+            gsum = fmaf(cA[i][4 * jj], cr.x, gsum);
+            gsum = fmaf(cA[i][4 * jj + 1], cr.y, gsum);
+            gsum = fmaf(cA[i][4 * jj + 2], cr.z, gsum);
+            gsum = fmaf(cA[i][4 * jj + 3], cr.w, gsum);
+          }
+        }
+      }
+      gsum = half_warp_sum(gsum);
+      if (tq == 0 && l < cs) gC_out[kh * cs + l] = l < vl ? gsum : 0.f;
+    }
+  }
+}
+
+// ===========================================================================
+// bwd_intra: per (chunk, head); u and y_grad of the whole chunk in shared memory.
+//   accY[l,p] = sum_{l<=s<len} CB[s,l] exp(min(cum_s - cum_l, 0)) y_grad[s,p]   (:272-293)
+//   acc = accS + accY;  u_grad = acc dt_l;  ddt[l] = sum_p acc u  (:296-314)
+//   gB[l] = dt_l sum_p accS u  (= sum_n B_grad contribution * B, :417-421)
+//   CB_grad[l,s] += (y_grad[l] . u[s]) dt_s exp(min(cum_l - cum_s, 0)), s <= l  (:632-659)
+//   w[l,s] = CB_grad_h[l,s] CB[l,s] (s < l):  row sums and column sums give the
+//   intra-chunk decay gradient decay[j] = sum_{m<j} (col_m - row_m)  (:847-895)
+// then the dt backward (:984-1039):
+//   total = decay_intra + excl_cumsum(gB shifted) + rev_cumsum(gC) + dlast
+//   delta_raw_grad = (total A + ddt), 0 where dt was clamped, * sigmoid(pre) (softplus)
+//   A / bias partials per (chunk, head).
+// ===========================================================================
+__global__ void __launch_bounds__(256) bwd_intra_kernel(
+    const void* __restrict__ u, const void* __restrict__ yg, const void* __restrict__ delta_raw,
+    const float* __restrict__ A, const float* __restrict__ delta_bias, const float* __restrict__ dt,
+    const float* __restrict__ cum, const float* __restrict__ CB, const float* __restrict__ accS,
+    const float* __restrict__ gC, const float* __restrict__ dl_part, int nsl, float* __restrict__ CBg,
+    void* __restrict__ u_grad, void* __restrict__ draw_grad, float* __restrict__ A_part,
+    float* __restrict__ bias_part, ChunkMap cm, int H, int G, int P, int xdt, int ydt, int ddt_dtype, int use_sp,
+    float dmin, float dmax) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int h = blockIdx.x, k = blockIdx.y, tid = threadIdx.x;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) {
+    if (tid == 0) {
+      A_part[(long long)k * H + h] = 0.f;
+      bias_part[(long long)k * H + h] = 0.f;
+    }
+    return;
+  }
+  const int cs = cm.cs, g = h / (H / G), vl = ci.vlim;
+  constexpr int LDS = kLT + 4;
+  float* uS = sm;                     // [kCSmax][kLDP]
+  float* yS = uS + kCSmax * kLDP;     // [kCSmax][kLDP]
+  float* Mt = yS + kCSmax * kLDP;     // [kLT][LDS]
+  float* dts = Mt + kLT * LDS;        // [kCSmax] each below
+  float* cms = dts + kCSmax;
+  float* rows = cms + kCSmax;
+  float* cols = rows + kCSmax;
+  float* ddts = cols + kCSmax;
+  float* gBs = ddts + kCSmax;
+  float* revc = gBs + kCSmax;
+  float* tmp = revc + kCSmax;         // [8]
+  const long long kh = (long long)k * H + h;
+  const long long kg = ((long long)k * G + g) * cs * cs;
+  for (int idx = tid; idx < cs * P; idx += 256) {
+    const int l = idx / P, p = idx - l * P;
+    float uv = 0.f, yv = 0.f;
+    if (l < vl) {
+      const long long off = ((ci.tok0 + l) * H + h) * (long long)P + p;
+      uv = ld_any(u, off, xdt);
+      yv = ld_any(yg, off, ydt);
+    }
+    uS[l * kLDP + p] = uv;
+    yS[l * kLDP + p] = yv;
+  }
+  for (int i = tid; i < kCSmax; i += 256) {
+    dts[i] = i < cs ? dt[kh * cs + i] : 0.f;
+    cms[i] = i < cs ? cum[kh * cs + i] : 0.f;
+    rows[i] = cols[i] = ddts[i] = gBs[i] = 0.f;
+  }
+  __syncthreads();
+  const int tl = tid >> 4, tq = tid & 15;
+  const int p0 = 4 * tq;
+  const bool pvalid = p0 < P;
+
+  for (int l0 = 0; l0 < ci.lim; l0 += kLT) {
+    // accY: rows l = l0 + tl + 16 i, columns p0 .. p0 + 3
+    float aY[2][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) aY[i][j] = 0.f;
+    for (int s0 = l0; s0 < vl; s0 += kLT) {
+      __syncthreads();
+      for (int idx = tid; idx < kLT * kLT; idx += 256) {
+        const int r = idx & (kLT - 1), c = idx >> 5;
+        const int l = l0 + r, s = s0 + c;
+        float v = 0.f;
+        if (s >= l && s < vl && l < vl) v = CB[kg + (long long)s * cs + l] * expf(fminf(cms[s] - cms[l], 0.f));
+        Mt[r * LDS + c] = v;
+      }
+      __syncthreads();
+      if (pvalid) {
+#pragma unroll 2
+        for (int c = 0; c < kLT; c += 4) {
+          float4 a[2];
+#pragma unroll
+          for (int i = 0; i < 2; ++i) a[i] = lds4(Mt + (tl + 16 * i) * LDS + c);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 y4 = lds4(yS + (s0 + c + q) * kLDP + p0);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+              const float m = comp(a[i], q);
+              aY[i][0] = fmaf(m, y4.x, aY[i][0]);
+              aY[i][1] = fmaf(m, y4.y, aY[i][1]);
+              aY[i][2] = fmaf(m, y4.z, aY[i][2]);
+              aY[i][3] = fmaf(m, y4.w, aY[i][3]);
+            }
+          }
+        }
+      }
+    }
+    // u_grad, ddt, gB for the tile rows
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int l = l0 + tl + 16 * i;
+      float dpart = 0.f, bpart = 0.f;
+      if (l < cs && pvalid) {
+        float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (l < vl) s4 = *reinterpret_cast<const float4*>(accS + (kh * cs + l) * P + p0);
+        const float4 acc = make_float4(s4.x + aY[i][0], s4.y + aY[i][1], s4.z + aY[i][2], s4.w + aY[i][3]);
+        const float4 u4 = lds4(uS + l * kLDP + p0);
+        dpart = dot4(acc, u4, 0.f);
+        bpart = dot4(s4, u4, 0.f);
+        if (l < ci.lim) {
+          const float d = l < vl ? dts[l] : 0.f;
+          const long long off = ((ci.tok0 + l) * H + h) * (long long)P + p0;
+          st_any(u_grad, off, xdt, acc.x * d);
+          st_any(u_grad, off + 1, xdt, acc.y * d);
+          st_any(u_grad, off + 2, xdt, acc.z * d);
+          st_any(u_grad, off + 3, xdt, acc.w * d);
+        }
+      }
+      dpart = half_warp_sum(dpart);
+      bpart = half_warp_sum(bpart);
+      if (tq == 0 && l < cs) {
+        ddts[l] = dpart;
+        gBs[l] = bpart * dts[l];
+      }
+    }
+    // CB_grad and the intra-chunk decay terms: rows l = l0 + tl + 16 i, columns
+    // s = sb + tq + 16 j of 64-wide column blocks left of the tile's end.
+    float rs[2] = {0.f, 0.f};
+    const int send = min(l0 + kLT, vl);
+    for (int sb = 0; sb < send; sb += 64) {
+      float gm[2][4];
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) gm[i][j] = 0.f;
+      int srow[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) srow[j] = min(sb + tq + 16 * j, cs - 1) * kLDP;
+      for (int p = 0; p < P; p += 4) {
+        float4 a[2], b[4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) a[i] = lds4(yS + (l0 + tl + 16 * i) * kLDP + p);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) b[j] = lds4(uS + srow[j] + p);
+#pragma unroll
+        for (int i = 0; i < 2; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) gm[i][j] = dot4(a[i], b[j], gm[i][j]);
+      }
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int l = l0 + tl + 16 * i;
+        if (l >= vl) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int s = sb + tq + 16 * j;
+          if (s > l) continue;
+          const float cbg = gm[i][j] * dts[s] * expf(fminf(cms[l] - cms[s], 0.f));
+          atomicAdd(CBg + kg + (long long)l * cs + s, cbg);
+          if (s < l) {
+            const float w = cbg * CB[kg + (long long)l * cs + s];
+            rs[i] += w;
+            atomicAdd(&cols[s], w);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float r = half_warp_sum(rs[i]);
+      const int l = l0 + tl + 16 * i;
+      if (tq == 0 && l < cs) rows[l] = r;
+    }
+  }
+  __syncthreads();
+
+  // dt backward, one token per thread
+  const int t = tid;
+  float dlast = 0.f;
+  for (int i = 0; i < nsl; ++i) dlast += dl_part[kh * nsl + i];
+  float unused;
+  const float xi = t < cs ? cols[t] - rows[t] : 0.f;
+  const float intra = block_excl_scan(xi, tmp, unused);
+  const float xb = t < vl - 1 ? gBs[t] : 0.f;
+  const float dB = block_excl_scan(xb, tmp, unused);
+  // sum_{m >= tr} gC_m: thread t scans element tr = cs-1-t, so threads before it hold m > tr
+  const int tr = cs - 1 - t;
+  const float xc = (tr >= 0 && tr < vl) ? gC[kh * cs + tr] : 0.f;
+  const float exc = block_excl_scan(xc, tmp, unused);
+  if (tr >= 0) revc[tr] = exc + xc;
+  __syncthreads();
+  float aP = 0.f, bP = 0.f;
+  if (t < ci.lim) {
+    const long long tok = ci.tok0 + t;
+    float gg = 0.f;
+    if (t < vl) {
+      const float total = intra + dB + revc[t] + dlast;
+      const float pre = ld_any(delta_raw, tok * H + h, ddt_dtype) + (delta_bias ? delta_bias[h] : 0.f);
+      const bool sp = use_sp && pre <= 20.0f;
+      float d = sp ? logf(expf(pre) + 1.0f) : pre;
+      const bool clamped = (d < dmin) || (d > dmax);
+      d = fminf(fmaxf(d, dmin), dmax);
+      gg = clamped ? 0.f : total * A[h] + ddts[t];
+      if (sp) gg *= 1.0f / (1.0f + expf(-pre));
+      aP = total * d;
+      bP = gg;
+    }
+    st_any(draw_grad, tok * H + h, ddt_dtype, gg);
+  }
+  const float as = block_sum(aP, tmp);
+  const float bs = block_sum(bP, tmp);
+  if (tid == 0) {
+    A_part[kh] = as;
+    bias_part[kh] = bs;
+  }
+}
+
+// ===========================================================================
+// bwd_bmm: bmm_chunk_backward (backward_kernel.py:686-780, called twice at
+// backward.py:534-535), per (64-row tile, group, chunk):
+//   C_grad[l,:] += sum_{s<=l} CB_grad[l,s] B[s,:]     (blockIdx.x <  nt)
+//   B_grad[s,:] += sum_{l>=s} CB_grad[l,s] C[l,:]     (blockIdx.x >= nt)
+// Each output row belongs to one CTA: read-modify-write, no atomics.
+// ===========================================================================
+__global__ void __launch_bounds__(256) bwd_bmm_kernel(const void* __restrict__ Bm, const void* __restrict__ Cm,
+                                                      const float* __restrict__ CBg, float* __restrict__ Bgrad,
+                                                      float* __restrict__ Cgrad, ChunkMap cm, int G, int N,
+                                                      int xdt) {
+  constexpr int LDA = kLT + 4;
+  __shared__ __align__(16) float At[64 * LDA];
+  __shared__ __align__(16) float Bt[kLT * kLDN];
+  const int k = blockIdx.z, g = blockIdx.y, tid = threadIdx.x;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int cs = cm.cs, vl = ci.vlim, nt = (cs + 63) / 64;
+  const int which = blockIdx.x / nt, r0 = (blockIdx.x - which * nt) * 64;
+  if (r0 >= vl) return;
+  const float* cbg = CBg + ((long long)k * G + g) * cs * cs;
+  const void* X = which == 0 ? Bm : Cm;
+  float* out = which == 0 ? Cgrad : Bgrad;
+  const int kbeg = which == 0 ? 0 : r0;
+  const int kend = which == 0 ? min(r0 + 64, vl) : vl;
+  const int tl = tid >> 4, tq = tid & 15;
+  float acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  for (int kb = kbeg; kb < kend; kb += kLT) {
+    __syncthreads();
+    for (int idx = tid; idx < 64 * kLT; idx += 256) {
+      float v = 0.f;
+      int r, c;
+      if (which == 0) {  // A[r][c] = CB_grad[r0 + r][kb + c]
+        r = idx >> 5;
+        c = idx & 31;
+        if (r0 + r < cs && kb + c < kend) v = cbg[(long long)(r0 + r) * cs + kb + c];
+      } else {           // A[r][c] = CB_grad[kb + c][r0 + r]
+        r = idx & 63;
+        c = idx >> 6;
+        if (r0 + r < cs && kb + c < kend) v = cbg[(long long)(kb + c) * cs + r0 + r];
+      }
+      At[r * LDA + c] = v;
+    }
+    for (int idx = tid; idx < kLT * N; idx += 256) {
+      const int c = idx / N, n = idx - c * N, t = kb + c;
+      Bt[c * kLDN + n] = t < kend ? ld_any(X, ((ci.tok0 + t) * G + g) * (long long)N + n, xdt) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int c = 0; c < kLT; c += 4) {
+      float4 a[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = lds4(At + (tl + 16 * i) * LDA + c);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 b0 = lds4(Bt + (c + q) * kLDN + 4 * tq), b1 = lds4(Bt + (c + q) * kLDN + 64 + 4 * tq);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float m = comp(a[i], q);
+          acc[i][0] = fmaf(m, b0.x, acc[i][0]);
+          acc[i][1] = fmaf(m, b0.y, acc[i][1]);
+          acc[i][2] = fmaf(m, b0.z, acc[i][2]);
+          acc[i][3] = fmaf(m, b0.w, acc[i][3]);
+          acc[i][4] = fmaf(m, b1.x, acc[i][4]);
+          acc[i][5] = fmaf(m, b1.y, acc[i][5]);
+          acc[i][6] = fmaf(m, b1.z, acc[i][6]);
+          acc[i][7] = fmaf(m, b1.w, acc[i][7]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = r0 + tl + 16 * i;
+    if (r >= vl) continue;
+    const long long row = ((ci.tok0 + r) * G + g) * (long long)N;
+#pragma unroll
+    for (int jj = 0; jj < 2; ++jj) {
+      const int n0 = 4 * tq + 64 * jj;
+      if (n0 >= N) continue;
+      float4* o = reinterpret_cast<float4*>(out + row + n0);
+      float4 v = *o;
+      v.x += acc[i][4 * jj];
+      v.y += acc[i][4 * jj + 1];
+      v.z += acc[i][4 * jj + 2];
+      v.w += acc[i][4 * jj + 3];
+      *o = v;
+    }
+  }
+}
+
+// A_grad[h] = sum_k A_part[k,h]; delta_bias_grad likewise (fixed order: deterministic).
+__global__ void __launch_bounds__(256) bwd_param_reduce_kernel(const float* __restrict__ A_part,
+                                                               const float* __restrict__ bias_part,
+                                                               float* __restrict__ A_grad,
+                                                               float* __restrict__ bias_grad, int nchunks, int H) {
+  __shared__ float tmp[8];
+  const int h = blockIdx.x;
+  float a = 0.f, b = 0.f;
+  for (int k = threadIdx.x; k < nchunks; k += 256) {
+    a += A_part[(long long)k * H + h];
+    b += bias_part[(long long)k * H + h];
+  }
+  a = block_sum(a, tmp);
+  b = block_sum(b, tmp);
+  if (threadIdx.x == 0) {
+    A_grad[h] = a;
+    if (bias_grad) bias_grad[h] = b;
+  }
+}
+
+constexpr size_t kSmemStates = (size_t)(2 * kPmax * kLDT + 2 * kNmax * kLDT + 2 * kCSmax) * sizeof(float);
+constexpr size_t kSmemCB = (size_t)(2 * 64 * kLDN) * sizeof(float);
+constexpr size_t kSmemStateGrad =
+    (size_t)(2 * kPmax * kLDN + 2 * kLT * kLDN + 2 * kLT * kLDP + 2 * kCSmax) * sizeof(float);
+constexpr size_t kSmemIntra =
+    (size_t)(2 * kCSmax * kLDP + kLT * (kLT + 4) + 7 * kCSmax + 8) * sizeof(float);
+
+cudaError_t opt_in(const void* fn, size_t bytes) {
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+}  // namespace
+
+bool bwd_supported(int P, int N, int cs) {
+  return P >= 4 && P <= kPmax && P % 4 == 0 && N >= 4 && N <= kNmax && N % 4 == 0 && cs >= kLT &&
+         cs <= kCSmax && cs % kLT == 0;
+}
+
+size_t bwd_dl_slices(int P, int N) { return (size_t)((P * N / 4 + 255) / 256); }
+
+cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
+  const int H = c.H, G = c.G, P = c.P, N = c.N, cs = c.cs, PN = P * N;
+  const int nk = c.nchunks_max;
+  if (nk > 65535 || H > 65535 || c.nrows > 65535) return cudaErrorInvalidValue;
+  cudaError_t e;
+  if ((e = opt_in((const void*)bwd_chunk_states_kernel, kSmemStates))) return e;
+  if ((e = opt_in((const void*)bwd_cb_kernel, kSmemCB))) return e;
+  if ((e = opt_in((const void*)bwd_state_grad_kernel, kSmemStateGrad))) return e;
+  if ((e = opt_in((const void*)bwd_intra_kernel, kSmemIntra))) return e;
+  const size_t bc_bytes = (size_t)c.T * G * N * sizeof(float);
+  if ((e = cudaMemsetAsync(a.B_grad, 0, bc_bytes, c.stream))) return e;
+  if ((e = cudaMemsetAsync(a.C_grad, 0, bc_bytes, c.stream))) return e;
+  if ((e = cudaMemsetAsync(a.CBg, 0, (size_t)nk * G * cs * cs * sizeof(float), c.stream))) return e;
+  if ((e = launch_chunk_cumsum(c, a.dt_dtype, a.A, a.delta_raw, a.delta_bias, a.dt, a.cum))) return e;
+  const dim3 gkh((unsigned)H, (unsigned)nk);
+  // grid x = head: the heads of one chunk run side by side and share its B, C, CB in L2
+  bwd_chunk_states_kernel<<<gkh, 256, kSmemStates, c.stream>>>(
+      a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, c.cm, H, G, P, N, a.x_dtype, a.y_dtype);
+  if ((e = cudaGetLastError())) return e;
+  if (a.ev[1]) cudaEventRecord(a.ev[1], c.stream);
+  const int nsl = (int)bwd_dl_slices(P, N);
+  bwd_state_pass_kernel<<<dim3((unsigned)nsl, (unsigned)H, (unsigned)c.nrows), 256, 0, c.stream>>>(
+      a.states, a.hg, a.cum, a.h_init, a.h_last_grad, a.h_init_grad, a.dl_part, c.cm, H, PN);
+  if ((e = cudaGetLastError())) return e;
+  const int nt = (cs + 63) / 64;
+  bwd_cb_kernel<<<dim3((unsigned)(nt * (nt + 1) / 2), (unsigned)G, (unsigned)nk), 256, kSmemCB, c.stream>>>(
+      a.B, a.C, a.CB, c.cm, G, N, a.x_dtype);
+  if ((e = cudaGetLastError())) return e;
+  if (a.ev[2]) cudaEventRecord(a.ev[2], c.stream);
+  bwd_state_grad_kernel<<<gkh, 256, kSmemStateGrad, c.stream>>>(
+      a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, a.accS, a.B_grad, a.C_grad, a.gC, c.cm, H, G, P, N,
+      a.x_dtype, a.y_dtype);
+  if ((e = cudaGetLastError())) return e;
+  if (a.ev[3]) cudaEventRecord(a.ev[3], c.stream);
+  bwd_intra_kernel<<<gkh, 256, kSmemIntra, c.stream>>>(
+      a.u, a.y_grad, a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, a.dl_part, nsl, a.CBg,
+      a.u_grad, a.delta_raw_grad, a.A_part, a.bias_part, c.cm, H, G, P, a.x_dtype, a.y_dtype, a.dt_dtype, c.use_sp,
+      c.dmin, c.dmax);
+  if ((e = cudaGetLastError())) return e;
+  if (a.ev[4]) cudaEventRecord(a.ev[4], c.stream);
+  bwd_bmm_kernel<<<dim3((unsigned)(2 * nt), (unsigned)G, (unsigned)nk), 256, 0, c.stream>>>(
+      a.B, a.C, a.CBg, a.B_grad, a.C_grad, c.cm, G, N, a.x_dtype);
+  if ((e = cudaGetLastError())) return e;
+  bwd_param_reduce_kernel<<<(unsigned)H, 256, 0, c.stream>>>(a.A_part, a.bias_part, a.A_grad, a.delta_bias_grad,
+                                                             nk, H);
+  return cudaGetLastError();
+}
+
+}  // namespace ssdb200

@@ -247,6 +247,64 @@ def ssd_scan_forward(u, A, B, C, delta_raw, delta_bias=None, h_init=None, length
     return y, h_last
 
 
+def ssd_scan_backward(u, A, B, C, delta_raw, delta_bias, h_init, y_grad, h_last_grad, length=None,
+                      chunk_size=256, use_delta_softplus=True, delta_limit=(0.0, INF), is_causal=True,
+                      cu_seqlens=None, workspace: Optional[torch.Tensor] = None, events=None):
+    """SSD backward, the reference's ``ssd_scan/backward.py:467 ssd_scan_backward``.
+
+    Same arguments and outputs: ``(u_grad, A_grad, B_grad, C_grad, delta_raw_grad,
+    delta_bias_grad, h_init_grad)`` with ``u_grad`` in ``u``'s dtype, ``delta_raw_grad``
+    in ``delta_raw``'s, the rest fp32 (``backward.py:90,144,200,254,439-441``);
+    ``delta_bias_grad`` / ``h_init_grad`` are None when ``delta_bias`` / ``h_init`` are.
+    ``h_last_grad`` may be None (zero). ``is_causal`` changes nothing (the forward is
+    always causal). ``cu_seqlens`` selects packed rows as in :func:`ssd_scan_forward`.
+    """
+    b, L, H, P = u.shape
+    G, N = B.shape[2], B.shape[3]
+    dev = check_cuda([u, A, B, C, delta_raw, delta_bias, h_init, length, y_grad, h_last_grad, cu_seqlens],
+                     ["u", "A", "B", "C", "delta_raw", "delta_bias", "h_init", "length", "y_grad",
+                      "h_last_grad", "cu_seqlens"])
+    u, B, C, delta_raw = to_contiguous(u), to_contiguous(B), to_contiguous(C), to_contiguous(delta_raw)
+    for t, n in ((B, "B"), (C, "C")):
+        if t.dtype != u.dtype:
+            raise ValueError(f"[{n}] dtype {t.dtype} differs from u's {u.dtype}")
+    if tuple(y_grad.shape) != (b, L, H, P):
+        raise ValueError(f"[y_grad] expected shape {(b, L, H, P)}, got {tuple(y_grad.shape)}")
+    y_grad = to_contiguous(y_grad)
+    nrows = b if cu_seqlens is None else cu_seqlens.numel() - 1
+    if h_last_grad is not None:
+        if tuple(h_last_grad.shape) != (nrows, H, P, N):
+            raise ValueError(f"[h_last_grad] expected shape {(nrows, H, P, N)}, got {tuple(h_last_grad.shape)}")
+        h_last_grad = _aligned16(to_contiguous(h_last_grad.float()))
+    p, keep, _ = ssd_scan_params(u, A, B, C, delta_raw, delta_bias, h_init, length, chunk_size,
+                                 use_delta_softplus, delta_limit, None, None, cu_seqlens, "simt",
+                                 y_dtype=torch.float32)
+    need = int(_lib.lib().ssd_scan_bwd_workspace_size(byref(p)))
+    if need == 0:
+        raise ValueError("unsupported SSD backward geometry (headdim <= 64 and dstate <= 128, multiples of 4; "
+                         "chunk_size a multiple of 32 up to 256; heads a multiple of groups)")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, device=dev, dtype=torch.uint8)
+    p.workspace, p.workspace_bytes = _lib.ptr(workspace), workspace.numel()
+    if events is not None:
+        for i, e in enumerate(events):
+            p.events[i] = None if e is None else e
+    u_grad = torch.empty_like(u)
+    A_grad = torch.empty(H, device=dev, dtype=torch.float32)
+    B_grad = torch.empty(b, L, G, N, device=dev, dtype=torch.float32)
+    C_grad = torch.empty(b, L, G, N, device=dev, dtype=torch.float32)
+    delta_raw_grad = torch.empty_like(delta_raw)
+    delta_bias_grad = None if delta_bias is None else torch.empty(H, device=dev, dtype=torch.float32)
+    h_init_grad = None if h_init is None else torch.empty(nrows, H, P, N, device=dev, dtype=torch.float32)
+    g = _lib.SSDBwdParams(y_grad=_lib.ptr(y_grad), y_grad_dtype=_lib.dtype_code(y_grad.dtype, "y_grad"),
+                          h_last_grad=_lib.ptr(h_last_grad), u_grad=_lib.ptr(u_grad), A_grad=_lib.ptr(A_grad),
+                          B_grad=_lib.ptr(B_grad), C_grad=_lib.ptr(C_grad), delta_raw_grad=_lib.ptr(delta_raw_grad),
+                          delta_bias_grad=_lib.ptr(delta_bias_grad), h_init_grad=_lib.ptr(h_init_grad))
+    _lib.check(_lib.lib().ssd_scan_bwd(byref(p), byref(g), _stream(dev)), "ssd_scan_backward")
+    del keep
+    return u_grad, A_grad, B_grad, C_grad, delta_raw_grad, delta_bias_grad, h_init_grad
+
+
 def ssu_forward(u, A, B, C, delta_raw, delta_bias, h, use_delta_softplus=True, delta_limit=(0.0, INF),
                 D=None, z=None, y=None):
     """One-token state update; ``h`` is updated in place. Returns ``(y, h)`` with ``y``

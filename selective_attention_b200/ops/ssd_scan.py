@@ -14,8 +14,12 @@ callers are unchanged:
   have batch 1 and ``h_last`` / ``h_init`` are ``(nseq, H, P, N)``.
 - ``impl``: ``"auto"`` (tensor cores when supported), ``"tc"`` or ``"simt"``.
 
-The backward pass is outside this build's scope (forward + decode): calling it
-raises ``NotImplementedError``.
+Backward: ``SSDScanFn.backward`` is the reference's (``ops/ssd_scan.py:83-96``):
+the forward intermediates are recomputed and ``kernels.ssd_scan_backward`` returns
+the gradients of ``u, A, B, C, delta_raw, delta_bias, h_init`` (``None`` for the
+rest), also for packed ``cu_seqlens`` rows. The fused ``D`` / ``z`` epilogue has no
+backward here (the reference applies ``D`` and ``z`` outside the op): a backward
+through a call that used them raises ``NotImplementedError``.
 """
 from __future__ import annotations
 
@@ -99,11 +103,22 @@ class SSDScanFn(torch.autograd.Function):
         y, h_last = kernels.ssd_scan_forward(
             u, A, B, C, delta_raw, delta_bias, h_init, length, chunk_size, use_delta_softplus,
             delta_limit, is_causal, D=D, z=z, cu_seqlens=cu_seqlens, impl=impl)
-        ctx.mark_non_differentiable(h_last)
+        ctx.save_for_backward(u, A, B, C, delta_raw, delta_bias, h_init, length, cu_seqlens)
+        ctx.chunk_size = chunk_size
+        ctx.use_delta_softplus = use_delta_softplus
+        ctx.delta_limit = delta_limit
+        ctx.is_causal = is_causal
+        ctx.fused_epilogue = D is not None or z is not None
         return y, h_last
 
     @staticmethod
     def backward(ctx, y_grad, h_last_grad):
-        raise NotImplementedError(
-            "SSDScanFn.backward is not part of the B200 build (forward prefill and decode only); "
-            "the reference's backward is triton_kernels/ssd_scan/backward.py")
+        if ctx.fused_epilogue:
+            raise NotImplementedError(
+                "SSDScanFn.backward: the fused D / z epilogue has no backward; apply D and z outside the op "
+                "(as modules/ssm.py:144-150 does) to train through it")
+        u, A, B, C, delta_raw, delta_bias, h_init, length, cu_seqlens = ctx.saved_tensors
+        grads = kernels.ssd_scan_backward(
+            u, A, B, C, delta_raw, delta_bias, h_init, y_grad, h_last_grad, length, ctx.chunk_size,
+            ctx.use_delta_softplus, ctx.delta_limit, ctx.is_causal, cu_seqlens=cu_seqlens)
+        return (*grads, None, None, None, None, None, None, None, None, None)

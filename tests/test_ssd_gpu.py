@@ -279,13 +279,15 @@ def test_errors_before_launch():
     assert sab.device_error() == 0
 
 
-def test_backward_raises():
+def test_backward_through_fused_epilogue_raises():
     import selective_attention_b200 as sab
 
     g = load_golden("ssd_c0_fp32")
     i = g["inputs"]
     u = dev(i["u"]).requires_grad_(True)
-    y, _ = sab.SSDScanFn.apply(u, dev(i["A"]), dev(i["B"]), dev(i["C"]), dev(i["delta_raw"]), None, None, None, 64)
+    D = torch.ones(u.shape[2] * u.shape[3], device="cuda")
+    y, _ = sab.SSDScanFn.apply(u, dev(i["A"]), dev(i["B"]), dev(i["C"]), dev(i["delta_raw"]), None, None, None, 64,
+                               True, (0.0, INF), True, D)
     with pytest.raises(NotImplementedError):
         y.sum().backward()
 
