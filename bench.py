@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--no-ssu", action="store_true", help="skip the decode (config 3) measurement")
     ap.add_argument("--no-front", action="store_true", help="skip the prefill front-end (conv) measurement")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-bwd", action="store_true", help="skip the SSD backward measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     return ap.parse_args()
 
@@ -378,6 +379,8 @@ def run_ours(args, rank, world, local):
         line["ssu"] = ssu_measure(args, dev, flush, hbm_peak, world)
     if not args.no_front:
         line["front"] = front_measure(args, dev, flush, hbm_peak)
+    if not args.no_bwd and world == 1:
+        line["bwd"] = bwd_measure(args, cfg, inp, dev, flush)
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
@@ -495,6 +498,64 @@ def front_measure(args, dev, flush, hbm_peak):
             "us_per_step": us, "alg_bytes": by, "gbs": gbs, "peak_gbs": hbm_peak, "frac": gbs / hbm_peak,
             "steps": steps, "timing": "median of per-step CUDA events around the C-ABI call (arguments prepared once), "
                                      "L2 flushed between steps"}
+
+
+FFMA_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # CUDA-core fp32 FMA, nominal (no measured figure)
+
+
+def bwd_measure(args, cfg, inp, dev, flush):
+    """SSD backward (row f1) on the bench workload's inputs: y_grad fp32 (the reference's
+    y dtype) and h_last_grad, through ``kernels.ssd_scan_backward`` (the C-ABI
+    ``ssd_scan_bwd``). CUDA-core kernels: reported in TFLOP/s of the algorithmic fp32
+    FLOPs against the nominal FFMA rate, with the per-stage split from the C-ABI's events."""
+    from selective_attention_b200 import kernels
+
+    u, A, B, C, dr = inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"]
+    b, L, H, P = u.shape
+    G, N = B.shape[2], B.shape[3]
+    cu = inp.get("cu_seqlens")
+    nrows = b if cu is None else cu.numel() - 1
+    g = torch.Generator(device=dev).manual_seed(2)
+    yg = torch.randn(b, L, H, P, device=dev, generator=g)
+    hlg = 0.1 * torch.randn(nrows, H, P, N, device=dev, generator=g)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for e in ev:
+        e.record()
+    handles = [e.cuda_event for e in ev]
+    ws = torch.empty(0, dtype=torch.uint8, device=dev)
+
+    def step(events=None):
+        kernels.ssd_scan_backward(u, A, B, C, dr, None, None, yg, hlg, None, cfg.chunk, cu_seqlens=cu,
+                                  events=events)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    steps = max(5, min(args.steps, 20))
+    per = time_steps(step, steps, flush, torch.cuda.current_stream(dev))
+    split = []
+    for _ in range(3):
+        step(handles)
+        torch.cuda.synchronize()
+        split.append([ev[i].elapsed_time(ev[i + 1]) for i in range(5)])
+    names = ["cumsum+states", "state_pass+cb", "state_grad", "intra", "bmm+reduce"]
+    stages = {n: statistics.median(x[i] for x in split) for i, n in enumerate(names)}
+    ms = statistics.median(per)
+    cs = cfg.chunk
+    if cu is None:
+        nk = b * ((L + cs - 1) // cs)
+    else:
+        nk = sum((n + cs - 1) // cs for n in (cu[1:] - cu[:-1]).tolist())
+    # per (chunk, head): five cs x P x N products (S, HG, accS, B_grad, C_grad terms) and two
+    # causal cs x cs x P ones (CB^T y_grad, y_grad u^T); per (chunk, group): CB and the two
+    # bmm-backward products, causal cs x cs x N. Counted on whole chunks.
+    flops = nk * H * (10 * cs * P * N + 2 * cs * cs * P) + nk * G * 3 * cs * cs * N
+    tf = flops / (ms * 1e-3) / 1e12
+    del ws
+    return {"config": f"{cfg.name} inputs, y_grad fp32 + h_last_grad, no D/z", "ms_per_step": ms,
+            "tokens_per_s": b * L / (ms * 1e-3), "stages_ms": stages, "alg_flops": flops, "tflops": tf,
+            "ffma_nominal_tflops": FFMA_NOMINAL_TFLOPS, "frac_of_nominal_ffma": tf / FFMA_NOMINAL_TFLOPS,
+            "steps": steps, "timing": "median of per-step CUDA events, L2 flushed between steps"}
 
 
 def ssu_measure(args, dev, flush, hbm_peak, world):

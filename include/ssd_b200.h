@@ -195,7 +195,7 @@ int ssd_chunk_scan_fwd(const ssd_params* p, void* stream);       /* u, dt, cum, 
  *   delta_raw_grad (b, L, H) dt_dtype;  delta_bias_grad (H,) fp32 (required iff
  *   delta_bias is given);  h_init_grad (b, H, P, N) fp32 (required iff h_init is given)
  * (the reference's output dtypes: backward.py:90,144,200,254,439-441). Supported shapes:
- * headdim <= 64, dstate <= 128, both multiples of 4; chunk_size a multiple of 32 up
+ * headdim <= 64, dstate <= 128, both multiples of 8; chunk_size a multiple of 32 up
  * to 256. Uses p->workspace (>= ssd_scan_bwd_workspace_size(p)); p->events, when
  * set, are recorded before the first stage [0], after the state recompute [1], the
  * state passes and CB [2], the state-side products [3], the intra-chunk products [4].

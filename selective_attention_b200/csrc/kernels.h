@@ -35,7 +35,7 @@ cudaError_t launch_simt_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype,
                                    const float* D, const void* z, void* y);
 unsigned int fetch_error_simt(cudaStream_t s);
 
-// ssd_bwd.cu (CUDA-core backward; P <= 64, N <= 128, chunk 32..256 in steps of 32)
+// ssd_bwd.cu (CUDA-core backward; P <= 64, N <= 128 (multiples of 8), chunk 32..256 in steps of 32)
 struct BwdArgs {
   int x_dtype, dt_dtype, y_dtype;
   const void* u;

@@ -85,6 +85,71 @@ __device__ __forceinline__ float block_sum(float v, float* tmp) {
   return total;
 }
 
+// 8 consecutive elements from element i (i % 8 == 0, 16-byte aligned) as fp32.
+__device__ __forceinline__ void ld8(const void* p, long long i, int dt, float (&o)[8]) {
+  if (dt == SSD_F32) {
+    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    const float4 a = __ldg(q), b = __ldg(q + 1);
+    o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w;
+    o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+  } else {
+    const uint4 w = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i));
+    float2 f[4];
+    if (dt == SSD_BF16) {
+      f[0] = unpack2<__nv_bfloat16>(w.x); f[1] = unpack2<__nv_bfloat16>(w.y);
+      f[2] = unpack2<__nv_bfloat16>(w.z); f[3] = unpack2<__nv_bfloat16>(w.w);
+    } else {
+      f[0] = unpack2<__half>(w.x); f[1] = unpack2<__half>(w.y);
+      f[2] = unpack2<__half>(w.z); f[3] = unpack2<__half>(w.w);
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      o[2 * e] = f[e].x;
+      o[2 * e + 1] = f[e].y;
+    }
+  }
+}
+
+// Stage R token rows of a token-major tensor into shared memory as fp32: row r is
+// token tok0 + t0 + r, its columns [0, W) start at element (tok0 + t0 + r) * rs + co
+// (W, rs, co multiples of 8). Rows with t0 + r >= lim are zero; each value is scaled by
+// scale[t0 + r] when `scale` is given. COLS=false writes dst[r * ldd + c], COLS=true
+// dst[c * ldd + r]. All of a thread's loads (V 16-byte vectors, R * W / 8 <= 256 V) are
+// issued before its stores, so the tile costs one memory latency.
+template <int V, bool COLS>
+__device__ __forceinline__ void stage(float* dst, int ldd, const void* src, int dt, long long tok0, int t0, int R,
+                                      long long rs, long long co, int W, int lim, const float* scale) {
+  const int vpr = W >> 3, nv = R * vpr;
+  float v[V][8];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int vi = threadIdx.x + 256 * j;
+    const int r = vi / vpr, c = (vi - r * vpr) << 3;
+    if (vi < nv && t0 + r < lim) {
+      ld8(src, (tok0 + t0 + r) * rs + co + c, dt, v[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int vi = threadIdx.x + 256 * j;
+    if (vi >= nv) continue;
+    const int r = vi / vpr, c = (vi - r * vpr) << 3;
+    const float sc = scale ? scale[t0 + r] : 1.f;
+    if (COLS) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) dst[(c + e) * ldd + r] = v[j][e] * sc;
+    } else {
+      *reinterpret_cast<float4*>(dst + r * ldd + c) =
+          make_float4(v[j][0] * sc, v[j][1] * sc, v[j][2] * sc, v[j][3] * sc);
+      *reinterpret_cast<float4*>(dst + r * ldd + c + 4) =
+          make_float4(v[j][4] * sc, v[j][5] * sc, v[j][6] * sc, v[j][7] * sc);
+    }
+  }
+}
+
 constexpr int kLT = 32;        // token rows per tile
 constexpr int kPmax = 64, kNmax = 128, kCSmax = 256;
 constexpr int kLDT = kLT + 4;  // [feature][token] tiles
@@ -92,95 +157,67 @@ constexpr int kLDN = kNmax + 4;
 constexpr int kLDP = kPmax + 4;
 
 // ===========================================================================
-// bwd_chunk_states: per (chunk, head)
-//   S[p,n]  = sum_{l<lim} u[l,p] exp(min(cum_last - cum_l, 0)) dt_l B[l,n]
-//             (chunk_state forward, backward.py:487)
-//   HG[p,n] = sum_{l<len} y_grad[l,p] exp(cum_l) C[l,n]   (backward_kernel.py:23-93)
-// Thread (tp, tn) owns p = tp + 16 i (i < 4), n = tn + 16 j (j < 8) of both.
+// bwd_chunk_states: per (chunk, head), one product per CTA (blockIdx.z):
+//   z = 0: S[p,n]  = sum_{l<len} u[l,p] exp(min(cum_last - cum_l, 0)) dt_l B[l,n]
+//          (the chunk_state forward recomputed, backward.py:487; dt = 0 past len)
+//   z = 1: HG[p,n] = sum_{l<len} y_grad[l,p] exp(cum_l) C[l,n]   (backward_kernel.py:23-93)
+// 32-token tiles staged transposed ([feature][token]); thread (tp, tn) owns
+// p = tp + 16 i (i < 4), n = tn + 16 j (j < 8).
 // ===========================================================================
-__global__ void __launch_bounds__(256) bwd_chunk_states_kernel(
+__global__ void __launch_bounds__(256, 2) bwd_chunk_states_kernel(
     const void* __restrict__ u, const void* __restrict__ Bm, const void* __restrict__ Cm,
     const void* __restrict__ yg, const float* __restrict__ dt, const float* __restrict__ cum,
     float* __restrict__ states, float* __restrict__ hg, ChunkMap cm, int H, int G, int P, int N, int xdt,
     int ydt) {
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
-  const int h = blockIdx.x, k = blockIdx.y;
+  const int h = blockIdx.x, k = blockIdx.y, which = blockIdx.z, tid = threadIdx.x;
   ChunkInfo ci;
   if (!chunk_info(cm, k, ci)) return;
-  const int cs = cm.cs, g = h / (H / G), tid = threadIdx.x;
-  float* xw = sm;                   // [kPmax][kLDT]
-  float* ye = xw + kPmax * kLDT;    // [kPmax][kLDT]
-  float* bt = ye + kPmax * kLDT;    // [kNmax][kLDT]
-  float* ct = bt + kNmax * kLDT;    // [kNmax][kLDT]
-  float* dts = ct + kNmax * kLDT;   // [kCSmax]
-  float* cms = dts + kCSmax;        // [kCSmax]
+  const int cs = cm.cs, g = h / (H / G), vl = ci.vlim;
+  float* aT = sm;                   // [kPmax][kLDT]
+  float* bT = aT + kPmax * kLDT;    // [kNmax][kLDT]
+  float* scl = bT + kNmax * kLDT;   // [kCSmax]
   const long long kh = (long long)k * H + h;
+  const float clast = cum[kh * cs + cs - 1];
   for (int i = tid; i < cs; i += 256) {
-    dts[i] = dt[kh * cs + i];
-    cms[i] = cum[kh * cs + i];
+    const float c = cum[kh * cs + i];
+    scl[i] = i < vl ? (which == 0 ? expf(fminf(clast - c, 0.f)) * dt[kh * cs + i] : expf(c)) : 0.f;
   }
-  __syncthreads();
-  const float clast = cms[cs - 1];
+  const void* asrc = which == 0 ? u : yg;
+  const void* bsrc = which == 0 ? Bm : Cm;
+  const int adt = which == 0 ? xdt : ydt;
   const int tp = tid >> 4, tn = tid & 15;
   int pr[4], nr[8];
 #pragma unroll
   for (int i = 0; i < 4; ++i) pr[i] = min(tp + 16 * i, P - 1) * kLDT;
 #pragma unroll
   for (int j = 0; j < 8; ++j) nr[j] = min(tn + 16 * j, N - 1) * kLDT;
-  float aS[4][8], aH[4][8];
+  float acc[4][8];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) aS[i][j] = aH[i][j] = 0.f;
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
-  for (int l0 = 0; l0 < ci.lim; l0 += kLT) {
+  for (int l0 = 0; l0 < vl; l0 += kLT) {
     __syncthreads();
-    for (int idx = tid; idx < kLT * P; idx += 256) {
-      const int l = idx / P, p = idx - l * P, t = l0 + l;
-      float xv = 0.f, yv = 0.f;
-      if (t < ci.lim) {
-        const long long off = ((ci.tok0 + t) * H + h) * (long long)P + p;
-        xv = ld_any(u, off, xdt) * (expf(fminf(clast - cms[t], 0.f)) * dts[t]);
-        if (t < ci.vlim) yv = ld_any(yg, off, ydt) * expf(cms[t]);
-      }
-      xw[p * kLDT + l] = xv;
-      ye[p * kLDT + l] = yv;
-    }
-    for (int idx = tid; idx < kLT * N; idx += 256) {
-      const int l = idx / N, n = idx - l * N, t = l0 + l;
-      float bv = 0.f, cv = 0.f;
-      if (t < ci.lim) {
-        const long long off = ((ci.tok0 + t) * G + g) * (long long)N + n;
-        bv = ld_any(Bm, off, xdt);
-        if (t < ci.vlim) cv = ld_any(Cm, off, xdt);
-      }
-      bt[n * kLDT + l] = bv;
-      ct[n * kLDT + l] = cv;
-    }
+    stage<1, true>(aT, kLDT, asrc, adt, ci.tok0, l0, kLT, (long long)H * P, (long long)h * P, P, vl, scl);
+    stage<2, true>(bT, kLDT, bsrc, xdt, ci.tok0, l0, kLT, (long long)G * N, (long long)g * N, N, vl, nullptr);
     __syncthreads();
 #pragma unroll 2
     for (int l = 0; l < kLT; l += 4) {
       float4 a[4], b[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = lds4(xw + pr[i] + l);
+      for (int i = 0; i < 4; ++i) a[i] = lds4(aT + pr[i] + l);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) b[j] = lds4(bt + nr[j] + l);
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) aS[i][j] = dot4(a[i], b[j], aS[i][j]);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = lds4(ye + pr[i] + l);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) b[j] = lds4(ct + nr[j] + l);
+      for (int j = 0; j < 8; ++j) b[j] = lds4(bT + nr[j] + l);
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) aH[i][j] = dot4(a[i], b[j], aH[i][j]);
+        for (int j = 0; j < 8; ++j) acc[i][j] = dot4(a[i], b[j], acc[i][j]);
     }
   }
-  const long long base = kh * P * N;
+  float* out = (which == 0 ? states : hg) + kh * P * N;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int p = tp + 16 * i;
@@ -188,10 +225,7 @@ __global__ void __launch_bounds__(256) bwd_chunk_states_kernel(
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int n = tn + 16 * j;
-      if (n < N) {
-        states[base + p * N + n] = aS[i][j];
-        hg[base + p * N + n] = aH[i][j];
-      }
+      if (n < N) out[p * N + n] = acc[i][j];
     }
   }
 }
@@ -280,12 +314,8 @@ __global__ void __launch_bounds__(256) bwd_cb_kernel(const void* __restrict__ Bm
   const int tj = t, cs = cm.cs, l0 = ti * 64, s0 = tj * 64, tid = threadIdx.x;
   float* cS = sm;               // [64][kLDN]
   float* bS = sm + 64 * kLDN;   // [64][kLDN]
-  for (int idx = tid; idx < 64 * N; idx += 256) {
-    const int r = idx / N, n = idx - r * N;
-    const int l = l0 + r, s = s0 + r;
-    cS[r * kLDN + n] = l < ci.lim ? ld_any(Cm, ((ci.tok0 + l) * G + g) * (long long)N + n, xdt) : 0.f;
-    bS[r * kLDN + n] = s < ci.lim ? ld_any(Bm, ((ci.tok0 + s) * G + g) * (long long)N + n, xdt) : 0.f;
-  }
+  stage<4, false>(cS, kLDN, Cm, xdt, ci.tok0, l0, 64, (long long)G * N, (long long)g * N, N, ci.lim, nullptr);
+  stage<4, false>(bS, kLDN, Bm, xdt, ci.tok0, s0, 64, (long long)G * N, (long long)g * N, N, ci.lim, nullptr);
   __syncthreads();
   const int ty = tid >> 4, tx = tid & 15;
   float acc[4][4];
@@ -344,23 +374,41 @@ __global__ void __launch_bounds__(256) bwd_state_grad_kernel(
   float* ct = bt + kLT * kLDN;      // [kLT][kLDN]
   float* uw = ct + kLT * kLDN;      // [kLT][kLDP]
   float* ye = uw + kLT * kLDP;      // [kLT][kLDP]
-  float* dts = ye + kLT * kLDP;     // [kCSmax]
-  float* cms = dts + kCSmax;        // [kCSmax]
+  float* sS = ye + kLT * kLDP;      // [kCSmax] exp(min(cum_last - cum_l, 0))
+  float* wS = sS + kCSmax;          // [kCSmax] sS * dt
+  float* eS = wS + kCSmax;          // [kCSmax] exp(cum_l)
   const long long kh = (long long)k * H + h;
   const float* hgk = hg + kh * P * N;
   const float* pvk = prev + kh * P * N;
-  for (int idx = tid * 4; idx < P * N; idx += 1024) {
-    const int p = idx / N, n = idx - p * N;
-    *reinterpret_cast<float4*>(hgS + p * kLDN + n) = *reinterpret_cast<const float4*>(hgk + idx);
-    *reinterpret_cast<float4*>(pvS + p * kLDN + n) = *reinterpret_cast<const float4*>(pvk + idx);
-  }
-  for (int i = tid; i < cs; i += 256) {
-    dts[i] = dt[kh * cs + i];
-    cms[i] = cum[kh * cs + i];
-  }
-  __syncthreads();
-  const float clast = cms[cs - 1];
   const int vl = ci.vlim;
+  {
+    float4 ha[8], pa[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int idx = (tid + 256 * j) * 4;
+      if (idx < P * N) {
+        ha[j] = __ldg(reinterpret_cast<const float4*>(hgk + idx));
+        pa[j] = __ldg(reinterpret_cast<const float4*>(pvk + idx));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int idx = (tid + 256 * j) * 4;
+      if (idx < P * N) {
+        const int p = idx / N, n = idx - p * N;
+        *reinterpret_cast<float4*>(hgS + p * kLDN + n) = ha[j];
+        *reinterpret_cast<float4*>(pvS + p * kLDN + n) = pa[j];
+      }
+    }
+  }
+  const float clast = cum[kh * cs + cs - 1];
+  for (int i = tid; i < cs; i += 256) {
+    const float c = cum[kh * cs + i];
+    const float sc = i < vl ? expf(fminf(clast - c, 0.f)) : 0.f;
+    sS[i] = sc;
+    wS[i] = sc * dt[kh * cs + i];
+    eS[i] = i < vl ? expf(c) : 0.f;
+  }
   const int tl = tid >> 4, tq = tid & 15;
   int prow[4];
 #pragma unroll
@@ -368,28 +416,11 @@ __global__ void __launch_bounds__(256) bwd_state_grad_kernel(
 
   for (int l0 = 0; l0 < ci.lim; l0 += kLT) {
     __syncthreads();
-    for (int idx = tid; idx < kLT * N; idx += 256) {
-      const int l = idx / N, n = idx - l * N, t = l0 + l;
-      float bv = 0.f, cv = 0.f;
-      if (t < vl) {
-        const long long off = ((ci.tok0 + t) * G + g) * (long long)N + n;
-        bv = ld_any(Bm, off, xdt);
-        cv = ld_any(Cm, off, xdt);
-      }
-      bt[l * kLDN + n] = bv;
-      ct[l * kLDN + n] = cv;
-    }
-    for (int idx = tid; idx < kLT * P; idx += 256) {
-      const int l = idx / P, p = idx - l * P, t = l0 + l;
-      float uv = 0.f, yv = 0.f;
-      if (t < vl) {
-        const long long off = ((ci.tok0 + t) * H + h) * (long long)P + p;
-        uv = ld_any(u, off, xdt) * (expf(fminf(clast - cms[t], 0.f)) * dts[t]);
-        yv = ld_any(yg, off, ydt) * expf(cms[t]);
-      }
-      uw[l * kLDP + p] = uv;
-      ye[l * kLDP + p] = yv;
-    }
+    const long long rsB = (long long)G * N, coB = (long long)g * N, rsU = (long long)H * P, coU = (long long)h * P;
+    stage<2, false>(bt, kLDN, Bm, xdt, ci.tok0, l0, kLT, rsB, coB, N, vl, nullptr);
+    stage<2, false>(ct, kLDN, Cm, xdt, ci.tok0, l0, kLT, rsB, coB, N, vl, nullptr);
+    stage<1, false>(uw, kLDP, u, xdt, ci.tok0, l0, kLT, rsU, coU, P, vl, wS);
+    stage<1, false>(ye, kLDP, yg, ydt, ci.tok0, l0, kLT, rsU, coU, P, vl, eS);
     __syncthreads();
 
     // accS: rows l = tl + 16 i, columns p = tq + 16 j
@@ -413,7 +444,7 @@ __global__ void __launch_bounds__(256) bwd_state_grad_kernel(
     for (int i = 0; i < 2; ++i) {
       const int l = l0 + tl + 16 * i;
       if (l >= cs) continue;
-      const float sc = l < vl ? expf(fminf(clast - cms[l], 0.f)) : 0.f;
+      const float sc = sS[l];
       float* o = accS_out + (kh * cs + l) * P;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -535,19 +566,11 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
   float* gBs = ddts + kCSmax;
   float* revc = gBs + kCSmax;
   float* tmp = revc + kCSmax;         // [8]
+  float* cbS = tmp + 8;               // [kLT][kLDP]: CB rows of the tile, 64 columns
   const long long kh = (long long)k * H + h;
   const long long kg = ((long long)k * G + g) * cs * cs;
-  for (int idx = tid; idx < cs * P; idx += 256) {
-    const int l = idx / P, p = idx - l * P;
-    float uv = 0.f, yv = 0.f;
-    if (l < vl) {
-      const long long off = ((ci.tok0 + l) * H + h) * (long long)P + p;
-      uv = ld_any(u, off, xdt);
-      yv = ld_any(yg, off, ydt);
-    }
-    uS[l * kLDP + p] = uv;
-    yS[l * kLDP + p] = yv;
-  }
+  stage<8, false>(uS, kLDP, u, xdt, ci.tok0, 0, cs, (long long)H * P, (long long)h * P, P, vl, nullptr);
+  stage<8, false>(yS, kLDP, yg, ydt, ci.tok0, 0, cs, (long long)H * P, (long long)h * P, P, vl, nullptr);
   for (int i = tid; i < kCSmax; i += 256) {
     dts[i] = i < cs ? dt[kh * cs + i] : 0.f;
     cms[i] = i < cs ? cum[kh * cs + i] : 0.f;
@@ -567,12 +590,19 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
       for (int j = 0; j < 4; ++j) aY[i][j] = 0.f;
     for (int s0 = l0; s0 < vl; s0 += kLT) {
       __syncthreads();
-      for (int idx = tid; idx < kLT * kLT; idx += 256) {
-        const int r = idx & (kLT - 1), c = idx >> 5;
-        const int l = l0 + r, s = s0 + c;
-        float v = 0.f;
-        if (s >= l && s < vl && l < vl) v = CB[kg + (long long)s * cs + l] * expf(fminf(cms[s] - cms[l], 0.f));
-        Mt[r * LDS + c] = v;
+      {
+        // thread: CB row s = s0 + c, columns l0 + r4 .. + 3 (one 16-byte load)
+        const int c = tid >> 3, r4 = (tid & 7) * 4, s = s0 + c;
+        float4 cb = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (s < vl) cb = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)s * cs + l0 + r4));
+        const float cs_ = cms[s];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int l = l0 + r4 + e;
+          float v = 0.f;
+          if (s >= l && s < vl && l < vl) v = comp(cb, e) * expf(fminf(cs_ - cms[l], 0.f));
+          Mt[(r4 + e) * LDS + c] = v;
+        }
       }
       __syncthreads();
       if (pvalid) {
@@ -629,6 +659,16 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
     float rs[2] = {0.f, 0.f};
     const int send = min(l0 + kLT, vl);
     for (int sb = 0; sb < send; sb += 64) {
+      __syncthreads();  // cbS of the previous block consumed
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int vi = tid + 256 * j, r = vi >> 4, c4 = (vi & 15) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (sb + c4 < cs && l0 + r < vl)
+          v = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)(l0 + r) * cs + sb + c4));
+        *reinterpret_cast<float4*>(cbS + r * kLDP + c4) = v;
+      }
+      __syncthreads();
       float gm[2][4];
 #pragma unroll
       for (int i = 0; i < 2; ++i)
@@ -659,7 +699,7 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
           const float cbg = gm[i][j] * dts[s] * expf(fminf(cms[l] - cms[s], 0.f));
           atomicAdd(CBg + kg + (long long)l * cs + s, cbg);
           if (s < l) {
-            const float w = cbg * CB[kg + (long long)l * cs + s];
+            const float w = cbg * cbS[(tl + 16 * i) * kLDP + tq + 16 * j];
             rs[i] += w;
             atomicAdd(&cols[s], w);
           }
@@ -749,24 +789,28 @@ __global__ void __launch_bounds__(256) bwd_bmm_kernel(const void* __restrict__ B
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
   for (int kb = kbeg; kb < kend; kb += kLT) {
     __syncthreads();
-    for (int idx = tid; idx < 64 * kLT; idx += 256) {
-      float v = 0.f;
-      int r, c;
-      if (which == 0) {  // A[r][c] = CB_grad[r0 + r][kb + c]
-        r = idx >> 5;
-        c = idx & 31;
-        if (r0 + r < cs && kb + c < kend) v = cbg[(long long)(r0 + r) * cs + kb + c];
-      } else {           // A[r][c] = CB_grad[kb + c][r0 + r]
-        r = idx & 63;
-        c = idx >> 6;
-        if (r0 + r < cs && kb + c < kend) v = cbg[(long long)(kb + c) * cs + r0 + r];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int vi = tid + 256 * j;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (which == 0) {  // A[r][c] = CB_grad[r0 + r][kb + c]: row r, 4 columns from c4
+        const int r = vi >> 3, c4 = (vi & 7) * 4;
+        if (r0 + r < cs && kb + c4 < cs)
+          v = __ldg(reinterpret_cast<const float4*>(cbg + (long long)(r0 + r) * cs + kb + c4));
+        if (kb + c4 >= kend) v.x = 0.f;
+        if (kb + c4 + 1 >= kend) v.y = 0.f;
+        if (kb + c4 + 2 >= kend) v.z = 0.f;
+        if (kb + c4 + 3 >= kend) v.w = 0.f;
+        *reinterpret_cast<float4*>(At + r * LDA + c4) = v;
+      } else {           // A[r][c] = CB_grad[kb + c][r0 + r]: CB_grad row kb + c, 4 columns from r4
+        const int c = vi >> 4, r4 = (vi & 15) * 4;
+        if (kb + c < kend && r0 + r4 < cs)
+          v = __ldg(reinterpret_cast<const float4*>(cbg + (long long)(kb + c) * cs + r0 + r4));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) At[(r4 + e) * LDA + c] = comp(v, e);
       }
-      At[r * LDA + c] = v;
     }
-    for (int idx = tid; idx < kLT * N; idx += 256) {
-      const int c = idx / N, n = idx - c * N, t = kb + c;
-      Bt[c * kLDN + n] = t < kend ? ld_any(X, ((ci.tok0 + t) * G + g) * (long long)N + n, xdt) : 0.f;
-    }
+    stage<2, false>(Bt, kLDN, X, xdt, ci.tok0, kb, kLT, (long long)G * N, (long long)g * N, N, kend, nullptr);
     __syncthreads();
 #pragma unroll 2
     for (int c = 0; c < kLT; c += 4) {
@@ -831,12 +875,12 @@ __global__ void __launch_bounds__(256) bwd_param_reduce_kernel(const float* __re
   }
 }
 
-constexpr size_t kSmemStates = (size_t)(2 * kPmax * kLDT + 2 * kNmax * kLDT + 2 * kCSmax) * sizeof(float);
+constexpr size_t kSmemStates = (size_t)((kPmax + kNmax) * kLDT + kCSmax) * sizeof(float);
 constexpr size_t kSmemCB = (size_t)(2 * 64 * kLDN) * sizeof(float);
 constexpr size_t kSmemStateGrad =
-    (size_t)(2 * kPmax * kLDN + 2 * kLT * kLDN + 2 * kLT * kLDP + 2 * kCSmax) * sizeof(float);
+    (size_t)(2 * kPmax * kLDN + 2 * kLT * kLDN + 2 * kLT * kLDP + 3 * kCSmax) * sizeof(float);
 constexpr size_t kSmemIntra =
-    (size_t)(2 * kCSmax * kLDP + kLT * (kLT + 4) + 7 * kCSmax + 8) * sizeof(float);
+    (size_t)(2 * kCSmax * kLDP + kLT * (kLT + 4) + 7 * kCSmax + 8 + kLT * kLDP) * sizeof(float);
 
 cudaError_t opt_in(const void* fn, size_t bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
@@ -845,7 +889,7 @@ cudaError_t opt_in(const void* fn, size_t bytes) {
 }  // namespace
 
 bool bwd_supported(int P, int N, int cs) {
-  return P >= 4 && P <= kPmax && P % 4 == 0 && N >= 4 && N <= kNmax && N % 4 == 0 && cs >= kLT &&
+  return P >= 8 && P <= kPmax && P % 8 == 0 && N >= 8 && N <= kNmax && N % 8 == 0 && cs >= kLT &&
          cs <= kCSmax && cs % kLT == 0;
 }
 
@@ -867,7 +911,7 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
   if ((e = launch_chunk_cumsum(c, a.dt_dtype, a.A, a.delta_raw, a.delta_bias, a.dt, a.cum))) return e;
   const dim3 gkh((unsigned)H, (unsigned)nk);
   // grid x = head: the heads of one chunk run side by side and share its B, C, CB in L2
-  bwd_chunk_states_kernel<<<gkh, 256, kSmemStates, c.stream>>>(
+  bwd_chunk_states_kernel<<<dim3((unsigned)H, (unsigned)nk, 2u), 256, kSmemStates, c.stream>>>(
       a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, c.cm, H, G, P, N, a.x_dtype, a.y_dtype);
   if ((e = cudaGetLastError())) return e;
   if (a.ev[1]) cudaEventRecord(a.ev[1], c.stream);

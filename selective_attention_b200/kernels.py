@@ -270,7 +270,7 @@ def ssd_scan_backward(u, A, B, C, delta_raw, delta_bias, h_init, y_grad, h_last_
             raise ValueError(f"[{n}] dtype {t.dtype} differs from u's {u.dtype}")
     if tuple(y_grad.shape) != (b, L, H, P):
         raise ValueError(f"[y_grad] expected shape {(b, L, H, P)}, got {tuple(y_grad.shape)}")
-    y_grad = to_contiguous(y_grad)
+    y_grad = _aligned16(to_contiguous(y_grad))
     nrows = b if cu_seqlens is None else cu_seqlens.numel() - 1
     if h_last_grad is not None:
         if tuple(h_last_grad.shape) != (nrows, H, P, N):
@@ -281,7 +281,7 @@ def ssd_scan_backward(u, A, B, C, delta_raw, delta_bias, h_init, y_grad, h_last_
                                  y_dtype=torch.float32)
     need = int(_lib.lib().ssd_scan_bwd_workspace_size(byref(p)))
     if need == 0:
-        raise ValueError("unsupported SSD backward geometry (headdim <= 64 and dstate <= 128, multiples of 4; "
+        raise ValueError("unsupported SSD backward geometry (headdim <= 64 and dstate <= 128, multiples of 8; "
                          "chunk_size a multiple of 32 up to 256; heads a multiple of groups)")
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(need, device=dev, dtype=torch.uint8)
