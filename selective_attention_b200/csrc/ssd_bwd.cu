@@ -55,8 +55,9 @@ __device__ __forceinline__ float half_warp_sum(float v) {
   return v;
 }
 
-// Exclusive prefix sum over a 256-thread block (one value per thread); `tmp` holds
-// 8 floats of shared memory. Also returns the block total.
+// Exclusive prefix sum over a block of NW warps (one value per thread); `tmp` holds NW
+// floats of shared memory. Also returns the block total.
+template <int NW = 8>
 __device__ __forceinline__ float block_excl_scan(float v, float* tmp, float& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   float x = v;
@@ -69,7 +70,7 @@ __device__ __forceinline__ float block_excl_scan(float v, float* tmp, float& tot
   __syncthreads();
   float before = 0.f, all = 0.f;
 #pragma unroll
-  for (int w = 0; w < 8; ++w) {
+  for (int w = 0; w < NW; ++w) {
     const float t = tmp[w];
     if (w < warp) before += t;
     all += t;
@@ -79,9 +80,10 @@ __device__ __forceinline__ float block_excl_scan(float v, float* tmp, float& tot
   return before + x - v;
 }
 
+template <int NW = 8>
 __device__ __forceinline__ float block_sum(float v, float* tmp) {
   float total;
-  block_excl_scan(v, tmp, total);
+  block_excl_scan<NW>(v, tmp, total);
   return total;
 }
 
@@ -110,20 +112,35 @@ __device__ __forceinline__ void ld8(const void* p, long long i, int dt, float (&
   }
 }
 
+// 4 consecutive elements from element i (i % 4 == 0, aligned) as fp32.
+__device__ __forceinline__ float4 ld4(const void* p, long long i, int dt) {
+  if (dt == SSD_F32) return __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p) + i));
+  const uint2 w = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p) + i));
+  float2 a, b;
+  if (dt == SSD_BF16) {
+    a = unpack2<__nv_bfloat16>(w.x);
+    b = unpack2<__nv_bfloat16>(w.y);
+  } else {
+    a = unpack2<__half>(w.x);
+    b = unpack2<__half>(w.y);
+  }
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 // Stage R token rows of a token-major tensor into shared memory as fp32: row r is
 // token tok0 + t0 + r, its columns [0, W) start at element (tok0 + t0 + r) * rs + co
 // (W, rs, co multiples of 8). Rows with t0 + r >= lim are zero; each value is scaled by
 // scale[t0 + r] when `scale` is given. COLS=false writes dst[r * ldd + c], COLS=true
-// dst[c * ldd + r]. All of a thread's loads (V 16-byte vectors, R * W / 8 <= 256 V) are
+// dst[c * ldd + r]. All of a thread's loads (V 16-byte vectors, R * W / 8 <= NT V) are
 // issued before its stores, so the tile costs one memory latency.
-template <int V, bool COLS>
+template <int V, bool COLS, int NT = 256>
 __device__ __forceinline__ void stage(float* dst, int ldd, const void* src, int dt, long long tok0, int t0, int R,
                                       long long rs, long long co, int W, int lim, const float* scale) {
   const int vpr = W >> 3, nv = R * vpr;
   float v[V][8];
 #pragma unroll
   for (int j = 0; j < V; ++j) {
-    const int vi = threadIdx.x + 256 * j;
+    const int vi = threadIdx.x + NT * j;
     const int r = vi / vpr, c = (vi - r * vpr) << 3;
     if (vi < nv && t0 + r < lim) {
       ld8(src, (tok0 + t0 + r) * rs + co + c, dt, v[j]);
@@ -134,7 +151,7 @@ __device__ __forceinline__ void stage(float* dst, int ldd, const void* src, int 
   }
 #pragma unroll
   for (int j = 0; j < V; ++j) {
-    const int vi = threadIdx.x + 256 * j;
+    const int vi = threadIdx.x + NT * j;
     if (vi >= nv) continue;
     const int r = vi / vpr, c = (vi - r * vpr) << 3;
     const float sc = scale ? scale[t0 + r] : 1.f;
@@ -234,15 +251,15 @@ __global__ void __launch_bounds__(256, 2) bwd_chunk_states_kernel(
 // bwd_state_pass: per (row, head, 1024 state elements), 4 elements per thread.
 // Forward (forward_kernel.py:244-249): states[c] <- prev; prev = exp(cl_c) prev + S_c.
 // Reverse (backward_kernel.py:144-157), g = gradient of the state leaving chunk c:
-//   dlast_c = sum(prev_c * g) * exp(cl_c)   (per-CTA partial, summed by bwd_intra)
+//   dlast_c = sum(prev_c * g) * exp(cl_c)   (per-warp partials, summed by bwd_intra)
 //   hg[c] <- g;  g = exp(cl_c) g + hg_intra[c];   h_init_grad = g after chunk 0.
 // ===========================================================================
 __global__ void __launch_bounds__(256) bwd_state_pass_kernel(
     float* __restrict__ states, float* __restrict__ hg, const float* __restrict__ cum,
     const float* __restrict__ h_init, const float* __restrict__ h_last_grad, float* __restrict__ h_init_grad,
     float* __restrict__ dl_part, ChunkMap cm, int H, int PN) {
-  __shared__ float tmp[8];
-  const int row = blockIdx.z, h = blockIdx.y, nsl = gridDim.x;
+  const int row = blockIdx.z, h = blockIdx.y;
+  const int nparts = gridDim.x * 8, part = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int e0 = (blockIdx.x * 256 + threadIdx.x) * 4;
   const bool act = e0 < PN;
   int first, count;
@@ -255,38 +272,40 @@ __global__ void __launch_bounds__(256) bwd_state_pass_kernel(
     count = cm.nc;
   }
   const int cs = cm.cs;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  auto at = [&](float* base, int c) { return base + ((long long)(first + c) * H + h) * PN + e0; };
+  auto scale = [&](int c) { return expf(cum[((long long)(first + c) * H + h) * cs + cs - 1]); };
   const long long hoff = ((long long)row * H + h) * PN + e0;
-  float4 prev = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (h_init && act) prev = *reinterpret_cast<const float4*>(h_init + hoff);
+  float4 prev = (h_init && act) ? *reinterpret_cast<const float4*>(h_init + hoff) : zero;
+  float4 nxt = (act && count > 0) ? *reinterpret_cast<const float4*>(at(states, 0)) : zero;
   for (int c = 0; c < count; ++c) {
-    const long long kk = first + c;
-    const long long off = (kk * H + h) * PN + e0;
-    const float sc = expf(cum[(kk * H + h) * cs + cs - 1]);
-    if (act) {
-      const float4 s = *reinterpret_cast<const float4*>(states + off);
-      *reinterpret_cast<float4*>(states + off) = prev;
-      prev.x = fmaf(sc, prev.x, s.x);
-      prev.y = fmaf(sc, prev.y, s.y);
-      prev.z = fmaf(sc, prev.z, s.z);
-      prev.w = fmaf(sc, prev.w, s.w);
-    }
+    const float4 sv = nxt;
+    if (act && c + 1 < count) nxt = *reinterpret_cast<const float4*>(at(states, c + 1));
+    const float sc = scale(c);
+    if (act) *reinterpret_cast<float4*>(at(states, c)) = prev;
+    prev.x = fmaf(sc, prev.x, sv.x);
+    prev.y = fmaf(sc, prev.y, sv.y);
+    prev.z = fmaf(sc, prev.z, sv.z);
+    prev.w = fmaf(sc, prev.w, sv.w);
   }
-  float4 gr = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (h_last_grad && act) gr = *reinterpret_cast<const float4*>(h_last_grad + hoff);
+  float4 gr = (h_last_grad && act) ? *reinterpret_cast<const float4*>(h_last_grad + hoff) : zero;
+  float4 pv_n = zero, hg_n = zero;
+  if (act && count > 0) {
+    pv_n = *reinterpret_cast<const float4*>(at(states, count - 1));
+    hg_n = *reinterpret_cast<const float4*>(at(hg, count - 1));
+  }
   for (int c = count - 1; c >= 0; --c) {
-    const long long kk = first + c;
-    const long long off = (kk * H + h) * PN + e0;
-    const float sc = expf(cum[(kk * H + h) * cs + cs - 1]);
-    float part = 0.f;
-    float4 hgi = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (act) {
-      const float4 pv = *reinterpret_cast<const float4*>(states + off);
-      part = dot4(pv, gr, 0.f);
-      hgi = *reinterpret_cast<const float4*>(hg + off);
-      *reinterpret_cast<float4*>(hg + off) = gr;
+    const float4 pv = pv_n, hgi = hg_n;
+    if (act && c > 0) {
+      pv_n = *reinterpret_cast<const float4*>(at(states, c - 1));
+      hg_n = *reinterpret_cast<const float4*>(at(hg, c - 1));
     }
-    const float tot = block_sum(part, tmp);
-    if (threadIdx.x == 0) dl_part[(kk * H + h) * nsl + blockIdx.x] = tot * sc;
+    const float sc = scale(c);
+    float d = act ? dot4(pv, gr, 0.f) : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+    if ((threadIdx.x & 31) == 0) dl_part[((long long)(first + c) * H + h) * nparts + part] = d * sc;
+    if (act) *reinterpret_cast<float4*>(at(hg, c)) = gr;
     gr.x = fmaf(sc, gr.x, hgi.x);
     gr.y = fmaf(sc, gr.y, hgi.y);
     gr.z = fmaf(sc, gr.z, hgi.z);
@@ -356,7 +375,7 @@ __global__ void __launch_bounds__(256) bwd_cb_kernel(const void* __restrict__ Bm
 //   gC[l] = sum_n (that C_grad row) C[l,n]                 (:537-538)
 // accS goes to a scratch buffer for bwd_intra; rows at or past `length` are zero.
 // ===========================================================================
-__global__ void __launch_bounds__(256) bwd_state_grad_kernel(
+__global__ void __launch_bounds__(256, 2) bwd_state_grad_kernel(
     const void* __restrict__ u, const void* __restrict__ Bm, const void* __restrict__ Cm,
     const void* __restrict__ yg, const float* __restrict__ dt, const float* __restrict__ cum,
     const float* __restrict__ prev, const float* __restrict__ hg, float* __restrict__ accS_out,
@@ -371,8 +390,7 @@ __global__ void __launch_bounds__(256) bwd_state_grad_kernel(
   float* hgS = sm;                  // [kPmax][kLDN]
   float* pvS = hgS + kPmax * kLDN;  // [kPmax][kLDN]
   float* bt = pvS + kPmax * kLDN;   // [kLT][kLDN]
-  float* ct = bt + kLT * kLDN;      // [kLT][kLDN]
-  float* uw = ct + kLT * kLDN;      // [kLT][kLDP]
+  float* uw = bt + kLT * kLDN;      // [kLT][kLDP]
   float* ye = uw + kLT * kLDP;      // [kLT][kLDP]
   float* sS = ye + kLT * kLDP;      // [kCSmax] exp(min(cum_last - cum_l, 0))
   float* wS = sS + kCSmax;          // [kCSmax] sS * dt
@@ -418,7 +436,6 @@ __global__ void __launch_bounds__(256) bwd_state_grad_kernel(
     __syncthreads();
     const long long rsB = (long long)G * N, coB = (long long)g * N, rsU = (long long)H * P, coU = (long long)h * P;
     stage<2, false>(bt, kLDN, Bm, xdt, ci.tok0, l0, kLT, rsB, coB, N, vl, nullptr);
-    stage<2, false>(ct, kLDN, Cm, xdt, ci.tok0, l0, kLT, rsB, coB, N, vl, nullptr);
     stage<1, false>(uw, kLDP, u, xdt, ci.tok0, l0, kLT, rsU, coU, P, vl, wS);
     stage<1, false>(ye, kLDP, yg, ydt, ci.tok0, l0, kLT, rsU, coU, P, vl, eS);
     __syncthreads();
@@ -507,7 +524,7 @@ __global__ void __launch_bounds__(256) bwd_state_grad_kernel(
                       make_float4(bA[i][4 * jj], bA[i][4 * jj + 1], bA[i][4 * jj + 2], bA[i][4 * jj + 3]));
             atomicAdd(reinterpret_cast<float4*>(Cgrad + row + n0),
                       make_float4(cA[i][4 * jj], cA[i][4 * jj + 1], cA[i][4 * jj + 2], cA[i][4 * jj + 3]));
-            const float4 cr = lds4(ct + lr * kLDN + n0);
+            const float4 cr = ld4(Cm, row + n0, xdt);
             gsum = fmaf(cA[i][4 * jj], cr.x, gsum);
             gsum = fmaf(cA[i][4 * jj + 1], cr.y, gsum);
             gsum = fmaf(cA[i][4 * jj + 2], cr.z, gsum);
@@ -534,7 +551,10 @@ __global__ void __launch_bounds__(256) bwd_state_grad_kernel(
 //   delta_raw_grad = (total A + ddt), 0 where dt was clamped, * sigmoid(pre) (softplus)
 //   A / bias partials per (chunk, head).
 // ===========================================================================
-__global__ void __launch_bounds__(256) bwd_intra_kernel(
+constexpr int kIT = 512;         // bwd_intra threads
+constexpr int kIR = 64;          // bwd_intra row tile
+
+__global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
     const void* __restrict__ u, const void* __restrict__ yg, const void* __restrict__ delta_raw,
     const float* __restrict__ A, const float* __restrict__ delta_bias, const float* __restrict__ dt,
     const float* __restrict__ cum, const float* __restrict__ CB, const float* __restrict__ accS,
@@ -557,32 +577,32 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
   constexpr int LDS = kLT + 4;
   float* uS = sm;                     // [kCSmax][kLDP]
   float* yS = uS + kCSmax * kLDP;     // [kCSmax][kLDP]
-  float* Mt = yS + kCSmax * kLDP;     // [kLT][LDS]
-  float* dts = Mt + kLT * LDS;        // [kCSmax] each below
+  float* Mt = yS + kCSmax * kLDP;     // [kIR][LDS]: rows l of the tile, 32 columns s
+  float* cbS = Mt + kIR * LDS;        // [kIR][kLDP]: CB rows of the tile, 64 columns
+  float* dts = cbS + kIR * kLDP;      // [kCSmax] each below
   float* cms = dts + kCSmax;
   float* rows = cms + kCSmax;
   float* cols = rows + kCSmax;
   float* ddts = cols + kCSmax;
   float* gBs = ddts + kCSmax;
   float* revc = gBs + kCSmax;
-  float* tmp = revc + kCSmax;         // [8]
-  float* cbS = tmp + 8;               // [kLT][kLDP]: CB rows of the tile, 64 columns
+  float* tmp = revc + kCSmax;         // [16]
   const long long kh = (long long)k * H + h;
   const long long kg = ((long long)k * G + g) * cs * cs;
-  stage<8, false>(uS, kLDP, u, xdt, ci.tok0, 0, cs, (long long)H * P, (long long)h * P, P, vl, nullptr);
-  stage<8, false>(yS, kLDP, yg, ydt, ci.tok0, 0, cs, (long long)H * P, (long long)h * P, P, vl, nullptr);
-  for (int i = tid; i < kCSmax; i += 256) {
+  stage<4, false, kIT>(uS, kLDP, u, xdt, ci.tok0, 0, cs, (long long)H * P, (long long)h * P, P, vl, nullptr);
+  stage<4, false, kIT>(yS, kLDP, yg, ydt, ci.tok0, 0, cs, (long long)H * P, (long long)h * P, P, vl, nullptr);
+  for (int i = tid; i < kCSmax; i += kIT) {
     dts[i] = i < cs ? dt[kh * cs + i] : 0.f;
     cms[i] = i < cs ? cum[kh * cs + i] : 0.f;
     rows[i] = cols[i] = ddts[i] = gBs[i] = 0.f;
   }
   __syncthreads();
-  const int tl = tid >> 4, tq = tid & 15;
+  const int tl = tid >> 4, tq = tid & 15;  // rows l0 + tl + 32 i (i < 2)
   const int p0 = 4 * tq;
   const bool pvalid = p0 < P;
 
-  for (int l0 = 0; l0 < ci.lim; l0 += kLT) {
-    // accY: rows l = l0 + tl + 16 i, columns p0 .. p0 + 3
+  for (int l0 = 0; l0 < ci.lim; l0 += kIR) {
+    // accY: rows l = l0 + tl + 32 i, columns p0 .. p0 + 3
     float aY[2][4];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
@@ -592,9 +612,9 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
       __syncthreads();
       {
         // thread: CB row s = s0 + c, columns l0 + r4 .. + 3 (one 16-byte load)
-        const int c = tid >> 3, r4 = (tid & 7) * 4, s = s0 + c;
+        const int c = tid >> 4, r4 = (tid & 15) * 4, s = s0 + c;
         float4 cb = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (s < vl) cb = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)s * cs + l0 + r4));
+        if (s < vl && l0 + r4 < cs) cb = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)s * cs + l0 + r4));
         const float cs_ = cms[s];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -610,7 +630,7 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
         for (int c = 0; c < kLT; c += 4) {
           float4 a[2];
 #pragma unroll
-          for (int i = 0; i < 2; ++i) a[i] = lds4(Mt + (tl + 16 * i) * LDS + c);
+          for (int i = 0; i < 2; ++i) a[i] = lds4(Mt + (tl + 32 * i) * LDS + c);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float4 y4 = lds4(yS + (s0 + c + q) * kLDP + p0);
@@ -629,7 +649,7 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
     // u_grad, ddt, gB for the tile rows
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-      const int l = l0 + tl + 16 * i;
+      const int l = l0 + tl + 32 * i;
       float dpart = 0.f, bpart = 0.f;
       if (l < cs && pvalid) {
         float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -654,15 +674,15 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
         gBs[l] = bpart * dts[l];
       }
     }
-    // CB_grad and the intra-chunk decay terms: rows l = l0 + tl + 16 i, columns
+    // CB_grad and the intra-chunk decay terms: rows l = l0 + tl + 32 i, columns
     // s = sb + tq + 16 j of 64-wide column blocks left of the tile's end.
     float rs[2] = {0.f, 0.f};
-    const int send = min(l0 + kLT, vl);
+    const int send = min(l0 + kIR, vl);
     for (int sb = 0; sb < send; sb += 64) {
       __syncthreads();  // cbS of the previous block consumed
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        const int vi = tid + 256 * j, r = vi >> 4, c4 = (vi & 15) * 4;
+        const int vi = tid + kIT * j, r = vi >> 4, c4 = (vi & 15) * 4;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (sb + c4 < cs && l0 + r < vl)
           v = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)(l0 + r) * cs + sb + c4));
@@ -677,10 +697,13 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
       int srow[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) srow[j] = min(sb + tq + 16 * j, cs - 1) * kLDP;
+      int lrow[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) lrow[i] = min(l0 + tl + 32 * i, cs - 1) * kLDP;
       for (int p = 0; p < P; p += 4) {
         float4 a[2], b[4];
 #pragma unroll
-        for (int i = 0; i < 2; ++i) a[i] = lds4(yS + (l0 + tl + 16 * i) * kLDP + p);
+        for (int i = 0; i < 2; ++i) a[i] = lds4(yS + lrow[i] + p);
 #pragma unroll
         for (int j = 0; j < 4; ++j) b[j] = lds4(uS + srow[j] + p);
 #pragma unroll
@@ -690,7 +713,7 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
       }
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        const int l = l0 + tl + 16 * i;
+        const int l = l0 + tl + 32 * i;
         if (l >= vl) continue;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -699,7 +722,7 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
           const float cbg = gm[i][j] * dts[s] * expf(fminf(cms[l] - cms[s], 0.f));
           atomicAdd(CBg + kg + (long long)l * cs + s, cbg);
           if (s < l) {
-            const float w = cbg * cbS[(tl + 16 * i) * kLDP + tq + 16 * j];
+            const float w = cbg * cbS[(tl + 32 * i) * kLDP + tq + 16 * j];
             rs[i] += w;
             atomicAdd(&cols[s], w);
           }
@@ -709,7 +732,7 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const float r = half_warp_sum(rs[i]);
-      const int l = l0 + tl + 16 * i;
+      const int l = l0 + tl + 32 * i;
       if (tq == 0 && l < cs) rows[l] = r;
     }
   }
@@ -721,13 +744,13 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
   for (int i = 0; i < nsl; ++i) dlast += dl_part[kh * nsl + i];
   float unused;
   const float xi = t < cs ? cols[t] - rows[t] : 0.f;
-  const float intra = block_excl_scan(xi, tmp, unused);
+  const float intra = block_excl_scan<kIT / 32>(xi, tmp, unused);
   const float xb = t < vl - 1 ? gBs[t] : 0.f;
-  const float dB = block_excl_scan(xb, tmp, unused);
+  const float dB = block_excl_scan<kIT / 32>(xb, tmp, unused);
   // sum_{m >= tr} gC_m: thread t scans element tr = cs-1-t, so threads before it hold m > tr
   const int tr = cs - 1 - t;
   const float xc = (tr >= 0 && tr < vl) ? gC[kh * cs + tr] : 0.f;
-  const float exc = block_excl_scan(xc, tmp, unused);
+  const float exc = block_excl_scan<kIT / 32>(xc, tmp, unused);
   if (tr >= 0) revc[tr] = exc + xc;
   __syncthreads();
   float aP = 0.f, bP = 0.f;
@@ -748,8 +771,8 @@ __global__ void __launch_bounds__(256) bwd_intra_kernel(
     }
     st_any(draw_grad, tok * H + h, ddt_dtype, gg);
   }
-  const float as = block_sum(aP, tmp);
-  const float bs = block_sum(bP, tmp);
+  const float as = block_sum<kIT / 32>(aP, tmp);
+  const float bs = block_sum<kIT / 32>(bP, tmp);
   if (tid == 0) {
     A_part[kh] = as;
     bias_part[kh] = bs;
@@ -878,9 +901,9 @@ __global__ void __launch_bounds__(256) bwd_param_reduce_kernel(const float* __re
 constexpr size_t kSmemStates = (size_t)((kPmax + kNmax) * kLDT + kCSmax) * sizeof(float);
 constexpr size_t kSmemCB = (size_t)(2 * 64 * kLDN) * sizeof(float);
 constexpr size_t kSmemStateGrad =
-    (size_t)(2 * kPmax * kLDN + 2 * kLT * kLDN + 2 * kLT * kLDP + 3 * kCSmax) * sizeof(float);
+    (size_t)(2 * kPmax * kLDN + kLT * kLDN + 2 * kLT * kLDP + 3 * kCSmax) * sizeof(float);
 constexpr size_t kSmemIntra =
-    (size_t)(2 * kCSmax * kLDP + kLT * (kLT + 4) + 7 * kCSmax + 8 + kLT * kLDP) * sizeof(float);
+    (size_t)(2 * kCSmax * kLDP + kIR * (kLT + 4) + kIR * kLDP + 7 * kCSmax + 16) * sizeof(float);
 
 cudaError_t opt_in(const void* fn, size_t bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
@@ -893,7 +916,7 @@ bool bwd_supported(int P, int N, int cs) {
          cs <= kCSmax && cs % kLT == 0;
 }
 
-size_t bwd_dl_slices(int P, int N) { return (size_t)((P * N / 4 + 255) / 256); }
+size_t bwd_dl_slices(int P, int N) { return (size_t)((P * N / 4 + 255) / 256) * 8; }
 
 cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
   const int H = c.H, G = c.G, P = c.P, N = c.N, cs = c.cs, PN = P * N;
@@ -915,8 +938,8 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
       a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, c.cm, H, G, P, N, a.x_dtype, a.y_dtype);
   if ((e = cudaGetLastError())) return e;
   if (a.ev[1]) cudaEventRecord(a.ev[1], c.stream);
-  const int nsl = (int)bwd_dl_slices(P, N);
-  bwd_state_pass_kernel<<<dim3((unsigned)nsl, (unsigned)H, (unsigned)c.nrows), 256, 0, c.stream>>>(
+  const int nsl = (int)bwd_dl_slices(P, N);  // per-warp partials of the decay_last gradient
+  bwd_state_pass_kernel<<<dim3((unsigned)(nsl / 8), (unsigned)H, (unsigned)c.nrows), 256, 0, c.stream>>>(
       a.states, a.hg, a.cum, a.h_init, a.h_last_grad, a.h_init_grad, a.dl_part, c.cm, H, PN);
   if ((e = cudaGetLastError())) return e;
   const int nt = (cs + 63) / 64;
@@ -929,7 +952,7 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
       a.x_dtype, a.y_dtype);
   if ((e = cudaGetLastError())) return e;
   if (a.ev[3]) cudaEventRecord(a.ev[3], c.stream);
-  bwd_intra_kernel<<<gkh, 256, kSmemIntra, c.stream>>>(
+  bwd_intra_kernel<<<gkh, kIT, kSmemIntra, c.stream>>>(
       a.u, a.y_grad, a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, a.dl_part, nsl, a.CBg,
       a.u_grad, a.delta_raw_grad, a.A_part, a.bias_part, c.cm, H, G, P, a.x_dtype, a.y_dtype, a.dt_dtype, c.use_sp,
       c.dmin, c.dmax);
