@@ -178,7 +178,7 @@ constexpr int kLDP = kPmax + 4;
 //   z = 0: S[p,n]  = sum_{l<len} u[l,p] exp(min(cum_last - cum_l, 0)) dt_l B[l,n]
 //          (the chunk_state forward recomputed, backward.py:487; dt = 0 past len)
 //   z = 1: HG[p,n] = sum_{l<len} y_grad[l,p] exp(cum_l) C[l,n]   (backward_kernel.py:23-93)
-// 32-token tiles staged transposed ([feature][token]); thread (tp, tn) owns
+// 64-token tiles staged transposed ([feature][token]); thread (tp, tn) owns
 // p = tp + 16 i (i < 4), n = tn + 16 j (j < 8).
 // ===========================================================================
 __global__ void __launch_bounds__(256, 2) bwd_chunk_states_kernel(
@@ -192,13 +192,14 @@ __global__ void __launch_bounds__(256, 2) bwd_chunk_states_kernel(
   ChunkInfo ci;
   if (!chunk_info(cm, k, ci)) return;
   const int cs = cm.cs, g = h / (H / G), vl = ci.vlim;
-  float* aT = sm;                   // [kPmax][kLDT]
-  float* bT = aT + kPmax * kLDT;    // [kNmax][kLDT]
-  float* scl = bT + kNmax * kLDT;   // [kCSmax]
+  constexpr int TT = 64, LD = TT + 4;  // 64-token tiles, [feature][token]
+  float* aT = sm;                   // [kPmax][LD]
+  float* bT = aT + kPmax * LD;      // [kNmax][LD]
+  float* scl = bT + kNmax * LD;     // [kCSmax]
   const long long kh = (long long)k * H + h;
   const float clast = cum[kh * cs + cs - 1];
-  for (int i = tid; i < cs; i += 256) {
-    const float c = cum[kh * cs + i];
+  for (int i = tid; i < kCSmax; i += 256) {
+    const float c = i < vl ? cum[kh * cs + i] : 0.f;
     scl[i] = i < vl ? (which == 0 ? expf(fminf(clast - c, 0.f)) * dt[kh * cs + i] : expf(c)) : 0.f;
   }
   const void* asrc = which == 0 ? u : yg;
@@ -207,22 +208,22 @@ __global__ void __launch_bounds__(256, 2) bwd_chunk_states_kernel(
   const int tp = tid >> 4, tn = tid & 15;
   int pr[4], nr[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) pr[i] = min(tp + 16 * i, P - 1) * kLDT;
+  for (int i = 0; i < 4; ++i) pr[i] = min(tp + 16 * i, P - 1) * LD;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) nr[j] = min(tn + 16 * j, N - 1) * kLDT;
+  for (int j = 0; j < 8; ++j) nr[j] = min(tn + 16 * j, N - 1) * LD;
   float acc[4][8];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
 
-  for (int l0 = 0; l0 < vl; l0 += kLT) {
+  for (int l0 = 0; l0 < vl; l0 += TT) {
     __syncthreads();
-    stage<1, true>(aT, kLDT, asrc, adt, ci.tok0, l0, kLT, (long long)H * P, (long long)h * P, P, vl, scl);
-    stage<2, true>(bT, kLDT, bsrc, xdt, ci.tok0, l0, kLT, (long long)G * N, (long long)g * N, N, vl, nullptr);
+    stage<2, true>(aT, LD, asrc, adt, ci.tok0, l0, TT, (long long)H * P, (long long)h * P, P, vl, scl);
+    stage<4, true>(bT, LD, bsrc, xdt, ci.tok0, l0, TT, (long long)G * N, (long long)g * N, N, vl, nullptr);
     __syncthreads();
 #pragma unroll 2
-    for (int l = 0; l < kLT; l += 4) {
+    for (int l = 0; l < TT; l += 4) {
       float4 a[4], b[8];
 #pragma unroll
       for (int i = 0; i < 4; ++i) a[i] = lds4(aT + pr[i] + l);
@@ -553,6 +554,8 @@ __global__ void __launch_bounds__(256, 2) bwd_state_grad_kernel(
 // ===========================================================================
 constexpr int kIT = 512;         // bwd_intra threads
 constexpr int kIR = 64;          // bwd_intra row tile
+constexpr int kIB = 128;         // bwd_intra column block
+constexpr int kLDB = kIB + 4;
 
 __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
     const void* __restrict__ u, const void* __restrict__ yg, const void* __restrict__ delta_raw,
@@ -574,12 +577,11 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
     return;
   }
   const int cs = cm.cs, g = h / (H / G), vl = ci.vlim;
-  constexpr int LDS = kLT + 4;
   float* uS = sm;                     // [kCSmax][kLDP]
   float* yS = uS + kCSmax * kLDP;     // [kCSmax][kLDP]
-  float* Mt = yS + kCSmax * kLDP;     // [kIR][LDS]: rows l of the tile, 32 columns s
-  float* cbS = Mt + kIR * LDS;        // [kIR][kLDP]: CB rows of the tile, 64 columns
-  float* dts = cbS + kIR * kLDP;      // [kCSmax] each below
+  float* Mt = yS + kCSmax * kLDP;     // [kIR][kLDB]: rows l of the tile, kIB columns s
+  float* cbS = Mt + kIR * kLDB;       // [kIR][kLDB]: CB rows of the tile, kIB columns
+  float* dts = cbS + kIR * kLDB;      // [kCSmax] each below
   float* cms = dts + kCSmax;
   float* rows = cms + kCSmax;
   float* cols = rows + kCSmax;
@@ -608,29 +610,39 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
     for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) aY[i][j] = 0.f;
-    for (int s0 = l0; s0 < vl; s0 += kLT) {
+    for (int s0 = l0; s0 < vl; s0 += kIB) {
       __syncthreads();
       {
-        // thread: CB row s = s0 + c, columns l0 + r4 .. + 3 (one 16-byte load)
-        const int c = tid >> 4, r4 = (tid & 15) * 4, s = s0 + c;
-        float4 cb = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (s < vl && l0 + r4 < cs) cb = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)s * cs + l0 + r4));
-        const float cs_ = cms[s];
+        // CB rows s = s0 + c (c < kIB), columns l0 + r4 .. + 3: four 16-byte loads per thread
+        float4 cb[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int l = l0 + r4 + e;
-          float v = 0.f;
-          if (s >= l && s < vl && l < vl) v = comp(cb, e) * expf(fminf(cs_ - cms[l], 0.f));
-          Mt[(r4 + e) * LDS + c] = v;
+        for (int j = 0; j < 4; ++j) {
+          const int vi = tid + kIT * j, c = vi >> 4, r4 = (vi & 15) * 4, s = s0 + c;
+          cb[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (s < vl && l0 + r4 < cs)
+            cb[j] = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)s * cs + l0 + r4));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int vi = tid + kIT * j, c = vi >> 4, r4 = (vi & 15) * 4, s = s0 + c;
+          const float cs_ = s < cs ? cms[s] : 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int l = l0 + r4 + e;
+            float v = 0.f;
+            if (s >= l && s < vl && l < vl) v = comp(cb[j], e) * expf(fminf(cs_ - cms[l], 0.f));
+            Mt[(r4 + e) * kLDB + c] = v;
+          }
         }
       }
       __syncthreads();
       if (pvalid) {
+        const int cend = min(kIB, cs - s0);  // yS rows stay inside the chunk
 #pragma unroll 2
-        for (int c = 0; c < kLT; c += 4) {
+        for (int c = 0; c < cend; c += 4) {
           float4 a[2];
 #pragma unroll
-          for (int i = 0; i < 2; ++i) a[i] = lds4(Mt + (tl + 32 * i) * LDS + c);
+          for (int i = 0; i < 2; ++i) a[i] = lds4(Mt + (tl + 32 * i) * kLDB + c);
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float4 y4 = lds4(yS + (s0 + c + q) * kLDP + p0);
@@ -675,54 +687,61 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
       }
     }
     // CB_grad and the intra-chunk decay terms: rows l = l0 + tl + 32 i, columns
-    // s = sb + tq + 16 j of 64-wide column blocks left of the tile's end.
+    // s = sb + tq + 16 j of kIB-wide column blocks left of the tile's end.
     float rs[2] = {0.f, 0.f};
     const int send = min(l0 + kIR, vl);
-    for (int sb = 0; sb < send; sb += 64) {
+    for (int sb = 0; sb < send; sb += kIB) {
       __syncthreads();  // cbS of the previous block consumed
+      {
+        float4 v[4];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int vi = tid + kIT * j, r = vi >> 4, c4 = (vi & 15) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (sb + c4 < cs && l0 + r < vl)
-          v = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)(l0 + r) * cs + sb + c4));
-        *reinterpret_cast<float4*>(cbS + r * kLDP + c4) = v;
+        for (int j = 0; j < 4; ++j) {
+          const int vi = tid + kIT * j, r = vi >> 5, c4 = (vi & 31) * 4;
+          v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (sb + c4 < cs && l0 + r < vl)
+            v[j] = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)(l0 + r) * cs + sb + c4));
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int vi = tid + kIT * j, r = vi >> 5, c4 = (vi & 31) * 4;
+          *reinterpret_cast<float4*>(cbS + r * kLDB + c4) = v[j];
+        }
       }
       __syncthreads();
-      float gm[2][4];
+      float gm[2][8];
 #pragma unroll
       for (int i = 0; i < 2; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) gm[i][j] = 0.f;
-      int srow[4];
+        for (int j = 0; j < 8; ++j) gm[i][j] = 0.f;
+      int srow[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) srow[j] = min(sb + tq + 16 * j, cs - 1) * kLDP;
+      for (int j = 0; j < 8; ++j) srow[j] = min(sb + tq + 16 * j, cs - 1) * kLDP;
       int lrow[2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) lrow[i] = min(l0 + tl + 32 * i, cs - 1) * kLDP;
       for (int p = 0; p < P; p += 4) {
-        float4 a[2], b[4];
+        float4 a[2], b[8];
 #pragma unroll
         for (int i = 0; i < 2; ++i) a[i] = lds4(yS + lrow[i] + p);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) b[j] = lds4(uS + srow[j] + p);
+        for (int j = 0; j < 8; ++j) b[j] = lds4(uS + srow[j] + p);
 #pragma unroll
         for (int i = 0; i < 2; ++i)
 #pragma unroll
-          for (int j = 0; j < 4; ++j) gm[i][j] = dot4(a[i], b[j], gm[i][j]);
+          for (int j = 0; j < 8; ++j) gm[i][j] = dot4(a[i], b[j], gm[i][j]);
       }
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int l = l0 + tl + 32 * i;
         if (l >= vl) continue;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 8; ++j) {
           const int s = sb + tq + 16 * j;
           if (s > l) continue;
           const float cbg = gm[i][j] * dts[s] * expf(fminf(cms[l] - cms[s], 0.f));
           atomicAdd(CBg + kg + (long long)l * cs + s, cbg);
           if (s < l) {
-            const float w = cbg * cbS[(tl + 32 * i) * kLDP + tq + 16 * j];
+            const float w = cbg * cbS[(tl + 32 * i) * kLDB + tq + 16 * j];
             rs[i] += w;
             atomicAdd(&cols[s], w);
           }
@@ -898,12 +917,11 @@ __global__ void __launch_bounds__(256) bwd_param_reduce_kernel(const float* __re
   }
 }
 
-constexpr size_t kSmemStates = (size_t)((kPmax + kNmax) * kLDT + kCSmax) * sizeof(float);
+constexpr size_t kSmemStates = (size_t)((kPmax + kNmax) * 68 + kCSmax) * sizeof(float);
 constexpr size_t kSmemCB = (size_t)(2 * 64 * kLDN) * sizeof(float);
 constexpr size_t kSmemStateGrad =
     (size_t)(2 * kPmax * kLDN + kLT * kLDN + 2 * kLT * kLDP + 3 * kCSmax) * sizeof(float);
-constexpr size_t kSmemIntra =
-    (size_t)(2 * kCSmax * kLDP + kIR * (kLT + 4) + kIR * kLDP + 7 * kCSmax + 16) * sizeof(float);
+constexpr size_t kSmemIntra = (size_t)(2 * kCSmax * kLDP + 2 * kIR * kLDB + 7 * kCSmax + 16) * sizeof(float);
 
 cudaError_t opt_in(const void* fn, size_t bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
