@@ -24,6 +24,9 @@
  *   ssm_conv_prefill       <- modules/ssm.py:112-134 (SiLU, depthwise causal conv1d,
  *                             split into x, B, C) and inference/ssm_cache.py:10-36
  *                             SSMCache.build_conv_ctx
+ *   sattn_decode_step      <- modules/selective_attention.py:394-405 (SelectiveMHA.step:
+ *                             cache update and pos-mode gated softmax attention) and
+ *                             inference/selective_attn_cache.py:27-42 SelectiveAttnCache.update_kv
  *   ssm_conv_decode        <- modules/ssm.py:173-186 (decode step: cache update, SiLU,
  *                             weighted sum, split) and inference/ssm_cache.py:38-43
  *                             SSMCache.update
@@ -259,6 +262,26 @@ int ssm_conv_prefill(const void* hbc, int64_t row_stride, const float* weight, c
 int ssm_conv_decode(const void* hbc_new, int64_t row_stride, void* conv_ctx, const float* weight, const float* bias,
                     void* x, void* B, void* C, int64_t batch, int64_t inner, int64_t gn, int64_t kernel_size,
                     int32_t dtype, void* stream);
+
+/*
+ * Selective-attention decode step (modules/selective_attention.py:394-405): writes the
+ * token's key, value and log-gate at slot write_idx of the cache (as
+ * SelectiveAttnCache.update_kv does), then with n = write_idx + 1 cached keys
+ *   s_j = scale * q . k_j + (j < n-1 ? log_gate_j : 0),   out = softmax(s) . v
+ * (the pos-mode gated softmax: every cached key but the token's own is gated; a key
+ * whose log-gate is -inf drops out). The caller advances write_idx.
+ *   q_rot, k_rot, v      (b, H, D)          dtype
+ *   log_gate             (b, H)             fp32
+ *   k_cache, v_cache     (b, H, cap, D)     dtype, updated in place
+ *   log_gate_cache       (b, H, cap)        fp32, updated in place
+ *   out                  (b, H, D)          dtype
+ * head_dim D in {8, 16, 32, 64, 128, 256}; q_rot, k_cache, v_cache 16-byte aligned;
+ * 0 <= write_idx < cap.
+ */
+int sattn_decode_step(const void* q_rot, const void* k_rot, const void* v, const float* log_gate,
+                      void* k_cache, void* v_cache, float* log_gate_cache, int64_t write_idx, int64_t capacity,
+                      void* out, int64_t batch, int64_t nheads, int64_t head_dim, float scale, int32_t dtype,
+                      void* stream);
 
 #ifdef __cplusplus
 }

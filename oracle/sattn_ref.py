@@ -1,0 +1,54 @@
+"""CPU restatement of the selective-attention decode step (TEST INFRASTRUCTURE ONLY).
+
+Parity checker for the CUDA decode kernel (``csrc/sattn.cu``). Imported only by
+``tests/`` and ``bench.py``'s CPU legs; the product never imports it.
+
+Follows nmquan1503/selective-attention (paths relative to ``src/selective_attention/``):
+- ``inference/selective_attn_cache.py:27-42`` ``SelectiveAttnCache.update_kv``: the new
+  key, value and log-gate are written at ``write_idx``, which then advances;
+- ``modules/selective_attention.py:394-405`` (``SelectiveMHA.step``): scores of the
+  query against the first ``write_idx`` cached keys, times ``scale``; the pos-mode gated
+  softmax (``:126-128``) adds every cached key's log-gate except the newest one's
+  (the token itself); the output is the weighted sum of the cached values.
+
+Parity pin: golden vectors made with the reference's own cache class, ``_reset_cache``
+and ``_gated_softmax`` (``tests/golden/make_golden_sattn.py``).
+"""
+from __future__ import annotations
+
+import torch
+
+
+def update_kv(k_cache, v_cache, lg_cache, write_idx, k_rot, v, log_gate):
+    """``selective_attn_cache.py:39-42``: in-place write at ``write_idx``; returns the new index."""
+    k_cache[:, :, write_idx, :] = k_rot
+    v_cache[:, :, write_idx, :] = v
+    lg_cache[:, :, write_idx] = log_gate
+    return write_idx + 1
+
+
+def gated_softmax_pos(attn, log_gate):
+    """``modules/selective_attention.py:126-128``: gate every key but the last, then softmax."""
+    attn = attn.clone()
+    attn[..., :-1] += log_gate[..., :-1]
+    return torch.softmax(attn, dim=-1)
+
+
+def decode_attention(q_rot, k_cache, v_cache, lg_cache, n_keys, scale, dtype=torch.float32):
+    """``modules/selective_attention.py:398-405`` over the first ``n_keys`` cache slots.
+
+    ``q_rot`` ``(b, H, D)``; caches ``(b, H, cap, D)`` / ``(b, H, cap)``. Returns ``(b, H, D)``.
+    """
+    k = k_cache[:, :, :n_keys, :].to(dtype)
+    v = v_cache[:, :, :n_keys, :].to(dtype)
+    lg = lg_cache[:, :, :n_keys].to(dtype)
+    attn = (q_rot.to(dtype).unsqueeze(2) @ k.transpose(-2, -1)).squeeze(2) * scale
+    w = gated_softmax_pos(attn, lg)
+    return (w.unsqueeze(2) @ v).squeeze(2)
+
+
+def decode_step(q_rot, k_rot, v, log_gate, k_cache, v_cache, lg_cache, write_idx, scale, dtype=torch.float32):
+    """One decode step's cache update plus attention, as ``SelectiveMHA.step`` runs them
+    (``:394``, ``:399-405``). Updates the caches in place; returns ``(out, new write_idx)``."""
+    n = update_kv(k_cache, v_cache, lg_cache, write_idx, k_rot, v, log_gate)
+    return decode_attention(q_rot, k_cache, v_cache, lg_cache, n, scale, dtype), n

@@ -46,6 +46,8 @@ EXPORTS = {
     "ssu_fwd": (c_int, [c_void_p] * 10 + [c_int64] * 5 + [c_int32] * 5 + [c_float, c_float, c_void_p]),
     "ssm_conv_prefill": (c_int, [c_void_p, c_int64] + [c_void_p] * 7 + [c_int64] * 5 + [c_int32, c_void_p]),
     "ssm_conv_decode": (c_int, [c_void_p, c_int64] + [c_void_p] * 6 + [c_int64] * 4 + [c_int32, c_void_p]),
+    "sattn_decode_step": (c_int, [c_void_p] * 7 + [c_int64, c_int64, c_void_p] + [c_int64] * 3
+                          + [c_float, c_int32, c_void_p]),
 }
 
 

@@ -491,4 +491,20 @@ int ssm_conv_decode(const void* hbc_new, int64_t row_stride, void* conv_ctx, con
                                             reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int sattn_decode_step(const void* q_rot, const void* k_rot, const void* v, const float* log_gate, void* k_cache,
+                      void* v_cache, float* log_gate_cache, int64_t write_idx, int64_t capacity, void* out,
+                      int64_t batch, int64_t nheads, int64_t head_dim, float scale, int32_t dtype, void* stream) {
+  if (!q_rot || !k_rot || !v || !log_gate || !k_cache || !v_cache || !log_gate_cache || !out)
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (batch <= 0 || nheads <= 0 || capacity <= 0 || write_idx < 0 || write_idx >= capacity)
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (!sattn_decode_supported((int)head_dim) || batch * nheads > 0x7fffffffll || capacity > 0x7fffffffll)
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  if (!aligned16(q_rot) || !aligned16(k_cache) || !aligned16(v_cache)) return SSD_ERR_INVALID_ARGUMENT;
+  return cuda_status(launch_sattn_decode(q_rot, k_rot, v, log_gate, k_cache, v_cache, log_gate_cache,
+                                         (long long)write_idx, (long long)capacity, out, batch * nheads,
+                                         (int)head_dim, scale, dtype, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

@@ -62,6 +62,12 @@ bool bwd_supported(int P, int N, int cs);
 size_t bwd_dl_slices(int P, int N);
 cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a);
 
+// sattn.cu (selective-attention decode step; head_dim 8..256, a power of two)
+bool sattn_decode_supported(int D);
+cudaError_t launch_sattn_decode(const void* q, const void* k, const void* v, const float* lg, void* kc, void* vc,
+                                float* lgc, long long widx, long long cap, void* out, long long bh, int D,
+                                float scale, int dtype, cudaStream_t s);
+
 // ssd_tc.cu (tcgen05 + TMA; bf16/fp16 inputs, P = 64, N = 128, cs = 256; prev16 in the input type)
 bool tc_supported(int x_dtype, int P, int N, int cs);
 // delta_raw == NULL: dt / cum are inputs; otherwise chunk_cumsum is fused in and they are written.

@@ -416,3 +416,58 @@ def ssm_conv_decode(hBC, conv_ctx, conv_weight, conv_bias, inner_dim, gn, out=No
         _lib.ptr(Co), b, inner_dim, gn, K, _lib.dtype_code(hBC.dtype, "hBC"), _stream(dev))
     _lib.check(st, "ssm_conv_decode")
     return x, Bo, Co
+
+
+def sattn_decode_step(q_rot, k_rot, v, log_gate, k_cache, v_cache, log_gate_cache, write_idx, scale=None,
+                      out=None):
+    """Selective-attention decode step on a KV cache (C-ABI ``sattn_decode_step``).
+
+    Writes ``k_rot``, ``v`` and ``log_gate`` at slot ``write_idx`` of the caches, in place
+    (``inference/selective_attn_cache.py:39-41``), then returns the pos-mode gated softmax
+    attention of ``q_rot`` over the first ``write_idx + 1`` slots
+    (``modules/selective_attention.py:399-405``), ``(b, H, D)`` in ``q_rot``'s dtype. The caller
+    advances its write index. ``scale`` defaults to ``D ** -0.5`` (``:163``). Caches must be
+    contiguous ``(b, H, cap, D)`` / ``(b, H, cap)`` with ``log_gate_cache`` fp32.
+    """
+    b, H, D = q_rot.shape
+    dev = check_cuda([q_rot, k_rot, v, log_gate, k_cache, v_cache, log_gate_cache],
+                     ["q_rot", "k_rot", "v", "log_gate", "k_cache", "v_cache", "log_gate_cache"])
+    cap = k_cache.shape[2]
+    if k_cache.dim() != 4 or tuple(k_cache.shape) != (b, H, cap, D) or tuple(v_cache.shape) != (b, H, cap, D):
+        raise ValueError(f"[k_cache] expected (b, H, cap, D) = ({b}, {H}, cap, {D}) caches")
+    if tuple(log_gate_cache.shape) != (b, H, cap) or log_gate_cache.dtype != torch.float32:
+        raise ValueError("[log_gate_cache] expected a (b, H, cap) float32 cache")
+    for t, n in ((k_rot, "k_rot"), (v, "v")):
+        if tuple(t.shape) != (b, H, D):
+            raise ValueError(f"[{n}] expected shape {(b, H, D)}, got {tuple(t.shape)}")
+    for t, n in ((k_rot, "k_rot"), (v, "v"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        if t.dtype != q_rot.dtype:
+            raise ValueError(f"[{n}] dtype {t.dtype} differs from q_rot's {q_rot.dtype}")
+    for t, n in ((k_cache, "k_cache"), (v_cache, "v_cache"), (log_gate_cache, "log_gate_cache")):
+        if not t.is_contiguous():
+            raise ValueError(f"[{n}] must be contiguous (it is updated in place)")
+    if not 0 <= int(write_idx) < cap:
+        raise ValueError(f"[write_idx] {write_idx} outside the cache's {cap} slots")
+    q_rot = _aligned16(to_contiguous(q_rot))
+    k_rot, v = to_contiguous(k_rot), to_contiguous(v)
+    log_gate = to_contiguous(log_gate.float()).reshape(b, H)
+    if out is None:
+        out = torch.empty(b, H, D, device=dev, dtype=q_rot.dtype)
+    scale = float(D ** -0.5 if scale is None else scale)
+    st = _lib.lib().sattn_decode_step(_lib.ptr(q_rot), _lib.ptr(k_rot), _lib.ptr(v), _lib.ptr(log_gate),
+                                      _lib.ptr(k_cache), _lib.ptr(v_cache), _lib.ptr(log_gate_cache),
+                                      int(write_idx), cap, _lib.ptr(out), b, H, D, scale,
+                                      _lib.dtype_code(q_rot.dtype, "q_rot"), _stream(dev))
+    _lib.check(st, "sattn_decode_step")
+    return out
+
+
+def selective_attn_step(cache, q_rot, k_rot, v, log_select_gate, scale=None):
+    """``SelectiveMHA.step``'s cache update and attention (``modules/selective_attention.py:394-406``)
+    on a ``SelectiveAttnCache``-like object (``k_rot``, ``v``, ``log_gate`` tensors and
+    ``write_idx``): one kernel, ``cache.write_idx`` advanced. Returns ``out`` as
+    ``(b, H * D)``, the tensor the layer gates and projects."""
+    out = sattn_decode_step(q_rot, k_rot, v, log_select_gate, cache.k_rot, cache.v, cache.log_gate,
+                            cache.write_idx, scale)
+    cache.write_idx += 1
+    return out.view(out.shape[0], -1)

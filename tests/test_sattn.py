@@ -1,0 +1,116 @@
+"""Selective-attention decode step (row f4's decode half): the CPU oracle against golden
+vectors made with the reference's own cache and softmax code, and the CUDA kernel (C-ABI
+``sattn_decode_step``) against both.
+
+Golden vectors: ``tests/golden/make_golden_sattn.py``. Tolerances: fp32 rel 1e-4
+(``assert_fp32_close``); 16-bit outputs atol 2e-2 / rel 1e-2 (``assert_bf16_close``).
+"""
+import math
+import types
+
+import pytest
+import torch
+
+from conftest import assert_bf16_close, assert_fp32_close, load_golden
+from oracle import sattn_ref
+
+CASES = ["sattn_decode_dropped_fp32", "sattn_decode_fresh_d128_fp32", "sattn_decode_long_fp32"]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_oracle_matches_reference_golden(case):
+    g = load_golden(case)
+    k, v, lg, w = g["k0"].clone(), g["v0"].clone(), g["lg0"].clone(), g["w0"]
+    for i in range(g["q"].shape[0]):
+        out, w = sattn_ref.decode_step(g["q"][i], g["k"][i], g["v"][i], g["lg"][i], k, v, lg, w, g["scale"])
+        assert_fp32_close(out, g["out"][i], f"{case} step {i}")
+    assert w == g["w_end"]
+    assert torch.equal(k, g["k_end"]) and torch.equal(v, g["v_end"]) and torch.equal(lg, g["lg_end"])
+
+
+# ----------------------------------------------------------------------------- GPU
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", CASES)
+def test_kernel_matches_reference_golden(case):
+    import selective_attention_b200 as sab
+    from selective_attention_b200 import kernels
+
+    g = load_golden(case)
+    k, v, lg, w = g["k0"].cuda(), g["v0"].cuda(), g["lg0"].cuda(), g["w0"]
+    for i in range(g["q"].shape[0]):
+        out = kernels.sattn_decode_step(g["q"][i].cuda(), g["k"][i].cuda(), g["v"][i].cuda(), g["lg"][i].cuda(),
+                                        k, v, lg, w, g["scale"])
+        w += 1
+        assert_fp32_close(out.cpu(), g["out"][i], f"{case} step {i}")
+    sab.check_device_error()
+    assert torch.equal(k.cpu(), g["k_end"]) and torch.equal(v.cpu(), g["v_end"])
+    assert torch.equal(lg.cpu(), g["lg_end"])
+
+
+@pytest.mark.gpu
+def test_cache_object_step_advances_write_idx():
+    from selective_attention_b200 import kernels
+
+    g = load_golden("sattn_decode_dropped_fp32")
+    cache = types.SimpleNamespace(k_rot=g["k0"].cuda(), v=g["v0"].cuda(), log_gate=g["lg0"].cuda(),
+                                  write_idx=g["w0"])
+    for i in range(g["q"].shape[0]):
+        out = kernels.selective_attn_step(cache, g["q"][i].cuda(), g["k"][i].cuda(), g["v"][i].cuda(),
+                                          g["lg"][i].cuda(), g["scale"])
+        assert out.shape == (g["q"].shape[1], g["q"].shape[2] * g["q"].shape[3])
+        assert_fp32_close(out.view_as(g["out"][i]).cpu(), g["out"][i], f"object step {i}")
+    assert cache.write_idx == g["w_end"]
+
+
+def random_cache(seed, b, H, D, cap, w, dtype, p_zero=0.1):
+    gen = torch.Generator().manual_seed(seed)
+    k = torch.randn(b, H, cap, D, generator=gen).to(dtype)
+    v = torch.randn(b, H, cap, D, generator=gen).to(dtype)
+    lg = torch.log(torch.sigmoid(torch.randn(b, H, cap, generator=gen) + 2.0)) * 2.0
+    lg = torch.where(torch.rand(b, H, cap, generator=gen) < p_zero, torch.full_like(lg, -math.inf), lg)
+    q = torch.randn(b, H, D, generator=gen).to(dtype)
+    kn = torch.randn(b, H, D, generator=gen).to(dtype)
+    vn = torch.randn(b, H, D, generator=gen).to(dtype)
+    lgn = torch.log(torch.sigmoid(torch.randn(b, H, generator=gen) + 2.0)) * 2.0
+    return q, kn, vn, lgn, k, v, lg
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 64), (torch.float32, 32),
+                                     (torch.float32, 256), (torch.bfloat16, 8)])
+def test_kernel_matches_oracle_long_cache(dtype, D):
+    from selective_attention_b200 import kernels
+
+    b, H, cap, w = 4, 6, 3000, 2411
+    q, kn, vn, lgn, k, v, lg = random_cache(7, b, H, D, cap, w, dtype)
+    kd, vd, lgd = k.cuda(), v.cuda(), lg.cuda()
+    out = kernels.sattn_decode_step(q.cuda(), kn.cuda(), vn.cuda(), lgn.cuda(), kd, vd, lgd, w)
+    ref, _ = sattn_ref.decode_step(q.float(), kn.float(), vn.float(), lgn, k.float(), v.float(), lg, w, D ** -0.5)
+    close = assert_fp32_close if dtype == torch.float32 else assert_bf16_close
+    close(out.float().cpu(), ref, f"{dtype} D{D}")
+    assert torch.equal(kd[:, :, w].cpu(), kn) and torch.equal(vd[:, :, w].cpu(), vn)
+    assert torch.equal(lgd[:, :, w].cpu(), lgn)
+
+
+@pytest.mark.gpu
+def test_first_step_returns_the_value():
+    """With one cached key (the token) the weight is exactly 1, as the reference's early
+    return ``out_proj(v * out_gate)`` (``modules/selective_attention.py:396-397``) assumes."""
+    from selective_attention_b200 import kernels
+
+    q, kn, vn, lgn, k, v, lg = random_cache(8, 2, 3, 64, 16, 0, torch.float32)
+    out = kernels.sattn_decode_step(q.cuda(), kn.cuda(), vn.cuda(), lgn.cuda(), k.cuda(), v.cuda(), lg.cuda(), 0)
+    assert torch.equal(out.cpu(), vn)
+
+
+@pytest.mark.gpu
+def test_kernel_rejects_bad_arguments():
+    from selective_attention_b200 import kernels
+
+    q, kn, vn, lgn, k, v, lg = random_cache(9, 1, 2, 64, 16, 0, torch.float32)
+    args = [t.cuda() for t in (q, kn, vn, lgn, k, v, lg)]
+    with pytest.raises(ValueError):  # no free slot
+        kernels.sattn_decode_step(*args, 16)
+    q2, kn2, vn2, lgn2, k2, v2, lg2 = random_cache(9, 1, 2, 48, 16, 0, torch.float32)
+    with pytest.raises(ValueError):  # head_dim 48 is not a supported power of two
+        kernels.sattn_decode_step(*[t.cuda() for t in (q2, kn2, vn2, lgn2, k2, v2, lg2)], 3)
