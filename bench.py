@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--no-front", action="store_true", help="skip the prefill front-end (conv) measurement")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-bwd", action="store_true", help="skip the SSD backward measurement")
+    ap.add_argument("--no-sattn", action="store_true", help="skip the selective-attention decode measurement")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     return ap.parse_args()
 
@@ -381,6 +382,8 @@ def run_ours(args, rank, world, local):
         line["front"] = front_measure(args, dev, flush, hbm_peak)
     if not args.no_bwd and world == 1:
         line["bwd"] = bwd_measure(args, cfg, inp, dev, flush)
+    if not args.no_sattn and world == 1:
+        line["sattn_decode"] = sattn_measure(args, dev, flush, hbm_peak)
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
@@ -556,6 +559,43 @@ def bwd_measure(args, cfg, inp, dev, flush):
             "tokens_per_s": b * L / (ms * 1e-3), "stages_ms": stages, "alg_flops": flops, "tflops": tf,
             "ffma_nominal_tflops": FFMA_NOMINAL_TFLOPS, "frac_of_nominal_ffma": tf / FFMA_NOMINAL_TFLOPS,
             "steps": steps, "timing": "median of per-step CUDA events, L2 flushed between steps"}
+
+
+def sattn_measure(args, dev, flush, hbm_peak):
+    """Selective-attention decode step (row f4): b 64, H 16, head_dim 64, an fp32 cache
+    (the reference allocates its cache in fp32) holding 4000 keys; each step writes the
+    token's key / value / log-gate and attends over the 4001 keys. Achieved HBM GB/s on the
+    step's bytes, through the C-ABI call with arguments prepared once."""
+    from selective_attention_b200 import _lib, kernels
+
+    b, H, D, cap, w = 64, 16, 64, 4096, 4000
+    g = torch.Generator(device=dev).manual_seed(3)
+    kc = torch.randn(b, H, cap, D, device=dev, generator=g)
+    vc = torch.randn(b, H, cap, D, device=dev, generator=g)
+    lgc = torch.log(torch.sigmoid(torch.randn(b, H, cap, device=dev, generator=g) + 2.0)) * 2.0
+    q, kn, vn = (torch.randn(b, H, D, device=dev, generator=g) for _ in range(3))
+    lgn = torch.zeros(b, H, device=dev)
+    out = kernels.sattn_decode_step(q, kn, vn, lgn, kc, vc, lgc, w)  # checks the wrapper once
+    fn = _lib.lib().sattn_decode_step
+    cargs = (_lib.ptr(q), _lib.ptr(kn), _lib.ptr(vn), _lib.ptr(lgn), _lib.ptr(kc), _lib.ptr(vc), _lib.ptr(lgc), w,
+             cap, _lib.ptr(out), b, H, D, D ** -0.5, 0, torch.cuda.current_stream(dev).cuda_stream)
+
+    def step():
+        _lib.check(fn(*cargs), "sattn_decode_step")
+
+    for _ in range(5):
+        step()
+    torch.cuda.synchronize()
+    steps = max(10, min(args.steps, 200))
+    per = time_steps(step, steps, flush, torch.cuda.current_stream(dev))
+    us = statistics.median(per) * 1e3
+    n = w + 1
+    by = b * H * (n * D * 4 * 2 + n * 4 + 4 * D * 4 + 4 + D * 4 * 2)  # K, V, gates read; q, new k/v/gate, out
+    gbs = by / (us / 1e6) / 1e9
+    return {"config": "b64 H16 D64, fp32 cache of 4096 slots, 4001 keys attended", "us_per_step": us,
+            "alg_bytes": by, "gbs": gbs, "peak_gbs": hbm_peak, "frac": gbs / hbm_peak, "steps": steps,
+            "timing": "median of per-step CUDA events around the C-ABI call (arguments prepared once), "
+                      "L2 flushed between steps"}
 
 
 def ssu_measure(args, dev, flush, hbm_peak, world):
