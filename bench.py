@@ -384,6 +384,7 @@ def run_ours(args, rank, world, local):
         line["bwd"] = bwd_measure(args, cfg, inp, dev, flush)
     if not args.no_sattn and world == 1:
         line["sattn_decode"] = sattn_measure(args, dev, flush, hbm_peak)
+        line["sattn_prefill"] = sattn_prefill_measure(args, dev, flush)
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
@@ -596,6 +597,35 @@ def sattn_measure(args, dev, flush, hbm_peak):
             "alg_bytes": by, "gbs": gbs, "peak_gbs": hbm_peak, "frac": gbs / hbm_peak, "steps": steps,
             "timing": "median of per-step CUDA events around the C-ABI call (arguments prepared once), "
                       "L2 flushed between steps"}
+
+
+def sattn_prefill_measure(args, dev, flush):
+    """Selective-attention prefill (row f4, inference): b 2, H 16, L 2048, head_dim 64, bf16
+    inputs (fp32 arithmetic), 10 % of the keys dropped. CUDA-core kernel: TFLOP/s of the
+    causal attention's 2 L^2 D FLOPs per (row, head) against the nominal FFMA rate."""
+    from selective_attention_b200 import kernels
+
+    b, H, L, D = 2, 16, 2048, 64
+    g = torch.Generator(device=dev).manual_seed(4)
+    q, k, v = (torch.randn(b, H, L, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+    lg = torch.log(torch.sigmoid(torch.randn(b, H, L, device=dev, generator=g) + 2.0)) * 2.0
+    lg = torch.where(torch.rand(b, H, L, device=dev, generator=g) < 0.1, torch.full_like(lg, -math.inf), lg)
+    out = torch.empty_like(q)
+
+    def step():
+        kernels.sattn_prefill(q, k, v, lg, out=out)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    steps = max(5, min(args.steps, 50))
+    per = time_steps(step, steps, flush, torch.cuda.current_stream(dev))
+    ms = statistics.median(per)
+    flops = 2 * b * H * L * L * D
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"config": "b2 H16 L2048 D64 bf16, 10% of keys dropped", "ms_per_step": ms, "alg_flops": flops,
+            "tflops": tf, "ffma_nominal_tflops": FFMA_NOMINAL_TFLOPS, "frac_of_nominal_ffma": tf / FFMA_NOMINAL_TFLOPS,
+            "steps": steps, "timing": "median of per-step CUDA events, L2 flushed between steps"}
 
 
 def ssu_measure(args, dev, flush, hbm_peak, world):

@@ -24,9 +24,12 @@
  *   ssm_conv_prefill       <- modules/ssm.py:112-134 (SiLU, depthwise causal conv1d,
  *                             split into x, B, C) and inference/ssm_cache.py:10-36
  *                             SSMCache.build_conv_ctx
- *   sattn_decode_step      <- modules/selective_attention.py:394-405 (SelectiveMHA.step:
+ *   sattn_decode_step      <- modules/selective_attention.py:390-404 (SelectiveMHA.step:
  *                             cache update and pos-mode gated softmax attention) and
  *                             inference/selective_attn_cache.py:27-42 SelectiveAttnCache.update_kv
+ *   sattn_prefill_fwd      <- modules/selective_attention.py:27-144 _build_attn_matrix and
+ *                             the seq-mode _gated_softmax, with the @ v of :270-280
+ *                             (SelectiveMHA.forward in inference, compressed or not)
  *   ssm_conv_decode        <- modules/ssm.py:173-186 (decode step: cache update, SiLU,
  *                             weighted sum, split) and inference/ssm_cache.py:38-43
  *                             SSMCache.update
@@ -264,7 +267,7 @@ int ssm_conv_decode(const void* hbc_new, int64_t row_stride, void* conv_ctx, con
                     int32_t dtype, void* stream);
 
 /*
- * Selective-attention decode step (modules/selective_attention.py:394-405): writes the
+ * Selective-attention decode step (modules/selective_attention.py:390-404): writes the
  * token's key, value and log-gate at slot write_idx of the cache (as
  * SelectiveAttnCache.update_kv does), then with n = write_idx + 1 cached keys
  *   s_j = scale * q . k_j + (j < n-1 ? log_gate_j : 0),   out = softmax(s) . v
@@ -281,6 +284,21 @@ int ssm_conv_decode(const void* hbc_new, int64_t row_stride, void* conv_ctx, con
 int sattn_decode_step(const void* q_rot, const void* k_rot, const void* v, const float* log_gate,
                       void* k_cache, void* v_cache, float* log_gate_cache, int64_t write_idx, int64_t capacity,
                       void* out, int64_t batch, int64_t nheads, int64_t head_dim, float scale, int32_t dtype,
+                      void* stream);
+
+/*
+ * Selective-attention prefill (inference): for every query i of a sequence
+ *   s_ij = scale * q_i . k_j + (j < i ? log_gate_j : 0)  for j <= i,   out_i = softmax_j(s_i) . v
+ * i.e. causal attention in which every earlier key adds its log-gate and the token's
+ * own score is ungated (the seq-mode _gated_softmax). Keys whose gate is zero (log-gate
+ * -inf; the reference compresses them away) and padding keys (log-gate -inf, as the
+ * layer's masked_fill sets them) drop out.
+ *   q_rot, k_rot, v, out  (b, H, L, D)  dtype, 16-byte aligned
+ *   log_gate              (b, H, L)     fp32
+ * head_dim D in {16, 32, 64, 128}.
+ */
+int sattn_prefill_fwd(const void* q_rot, const void* k_rot, const void* v, const float* log_gate, void* out,
+                      int64_t batch, int64_t nheads, int64_t seqlen, int64_t head_dim, float scale, int32_t dtype,
                       void* stream);
 
 #ifdef __cplusplus

@@ -6,9 +6,9 @@ Parity checker for the CUDA decode kernel (``csrc/sattn.cu``). Imported only by
 Follows nmquan1503/selective-attention (paths relative to ``src/selective_attention/``):
 - ``inference/selective_attn_cache.py:27-42`` ``SelectiveAttnCache.update_kv``: the new
   key, value and log-gate are written at ``write_idx``, which then advances;
-- ``modules/selective_attention.py:394-405`` (``SelectiveMHA.step``): scores of the
+- ``modules/selective_attention.py:390-404`` (``SelectiveMHA.step``): scores of the
   query against the first ``write_idx`` cached keys, times ``scale``; the pos-mode gated
-  softmax (``:126-128``) adds every cached key's log-gate except the newest one's
+  softmax (``:121-123``) adds every cached key's log-gate except the newest one's
   (the token itself); the output is the weighted sum of the cached values.
 
 Parity pin: golden vectors made with the reference's own cache class, ``_reset_cache``
@@ -28,7 +28,7 @@ def update_kv(k_cache, v_cache, lg_cache, write_idx, k_rot, v, log_gate):
 
 
 def gated_softmax_pos(attn, log_gate):
-    """``modules/selective_attention.py:126-128``: gate every key but the last, then softmax."""
+    """``modules/selective_attention.py:121-123``: gate every key but the last, then softmax."""
     attn = attn.clone()
     attn[..., :-1] += log_gate[..., :-1]
     return torch.softmax(attn, dim=-1)
@@ -49,6 +49,22 @@ def decode_attention(q_rot, k_cache, v_cache, lg_cache, n_keys, scale, dtype=tor
 
 def decode_step(q_rot, k_rot, v, log_gate, k_cache, v_cache, lg_cache, write_idx, scale, dtype=torch.float32):
     """One decode step's cache update plus attention, as ``SelectiveMHA.step`` runs them
-    (``:394``, ``:399-405``). Updates the caches in place; returns ``(out, new write_idx)``."""
+    (``:390``, ``:399-404``). Updates the caches in place; returns ``(out, new write_idx)``."""
     n = update_kv(k_cache, v_cache, lg_cache, write_idx, k_rot, v, log_gate)
     return decode_attention(q_rot, k_cache, v_cache, lg_cache, n, scale, dtype), n
+
+
+def prefill_attention(q_rot, k_rot, v, log_gate, scale, dtype=torch.float32):
+    """Inference prefill without compression, ``modules/selective_attention.py:27-144``:
+    ``_build_attn_matrix`` (``q k^T * scale``, causal ``-inf`` above the diagonal, ``:55-64``),
+    the seq-mode ``_gated_softmax`` (log-gate of each key added off the diagonal, ``:134-137``)
+    and ``attn_weight @ v`` (``:280``). Keys with log-gate ``-inf`` drop out, which is also
+    what the compressed path (``:66-88``, ``:270-278``) computes. Shapes ``(b, H, L, D)``."""
+    L = q_rot.shape[2]
+    attn = (q_rot.to(dtype) @ k_rot.to(dtype).transpose(-2, -1)) * scale
+    attn = attn.masked_fill(torch.triu(torch.ones(L, L, dtype=torch.bool), diagonal=1), float("-inf"))
+    diag = torch.arange(L)
+    d = attn[:, :, diag, diag].clone()
+    attn = attn + log_gate.to(dtype).unsqueeze(2)
+    attn[:, :, diag, diag] = d
+    return torch.softmax(attn, dim=-1) @ v.to(dtype)

@@ -507,4 +507,17 @@ int sattn_decode_step(const void* q_rot, const void* k_rot, const void* v, const
                                          (int)head_dim, scale, dtype, reinterpret_cast<cudaStream_t>(stream)));
 }
 
+int sattn_prefill_fwd(const void* q_rot, const void* k_rot, const void* v, const float* log_gate, void* out,
+                      int64_t batch, int64_t nheads, int64_t seqlen, int64_t head_dim, float scale, int32_t dtype,
+                      void* stream) {
+  if (!q_rot || !k_rot || !v || !log_gate || !out) return SSD_ERR_INVALID_ARGUMENT;
+  if (batch <= 0 || nheads <= 0 || seqlen <= 0 || batch > 65535 || nheads > 65535 || seqlen > 0x7fffffffll)
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (!sattn_prefill_supported((int)head_dim)) return SSD_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  if (!aligned16(q_rot) || !aligned16(k_rot) || !aligned16(v)) return SSD_ERR_INVALID_ARGUMENT;
+  return cuda_status(launch_sattn_prefill(q_rot, k_rot, v, log_gate, out, (int)batch, (int)nheads, (int)seqlen,
+                                          (int)head_dim, scale, dtype, reinterpret_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"

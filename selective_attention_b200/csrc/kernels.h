@@ -67,6 +67,9 @@ bool sattn_decode_supported(int D);
 cudaError_t launch_sattn_decode(const void* q, const void* k, const void* v, const float* lg, void* kc, void* vc,
                                 float* lgc, long long widx, long long cap, void* out, long long bh, int D,
                                 float scale, int dtype, cudaStream_t s);
+bool sattn_prefill_supported(int D);
+cudaError_t launch_sattn_prefill(const void* q, const void* k, const void* v, const float* lg, void* out, int b, int H,
+                                 int L, int D, float scale, int dtype, cudaStream_t s);
 
 // ssd_tc.cu (tcgen05 + TMA; bf16/fp16 inputs, P = 64, N = 128, cs = 256; prev16 in the input type)
 bool tc_supported(int x_dtype, int P, int N, int cs);

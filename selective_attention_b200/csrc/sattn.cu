@@ -1,5 +1,5 @@
 // sattn.cu - selective-attention decode step: the cache update and the pos-mode gated
-// softmax attention of SelectiveMHA.step (modules/selective_attention.py:394-405,
+// softmax attention of SelectiveMHA.step (modules/selective_attention.py:390-404,
 // inference/selective_attn_cache.py:27-42) in one kernel.
 //
 // One CTA per (batch row, head). Its threads first write the new key, value and
@@ -8,6 +8,13 @@
 // the score q.k*scale (+ the key's log-gate, except for the newest key, the token
 // itself) goes through an online softmax per lane group, and the groups and warps are
 // merged at the end. The step is bound by reading the cache from HBM.
+//
+// The prefill kernel computes the same gated attention for a whole sequence
+// (_build_attn_matrix + the seq-mode _gated_softmax + @ v, :27-144 and :270-280 of
+// SelectiveMHA.forward in inference): causal softmax of q.k*scale where every key adds
+// its log-gate except on the diagonal. The reference's compressed path (keys whose gate
+// is zero removed, the token's own score appended ungated) is the same function with
+// those keys' log-gates at -inf, which is how this kernel runs it.
 #include <math.h>
 
 #include "common.cuh"
@@ -90,7 +97,7 @@ __global__ void __launch_bounds__(kWarps * 32) sattn_decode_kernel(
       if (j < W) {
         load8<T>(kb + (long long)j * D + sl * 8, kv[u]);
         load8<T>(vb + (long long)j * D + sl * 8, vv[u]);
-        g[u] = j < W - 1 ? lgb[j] : 0.f;  // the token's own key is not gated (:127)
+        g[u] = j < W - 1 ? lgb[j] : 0.f;  // the token's own key is not gated (:122)
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) kv[u][e] = vv[u][e] = 0.f;
@@ -157,6 +164,186 @@ cudaError_t launch_t(const void* q, const void* k, const void* v, const float* l
   return cudaGetLastError();
 }
 
+// ===========================================================================
+// Prefill: CTA = (64-query tile, head, row); 64-key tiles of K and V staged in shared
+// memory; thread (tr, tc) owns rows tr + 16 i (i < 4), score columns tc + 16 j, output
+// columns 4 tc + 64 g (g < 2). Online softmax per row across the half warp of the row.
+// ===========================================================================
+constexpr int kPT = 64;
+
+template <typename T>
+__device__ __forceinline__ void stage_rows64(float* dst, int ld, const T* src, int r0, int L, int D) {
+  const int vpr = D >> 3, nv = kPT * vpr;  // <= 1024 vectors of 8
+  float v[4][8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int vi = threadIdx.x + 256 * j, r = vi / vpr, c = (vi - r * vpr) * 8;
+    if (vi < nv && r0 + r < L) {
+      load8<T>(src + (long long)(r0 + r) * D + c, v[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int vi = threadIdx.x + 256 * j, r = vi / vpr, c = (vi - r * vpr) * 8;
+    if (vi >= nv) continue;
+    *reinterpret_cast<float4*>(dst + r * ld + c) = make_float4(v[j][0], v[j][1], v[j][2], v[j][3]);
+    *reinterpret_cast<float4*>(dst + r * ld + c + 4) = make_float4(v[j][4], v[j][5], v[j][6], v[j][7]);
+  }
+}
+
+__device__ __forceinline__ float hw_max(float v) {
+#pragma unroll
+  for (int off = 1; off < 16; off <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+__device__ __forceinline__ float hw_sum(float v) {
+#pragma unroll
+  for (int off = 1; off < 16; off <<= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) sattn_prefill_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                            const T* __restrict__ v, const float* __restrict__ lg,
+                                                            T* __restrict__ out, int H, int L, int D, float scale) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int LD = D + 4, LDP = kPT + 4;
+  float* Qs = sm;              // [64][LD]
+  float* Ks = Qs + kPT * LD;   // [64][LD]
+  float* Vs = Ks + kPT * LD;   // [64][LD]
+  float* Ps = Vs + kPT * LD;   // [64][LDP]
+  float* gs = Ps + kPT * LDP;  // [64] log-gates of the key tile
+  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // the longest (last) query tiles start first
+  const long long bh = (long long)blockIdx.z * H + blockIdx.y;
+  const int q0 = qt * kPT, tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  const T* qb = q + bh * L * D;
+  const T* kb = k + bh * L * D;
+  const T* vb = v + bh * L * D;
+  const float* gb = lg + bh * L;
+  stage_rows64<T>(Qs, LD, qb, q0, L, D);
+  float o[4][8], m[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[i][e] = 0.f;
+  }
+  int dcol[2];
+#pragma unroll
+  for (int g = 0; g < 2; ++g) dcol[g] = min(4 * tc + 64 * g, D - 4);
+  for (int kt = 0; kt <= qt; ++kt) {
+    const int k0 = kt * kPT;
+    __syncthreads();  // previous tile's K, V, P consumed
+    stage_rows64<T>(Ks, LD, kb, k0, L, D);
+    stage_rows64<T>(Vs, LD, vb, k0, L, D);
+    if (tid < kPT) gs[tid] = k0 + tid < L ? gb[k0 + tid] : 0.f;
+    __syncthreads();
+    float sc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+    for (int d = 0; d < D; d += 4) {
+      float4 a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(Qs + (tr + 16 * i) * LD + d);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = *reinterpret_cast<const float4*>(Ks + (tc + 16 * j) * LD + d);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float t = sc[i][j];
+          t = fmaf(a[i].x, b[j].x, t);
+          t = fmaf(a[i].y, b[j].y, t);
+          t = fmaf(a[i].z, b[j].z, t);
+          sc[i][j] = fmaf(a[i].w, b[j].w, t);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int qi = q0 + tr + 16 * i;
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int kj = k0 + tc + 16 * j;
+        float s = -INFINITY;
+        if (kj <= qi && kj < L) s = sc[i][j] * scale + (kj < qi ? gs[tc + 16 * j] : 0.f);
+        sc[i][j] = s;
+        rmax = fmaxf(rmax, s);
+      }
+      rmax = hw_max(rmax);
+      const float mn = fmaxf(m[i], rmax);
+      const float corr = m[i] == -INFINITY ? 0.f : expf(m[i] - mn);
+      float rs = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = sc[i][j] == -INFINITY ? 0.f : expf(sc[i][j] - mn);
+        rs += p;
+        Ps[(tr + 16 * i) * LDP + tc + 16 * j] = p;
+      }
+      l[i] = l[i] * corr + hw_sum(rs);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[i][e] *= corr;
+      m[i] = mn;
+    }
+    __syncthreads();
+#pragma unroll 2
+    for (int j = 0; j < kPT; j += 4) {
+      float4 pa[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pa[i] = *reinterpret_cast<const float4*>(Ps + (tr + 16 * i) * LDP + j);
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq) {
+        float4 vv[2];
+#pragma unroll
+        for (int g = 0; g < 2; ++g) vv[g] = *reinterpret_cast<const float4*>(Vs + (j + qq) * LD + dcol[g]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float p = qq == 0 ? pa[i].x : (qq == 1 ? pa[i].y : (qq == 2 ? pa[i].z : pa[i].w));
+#pragma unroll
+          for (int g = 0; g < 2; ++g) {
+            o[i][4 * g] = fmaf(p, vv[g].x, o[i][4 * g]);
+            o[i][4 * g + 1] = fmaf(p, vv[g].y, o[i][4 * g + 1]);
+            o[i][4 * g + 2] = fmaf(p, vv[g].z, o[i][4 * g + 2]);
+            o[i][4 * g + 3] = fmaf(p, vv[g].w, o[i][4 * g + 3]);
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qi = q0 + tr + 16 * i;
+    if (qi >= L) continue;
+    const float inv = 1.0f / l[i];
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const int d = 4 * tc + 64 * g;
+      if (d >= D) continue;
+      T* op = out + (bh * L + qi) * D + d;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) op[e] = from_f32<T>(o[i][4 * g + e] * inv);
+    }
+  }
+}
+
+template <typename T>
+cudaError_t prefill_t(const void* q, const void* k, const void* v, const float* lg, void* out, int b, int H, int L,
+                      int D, float scale, cudaStream_t s) {
+  const size_t smem = (size_t)(3 * kPT * (D + 4) + kPT * (kPT + 4) + kPT) * sizeof(float);
+  cudaError_t e = cudaFuncSetAttribute(sattn_prefill_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((L + kPT - 1) / kPT), (unsigned)H, (unsigned)b);
+  sattn_prefill_kernel<T><<<grid, 256, smem, s>>>((const T*)q, (const T*)k, (const T*)v, lg, (T*)out, H, L, D, scale);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 bool sattn_decode_supported(int D) { return D == 8 || D == 16 || D == 32 || D == 64 || D == 128 || D == 256; }
@@ -168,6 +355,22 @@ cudaError_t launch_sattn_decode(const void* q, const void* k, const void* v, con
     case SSD_F32: return launch_t<float>(q, k, v, lg, kc, vc, lgc, widx, cap, out, bh, D, scale, s);
     case SSD_BF16: return launch_t<__nv_bfloat16>(q, k, v, lg, kc, vc, lgc, widx, cap, out, bh, D, scale, s);
     case SSD_F16: return launch_t<__half>(q, k, v, lg, kc, vc, lgc, widx, cap, out, bh, D, scale, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ssdb200
+
+namespace ssdb200 {
+
+bool sattn_prefill_supported(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
+
+cudaError_t launch_sattn_prefill(const void* q, const void* k, const void* v, const float* lg, void* out, int b, int H,
+                                 int L, int D, float scale, int dtype, cudaStream_t s) {
+  switch (dtype) {
+    case SSD_F32: return prefill_t<float>(q, k, v, lg, out, b, H, L, D, scale, s);
+    case SSD_BF16: return prefill_t<__nv_bfloat16>(q, k, v, lg, out, b, H, L, D, scale, s);
+    case SSD_F16: return prefill_t<__half>(q, k, v, lg, out, b, H, L, D, scale, s);
   }
   return cudaErrorInvalidValue;
 }

@@ -425,7 +425,7 @@ def sattn_decode_step(q_rot, k_rot, v, log_gate, k_cache, v_cache, log_gate_cach
     Writes ``k_rot``, ``v`` and ``log_gate`` at slot ``write_idx`` of the caches, in place
     (``inference/selective_attn_cache.py:39-41``), then returns the pos-mode gated softmax
     attention of ``q_rot`` over the first ``write_idx + 1`` slots
-    (``modules/selective_attention.py:399-405``), ``(b, H, D)`` in ``q_rot``'s dtype. The caller
+    (``modules/selective_attention.py:399-404``), ``(b, H, D)`` in ``q_rot``'s dtype. The caller
     advances its write index. ``scale`` defaults to ``D ** -0.5`` (``:163``). Caches must be
     contiguous ``(b, H, cap, D)`` / ``(b, H, cap)`` with ``log_gate_cache`` fp32.
     """
@@ -463,7 +463,7 @@ def sattn_decode_step(q_rot, k_rot, v, log_gate, k_cache, v_cache, log_gate_cach
 
 
 def selective_attn_step(cache, q_rot, k_rot, v, log_select_gate, scale=None):
-    """``SelectiveMHA.step``'s cache update and attention (``modules/selective_attention.py:394-406``)
+    """``SelectiveMHA.step``'s cache update and attention (``modules/selective_attention.py:390-404``)
     on a ``SelectiveAttnCache``-like object (``k_rot``, ``v``, ``log_gate`` tensors and
     ``write_idx``): one kernel, ``cache.write_idx`` advanced. Returns ``out`` as
     ``(b, H * D)``, the tensor the layer gates and projects."""
@@ -471,3 +471,34 @@ def selective_attn_step(cache, q_rot, k_rot, v, log_select_gate, scale=None):
                             cache.write_idx, scale)
     cache.write_idx += 1
     return out.view(out.shape[0], -1)
+
+
+def sattn_prefill(q_rot, k_rot, v, log_gate, scale=None, out=None):
+    """Selective-attention prefill (inference) over whole sequences (C-ABI ``sattn_prefill_fwd``).
+
+    ``q_rot, k_rot, v`` ``(b, H, L, D)``; ``log_gate`` ``(b, H, L)`` (the layer's
+    ``log_select_gate`` after its padding mask). Returns ``(b, H, L, D)`` in ``q_rot``'s dtype:
+    causal softmax attention where each earlier key adds its log-gate and the token's own
+    score is ungated (``modules/selective_attention.py:27-144``, ``:270-280``); zero gates
+    (log-gate ``-inf``) drop their key, which is what the reference's compressed path computes.
+    ``scale`` defaults to ``D ** -0.5``.
+    """
+    b, H, L, D = q_rot.shape
+    dev = check_cuda([q_rot, k_rot, v, log_gate], ["q_rot", "k_rot", "v", "log_gate"])
+    for t, n in ((k_rot, "k_rot"), (v, "v")):
+        if tuple(t.shape) != (b, H, L, D):
+            raise ValueError(f"[{n}] expected shape {(b, H, L, D)}, got {tuple(t.shape)}")
+        if t.dtype != q_rot.dtype:
+            raise ValueError(f"[{n}] dtype {t.dtype} differs from q_rot's {q_rot.dtype}")
+    if tuple(log_gate.shape) != (b, H, L):
+        raise ValueError(f"[log_gate] expected shape {(b, H, L)}, got {tuple(log_gate.shape)}")
+    q_rot, k_rot, v = (_aligned16(to_contiguous(t)) for t in (q_rot, k_rot, v))
+    log_gate = to_contiguous(log_gate.float())
+    if out is None:
+        out = torch.empty(b, H, L, D, device=dev, dtype=q_rot.dtype)
+    scale = float(D ** -0.5 if scale is None else scale)
+    st = _lib.lib().sattn_prefill_fwd(_lib.ptr(q_rot), _lib.ptr(k_rot), _lib.ptr(v), _lib.ptr(log_gate),
+                                      _lib.ptr(out), b, H, L, D, scale, _lib.dtype_code(q_rot.dtype, "q_rot"),
+                                      _stream(dev))
+    _lib.check(st, "sattn_prefill")
+    return out

@@ -1,6 +1,6 @@
-"""Selective-attention decode step (row f4's decode half): the CPU oracle against golden
-vectors made with the reference's own cache and softmax code, and the CUDA kernel (C-ABI
-``sattn_decode_step``) against both.
+"""Selective attention (row f4): the decode step and the inference prefill. The CPU oracle
+against golden vectors made with the reference's own cache, compression and softmax code,
+and the CUDA kernels (C-ABI ``sattn_decode_step``, ``sattn_prefill_fwd``) against both.
 
 Golden vectors: ``tests/golden/make_golden_sattn.py``. Tolerances: fp32 rel 1e-4
 (``assert_fp32_close``); 16-bit outputs atol 2e-2 / rel 1e-2 (``assert_bf16_close``).
@@ -95,7 +95,7 @@ def test_kernel_matches_oracle_long_cache(dtype, D):
 @pytest.mark.gpu
 def test_first_step_returns_the_value():
     """With one cached key (the token) the weight is exactly 1, as the reference's early
-    return ``out_proj(v * out_gate)`` (``modules/selective_attention.py:396-397``) assumes."""
+    return ``out_proj(v * out_gate)`` (``modules/selective_attention.py:392-393``) assumes."""
     from selective_attention_b200 import kernels
 
     q, kn, vn, lgn, k, v, lg = random_cache(8, 2, 3, 64, 16, 0, torch.float32)
@@ -114,3 +114,54 @@ def test_kernel_rejects_bad_arguments():
     q2, kn2, vn2, lgn2, k2, v2, lg2 = random_cache(9, 1, 2, 48, 16, 0, torch.float32)
     with pytest.raises(ValueError):  # head_dim 48 is not a supported power of two
         kernels.sattn_decode_step(*[t.cuda() for t in (q2, kn2, vn2, lgn2, k2, v2, lg2)], 3)
+
+
+# ----------------------------------------------------------------------------- prefill
+PREFILL_CASES = ["sattn_prefill_dropped_fp32", "sattn_prefill_padded_d32_fp32", "sattn_prefill_kept_d128_fp32"]
+
+
+@pytest.mark.parametrize("case", PREFILL_CASES)
+def test_prefill_oracle_matches_reference_golden(case):
+    g = load_golden(case)
+    out = sattn_ref.prefill_attention(g["q"], g["k"], g["v"], g["log_gate"], g["scale"])
+    assert_fp32_close(out, g["out"], case)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", PREFILL_CASES)
+def test_prefill_kernel_matches_reference_golden(case):
+    import selective_attention_b200 as sab
+    from selective_attention_b200 import kernels
+
+    g = load_golden(case)
+    out = kernels.sattn_prefill(g["q"].cuda(), g["k"].cuda(), g["v"].cuda(), g["log_gate"].cuda(), g["scale"])
+    sab.check_device_error()
+    assert_fp32_close(out.cpu(), g["out"], case)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,D,L", [(torch.bfloat16, 128, 1000), (torch.float16, 64, 777), (torch.float32, 16, 300)])
+def test_prefill_kernel_matches_oracle(dtype, D, L):
+    from selective_attention_b200 import kernels
+
+    gen = torch.Generator().manual_seed(11)
+    b, H = 2, 3
+    q, k, v = (torch.randn(b, H, L, D, generator=gen).to(dtype) for _ in range(3))
+    lg = torch.log(torch.sigmoid(torch.randn(b, H, L, generator=gen) + 2.0)) * 2.0
+    lg = torch.where(torch.rand(b, H, L, generator=gen) < 0.1, torch.full_like(lg, -math.inf), lg)
+    out = kernels.sattn_prefill(q.cuda(), k.cuda(), v.cuda(), lg.cuda())
+    ref = sattn_ref.prefill_attention(q.float(), k.float(), v.float(), lg, D ** -0.5)
+    close = assert_fp32_close if dtype == torch.float32 else assert_bf16_close
+    close(out.float().cpu(), ref, f"prefill {dtype} D{D} L{L}")
+
+
+@pytest.mark.gpu
+def test_prefill_rejects_bad_arguments():
+    from selective_attention_b200 import kernels
+
+    q = torch.randn(1, 2, 10, 48, device="cuda")
+    with pytest.raises(ValueError):  # head_dim 48 unsupported
+        kernels.sattn_prefill(q, q, q, torch.zeros(1, 2, 10, device="cuda"))
+    q = torch.randn(1, 2, 10, 64, device="cuda")
+    with pytest.raises(ValueError):  # log_gate shape
+        kernels.sattn_prefill(q, q, q, torch.zeros(1, 2, 9, device="cuda"))
