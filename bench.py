@@ -384,7 +384,7 @@ def run_ours(args, rank, world, local):
         line["bwd"] = bwd_measure(args, cfg, inp, dev, flush)
     if not args.no_sattn and world == 1:
         line["sattn_decode"] = sattn_measure(args, dev, flush, hbm_peak)
-        line["sattn_prefill"] = sattn_prefill_measure(args, dev, flush)
+        line["sattn_prefill"] = sattn_prefill_measure(args, dev, flush, peaks.get("bf16_tflops", 1590.0))
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
@@ -599,10 +599,11 @@ def sattn_measure(args, dev, flush, hbm_peak):
                       "L2 flushed between steps"}
 
 
-def sattn_prefill_measure(args, dev, flush):
+def sattn_prefill_measure(args, dev, flush, tc_peak):
     """Selective-attention prefill (row f4, inference): b 2, H 16, L 2048, head_dim 64, bf16
-    inputs (fp32 arithmetic), 10 % of the keys dropped. CUDA-core kernel: TFLOP/s of the
-    causal attention's 2 L^2 D FLOPs per (row, head) against the nominal FFMA rate."""
+    inputs, 10 % of the keys dropped. TFLOP/s of the causal attention's 2 L^2 D FLOPs per
+    (row, head), for the tensor-core kernel (against the measured bf16 dense peak) and the
+    CUDA-core one (against the nominal FFMA rate)."""
     from selective_attention_b200 import kernels
 
     b, H, L, D = 2, 16, 2048, 64
@@ -611,21 +612,24 @@ def sattn_prefill_measure(args, dev, flush):
     lg = torch.log(torch.sigmoid(torch.randn(b, H, L, device=dev, generator=g) + 2.0)) * 2.0
     lg = torch.where(torch.rand(b, H, L, device=dev, generator=g) < 0.1, torch.full_like(lg, -math.inf), lg)
     out = torch.empty_like(q)
-
-    def step():
-        kernels.sattn_prefill(q, k, v, lg, out=out)
-
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    steps = max(5, min(args.steps, 50))
-    per = time_steps(step, steps, flush, torch.cuda.current_stream(dev))
-    ms = statistics.median(per)
     flops = 2 * b * H * L * L * D
-    tf = flops / (ms * 1e-3) / 1e12
-    return {"config": "b2 H16 L2048 D64 bf16, 10% of keys dropped", "ms_per_step": ms, "alg_flops": flops,
-            "tflops": tf, "ffma_nominal_tflops": FFMA_NOMINAL_TFLOPS, "frac_of_nominal_ffma": tf / FFMA_NOMINAL_TFLOPS,
-            "steps": steps, "timing": "median of per-step CUDA events, L2 flushed between steps"}
+    res = {"config": "b2 H16 L2048 D64 bf16, 10% of keys dropped", "alg_flops": flops,
+           "timing": "median of per-step CUDA events, L2 flushed between steps"}
+    for impl, peak, peak_name in (("tc", tc_peak, "bf16 dense, measured"),
+                                  ("simt", FFMA_NOMINAL_TFLOPS, "fp32 FFMA, nominal")):
+        def step():
+            kernels.sattn_prefill(q, k, v, lg, out=out, impl=impl)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        steps = max(5, min(args.steps, 50))
+        per = time_steps(step, steps, flush, torch.cuda.current_stream(dev))
+        ms = statistics.median(per)
+        tf = flops / (ms * 1e-3) / 1e12
+        res[impl] = {"ms_per_step": ms, "tflops": tf, "peak_tflops": peak, "peak": peak_name, "frac": tf / peak,
+                     "steps": steps}
+    return res
 
 
 def ssu_measure(args, dev, flush, hbm_peak, world):

@@ -295,11 +295,13 @@ int sattn_decode_step(const void* q_rot, const void* k_rot, const void* v, const
  * layer's masked_fill sets them) drop out.
  *   q_rot, k_rot, v, out  (b, H, L, D)  dtype, 16-byte aligned
  *   log_gate              (b, H, L)     fp32
- * head_dim D in {16, 32, 64, 128}.
+ * head_dim D in {16, 32, 64, 128}. impl: SSD_IMPL_AUTO takes the tcgen05 kernel for
+ * 16-bit inputs with D 64 or 128 (out 16-byte aligned) and the CUDA-core kernel
+ * otherwise; SSD_IMPL_TC requires the former, SSD_IMPL_SIMT forces the latter.
  */
 int sattn_prefill_fwd(const void* q_rot, const void* k_rot, const void* v, const float* log_gate, void* out,
                       int64_t batch, int64_t nheads, int64_t seqlen, int64_t head_dim, float scale, int32_t dtype,
-                      void* stream);
+                      int32_t impl, void* stream);
 
 #ifdef __cplusplus
 }

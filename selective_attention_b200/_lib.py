@@ -48,7 +48,7 @@ EXPORTS = {
     "ssm_conv_decode": (c_int, [c_void_p, c_int64] + [c_void_p] * 6 + [c_int64] * 4 + [c_int32, c_void_p]),
     "sattn_decode_step": (c_int, [c_void_p] * 7 + [c_int64, c_int64, c_void_p] + [c_int64] * 3
                           + [c_float, c_int32, c_void_p]),
-    "sattn_prefill_fwd": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_float, c_int32, c_void_p]),
+    "sattn_prefill_fwd": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_float, c_int32, c_int32, c_void_p]),
 }
 
 

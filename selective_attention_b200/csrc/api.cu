@@ -172,7 +172,8 @@ int ssd_b200_device_error(void* stream) {
   const unsigned int a = fetch_error_simt(s);
   const unsigned int b = fetch_error_tc(s);
   const unsigned int c = fetch_error_ssu(s);
-  return (int)(a ? a : (b ? b : c));
+  const unsigned int d = fetch_error_sattn(s);
+  return (int)(a ? a : (b ? b : (c ? c : d)));
 }
 
 int ssd_scan_uses_tensor_cores(const ssd_params* p) {
@@ -509,15 +510,19 @@ int sattn_decode_step(const void* q_rot, const void* k_rot, const void* v, const
 
 int sattn_prefill_fwd(const void* q_rot, const void* k_rot, const void* v, const float* log_gate, void* out,
                       int64_t batch, int64_t nheads, int64_t seqlen, int64_t head_dim, float scale, int32_t dtype,
-                      void* stream) {
+                      int32_t impl, void* stream) {
   if (!q_rot || !k_rot || !v || !log_gate || !out) return SSD_ERR_INVALID_ARGUMENT;
   if (batch <= 0 || nheads <= 0 || seqlen <= 0 || batch > 65535 || nheads > 65535 || seqlen > 0x7fffffffll)
     return SSD_ERR_INVALID_ARGUMENT;
   if (!sattn_prefill_supported((int)head_dim)) return SSD_ERR_INVALID_ARGUMENT;
   if (!dtype_ok(dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
   if (!aligned16(q_rot) || !aligned16(k_rot) || !aligned16(v)) return SSD_ERR_INVALID_ARGUMENT;
+  const bool tc_ok = sattn_prefill_tc_supported((int)head_dim, dtype);
+  if (impl == SSD_IMPL_TC && (!tc_ok || !aligned16(out))) return SSD_ERR_INVALID_ARGUMENT;
+  const int use_tc = impl != SSD_IMPL_SIMT && tc_ok && aligned16(out);
   return cuda_status(launch_sattn_prefill(q_rot, k_rot, v, log_gate, out, (int)batch, (int)nheads, (int)seqlen,
-                                          (int)head_dim, scale, dtype, reinterpret_cast<cudaStream_t>(stream)));
+                                          (int)head_dim, scale, dtype, use_tc,
+                                          reinterpret_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

@@ -68,8 +68,11 @@ cudaError_t launch_sattn_decode(const void* q, const void* k, const void* v, con
                                 float* lgc, long long widx, long long cap, void* out, long long bh, int D,
                                 float scale, int dtype, cudaStream_t s);
 bool sattn_prefill_supported(int D);
+bool sattn_prefill_tc_supported(int D, int dtype);
+// use_tc: tcgen05 kernel (16-bit inputs, D 64 or 128); otherwise the CUDA-core kernel.
 cudaError_t launch_sattn_prefill(const void* q, const void* k, const void* v, const float* lg, void* out, int b, int H,
-                                 int L, int D, float scale, int dtype, cudaStream_t s);
+                                 int L, int D, float scale, int dtype, int use_tc, cudaStream_t s);
+unsigned int fetch_error_sattn(cudaStream_t s);
 
 // ssd_tc.cu (tcgen05 + TMA; bf16/fp16 inputs, P = 64, N = 128, cs = 256; prev16 in the input type)
 bool tc_supported(int x_dtype, int P, int N, int cs);

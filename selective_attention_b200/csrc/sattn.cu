@@ -14,11 +14,16 @@
 // SelectiveMHA.forward in inference): causal softmax of q.k*scale where every key adds
 // its log-gate except on the diagonal. The reference's compressed path (keys whose gate
 // is zero removed, the token's own score appended ungated) is the same function with
-// those keys' log-gates at -inf, which is how this kernel runs it.
+// those keys' log-gates at -inf, which is how this kernel runs it. For 16-bit inputs with
+// head_dim 64 or 128 a tensor-core version runs the two products on tcgen05 with the
+// scores, the probabilities and the output accumulator in tensor memory.
 #include <math.h>
+
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace ssdb200 {
 namespace {
@@ -344,6 +349,250 @@ cudaError_t prefill_t(const void* q, const void* k, const void* v, const float* 
   return cudaGetLastError();
 }
 
+// ===========================================================================
+// Tensor-core prefill (16-bit inputs, head_dim 64 or 128). CTA = 128 queries of one
+// (row, head), 4 warps, thread t = query row q0 + t = TMEM lane t. Per 64-key tile:
+//   S = Q K^T          tcgen05 (A = Q, B = K, both K-major SW128 in shared memory) -> TMEM
+//   softmax            thread reads its S row, adds the log-gates (not on the diagonal),
+//                      masks keys past the query, keeps a running reference max and sum
+//   P -> TMEM          16-bit probabilities, two per 32-bit column
+//   O += P V           tcgen05 TS form (A = P from TMEM, B = V MN-major), 64 columns a block
+// O is rescaled (TMEM load / store of the row) only when a row's max grows by more than 8
+// (e^8 bounds the unnormalised probabilities). Every wait is bounded; on a timeout the
+// kernel records an error code and releases its tensor memory.
+// TMEM columns: S [0, 64), P [64, 96), O [128, 128 + D).
+// ===========================================================================
+using namespace sm100;
+constexpr unsigned int kSiteAttnMma = 0x301;
+constexpr int kTQ = 128;           // queries per CTA
+constexpr int kTK = 64;            // keys per tile
+constexpr int kQBlk = kTQ * 128;   // bytes of one 64-column block of the Q tile
+constexpr int kKBlk = kTK * 128;   // bytes of one 64-column block of a K or V tile
+constexpr size_t kTcSmem = 100 * 1024;  // at most two CTAs (2 x 256 TMEM columns) per SM
+
+// rows x D 16-bit tile -> shared memory, 64-column blocks of 128-byte swizzled rows.
+template <int ROWS, int D>
+__device__ __forceinline__ void load_tile_sw128(uint8_t* dst, int blk_bytes, const uint16_t* src, int valid) {
+  constexpr int CPR = D / 8, N = ROWS * CPR / 128;  // 16-byte chunks per row, per thread
+  uint4 v[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int ci = threadIdx.x + 128 * i, r = ci / CPR, c = ci % CPR;
+    v[i] = r < valid ? __ldg(reinterpret_cast<const uint4*>(src + (long long)r * D + c * 8)) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int ci = threadIdx.x + 128 * i, r = ci / CPR, c = ci % CPR;
+    *reinterpret_cast<uint4*>(dst + (c >> 3) * blk_bytes + sw128_off((uint32_t)r, (uint32_t)(c & 7))) = v[i];
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                                  const T* __restrict__ v,
+                                                                  const float* __restrict__ lg, T* __restrict__ out,
+                                                                  int H, int L, float scale) {
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int NB = D / 64;
+  extern __shared__ uint8_t smraw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = base;
+  uint8_t* sK = sQ + NB * kQBlk;
+  uint8_t* sV = sK + NB * kKBlk;
+  float* sg = reinterpret_cast<float*>(sV + NB * kKBlk);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sg + kTK);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest query tiles first
+  const long long bh = (long long)blockIdx.z * H + blockIdx.y;
+  const int q0 = qt * kTQ, qi = q0 + tid;
+  const uint16_t* qb = reinterpret_cast<const uint16_t*>(q) + bh * L * D;
+  const uint16_t* kb = reinterpret_cast<const uint16_t*>(k) + bh * L * D;
+  const uint16_t* vb = reinterpret_cast<const uint16_t*>(v) + bh * L * D;
+  const float* gb = lg + bh * L;
+  const uint32_t b_addr = smem_u32(bar);
+  if (tid == 0) {
+    mbar_init(b_addr, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
+  load_tile_sw128<kTQ, D>(sQ, kQBlk, qb + (long long)q0 * D, L - q0);
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tl = (uint32_t)(warp * 32) << 16;
+  constexpr uint32_t T_S = 0, T_P = 64, T_O = 128;
+  constexpr uint32_t ID_S = idesc_f16(128, 64, BF16, false, false);
+  constexpr uint32_t ID_O = idesc_f16(128, 64, BF16, false, true);
+  float m_used = -INFINITY, lsum = 0.f;
+  uint32_t uses = 0;
+  bool ok = true;
+  const int nkt = min((q0 + kTQ + kTK - 1) / kTK, (L + kTK - 1) / kTK);
+  for (int kt = 0; kt < nkt; ++kt) {
+    const int k0 = kt * kTK;
+    load_tile_sw128<kTK, D>(sK, kKBlk, kb + (long long)k0 * D, L - k0);
+    load_tile_sw128<kTK, D>(sV, kKBlk, vb + (long long)k0 * D, L - k0);
+    if (tid < kTK) sg[tid] = k0 + tid < L ? gb[k0 + tid] : 0.f;
+    fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
+        umma_f16(tmem + T_S, sdesc_sw128(smem_u32(sQ) + hf * kQBlk + kk, 16, 1024),
+                 sdesc_sw128(smem_u32(sK) + hf * kKBlk + kk, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
+      }
+      umma_commit(b_addr);
+    }
+    ok = mbar_wait(b_addr, uses & 1, kSiteAttnMma);
+    ++uses;
+    if (!__syncthreads_and(ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    uint32_t sr[64];
+    {
+      uint32_t a[32], b2[32];
+      tmem_ld32(tmem + tl + T_S, a);
+      tmem_ld32(tmem + tl + T_S + 32, b2);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        sr[j] = a[j];
+        sr[32 + j] = b2[j];
+      }
+    }
+    float mt = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      const int kj = k0 + j;
+      float s = -INFINITY;
+      if (kj <= qi && kj < L) s = __uint_as_float(sr[j]) * scale + (kj < qi ? sg[j] : 0.f);
+      sr[j] = __float_as_uint(s);
+      mt = fmaxf(mt, s);
+    }
+    float f = 1.f;
+    bool rescale = false;
+    if (mt != -INFINITY && (m_used == -INFINITY || mt > m_used + 8.f)) {
+      if (kt > 0 && m_used != -INFINITY) {  // O and the sum hold earlier tiles: rescale them
+        f = expf(m_used - mt);
+        lsum *= f;
+        rescale = true;
+      }
+      m_used = mt;
+    }
+    // TMEM loads / stores are warp-collective: the whole warp runs them when any lane
+    // rescales (the others with f = 1).
+    if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+      for (int c = 0; c < D; c += 32) {
+        uint32_t o[32];
+        tmem_ld32(tmem + tl + T_O + c, o);
+        tmem_wait_ld();
+        uint32_t lo[16], hi[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          lo[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+          hi[e] = __float_as_uint(__uint_as_float(o[16 + e]) * f);
+        }
+        tmem_st16(tmem + tl + T_O + c, lo);
+        tmem_st16(tmem + tl + T_O + c + 16, hi);
+      }
+    }
+    uint32_t pk[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float s0 = __uint_as_float(sr[2 * j]), s1 = __uint_as_float(sr[2 * j + 1]);
+      const float p0 = s0 == -INFINITY ? 0.f : expf(s0 - m_used);
+      const float p1 = s1 == -INFINITY ? 0.f : expf(s1 - m_used);
+      pk[j] = pack2<T>(p0, p1);
+      const float2 r = unpack2<T>(pk[j]);  // the sum uses the probabilities the MMA sees
+      lsum += r.x + r.y;
+    }
+    {
+      uint32_t lo[16], hi[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        lo[e] = pk[e];
+        hi[e] = pk[16 + e];
+      }
+      tmem_st16(tmem + tl + T_P, lo);
+      tmem_st16(tmem + tl + T_P + 16, hi);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_f16_ts(tmem + T_O + 64 * nb, tmem + T_P + 8 * ks,
+                      sdesc_sw128(smem_u32(sV) + nb * kKBlk + ks * 2048, 16, 1024), ID_O,
+                      (kt > 0 || ks > 0) ? 1u : 0u);
+      umma_commit(b_addr);
+    }
+    ok = mbar_wait(b_addr, uses & 1, kSiteAttnMma);
+    ++uses;
+    if (!__syncthreads_and(ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+  }
+  if (ok) {  // uniform: every lane loads its row (warp-collective); rows past L store nothing
+    const float inv = 1.0f / lsum;
+    T* op = out + (bh * L + qi) * D;
+#pragma unroll
+    for (int c = 0; c < D; c += 32) {
+      uint32_t o[32];
+      tmem_ld32(tmem + tl + T_O + c, o);
+      tmem_wait_ld();
+      if (qi < L) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          uint4 w;
+          w.x = pack2<T>(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv);
+          w.y = pack2<T>(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv);
+          w.z = pack2<T>(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv);
+          w.w = pack2<T>(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv);
+          *reinterpret_cast<uint4*>(op + c + e) = w;
+        }
+      }
+    }
+  }
+  if (!ok && tid == 0) mbar_wait(b_addr, (uses - 1) & 1, kSiteAttnMma);  // drain the pending MMA (bounded)
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+template <typename T>
+cudaError_t prefill_tc_t(const void* q, const void* k, const void* v, const float* lg, void* out, int b, int H, int L,
+                         int D, float scale, cudaStream_t s) {
+  dim3 grid((unsigned)((L + kTQ - 1) / kTQ), (unsigned)H, (unsigned)b);
+  cudaError_t e;
+  if (D == 64) {
+    if ((e = cudaFuncSetAttribute(sattn_prefill_tc_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kTcSmem)))
+      return e;
+    sattn_prefill_tc_kernel<T, 64><<<grid, 128, kTcSmem, s>>>((const T*)q, (const T*)k, (const T*)v, lg, (T*)out, H,
+                                                              L, scale);
+  } else {
+    if ((e = cudaFuncSetAttribute(sattn_prefill_tc_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)kTcSmem)))
+      return e;
+    sattn_prefill_tc_kernel<T, 128><<<grid, 128, kTcSmem, s>>>((const T*)q, (const T*)k, (const T*)v, lg, (T*)out, H,
+                                                               L, scale);
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 bool sattn_decode_supported(int D) { return D == 8 || D == 16 || D == 32 || D == 64 || D == 128 || D == 256; }
@@ -365,8 +614,15 @@ namespace ssdb200 {
 
 bool sattn_prefill_supported(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
 
+bool sattn_prefill_tc_supported(int D, int dtype) { return (D == 64 || D == 128) && dtype != SSD_F32; }
+
 cudaError_t launch_sattn_prefill(const void* q, const void* k, const void* v, const float* lg, void* out, int b, int H,
-                                 int L, int D, float scale, int dtype, cudaStream_t s) {
+                                 int L, int D, float scale, int dtype, int use_tc, cudaStream_t s) {
+  if (use_tc) {
+    if (!sattn_prefill_tc_supported(D, dtype)) return cudaErrorInvalidValue;
+    if (dtype == SSD_BF16) return prefill_tc_t<__nv_bfloat16>(q, k, v, lg, out, b, H, L, D, scale, s);
+    return prefill_tc_t<__half>(q, k, v, lg, out, b, H, L, D, scale, s);
+  }
   switch (dtype) {
     case SSD_F32: return prefill_t<float>(q, k, v, lg, out, b, H, L, D, scale, s);
     case SSD_BF16: return prefill_t<__nv_bfloat16>(q, k, v, lg, out, b, H, L, D, scale, s);
@@ -375,4 +631,8 @@ cudaError_t launch_sattn_prefill(const void* q, const void* k, const void* v, co
   return cudaErrorInvalidValue;
 }
 
+}  // namespace ssdb200
+
+namespace ssdb200 {
+SSDB200_DEFINE_ERROR_FETCH(fetch_error_sattn)
 }  // namespace ssdb200

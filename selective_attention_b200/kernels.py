@@ -473,7 +473,7 @@ def selective_attn_step(cache, q_rot, k_rot, v, log_select_gate, scale=None):
     return out.view(out.shape[0], -1)
 
 
-def sattn_prefill(q_rot, k_rot, v, log_gate, scale=None, out=None):
+def sattn_prefill(q_rot, k_rot, v, log_gate, scale=None, out=None, impl: str = "auto"):
     """Selective-attention prefill (inference) over whole sequences (C-ABI ``sattn_prefill_fwd``).
 
     ``q_rot, k_rot, v`` ``(b, H, L, D)``; ``log_gate`` ``(b, H, L)`` (the layer's
@@ -481,7 +481,8 @@ def sattn_prefill(q_rot, k_rot, v, log_gate, scale=None, out=None):
     causal softmax attention where each earlier key adds its log-gate and the token's own
     score is ungated (``modules/selective_attention.py:27-144``, ``:270-280``); zero gates
     (log-gate ``-inf``) drop their key, which is what the reference's compressed path computes.
-    ``scale`` defaults to ``D ** -0.5``.
+    ``scale`` defaults to ``D ** -0.5``. ``impl``: ``"auto"`` (tensor cores for 16-bit inputs
+    with ``D`` 64 or 128), ``"tc"`` or ``"simt"``.
     """
     b, H, L, D = q_rot.shape
     dev = check_cuda([q_rot, k_rot, v, log_gate], ["q_rot", "k_rot", "v", "log_gate"])
@@ -499,6 +500,6 @@ def sattn_prefill(q_rot, k_rot, v, log_gate, scale=None, out=None):
     scale = float(D ** -0.5 if scale is None else scale)
     st = _lib.lib().sattn_prefill_fwd(_lib.ptr(q_rot), _lib.ptr(k_rot), _lib.ptr(v), _lib.ptr(log_gate),
                                       _lib.ptr(out), b, H, L, D, scale, _lib.dtype_code(q_rot.dtype, "q_rot"),
-                                      _stream(dev))
+                                      _lib.IMPLS[impl], _stream(dev))
     _lib.check(st, "sattn_prefill")
     return out

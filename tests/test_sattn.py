@@ -140,8 +140,12 @@ def test_prefill_kernel_matches_reference_golden(case):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dtype,D,L", [(torch.bfloat16, 128, 1000), (torch.float16, 64, 777), (torch.float32, 16, 300)])
-def test_prefill_kernel_matches_oracle(dtype, D, L):
+@pytest.mark.parametrize("impl", ["auto", "simt"])
+@pytest.mark.parametrize("dtype,D,L", [(torch.bfloat16, 128, 1000), (torch.float16, 64, 777),
+                                       (torch.bfloat16, 64, 130), (torch.float16, 128, 64),
+                                       (torch.float32, 16, 300)])
+def test_prefill_kernel_matches_oracle(dtype, D, L, impl):
+    """``auto`` takes the tensor-core kernel for 16-bit inputs with head_dim 64 / 128."""
     from selective_attention_b200 import kernels
 
     gen = torch.Generator().manual_seed(11)
@@ -149,7 +153,7 @@ def test_prefill_kernel_matches_oracle(dtype, D, L):
     q, k, v = (torch.randn(b, H, L, D, generator=gen).to(dtype) for _ in range(3))
     lg = torch.log(torch.sigmoid(torch.randn(b, H, L, generator=gen) + 2.0)) * 2.0
     lg = torch.where(torch.rand(b, H, L, generator=gen) < 0.1, torch.full_like(lg, -math.inf), lg)
-    out = kernels.sattn_prefill(q.cuda(), k.cuda(), v.cuda(), lg.cuda())
+    out = kernels.sattn_prefill(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), impl=impl)
     ref = sattn_ref.prefill_attention(q.float(), k.float(), v.float(), lg, D ** -0.5)
     close = assert_fp32_close if dtype == torch.float32 else assert_bf16_close
     close(out.float().cpu(), ref, f"prefill {dtype} D{D} L{L}")
@@ -165,3 +169,5 @@ def test_prefill_rejects_bad_arguments():
     q = torch.randn(1, 2, 10, 64, device="cuda")
     with pytest.raises(ValueError):  # log_gate shape
         kernels.sattn_prefill(q, q, q, torch.zeros(1, 2, 9, device="cuda"))
+    with pytest.raises(ValueError):  # the tensor-core kernel takes 16-bit inputs
+        kernels.sattn_prefill(q, q, q, torch.zeros(1, 2, 10, device="cuda"), impl="tc")
