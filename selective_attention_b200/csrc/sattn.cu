@@ -387,6 +387,23 @@ __device__ __forceinline__ void load_tile_sw128(uint8_t* dst, int blk_bytes, con
   }
 }
 
+// The same tile through cp.async (16-byte copies straight into shared memory; rows past
+// `valid` are zero-filled), committed as one group.
+template <int ROWS, int D>
+__device__ __forceinline__ void load_tile_sw128_async(uint8_t* dst, int blk_bytes, const uint16_t* src, int valid) {
+  constexpr int CPR = D / 8, N = ROWS * CPR / 128;
+#pragma unroll
+  for (int i = 0; i < N; ++i) {
+    const int ci = threadIdx.x + 128 * i, r = ci / CPR, c = ci % CPR;
+    const uint32_t d = smem_u32(dst + (c >> 3) * blk_bytes + sw128_off((uint32_t)r, (uint32_t)(c & 7)));
+    const uint16_t* g = r < valid ? src + (long long)r * D + c * 8 : src;
+    const uint32_t n = r < valid ? 16u : 0u;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(g), "r"(n) : "memory");
+  }
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 template <typename T, int D>
 __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __restrict__ q, const T* __restrict__ k,
                                                                   const T* __restrict__ v,
@@ -397,10 +414,11 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
   extern __shared__ uint8_t smraw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = base;
-  uint8_t* sK = sQ + NB * kQBlk;
-  uint8_t* sV = sK + NB * kKBlk;
-  float* sg = reinterpret_cast<float*>(sV + NB * kKBlk);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sg + kTK);
+  uint8_t* sKV = sQ + NB * kQBlk;                     // two buffers of (K, V)
+  float* sg = reinterpret_cast<float*>(sKV + 4 * NB * kKBlk);  // two buffers of 64 log-gates
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sg + 2 * kTK);
+  auto bufK = [&](int i) { return sKV + (2 * i) * NB * kKBlk; };
+  auto bufV = [&](int i) { return sKV + (2 * i + 1) * NB * kKBlk; };
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
   const int tid = threadIdx.x, warp = tid >> 5;
   const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest query tiles first
@@ -417,6 +435,11 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
   load_tile_sw128<kTQ, D>(sQ, kQBlk, qb + (long long)q0 * D, L - q0);
+  load_tile_sw128_async<kTK, D>(bufK(0), kKBlk, kb, L);
+  load_tile_sw128_async<kTK, D>(bufV(0), kKBlk, vb, L);
+  cp_async_commit();
+  if (tid < kTK) sg[tid] = tid < L ? gb[tid] : 0.f;
+  cp_async_wait_all();
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -431,12 +454,20 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
   bool ok = true;
   const int nkt = min((q0 + kTQ + kTK - 1) / kTK, (L + kTK - 1) / kTK);
   for (int kt = 0; kt < nkt; ++kt) {
-    const int k0 = kt * kTK;
-    load_tile_sw128<kTK, D>(sK, kKBlk, kb + (long long)k0 * D, L - k0);
-    load_tile_sw128<kTK, D>(sV, kKBlk, vb + (long long)k0 * D, L - k0);
-    if (tid < kTK) sg[tid] = k0 + tid < L ? gb[k0 + tid] : 0.f;
-    fence_proxy_async_smem();
-    __syncthreads();
+    const int k0 = kt * kTK, cur = kt & 1;
+    uint8_t* sK = bufK(cur);
+    uint8_t* sV = bufV(cur);
+    const float* gcur = sg + cur * kTK;
+    // tile kt is resident (previous iteration); its other buffer was last read by the
+    // MMAs of tile kt-1, which have completed: prefetch tile kt+1 there
+    if (kt + 1 < nkt) {
+      const int k1 = k0 + kTK;
+      load_tile_sw128_async<kTK, D>(bufK(cur ^ 1), kKBlk, kb + (long long)k1 * D, L - k1);
+      load_tile_sw128_async<kTK, D>(bufV(cur ^ 1), kKBlk, vb + (long long)k1 * D, L - k1);
+      cp_async_commit();
+    }
+    float gnext = 0.f;
+    if (tid < kTK && k0 + kTK + tid < L) gnext = gb[k0 + kTK + tid];
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
@@ -467,13 +498,22 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
       }
     }
     float mt = -INFINITY;
+    if (k0 + kTK <= q0 && k0 + kTK <= L) {  // whole tile before every query of the CTA: all gated
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-      const int kj = k0 + j;
-      float s = -INFINITY;
-      if (kj <= qi && kj < L) s = __uint_as_float(sr[j]) * scale + (kj < qi ? sg[j] : 0.f);
-      sr[j] = __float_as_uint(s);
-      mt = fmaxf(mt, s);
+      for (int j = 0; j < 64; ++j) {
+        const float s = fmaf(__uint_as_float(sr[j]), scale, gcur[j]);
+        sr[j] = __float_as_uint(s);
+        mt = fmaxf(mt, s);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        const int kj = k0 + j;
+        float s = -INFINITY;
+        if (kj <= qi && kj < L) s = kj < qi ? fmaf(__uint_as_float(sr[j]), scale, gcur[j]) : __uint_as_float(sr[j]) * scale;
+        sr[j] = __float_as_uint(s);
+        mt = fmaxf(mt, s);
+      }
     }
     float f = 1.f;
     bool rescale = false;
@@ -507,8 +547,8 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const float s0 = __uint_as_float(sr[2 * j]), s1 = __uint_as_float(sr[2 * j + 1]);
-      const float p0 = s0 == -INFINITY ? 0.f : expf(s0 - m_used);
-      const float p1 = s1 == -INFINITY ? 0.f : expf(s1 - m_used);
+      const float p0 = s0 == -INFINITY ? 0.f : __expf(s0 - m_used);
+      const float p1 = s1 == -INFINITY ? 0.f : __expf(s1 - m_used);
       pk[j] = pack2<T>(p0, p1);
       const float2 r = unpack2<T>(pk[j]);  // the sum uses the probabilities the MMA sees
       lsum += r.x + r.y;
@@ -539,6 +579,10 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
     }
     ok = mbar_wait(b_addr, uses & 1, kSiteAttnMma);
     ++uses;
+    // the prefetched tile lands before the next iteration reads it
+    if (tid < kTK) sg[(cur ^ 1) * kTK + tid] = gnext;
+    cp_async_wait_all();
+    fence_proxy_async_smem();
     if (!__syncthreads_and(ok)) {
       ok = false;
       break;
