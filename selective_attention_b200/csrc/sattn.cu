@@ -351,7 +351,8 @@ cudaError_t prefill_t(const void* q, const void* k, const void* v, const float* 
 
 // ===========================================================================
 // Tensor-core prefill (16-bit inputs, head_dim 64 or 128). CTA = 128 queries of one
-// (row, head), 4 warps, thread t = query row q0 + t = TMEM lane t. Per 64-key tile:
+// (row, head), 8 warps: threads t and t + 128 share query row q0 + t = TMEM lane t
+// (each takes 32 of a tile's keys and half of O's columns). Per 64-key tile:
 //   S = Q K^T          tcgen05 (A = Q, B = K, both K-major SW128 in shared memory) -> TMEM
 //   softmax            thread reads its S row, adds the log-gates (not on the diagonal),
 //                      masks keys past the query, keeps a running reference max and sum
@@ -368,21 +369,22 @@ constexpr int kTQ = 128;           // queries per CTA
 constexpr int kTK = 64;            // keys per tile
 constexpr int kQBlk = kTQ * 128;   // bytes of one 64-column block of the Q tile
 constexpr int kKBlk = kTK * 128;   // bytes of one 64-column block of a K or V tile
-constexpr size_t kTcSmem = 100 * 1024;  // at most two CTAs (2 x 256 TMEM columns) per SM
+constexpr size_t kTcSmem = 104 * 1024;  // at most two CTAs (2 x 256 TMEM columns) per SM
+constexpr int kTcThreads = 256;          // two threads per query row
 
 // rows x D 16-bit tile -> shared memory, 64-column blocks of 128-byte swizzled rows.
 template <int ROWS, int D>
 __device__ __forceinline__ void load_tile_sw128(uint8_t* dst, int blk_bytes, const uint16_t* src, int valid) {
-  constexpr int CPR = D / 8, N = ROWS * CPR / 128;  // 16-byte chunks per row, per thread
+  constexpr int CPR = D / 8, N = ROWS * CPR / kTcThreads;  // 16-byte chunks per row, per thread
   uint4 v[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    const int ci = threadIdx.x + 128 * i, r = ci / CPR, c = ci % CPR;
+    const int ci = threadIdx.x + kTcThreads * i, r = ci / CPR, c = ci % CPR;
     v[i] = r < valid ? __ldg(reinterpret_cast<const uint4*>(src + (long long)r * D + c * 8)) : make_uint4(0, 0, 0, 0);
   }
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    const int ci = threadIdx.x + 128 * i, r = ci / CPR, c = ci % CPR;
+    const int ci = threadIdx.x + kTcThreads * i, r = ci / CPR, c = ci % CPR;
     *reinterpret_cast<uint4*>(dst + (c >> 3) * blk_bytes + sw128_off((uint32_t)r, (uint32_t)(c & 7))) = v[i];
   }
 }
@@ -391,10 +393,10 @@ __device__ __forceinline__ void load_tile_sw128(uint8_t* dst, int blk_bytes, con
 // `valid` are zero-filled), committed as one group.
 template <int ROWS, int D>
 __device__ __forceinline__ void load_tile_sw128_async(uint8_t* dst, int blk_bytes, const uint16_t* src, int valid) {
-  constexpr int CPR = D / 8, N = ROWS * CPR / 128;
+  constexpr int CPR = D / 8, N = ROWS * CPR / kTcThreads;
 #pragma unroll
   for (int i = 0; i < N; ++i) {
-    const int ci = threadIdx.x + 128 * i, r = ci / CPR, c = ci % CPR;
+    const int ci = threadIdx.x + kTcThreads * i, r = ci / CPR, c = ci % CPR;
     const uint32_t d = smem_u32(dst + (c >> 3) * blk_bytes + sw128_off((uint32_t)r, (uint32_t)(c & 7)));
     const uint16_t* g = r < valid ? src + (long long)r * D + c * 8 : src;
     const uint32_t n = r < valid ? 16u : 0u;
@@ -405,25 +407,31 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __restrict__ q, const T* __restrict__ k,
-                                                                  const T* __restrict__ v,
-                                                                  const float* __restrict__ lg, T* __restrict__ out,
-                                                                  int H, int L, float scale) {
+__global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T* __restrict__ q,
+                                                                         const T* __restrict__ k,
+                                                                         const T* __restrict__ v,
+                                                                         const float* __restrict__ lg,
+                                                                         T* __restrict__ out, int H, int L,
+                                                                         float scale) {
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int NB = D / 64;
   extern __shared__ uint8_t smraw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = base;
-  uint8_t* sKV = sQ + NB * kQBlk;                     // two buffers of (K, V)
+  uint8_t* sKV = sQ + NB * kQBlk;                              // two buffers of (K, V)
   float* sg = reinterpret_cast<float*>(sKV + 4 * NB * kKBlk);  // two buffers of 64 log-gates
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sg + 2 * kTK);
+  float* xmax = sg + 2 * kTK;                                  // [2][128] row max of each half
+  float* xsum = xmax + 2 * kTQ;                                // [2][128] row sum of each half
+  uint64_t* bar = reinterpret_cast<uint64_t*>(xsum + 2 * kTQ);
   auto bufK = [&](int i) { return sKV + (2 * i) * NB * kKBlk; };
   auto bufV = [&](int i) { return sKV + (2 * i + 1) * NB * kKBlk; };
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  // threads 0-127 own the first 32 keys of each tile and the first half of O's columns for
+  // query row tid; threads 128-255 the second halves of the same rows
+  const int tid = threadIdx.x, warp = tid >> 5, half = tid >> 7, row = tid & 127;
   const int qt = (int)gridDim.x - 1 - (int)blockIdx.x;  // longest query tiles first
   const long long bh = (long long)blockIdx.z * H + blockIdx.y;
-  const int q0 = qt * kTQ, qi = q0 + tid;
+  const int q0 = qt * kTQ, qi = q0 + row;
   const uint16_t* qb = reinterpret_cast<const uint16_t*>(q) + bh * L * D;
   const uint16_t* kb = reinterpret_cast<const uint16_t*>(k) + bh * L * D;
   const uint16_t* vb = reinterpret_cast<const uint16_t*>(v) + bh * L * D;
@@ -445,10 +453,12 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tl = (uint32_t)(warp * 32) << 16;
+  const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;  // TMEM lanes of this warp's rows
   constexpr uint32_t T_S = 0, T_P = 64, T_O = 128;
   constexpr uint32_t ID_S = idesc_f16(128, 64, BF16, false, false);
   constexpr uint32_t ID_O = idesc_f16(128, 64, BF16, false, true);
+  const int jh = 32 * half;          // this thread's first key of a tile
+  const int ch = (D / 2) * half;     // this thread's first O column
   float m_used = -INFINITY, lsum = 0.f;
   uint32_t uses = 0;
   bool ok = true;
@@ -485,36 +495,36 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
       break;
     }
     tc_fence_after();
-    uint32_t sr[64];
-    {
-      uint32_t a[32], b2[32];
-      tmem_ld32(tmem + tl + T_S, a);
-      tmem_ld32(tmem + tl + T_S + 32, b2);
-      tmem_wait_ld();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        sr[j] = a[j];
-        sr[32 + j] = b2[j];
-      }
-    }
+    uint32_t sr[32];
+    tmem_ld32(tmem + tl + T_S + jh, sr);
+    tmem_wait_ld();
     float mt = -INFINITY;
     if (k0 + kTK <= q0 && k0 + kTK <= L) {  // whole tile before every query of the CTA: all gated
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const float s = fmaf(__uint_as_float(sr[j]), scale, gcur[j]);
-        sr[j] = __float_as_uint(s);
-        mt = fmaxf(mt, s);
+      for (int j = 0; j < 32; j += 4) {
+        const float4 g4 = *reinterpret_cast<const float4*>(gcur + jh + j);
+        const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float s = fmaf(__uint_as_float(sr[j + e]), scale, gg[e]);
+          sr[j + e] = __float_as_uint(s);
+          mt = fmaxf(mt, s);
+        }
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const int kj = k0 + j;
+      for (int j = 0; j < 32; ++j) {
+        const int kj = k0 + jh + j;
         float s = -INFINITY;
-        if (kj <= qi && kj < L) s = kj < qi ? fmaf(__uint_as_float(sr[j]), scale, gcur[j]) : __uint_as_float(sr[j]) * scale;
+        if (kj <= qi && kj < L)
+          s = kj < qi ? fmaf(__uint_as_float(sr[j]), scale, gcur[jh + j]) : __uint_as_float(sr[j]) * scale;
         sr[j] = __float_as_uint(s);
         mt = fmaxf(mt, s);
       }
     }
+    xmax[half * kTQ + row] = mt;
+    __syncthreads();
+    mt = fmaxf(xmax[row], xmax[kTQ + row]);  // both threads of the row see the same max
     float f = 1.f;
     bool rescale = false;
     if (mt != -INFINITY && (m_used == -INFINITY || mt > m_used + 8.f)) {
@@ -529,9 +539,9 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
     // rescales (the others with f = 1).
     if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
+      for (int c = 0; c < D / 2; c += 32) {
         uint32_t o[32];
-        tmem_ld32(tmem + tl + T_O + c, o);
+        tmem_ld32(tmem + tl + T_O + ch + c, o);
         tmem_wait_ld();
         uint32_t lo[16], hi[16];
 #pragma unroll
@@ -539,13 +549,13 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
           lo[e] = __float_as_uint(__uint_as_float(o[e]) * f);
           hi[e] = __float_as_uint(__uint_as_float(o[16 + e]) * f);
         }
-        tmem_st16(tmem + tl + T_O + c, lo);
-        tmem_st16(tmem + tl + T_O + c + 16, hi);
+        tmem_st16(tmem + tl + T_O + ch + c, lo);
+        tmem_st16(tmem + tl + T_O + ch + c + 16, hi);
       }
     }
-    uint32_t pk[32];
+    uint32_t pk[16];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
+    for (int j = 0; j < 16; ++j) {
       const float s0 = __uint_as_float(sr[2 * j]), s1 = __uint_as_float(sr[2 * j + 1]);
       const float p0 = s0 == -INFINITY ? 0.f : __expf(s0 - m_used);
       const float p1 = s1 == -INFINITY ? 0.f : __expf(s1 - m_used);
@@ -553,16 +563,7 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
       const float2 r = unpack2<T>(pk[j]);  // the sum uses the probabilities the MMA sees
       lsum += r.x + r.y;
     }
-    {
-      uint32_t lo[16], hi[16];
-#pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        lo[e] = pk[e];
-        hi[e] = pk[16 + e];
-      }
-      tmem_st16(tmem + tl + T_P, lo);
-      tmem_st16(tmem + tl + T_P + 16, hi);
-    }
+    tmem_st16(tmem + tl + T_P + 16 * half, pk);
     tmem_wait_st();
     tc_fence_before();
     __syncthreads();
@@ -589,13 +590,15 @@ __global__ void __launch_bounds__(128, 1) sattn_prefill_tc_kernel(const T* __res
     }
     tc_fence_after();
   }
-  if (ok) {  // uniform: every lane loads its row (warp-collective); rows past L store nothing
-    const float inv = 1.0f / lsum;
-    T* op = out + (bh * L + qi) * D;
+  if (ok) {  // uniform across the CTA: every lane loads its row (warp-collective); rows past L store nothing
+    xsum[half * kTQ + row] = lsum;
+    __syncthreads();
+    const float inv = 1.0f / (xsum[row] + xsum[kTQ + row]);
+    T* op = out + (bh * L + qi) * D + ch;
 #pragma unroll
-    for (int c = 0; c < D; c += 32) {
+    for (int c = 0; c < D / 2; c += 32) {
       uint32_t o[32];
-      tmem_ld32(tmem + tl + T_O + c, o);
+      tmem_ld32(tmem + tl + T_O + ch + c, o);
       tmem_wait_ld();
       if (qi < L) {
 #pragma unroll
@@ -625,13 +628,13 @@ cudaError_t prefill_tc_t(const void* q, const void* k, const void* v, const floa
     if ((e = cudaFuncSetAttribute(sattn_prefill_tc_kernel<T, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)kTcSmem)))
       return e;
-    sattn_prefill_tc_kernel<T, 64><<<grid, 128, kTcSmem, s>>>((const T*)q, (const T*)k, (const T*)v, lg, (T*)out, H,
+    sattn_prefill_tc_kernel<T, 64><<<grid, kTcThreads, kTcSmem, s>>>((const T*)q, (const T*)k, (const T*)v, lg, (T*)out, H,
                                                               L, scale);
   } else {
     if ((e = cudaFuncSetAttribute(sattn_prefill_tc_kernel<T, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)kTcSmem)))
       return e;
-    sattn_prefill_tc_kernel<T, 128><<<grid, 128, kTcSmem, s>>>((const T*)q, (const T*)k, (const T*)v, lg, (T*)out, H,
+    sattn_prefill_tc_kernel<T, 128><<<grid, kTcThreads, kTcSmem, s>>>((const T*)q, (const T*)k, (const T*)v, lg, (T*)out, H,
                                                                L, scale);
   }
   return cudaGetLastError();
