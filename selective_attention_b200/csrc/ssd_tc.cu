@@ -328,6 +328,9 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
     float* __restrict__ dt_out, float* __restrict__ cum_out, typename T16Of<BF16>::type* __restrict__ prev16,
     const float* __restrict__ h_init, float* __restrict__ h_last, ChunkMap cm, int H, int hpg, int use_sp,
     float dmin, float dmax) {
+  // the chunk_scan launched after this kernel may start its set-up on the free SMs now;
+  // it waits for this grid's completion before it reads dt, cum or prev16
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   using T16 = typename T16Of<BF16>::type;
   constexpr int NST = kSpStages;
   extern __shared__ uint8_t smem_raw[];
@@ -878,6 +881,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         tma_load_3d(smem_u32(sB), &tm_b, 0, si.g, t0, bar(ITEM_FULL));
         tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, si.g, t0, bar(ITEM_FULL));
         ++Bc;
+        // dt, cum and prev16 come from the state pass, which may still be running when
+        // this kernel starts (programmatic dependent launch): this thread alone reads
+        // them, so it alone waits for that grid's completion and its writes
+        if (I == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
         for (int i = 0; i < si.nh; ++i) {
           const int h = si.h0 + i, hs = Hc % NS;
           // The stage is free once the epilogue of the head NS back copied what it
@@ -1474,10 +1481,26 @@ static cudaError_t tc_scan_launch(const LaunchCtx& c, const CUtensorMap& mx, con
   const long long items = n_items(hb);
   if (items > 0x7fffffffll) return cudaErrorInvalidValue;
   const int grid = (int)(items < sms ? items : sms);  // persistent: one CTA per SM
-  kern<<<grid, kScanThreads, kScanSmem, c.stream>>>(mx, mc, mb, mh, mz, A, dt, cum, D, has_z,
-                                                    reinterpret_cast<YT*>(y), c.cm, c.H, c.G, hb, dt_nonneg,
-                                                    (int)items);
-  return cudaGetLastError();
+  // Programmatic dependent launch: the kernel may begin while the preceding kernel on the
+  // stream (the state pass) finishes; its producer waits for that grid before reading
+  // dt, cum and prev16 (griddepcontrol.wait), so only the set-up and the first C / B
+  // loads overlap. Used when the fused state pass runs in one wave (chains <= SMs: SMs
+  // idle beside it, c1: 3.6 % faster); with several waves it made this kernel slower
+  // (c2 -9 %, c4 -11 %), so there the launch is ordinary.
+  const long long chains = (long long)c.nrows * c.G * ((hpg + 1) / 2);
+  const bool pdl = chains <= sms;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kScanThreads);
+  cfg.dynamicSmemBytes = kScanSmem;
+  cfg.stream = c.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, mx, mc, mb, mh, mz, A, dt, cum, D, has_z, reinterpret_cast<YT*>(y), c.cm,
+                            c.H, c.G, hb, dt_nonneg, (int)items);
 }
 
 cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, const void* u, const float* A,
