@@ -552,6 +552,11 @@ __global__ void __launch_bounds__(256, 2) bwd_state_grad_kernel(
 //   delta_raw_grad = (total A + ddt), 0 where dt was clamped, * sigmoid(pre) (softplus)
 //   A / bias partials per (chunk, head).
 // ===========================================================================
+// Column of element (row, c) of the intra kernel's M tile: 4-column groups XOR-swizzled by
+// the row's 4-row block, so the tile's transposed writes (lanes 4 rows apart) spread over
+// the banks while each 4-column group stays one aligned float4 for the reads.
+__device__ __forceinline__ int mt_col(int row, int c) { return c ^ (((row >> 2) & 7) << 2); }
+
 constexpr int kIT = 512;         // bwd_intra threads
 constexpr int kIR = 64;          // bwd_intra row tile
 constexpr int kIB = 128;         // bwd_intra column block
@@ -631,7 +636,7 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
             const int l = l0 + r4 + e;
             float v = 0.f;
             if (s >= l && s < vl && l < vl) v = comp(cb[j], e) * expf(fminf(cs_ - cms[l], 0.f));
-            Mt[(r4 + e) * kLDB + c] = v;
+            Mt[(r4 + e) * kLDB + mt_col(r4 + e, c)] = v;
           }
         }
       }
@@ -642,7 +647,7 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
         for (int c = 0; c < cend; c += 4) {
           float4 a[2];
 #pragma unroll
-          for (int i = 0; i < 2; ++i) a[i] = lds4(Mt + (tl + 32 * i) * kLDB + c);
+          for (int i = 0; i < 2; ++i) a[i] = lds4(Mt + (tl + 32 * i) * kLDB + mt_col(tl + 32 * i, c));
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float4 y4 = lds4(yS + (s0 + c + q) * kLDP + p0);
