@@ -371,6 +371,8 @@ constexpr int kQBlk = kTQ * 128;   // bytes of one 64-column block of the Q tile
 constexpr int kKBlk = kTK * 128;   // bytes of one 64-column block of a K or V tile
 constexpr size_t kTcSmem = 104 * 1024;  // at most two CTAs (2 x 256 TMEM columns) per SM
 constexpr int kTcThreads = 256;          // two threads per query row
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.0f * kLog2e;  // rescale O when a row max grows by more than e^8
 
 // rows x D 16-bit tile -> shared memory, 64-column blocks of 128-byte swizzled rows.
 template <int ROWS, int D>
@@ -405,6 +407,13 @@ __device__ __forceinline__ void load_tile_sw128_async(uint8_t* dst, int blk_byte
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// 2^x on the special-function unit (PTX ex2.approx; 2^-inf = +0).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T* __restrict__ q,
@@ -446,7 +455,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T
   load_tile_sw128_async<kTK, D>(bufK(0), kKBlk, kb, L);
   load_tile_sw128_async<kTK, D>(bufV(0), kKBlk, vb, L);
   cp_async_commit();
-  if (tid < kTK) sg[tid] = tid < L ? gb[tid] : 0.f;
+  if (tid < kTK) sg[tid] = tid < L ? gb[tid] * kLog2e : 0.f;
   cp_async_wait_all();
   fence_proxy_async_smem();
   tc_fence_before();
@@ -459,6 +468,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T
   constexpr uint32_t ID_O = idesc_f16(128, 64, BF16, false, true);
   const int jh = 32 * half;          // this thread's first key of a tile
   const int ch = (D / 2) * half;     // this thread's first O column
+  // scores in the log2 domain (scale and gates times log2(e)): p = 2^(s - m)
+  const float scale2 = scale * kLog2e;
   float m_used = -INFINITY, lsum = 0.f;
   uint32_t uses = 0;
   bool ok = true;
@@ -477,7 +488,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T
       cp_async_commit();
     }
     float gnext = 0.f;
-    if (tid < kTK && k0 + kTK + tid < L) gnext = gb[k0 + kTK + tid];
+    if (tid < kTK && k0 + kTK + tid < L) gnext = gb[k0 + kTK + tid] * kLog2e;
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
@@ -506,7 +517,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T
         const float gg[4] = {g4.x, g4.y, g4.z, g4.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float s = fmaf(__uint_as_float(sr[j + e]), scale, gg[e]);
+          const float s = fmaf(__uint_as_float(sr[j + e]), scale2, gg[e]);
           sr[j + e] = __float_as_uint(s);
           mt = fmaxf(mt, s);
         }
@@ -517,7 +528,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T
         const int kj = k0 + jh + j;
         float s = -INFINITY;
         if (kj <= qi && kj < L)
-          s = kj < qi ? fmaf(__uint_as_float(sr[j]), scale, gcur[jh + j]) : __uint_as_float(sr[j]) * scale;
+          s = kj < qi ? fmaf(__uint_as_float(sr[j]), scale2, gcur[jh + j]) : __uint_as_float(sr[j]) * scale2;
         sr[j] = __float_as_uint(s);
         mt = fmaxf(mt, s);
       }
@@ -527,9 +538,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T
     mt = fmaxf(xmax[row], xmax[kTQ + row]);  // both threads of the row see the same max
     float f = 1.f;
     bool rescale = false;
-    if (mt != -INFINITY && (m_used == -INFINITY || mt > m_used + 8.f)) {
+    if (mt != -INFINITY && (m_used == -INFINITY || mt > m_used + kRescaleLog2)) {
       if (kt > 0 && m_used != -INFINITY) {  // O and the sum hold earlier tiles: rescale them
-        f = expf(m_used - mt);
+        f = ex2(m_used - mt);
         lsum *= f;
         rescale = true;
       }
@@ -553,12 +564,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T
         tmem_st16(tmem + tl + T_O + ch + c + 16, hi);
       }
     }
+    // while a row has no finite score yet, every s of the tile is -inf and 2^-inf = 0
+    const float mb = m_used == -INFINITY ? 0.f : m_used;
     uint32_t pk[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const float s0 = __uint_as_float(sr[2 * j]), s1 = __uint_as_float(sr[2 * j + 1]);
-      const float p0 = s0 == -INFINITY ? 0.f : __expf(s0 - m_used);
-      const float p1 = s1 == -INFINITY ? 0.f : __expf(s1 - m_used);
+      const float p0 = ex2(s0 - mb), p1 = ex2(s1 - mb);
       pk[j] = pack2<T>(p0, p1);
       const float2 r = unpack2<T>(pk[j]);  // the sum uses the probabilities the MMA sees
       lsum += r.x + r.y;
