@@ -36,13 +36,15 @@ def test_library_exports_every_declared_symbol():
 
 
 @pytest.mark.skipif(shutil.which("gcc") is None, reason="gcc not available")
-def test_params_struct_layout_matches_c():
+@pytest.mark.parametrize("cname,pyname", [("ssd_params", "SSDParams"), ("ssd_bwd_params", "SSDBwdParams")])
+def test_params_struct_layout_matches_c(cname, pyname):
     from selective_attention_b200 import _lib
 
-    fields = [f[0] for f in _lib.SSDParams._fields_]
+    cls = getattr(_lib, pyname)
+    fields = [f[0] for f in cls._fields_]
     prog = ["#include <stdio.h>", "#include <stddef.h>", f'#include "{HEADER}"', "int main(void){",
-            'printf("%zu\\n", sizeof(ssd_params));']
-    prog += [f'printf("%zu\\n", offsetof(ssd_params, {f}));' for f in fields]
+            f'printf("%zu\\n", sizeof({cname}));']
+    prog += [f'printf("%zu\\n", offsetof({cname}, {f}));' for f in fields]
     prog += ["return 0;}"]
     with tempfile.TemporaryDirectory() as d:
         c = os.path.join(d, "p.c")
@@ -50,9 +52,9 @@ def test_params_struct_layout_matches_c():
         open(c, "w").write("\n".join(prog))
         subprocess.run(["gcc", "-std=c99", c, "-o", exe], check=True)
         out = [int(x) for x in subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split()]
-    assert out[0] == ctypes.sizeof(_lib.SSDParams)
+    assert out[0] == ctypes.sizeof(cls)
     for f, off in zip(fields, out[1:]):
-        assert getattr(_lib.SSDParams, f).offset == off, f
+        assert getattr(cls, f).offset == off, f
 
 
 def test_header_constants_match_the_binding():
@@ -114,6 +116,12 @@ def test_entry_points_reject_bad_arguments_without_launching():
     bad = _params(x_dtype=7)
     assert L.ssd_scan_fwd(ctypes.byref(bad), None) == _lib.SSD_ERR_UNSUPPORTED_DTYPE
     assert L.ssu_fwd(*([None] * 10), 1, 1, 1, 1, 1, 0, 0, 0, 0, 1, 0.0, 1.0, None) == _lib.SSD_ERR_INVALID_ARGUMENT
+    g = _lib.SSDBwdParams()
+    assert L.ssd_scan_bwd(ctypes.byref(p), ctypes.byref(g), None) == _lib.SSD_ERR_INVALID_ARGUMENT
+    assert L.ssd_scan_bwd_workspace_size(ctypes.byref(_params(headdim=128))) == 0  # outside the backward's shapes
+    assert L.ssd_scan_bwd_workspace_size(ctypes.byref(_params())) > 0
+    assert L.sattn_decode_step(*([None] * 7), 0, 16, None, 1, 1, 64, 0.125, 0, None) == _lib.SSD_ERR_INVALID_ARGUMENT
+    assert L.sattn_prefill_fwd(*([None] * 5), 1, 1, 16, 64, 0.125, 0, 0, None) == _lib.SSD_ERR_INVALID_ARGUMENT
     for s in range(7):
         assert L.ssd_b200_status_string(s)
 
