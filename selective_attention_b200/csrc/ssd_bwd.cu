@@ -127,11 +127,17 @@ __device__ __forceinline__ float4 ld4(const void* p, long long i, int dt) {
   return make_float4(a.x, a.y, b.x, b.y);
 }
 
+// Column of token r in row `row` of a transposed ([feature][token]) tile: 4-token groups
+// XOR-swizzled by the row's 8-row block, so the staging stores (lanes 8 rows apart) spread
+// over the banks; a 4-token group stays one aligned float4 (tiles of <= 64 tokens).
+__device__ __forceinline__ int tok_col(int row, int r) { return r ^ (((row >> 3) & 7) << 2); }
+
 // Stage R token rows of a token-major tensor into shared memory as fp32: row r is
 // token tok0 + t0 + r, its columns [0, W) start at element (tok0 + t0 + r) * rs + co
 // (W, rs, co multiples of 8). Rows with t0 + r >= lim are zero; each value is scaled by
 // scale[t0 + r] when `scale` is given. COLS=false writes dst[r * ldd + c], COLS=true
-// dst[c * ldd + r]. All of a thread's loads (V 16-byte vectors, R * W / 8 <= NT V) are
+// dst[c * ldd + tok_col(c, r)] (R <= 64). All of a thread's loads (V 16-byte vectors,
+// R * W / 8 <= NT V) are
 // issued before its stores, so the tile costs one memory latency.
 template <int V, bool COLS, int NT = 256>
 __device__ __forceinline__ void stage(float* dst, int ldd, const void* src, int dt, long long tok0, int t0, int R,
@@ -157,7 +163,7 @@ __device__ __forceinline__ void stage(float* dst, int ldd, const void* src, int 
     const float sc = scale ? scale[t0 + r] : 1.f;
     if (COLS) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) dst[(c + e) * ldd + r] = v[j][e] * sc;
+      for (int e = 0; e < 8; ++e) dst[(c + e) * ldd + tok_col(c + e, r)] = v[j][e] * sc;
     } else {
       *reinterpret_cast<float4*>(dst + r * ldd + c) =
           make_float4(v[j][0] * sc, v[j][1] * sc, v[j][2] * sc, v[j][3] * sc);
@@ -206,11 +212,19 @@ __global__ void __launch_bounds__(256, 2) bwd_chunk_states_kernel(
   const void* bsrc = which == 0 ? Bm : Cm;
   const int adt = which == 0 ? xdt : ydt;
   const int tp = tid >> 4, tn = tid & 15;
-  int pr[4], nr[8];
+  int pr[4], nr[8], ps[4], ns[8];  // row offsets and their token swizzles (tok_col)
 #pragma unroll
-  for (int i = 0; i < 4; ++i) pr[i] = min(tp + 16 * i, P - 1) * LD;
+  for (int i = 0; i < 4; ++i) {
+    const int r = min(tp + 16 * i, P - 1);
+    pr[i] = r * LD;
+    ps[i] = tok_col(r, 0);
+  }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) nr[j] = min(tn + 16 * j, N - 1) * LD;
+  for (int j = 0; j < 8; ++j) {
+    const int r = min(tn + 16 * j, N - 1);
+    nr[j] = r * LD;
+    ns[j] = tok_col(r, 0);
+  }
   float acc[4][8];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -226,9 +240,9 @@ __global__ void __launch_bounds__(256, 2) bwd_chunk_states_kernel(
     for (int l = 0; l < TT; l += 4) {
       float4 a[4], b[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) a[i] = lds4(aT + pr[i] + l);
+      for (int i = 0; i < 4; ++i) a[i] = lds4(aT + pr[i] + (l ^ ps[i]));
 #pragma unroll
-      for (int j = 0; j < 8; ++j) b[j] = lds4(bT + nr[j] + l);
+      for (int j = 0; j < 8; ++j) b[j] = lds4(bT + nr[j] + (l ^ ns[j]));
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
