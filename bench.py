@@ -5,10 +5,20 @@
 
 One JSON line on stdout (rank 0). A "step" is one SSD forward over one batch of
 the workload (default: benchmark config c1, 8 x 2048 tokens, H24 P64 N128 cs256,
-bf16 with D + z). Multi-GPU (torchrun, one process per GPU): every rank runs its
-own batch of the same shape from its own seed (the scan has no cross-row or
-cross-head exchange), so scaling is weak and ``value`` = all ranks' tokens / the
-slowest rank's device time.
+bf16 with D + z).
+
+Multi-GPU (torchrun, one process per GPU; the scan has no cross-row or cross-group
+exchange, so nothing crosses NVLink on the data path):
+- headline: one global batch of ``8 N`` rows split by batch rows, 8 rows per rank
+  (weak scaling; at N = 1 it is config c1 itself); ``value`` = all ranks' tokens / the
+  slowest rank's device time. After the timed loop the ranks' ``y`` / ``h_last`` are
+  gathered over NCCL and rank 0 checks them against its own run of each rank's rows
+  (``verify``);
+- ``c4``: config c4 (8 x 65536, H128 over G8) as ONE global problem split by whole
+  head groups over the N ranks (strong scaling), tokens/s of that problem from the
+  slowest rank, and with N > 1 an NCCL gather of the outputs checked against rank 0's
+  one-GPU run of the whole problem. At N = 1 the line also carries c2, the c1 shape in
+  fp32 (the reference's own precision), the decode step and the other rows' kernels.
 
 Timing: CUDA events on the launching stream around each step, L2 flushed
 (256 MiB write) between steps outside the events, barrier + synchronize on both
@@ -51,6 +61,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-bwd", action="store_true", help="skip the SSD backward measurement")
     ap.add_argument("--no-sattn", action="store_true", help="skip the selective-attention decode measurement")
+    ap.add_argument("--no-c4", action="store_true", help="skip the config-c4 (head-group split) measurement")
+    ap.add_argument("--no-extra", action="store_true", help="skip the one-GPU c2 and fp32 measurements")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     return ap.parse_args()
 
@@ -257,81 +269,93 @@ def time_steps(fn, steps, flush_buf, stream):
     return [s.elapsed_time(e) for s, e in evs]
 
 
-def run_ours(args, rank, world, local):
-    import selective_attention_b200 as sab
-    from selective_attention_b200 import kernels, workloads
-
-    dev = torch.device("cuda", local)
-    cfg = workloads.CONFIGS[args.config]
-    peaks = {}
+def _peaks():
     try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except (OSError, ValueError):
-        pass
-    hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+        return {}
 
-    inp = workloads.make_ssd_inputs(cfg, seed=1 + rank, device=dev, gen_device="cuda")
-    T = cfg.tokens
-    stream = torch.cuda.current_stream(dev)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
-    cu = inp["cu_seqlens"]
-    nseq = None if cu is None else cu.numel() - 1
-    y = torch.empty(cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, dtype=inp["u"].dtype, device=dev)
-    h_last = torch.empty(nseq or cfg.batch, cfg.nheads, cfg.headdim, cfg.dstate, dtype=torch.float32, device=dev)
-    p, keep, _ = kernels.ssd_scan_params(inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None, None,
-                                         cfg.chunk, True, (0.0, INF), inp["D"], inp["z"], cu, args.kernel_impl)
-    ws = torch.empty(kernels.workspace_size(p), dtype=torch.uint8, device=dev)
-    tc = kernels.uses_tensor_cores(p)
-    path = kernels.scan_path(p)
+class SSDRun:
+    """One SSD forward problem resident on the device, its outputs and workspace, and a
+    ``step`` that runs ``kernels.ssd_scan_forward`` on it (the C-ABI ``ssd_scan_fwd``)."""
+
+    def __init__(self, cfg, inp, kernel_impl, dev):
+        from selective_attention_b200 import kernels
+
+        self.cfg, self.inp, self.dev = cfg, inp, dev
+        u = inp["u"]
+        b, L, H, P = u.shape
+        G, N = inp["B"].shape[2], inp["B"].shape[3]
+        self.shape = (b, L, H, P, N, G)
+        cu = inp["cu_seqlens"]
+        self.nseq = None if cu is None else cu.numel() - 1
+        self.y = torch.empty(b, L, H, P, dtype=u.dtype, device=dev)
+        self.h_last = torch.empty(self.nseq or b, H, P, N, dtype=torch.float32, device=dev)
+        p, self._keep, _ = kernels.ssd_scan_params(u, inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None,
+                                                   None, cfg.chunk, True, (0.0, INF), inp["D"], inp["z"], cu,
+                                                   kernel_impl)
+        self.ws = torch.empty(kernels.workspace_size(p), dtype=torch.uint8, device=dev)
+        self.tc = kernels.uses_tensor_cores(p)
+        self.path = kernels.scan_path(p)
+        self.kernel_impl = kernel_impl
+        self.launches = {"tc_fused": 2, "tc_staged": 3, "simt": 5}[self.path] + (1 if cu is not None else 0)
+
+    def step(self, events=None):
+        from selective_attention_b200 import kernels
+
+        i = self.inp
+        kernels.ssd_scan_forward(i["u"], i["A"], i["B"], i["C"], i["delta_raw"], None, None, None, self.cfg.chunk,
+                                 True, (0.0, INF), True, i["D"], i["z"], i["cu_seqlens"], self.kernel_impl,
+                                 out=(self.y, self.h_last), workspace=self.ws, events=events)
+
+
+def measure_ssd(run, args, world, flush, hbm_peak, peak_src, global_tokens, steps, clocks=None):
+    """Device time of ``steps`` SSD forwards (L2 flushed between them, barrier and
+    synchronize around the loop, max over ranks) and the per-stage split of a second
+    pass, with the dominant kernel's roofline. ``value`` = ``global_tokens`` / step time."""
+    import selective_attention_b200 as sab
+
+    dev, stream = run.dev, torch.cuda.current_stream(run.dev)
+    for _ in range(max(3, args.warmup)):
+        run.step()
+    torch.cuda.synchronize()
+    sab.check_device_error(dev)
+    barrier(world)
+    torch.cuda.synchronize()
+    if clocks is not None:
+        clocks.mark_start()
+    per_step = time_steps(run.step, steps, flush, stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    if clocks is not None:
+        clocks.mark_end()
+    ms_total = max_over_ranks(sum(per_step), world)
+    ms_step = ms_total / steps
+
     stage_ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
     for e in stage_ev:
         e.record(stream)  # materialise the handles
-    ev_handles = [e.cuda_event for e in stage_ev]
-
-    def step(events=None):
-        kernels.ssd_scan_forward(inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None, None,
-                                 cfg.chunk, True, (0.0, INF), True, inp["D"], inp["z"], cu, args.kernel_impl,
-                                 out=(y, h_last), workspace=ws, events=events)
-
-    for _ in range(max(3, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    sab.check_device_error(dev)
-
-    clocks = ClockSampler(local)
-    time.sleep(1.0)  # let the sampler start before the timed loop
-    barrier(world)
-    torch.cuda.synchronize()
-    clocks.mark_start()
-    per_step = time_steps(step, args.steps, flush, stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    clocks.mark_end()
-    ms_total = max_over_ranks(sum(per_step), world)
-    ms_step = ms_total / args.steps
-    value = world * T / (ms_total / 1e3 / args.steps)
-
-    # per-stage times (separate pass, same flushing) for the roofline
-    n_stage = min(args.steps, 50)
-    st = [[0.0] * 5 for _ in range(n_stage)]
-    for i in range(n_stage):
+    handles = [e.cuda_event for e in stage_ev]
+    n_stage = min(steps, 50)
+    st = []
+    for _ in range(n_stage):
         flush.fill_(1)
-        step(events=ev_handles)
+        run.step(events=handles)
         torch.cuda.synchronize()
-        for j in range(5):
-            st[i][j] = stage_ev[j].elapsed_time(stage_ev[j + 1])
+        st.append([stage_ev[j].elapsed_time(stage_ev[j + 1]) for j in range(5)])
     stage_ms = [statistics.median(r[j] for r in st) for j in range(5)]
-    clk = clocks.stop()
     sab.check_device_error(dev)
 
-    # algorithmic bytes of the dominant kernel (chunk_scan with bmm fused, D/z epilogue)
-    sx = inp["u"].element_size()
-    b, L, H, P, N, G = cfg.batch, cfg.seqlen, cfg.nheads, cfg.headdim, cfg.dstate, cfg.ngroups
+    cfg, tc, path, nseq = run.cfg, run.tc, run.path, run.nseq
+    b, L, H, P, N, G = run.shape
+    T = b * L
+    sx = run.inp["u"].element_size()
+    cu = run.inp["cu_seqlens"]
     nck = (T + cfg.chunk - 1) // cfg.chunk + (nseq or 0) if cu is not None else b * math.ceil(L / cfg.chunk)
     s_prev = 2 if tc else 4
-    scan_bytes = (T * H * P * (sx + sx + y.element_size()) + 2 * T * G * N * sx + 8 * T * H
+    # algorithmic bytes per launch of each stage (fp32 intermediates on the CUDA-core chain)
+    scan_bytes = (T * H * P * (sx + sx + run.y.element_size()) + 2 * T * G * N * sx + 8 * T * H
                   + s_prev * nck * H * P * N)
     state_bytes = T * H * P * sx + T * G * N * sx + 8 * T * H + 4 * nck * H * P * N
     pass_bytes = 4 * nck * H * P * N + s_prev * nck * H * P * N + 4 * (nseq or b) * H * P * N + 4 * nck * H
@@ -355,36 +379,189 @@ def run_ours(args, rank, world, local):
         gbs = by / (ms_ / 1e3) / 1e9 if ms_ > 0 else None
         stages[n_] = {"us": ms_ * 1e3, "alg_bytes": by, "gbs": gbs, "frac": (gbs / hbm_peak) if gbs else None}
     dom = max(stages, key=lambda k: stages[k]["us"])
-    traffic = _traffic_from_profiles(dom, cfg.name)
     roof = {"kernel": dom, "bound": "hbm", "achieved": stages[dom]["gbs"], "peak": hbm_peak, "unit": "GB/s",
-            "frac": stages[dom]["frac"], "traffic": traffic, "peak_source": peak_src,
-            "alg_bytes_per_launch": stages[dom]["alg_bytes"], "us_per_launch": stages[dom]["us"]}
-    fused_min = workloads.ssd_algorithmic_bytes(cfg, y_bytes=y.element_size(), nseq=nseq)
+            "frac": stages[dom]["frac"], "traffic": _traffic_from_profiles(dom, cfg.name, T, H),
+            "peak_source": peak_src, "alg_bytes_per_launch": stages[dom]["alg_bytes"],
+            "us_per_launch": stages[dom]["us"]}
+    from selective_attention_b200 import workloads
+
+    local_cfg = workloads.SSDConfig(**{**cfg.__dict__, "batch": b, "seqlen": L, "nheads": H, "ngroups": G})
+    fused_min = workloads.ssd_algorithmic_bytes(local_cfg, y_bytes=run.y.element_size(), nseq=nseq)
     whole = {"alg_min_bytes": fused_min, "gbs": fused_min / (ms_step / 1e3) / 1e9,
              "frac_of_fused_roof": fused_min / (ms_step / 1e3) / 1e9 / hbm_peak}
+    return {"value": global_tokens / (ms_step / 1e3), "unit": "tokens/s", "ms_per_step": ms_step, "steps": steps,
+            "path": {"tc_fused": "tcgen05, chunk_state+state_passing fused", "tc_staged": "tcgen05",
+                     "simt": "cuda-core"}[path],
+            "roofline": roof, "stages": stages, "whole_step": whole, "launches_per_step": run.launches}
 
+
+def _row_split_inputs(cfg, rank, world, dev):
+    """This rank's rows of the global batch (``cfg.batch`` rows per rank), or for packed
+    varlen configs its own packed batch (batch ``rank`` of the global problem)."""
+    from selective_attention_b200 import sharding, workloads
+
+    if cfg.varlen:
+        return workloads.make_ssd_inputs(cfg, seed=1 + rank, device=dev, gen_device="cuda")
+    glob = workloads.SSDConfig(**{**cfg.__dict__, "batch": cfg.batch * world})
+    return sharding.make_row_inputs(glob, 1, sharding.row_range(rank, world, glob.batch), device=dev,
+                                    gen_device="cuda")
+
+
+def verify_row_split(run, cfg, rank, world, dev, args):
+    """NCCL all_gather of every rank's y and h_last (outside the timed region); rank 0
+    rebuilds each other rank's rows from the shared seed, runs them through the same
+    kernels and compares."""
+    from selective_attention_b200 import sharding
+
+    y_all = sharding.gather_rows(run.y, world)
+    h_all = sharding.gather_rows(run.h_last, world)
+    if rank != 0:
+        return None
+    worst = {"bit_identical": True, "max_abs_diff": 0.0}
+    b = run.y.shape[0]
+    for r in range(1, world):
+        other = SSDRun(cfg, _row_split_inputs(cfg, r, world, dev), args.kernel_impl, dev)
+        other.step()
+        torch.cuda.synchronize()
+        for got, want in ((y_all[r * b:(r + 1) * b], other.y), (h_all[r * b:(r + 1) * b], other.h_last)):
+            c = sharding.compare(got, want)
+            worst["bit_identical"] &= c["bit_identical"]
+            worst["max_abs_diff"] = max(worst["max_abs_diff"], c["max_abs_diff"])
+        del other
+    return {"collective": "nccl all_gather of y and h_last", "checked_ranks": list(range(1, world)),
+            "against": "rank 0 re-running each rank's rows from the shared seed", **worst}
+
+
+def c4_measure(args, rank, world, dev, flush, hbm_peak, peak_src):
+    """Config c4 (bf16 8 x 65536, H128 P64 N128 G8 cs256, D + z), one global problem split
+    by whole head groups over the ranks (strong scaling: rank r takes groups
+    [8r/N, 8(r+1)/N)); tokens/s for the global problem from the slowest rank's device
+    time. With N > 1, the ranks' y and h_last are gathered over NCCL after the timed
+    loop, batch row by batch row, and rank 0 compares them with its own one-GPU run of
+    the whole problem."""
+    from selective_attention_b200 import sharding, workloads
+
+    cfg = workloads.CONFIGS["c4"]
+    groups = sharding.group_range(rank, world, cfg.ngroups)
+    inp = sharding.make_group_inputs(cfg, 1, groups, device=dev, gen_device="cuda")
+    run = SSDRun(cfg, inp, args.kernel_impl, dev)
+    steps = max(5, min(args.steps, 50))
+    res = measure_ssd(run, args, world, flush, hbm_peak, peak_src, cfg.tokens, steps)
+    res.update(workload=_workload_name(cfg), scaling="strong", n_gpus=world,
+               split=f"head groups {groups[0]}..{groups[1] - 1} of {cfg.ngroups} on rank {rank}" if world > 1
+               else "whole problem on one GPU", dtype="bf16")
+    if world > 1:
+        full = None
+        if rank == 0:
+            torch.cuda.empty_cache()
+            full = SSDRun(cfg, sharding.make_group_inputs(cfg, 1, (0, cfg.ngroups), device=dev, gen_device="cuda"),
+                          args.kernel_impl, dev)
+            full.step()
+            torch.cuda.synchronize()
+        worst = {"bit_identical": True, "max_abs_diff": 0.0}
+        for r in range(cfg.batch):
+            got = sharding.gather_heads(run.y[r:r + 1], world, 2)
+            if full is not None:
+                c = sharding.compare(got, full.y[r:r + 1])
+                worst["bit_identical"] &= c["bit_identical"]
+                worst["max_abs_diff"] = max(worst["max_abs_diff"], c["max_abs_diff"])
+            del got
+        got = sharding.gather_heads(run.h_last, world, 1)
+        if full is not None:
+            c = sharding.compare(got, full.h_last)
+            worst["bit_identical"] &= c["bit_identical"]
+            worst["max_abs_diff"] = max(worst["max_abs_diff"], c["max_abs_diff"])
+            res["verify"] = {"collective": "nccl all_gather of y (per batch row) and h_last",
+                             "against": "rank 0's one-GPU run of the whole c4 problem", **worst}
+        del full, got
+    del run, inp
+    torch.cuda.empty_cache()
+    return res
+
+
+def c2_measure(args, dev, flush, hbm_peak, peak_src):
+    """Config c2 (32768 packed tokens, H80 P64 N128 G1 cs256, D + z, bf16) on one GPU."""
+    from selective_attention_b200 import workloads
+
+    cfg = workloads.CONFIGS["c2"]
+    inp = workloads.make_ssd_inputs(cfg, seed=1, device=dev, gen_device="cuda")
+    run = SSDRun(cfg, inp, args.kernel_impl, dev)
+    res = measure_ssd(run, args, 1, flush, hbm_peak, peak_src, cfg.tokens, max(5, min(args.steps, 100)))
+    res.update(workload=_workload_name(cfg), n_gpus=1, dtype="bf16")
+    del run, inp
+    torch.cuda.empty_cache()
+    return res
+
+
+def fp32_measure(args, dev, flush, hbm_peak, peak_src):
+    """Config c1's shape in fp32 (the reference's own precision: its SSD takes fp32
+    operands only) on one GPU: fp32 u, B, C, z in and y out, on the CUDA-core chain."""
+    from selective_attention_b200 import workloads
+
+    cfg = workloads.SSDConfig(**{**workloads.CONFIGS["c1"].__dict__, "dtype": "f32"})
+    inp = workloads.make_ssd_inputs(cfg, seed=1, device=dev, gen_device="cuda")
+    run = SSDRun(cfg, inp, "auto", dev)
+    res = measure_ssd(run, args, 1, flush, hbm_peak, peak_src, cfg.tokens, max(5, min(args.steps, 50)))
+    res.update(workload=_workload_name(cfg), n_gpus=1, dtype="f32")
+    del run, inp
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_ours(args, rank, world, local):
+    dev = torch.device("cuda", local)
+    from selective_attention_b200 import workloads
+
+    cfg = workloads.CONFIGS[args.config]
+    peaks = _peaks()
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    # Headline: the workload split by batch rows, cfg.batch rows per rank (weak scaling);
+    # at one GPU it is the benchmark config itself.
+    inp = _row_split_inputs(cfg, rank, world, dev)
+    run = SSDRun(cfg, inp, args.kernel_impl, dev)
+    clocks = ClockSampler(local)
+    time.sleep(1.0)  # let the sampler start before the timed loop
+    head = measure_ssd(run, args, world, flush, hbm_peak, peak_src, world * cfg.tokens, args.steps, clocks)
+    clk = clocks.stop()
+    sx = inp["u"].element_size()
+    parallelism = "single" if world == 1 else f"dp{world}: batch rows split, {cfg.batch} rows per rank"
+    if cfg.varlen and world > 1:
+        parallelism = f"dp{world}: one packed batch per rank"
     line = {
-        "metric": "SSD chunked-scan fwd tokens/s", "value": value, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "metric": "SSD chunked-scan fwd tokens/s", "value": head["value"], "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16" if sx == 2 else "f32", "data": "synthetic",
         "config": {"workload": _workload_name(cfg), "global_batch": cfg.batch * world, "seq_len": cfg.seqlen,
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
-                   "path": {"tc_fused": "tcgen05, chunk_state+state_passing fused", "tc_staged": "tcgen05",
-                            "simt": "cuda-core"}[path], "l2": "flushed between timed steps (256 MiB write)"},
-        "roofline": roof, "stages": stages, "whole_step": whole, "clocks": clk,
-        "gpu_launches": args.steps * ({"tc_fused": 2, "tc_staged": 3, "simt": 5}[path] + (1 if cu is not None else 0)),
+                   "parallelism": parallelism, "path": head["path"],
+                   "l2": "flushed between timed steps (256 MiB write)"},
+        "roofline": head["roofline"], "stages": head["stages"], "whole_step": head["whole_step"], "clocks": clk,
+        "gpu_launches": args.steps * run.launches,
     }
+    if world > 1 and not cfg.varlen:
+        line["verify"] = verify_row_split(run, cfg, rank, world, dev, args)
     if not args.no_e2e:
         line["e2e"] = e2e_measure(args, cfg, inp, dev, world, flush)
-    if not args.no_ssu:
-        line["ssu"] = ssu_measure(args, dev, flush, hbm_peak, world)
-    if not args.no_front:
-        line["front"] = front_measure(args, dev, flush, hbm_peak)
-    if not args.no_bwd and world == 1:
-        line["bwd"] = bwd_measure(args, cfg, inp, dev, flush)
-    if not args.no_sattn and world == 1:
-        line["sattn_decode"] = sattn_measure(args, dev, flush, hbm_peak)
-        line["sattn_prefill"] = sattn_prefill_measure(args, dev, flush, peaks.get("bf16_tflops", 1590.0))
+    del run
+    torch.cuda.empty_cache()
+    if not args.no_c4:
+        line["c4"] = c4_measure(args, rank, world, dev, flush, hbm_peak, peak_src)
+    if world == 1:
+        if not args.no_extra and args.config != "c2":
+            line["c2"] = c2_measure(args, dev, flush, hbm_peak, peak_src)
+        if not args.no_extra:
+            line["fp32"] = fp32_measure(args, dev, flush, hbm_peak, peak_src)
+        if not args.no_ssu:
+            line["ssu"] = ssu_measure(args, dev, flush, hbm_peak, world)
+        if not args.no_front:
+            line["front"] = front_measure(args, dev, flush, hbm_peak)
+        if not args.no_bwd:
+            line["bwd"] = bwd_measure(args, cfg, inp, dev, flush)
+        if not args.no_sattn:
+            line["sattn_decode"] = sattn_measure(args, dev, flush, hbm_peak)
+            line["sattn_prefill"] = sattn_prefill_measure(args, dev, flush, peaks.get("bf16_tflops", 1590.0))
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
@@ -399,13 +576,20 @@ def _workload_name(cfg):
             f"G{cfg.ngroups} cs{cfg.chunk} {extra}").strip()
 
 
-def _traffic_from_profiles(kernel, cfg_name):
+def _traffic_from_profiles(kernel, cfg_name, tokens, heads):
+    """DRAM bytes per launch of ``kernel`` from the committed ncu summary
+    (``profiles/dram_traffic.json``: per config, the bytes of one captured launch and the
+    token-heads it processed), scaled to this launch's token-heads; None without a capture."""
     path = os.path.join(ROOT, "profiles", "dram_traffic.json")
     try:
-        d = json.load(open(path))
-        return d.get(cfg_name, {}).get(kernel)
+        d = json.load(open(path)).get(cfg_name, {}).get(kernel)
     except (OSError, ValueError):
         return None
+    if d is None:
+        return None
+    if isinstance(d, dict):
+        return d["bytes"] * (tokens * heads) / d["token_heads"]
+    return d
 
 
 E2E_SLICES = 4

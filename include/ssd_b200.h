@@ -169,10 +169,14 @@ int ssd_scan_fwd(const ssd_params* p, void* stream);
  * SSD_NOALLOC_SCRATCH_BYTES on every GPU that loads it, until the process exits;
  * p->workspace and p->workspace_bytes are ignored. A problem whose
  * ssd_scan_fwd_workspace_size() exceeds the array returns SSD_ERR_SCRATCH_LIMIT
- * (the tensor-core path needs about 50 KB per chunk and head: b=2, L=2048, H=32 fits;
- * b=8, L=2048, H=24, at 78 MB, does not).
+ * (the fused tensor-core chain, the default from SSD_FUSED_MIN_CHAINS (row, head)
+ * chains, needs about 18 KB per chunk and head: b=8, L=2048, H=24 takes about 28 MB
+ * and fits; the staged chain (SSD_IMPL_TC_STAGED, or fewer chains under AUTO) needs
+ * about 50 KB per chunk and head, so the same shape forced onto it, at 78 MB, is
+ * rejected; b=2, L=2048, H=32 on the staged chain takes 26 MB and fits).
  * The first call on a device resolves the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture. All calls
+ * (cudaGetSymbolAddress); make that first call before any stream capture. A failed
+ * lookup is not remembered: the next call on that device tries again. All calls
  * share the array: calls that overlap on the GPU (other streams or host threads)
  * race on it. Nothing in it needs to start at zero.
  */

@@ -1,9 +1,10 @@
 """Run the reference's own Triton kernels on CPU under the Triton interpreter.
 
-TEST INFRASTRUCTURE ONLY: used by ``tests/golden/make_golden.py`` to produce the
-committed golden vectors. It needs the reference checkout (``SA_REFERENCE_SRC`` or
-the default mount) and therefore never runs on a GPU box; nothing in the product,
-the GPU tests or ``bench.py`` imports it.
+TEST INFRASTRUCTURE ONLY: used by ``tests/golden/make_golden*.py`` to produce the
+committed golden vectors. It needs the reference's Python sources: the directory named
+by ``SA_REFERENCE_SRC`` (the checkout's ``src/``), else the copy that
+``baseline/install_reference.sh`` installs into ``baseline/_ref`` of this repository.
+Nothing in the product, the GPU tests or ``bench.py`` imports it.
 
 Recipe:
 - ``TRITON_INTERPRET=1`` must be set before ``triton`` is first imported;
@@ -17,7 +18,8 @@ from __future__ import annotations
 import os
 import sys
 
-DEFAULT_SRC = os.environ.get("SA_REFERENCE_SRC", "/root/reference/src")
+_REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+DEFAULT_SRC = os.environ.get("SA_REFERENCE_SRC") or os.path.join(_REPO, "baseline", "_ref")
 
 _loaded = None
 
@@ -31,7 +33,8 @@ def load():
         raise RuntimeError("triton was imported before TRITON_INTERPRET=1 could be set")
     os.environ["TRITON_INTERPRET"] = "1"
     if not os.path.isdir(DEFAULT_SRC):
-        raise FileNotFoundError(f"reference sources not found at {DEFAULT_SRC}")
+        raise FileNotFoundError(f"reference sources not found at {DEFAULT_SRC}: set SA_REFERENCE_SRC to the "
+                                "reference checkout's src/ or run baseline/install_reference.sh")
     if DEFAULT_SRC not in sys.path:
         sys.path.insert(0, DEFAULT_SRC)
     import selective_attention.triton_kernels.ssd_scan.forward_kernel as fk  # noqa: E402

@@ -11,7 +11,8 @@
 // holds its SSD_NOALLOC_SCRATCH_BYTES until the process exits. Host code cannot use
 // the variable's name as a device address, so its address is resolved with
 // cudaGetSymbolAddress once per device, with that device current, on the first call
-// on that device (that first call should come before any stream capture). All calls
+// on that device (that first call should come before any stream capture; a lookup that
+// fails is not remembered, so a later call on that device tries again). All calls
 // share the one array and it keeps the last call's contents; nothing in it needs to
 // start at zero because every call writes each region before reading it. Calls that
 // overlap on the GPU (other streams, other host threads) race on the array.
@@ -24,22 +25,29 @@ namespace {
 static __device__ __align__(256) unsigned char g_ssd_noalloc_scratch[SSD_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_setup_once[kMaxDevices];
+std::mutex g_setup_mutex;
+bool g_resolved[kMaxDevices];
 void* g_scratch_addr[kMaxDevices];
-cudaError_t g_setup_status[kMaxDevices];
 
-// Device address of the scratch array on the current device (resolved once per device).
+// Device address of the scratch array on the current device. Only a successful lookup
+// is cached: a lookup that failed (for instance one made while the stream was being
+// captured) is tried again on the next call.
 cudaError_t scratch_on_current_device(void** addr) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::call_once(g_setup_once[dev], [dev]() {
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (!g_resolved[dev]) {
     void* p = nullptr;
-    g_setup_status[dev] = cudaGetSymbolAddress(&p, g_ssd_noalloc_scratch);
-    g_scratch_addr[dev] = (g_setup_status[dev] == cudaSuccess) ? p : nullptr;
-  });
-  if (g_setup_status[dev] != cudaSuccess) return g_setup_status[dev];
+    e = cudaGetSymbolAddress(&p, g_ssd_noalloc_scratch);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();  // clear the failed lookup from the thread's last-error state
+      return e;
+    }
+    g_scratch_addr[dev] = p;
+    g_resolved[dev] = true;
+  }
   *addr = g_scratch_addr[dev];
   return cudaSuccess;
 }

@@ -385,3 +385,68 @@ def test_repeated_runs_are_bit_identical(impl):
         differ += int(not (torch.equal(y, y0) and torch.equal(h, h0)))
     torch.cuda.synchronize()
     assert differ == 0, f"{differ} of 40 runs differ from the first"
+
+
+def _oracle_slice(inp, row, group, hpg, chunk=256):
+    """Oracle y (with the D / z epilogue) and h_last of one batch row x one head group:
+    the scan is independent per (row, group), so a slice of the full problem is a
+    complete problem of its own."""
+    hs = slice(group * hpg, (group + 1) * hpg)
+    P = inp["u"].shape[-1]
+    u = inp["u"][row:row + 1, :, hs].cpu()
+    B = inp["B"][row:row + 1, :, group:group + 1].cpu().float()
+    C = inp["C"][row:row + 1, :, group:group + 1].cpu().float()
+    dr = inp["delta_raw"][row:row + 1, :, hs].cpu()
+    A = inp["A"][hs].cpu()
+    D = inp["D"][group * hpg * P:(group + 1) * hpg * P].cpu()
+    z = inp["z"][row:row + 1, :, group * hpg * P:(group + 1) * hpg * P].cpu()
+    y, h = ssd_ref.ssd_scan_forward(u.float(), A, B, C, dr, None, None, None, chunk)
+    return ssd_ref.gate_epilogue(y, u, D, z), h
+
+
+def test_c4_full_size_first_and_last_row_group_vs_oracle():
+    """Benchmark config c4 at its real size on one GPU: 8 x 65536 tokens, H128 over G8
+    (16 heads a group), P64 N128, cs256, D + z, bf16: 256 chunks per state chain and
+    u / z / y of 4.3e9 elements, so byte offsets run far past 2^32. The first and the last
+    (row, group) slices, which hold the smallest and the largest offsets, are checked
+    against the oracle (forward.py:223-276 over the whole chain)."""
+    import selective_attention_b200 as sab
+    from selective_attention_b200 import kernels, workloads
+
+    cfg = workloads.CONFIGS["c4"]
+    inp = workloads.make_ssd_inputs(cfg, seed=0, device=torch.device("cuda"), gen_device="cuda")
+    p, keep, _ = kernels.ssd_scan_params(inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None, None,
+                                         256, True, (0.0, INF), inp["D"], inp["z"])
+    assert kernels.scan_path(p) == "tc_fused"
+    y, h = kernels.ssd_scan_forward(inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None, None, 256,
+                                    True, (0.0, INF), True, inp["D"], inp["z"])
+    torch.cuda.synchronize()
+    sab.check_device_error()
+    assert y.numel() > (1 << 32)
+    hpg = cfg.nheads // cfg.ngroups
+    for row, group in ((0, 0), (cfg.batch - 1, cfg.ngroups - 1)):
+        y_ref, h_ref = _oracle_slice(inp, row, group, hpg)
+        hs = slice(group * hpg, (group + 1) * hpg)
+        assert_bf16_close(y[row:row + 1, :, hs], y_ref, f"c4 row {row} group {group} y")
+        assert_bf16_close(h[row:row + 1, hs], h_ref, f"c4 row {row} group {group} h_last")
+
+
+def test_c1_default_dispatch_repeated_runs_are_bit_identical():
+    """c1 on the default dispatch: the fused chain with 8 rows x 12 head pairs = 96 state
+    chains, one wave on 148 SMs, so chunk_scan is launched as a programmatic dependent of
+    the state pass and its producer waits on the grid before reading dt, cum and the
+    16-bit states. 40 repeated runs must match the first bit for bit."""
+    from selective_attention_b200 import kernels, workloads
+
+    inp = workloads.make_ssd_inputs(workloads.CONFIGS["c1"], seed=0, device=torch.device("cuda"), gen_device="cuda")
+    args = (inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None, None, 256, True, (0.0, INF), True,
+            inp["D"], inp["z"], None)
+    p, keep, _ = kernels.ssd_scan_params(*args[:11], inp["D"], inp["z"])
+    assert kernels.scan_path(p) == "tc_fused"
+    y0, h0 = kernels.ssd_scan_forward(*args)
+    differ = 0
+    for _ in range(40):
+        y, h = kernels.ssd_scan_forward(*args)
+        differ += int(not (torch.equal(y, y0) and torch.equal(h, h0)))
+    torch.cuda.synchronize()
+    assert differ == 0, f"{differ} of 40 runs differ from the first"

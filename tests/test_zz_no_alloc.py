@@ -22,12 +22,23 @@ pytestmark = pytest.mark.gpu
 INF = float("inf")
 
 
-def _inputs(dtype, seed):
+# (dtype, batch, seqlen, heads, chain the default dispatch takes). 2 x 8 (row, head)
+# chains run the staged tensor-core chain (bf16) or the CUDA-core chain (fp32); 8 x 16 =
+# 128 chains reach the fused chain, whose state pass and chunk_scan overlap through a
+# dependent launch and read dt, cum and the 16-bit chunk states from the scratch array.
+CASES = [
+    (torch.bfloat16, 2, 700, 8, "tc_staged"),
+    (torch.float32, 2, 700, 8, "simt"),
+    (torch.bfloat16, 8, 700, 16, "tc_fused"),
+]
+
+
+def _inputs(dtype, seed, batch, seqlen, nheads):
     from selective_attention_b200 import workloads
 
     cfg = workloads.CONFIGS["c1"]
     name = {torch.bfloat16: "bf16", torch.float32: "f32"}[dtype]
-    inp = workloads.make_ssd_inputs(cfg, seed=seed, batch=2, seqlen=700, nheads=8, dtype=name,
+    inp = workloads.make_ssd_inputs(cfg, seed=seed, batch=batch, seqlen=seqlen, nheads=nheads, dtype=name,
                                     delta_bias=True, h_init=True)
     return {k: (v.cuda() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
 
@@ -42,12 +53,12 @@ def _params(inp, y, h_last):
     return p, keep
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_noalloc_matches_workspace_entry_point_twice(dtype):
+@pytest.mark.parametrize("dtype,batch,seqlen,nheads,path", CASES, ids=[c[4] for c in CASES])
+def test_noalloc_matches_workspace_entry_point_twice(dtype, batch, seqlen, nheads, path):
     import selective_attention_b200 as sab
     from selective_attention_b200 import _lib, kernels
 
-    inp = _inputs(dtype, seed=21)
+    inp = _inputs(dtype, 21, batch, seqlen, nheads)
     y_ref, h_ref = kernels.ssd_scan_forward(inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"],
                                             inp["delta_bias"], inp["h_init"], None, 256, True, (0.0, INF), True,
                                             inp["D"], inp["z"])
@@ -59,6 +70,8 @@ def test_noalloc_matches_workspace_entry_point_twice(dtype):
         h_last = torch.full_like(h_ref, float("nan"))
         p, keep = _params(inp, y, h_last)
         assert p.workspace is None  # nothing is passed in
+        assert kernels.scan_path(p) == path
+        assert L.ssd_scan_fwd_workspace_size(ctypes.byref(p)) <= (32 << 20)
         st = L.ssd_scan_fwd_noalloc(ctypes.byref(p), stream)
         assert st == _lib.SSD_OK, L.ssd_b200_status_string(st).decode()
         torch.cuda.synchronize()
