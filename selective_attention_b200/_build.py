@@ -20,7 +20,7 @@ LIB_NAME = "libssd_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
 SOURCES = ["api.cu", "ssd_simt.cu", "ssd_tc.cu", "ssd_bwd.cu", "ssu.cu", "ssm_conv.cu", "sattn.cu", "noalloc.cu"]
-HEADERS = ["common.cuh", "sm100.cuh", "kernels.h"]
+HEADERS = ["common.cuh", "sm100.cuh", "tmap.cuh", "kernels.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",

@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "sm100.cuh"
+#include "tmap.cuh"
 
 namespace ssdb200 {
 namespace {
@@ -652,6 +653,348 @@ cudaError_t prefill_tc_t(const void* q, const void* k, const void* v, const floa
   return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------
+// Pipelined tensor-core prefill, head_dim 64 (16-bit inputs)
+// ---------------------------------------------------------------------------
+// One CTA per (batch row x head, pair of 128-query tiles A = 2t and B = 2t + 1), the
+// pairs with the most key tiles first. Warp roles (12 warps):
+//   warp 0            loads: Q_A and Q_B once, then per 128-key tile K and V (TMA,
+//                     128-byte swizzle) and its log-gates times log2(e), in a ring of
+//                     kFaStages;
+//   warp 1 (lane 0)   MMA issuer: S_w = Q_w K_j^T into TMEM; once softmax w has written
+//                     P_w(j): O_w += P_w V_j (A from TMEM) and at once S_w(j + 1). The
+//                     two tiles alternate, so the tensor core works on one tile while
+//                     the other tile's softmax runs;
+//   warps 4-7, 8-11   softmax of tile A, B: thread = query row = TMEM lane. A key tile's
+//                     128 scores sit in registers: gate (every earlier key adds its
+//                     log-gate, the token's own score is ungated), causal and length
+//                     masks on the diagonal and tail tiles only, running max in the
+//                     log2 domain (O and the sum are rescaled only when it grows by more
+//                     than e^8), P = 2^(s - m) in 16 bits to TMEM, the row sum; at the
+//                     end out = O / sum;
+//   warps 2-3         no work (they keep the softmax warpgroups aligned to TMEM lanes).
+// TMEM (512 columns): S_A [0,128) S_B [128,256) P_A [256,320) P_B [320,384)
+//                     O_A [384,448) O_B [448,512). Every wait is bounded; a role that
+// gives up records a site code, raises the CTA's abort flag and leaves its loop.
+constexpr int kFaThreads = 384;
+constexpr int kFaStages = 3;
+constexpr int kFaTile = 128 * 128;                 // 128 rows x 64 16-bit elements
+constexpr int kFaStageBytes = 2 * kFaTile + 1024;  // K | V | 128 log-gates (1 KB keeps the alignment)
+constexpr size_t kFaSmem = 1024 + 2 * kFaTile + kFaStages * kFaStageBytes + 256;
+constexpr unsigned int kSiteFaLoad = 0x311, kSiteFaMma = 0x312, kSiteFaSoft = 0x313;
+
+template <typename T>
+__global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                                          const __grid_constant__ CUtensorMap tm_k,
+                                                                          const __grid_constant__ CUtensorMap tm_v,
+                                                                          const float* __restrict__ lg,
+                                                                          T* __restrict__ out, int L, float scale) {
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr int NS = kFaStages;
+  extern __shared__ uint8_t smraw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = base;  // Q_A | Q_B
+  auto sK = [&](int s) { return base + 2 * kFaTile + s * kFaStageBytes; };
+  auto sV = [&](int s) { return sK(s) + kFaTile; };
+  auto sG = [&](int s) { return reinterpret_cast<float*>(sK(s) + 2 * kFaTile); };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * kFaTile + NS * kFaStageBytes);
+  enum {
+    Q_FULL = 0, K_FULL = 1, V_FULL = K_FULL + NS, KV_EMPTY = V_FULL + NS, S_FULL = KV_EMPTY + NS,
+    P_FULL = S_FULL + 2, O_DONE = P_FULL + 2, DRAIN = O_DONE + 2, NBARS = DRAIN + 1
+  };
+  static_assert(NBARS * 8 + 8 <= 256, "barrier area");
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  const int bh = blockIdx.x;
+  const int t = (int)gridDim.y - 1 - (int)blockIdx.y;  // pairs with the most key tiles first
+  const int q0A = 256 * t, q0B = q0A + 128;
+  const int nkA = q0A < L ? min(q0A + 127, L - 1) / 128 + 1 : 0;
+  const int nkB = q0B < L ? min(q0B + 127, L - 1) / 128 + 1 : 0;
+  const int nk = max(nkA, nkB);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+    mbar_init(bar(Q_FULL), 1);
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(bar(K_FULL + s), 1);
+      mbar_init(bar(V_FULL + s), 1);
+      mbar_init(bar(KV_EMPTY + s), 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(bar(S_FULL + w), 1);
+      mbar_init(bar(P_FULL + w), 4);
+      mbar_init(bar(O_DONE + w), 1);
+    }
+    mbar_init(bar(DRAIN), 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(smem_u32(tslot), 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  constexpr uint32_t T_S = 0, T_P = 256, T_O = 384;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ loads
+    if (lane == 0) {
+      mbar_expect_tx(bar(Q_FULL), (nkB > 0 ? 2u : 1u) * (uint32_t)kFaTile);
+      tma_load_3d(smem_u32(sQ), &tm_q, 0, q0A, bh, bar(Q_FULL));
+      if (nkB > 0) tma_load_3d(smem_u32(sQ + kFaTile), &tm_q, 0, q0B, bh, bar(Q_FULL));
+    }
+    const float* gb = lg + (long long)bh * L;
+    bool fail = false;
+    int j = 0;
+    for (; j < nk; ++j) {
+      const int s = j % NS;
+      // the stage's gates are rewritten below: every lane waits for its release
+      if (j >= NS && (!__all_sync(0xffffffffu, mbar_wait(bar(KV_EMPTY + s), ((j / NS) - 1) & 1, kSiteFaLoad)) ||
+                      *s_abort)) {
+        fail = true;
+        break;
+      }
+      const int k = 128 * j + 4 * lane;
+      float4 g4;
+      g4.x = k < L ? gb[k] * kLog2e : -INFINITY;
+      g4.y = k + 1 < L ? gb[k + 1] * kLog2e : -INFINITY;
+      g4.z = k + 2 < L ? gb[k + 2] * kLog2e : -INFINITY;
+      g4.w = k + 3 < L ? gb[k + 3] * kLog2e : -INFINITY;
+      reinterpret_cast<float4*>(sG(s))[lane] = g4;
+      __syncwarp();
+      if (lane == 0) {
+        mbar_expect_tx(bar(K_FULL + s), (uint32_t)kFaTile);
+        tma_load_3d(smem_u32(sK(s)), &tm_k, 0, 128 * j, bh, bar(K_FULL + s));
+        mbar_expect_tx(bar(V_FULL + s), (uint32_t)kFaTile);
+        tma_load_3d(smem_u32(sV(s)), &tm_v, 0, 128 * j, bh, bar(V_FULL + s));
+      }
+    }
+    if (fail && lane == 0) *s_abort = 1;
+    if (lane == 0) {
+      // no copy may still be in flight when the CTA exits
+      mbar_wait(bar(Q_FULL), 0, kSiteFaLoad);
+      for (int d = 1; d <= NS && d <= j; ++d) {
+        const int jj = j - d;
+        mbar_wait(bar(K_FULL + jj % NS), (jj / NS) & 1, kSiteFaLoad);
+        mbar_wait(bar(V_FULL + jj % NS), (jj / NS) & 1, kSiteFaLoad);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_S = idesc_f16(128, 128, BF16, false, false);
+      constexpr uint32_t ID_O = idesc_f16(128, 64, BF16, false, true);
+      const uint32_t qa = smem_u32(sQ);
+      const int nkw[2] = {nkA, nkB};
+      bool issued = false;
+      auto issue_s = [&](int w, int jj) -> bool {
+        const int s = jj % NS;
+        if (!mbar_wait(bar(K_FULL + s), (jj / NS) & 1, kSiteFaMma)) return false;
+        tc_fence_after();
+        const uint32_t qb = qa + (uint32_t)(w * kFaTile), kb = smem_u32(sK(s));
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_f16(tmem + T_S + 128 * w, sdesc_sw128(qb + 32 * ks, 16, 1024), sdesc_sw128(kb + 32 * ks, 16, 1024),
+                   ID_S, ks > 0 ? 1u : 0u);
+        umma_commit(bar(S_FULL + w));
+        issued = true;
+        return true;
+      };
+      bool fail = !mbar_wait(bar(Q_FULL), 0, kSiteFaMma);
+      if (!fail) fail = !issue_s(0, 0);
+      if (!fail && nkB > 0) fail = !issue_s(1, 0);
+      for (int j = 0; j < nk && !fail && !*s_abort; ++j) {
+        const int s = j % NS;
+        if (!mbar_wait(bar(V_FULL + s), (j / NS) & 1, kSiteFaMma)) {
+          fail = true;
+          break;
+        }
+        const uint32_t vb = smem_u32(sV(s));
+        for (int w = 0; w < 2; ++w) {
+          if (j >= nkw[w]) continue;
+          if (!mbar_wait(bar(P_FULL + w), j & 1, kSiteFaMma)) {
+            fail = true;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            umma_f16_ts(tmem + T_O + 64 * w, tmem + T_P + 64 * w + 8 * ks, sdesc_sw128(vb + 2048 * ks, 16, 1024),
+                        ID_O, (j > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(bar(O_DONE + w));
+          if (j + 1 < nkw[w] && !issue_s(w, j + 1)) {
+            fail = true;
+            break;
+          }
+        }
+        if (fail) break;
+        umma_commit(bar(KV_EMPTY + s));
+      }
+      if (fail) *s_abort = 1;
+      // every MMA has completed before TMEM is released
+      if (issued) {
+        umma_commit(bar(DRAIN));
+        mbar_wait(bar(DRAIN), 0, kSiteFaMma);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax of tile w
+    const int w = (warp - 4) >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;
+    const int nkw = w ? nkB : nkA;
+    const int q0 = w ? q0B : q0A;
+    const int qi = q0 + r;
+    const float scale2 = scale * kLog2e;
+    float m_used = -INFINITY, lsum = 0.f;
+    bool wfail = false;
+    auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
+      if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
+      return !wfail;
+    };
+    for (int j = 0; j < nkw; ++j) {
+      const int s = j % NS;
+      if (!warp_wait(bar(S_FULL + w), j & 1, kSiteFaSoft) || !warp_wait(bar(K_FULL + s), (j / NS) & 1, kSiteFaSoft))
+        break;
+      tc_fence_after();
+      uint32_t sv[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + tl + T_S + 128 * w + 32 * c, sv[c]);
+      tmem_wait_ld();
+      const float4* g4 = reinterpret_cast<const float4*>(sG(s));
+      const int k0 = 128 * j;
+      float mt = -INFINITY;
+      if (k0 + 127 < q0 && k0 + 128 <= L) {  // every key before every query of the tile: all gated
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            const float4 g = g4[(32 * c + e) >> 2];
+            const float x0 = fmaf(__uint_as_float(sv[c][e]), scale2, g.x);
+            const float x1 = fmaf(__uint_as_float(sv[c][e + 1]), scale2, g.y);
+            const float x2 = fmaf(__uint_as_float(sv[c][e + 2]), scale2, g.z);
+            const float x3 = fmaf(__uint_as_float(sv[c][e + 3]), scale2, g.w);
+            sv[c][e] = __float_as_uint(x0);
+            sv[c][e + 1] = __float_as_uint(x1);
+            sv[c][e + 2] = __float_as_uint(x2);
+            sv[c][e + 3] = __float_as_uint(x3);
+            mt = fmaxf(mt, fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)));
+          }
+      } else {
+        const float* g = sG(s);
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int key = k0 + 32 * c + e;
+            const float sc = __uint_as_float(sv[c][e]);
+            float x = -INFINITY;
+            if (key < qi && key < L) x = fmaf(sc, scale2, g[32 * c + e]);
+            else if (key == qi && key < L) x = sc * scale2;
+            sv[c][e] = __float_as_uint(x);
+            mt = fmaxf(mt, x);
+          }
+      }
+      float f = 1.f;
+      bool resc = false;
+      if (mt != -INFINITY && (m_used == -INFINITY || mt > m_used + kRescaleLog2)) {
+        if (j > 0 && m_used != -INFINITY) {  // O and the sum hold earlier tiles: rescale them
+          f = ex2(m_used - mt);
+          lsum *= f;
+          resc = true;
+        }
+        m_used = mt;
+      }
+      // P_w and O_w are free again once PV_w(j - 1) has completed
+      if (j > 0) {
+        if (!warp_wait(bar(O_DONE + w), (j - 1) & 1, kSiteFaSoft)) break;
+        tc_fence_after();
+      }
+      // TMEM loads / stores are warp-collective: the whole warp runs them when any lane
+      // rescales (the others with f = 1)
+      if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // 16 columns at a time: the scores stay in registers
+          uint32_t o[16];
+          tmem_ld16(tmem + tl + T_O + 64 * w + 16 * c, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+          tmem_st16(tmem + tl + T_O + 64 * w + 16 * c, o);
+        }
+      }
+      // while a row has no finite score yet, every score of the tile is -inf and 2^-inf = 0
+      const float mb = m_used == -INFINITY ? 0.f : m_used;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const float p0 = ex2(__uint_as_float(sv[c][2 * q]) - mb), p1 = ex2(__uint_as_float(sv[c][2 * q + 1]) - mb);
+          lsum += p0 + p1;
+          pk[q] = pack2<T>(p0, p1);
+        }
+        tmem_st16(tmem + tl + T_P + 64 * w + 16 * c, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(P_FULL + w));
+    }
+    if (!wfail && nkw > 0 && warp_wait(bar(O_DONE + w), (nkw - 1) & 1, kSiteFaSoft)) {
+      tc_fence_after();
+      uint32_t o[2][32];
+      tmem_ld32(tmem + tl + T_O + 64 * w, o[0]);
+      tmem_ld32(tmem + tl + T_O + 64 * w + 32, o[1]);
+      tmem_wait_ld();
+      const float inv = 1.0f / lsum;
+      if (qi < L) {
+        uint4* op = reinterpret_cast<uint4*>(out + ((long long)bh * L + qi) * 64);
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            uint4 v4;
+            v4.x = pack2<T>(__uint_as_float(o[c][e]) * inv, __uint_as_float(o[c][e + 1]) * inv);
+            v4.y = pack2<T>(__uint_as_float(o[c][e + 2]) * inv, __uint_as_float(o[c][e + 3]) * inv);
+            v4.z = pack2<T>(__uint_as_float(o[c][e + 4]) * inv, __uint_as_float(o[c][e + 5]) * inv);
+            v4.w = pack2<T>(__uint_as_float(o[c][e + 6]) * inv, __uint_as_float(o[c][e + 7]) * inv);
+            op[(32 * c + e) >> 3] = v4;
+          }
+      }
+    }
+    if (wfail) *s_abort = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+template <typename T>
+cudaError_t prefill_fa_t(const void* q, const void* k, const void* v, const float* lg, void* out, int b, int H, int L,
+                         float scale, cudaStream_t s) {
+  const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  const long long bhn = (long long)b * H, npairs = ((long long)L + 255) / 256;
+  if (bhn > 0x7fffffffll || npairs > 65535) return cudaErrorInvalidValue;
+  CUtensorMap mq, mk, mv;
+  if (!make_map_3d(&mq, q, bf16, 64, (uint64_t)L, (uint64_t)bhn, 64, 128, 1) ||
+      !make_map_3d(&mk, k, bf16, 64, (uint64_t)L, (uint64_t)bhn, 64, 128, 1) ||
+      !make_map_3d(&mv, v, bf16, 64, (uint64_t)L, (uint64_t)bhn, 64, 128, 1))
+    return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(sattn_prefill_fa_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kFaSmem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)bhn, (unsigned)npairs);
+  sattn_prefill_fa_kernel<T><<<grid, kFaThreads, kFaSmem, s>>>(mq, mk, mv, lg, (T*)out, L, scale);
+  return cudaGetLastError();
+}
 }  // namespace
 
 bool sattn_decode_supported(int D) { return D == 8 || D == 16 || D == 32 || D == 64 || D == 128 || D == 256; }
@@ -679,6 +1022,10 @@ cudaError_t launch_sattn_prefill(const void* q, const void* k, const void* v, co
                                  int L, int D, float scale, int dtype, int use_tc, cudaStream_t s) {
   if (use_tc) {
     if (!sattn_prefill_tc_supported(D, dtype)) return cudaErrorInvalidValue;
+    if (D == 64) {  // the pipelined kernel; head_dim 128 keeps the single-tile one
+      if (dtype == SSD_BF16) return prefill_fa_t<__nv_bfloat16>(q, k, v, lg, out, b, H, L, scale, s);
+      return prefill_fa_t<__half>(q, k, v, lg, out, b, H, L, scale, s);
+    }
     if (dtype == SSD_BF16) return prefill_tc_t<__nv_bfloat16>(q, k, v, lg, out, b, H, L, D, scale, s);
     return prefill_tc_t<__half>(q, k, v, lg, out, b, H, L, D, scale, s);
   }

@@ -171,3 +171,62 @@ def test_prefill_rejects_bad_arguments():
         kernels.sattn_prefill(q, q, q, torch.zeros(1, 2, 9, device="cuda"))
     with pytest.raises(ValueError):  # the tensor-core kernel takes 16-bit inputs
         kernels.sattn_prefill(q, q, q, torch.zeros(1, 2, 10, device="cuda"), impl="tc")
+
+
+def _prefill_inputs(b, H, L, D, dtype, seed, drop=0.1):
+    gen = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn(b, H, L, D, generator=gen).to(dtype) for _ in range(3))
+    lg = torch.log(torch.sigmoid(torch.randn(b, H, L, generator=gen) + 2.0)) * 2.0
+    lg = torch.where(torch.rand(b, H, L, generator=gen) < drop, torch.full_like(lg, -math.inf), lg)
+    return q, k, v, lg
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("L", [1, 127, 128, 255, 256, 257, 600, 2048])
+def test_prefill_tc_head64_tile_edges(L):
+    """The pipelined head_dim-64 kernel (two 128-query tiles per CTA, 128-key tiles in a
+    TMA ring) at lengths around its tile edges: a missing second query tile, a partial
+    key tile, one token."""
+    from selective_attention_b200 import kernels
+
+    q, k, v, lg = _prefill_inputs(2, 3, L, 64, torch.bfloat16, 40 + L)
+    out = kernels.sattn_prefill(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), impl="tc")
+    ref = sattn_ref.prefill_attention(q.float(), k.float(), v.float(), lg, 64 ** -0.5)
+    assert_bf16_close(out.float().cpu(), ref, f"prefill tc D64 L{L}")
+
+
+@pytest.mark.gpu
+def test_prefill_tc_head64_growing_scores_and_dropped_prefix():
+    """Scores that grow along the keys (the running max rises tile after tile, so the
+    output accumulator is rescaled) and a prefix of 300 dropped keys (rows past it see
+    only -inf scores in their first key tiles)."""
+    from selective_attention_b200 import kernels
+
+    b, H, L, D = 1, 2, 1100, 64
+    q, k, v, lg = _prefill_inputs(b, H, L, D, torch.bfloat16, 5, drop=0.0)
+    ramp = torch.linspace(0.0, 6.0, L).view(1, 1, L, 1)
+    k = (k.float() * 0.2 + ramp).to(torch.bfloat16)
+    q = (q.float() * 0.2 + 1.0).to(torch.bfloat16)
+    lg2 = lg.clone()
+    lg2[..., :300] = -math.inf
+    for lgx in (lg, lg2):
+        out = kernels.sattn_prefill(q.cuda(), k.cuda(), v.cuda(), lgx.cuda(), impl="tc")
+        ref = sattn_ref.prefill_attention(q.float(), k.float(), v.float(), lgx, D ** -0.5)
+        assert_bf16_close(out.float().cpu(), ref, "prefill tc D64 growing scores")
+
+
+@pytest.mark.gpu
+def test_prefill_tc_repeated_runs_are_bit_identical():
+    """The pipelined kernel has no atomics and a fixed MMA order: 20 runs on the same
+    inputs must match the first bit for bit (a missing wait between its warp roles shows
+    up here first)."""
+    from selective_attention_b200 import kernels
+
+    q, k, v, lg = (t.cuda() for t in _prefill_inputs(2, 16, 2048, 64, torch.bfloat16, 9))
+    out0 = kernels.sattn_prefill(q, k, v, lg, impl="tc")
+    differ = 0
+    for _ in range(20):
+        out = kernels.sattn_prefill(q, k, v, lg, impl="tc")
+        differ += int(not torch.equal(out, out0))
+    torch.cuda.synchronize()
+    assert differ == 0, f"{differ} of 20 runs differ from the first"
