@@ -701,7 +701,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * kFaTile + NS * kFaStageBytes);
   enum {
     Q_FULL = 0, K_FULL = 1, V_FULL = K_FULL + NS, KV_EMPTY = V_FULL + NS, S_FULL = KV_EMPTY + NS,
-    P_FULL = S_FULL + 2, O_DONE = P_FULL + 2, DRAIN = O_DONE + 2, NBARS = DRAIN + 1
+    S_FREE = S_FULL + 2, P_FULL = S_FREE + 2, O_DONE = P_FULL + 2, DRAIN = O_DONE + 2, NBARS = DRAIN + 1
   };
   static_assert(NBARS * 8 + 8 <= 256, "barrier area");
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + NBARS);
@@ -727,6 +727,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
     }
     for (int w = 0; w < 2; ++w) {
       mbar_init(bar(S_FULL + w), 1);
+      mbar_init(bar(S_FREE + w), 4);
       mbar_init(bar(P_FULL + w), 4);
       mbar_init(bar(O_DONE + w), 1);
     }
@@ -740,9 +741,16 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
   tc_fence_after();
   const uint32_t tmem = *tslot;
   constexpr uint32_t T_S = 0, T_P = 256, T_O = 384;
+  // Registers: launched with 168 a thread (384 x 168 = 64512, 16128 per SM sub-partition);
+  // warpgroup 0 (loads, MMA) keeps 56 and the two softmax warpgroups take 208 each, which
+  // holds a row's 128 scores without spilling: 128 x 56 + 256 x 208 = 60416 <= 64512, and
+  // per sub-partition (one warp of each warpgroup) 32 x (56 + 2 x 208) = 15104 <= 16128.
+  // (each role branch below starts with its warpgroup's share)
+  static_assert(kFaThreads == 384, "register split assumes three warpgroups");
 
   if (warp == 0) {
     // ------------------------------------------------------------ loads
+    regs_dec<56>();
     if (lane == 0) {
       mbar_expect_tx(bar(Q_FULL), (nkB > 0 ? 2u : 1u) * (uint32_t)kFaTile);
       tma_load_3d(smem_u32(sQ), &tm_q, 0, q0A, bh, bar(Q_FULL));
@@ -787,6 +795,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    regs_dec<56>();
     if (lane == 0) {
       constexpr uint32_t ID_S = idesc_f16(128, 128, BF16, false, false);
       constexpr uint32_t ID_O = idesc_f16(128, 64, BF16, false, true);
@@ -811,7 +820,13 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
       if (!fail && nkB > 0) fail = !issue_s(1, 0);
       for (int j = 0; j < nk && !fail && !*s_abort; ++j) {
         const int s = j % NS;
-        if (!mbar_wait(bar(V_FULL + s), (j / NS) & 1, kSiteFaMma)) {
+        // S_w(j + 1) as soon as softmax w holds S_w(j) in registers: it runs on the tensor
+        // core while that softmax computes the probabilities of step j
+        for (int w = 0; w < 2 && !fail; ++w) {
+          if (j + 1 >= nkw[w]) continue;
+          if (!mbar_wait(bar(S_FREE + w), j & 1, kSiteFaMma) || !issue_s(w, j + 1)) fail = true;
+        }
+        if (fail || !mbar_wait(bar(V_FULL + s), (j / NS) & 1, kSiteFaMma)) {
           fail = true;
           break;
         }
@@ -828,10 +843,6 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
             umma_f16_ts(tmem + T_O + 64 * w, tmem + T_P + 64 * w + 8 * ks, sdesc_sw128(vb + 2048 * ks, 16, 1024),
                         ID_O, (j > 0 || ks > 0) ? 1u : 0u);
           umma_commit(bar(O_DONE + w));
-          if (j + 1 < nkw[w] && !issue_s(w, j + 1)) {
-            fail = true;
-            break;
-          }
         }
         if (fail) break;
         umma_commit(bar(KV_EMPTY + s));
@@ -844,8 +855,11 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
       }
     }
     __syncwarp();
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    regs_dec<56>();  // warps 2-3: no work
+  } else {
     // ------------------------------------------------------------ softmax of tile w
+    regs_inc<208>();
     const int w = (warp - 4) >> 2;
     const int r = (warp & 3) * 32 + lane;
     const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;
@@ -868,9 +882,16 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tmem + tl + T_S + 128 * w + 32 * c, sv[c]);
       tmem_wait_ld();
+      // S_w(j) is in registers: the MMA may overwrite it with S_w(j + 1)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(S_FREE + w));
       const float4* g4 = reinterpret_cast<const float4*>(sG(s));
       const int k0 = 128 * j;
-      float mt = -INFINITY;
+      // eight partial maxima (columns e mod 8), so the reduction is not one long chain
+      float mp[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) mp[q] = -INFINITY;
       if (k0 + 127 < q0 && k0 + 128 <= L) {  // every key before every query of the tile: all gated
 #pragma unroll
         for (int c = 0; c < 4; ++c)
@@ -885,23 +906,32 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
             sv[c][e + 1] = __float_as_uint(x1);
             sv[c][e + 2] = __float_as_uint(x2);
             sv[c][e + 3] = __float_as_uint(x3);
-            mt = fmaxf(mt, fmaxf(fmaxf(x0, x1), fmaxf(x2, x3)));
+            const int q = e & 4;
+            mp[q] = fmaxf(mp[q], x0);
+            mp[q + 1] = fmaxf(mp[q + 1], x1);
+            mp[q + 2] = fmaxf(mp[q + 2], x2);
+            mp[q + 3] = fmaxf(mp[q + 3], x3);
           }
       } else {
+        // diagonal or tail tile: keys past the query or past L drop out, the query's own
+        // key is ungated
         const float* g = sG(s);
+        const int gate_end = min(qi, L);      // keys below this are gated
+        const bool own = qi < L && qi >= k0;  // the query's own key is in this tile
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
             const int key = k0 + 32 * c + e;
             const float sc = __uint_as_float(sv[c][e]);
-            float x = -INFINITY;
-            if (key < qi && key < L) x = fmaf(sc, scale2, g[32 * c + e]);
-            else if (key == qi && key < L) x = sc * scale2;
+            float x = key < gate_end ? fmaf(sc, scale2, g[32 * c + e]) : -INFINITY;
+            if (own && key == qi) x = sc * scale2;
             sv[c][e] = __float_as_uint(x);
-            mt = fmaxf(mt, x);
+            mp[e & 7] = fmaxf(mp[e & 7], x);
           }
       }
+      const float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
       float f = 1.f;
       bool resc = false;
       if (mt != -INFINITY && (m_used == -INFINITY || mt > m_used + kRescaleLog2)) {
@@ -932,17 +962,19 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
       }
       // while a row has no finite score yet, every score of the tile is -inf and 2^-inf = 0
       const float mb = m_used == -INFINITY ? 0.f : m_used;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
           const float p0 = ex2(__uint_as_float(sv[c][2 * q]) - mb), p1 = ex2(__uint_as_float(sv[c][2 * q + 1]) - mb);
-          lsum += p0 + p1;
+          ls[q & 3] += p0 + p1;
           pk[q] = pack2<T>(p0, p1);
         }
         tmem_st16(tmem + tl + T_P + 64 * w + 16 * c, pk);
       }
+      lsum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();

@@ -108,6 +108,18 @@ __device__ __forceinline__ float tanh_approx(float x) {
   return y;
 }
 
+// Per-warpgroup register reallocation: every warp of a warpgroup executes the same one.
+// The counts a kernel's warpgroups settle on must add up to no more than the registers it
+// was launched with (threads x registers per thread), or the increase waits forever.
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
