@@ -678,6 +678,42 @@ cudaError_t prefill_tc_t(const void* q, const void* k, const void* v, const floa
 //                     O_A [384,448) O_B [448,512). Every wait is bounded; a role that
 // gives up records a site code, raises the CTA's abort flag and leaves its loop.
 constexpr int kFaThreads = 384;
+// Every kFaPolyEvery-th pair of probabilities is computed on the FMA pipes instead of the
+// special-function unit (0: none), which the rest share with the 16-bit packing.
+#ifndef SSD_FA_POLY_EVERY
+#define SSD_FA_POLY_EVERY 0
+#endif
+
+// Packed fp32 pairs (Blackwell f32x2 arithmetic on 64-bit register pairs).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  return (uint64_t)__float_as_uint(a) | ((uint64_t)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+// 2^d for a pair, on the FMA pipes: d = n + f with n = round(d) (adding and subtracting
+// 1.5 * 2^23 rounds to an integer, which then sits in the low mantissa bits) and
+// f in [-0.5, 0.5]; 2^f by a cubic least-squares fit on Chebyshev nodes (relative error
+// below 8e-5, far inside the 16-bit rounding of P); n goes into the exponent field. d is
+// clamped at -125 so the exponent stays normal (2^-125 in place of 0 for masked scores).
+__device__ __forceinline__ void exp2_pair_fma(float d0, float d1, float& p0, float& p1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const uint64_t d = f2_pack(fmaxf(d0, -125.f), fmaxf(d1, -125.f));
+  const uint64_t r = f2_add(d, f2_pack(kMagic, kMagic));
+  const uint64_t f = f2_add(d, f2_add(f2_pack(kMagic, kMagic), r ^ 0x8000000080000000ull));  // d - (r - M)
+  uint64_t p = f2_fma(f, f2_pack(0.055171605f, 0.055171605f), f2_pack(0.24261111f, 0.24261111f));
+  p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+  p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
+  p0 = __uint_as_float((uint32_t)p + ((uint32_t)r << 23));
+  p1 = __uint_as_float((uint32_t)(p >> 32) + ((uint32_t)(r >> 32) << 23));
+}
 constexpr int kFaStages = 3;
 constexpr int kFaTile = 128 * 128;                 // 128 rows x 64 16-bit elements
 constexpr int kFaStageBytes = 2 * kFaTile + 1024;  // K | V | 128 log-gates (1 KB keeps the alignment)
@@ -942,7 +978,27 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
         }
         m_used = mt;
       }
-      // P_w and O_w are free again once PV_w(j - 1) has completed
+      // the probabilities first, into registers: computing them overlaps PV_w(j - 1),
+      // which must complete before P_w is rewritten and before O_w is rescaled
+      // (while a row has no finite score yet, every score of the tile is -inf and 2^-inf = 0)
+      const float mb = m_used == -INFINITY ? 0.f : m_used;
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums
+      uint32_t pk[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          float p0, p1;
+          if (SSD_FA_POLY_EVERY > 0 && q % (SSD_FA_POLY_EVERY > 0 ? SSD_FA_POLY_EVERY : 1) == 0) {
+            exp2_pair_fma(__uint_as_float(sv[c][2 * q]) - mb, __uint_as_float(sv[c][2 * q + 1]) - mb, p0, p1);
+          } else {
+            p0 = ex2(__uint_as_float(sv[c][2 * q]) - mb);
+            p1 = ex2(__uint_as_float(sv[c][2 * q + 1]) - mb);
+          }
+          ls[q & 3] += p0 + p1;
+          pk[c][q] = pack2<T>(p0, p1);
+        }
+      lsum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       if (j > 0) {
         if (!warp_wait(bar(O_DONE + w), (j - 1) & 1, kSiteFaSoft)) break;
         tc_fence_after();
@@ -951,7 +1007,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
       // rescales (the others with f = 1)
       if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {  // 16 columns at a time: the scores stay in registers
+        for (int c = 0; c < 4; ++c) {  // 16 columns at a time
           uint32_t o[16];
           tmem_ld16(tmem + tl + T_O + 64 * w + 16 * c, o);
           tmem_wait_ld();
@@ -960,21 +1016,8 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
           tmem_st16(tmem + tl + T_O + 64 * w + 16 * c, o);
         }
       }
-      // while a row has no finite score yet, every score of the tile is -inf and 2^-inf = 0
-      const float mb = m_used == -INFINITY ? 0.f : m_used;
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};  // four partial sums
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          const float p0 = ex2(__uint_as_float(sv[c][2 * q]) - mb), p1 = ex2(__uint_as_float(sv[c][2 * q + 1]) - mb);
-          ls[q & 3] += p0 + p1;
-          pk[q] = pack2<T>(p0, p1);
-        }
-        tmem_st16(tmem + tl + T_P + 64 * w + 16 * c, pk);
-      }
-      lsum += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      for (int c = 0; c < 4; ++c) tmem_st16(tmem + tl + T_P + 64 * w + 16 * c, pk[c]);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();

@@ -61,6 +61,33 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
   return false;
 }
 
+// Test of the phase with the given parity that may suspend the thread (without issuing
+// instructions) for up to `hint_ns` while the phase is incomplete.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait for waits that are often long: the waiting thread is suspended instead of
+// polling, so it takes no issue slots from the warps that share its sub-partition.
+// Bounded the same way (1 s of %globaltimer).
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, unsigned int site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1; it < kWaitMaxPolls; ++it) {
+    if (mbar_try_wait(bar, parity, 20000u)) return true;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+  }
+  record_error(site);
+  return false;
+}
+
 // ---------------------------------------------------------------- TMA
 // Tiled tensor loads into this CTA's shared memory, completing on `bar`.
 // Innermost coordinate x must be a multiple of 16 bytes of elements (every caller
