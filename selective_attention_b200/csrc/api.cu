@@ -173,7 +173,8 @@ int ssd_b200_device_error(void* stream) {
   const unsigned int b = fetch_error_tc(s);
   const unsigned int c = fetch_error_ssu(s);
   const unsigned int d = fetch_error_sattn(s);
-  return (int)(a ? a : (b ? b : (c ? c : d)));
+  const unsigned int e = fetch_error_bwd_tc(s);
+  return (int)(a ? a : (b ? b : (c ? c : (d ? d : e))));
 }
 
 int ssd_scan_uses_tensor_cores(const ssd_params* p) {

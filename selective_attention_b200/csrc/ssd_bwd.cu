@@ -984,10 +984,14 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
       a.B, a.C, a.CB, c.cm, G, N, a.x_dtype);
   if ((e = cudaGetLastError())) return e;
   if (a.ev[2]) cudaEventRecord(a.ev[2], c.stream);
-  bwd_state_grad_kernel<<<gkh, 256, kSmemStateGrad, c.stream>>>(
-      a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, a.accS, a.B_grad, a.C_grad, a.gC, c.cm, H, G, P, N,
-      a.x_dtype, a.y_dtype);
-  if ((e = cudaGetLastError())) return e;
+  if (bwd_state_grad_tc_supported(a.x_dtype, a.y_dtype, P, N, cs)) {
+    if ((e = launch_bwd_state_grad_tc(c, a))) return e;
+  } else {
+    bwd_state_grad_kernel<<<gkh, 256, kSmemStateGrad, c.stream>>>(
+        a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, a.accS, a.B_grad, a.C_grad, a.gC, c.cm, H, G, P, N,
+        a.x_dtype, a.y_dtype);
+    if ((e = cudaGetLastError())) return e;
+  }
   if (a.ev[3]) cudaEventRecord(a.ev[3], c.stream);
   bwd_intra_kernel<<<gkh, kIT, kSmemIntra, c.stream>>>(
       a.u, a.y_grad, a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, a.dl_part, nsl, a.CBg,

@@ -1,0 +1,319 @@
+// ssd_bwd_tc.cu - the state-side products of the SSD backward on tcgen05 tensor cores
+// (16-bit u / B / C, headdim 64, dstate 128, chunk 256).
+//
+// Per (chunk, head), with scale_l = exp(min(cum_last - cum_l, 0)), w_l = scale_l dt_l and
+// e_l = exp(cum_l) (all zero at or past the row's length), the same products as
+// bwd_state_grad_kernel in ssd_bwd.cu (backward_kernel.py:255-262, :402-415, :522-538):
+//   accS[l,p]     = scale_l sum_n B[l,n] hg[p,n]
+//   B_grad[l,:]  += w_l     sum_p u[l,p] hg[p,:]
+//   C_grad[l,:]  += e_l     sum_p y_grad[l,p] prev[p,:]
+//   gC[l]         = sum_n (that C_grad row) C[l,n]
+// The chunk's hg and prev (fp32 state gradients / states) and, when it is fp32, y_grad are
+// rounded to the input's 16-bit type in shared memory; u and B arrive by TMA. Products
+// accumulate in fp32 in TMEM (accS 64 columns, the B_grad / C_grad row block 128 columns,
+// one after the other), the row factors are applied in the epilogue, where thread = row
+// l = TMEM lane, and B_grad / C_grad are summed over the group's heads with 16-byte fp32
+// atomics as in the CUDA-core kernel. One CTA of 4 warps per (chunk, head), two halves of
+// 128 rows; 99 KB of shared memory and 256 TMEM columns, two CTAs per SM. Every mbarrier
+// wait is bounded; a CTA that gives up records a site code and skips its remaining work.
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+#include "tmap.cuh"
+
+namespace ssdb200 {
+
+using namespace sm100;
+
+namespace {
+
+constexpr unsigned int kSiteBwdTcTma = 0x121, kSiteBwdTcMma = 0x122;
+constexpr int kBgThreads = 128;
+// hg16 [2 n-blocks][64 p][128 B] | prev16 (same) | B [2 n-blocks][128 l][128 B] | u [128 l][128 B]
+// | y_grad [128 l][128 B] | row factors [3][256] | barriers, TMEM slot
+constexpr int kBgOffHg = 0, kBgOffPv = 16384, kBgOffB = 32768, kBgOffU = 65536, kBgOffY = 81920,
+              kBgOffF = 98304, kBgOffBar = kBgOffF + 3 * 1024;
+constexpr size_t kBgSmem = 1024 + kBgOffBar + 64;
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2f(float a, float b) {
+  return pack2<typename std::conditional<BF16, __nv_bfloat16, __half>::type>(a, b);
+}
+
+// Rounds a (64 x 128) fp32 state block [p][n] (n contiguous) to 16 bits into the 128-byte
+// swizzled layout [n / 64][p][n % 64]: K-major over n for one MMA and MN-major over n for
+// the other.
+template <bool BF16>
+__device__ __forceinline__ void stage_state16(uint8_t* dst, const float* __restrict__ src) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int q = threadIdx.x + kBgThreads * i;  // 1024 chunks of 8 elements
+    const int p = q >> 4, n0 = (q & 15) * 8;
+    const float4 a = __ldg(reinterpret_cast<const float4*>(src + p * 128 + n0));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(src + p * 128 + n0 + 4));
+    const uint4 v = make_uint4(pack2f<BF16>(a.x, a.y), pack2f<BF16>(a.z, a.w), pack2f<BF16>(b.x, b.y),
+                               pack2f<BF16>(b.z, b.w));
+    *reinterpret_cast<uint4*>(dst + (n0 >> 6) * 8192 + sw128_off((uint32_t)p, (uint32_t)((n0 & 63) >> 3))) = v;
+  }
+}
+
+template <bool BF16, typename YT>
+__global__ void __launch_bounds__(kBgThreads, 2) bwd_state_grad_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_u,
+    const __grid_constant__ CUtensorMap tm_y, const void* __restrict__ Cm, const YT* __restrict__ yg,
+    const float* __restrict__ dt, const float* __restrict__ cum, const float* __restrict__ prev,
+    const float* __restrict__ hg, float* __restrict__ accS_out, float* __restrict__ Bgrad,
+    float* __restrict__ Cgrad, float* __restrict__ gC_out, ChunkMap cm, int H, int G) {
+  using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr bool kY16 = sizeof(YT) == 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sHg = sm + kBgOffHg;
+  uint8_t* sPv = sm + kBgOffPv;
+  uint8_t* sB = sm + kBgOffB;
+  uint8_t* sU = sm + kBgOffU;
+  uint8_t* sY = sm + kBgOffY;
+  float* sS = reinterpret_cast<float*>(sm + kBgOffF);
+  float* wS = sS + 256;
+  float* eS = wS + 256;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kBgOffBar);  // TMA, MMA
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  const uint32_t bar_tma = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
+
+  const int h = blockIdx.x, k = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5;
+  const long long kh = (long long)k * H + h;
+  const int vl = ci.vlim;
+  if (tid == 0) {
+    prefetch_tmap(&tm_b);
+    prefetch_tmap(&tm_u);
+    if (kY16) prefetch_tmap(&tm_y);
+    mbar_init(bar_tma, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
+  stage_state16<BF16>(sHg, hg + kh * 8192);
+  stage_state16<BF16>(sPv, prev + kh * 8192);
+  {
+    const float clast = cum[kh * 256 + 255];
+    for (int i = tid; i < 256; i += kBgThreads) {
+      const float c = cum[kh * 256 + i];
+      const float sc = i < vl ? __expf(fminf(clast - c, 0.f)) : 0.f;
+      sS[i] = sc;
+      wS[i] = sc * dt[kh * 256 + i];
+      eS[i] = i < vl ? __expf(c) : 0.f;
+    }
+  }
+  fence_proxy_async_smem();  // the 16-bit states are operands of the MMAs
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tl = (uint32_t)(warp * 32) << 16;
+  constexpr uint32_t T_ACC = 0, T_G = 128;
+  constexpr uint32_t ID_S = idesc_f16(128, 64, BF16, false, false);   // accS: K = n
+  constexpr uint32_t ID_G = idesc_f16(128, 128, BF16, false, true);   // B_grad / C_grad: K = p, N = n MN-major
+  int uses_tma = 0, uses_mma = 0;
+  bool ok = true;
+  const int r = tid;  // row of the half = TMEM lane
+
+  for (int m = 0; m < 2 && ok; ++m) {
+    const int l0 = 128 * m;
+    if (l0 >= ci.lim) break;
+    const int t0 = (int)(ci.tok0 + l0);
+    if (tid == 0) {
+      mbar_expect_tx(bar_tma, 32768u + 16384u + (kY16 ? 16384u : 0u));
+      tma_load_3d(smem_u32(sB), &tm_b, 0, g, t0, bar_tma);
+      tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, g, t0, bar_tma);
+      tma_load_3d(smem_u32(sU), &tm_u, 0, h, t0, bar_tma);
+      if (kY16) tma_load_3d(smem_u32(sY), &tm_y, 0, h, t0, bar_tma);
+    }
+    if (!kY16) {
+      // y_grad rows (fp32) rounded to 16 bits, K-major over p; rows past the length are 0
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = tid + kBgThreads * i;  // 1024 chunks of 8 elements
+        const int row = q >> 3, c8 = q & 7, l = l0 + row;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (l < vl) {
+          const float* s = reinterpret_cast<const float*>(yg) + ((ci.tok0 + l) * H + h) * 64 + c8 * 8;
+          const float4 a = __ldg(reinterpret_cast<const float4*>(s));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(s + 4));
+          v = make_uint4(pack2f<BF16>(a.x, a.y), pack2f<BF16>(a.z, a.w), pack2f<BF16>(b.x, b.y),
+                         pack2f<BF16>(b.z, b.w));
+        }
+        *reinterpret_cast<uint4*>(sY + sw128_off((uint32_t)row, (uint32_t)c8)) = v;
+      }
+    }
+    const bool landed = mbar_wait(bar_tma, uses_tma & 1, kSiteBwdTcTma);
+    ++uses_tma;
+    if (landed && vl - l0 < 128) {
+      // rows at or past the length: zeros in every operand (their row factors are 0,
+      // but the data there need not be finite)
+      const int z0 = max(vl - l0, 0);
+      for (int q = tid; q < (128 - z0) * 8; q += kBgThreads) {
+        const int row = z0 + (q >> 3);
+        const uint32_t off = (uint32_t)row * 128u + (uint32_t)(q & 7) * 16u;
+        const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(sB + off) = zero;
+        *reinterpret_cast<uint4*>(sB + 16384 + off) = zero;
+        *reinterpret_cast<uint4*>(sU + off) = zero;
+        *reinterpret_cast<uint4*>(sY + off) = zero;
+      }
+    }
+    fence_proxy_async_smem();
+    ok = __syncthreads_and(landed) != 0;
+    if (!ok) break;
+    if (tid == 0) {
+      tc_fence_after();
+      // accS = B hg^T: A = B rows (K = n in two 64-blocks), B = hg16 (N = p, K = n)
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
+        umma_f16(tmem + T_ACC, sdesc_sw128(smem_u32(sB) + hf * 16384 + kk, 16, 1024),
+                 sdesc_sw128(smem_u32(sHg) + hf * 8192 + kk, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
+      }
+      // B_grad rows = u hg: A = u rows (K = p), B = hg16 as N = n MN-major (64-blocks 8 KB apart)
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_f16(tmem + T_G, sdesc_sw128(smem_u32(sU) + ks * 32, 16, 1024),
+                 sdesc_sw128(smem_u32(sHg) + ks * 2048, 8192, 1024), ID_G, ks > 0 ? 1u : 0u);
+      umma_commit(bar_mma);
+    }
+    ok = __syncthreads_and(mbar_wait(bar_mma, uses_mma & 1, kSiteBwdTcMma)) != 0;
+    ++uses_mma;
+    tc_fence_after();
+    if (!ok) break;
+    const int l = l0 + r;
+    {
+      // accS row l (64 columns) times scale_l
+      float* o = accS_out + (kh * 256 + l) * 64;
+      const float sc = sS[l];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + tl + T_ACC + 32 * c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+          *reinterpret_cast<float4*>(o + 32 * c + e) =
+              make_float4(__uint_as_float(v[e]) * sc, __uint_as_float(v[e + 1]) * sc, __uint_as_float(v[e + 2]) * sc,
+                          __uint_as_float(v[e + 3]) * sc);
+      }
+      // B_grad row l (128 columns) times w_l, summed over the group's heads
+      const float wl = wS[l];
+      float* bgr = Bgrad + ((ci.tok0 + l) * G + g) * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + tl + T_G + 32 * c, v);
+        tmem_wait_ld();
+        if (l < vl) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            atomicAdd(reinterpret_cast<float4*>(bgr + 32 * c + e),
+                      make_float4(__uint_as_float(v[e]) * wl, __uint_as_float(v[e + 1]) * wl,
+                                  __uint_as_float(v[e + 2]) * wl, __uint_as_float(v[e + 3]) * wl));
+        }
+      }
+    }
+    // C_grad rows = y_grad prev into the same TMEM columns, once every thread has read them
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_f16(tmem + T_G, sdesc_sw128(smem_u32(sY) + ks * 32, 16, 1024),
+                 sdesc_sw128(smem_u32(sPv) + ks * 2048, 8192, 1024), ID_G, ks > 0 ? 1u : 0u);
+      umma_commit(bar_mma);
+    }
+    ok = __syncthreads_and(mbar_wait(bar_mma, uses_mma & 1, kSiteBwdTcMma)) != 0;
+    ++uses_mma;
+    tc_fence_after();
+    if (!ok) break;
+    {
+      const float el = eS[l];
+      float* cgr = Cgrad + ((ci.tok0 + l) * G + g) * 128;
+      const uint16_t* crow = reinterpret_cast<const uint16_t*>(Cm) + ((ci.tok0 + l) * G + g) * 128;
+      float gsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + tl + T_G + 32 * c, v);
+        tmem_wait_ld();
+        if (l < vl) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            const uint4 c8 = __ldg(reinterpret_cast<const uint4*>(crow + 32 * c + e));
+            const uint32_t cw[4] = {c8.x, c8.y, c8.z, c8.w};
+            float x[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) x[q] = __uint_as_float(v[e + q]) * el;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 cf = unpack2<T16>(cw[q]);
+              gsum = fmaf(x[2 * q], cf.x, fmaf(x[2 * q + 1], cf.y, gsum));
+            }
+            atomicAdd(reinterpret_cast<float4*>(cgr + 32 * c + e), make_float4(x[0], x[1], x[2], x[3]));
+            atomicAdd(reinterpret_cast<float4*>(cgr + 32 * c + e + 4), make_float4(x[4], x[5], x[6], x[7]));
+          }
+        }
+      }
+      gC_out[kh * 256 + l] = l < vl ? gsum : 0.f;
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  if (!ok && tid == 0) {
+    // let an MMA still in flight land before TMEM is released (bounded)
+    if (uses_mma > 0) mbar_wait(bar_mma, (uses_mma - 1) & 1, kSiteBwdTcMma);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+template <bool BF16, typename YT>
+cudaError_t launch_typed(const LaunchCtx& c, const BwdArgs& a) {
+  CUtensorMap mb, mu, my;
+  if (!make_map_3d(&mb, a.B, BF16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&mu, a.u, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&my, sizeof(YT) == 2 ? a.y_grad : a.u, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128))
+    return cudaErrorInvalidValue;
+  auto kern = bwd_state_grad_tc_kernel<BF16, YT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBgSmem);
+  if (e != cudaSuccess) return e;
+  kern<<<dim3((unsigned)c.H, (unsigned)c.nchunks_max), kBgThreads, kBgSmem, c.stream>>>(
+      mb, mu, my, a.C, reinterpret_cast<const YT*>(a.y_grad), a.dt, a.cum, a.states, a.hg, a.accS, a.B_grad,
+      a.C_grad, a.gC, c.cm, c.H, c.G);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool bwd_state_grad_tc_supported(int x_dtype, int y_dtype, int P, int N, int cs) {
+  const bool x16 = x_dtype == SSD_BF16 || x_dtype == SSD_F16;
+  return x16 && (y_dtype == SSD_F32 || y_dtype == x_dtype) && P == 64 && N == 128 && cs == 256;
+}
+
+cudaError_t launch_bwd_state_grad_tc(const LaunchCtx& c, const BwdArgs& a) {
+  if (c.nchunks_max > 65535 || c.H > 65535) return cudaErrorInvalidValue;
+  if (a.x_dtype == SSD_BF16) {
+    if (a.y_dtype == SSD_F32) return launch_typed<true, float>(c, a);
+    return launch_typed<true, __nv_bfloat16>(c, a);
+  }
+  if (a.y_dtype == SSD_F32) return launch_typed<false, float>(c, a);
+  return launch_typed<false, __half>(c, a);
+}
+
+SSDB200_DEFINE_ERROR_FETCH(fetch_error_bwd_tc)
+
+}  // namespace ssdb200

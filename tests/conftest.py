@@ -52,5 +52,19 @@ def assert_bf16_close(actual, expected, what=""):
                            f"(max abs err {err.max().item():.3e})")
 
 
+def assert_bf16_operand_close(actual, expected, what=""):
+    """An fp32 result of a problem whose inputs are 16-bit, computed with 16-bit
+    tensor-core operands (the backward's state-side products): within rel 1e-2 of each
+    element plus 5e-3 of the tensor's largest magnitude (the north star's bf16 rel 1e-2,
+    with an absolute term scaled to the tensor instead of a fixed 2e-2)."""
+    a, e = actual.double().cpu(), expected.double().cpu()
+    scale = e.abs().max().item()
+    tol = 1e-2 * e.abs() + 5e-3 * scale + 1e-12
+    err = (a - e).abs()
+    bad = err > tol
+    assert not bad.any(), (f"{what}: {int(bad.sum())} of {e.numel()} elements outside rel 1e-2 + 5e-3 max "
+                           f"(max abs err {err.max().item():.3e}, max |ref| {scale:.3e})")
+
+
 def assert_close_for(dtype):
     return assert_fp32_close if dtype == torch.float32 else assert_bf16_close
