@@ -64,6 +64,7 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a);
 // ssd_bwd_tc.cu (state-side products on tcgen05: 16-bit u / B / C, P 64, N 128, chunk 256)
 bool bwd_state_grad_tc_supported(int x_dtype, int y_dtype, int P, int N, int cs);
 cudaError_t launch_bwd_state_grad_tc(const LaunchCtx& c, const BwdArgs& a);
+cudaError_t launch_bwd_chunk_states_tc(const LaunchCtx& c, const BwdArgs& a);  // same shapes
 unsigned int fetch_error_bwd_tc(cudaStream_t s);
 
 // sattn.cu (selective-attention decode step; head_dim 8..256, a power of two)

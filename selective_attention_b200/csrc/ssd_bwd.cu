@@ -971,9 +971,14 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
   if ((e = launch_chunk_cumsum(c, a.dt_dtype, a.A, a.delta_raw, a.delta_bias, a.dt, a.cum))) return e;
   const dim3 gkh((unsigned)H, (unsigned)nk);
   // grid x = head: the heads of one chunk run side by side and share its B, C, CB in L2
-  bwd_chunk_states_kernel<<<dim3((unsigned)H, (unsigned)nk, 2u), 256, kSmemStates, c.stream>>>(
-      a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, c.cm, H, G, P, N, a.x_dtype, a.y_dtype);
-  if ((e = cudaGetLastError())) return e;
+  const bool tc = bwd_state_grad_tc_supported(a.x_dtype, a.y_dtype, P, N, cs);
+  if (tc) {
+    if ((e = launch_bwd_chunk_states_tc(c, a))) return e;
+  } else {
+    bwd_chunk_states_kernel<<<dim3((unsigned)H, (unsigned)nk, 2u), 256, kSmemStates, c.stream>>>(
+        a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, c.cm, H, G, P, N, a.x_dtype, a.y_dtype);
+    if ((e = cudaGetLastError())) return e;
+  }
   if (a.ev[1]) cudaEventRecord(a.ev[1], c.stream);
   const int nsl = (int)bwd_dl_slices(P, N);  // per-warp partials of the decay_last gradient
   bwd_state_pass_kernel<<<dim3((unsigned)(nsl / 8), (unsigned)H, (unsigned)c.nrows), 256, 0, c.stream>>>(
@@ -984,7 +989,7 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
       a.B, a.C, a.CB, c.cm, G, N, a.x_dtype);
   if ((e = cudaGetLastError())) return e;
   if (a.ev[2]) cudaEventRecord(a.ev[2], c.stream);
-  if (bwd_state_grad_tc_supported(a.x_dtype, a.y_dtype, P, N, cs)) {
+  if (tc) {
     if ((e = launch_bwd_state_grad_tc(c, a))) return e;
   } else {
     bwd_state_grad_kernel<<<gkh, 256, kSmemStateGrad, c.stream>>>(

@@ -39,6 +39,18 @@ constexpr int kBgOffHg = 0, kBgOffPv = 16384, kBgOffB = 32768, kBgOffU = 65536, 
               kBgOffF = 98304, kBgOffBar = kBgOffF + 3 * 1024;
 constexpr size_t kBgSmem = 1024 + kBgOffBar + 64;
 
+// 8 elements of a 16-byte chunk times w (fp32 products, one rounding to 16 bits).
+template <typename T16>
+__device__ __forceinline__ uint4 scaled8(uint4 a, float w) {
+  float2 f;
+  uint4 v;
+  f = unpack2<T16>(a.x); v.x = pack2<T16>(f.x * w, f.y * w);
+  f = unpack2<T16>(a.y); v.y = pack2<T16>(f.x * w, f.y * w);
+  f = unpack2<T16>(a.z); v.z = pack2<T16>(f.x * w, f.y * w);
+  f = unpack2<T16>(a.w); v.w = pack2<T16>(f.x * w, f.y * w);
+  return v;
+}
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2f(float a, float b) {
   return pack2<typename std::conditional<BF16, __nv_bfloat16, __half>::type>(a, b);
@@ -297,6 +309,158 @@ cudaError_t launch_typed(const LaunchCtx& c, const BwdArgs& a) {
   return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------
+// Chunk states and intra-chunk state gradients (ssd_bwd.cu bwd_chunk_states_kernel's
+// two products) on tcgen05, per (chunk, head, product):
+//   product 0: S[p,n]  = sum_l u[l,p] w_l B[l,n],         w_l = exp(min(cum_last - cum_l, 0)) dt_l
+//   product 1: HG[p,n] = sum_l y_grad[l,p] e_l C[l,n],    e_l = exp(cum_l)
+// (backward.py:487, backward_kernel.py:23-93), both zero past the row's length. As in the
+// forward's chunk_state: two 128-token phases, the token rows of u (TMA) or y_grad (TMA, or
+// fp32 rounded here) scaled by their weight in shared memory, then M = 128 (dstate) x
+// N = 64 (headdim) x K = 128 MMAs with both operands MN-major; thread = n = TMEM lane
+// writes S / HG as [p][n] fp32.
+// ---------------------------------------------------------------------------
+constexpr int kCsThreads = 128;
+constexpr size_t kCsSmem = 1024 + 32768 + 16384 + 1024 + 64;
+
+template <bool BF16, typename YT>
+__global__ void __launch_bounds__(kCsThreads) bwd_chunk_states_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_b,
+    const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_c, const YT* __restrict__ yg,
+    const float* __restrict__ dt, const float* __restrict__ cum, float* __restrict__ states, float* __restrict__ hg,
+    ChunkMap cm, int H, int G) {
+  using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr bool kY16 = sizeof(YT) == 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sB = sm;           // 2 x (128 tokens x 128 B): dstate halves
+  uint8_t* sX = sm + 32768;   // 128 tokens x 128 B
+  float* sW = reinterpret_cast<float*>(sm + 49152);  // [256] token weights
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + 49152 + 1024);  // TMA, MMA
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  const uint32_t bar_tma = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
+  const int h = blockIdx.x, k = blockIdx.y, which = blockIdx.z;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long kh = (long long)k * H + h;
+  const int vl = ci.vlim;
+  const bool from_y = which == 1;
+  if (tid == 0) {
+    prefetch_tmap(from_y ? &tm_c : &tm_b);
+    if (!from_y) prefetch_tmap(&tm_u);
+    else if (kY16) prefetch_tmap(&tm_y);
+    mbar_init(bar_tma, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 64);
+  {
+    const float clast = cum[kh * 256 + 255];
+    for (int i = tid; i < 256; i += kCsThreads) {
+      const float c = cum[kh * 256 + i];
+      sW[i] = i < vl ? (from_y ? __expf(c) : __expf(fminf(clast - c, 0.f)) * dt[kh * 256 + i]) : 0.f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  constexpr uint32_t ID = idesc_f16(128, 64, BF16, /*a_mn=*/true, /*b_mn=*/true);
+  bool ok = true;
+  int uses = 0;
+  for (int ph = 0; ph < 2 && ok; ++ph) {
+    if (128 * ph >= vl) break;  // weights past the length are 0: nothing to add
+    const int t0 = (int)(ci.tok0 + 128 * ph);
+    if (tid == 0) {
+      const CUtensorMap* mbc = from_y ? &tm_c : &tm_b;
+      const bool x_tma = !from_y || kY16;
+      mbar_expect_tx(bar_tma, 32768u + (x_tma ? 16384u : 0u));
+      tma_load_3d(smem_u32(sB), mbc, 0, g, t0, bar_tma);
+      tma_load_3d(smem_u32(sB + 16384), mbc, 64, g, t0, bar_tma);
+      if (x_tma) tma_load_3d(smem_u32(sX), from_y ? &tm_y : &tm_u, 0, h, t0, bar_tma);
+    }
+    if (from_y && !kY16) {
+      // fp32 y_grad rows times e_l, rounded to 16 bits into the swizzled tile
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = tid + kCsThreads * i, row = q >> 3, c8 = q & 7, l = 128 * ph + row;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        const float w = sW[l];
+        if (w != 0.f) {
+          const float* src = reinterpret_cast<const float*>(yg) + ((ci.tok0 + l) * H + h) * 64 + c8 * 8;
+          const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
+          v = make_uint4(pack2<T16>(a.x * w, a.y * w), pack2<T16>(a.z * w, a.w * w), pack2<T16>(b.x * w, b.y * w),
+                         pack2<T16>(b.z * w, b.w * w));
+        }
+        *reinterpret_cast<uint4*>(sX + sw128_off((uint32_t)row, (uint32_t)c8)) = v;
+      }
+    }
+    const bool landed = mbar_wait(bar_tma, uses & 1, kSiteBwdTcTma);
+    if (landed && (!from_y || kY16)) {
+      // token rows scaled in place by their weight (rows with weight 0 become exact zeros)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = tid + kCsThreads * i;
+        uint4* pch = reinterpret_cast<uint4*>(sX + q * 16);
+        const float w = sW[128 * ph + (q >> 3)];
+        *pch = (w == 0.f) ? make_uint4(0u, 0u, 0u, 0u) : scaled8<T16>(*pch, w);
+      }
+    }
+    fence_proxy_async_smem();
+    ok = __syncthreads_and(landed) != 0;
+    if (!ok) break;
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_f16(tmem, sdesc_sw128(smem_u32(sB) + ks * 2048, 16384, 1024), sdesc_sw128(smem_u32(sX) + ks * 2048, 16, 1024),
+                 ID, (ph > 0 || ks > 0) ? 1u : 0u);
+      umma_commit(bar_mma);
+    }
+    // the next phase reuses both tiles, the epilogue reads the accumulator
+    ok = __syncthreads_and(mbar_wait(bar_mma, uses & 1, kSiteBwdTcMma)) != 0;
+    ++uses;
+    tc_fence_after();
+  }
+  if (ok) {
+    const int n = warp * 32 + lane;
+    float* out = (from_y ? hg : states) + kh * 8192;
+    if (uses == 0) {  // no valid token: the state is zero
+      for (int p = 0; p < 64; ++p) out[p * 128 + n] = 0.f;
+    } else {
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + half * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) out[(half * 32 + j) * 128 + n] = __uint_as_float(v[j]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 64);
+}
+
+template <bool BF16, typename YT>
+cudaError_t launch_states_typed(const LaunchCtx& c, const BwdArgs& a) {
+  CUtensorMap mu, mb, my, mc;
+  if (!make_map_3d(&mu, a.u, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&mb, a.B, BF16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&my, sizeof(YT) == 2 ? a.y_grad : a.u, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&mc, a.C, BF16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128))
+    return cudaErrorInvalidValue;
+  auto kern = bwd_chunk_states_tc_kernel<BF16, YT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCsSmem);
+  if (e != cudaSuccess) return e;
+  kern<<<dim3((unsigned)c.H, (unsigned)c.nchunks_max, 2u), kCsThreads, kCsSmem, c.stream>>>(
+      mu, mb, my, mc, reinterpret_cast<const YT*>(a.y_grad), a.dt, a.cum, a.states, a.hg, c.cm, c.H, c.G);
+  return cudaGetLastError();
+}
 }  // namespace
 
 bool bwd_state_grad_tc_supported(int x_dtype, int y_dtype, int P, int N, int cs) {
@@ -312,6 +476,16 @@ cudaError_t launch_bwd_state_grad_tc(const LaunchCtx& c, const BwdArgs& a) {
   }
   if (a.y_dtype == SSD_F32) return launch_typed<false, float>(c, a);
   return launch_typed<false, __half>(c, a);
+}
+
+cudaError_t launch_bwd_chunk_states_tc(const LaunchCtx& c, const BwdArgs& a) {
+  if (c.nchunks_max > 65535 || c.H > 65535) return cudaErrorInvalidValue;
+  if (a.x_dtype == SSD_BF16) {
+    if (a.y_dtype == SSD_F32) return launch_states_typed<true, float>(c, a);
+    return launch_states_typed<true, __nv_bfloat16>(c, a);
+  }
+  if (a.y_dtype == SSD_F32) return launch_states_typed<false, float>(c, a);
+  return launch_states_typed<false, __half>(c, a);
 }
 
 SSDB200_DEFINE_ERROR_FETCH(fetch_error_bwd_tc)
