@@ -299,6 +299,7 @@ size_t carve_bwd(const Geometry& g, uint8_t* base, BwdArgs* a, ChunkEntry** tabl
   w.dl_part = take(nk * H * bwd_dl_slices(g.P, g.N) * 4);
   w.A_part = take(nk * H * 4);
   w.bias_part = take(nk * H * 4);
+  w.rows4 = take(4 * nk * H * cs * 4);
   ChunkEntry* t = nullptr;
   int2* r = nullptr;
   int* c = nullptr;

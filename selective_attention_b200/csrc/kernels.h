@@ -56,6 +56,7 @@ struct BwdArgs {
   float* h_init_grad;
   // workspace
   float *dt, *cum, *states, *hg, *CB, *CBg, *accS, *gC, *dl_part, *A_part, *bias_part;
+  float* rows4;  // (4, chunks, H, cs): ddt, gB, row and column decay sums of the tensor-core intra kernel
   cudaEvent_t ev[6];
 };
 bool bwd_supported(int P, int N, int cs);
@@ -65,6 +66,7 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a);
 bool bwd_state_grad_tc_supported(int x_dtype, int y_dtype, int P, int N, int cs);
 cudaError_t launch_bwd_state_grad_tc(const LaunchCtx& c, const BwdArgs& a);
 cudaError_t launch_bwd_chunk_states_tc(const LaunchCtx& c, const BwdArgs& a);  // same shapes
+cudaError_t launch_bwd_intra_tc(const LaunchCtx& c, const BwdArgs& a);         // same shapes; fills rows4
 unsigned int fetch_error_bwd_tc(cudaStream_t s);
 
 // sattn.cu (selective-attention decode step; head_dim 8..256, a power of two)

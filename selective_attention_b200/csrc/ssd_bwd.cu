@@ -553,6 +553,61 @@ __global__ void __launch_bounds__(256, 2) bwd_state_grad_kernel(
   }
 }
 
+// dt backward per (chunk, head), one token t per thread, NT threads >= cs
+// (backward_kernel.py:984-1039):
+//   total = decay_intra + excl_cumsum(gB shifted) + rev_cumsum(gC) + dlast
+//   delta_raw_grad = (total A + ddt), 0 where dt was clamped, * sigmoid(pre) (softplus)
+// and the A / bias partials of the chunk. cols, rows, gBs, ddts: [cs] in shared or global
+// memory; revc [kCSmax] and tmp [16] in shared memory.
+template <int NT>
+__device__ __forceinline__ void dt_backward(const float* cols, const float* rows, const float* gBs, const float* ddts,
+                                            float* revc, float* tmp, const float* __restrict__ gC,
+                                            const float* __restrict__ dl_part, int nsl, const void* __restrict__ delta_raw,
+                                            const float* __restrict__ A, const float* __restrict__ delta_bias,
+                                            void* __restrict__ draw_grad, float* __restrict__ A_part,
+                                            float* __restrict__ bias_part, const ChunkInfo& ci, long long kh, int h,
+                                            int H, int cs, int vl, int ddt_dtype, int use_sp, float dmin, float dmax) {
+  const int tid = threadIdx.x;
+  const int t = tid;
+  float dlast = 0.f;
+  for (int i = 0; i < nsl; ++i) dlast += dl_part[kh * nsl + i];
+  float unused;
+  const float xi = t < cs ? cols[t] - rows[t] : 0.f;
+  const float intra = block_excl_scan<NT / 32>(xi, tmp, unused);
+  const float xb = t < vl - 1 ? gBs[t] : 0.f;
+  const float dB = block_excl_scan<NT / 32>(xb, tmp, unused);
+  // sum_{m >= tr} gC_m: thread t scans element tr = cs-1-t, so threads before it hold m > tr
+  const int tr = cs - 1 - t;
+  const float xc = (tr >= 0 && tr < vl) ? gC[kh * cs + tr] : 0.f;
+  const float exc = block_excl_scan<NT / 32>(xc, tmp, unused);
+  if (tr >= 0) revc[tr] = exc + xc;
+  __syncthreads();
+  float aP = 0.f, bP = 0.f;
+  if (t < ci.lim) {
+    const long long tok = ci.tok0 + t;
+    float gg = 0.f;
+    if (t < vl) {
+      const float total = intra + dB + revc[t] + dlast;
+      const float pre = ld_any(delta_raw, tok * H + h, ddt_dtype) + (delta_bias ? delta_bias[h] : 0.f);
+      const bool sp = use_sp && pre <= 20.0f;
+      float d = sp ? logf(expf(pre) + 1.0f) : pre;
+      const bool clamped = (d < dmin) || (d > dmax);
+      d = fminf(fmaxf(d, dmin), dmax);
+      gg = clamped ? 0.f : total * A[h] + ddts[t];
+      if (sp) gg *= 1.0f / (1.0f + expf(-pre));
+      aP = total * d;
+      bP = gg;
+    }
+    st_any(draw_grad, tok * H + h, ddt_dtype, gg);
+  }
+  const float as = block_sum<NT / 32>(aP, tmp);
+  const float bs = block_sum<NT / 32>(bP, tmp);
+  if (tid == 0) {
+    A_part[kh] = as;
+    bias_part[kh] = bs;
+  }
+}
+
 // ===========================================================================
 // bwd_intra: per (chunk, head); u and y_grad of the whole chunk in shared memory.
 //   accY[l,p] = sum_{l<=s<len} CB[s,l] exp(min(cum_s - cum_l, 0)) y_grad[s,p]   (:272-293)
@@ -777,44 +832,34 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
   __syncthreads();
 
   // dt backward, one token per thread
-  const int t = tid;
-  float dlast = 0.f;
-  for (int i = 0; i < nsl; ++i) dlast += dl_part[kh * nsl + i];
-  float unused;
-  const float xi = t < cs ? cols[t] - rows[t] : 0.f;
-  const float intra = block_excl_scan<kIT / 32>(xi, tmp, unused);
-  const float xb = t < vl - 1 ? gBs[t] : 0.f;
-  const float dB = block_excl_scan<kIT / 32>(xb, tmp, unused);
-  // sum_{m >= tr} gC_m: thread t scans element tr = cs-1-t, so threads before it hold m > tr
-  const int tr = cs - 1 - t;
-  const float xc = (tr >= 0 && tr < vl) ? gC[kh * cs + tr] : 0.f;
-  const float exc = block_excl_scan<kIT / 32>(xc, tmp, unused);
-  if (tr >= 0) revc[tr] = exc + xc;
-  __syncthreads();
-  float aP = 0.f, bP = 0.f;
-  if (t < ci.lim) {
-    const long long tok = ci.tok0 + t;
-    float gg = 0.f;
-    if (t < vl) {
-      const float total = intra + dB + revc[t] + dlast;
-      const float pre = ld_any(delta_raw, tok * H + h, ddt_dtype) + (delta_bias ? delta_bias[h] : 0.f);
-      const bool sp = use_sp && pre <= 20.0f;
-      float d = sp ? logf(expf(pre) + 1.0f) : pre;
-      const bool clamped = (d < dmin) || (d > dmax);
-      d = fminf(fmaxf(d, dmin), dmax);
-      gg = clamped ? 0.f : total * A[h] + ddts[t];
-      if (sp) gg *= 1.0f / (1.0f + expf(-pre));
-      aP = total * d;
-      bP = gg;
+  dt_backward<kIT>(cols, rows, gBs, ddts, revc, tmp, gC, dl_part, nsl, delta_raw, A, delta_bias, draw_grad, A_part,
+                   bias_part, ci, kh, h, H, cs, vl, ddt_dtype, use_sp, dmin, dmax);
+}
+
+// bwd_dt: the dt backward alone, for the tensor-core intra kernel (ssd_bwd_tc.cu), which
+// leaves ddt, gB, the row and the column decay sums per (chunk, head) in rows4 planes 0..3.
+__global__ void __launch_bounds__(256) bwd_dt_kernel(
+    const float* __restrict__ rows4, long long plane, const void* __restrict__ delta_raw, const float* __restrict__ A,
+    const float* __restrict__ delta_bias, const float* __restrict__ gC, const float* __restrict__ dl_part, int nsl,
+    void* __restrict__ draw_grad, float* __restrict__ A_part, float* __restrict__ bias_part, ChunkMap cm, int H,
+    int ddt_dtype, int use_sp, float dmin, float dmax) {
+  __shared__ float revc[kCSmax];
+  __shared__ float tmp[16];
+  const int h = blockIdx.x, k = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) {
+    if (threadIdx.x == 0) {
+      A_part[(long long)k * H + h] = 0.f;
+      bias_part[(long long)k * H + h] = 0.f;
     }
-    st_any(draw_grad, tok * H + h, ddt_dtype, gg);
+    return;
   }
-  const float as = block_sum<kIT / 32>(aP, tmp);
-  const float bs = block_sum<kIT / 32>(bP, tmp);
-  if (tid == 0) {
-    A_part[kh] = as;
-    bias_part[kh] = bs;
-  }
+  const long long kh = (long long)k * H + h;
+  const int cs = cm.cs;
+  const float* base = rows4 + kh * cs;
+  dt_backward<256>(base + 3 * plane, base + 2 * plane, base + plane, base, revc, tmp, gC, dl_part, nsl, delta_raw,
+                   A, delta_bias, draw_grad, A_part, bias_part, ci, kh, h, H, cs, ci.vlim, ddt_dtype, use_sp, dmin,
+                   dmax);
 }
 
 // ===========================================================================
@@ -998,10 +1043,17 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
     if ((e = cudaGetLastError())) return e;
   }
   if (a.ev[3]) cudaEventRecord(a.ev[3], c.stream);
-  bwd_intra_kernel<<<gkh, kIT, kSmemIntra, c.stream>>>(
-      a.u, a.y_grad, a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, a.dl_part, nsl, a.CBg,
-      a.u_grad, a.delta_raw_grad, a.A_part, a.bias_part, c.cm, H, G, P, a.x_dtype, a.y_dtype, a.dt_dtype, c.use_sp,
-      c.dmin, c.dmax);
+  if (tc) {
+    if ((e = launch_bwd_intra_tc(c, a))) return e;
+    bwd_dt_kernel<<<gkh, 256, 0, c.stream>>>(a.rows4, (long long)nk * H * cs, a.delta_raw, a.A, a.delta_bias, a.gC,
+                                              a.dl_part, nsl, a.delta_raw_grad, a.A_part, a.bias_part, c.cm, H,
+                                              a.dt_dtype, c.use_sp, c.dmin, c.dmax);
+  } else {
+    bwd_intra_kernel<<<gkh, kIT, kSmemIntra, c.stream>>>(
+        a.u, a.y_grad, a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, a.dl_part, nsl, a.CBg,
+        a.u_grad, a.delta_raw_grad, a.A_part, a.bias_part, c.cm, H, G, P, a.x_dtype, a.y_dtype, a.dt_dtype,
+        c.use_sp, c.dmin, c.dmax);
+  }
   if ((e = cudaGetLastError())) return e;
   if (a.ev[4]) cudaEventRecord(a.ev[4], c.stream);
   bwd_bmm_kernel<<<dim3((unsigned)(2 * nt), (unsigned)G, (unsigned)nk), 256, 0, c.stream>>>(

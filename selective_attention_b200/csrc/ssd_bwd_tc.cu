@@ -461,6 +461,303 @@ cudaError_t launch_states_typed(const LaunchCtx& c, const BwdArgs& a) {
       mu, mb, my, mc, reinterpret_cast<const YT*>(a.y_grad), a.dt, a.cum, a.states, a.hg, c.cm, c.H, c.G);
   return cudaGetLastError();
 }
+
+// ---------------------------------------------------------------------------
+// Intra-chunk products of the backward (ssd_bwd.cu bwd_intra_kernel's contractions and
+// its per-row work) on tcgen05, per (chunk, head); the dt backward (scans) stays on CUDA
+// cores (bwd_dt_kernel). For each 128-row half of the chunk (rows l = query tokens):
+//   accY[l,p] = sum_{s >= l} CB[s,l] exp(min(cum_s - cum_l, 0)) y_grad[s,p]        (:272-293)
+//     A operand = the decay-weighted CB rows s, l contiguous (MN-major), 16 bits, B = y_grad
+//   G[l,s]    = y_grad[l] . u[s]  (s <= l)                                       (:632-659)
+//   CB_grad[l,s] += G dt_s exp(min(cum_l - cum_s, 0));  w = CB_grad_h[l,s] CB[l,s] (s < l)
+//   rows[l] = sum_s w,  cols[s] = sum_l w                                         (:847-895)
+//   acc = accS + accY:  u_grad = acc dt_l,  ddt[l] = sum_p acc u,  gB[l] = dt_l sum_p accS u
+// Thread = row l = TMEM lane. TMEM: accY [0, 64), G (one 128-column block of s) [128, 256).
+// ---------------------------------------------------------------------------
+constexpr int kInThreads = 128;
+// u [256][128 B] | y_grad [256][128 B] | A: one 128-s block [2 l-blocks][128 s][128 B] |
+// dt, cum, cols [3][256] | barriers
+constexpr int kInOffU = 0, kInOffY = 32768, kInOffA = 65536, kInOffF = 98304, kInOffBar = kInOffF + 3072;
+constexpr size_t kInSmem = 1024 + kInOffBar + 64;
+
+// Sums of 32 values over the warp's lanes, transposed: lane i returns sum over lanes of
+// v[i] (31 shuffles in five halving steps; v is overwritten).
+__device__ __forceinline__ float warp_transpose_sum32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 16; k >= 1; k >>= 1) {
+    const bool upper = (lane & k) != 0;
+#pragma unroll
+    for (int i = 0; i < k; ++i) {
+      const float send = upper ? v[i] : v[i + k];
+      const float keep = upper ? v[i + k] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, k);
+    }
+  }
+  return v[0];
+}
+
+template <bool BF16, typename YT>
+__global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_y, const void* __restrict__ u,
+    const YT* __restrict__ yg, const float* __restrict__ dt, const float* __restrict__ cum,
+    const float* __restrict__ CB, const float* __restrict__ accS, float* __restrict__ CBg, void* __restrict__ u_grad,
+    float* __restrict__ rows4, ChunkMap cm, int H, int G, long long plane) {
+  using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  constexpr bool kY16 = sizeof(YT) == 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sU = sm + kInOffU;
+  uint8_t* sY = sm + kInOffY;
+  uint8_t* sA = sm + kInOffA;
+  float* dts = reinterpret_cast<float*>(sm + kInOffF);
+  float* cms = dts + 256;
+  float* cols = cms + 256;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kInOffBar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  const uint32_t bar_tma = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
+  const int h = blockIdx.x, k = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5;
+  const long long kh = (long long)k * H + h;
+  const long long kg = ((long long)k * G + g) * 65536;
+  const int vl = ci.vlim, lim = ci.lim;
+  if (tid == 0) {
+    prefetch_tmap(&tm_u);
+    if (kY16) prefetch_tmap(&tm_y);
+    mbar_init(bar_tma, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
+  for (int i = tid; i < 256; i += kInThreads) {
+    dts[i] = dt[kh * 256 + i];
+    cms[i] = cum[kh * 256 + i];
+    cols[i] = 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tl = (uint32_t)(warp * 32) << 16;
+  constexpr uint32_t T_Y = 0, T_G = 128;
+  constexpr uint32_t ID_Y = idesc_f16(128, 64, BF16, /*a_mn=*/true, /*b_mn=*/true);
+  constexpr uint32_t ID_G = idesc_f16(128, 128, BF16, false, false);
+  int uses = 0;
+  if (tid == 0) {
+    mbar_expect_tx(bar_tma, 32768u + (kY16 ? 32768u : 0u));
+    for (int b = 0; b < 2; ++b) {
+      tma_load_3d(smem_u32(sU + 16384 * b), &tm_u, 0, h, (int)(ci.tok0 + 128 * b), bar_tma);
+      if (kY16) tma_load_3d(smem_u32(sY + 16384 * b), &tm_y, 0, h, (int)(ci.tok0 + 128 * b), bar_tma);
+    }
+  }
+  if (!kY16) {
+#pragma unroll 4
+    for (int i = 0; i < 16; ++i) {
+      const int q = tid + kInThreads * i, row = q >> 3, c8 = q & 7;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (row < vl) {
+        const float* src = reinterpret_cast<const float*>(yg) + ((ci.tok0 + row) * H + h) * 64 + c8 * 8;
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
+        v = make_uint4(pack2<T16>(a.x, a.y), pack2<T16>(a.z, a.w), pack2<T16>(b.x, b.y), pack2<T16>(b.z, b.w));
+      }
+      *reinterpret_cast<uint4*>(sY + row * 128 + ((c8 ^ (row & 7)) << 4)) = v;
+    }
+  }
+  bool ok = mbar_wait(bar_tma, 0, kSiteBwdTcTma);
+  if (ok && vl < 256) {
+    // token rows at or past the length: zeros (their y_grad is ignored, their u unused)
+    for (int q = tid; q < (256 - vl) * 8; q += kInThreads) {
+      const uint32_t off = (uint32_t)(vl + (q >> 3)) * 128u + (uint32_t)(q & 7) * 16u;
+      *reinterpret_cast<uint4*>(sU + off) = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(sY + off) = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  fence_proxy_async_smem();
+  ok = __syncthreads_and(ok) != 0;
+
+  for (int m = 0; m < 2 && ok; ++m) {
+    const int l0 = 128 * m;
+    const int l = l0 + tid;
+    if (l0 >= lim) {  // no row of this half is produced: its per-row sums are 0
+      rows4[kh * 256 + l] = 0.f;
+      rows4[plane + kh * 256 + l] = 0.f;
+      rows4[2 * plane + kh * 256 + l] = 0.f;
+      continue;
+    }
+    const bool lv = l < vl;
+    // ---- accY over source blocks j = m .. 1 (s >= l); none when l0 >= vl (then no row is valid)
+    for (int j = m; j < 2 && ok; ++j) {
+      if (128 * j >= vl) break;
+      // A block: rows s = 128 j + sl, columns l = l0 + ll, the decay-weighted CB, 16 bits
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const int q = tid + kInThreads * i, sl = q >> 4, l8 = (q & 15) * 8;
+        const int s_ = 128 * j + sl, lb = l0 + l8;
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (s_ < vl && lb < vl && s_ >= lb) {
+          const float4 a = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)s_ * 256 + lb));
+          const float4 b = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)s_ * 256 + lb + 4));
+          const float cb8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+          const float cs_ = cms[s_];
+          float x[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int le = lb + e;
+            x[e] = (le <= s_ && le < vl) ? cb8[e] * __expf(fminf(cs_ - cms[le], 0.f)) : 0.f;
+          }
+          v = make_uint4(pack2<T16>(x[0], x[1]), pack2<T16>(x[2], x[3]), pack2<T16>(x[4], x[5]),
+                         pack2<T16>(x[6], x[7]));
+        }
+        *reinterpret_cast<uint4*>(sA + (l8 >> 6) * 16384 + sw128_off((uint32_t)sl, (uint32_t)((l8 & 63) >> 3))) = v;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_f16(tmem + T_Y, sdesc_sw128(smem_u32(sA) + ks * 2048, 16384, 1024),
+                   sdesc_sw128(smem_u32(sY) + (128 * j + 16 * ks) * 128, 16, 1024), ID_Y,
+                   (j > m || ks > 0) ? 1u : 0u);
+        umma_commit(bar_mma);
+      }
+      ok = __syncthreads_and(mbar_wait(bar_mma, uses & 1, kSiteBwdTcMma)) != 0;  // sA is reused
+      ++uses;
+      tc_fence_after();
+    }
+    if (!ok) break;
+    // ---- G = y_grad u^T over source blocks j = 0 .. m (s <= l), one block at a time
+    float rs = 0.f;
+    for (int j = 0; j <= m && ok; ++j) {
+      if (128 * j >= vl) break;
+      if (tid == 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma_f16(tmem + T_G, sdesc_sw128(smem_u32(sY) + l0 * 128 + ks * 32, 16, 1024),
+                   sdesc_sw128(smem_u32(sU) + 128 * j * 128 + ks * 32, 16, 1024), ID_G, ks > 0 ? 1u : 0u);
+        umma_commit(bar_mma);
+      }
+      ok = __syncthreads_and(mbar_wait(bar_mma, uses & 1, kSiteBwdTcMma)) != 0;
+      ++uses;
+      tc_fence_after();
+      if (!ok) break;
+      const float cl = cms[l];
+      const int wl0 = l0 + 32 * warp;  // first row of this warp
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        const int sb = 128 * j + 32 * c;
+        if (sb > wl0 + 31 || wl0 >= vl) continue;  // warp-uniform: no s <= l in this block
+        uint32_t v[32];
+        tmem_ld32(tmem + tl + T_G + 32 * c, v);
+        tmem_wait_ld();
+        float w[32];
+        const float* cbrow = CB + kg + (long long)l * 256 + sb;
+        float* cbgrow = CBg + kg + (long long)l * 256 + sb;
+#pragma unroll
+        for (int e4 = 0; e4 < 32; e4 += 4) {
+          float cbg[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int s_ = sb + e4 + e;
+            cbg[e] = (lv && s_ <= l) ? __uint_as_float(v[e4 + e]) * dts[s_] * __expf(fminf(cl - cms[s_], 0.f)) : 0.f;
+          }
+          const bool any = lv && sb + e4 <= l;
+          float4 cb4 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (any) {
+            atomicAdd(reinterpret_cast<float4*>(cbgrow + e4), make_float4(cbg[0], cbg[1], cbg[2], cbg[3]));
+            cb4 = __ldg(reinterpret_cast<const float4*>(cbrow + e4));
+          }
+          const float cbv[4] = {cb4.x, cb4.y, cb4.z, cb4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            w[e4 + e] = (sb + e4 + e < l) ? cbg[e] * cbv[e] : 0.f;
+            rs += w[e4 + e];
+          }
+        }
+        // column sums over the warp's 32 rows: lane i ends with the sum for s = sb + i
+        atomicAdd(&cols[sb + (tid & 31)], warp_transpose_sum32(w));
+      }
+      tc_fence_before();
+      __syncthreads();  // every thread has read G before the next block overwrites it
+    }
+    if (!ok) break;
+    // ---- per-row work: u_grad, ddt, gB, rows
+    {
+      uint32_t yv[2][32];
+      tmem_ld32(tmem + tl + T_Y, yv[0]);
+      tmem_ld32(tmem + tl + T_Y + 32, yv[1]);
+      tmem_wait_ld();
+      float dpart = 0.f, bpart = 0.f;
+      if (!lv) {  // rows at or past the length: u_grad 0
+        if (l < lim) {
+          uint4* grow = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(u_grad) + ((ci.tok0 + l) * H + h) * 64);
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) grow[c8] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      } else {
+        const float d = dts[l];
+        const float* srow = accS + (kh * 256 + l) * 64;
+        const uint16_t* urow = reinterpret_cast<const uint16_t*>(u) + ((ci.tok0 + l) * H + h) * 64;
+        uint16_t* grow = reinterpret_cast<uint16_t*>(u_grad) + ((ci.tok0 + l) * H + h) * 64;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          const float4 s0 = *reinterpret_cast<const float4*>(srow + 8 * c8);
+          const float4 s1 = *reinterpret_cast<const float4*>(srow + 8 * c8 + 4);
+          const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+          const uint4 u8 = __ldg(reinterpret_cast<const uint4*>(urow + 8 * c8));
+          const uint32_t uw[4] = {u8.x, u8.y, u8.z, u8.w};
+          uint32_t og[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 uf = unpack2<T16>(uw[q]);
+            const int e0 = 8 * c8 + 2 * q;
+            const float a0 = sv[2 * q] + __uint_as_float(yv[e0 >> 5][e0 & 31]);
+            const float a1 = sv[2 * q + 1] + __uint_as_float(yv[e0 >> 5][(e0 & 31) + 1]);
+            dpart = fmaf(a0, uf.x, fmaf(a1, uf.y, dpart));
+            bpart = fmaf(sv[2 * q], uf.x, fmaf(sv[2 * q + 1], uf.y, bpart));
+            og[q] = pack2<T16>(a0 * d, a1 * d);
+          }
+          *reinterpret_cast<uint4*>(grow + 8 * c8) = make_uint4(og[0], og[1], og[2], og[3]);
+        }
+      }
+      // rows4: [0] ddt, [1] gB, [2] rows, [3] cols, each (chunk, head, 256)
+      rows4[kh * 256 + l] = dpart;
+      rows4[plane + kh * 256 + l] = lv ? bpart * dts[l] : 0.f;
+      rows4[2 * plane + kh * 256 + l] = rs;
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  if (ok) {
+    for (int i = tid; i < 256; i += kInThreads) rows4[3 * plane + kh * 256 + i] = cols[i];
+  } else if (tid == 0 && uses > 0) {
+    mbar_wait(bar_mma, (uses - 1) & 1, kSiteBwdTcMma);  // let an MMA in flight land (bounded)
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+template <bool BF16, typename YT>
+cudaError_t launch_intra_typed(const LaunchCtx& c, const BwdArgs& a) {
+  CUtensorMap mu, my;
+  if (!make_map_3d(&mu, a.u, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&my, sizeof(YT) == 2 ? a.y_grad : a.u, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128))
+    return cudaErrorInvalidValue;
+  auto kern = bwd_intra_tc_kernel<BF16, YT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kInSmem);
+  if (e != cudaSuccess) return e;
+  const long long plane = (long long)c.nchunks_max * c.H * 256;
+  kern<<<dim3((unsigned)c.H, (unsigned)c.nchunks_max), kInThreads, kInSmem, c.stream>>>(
+      mu, my, a.u, reinterpret_cast<const YT*>(a.y_grad), a.dt, a.cum, a.CB, a.accS, a.CBg, a.u_grad, a.rows4,
+      c.cm, c.H, c.G, plane);
+  return cudaGetLastError();
+}
 }  // namespace
 
 bool bwd_state_grad_tc_supported(int x_dtype, int y_dtype, int P, int N, int cs) {
@@ -486,6 +783,16 @@ cudaError_t launch_bwd_chunk_states_tc(const LaunchCtx& c, const BwdArgs& a) {
   }
   if (a.y_dtype == SSD_F32) return launch_states_typed<false, float>(c, a);
   return launch_states_typed<false, __half>(c, a);
+}
+
+cudaError_t launch_bwd_intra_tc(const LaunchCtx& c, const BwdArgs& a) {
+  if (c.nchunks_max > 65535 || c.H > 65535) return cudaErrorInvalidValue;
+  if (a.x_dtype == SSD_BF16) {
+    if (a.y_dtype == SSD_F32) return launch_intra_typed<true, float>(c, a);
+    return launch_intra_typed<true, __nv_bfloat16>(c, a);
+  }
+  if (a.y_dtype == SSD_F32) return launch_intra_typed<false, float>(c, a);
+  return launch_intra_typed<false, __half>(c, a);
 }
 
 SSDB200_DEFINE_ERROR_FETCH(fetch_error_bwd_tc)
