@@ -472,12 +472,14 @@ cudaError_t launch_states_typed(const LaunchCtx& c, const BwdArgs& a) {
 //   CB_grad[l,s] += G dt_s exp(min(cum_l - cum_s, 0));  w = CB_grad_h[l,s] CB[l,s] (s < l)
 //   rows[l] = sum_s w,  cols[s] = sum_l w                                         (:847-895)
 //   acc = accS + accY:  u_grad = acc dt_l,  ddt[l] = sum_p acc u,  gB[l] = dt_l sum_p accS u
-// Thread = row l = TMEM lane. TMEM: accY [0, 64), G (one 128-column block of s) [128, 256).
+// Row l = TMEM lane; two warps per lane quadrant split each accumulator's columns.
+// TMEM: accY [0, 64), G (one 128-column block of s) [128, 256).
 // ---------------------------------------------------------------------------
-constexpr int kInThreads = 128;
+constexpr int kInThreads = 256;
 // u [256][128 B] | y_grad [256][128 B] | A: one 128-s block [2 l-blocks][128 s][128 B] |
-// dt, cum, cols [3][256] | barriers
-constexpr int kInOffU = 0, kInOffY = 32768, kInOffA = 65536, kInOffF = 98304, kInOffBar = kInOffF + 3072;
+// dt, cum, cols [3][256], row-sum / ddt / gB partials of the two column halves [3][2][128] |
+// barriers
+constexpr int kInOffU = 0, kInOffY = 32768, kInOffA = 65536, kInOffF = 98304, kInOffBar = kInOffF + 6144;
 constexpr size_t kInSmem = 1024 + kInOffBar + 64;
 
 // Sums of 32 values over the warp's lanes, transposed: lane i returns sum over lanes of
@@ -497,6 +499,8 @@ __device__ __forceinline__ float warp_transpose_sum32(float (&v)[32]) {
   return v[0];
 }
 
+// 8 warps: warp w reads TMEM lane quadrant w % 4 (rows l0 + 32 (w % 4) + lane) and the
+// column half w / 4 of each accumulator; two CTAs per SM.
 template <bool BF16, typename YT>
 __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
     const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_y, const void* __restrict__ u,
@@ -513,13 +517,17 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
   float* dts = reinterpret_cast<float*>(sm + kInOffF);
   float* cms = dts + 256;
   float* cols = cms + 256;
+  float* rsp = cols + 256;  // [2][128] each
+  float* dpp = rsp + 256;
+  float* bpp = dpp + 256;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kInOffBar);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
   const uint32_t bar_tma = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
   const int h = blockIdx.x, k = blockIdx.y;
   ChunkInfo ci;
   if (!chunk_info(cm, k, ci)) return;
-  const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5;
+  const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3, hc = warp >> 2;
   const long long kh = (long long)k * H + h;
   const long long kg = ((long long)k * G + g) * 65536;
   const int vl = ci.vlim, lim = ci.lim;
@@ -531,7 +539,8 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
-  for (int i = tid; i < 256; i += kInThreads) {
+  {
+    const int i = tid;  // kInThreads == 256
     dts[i] = dt[kh * 256 + i];
     cms[i] = cum[kh * 256 + i];
     cols[i] = 0.f;
@@ -540,7 +549,7 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tl = (uint32_t)(warp * 32) << 16;
+  const uint32_t tl = (uint32_t)(qd * 32) << 16;
   constexpr uint32_t T_Y = 0, T_G = 128;
   constexpr uint32_t ID_Y = idesc_f16(128, 64, BF16, /*a_mn=*/true, /*b_mn=*/true);
   constexpr uint32_t ID_G = idesc_f16(128, 128, BF16, false, false);
@@ -553,8 +562,9 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
     }
   }
   if (!kY16) {
+    // fp32 y_grad rows rounded to 16 bits, K-major over p; rows past the length are 0
 #pragma unroll 4
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 8; ++i) {
       const int q = tid + kInThreads * i, row = q >> 3, c8 = q & 7;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
       if (row < vl) {
@@ -563,7 +573,7 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
         const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
         v = make_uint4(pack2<T16>(a.x, a.y), pack2<T16>(a.z, a.w), pack2<T16>(b.x, b.y), pack2<T16>(b.z, b.w));
       }
-      *reinterpret_cast<uint4*>(sY + row * 128 + ((c8 ^ (row & 7)) << 4)) = v;
+      *reinterpret_cast<uint4*>(sY + sw128_off((uint32_t)row, (uint32_t)c8)) = v;
     }
   }
   bool ok = mbar_wait(bar_tma, 0, kSiteBwdTcTma);
@@ -580,11 +590,13 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
 
   for (int m = 0; m < 2 && ok; ++m) {
     const int l0 = 128 * m;
-    const int l = l0 + tid;
+    const int r = 32 * qd + lane, l = l0 + r;
     if (l0 >= lim) {  // no row of this half is produced: its per-row sums are 0
-      rows4[kh * 256 + l] = 0.f;
-      rows4[plane + kh * 256 + l] = 0.f;
-      rows4[2 * plane + kh * 256 + l] = 0.f;
+      if (hc == 0) {
+        rows4[kh * 256 + l] = 0.f;
+        rows4[plane + kh * 256 + l] = 0.f;
+        rows4[2 * plane + kh * 256 + l] = 0.f;
+      }
       continue;
     }
     const bool lv = l < vl;
@@ -593,7 +605,7 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
       if (128 * j >= vl) break;
       // A block: rows s = 128 j + sl, columns l = l0 + ll, the decay-weighted CB, 16 bits
 #pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 8; ++i) {
         const int q = tid + kInThreads * i, sl = q >> 4, l8 = (q & 15) * 8;
         const int s_ = 128 * j + sl, lb = l0 + l8;
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
@@ -647,9 +659,9 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
       tc_fence_after();
       if (!ok) break;
       const float cl = cms[l];
-      const int wl0 = l0 + 32 * warp;  // first row of this warp
+      const int wl0 = l0 + 32 * qd;  // first row of this warp
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 2 * hc; c < 2 * hc + 2; ++c) {
         const int sb = 128 * j + 32 * c;
         if (sb > wl0 + 31 || wl0 >= vl) continue;  // warp-uniform: no s <= l in this block
         uint32_t v[32];
@@ -680,61 +692,65 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
           }
         }
         // column sums over the warp's 32 rows: lane i ends with the sum for s = sb + i
-        atomicAdd(&cols[sb + (tid & 31)], warp_transpose_sum32(w));
+        atomicAdd(&cols[sb + lane], warp_transpose_sum32(w));
       }
       tc_fence_before();
       __syncthreads();  // every thread has read G before the next block overwrites it
     }
     if (!ok) break;
-    // ---- per-row work: u_grad, ddt, gB, rows
+    // ---- per-row work on this warp's 32 columns p: u_grad, and the ddt / gB partials
     {
-      uint32_t yv[2][32];
-      tmem_ld32(tmem + tl + T_Y, yv[0]);
-      tmem_ld32(tmem + tl + T_Y + 32, yv[1]);
+      uint32_t yv[32];
+      tmem_ld32(tmem + tl + T_Y + 32 * hc, yv);
       tmem_wait_ld();
       float dpart = 0.f, bpart = 0.f;
+      uint4* grow = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(u_grad) + ((ci.tok0 + l) * H + h) * 64 + 32 * hc);
       if (!lv) {  // rows at or past the length: u_grad 0
         if (l < lim) {
-          uint4* grow = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(u_grad) + ((ci.tok0 + l) * H + h) * 64);
 #pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) grow[c8] = make_uint4(0u, 0u, 0u, 0u);
+          for (int c8 = 0; c8 < 4; ++c8) grow[c8] = make_uint4(0u, 0u, 0u, 0u);
         }
       } else {
         const float d = dts[l];
-        const float* srow = accS + (kh * 256 + l) * 64;
-        const uint16_t* urow = reinterpret_cast<const uint16_t*>(u) + ((ci.tok0 + l) * H + h) * 64;
-        uint16_t* grow = reinterpret_cast<uint16_t*>(u_grad) + ((ci.tok0 + l) * H + h) * 64;
+        const float* srow = accS + (kh * 256 + l) * 64 + 32 * hc;
+        const uint4* urow = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(u) +
+                                                           ((ci.tok0 + l) * H + h) * 64 + 32 * hc);
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
+        for (int c8 = 0; c8 < 4; ++c8) {
           const float4 s0 = *reinterpret_cast<const float4*>(srow + 8 * c8);
           const float4 s1 = *reinterpret_cast<const float4*>(srow + 8 * c8 + 4);
           const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-          const uint4 u8 = __ldg(reinterpret_cast<const uint4*>(urow + 8 * c8));
+          const uint4 u8 = __ldg(urow + c8);
           const uint32_t uw[4] = {u8.x, u8.y, u8.z, u8.w};
           uint32_t og[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float2 uf = unpack2<T16>(uw[q]);
-            const int e0 = 8 * c8 + 2 * q;
-            const float a0 = sv[2 * q] + __uint_as_float(yv[e0 >> 5][e0 & 31]);
-            const float a1 = sv[2 * q + 1] + __uint_as_float(yv[e0 >> 5][(e0 & 31) + 1]);
+            const float a0 = sv[2 * q] + __uint_as_float(yv[8 * c8 + 2 * q]);
+            const float a1 = sv[2 * q + 1] + __uint_as_float(yv[8 * c8 + 2 * q + 1]);
             dpart = fmaf(a0, uf.x, fmaf(a1, uf.y, dpart));
             bpart = fmaf(sv[2 * q], uf.x, fmaf(sv[2 * q + 1], uf.y, bpart));
             og[q] = pack2<T16>(a0 * d, a1 * d);
           }
-          *reinterpret_cast<uint4*>(grow + 8 * c8) = make_uint4(og[0], og[1], og[2], og[3]);
+          grow[c8] = make_uint4(og[0], og[1], og[2], og[3]);
         }
       }
-      // rows4: [0] ddt, [1] gB, [2] rows, [3] cols, each (chunk, head, 256)
-      rows4[kh * 256 + l] = dpart;
-      rows4[plane + kh * 256 + l] = lv ? bpart * dts[l] : 0.f;
-      rows4[2 * plane + kh * 256 + l] = rs;
+      rsp[hc * 128 + r] = rs;
+      dpp[hc * 128 + r] = dpart;
+      bpp[hc * 128 + r] = bpart;
     }
     tc_fence_before();
     __syncthreads();
+    if (hc == 0) {
+      // rows4: [0] ddt, [1] gB, [2] rows, [3] cols, each (chunk, head, 256)
+      rows4[kh * 256 + l] = dpp[r] + dpp[128 + r];
+      rows4[plane + kh * 256 + l] = lv ? (bpp[r] + bpp[128 + r]) * dts[l] : 0.f;
+      rows4[2 * plane + kh * 256 + l] = rsp[r] + rsp[128 + r];
+    }
+    __syncthreads();  // partials read before the next half writes them
   }
   if (ok) {
-    for (int i = tid; i < 256; i += kInThreads) rows4[3 * plane + kh * 256 + i] = cols[i];
+    rows4[3 * plane + kh * 256 + tid] = cols[tid];
   } else if (tid == 0 && uses > 0) {
     mbar_wait(bar_mma, (uses - 1) & 1, kSiteBwdTcMma);  // let an MMA in flight land (bounded)
   }
