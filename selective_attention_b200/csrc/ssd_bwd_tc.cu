@@ -4,7 +4,7 @@
 // Per (chunk, head), with scale_l = exp(min(cum_last - cum_l, 0)), w_l = scale_l dt_l and
 // e_l = exp(cum_l) (all zero at or past the row's length), the same products as
 // bwd_state_grad_kernel in ssd_bwd.cu (backward_kernel.py:255-262, :402-415, :522-538):
-//   accS[l,p]     = scale_l sum_n B[l,n] hg[p,n]
+//   accS[l,p]     = scale_l sum_n B[l,n] hg[p,n]   (stored [chunk, head][p / 4][l][4])
 //   B_grad[l,:]  += w_l     sum_p u[l,p] hg[p,:]
 //   C_grad[l,:]  += e_l     sum_p y_grad[l,p] prev[p,:]
 //   gC[l]         = sum_n (that C_grad row) C[l,n]
@@ -205,8 +205,9 @@ __global__ void __launch_bounds__(kBgThreads, 2) bwd_state_grad_tc_kernel(
     if (!ok) break;
     const int l = l0 + r;
     {
-      // accS row l (64 columns) times scale_l
-      float* o = accS_out + (kh * 256 + l) * 64;
+      // accS row l (64 columns) times scale_l, stored as [p / 4][l][4] per (chunk, head) so
+      // that the lanes' 16-byte stores (and the intra kernel's loads) are contiguous
+      float4* o = reinterpret_cast<float4*>(accS_out) + kh * 16 * 256 + l;
       const float sc = sS[l];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) bwd_state_grad_tc_kernel(
         tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 32; e += 4)
-          *reinterpret_cast<float4*>(o + 32 * c + e) =
+          o[(8 * c + e / 4) * 256] =
               make_float4(__uint_as_float(v[e]) * sc, __uint_as_float(v[e + 1]) * sc, __uint_as_float(v[e + 2]) * sc,
                           __uint_as_float(v[e + 3]) * sc);
       }
@@ -468,19 +469,20 @@ cudaError_t launch_states_typed(const LaunchCtx& c, const BwdArgs& a) {
 // cores (bwd_dt_kernel). For each 128-row half of the chunk (rows l = query tokens):
 //   accY[l,p] = sum_{s >= l} CB[s,l] exp(min(cum_s - cum_l, 0)) y_grad[s,p]        (:272-293)
 //     A operand = the decay-weighted CB rows s, l contiguous (MN-major), 16 bits, B = y_grad
-//   G[l,s]    = y_grad[l] . u[s]  (s <= l)                                       (:632-659)
+//   G[l,s]    = y_grad[l] . u[s]  (s <= l), computed as G^T: lane s, column l    (:632-659)
 //   CB_grad[l,s] += G dt_s exp(min(cum_l - cum_s, 0));  w = CB_grad_h[l,s] CB[l,s] (s < l)
 //   rows[l] = sum_s w,  cols[s] = sum_l w                                         (:847-895)
 //   acc = accS + accY:  u_grad = acc dt_l,  ddt[l] = sum_p acc u,  gB[l] = dt_l sum_p accS u
-// Row l = TMEM lane; two warps per lane quadrant split each accumulator's columns.
-// TMEM: accY [0, 64), G (one 128-column block of s) [128, 256).
+// accY: TMEM lane = row l. G^T: lane = source token s, so a warp's 32 lanes read CB and add
+// into CB_grad along contiguous rows. Two warps per lane quadrant split each accumulator's
+// columns. TMEM: accY [0, 64), G^T (one 128 x 128 block) [128, 256).
 // ---------------------------------------------------------------------------
 constexpr int kInThreads = 256;
-// u [256][128 B] | y_grad [256][128 B] | A: one 128-s block [2 l-blocks][128 s][128 B] |
-// dt, cum, cols [3][256], row-sum / ddt / gB partials of the two column halves [3][2][128] |
+// dynamic: u [256][128 B] | y_grad [256][128 B] | A: one 128-s block [2 l-blocks][128 s][128 B];
+// static: dt, cum, cols, rows [4][256], ddt / gB partials of the two column halves [2][2][128],
 // barriers
-constexpr int kInOffU = 0, kInOffY = 32768, kInOffA = 65536, kInOffF = 98304, kInOffBar = kInOffF + 6144;
-constexpr size_t kInSmem = 1024 + kInOffBar + 64;
+constexpr int kInOffU = 0, kInOffY = 32768, kInOffA = 65536;
+constexpr size_t kInSmem = 1024 + 98304;  // + 6 KB of static shared arrays
 
 // Sums of 32 values over the warp's lanes, transposed: lane i returns sum over lanes of
 // v[i] (31 shuffles in five halving steps; v is overwritten).
@@ -510,18 +512,15 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr bool kY16 = sizeof(YT) == 2;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // offset from the shared array itself, so that every access below stays a shared one
+  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sU = sm + kInOffU;
   uint8_t* sY = sm + kInOffY;
   uint8_t* sA = sm + kInOffA;
-  float* dts = reinterpret_cast<float*>(sm + kInOffF);
-  float* cms = dts + 256;
-  float* cols = cms + 256;
-  float* rsp = cols + 256;  // [2][128] each
-  float* dpp = rsp + 256;
-  float* bpp = dpp + 256;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kInOffBar);
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  __shared__ float dts[256], cms[256], cols[256], rws[256];
+  __shared__ float dpp[256], bpp[256];  // [2][128] each
+  __shared__ uint64_t bars[2];
+  __shared__ uint32_t tslot[1];
   const uint32_t bar_tma = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
   const int h = blockIdx.x, k = blockIdx.y;
   ChunkInfo ci;
@@ -544,6 +543,7 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
     dts[i] = dt[kh * 256 + i];
     cms[i] = cum[kh * 256 + i];
     cols[i] = 0.f;
+    rws[i] = 0.f;
   }
   tc_fence_before();
   __syncthreads();
@@ -562,17 +562,24 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
     }
   }
   if (!kY16) {
-    // fp32 y_grad rows rounded to 16 bits, K-major over p; rows past the length are 0
-#pragma unroll 4
+    // fp32 y_grad rows rounded to 16 bits, K-major over p; rows past the length are 0. All
+    // loads are issued before any is used (rows past the length read the last valid row).
+    float4 ya[8], yb[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int q = tid + kInThreads * i, row = q >> 3, c8 = q & 7;
+      const int rr = row < vl ? row : max(vl - 1, 0);
+      const float* src = reinterpret_cast<const float*>(yg) + ((ci.tok0 + rr) * H + h) * 64 + c8 * 8;
+      ya[i] = __ldg(reinterpret_cast<const float4*>(src));
+      yb[i] = __ldg(reinterpret_cast<const float4*>(src + 4));
+    }
+#pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int q = tid + kInThreads * i, row = q >> 3, c8 = q & 7;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (row < vl) {
-        const float* src = reinterpret_cast<const float*>(yg) + ((ci.tok0 + row) * H + h) * 64 + c8 * 8;
-        const float4 a = __ldg(reinterpret_cast<const float4*>(src));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
-        v = make_uint4(pack2<T16>(a.x, a.y), pack2<T16>(a.z, a.w), pack2<T16>(b.x, b.y), pack2<T16>(b.z, b.w));
-      }
+      if (row < vl)
+        v = make_uint4(pack2<T16>(ya[i].x, ya[i].y), pack2<T16>(ya[i].z, ya[i].w), pack2<T16>(yb[i].x, yb[i].y),
+                       pack2<T16>(yb[i].z, yb[i].w));
       *reinterpret_cast<uint4*>(sY + sw128_off((uint32_t)row, (uint32_t)c8)) = v;
     }
   }
@@ -595,7 +602,6 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
       if (hc == 0) {
         rows4[kh * 256 + l] = 0.f;
         rows4[plane + kh * 256 + l] = 0.f;
-        rows4[2 * plane + kh * 256 + l] = 0.f;
       }
       continue;
     }
@@ -603,27 +609,37 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
     // ---- accY over source blocks j = m .. 1 (s >= l); none when l0 >= vl (then no row is valid)
     for (int j = m; j < 2 && ok; ++j) {
       if (128 * j >= vl) break;
-      // A block: rows s = 128 j + sl, columns l = l0 + ll, the decay-weighted CB, 16 bits
-#pragma unroll 4
-      for (int i = 0; i < 8; ++i) {
-        const int q = tid + kInThreads * i, sl = q >> 4, l8 = (q & 15) * 8;
-        const int s_ = 128 * j + sl, lb = l0 + l8;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (s_ < vl && lb < vl && s_ >= lb) {
-          const float4 a = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)s_ * 256 + lb));
-          const float4 b = __ldg(reinterpret_cast<const float4*>(CB + kg + (long long)s_ * 256 + lb + 4));
-          const float cb8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      // A block: rows s = 128 j + sl, columns l = l0 + ll, the decay-weighted CB, 16 bits.
+      // Two passes of four chunks: the eight 16-byte loads of a pass are issued together
+      // (the whole tile is inside the chunk's CB; entries outside s >= l, s, l < len are
+      // loaded and dropped).
+#pragma unroll
+      for (int i0 = 0; i0 < 8; i0 += 4) {
+        float4 ca[4], cb[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int q = tid + kInThreads * (i0 + i), sl = q >> 4, l8 = (q & 15) * 8;
+          const float* src = CB + kg + (long long)(128 * j + sl) * 256 + l0 + l8;
+          ca[i] = __ldg(reinterpret_cast<const float4*>(src));
+          cb[i] = __ldg(reinterpret_cast<const float4*>(src + 4));
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int q = tid + kInThreads * (i0 + i), sl = q >> 4, l8 = (q & 15) * 8;
+          const int s_ = 128 * j + sl, lb = l0 + l8;
+          const float cb8[8] = {ca[i].x, ca[i].y, ca[i].z, ca[i].w, cb[i].x, cb[i].y, cb[i].z, cb[i].w};
           const float cs_ = cms[s_];
+          const bool srow = s_ < vl;
           float x[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int le = lb + e;
-            x[e] = (le <= s_ && le < vl) ? cb8[e] * __expf(fminf(cs_ - cms[le], 0.f)) : 0.f;
+            x[e] = (srow && le <= s_) ? cb8[e] * __expf(fminf(cs_ - cms[le], 0.f)) : 0.f;
           }
-          v = make_uint4(pack2<T16>(x[0], x[1]), pack2<T16>(x[2], x[3]), pack2<T16>(x[4], x[5]),
-                         pack2<T16>(x[6], x[7]));
+          const uint4 v = make_uint4(pack2<T16>(x[0], x[1]), pack2<T16>(x[2], x[3]), pack2<T16>(x[4], x[5]),
+                                     pack2<T16>(x[6], x[7]));
+          *reinterpret_cast<uint4*>(sA + (l8 >> 6) * 16384 + sw128_off((uint32_t)sl, (uint32_t)((l8 & 63) >> 3))) = v;
         }
-        *reinterpret_cast<uint4*>(sA + (l8 >> 6) * 16384 + sw128_off((uint32_t)sl, (uint32_t)((l8 & 63) >> 3))) = v;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -642,58 +658,55 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
       tc_fence_after();
     }
     if (!ok) break;
-    // ---- G = y_grad u^T over source blocks j = 0 .. m (s <= l), one block at a time
-    float rs = 0.f;
+    // ---- G^T[s, l] = u[s] . y_grad[l] over source blocks j = 0 .. m (s <= l), one block at a
+    // time; TMEM lane = source token s, so CB / CB_grad rows are read and added coalesced
     for (int j = 0; j <= m && ok; ++j) {
       if (128 * j >= vl) break;
       if (tid == 0) {
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
-          umma_f16(tmem + T_G, sdesc_sw128(smem_u32(sY) + l0 * 128 + ks * 32, 16, 1024),
-                   sdesc_sw128(smem_u32(sU) + 128 * j * 128 + ks * 32, 16, 1024), ID_G, ks > 0 ? 1u : 0u);
+          umma_f16(tmem + T_G, sdesc_sw128(smem_u32(sU) + 128 * j * 128 + ks * 32, 16, 1024),
+                   sdesc_sw128(smem_u32(sY) + l0 * 128 + ks * 32, 16, 1024), ID_G, ks > 0 ? 1u : 0u);
         umma_commit(bar_mma);
       }
       ok = __syncthreads_and(mbar_wait(bar_mma, uses & 1, kSiteBwdTcMma)) != 0;
       ++uses;
       tc_fence_after();
       if (!ok) break;
-      const float cl = cms[l];
-      const int wl0 = l0 + 32 * qd;  // first row of this warp
+      const int ws0 = 128 * j + 32 * qd;  // first source token of this warp
+      const int sj = ws0 + lane;
+      const bool sv = sj < vl;
+      const float dsj = dts[sj], csj = cms[sj];
+      float cacc = 0.f;
 #pragma unroll 1
       for (int c = 2 * hc; c < 2 * hc + 2; ++c) {
-        const int sb = 128 * j + 32 * c;
-        if (sb > wl0 + 31 || wl0 >= vl) continue;  // warp-uniform: no s <= l in this block
+        const int lb = l0 + 32 * c;  // columns l = lb + i
+        if (lb + 31 < ws0 || ws0 >= vl || lb >= vl) continue;  // warp-uniform: no pair s <= l < len
+        const float cml = cms[lb + lane];  // lane i: cum of column l = lb + i (shuffled below)
+        // CB[l, s] for the 32 columns (inside the chunk's tile; pairs outside s <= l < len dropped)
+        float w[32];
+        const float* cbcol = CB + kg + (long long)lb * 256 + sj;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i] = __ldg(cbcol + i * 256);
         uint32_t v[32];
         tmem_ld32(tmem + tl + T_G + 32 * c, v);
         tmem_wait_ld();
-        float w[32];
-        const float* cbrow = CB + kg + (long long)l * 256 + sb;
-        float* cbgrow = CBg + kg + (long long)l * 256 + sb;
+        float* cbgcol = CBg + kg + (long long)lb * 256 + sj;
 #pragma unroll
-        for (int e4 = 0; e4 < 32; e4 += 4) {
-          float cbg[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int s_ = sb + e4 + e;
-            cbg[e] = (lv && s_ <= l) ? __uint_as_float(v[e4 + e]) * dts[s_] * __expf(fminf(cl - cms[s_], 0.f)) : 0.f;
-          }
-          const bool any = lv && sb + e4 <= l;
-          float4 cb4 = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (any) {
-            atomicAdd(reinterpret_cast<float4*>(cbgrow + e4), make_float4(cbg[0], cbg[1], cbg[2], cbg[3]));
-            cb4 = __ldg(reinterpret_cast<const float4*>(cbrow + e4));
-          }
-          const float cbv[4] = {cb4.x, cb4.y, cb4.z, cb4.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            w[e4 + e] = (sb + e4 + e < l) ? cbg[e] * cbv[e] : 0.f;
-            rs += w[e4 + e];
-          }
+        for (int i = 0; i < 32; ++i) {
+          const int l_ = lb + i;
+          const bool pv = sv && sj <= l_ && l_ < vl;
+          const float cl = __shfl_sync(0xffffffffu, cml, i);  // every lane takes part
+          const float cbg = pv ? __uint_as_float(v[i]) * dsj * __expf(fminf(cl - csj, 0.f)) : 0.f;
+          if (pv) atomicAdd(cbgcol + i * 256, cbg);
+          w[i] = (pv && sj < l_) ? cbg * w[i] : 0.f;
+          cacc += w[i];
         }
-        // column sums over the warp's 32 rows: lane i ends with the sum for s = sb + i
-        atomicAdd(&cols[sb + lane], warp_transpose_sum32(w));
+        // row sums over the warp's 32 source tokens: lane i ends with the sum for l = lb + i
+        atomicAdd(&rws[lb + lane], warp_transpose_sum32(w));
       }
+      atomicAdd(&cols[sj], cacc);
       tc_fence_before();
       __syncthreads();  // every thread has read G before the next block overwrites it
     }
@@ -712,15 +725,14 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
         }
       } else {
         const float d = dts[l];
-        const float* srow = accS + (kh * 256 + l) * 64 + 32 * hc;
-        const uint4* urow = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(u) +
-                                                           ((ci.tok0 + l) * H + h) * 64 + 32 * hc);
+        // accS [p / 4][l][4]: lanes read consecutive 16-byte pieces
+        const float4* srow = reinterpret_cast<const float4*>(accS) + (kh * 16 + 8 * hc) * 256 + l;
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
-          const float4 s0 = *reinterpret_cast<const float4*>(srow + 8 * c8);
-          const float4 s1 = *reinterpret_cast<const float4*>(srow + 8 * c8 + 4);
+          const float4 s0 = srow[(2 * c8) * 256];
+          const float4 s1 = srow[(2 * c8 + 1) * 256];
           const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-          const uint4 u8 = __ldg(urow + c8);
+          const uint4 u8 = *reinterpret_cast<const uint4*>(sU + sw128_off((uint32_t)l, (uint32_t)(4 * hc + c8)));
           const uint32_t uw[4] = {u8.x, u8.y, u8.z, u8.w};
           uint32_t og[4];
 #pragma unroll
@@ -735,7 +747,6 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
           grow[c8] = make_uint4(og[0], og[1], og[2], og[3]);
         }
       }
-      rsp[hc * 128 + r] = rs;
       dpp[hc * 128 + r] = dpart;
       bpp[hc * 128 + r] = bpart;
     }
@@ -745,11 +756,11 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
       // rows4: [0] ddt, [1] gB, [2] rows, [3] cols, each (chunk, head, 256)
       rows4[kh * 256 + l] = dpp[r] + dpp[128 + r];
       rows4[plane + kh * 256 + l] = lv ? (bpp[r] + bpp[128 + r]) * dts[l] : 0.f;
-      rows4[2 * plane + kh * 256 + l] = rsp[r] + rsp[128 + r];
     }
     __syncthreads();  // partials read before the next half writes them
   }
   if (ok) {
+    rows4[2 * plane + kh * 256 + tid] = rws[tid];
     rows4[3 * plane + kh * 256 + tid] = cols[tid];
   } else if (tid == 0 && uses > 0) {
     mbar_wait(bar_mma, (uses - 1) & 1, kSiteBwdTcMma);  // let an MMA in flight land (bounded)
