@@ -426,7 +426,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sattn_prefill_tc_kernel(const T
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int NB = D / 64;
   extern __shared__ uint8_t smraw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = align1024_shared(smraw);
   uint8_t* sQ = base;
   uint8_t* sKV = sQ + NB * kQBlk;                              // two buffers of (K, V)
   float* sg = reinterpret_cast<float*>(sKV + 4 * NB * kKBlk);  // two buffers of 64 log-gates
@@ -729,7 +729,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int NS = kFaStages;
   extern __shared__ uint8_t smraw[];
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  uint8_t* base = align1024_shared(smraw);
   uint8_t* sQ = base;  // Q_A | Q_B
   auto sK = [&](int s) { return base + 2 * kFaTile + s * kFaStageBytes; };
   auto sV = [&](int s) { return sK(s) + kFaTile; };

@@ -22,6 +22,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The dynamic shared array rounded up to 1024 bytes (SW128 operands, TMA boxes). The
+// offset is added to the array pointer itself, not computed through an integer, so the
+// compiler keeps every access through the result a shared-memory one (an integer round trip
+// turns them into generic accesses that it may not reorder around global ones).
+__device__ __forceinline__ uint8_t* align1024_shared(uint8_t* p) {
+  return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");

@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kBgThreads, 2) bwd_state_grad_tc_kernel(
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr bool kY16 = sizeof(YT) == 2;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = align1024_shared(smem_raw);
   uint8_t* sHg = sm + kBgOffHg;
   uint8_t* sPv = sm + kBgOffPv;
   uint8_t* sB = sm + kBgOffB;
@@ -334,7 +334,7 @@ __global__ void __launch_bounds__(kCsThreads) bwd_chunk_states_tc_kernel(
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr bool kY16 = sizeof(YT) == 2;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = align1024_shared(smem_raw);
   uint8_t* sB = sm;           // 2 x (128 tokens x 128 B): dstate halves
   uint8_t* sX = sm + 32768;   // 128 tokens x 128 B
   float* sW = reinterpret_cast<float*>(sm + 49152);  // [256] token weights
@@ -512,8 +512,7 @@ __global__ void __launch_bounds__(kInThreads, 2) bwd_intra_tc_kernel(
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr bool kY16 = sizeof(YT) == 2;
   extern __shared__ uint8_t smem_raw[];
-  // offset from the shared array itself, so that every access below stays a shared one
-  uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t* sm = align1024_shared(smem_raw);
   uint8_t* sU = sm + kInOffU;
   uint8_t* sY = sm + kInOffY;
   uint8_t* sA = sm + kInOffA;

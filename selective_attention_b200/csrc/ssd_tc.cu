@@ -52,11 +52,7 @@ template <bool BF16> struct T16Of;
 template <> struct T16Of<true> { using type = __nv_bfloat16; };
 template <> struct T16Of<false> { using type = __half; };
 
-// p rounded up to 1024 bytes by an offset from p itself (not through an integer), so that
-// accesses through the result stay shared-memory ones for the compiler.
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return p + ((1024u - (static_cast<uint32_t>(__cvta_generic_to_shared(p)) & 1023u)) & 1023u);
-}
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) { return align1024_shared(p); }
 
 // Scale the 16-byte chunk (8 elements of T16) by w (fp32 products, one rounding).
 template <typename T16>
