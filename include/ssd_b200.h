@@ -30,6 +30,11 @@
  *   sattn_prefill_fwd      <- modules/selective_attention.py:27-144 _build_attn_matrix and
  *                             the seq-mode _gated_softmax, with the @ v of :270-280
  *                             (SelectiveMHA.forward in inference, compressed or not)
+ *   sattn_train_fwd        <- modules/selective_attention.py:232-280 (SelectiveMHA.forward with
+ *                             self.training: score statistics, std-scaled log-gates, gated
+ *                             softmax, @ v)
+ *   sattn_train_bwd        <- the autograd backward of the same lines (torch's, for the
+ *                             reference), including the gradient through the score std
  *   ssm_conv_decode        <- modules/ssm.py:173-186 (decode step: cache update, SiLU,
  *                             weighted sum, split) and inference/ssm_cache.py:38-43
  *                             SSMCache.update
@@ -306,6 +311,51 @@ int sattn_decode_step(const void* q_rot, const void* k_rot, const void* v, const
 int sattn_prefill_fwd(const void* q_rot, const void* k_rot, const void* v, const float* log_gate, void* out,
                       int64_t batch, int64_t nheads, int64_t seqlen, int64_t head_dim, float scale, int32_t dtype,
                       int32_t impl, void* stream);
+
+/*
+ * Selective attention in training mode (modules/selective_attention.py:232-280 with
+ * self.training) and its backward. Forward, per head h over the batch:
+ *   S_ij      = scale * q_i . k_j  (j <= i when is_causal)
+ *   mean, std = over the valid scores: i, j < lengths[b] (and j <= i when causal)
+ *   log_gate  = log(select_gate) * (std * log_gate_penalty), -inf for j >= lengths[b]
+ *   out_i     = softmax_j(S_ij + (j != i ? log_gate_j : 0)) . v
+ *   q_rot, k_rot, v, out  (b, H, L, D)  dtype, 16-byte aligned
+ *   select_gate           (b, H, L)     dtype (the sigmoid gate, transposed as :204)
+ *   lengths               (b,)          int64, or NULL (every position valid)
+ * and, saved for the backward (and for the layer's score_std_ema update, :252-256):
+ *   lse       (b, H, L) fp32  row log-sum-exp of the gated scores
+ *   log_gate  (b, H, L) fp32
+ *   stats     (H, 4)    fp32  mean, std, count of valid scores, and a coefficient the
+ *                             backward fills in
+ * The backward takes dout (b, H, L, D) and writes dq, dk, dv (b, H, L, D) and
+ * dselect_gate (b, H, L), all in dtype, including the path through std (the gates are
+ * scaled by it). head_dim D in {16, 32, 64, 128}; CUDA cores, fp32 arithmetic. Both
+ * calls use p->workspace (>= sattn_train_workspace_size(p)); the backward needs the
+ * forward's out, lse, log_gate and stats unchanged.
+ */
+typedef struct sattn_train_params {
+  int64_t batch, nheads, seqlen, head_dim;
+  int32_t dtype;
+  int32_t is_causal;
+  float scale;
+  float log_gate_penalty;
+  const void* q_rot;
+  const void* k_rot;
+  const void* v;
+  const void* select_gate;
+  const int64_t* lengths;
+  void* out;
+  float* lse;
+  float* log_gate;
+  float* stats;
+  void* workspace;
+  size_t workspace_bytes;
+} sattn_train_params;
+
+size_t sattn_train_workspace_size(const sattn_train_params* p);
+int sattn_train_fwd(const sattn_train_params* p, void* stream);
+int sattn_train_bwd(const sattn_train_params* p, const void* dout, void* dq, void* dk, void* dv,
+                    void* dselect_gate, void* stream);
 
 #ifdef __cplusplus
 }

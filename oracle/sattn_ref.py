@@ -1,7 +1,8 @@
-"""CPU restatement of the selective-attention decode step (TEST INFRASTRUCTURE ONLY).
+"""CPU restatement of selective attention: decode step, inference prefill and the
+training-mode forward (TEST INFRASTRUCTURE ONLY).
 
-Parity checker for the CUDA decode kernel (``csrc/sattn.cu``). Imported only by
-``tests/`` and ``bench.py``'s CPU legs; the product never imports it.
+Parity checker for the CUDA kernels (``csrc/sattn.cu``, ``csrc/sattn_train.cu``). Imported
+only by ``tests/`` and ``bench.py``'s CPU legs; the product never imports it.
 
 Follows nmquan1503/selective-attention (paths relative to ``src/selective_attention/``):
 - ``inference/selective_attn_cache.py:27-42`` ``SelectiveAttnCache.update_kv``: the new
@@ -68,3 +69,37 @@ def prefill_attention(q_rot, k_rot, v, log_gate, scale, dtype=torch.float32):
     attn = attn + log_gate.to(dtype).unsqueeze(2)
     attn[:, :, diag, diag] = d
     return torch.softmax(attn, dim=-1) @ v.to(dtype)
+
+
+def train_attention(q_rot, k_rot, v, select_gate, log_gate_penalty, lengths=None, is_causal=True, scale=None,
+                    dtype=torch.float32):
+    """``SelectiveMHA.forward`` with ``self.training`` from the score matrix to ``attn_weight @ v``
+    (``modules/selective_attention.py:232-280``), differentiable with torch autograd (the
+    reference's backward is autograd over these same lines). Shapes: ``q_rot, k_rot, v``
+    ``(b, H, L, D)``, ``select_gate`` ``(b, H, L)``, ``lengths`` ``(b,)`` or ``None``.
+    Returns ``(out, std)``.
+    """
+    b, H, L, D = q_rot.shape
+    scale = D ** -0.5 if scale is None else scale
+    q, k, vv = (t.to(dtype) for t in (q_rot, k_rot, v))
+    attn = (q @ k.transpose(-2, -1)) * scale                                        # :89-90
+    if is_causal:                                                                    # :92-98
+        attn = attn.masked_fill(torch.triu(torch.ones(L, L, dtype=torch.bool), diagonal=1), float("-inf"))
+    valid = attn != float("-inf")                                                    # :235
+    pad = None
+    if lengths is not None:
+        pad = torch.arange(L).unsqueeze(0) >= lengths.to(torch.long).unsqueeze(1)    # :208
+        valid = valid & ~pad[:, None, :, None] & ~pad[:, None, None, :]              # :236-237
+    count = valid.sum(dim=(0, 2, 3)).to(dtype)                                       # :238
+    vs = attn.masked_fill(~valid, 0.0)
+    mean = vs.sum(dim=(0, 2, 3)) / count.clamp(min=1)                                # :242-246
+    var = vs.square().sum(dim=(0, 2, 3)) / count.clamp(min=1) - mean.square()       # :247-250
+    std = var.clamp(min=0).sqrt()                                                    # :251
+    lg = torch.log(select_gate.to(dtype)) * (std[None, :, None] * log_gate_penalty)  # :259-263
+    if pad is not None:
+        lg = lg.masked_fill(pad.unsqueeze(1), float("-inf"))                         # :265-269
+    diag = torch.arange(L)                                                           # :134-142 (training)
+    d = attn[:, :, diag, diag]
+    attn = attn + lg.unsqueeze(2)
+    attn[:, :, diag, diag] = d
+    return torch.softmax(attn, dim=-1) @ vv, std                                     # :144, :278

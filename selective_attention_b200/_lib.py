@@ -49,6 +49,9 @@ EXPORTS = {
     "sattn_decode_step": (c_int, [c_void_p] * 7 + [c_int64, c_int64, c_void_p] + [c_int64] * 3
                           + [c_float, c_int32, c_void_p]),
     "sattn_prefill_fwd": (c_int, [c_void_p] * 5 + [c_int64] * 4 + [c_float, c_int32, c_int32, c_void_p]),
+    "sattn_train_workspace_size": (c_size_t, [c_void_p]),
+    "sattn_train_fwd": (c_int, [c_void_p, c_void_p]),
+    "sattn_train_bwd": (c_int, [c_void_p] * 7),
 }
 
 
@@ -75,6 +78,18 @@ class SSDBwdParams(ctypes.Structure):
         ("y_grad", c_void_p), ("y_grad_dtype", c_int32), ("h_last_grad", c_void_p), ("u_grad", c_void_p),
         ("A_grad", c_void_p), ("B_grad", c_void_p), ("C_grad", c_void_p), ("delta_raw_grad", c_void_p),
         ("delta_bias_grad", c_void_p), ("h_init_grad", c_void_p),
+    ]
+
+
+class SattnTrainParams(ctypes.Structure):
+    """Mirror of ``sattn_train_params`` in include/ssd_b200.h."""
+
+    _fields_ = [
+        ("batch", c_int64), ("nheads", c_int64), ("seqlen", c_int64), ("head_dim", c_int64),
+        ("dtype", c_int32), ("is_causal", c_int32), ("scale", c_float), ("log_gate_penalty", c_float),
+        ("q_rot", c_void_p), ("k_rot", c_void_p), ("v", c_void_p), ("select_gate", c_void_p), ("lengths", c_void_p),
+        ("out", c_void_p), ("lse", c_void_p), ("log_gate", c_void_p), ("stats", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
     ]
 
 

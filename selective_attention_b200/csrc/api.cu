@@ -528,3 +528,92 @@ int sattn_prefill_fwd(const void* q_rot, const void* k_rot, const void* v, const
 }
 
 }  // extern "C"
+
+namespace {
+
+// Checks the training-attention parameters and carves the workspace (base NULL: size only).
+int train_args(const sattn_train_params* p, SattnTrainArgs* a, size_t* need) {
+  if (!p) return SSD_ERR_INVALID_ARGUMENT;
+  if (p->batch <= 0 || p->nheads <= 0 || p->seqlen <= 0 || p->batch > 65535 || p->nheads > 65535 ||
+      p->seqlen > (1ll << 30))
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (!sattn_train_supported((int)p->head_dim)) return SSD_ERR_INVALID_ARGUMENT;
+  if (!dtype_ok(p->dtype)) return SSD_ERR_UNSUPPORTED_DTYPE;
+  const size_t B = (size_t)p->batch, H = (size_t)p->nheads, L = (size_t)p->seqlen;
+  const size_t nt = (L + 63) / 64;
+  uint8_t* base = reinterpret_cast<uint8_t*>(p->workspace);
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    uint8_t* ptr = base ? base + off : nullptr;
+    off += align_up(n);
+    return ptr;
+  };
+  a->part = reinterpret_cast<double*>(take(B * H * nt * 2 * sizeof(double)));
+  a->Di = reinterpret_cast<float*>(take(B * H * L * sizeof(float)));
+  a->dlg = reinterpret_cast<float*>(take(B * H * L * sizeof(float)));
+  *need = off;
+  a->B = (int)B;
+  a->H = (int)H;
+  a->L = (int)L;
+  a->D = (int)p->head_dim;
+  a->dtype = p->dtype;
+  a->causal = p->is_causal ? 1 : 0;
+  a->scale = p->scale;
+  a->penalty = p->log_gate_penalty;
+  a->q = p->q_rot;
+  a->k = p->k_rot;
+  a->v = p->v;
+  a->gate = p->select_gate;
+  a->lengths = p->lengths;
+  a->out = p->out;
+  a->lse = p->lse;
+  a->lg = p->log_gate;
+  a->stats = p->stats;
+  return SSD_OK;
+}
+
+int train_common_checks(const sattn_train_params* p, const SattnTrainArgs& a, size_t need) {
+  if (!p->q_rot || !p->k_rot || !p->v || !p->select_gate || !p->out || !p->lse || !p->log_gate || !p->stats ||
+      !p->workspace)
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (!aligned16(p->q_rot) || !aligned16(p->k_rot) || !aligned16(p->v) || !aligned16(p->out))
+    return SSD_ERR_INVALID_ARGUMENT;
+  if (p->workspace_bytes < need) return SSD_ERR_WORKSPACE_TOO_SMALL;
+  (void)a;
+  return SSD_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t sattn_train_workspace_size(const sattn_train_params* p) {
+  SattnTrainArgs a{};
+  size_t need = 0;
+  sattn_train_params q = p ? *p : sattn_train_params{};
+  q.workspace = nullptr;
+  return train_args(&q, &a, &need) == SSD_OK ? need : 0;
+}
+
+int sattn_train_fwd(const sattn_train_params* p, void* stream) {
+  SattnTrainArgs a{};
+  size_t need = 0;
+  int st = train_args(p, &a, &need);
+  if (st) return st;
+  if ((st = train_common_checks(p, a, need))) return st;
+  return cuda_status(launch_sattn_train_fwd(a, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+int sattn_train_bwd(const sattn_train_params* p, const void* dout, void* dq, void* dk, void* dv, void* dselect_gate,
+                    void* stream) {
+  SattnTrainArgs a{};
+  size_t need = 0;
+  int st = train_args(p, &a, &need);
+  if (st) return st;
+  if ((st = train_common_checks(p, a, need))) return st;
+  if (!dout || !dq || !dk || !dv || !dselect_gate) return SSD_ERR_INVALID_ARGUMENT;
+  if (!aligned16(dout)) return SSD_ERR_INVALID_ARGUMENT;
+  return cuda_status(launch_sattn_train_bwd(a, dout, dq, dk, dv, dselect_gate, reinterpret_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -81,6 +81,29 @@ cudaError_t launch_sattn_prefill(const void* q, const void* k, const void* v, co
                                  int L, int D, float scale, int dtype, int use_tc, cudaStream_t s);
 unsigned int fetch_error_sattn(cudaStream_t s);
 
+// sattn_train.cu (training-mode selective attention and its backward; CUDA cores)
+struct SattnTrainArgs {
+  int B, H, L, D, dtype, causal;
+  float scale, penalty;
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* gate;
+  const int64_t* lengths;
+  void* out;
+  float* lse;
+  float* lg;
+  float* stats;
+  // workspace
+  double* part;  // (B, H, L / 64, 2) per query tile: sum and sum of squares of the valid scores
+  float* Di;     // (B, H, L) dout . out
+  float* dlg;    // (B, H, L) gradient of the log-gates
+};
+bool sattn_train_supported(int D);
+cudaError_t launch_sattn_train_fwd(const SattnTrainArgs& a, cudaStream_t s);
+cudaError_t launch_sattn_train_bwd(const SattnTrainArgs& a, const void* dout, void* dq, void* dk, void* dv,
+                                   void* dgate, cudaStream_t s);
+
 // ssd_tc.cu (tcgen05 + TMA; bf16/fp16 inputs, P = 64, N = 128, cs = 256; prev16 in the input type)
 bool tc_supported(int x_dtype, int P, int N, int cs);
 // delta_raw == NULL: dt / cum are inputs; otherwise chunk_cumsum is fused in and they are written.

@@ -1,0 +1,596 @@
+// sattn_train.cu - training-mode selective attention and its backward, on CUDA cores.
+//
+// SelectiveMHA.forward with self.training (modules/selective_attention.py:232-280):
+//   S[i,j]   = scale q_i . k_j, causal (j <= i) or not                       (_build_attn_matrix :89-99)
+//   stats    = mean and std over the valid scores of each head: i, j below the row's length
+//              (and j <= i when causal), over batch and both positions       (:234-251)
+//   lg[j]    = log(select_gate[j]) std penalty, -inf for keys past the length (:259-268)
+//   P[i,:]   = softmax_j(S[i,j] + lg[j] for j != i, S[i,i] on the diagonal)   (_gated_softmax :125-144)
+//   out[i]   = sum_j P[i,j] v_j                                               (:278)
+// The std feeds the gate, so the backward has a path through the statistics:
+//   dlg[j]   = sum_{i != j} dS[i,j],  dS = P (dP - D_i),  dP = dO v^T,  D_i = dO_i . out_i
+//   dstd     = sum_{b, j < len} dlg[j] log(g[j]) penalty;  d select_gate[j] = dlg[j] std penalty / g[j]
+//   dS_total = dS + c (S - mean) on valid scores,  c = dstd / (count std)  (d std / d S = (S - mean) / (count std))
+//   dq_i = scale sum_j dS_total[i,j] k_j,  dk_j = scale sum_i dS_total[i,j] q_i,  dv_j = sum_i P[i,j] dO_i
+//
+// Kernels (all 64 x 64 tiles, 256 threads, fp32 arithmetic on any input type):
+//   stats      per (query tile, head, row): sums of the valid scores and of their squares
+//   stats_fin  per head: mean, std, count (fp64 sums)
+//   gate       lg = log(g) std penalty, -inf past the length
+//   fwd        online-softmax attention with the row log-sum-exp saved (flash style)
+//   rowdot     D_i = dO_i . out_i
+//   dv         per key tile over the query tiles: dv and dlg
+//   fin        per head: dstd, c, d select_gate
+//   dk         per key tile: dk with dS_total
+//   dq         per query tile: dq with dS_total
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sattn_tiles.cuh"
+
+namespace ssdb200 {
+namespace {
+
+constexpr int kLDT = kPT + 4;  // fp32 64 x 64 score tiles
+
+// sc[a][c] = sum_d A[ra + 16 a][d] * Bm[rb + 16 c][d] over the staged rows (ld floats apart).
+__device__ __forceinline__ void tile_dot(float (&sc)[4][4], const float* A, const float* Bm, int ld, int ra, int rb,
+                                         int D) {
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) sc[a][c] = 0.f;
+  for (int d = 0; d < D; d += 4) {
+    float4 x[4], y[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) x[a] = *reinterpret_cast<const float4*>(A + (ra + 16 * a) * ld + d);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) y[c] = *reinterpret_cast<const float4*>(Bm + (rb + 16 * c) * ld + d);
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float t = sc[a][c];
+        t = fmaf(x[a].x, y[c].x, t);
+        t = fmaf(x[a].y, y[c].y, t);
+        t = fmaf(x[a].z, y[c].z, t);
+        sc[a][c] = fmaf(x[a].w, y[c].w, t);
+      }
+  }
+}
+
+// acc[a][4 g + e] += sum_r W[wr + 16 a][r] * R[r][dcol[g] + e] over the 64 tile rows r.
+__device__ __forceinline__ void tile_acc(float (&acc)[4][8], const float* W, const float* R, int ld, int wr,
+                                         const int (&dcol)[2]) {
+#pragma unroll 2
+  for (int r = 0; r < kPT; r += 4) {
+    float4 w[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) w[a] = *reinterpret_cast<const float4*>(W + (wr + 16 * a) * kLDT + r);
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      float4 x[2];
+#pragma unroll
+      for (int g = 0; g < 2; ++g) x[g] = *reinterpret_cast<const float4*>(R + (r + rr) * ld + dcol[g]);
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const float p = rr == 0 ? w[a].x : (rr == 1 ? w[a].y : (rr == 2 ? w[a].z : w[a].w));
+#pragma unroll
+        for (int g = 0; g < 2; ++g) {
+          acc[a][4 * g] = fmaf(p, x[g].x, acc[a][4 * g]);
+          acc[a][4 * g + 1] = fmaf(p, x[g].y, acc[a][4 * g + 1]);
+          acc[a][4 * g + 2] = fmaf(p, x[g].z, acc[a][4 * g + 2]);
+          acc[a][4 * g + 3] = fmaf(p, x[g].w, acc[a][4 * g + 3]);
+        }
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ int row_len(const int64_t* lengths, int b, int L) {
+  if (!lengths) return L;
+  const long long n = lengths[b];
+  return n < 0 ? 0 : (n > L ? L : (int)n);
+}
+
+// Key j takes part in query i's softmax: causal order, inside the tensor, and a finite logit
+// (a key past the length has lg = -inf, except on the diagonal, which is not gated).
+__device__ __forceinline__ float logit(float s, int qi, int kj, float g, int L, int causal) {
+  if ((causal && kj > qi) || kj >= L || qi >= L) return -INFINITY;
+  return kj == qi ? s : s + g;
+}
+
+__device__ __forceinline__ bool stat_valid(int qi, int kj, int len, int causal) {
+  return qi < len && kj < len && (!causal || kj <= qi);
+}
+
+template <typename V>
+__device__ __forceinline__ V block_sum256(V v, V* red) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int w = threadIdx.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  __syncthreads();
+  V t = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t += red[i];
+  return t;
+}
+
+__device__ __forceinline__ void dcols(int (&dcol)[2], int tc, int D) {
+#pragma unroll
+  for (int g = 0; g < 2; ++g) dcol[g] = min(4 * tc + 64 * g, D - 4);
+}
+
+template <typename T>
+__device__ __forceinline__ void store_rows(T* dst, const float (&acc)[4][8], int r0, int tr, int tc, int L, int D,
+                                           float mul) {
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int r = r0 + tr + 16 * a;
+    if (r >= L) continue;
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+      const int d = 4 * tc + 64 * g;
+      if (d >= D) continue;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dst[(long long)r * D + d + e] = from_f32<T>(acc[a][4 * g + e] * mul);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------- statistics
+template <typename T>
+__global__ void __launch_bounds__(256) sattn_train_stats_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                                const int64_t* __restrict__ lengths, int H, int L,
+                                                                int D, float scale, int causal, double* part) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  __shared__ double red[8];
+  const int LD = D + 4;
+  float* Qs = sm;
+  float* Ks = Qs + kPT * LD;
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const long long bh = (long long)b * H + h;
+  const int len = row_len(lengths, b, L);
+  const int q0 = qt * kPT, tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  float s1 = 0.f, s2 = 0.f;
+  if (q0 < len) {
+    stage_rows64<T>(Qs, LD, q + bh * L * D, q0, L, D);
+    const int kend = causal ? min(q0 + kPT, len) : len;
+    for (int k0 = 0; k0 < kend; k0 += kPT) {
+      __syncthreads();
+      stage_rows64<T>(Ks, LD, k + bh * L * D, k0, L, D);
+      __syncthreads();
+      float sc[4][4];
+      tile_dot(sc, Qs, Ks, LD, tr, tc, D);
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          if (stat_valid(q0 + tr + 16 * a, k0 + tc + 16 * c, len, causal)) {
+            const float s = sc[a][c] * scale;
+            s1 += s;
+            s2 = fmaf(s, s, s2);
+          }
+    }
+  }
+  const double t1 = block_sum256<double>((double)s1, red);
+  const double t2 = block_sum256<double>((double)s2, red);
+  if (tid == 0) {
+    part[(bh * gridDim.x + qt) * 2] = t1;
+    part[(bh * gridDim.x + qt) * 2 + 1] = t2;
+  }
+}
+
+// stats[h] = (mean, std, count, c): c is filled by the backward.
+__global__ void __launch_bounds__(256) sattn_train_stats_fin_kernel(const double* __restrict__ part,
+                                                                    const int64_t* __restrict__ lengths, int B, int H,
+                                                                    int L, int nqt, int causal, float* stats) {
+  __shared__ double red[8];
+  const int h = blockIdx.x;
+  double s1 = 0.0, s2 = 0.0, n = 0.0;
+  for (int idx = threadIdx.x; idx < B * nqt; idx += 256) {
+    const int b = idx / nqt, qt = idx - b * nqt;
+    const double* p = part + (((long long)b * H + h) * nqt + qt) * 2;
+    s1 += p[0];
+    s2 += p[1];
+  }
+  for (int b = threadIdx.x; b < B; b += 256) {
+    const double len = row_len(lengths, b, L);
+    n += causal ? len * (len + 1.0) * 0.5 : len * len;
+  }
+  s1 = block_sum256<double>(s1, red);
+  s2 = block_sum256<double>(s2, red);
+  n = block_sum256<double>(n, red);
+  if (threadIdx.x == 0) {
+    const double N = n < 1.0 ? 1.0 : n;  // count.clamp(min=1) (:245-250)
+    const double mean = s1 / N;
+    const double var = s2 / N - mean * mean;
+    stats[h * 4] = (float)mean;
+    stats[h * 4 + 1] = (float)sqrt(var > 0.0 ? var : 0.0);
+    stats[h * 4 + 2] = (float)n;
+    stats[h * 4 + 3] = 0.f;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) sattn_train_gate_kernel(const T* __restrict__ gate,
+                                                               const int64_t* __restrict__ lengths,
+                                                               const float* __restrict__ stats, int H, int L,
+                                                               long long n, float penalty, float* __restrict__ lg) {
+  const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n) return;
+  const int j = (int)(i % L);
+  const long long bh = i / L;
+  const int h = (int)(bh % H), b = (int)(bh / H);
+  lg[i] = j < row_len(lengths, b, L) ? logf(to_f32<T>(gate[i])) * stats[h * 4 + 1] * penalty : -INFINITY;
+}
+
+// ---------------------------------------------------------------------------- forward
+template <typename T>
+__global__ void __launch_bounds__(256) sattn_train_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k,
+                                                              const T* __restrict__ v, const float* __restrict__ lg,
+                                                              T* __restrict__ out, float* __restrict__ lse, int H,
+                                                              int L, int D, float scale, int causal) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int LD = D + 4;
+  float* Qs = sm;
+  float* Ks = Qs + kPT * LD;
+  float* Vs = Ks + kPT * LD;
+  float* Ps = Vs + kPT * LD;  // [64][kLDT]
+  float* gs = Ps + kPT * kLDT;
+  const int nt = (int)gridDim.x;
+  const int qt = causal ? nt - 1 - (int)blockIdx.x : (int)blockIdx.x;  // causal: longest rows first
+  const long long bh = (long long)blockIdx.z * H + blockIdx.y;
+  const int q0 = qt * kPT, tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  stage_rows64<T>(Qs, LD, q + bh * L * D, q0, L, D);
+  float o[4][8], m[4], l[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    m[a] = -INFINITY;
+    l[a] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[a][e] = 0.f;
+  }
+  int dcol[2];
+  dcols(dcol, tc, D);
+  const int kend = causal ? qt + 1 : nt;
+  for (int kt = 0; kt < kend; ++kt) {
+    const int k0 = kt * kPT;
+    __syncthreads();
+    stage_rows64<T>(Ks, LD, k + bh * L * D, k0, L, D);
+    stage_rows64<T>(Vs, LD, v + bh * L * D, k0, L, D);
+    if (tid < kPT) gs[tid] = k0 + tid < L ? lg[bh * L + k0 + tid] : -INFINITY;
+    __syncthreads();
+    float sc[4][4];
+    tile_dot(sc, Qs, Ks, LD, tr, tc, D);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int qi = q0 + tr + 16 * a;
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        sc[a][c] = logit(sc[a][c] * scale, qi, k0 + tc + 16 * c, gs[tc + 16 * c], L, causal);
+        rmax = fmaxf(rmax, sc[a][c]);
+      }
+      rmax = hw_max(rmax);
+      const float mn = fmaxf(m[a], rmax);
+      const float corr = m[a] == -INFINITY ? 0.f : expf(m[a] - mn);
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float p = sc[a][c] == -INFINITY ? 0.f : expf(sc[a][c] - mn);
+        rs += p;
+        Ps[(tr + 16 * a) * kLDT + tc + 16 * c] = p;
+      }
+      l[a] = l[a] * corr + hw_sum(rs);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[a][e] *= corr;
+      m[a] = mn;
+    }
+    __syncthreads();
+    tile_acc(o, Ps, Vs, LD, tr, dcol);
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int qi = q0 + tr + 16 * a;
+    if (qi < L && tc == 0) lse[bh * L + qi] = m[a] + logf(l[a]);
+    const float inv = 1.0f / l[a];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[a][e] *= inv;
+  }
+  store_rows<T>(out + bh * L * D, o, q0, tr, tc, L, D, 1.f);
+}
+
+// ---------------------------------------------------------------------------- backward
+// D_i = dO_i . out_i, one warp per row.
+template <typename T>
+__global__ void __launch_bounds__(256) sattn_train_rowdot_kernel(const T* __restrict__ dout, const T* __restrict__ out,
+                                                                 long long rows, int D, float* __restrict__ Di) {
+  const long long r = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  float s = 0.f;
+  for (int d = lane; d < D; d += 32) s = fmaf(to_f32<T>(dout[r * D + d]), to_f32<T>(out[r * D + d]), s);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) Di[r] = s;
+}
+
+// Key-major sweep: thread (tk, tq) owns keys k0 + tk + 16 a and, per query tile, queries
+// q0 + tq + 16 c. MODE 0: dv and dlg (softmax part of dS). MODE 1: dk with dS_total.
+template <typename T, int MODE>
+__global__ void __launch_bounds__(256) sattn_train_bwd_kv_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ dout,
+    const float* __restrict__ lg, const float* __restrict__ lse, const float* __restrict__ Di,
+    const float* __restrict__ stats, const int64_t* __restrict__ lengths, int H, int L, int D, float scale,
+    int causal, T* __restrict__ dkv, float* __restrict__ dlg) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int LD = D + 4;
+  float* Ks = sm;
+  float* Vs = Ks + kPT * LD;
+  float* Qs = Vs + kPT * LD;
+  float* Os = Qs + kPT * LD;    // dO tile
+  float* Wt = Os + kPT * LD;    // [key][query]: P^T (MODE 0) or dS_total^T (MODE 1)
+  float* ls = Wt + kPT * kLDT;  // lse of the query tile
+  float* ds = ls + kPT;         // D_i of the query tile
+  const int nt = (int)gridDim.x, kt = (int)blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const long long bh = (long long)b * H + h;
+  const int len = row_len(lengths, b, L);
+  const int k0 = kt * kPT, tid = threadIdx.x, tk = tid >> 4, tq = tid & 15;
+  const float mean = stats[h * 4], c_st = stats[h * 4 + 3];
+  stage_rows64<T>(Ks, LD, k + bh * L * D, k0, L, D);
+  stage_rows64<T>(Vs, LD, v + bh * L * D, k0, L, D);
+  float g[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int kj = k0 + tk + 16 * a;
+    g[a] = kj < L ? lg[bh * L + kj] : -INFINITY;
+  }
+  float acc[4][8], dl[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    dl[a] = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[a][e] = 0.f;
+  }
+  int dcol[2];
+  dcols(dcol, tq, D);
+  for (int qt = causal ? kt : 0; qt < nt; ++qt) {
+    const int q0 = qt * kPT;
+    __syncthreads();
+    stage_rows64<T>(Qs, LD, q + bh * L * D, q0, L, D);
+    stage_rows64<T>(Os, LD, dout + bh * L * D, q0, L, D);
+    if (tid < kPT) {
+      ls[tid] = q0 + tid < L ? lse[bh * L + q0 + tid] : 0.f;
+      ds[tid] = q0 + tid < L ? Di[bh * L + q0 + tid] : 0.f;
+    }
+    __syncthreads();
+    float st[4][4], dp[4][4];
+    tile_dot(st, Ks, Qs, LD, tk, tq, D);
+    tile_dot(dp, Vs, Os, LD, tk, tq, D);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int kj = k0 + tk + 16 * a;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int qi = q0 + tq + 16 * c;
+        const float s = st[a][c] * scale;
+        const float x = logit(s, qi, kj, g[a], L, causal);
+        const float p = x == -INFINITY ? 0.f : expf(x - ls[tq + 16 * c]);
+        const float dsm = p * (dp[a][c] - ds[tq + 16 * c]);
+        float w;
+        if (MODE == 0) {
+          if (kj != qi) dl[a] += dsm;
+          w = p;
+        } else {
+          w = dsm + (stat_valid(qi, kj, len, causal) ? c_st * (s - mean) : 0.f);
+        }
+        Wt[(tk + 16 * a) * kLDT + tq + 16 * c] = w;
+      }
+    }
+    __syncthreads();
+    tile_acc(acc, Wt, MODE == 0 ? Os : Qs, LD, tk, dcol);
+  }
+  if (MODE == 0) {
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const float t = hw_sum(dl[a]);
+      const int kj = k0 + tk + 16 * a;
+      if (tq == 0 && kj < L) dlg[bh * L + kj] = t;
+    }
+  }
+  store_rows<T>(dkv + bh * L * D, acc, k0, tk, tq, L, D, MODE == 0 ? 1.f : scale);
+}
+
+// Per head: dstd, the statistics coefficient c, and d select_gate.
+template <typename T>
+__global__ void __launch_bounds__(256) sattn_train_bwd_fin_kernel(const T* __restrict__ gate,
+                                                                  const int64_t* __restrict__ lengths,
+                                                                  const float* __restrict__ dlg, int B, int H, int L,
+                                                                  float penalty, float* stats, T* __restrict__ dgate) {
+  __shared__ double red[8];
+  const int h = blockIdx.x;
+  const float sd = stats[h * 4 + 1];
+  double acc = 0.0;
+  for (long long idx = threadIdx.x; idx < (long long)B * L; idx += 256) {
+    const int b = (int)(idx / L), j = (int)(idx - (long long)b * L);
+    const long long i = ((long long)b * H + h) * L + j;
+    float dg = 0.f;
+    if (j < row_len(lengths, b, L)) {
+      const float gv = to_f32<T>(gate[i]);
+      acc += (double)dlg[i] * (double)logf(gv) * (double)penalty;
+      dg = dlg[i] * sd * penalty / gv;
+    }
+    dgate[i] = from_f32<T>(dg);
+  }
+  acc = block_sum256<double>(acc, red);
+  if (threadIdx.x == 0) {
+    const double n = stats[h * 4 + 2] < 1.f ? 1.0 : (double)stats[h * 4 + 2];
+    stats[h * 4 + 3] = sd > 0.f ? (float)(acc / (n * (double)sd)) : 0.f;
+  }
+}
+
+// Query-major sweep for dq: thread (tr, tc) owns queries q0 + tr + 16 a, keys k0 + tc + 16 c.
+template <typename T>
+__global__ void __launch_bounds__(256) sattn_train_bwd_q_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const T* __restrict__ dout,
+    const float* __restrict__ lg, const float* __restrict__ lse, const float* __restrict__ Di,
+    const float* __restrict__ stats, const int64_t* __restrict__ lengths, int H, int L, int D, float scale,
+    int causal, T* __restrict__ dq) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int LD = D + 4;
+  float* Qs = sm;
+  float* Os = Qs + kPT * LD;
+  float* Ks = Os + kPT * LD;
+  float* Vs = Ks + kPT * LD;
+  float* Ws = Vs + kPT * LD;  // dS_total [query][key]
+  float* gs = Ws + kPT * kLDT;
+  const int nt = (int)gridDim.x;
+  const int qt = causal ? nt - 1 - (int)blockIdx.x : (int)blockIdx.x;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const long long bh = (long long)b * H + h;
+  const int len = row_len(lengths, b, L);
+  const int q0 = qt * kPT, tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  const float mean = stats[h * 4], c_st = stats[h * 4 + 3];
+  stage_rows64<T>(Qs, LD, q + bh * L * D, q0, L, D);
+  stage_rows64<T>(Os, LD, dout + bh * L * D, q0, L, D);
+  float lr[4], dr[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int qi = q0 + tr + 16 * a;
+    lr[a] = qi < L ? lse[bh * L + qi] : 0.f;
+    dr[a] = qi < L ? Di[bh * L + qi] : 0.f;
+  }
+  float acc[4][8];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[a][e] = 0.f;
+  int dcol[2];
+  dcols(dcol, tc, D);
+  const int kend = causal ? qt + 1 : nt;
+  for (int kt = 0; kt < kend; ++kt) {
+    const int k0 = kt * kPT;
+    __syncthreads();
+    stage_rows64<T>(Ks, LD, k + bh * L * D, k0, L, D);
+    stage_rows64<T>(Vs, LD, v + bh * L * D, k0, L, D);
+    if (tid < kPT) gs[tid] = k0 + tid < L ? lg[bh * L + k0 + tid] : -INFINITY;
+    __syncthreads();
+    float sc[4][4], dp[4][4];
+    tile_dot(sc, Qs, Ks, LD, tr, tc, D);
+    tile_dot(dp, Os, Vs, LD, tr, tc, D);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int qi = q0 + tr + 16 * a;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int kj = k0 + tc + 16 * c;
+        const float s = sc[a][c] * scale;
+        const float x = logit(s, qi, kj, gs[tc + 16 * c], L, causal);
+        const float p = x == -INFINITY ? 0.f : expf(x - lr[a]);
+        Ws[(tr + 16 * a) * kLDT + tc + 16 * c] =
+            p * (dp[a][c] - dr[a]) + (stat_valid(qi, kj, len, causal) ? c_st * (s - mean) : 0.f);
+      }
+    }
+    __syncthreads();
+    tile_acc(acc, Ws, Ks, LD, tr, dcol);
+  }
+  store_rows<T>(dq + bh * L * D, acc, q0, tr, tc, L, D, scale);
+}
+
+template <typename T>
+cudaError_t train_fwd_t(const SattnTrainArgs& a, cudaStream_t s) {
+  const int H = a.H, L = a.L, D = a.D, nt = (L + kPT - 1) / kPT;
+  const size_t LDf = (size_t)(D + 4);
+  const size_t sm_stats = 2 * kPT * LDf * sizeof(float);
+  const size_t sm_fwd = (3 * kPT * LDf + kPT * kLDT + kPT) * sizeof(float);
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(sattn_train_stats_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sm_stats)))
+    return e;
+  if ((e = cudaFuncSetAttribute(sattn_train_fwd_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_fwd)))
+    return e;
+  const dim3 grid((unsigned)nt, (unsigned)H, (unsigned)a.B);
+  sattn_train_stats_kernel<T><<<grid, 256, sm_stats, s>>>((const T*)a.q, (const T*)a.k, a.lengths, H, L, D, a.scale,
+                                                          a.causal, a.part);
+  if ((e = cudaGetLastError())) return e;
+  sattn_train_stats_fin_kernel<<<(unsigned)H, 256, 0, s>>>(a.part, a.lengths, a.B, H, L, nt, a.causal, a.stats);
+  if ((e = cudaGetLastError())) return e;
+  const long long n = (long long)a.B * H * L;
+  sattn_train_gate_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const T*)a.gate, a.lengths, a.stats, H, L, n,
+                                                                         a.penalty, a.lg);
+  if ((e = cudaGetLastError())) return e;
+  sattn_train_fwd_kernel<T><<<grid, 256, sm_fwd, s>>>((const T*)a.q, (const T*)a.k, (const T*)a.v, a.lg, (T*)a.out,
+                                                      a.lse, H, L, D, a.scale, a.causal);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t train_bwd_t(const SattnTrainArgs& a, const void* dout, void* dq, void* dk, void* dv, void* dgate,
+                        cudaStream_t s) {
+  const int H = a.H, L = a.L, D = a.D, nt = (L + kPT - 1) / kPT;
+  const size_t LDf = (size_t)(D + 4);
+  const size_t sm_kv = (4 * kPT * LDf + kPT * kLDT + 2 * kPT) * sizeof(float);
+  const size_t sm_q = (4 * kPT * LDf + kPT * kLDT + kPT) * sizeof(float);
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(sattn_train_bwd_kv_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sm_kv)))
+    return e;
+  if ((e = cudaFuncSetAttribute(sattn_train_bwd_kv_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)sm_kv)))
+    return e;
+  if ((e = cudaFuncSetAttribute(sattn_train_bwd_q_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_q)))
+    return e;
+  const long long rows = (long long)a.B * H * L;
+  sattn_train_rowdot_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>((const T*)dout, (const T*)a.out, rows, D,
+                                                                          a.Di);
+  if ((e = cudaGetLastError())) return e;
+  const dim3 grid((unsigned)nt, (unsigned)H, (unsigned)a.B);
+  sattn_train_bwd_kv_kernel<T, 0><<<grid, 256, sm_kv, s>>>((const T*)a.q, (const T*)a.k, (const T*)a.v,
+                                                           (const T*)dout, a.lg, a.lse, a.Di, a.stats, a.lengths, H,
+                                                           L, D, a.scale, a.causal, (T*)dv, a.dlg);
+  if ((e = cudaGetLastError())) return e;
+  sattn_train_bwd_fin_kernel<T><<<(unsigned)H, 256, 0, s>>>((const T*)a.gate, a.lengths, a.dlg, a.B, H, L, a.penalty,
+                                                            a.stats, (T*)dgate);
+  if ((e = cudaGetLastError())) return e;
+  sattn_train_bwd_kv_kernel<T, 1><<<grid, 256, sm_kv, s>>>((const T*)a.q, (const T*)a.k, (const T*)a.v,
+                                                           (const T*)dout, a.lg, a.lse, a.Di, a.stats, a.lengths, H,
+                                                           L, D, a.scale, a.causal, (T*)dk, nullptr);
+  if ((e = cudaGetLastError())) return e;
+  sattn_train_bwd_q_kernel<T><<<grid, 256, sm_q, s>>>((const T*)a.q, (const T*)a.k, (const T*)a.v, (const T*)dout,
+                                                      a.lg, a.lse, a.Di, a.stats, a.lengths, H, L, D, a.scale,
+                                                      a.causal, (T*)dq);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool sattn_train_supported(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
+
+cudaError_t launch_sattn_train_fwd(const SattnTrainArgs& a, cudaStream_t s) {
+  switch (a.dtype) {
+    case SSD_F32: return train_fwd_t<float>(a, s);
+    case SSD_BF16: return train_fwd_t<__nv_bfloat16>(a, s);
+    case SSD_F16: return train_fwd_t<__half>(a, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_sattn_train_bwd(const SattnTrainArgs& a, const void* dout, void* dq, void* dk, void* dv,
+                                   void* dgate, cudaStream_t s) {
+  switch (a.dtype) {
+    case SSD_F32: return train_bwd_t<float>(a, dout, dq, dk, dv, dgate, s);
+    case SSD_BF16: return train_bwd_t<__nv_bfloat16>(a, dout, dq, dk, dv, dgate, s);
+    case SSD_F16: return train_bwd_t<__half>(a, dout, dq, dk, dv, dgate, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace ssdb200

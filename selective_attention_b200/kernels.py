@@ -503,3 +503,81 @@ def sattn_prefill(q_rot, k_rot, v, log_gate, scale=None, out=None, impl: str = "
                                       _lib.IMPLS[impl], _stream(dev))
     _lib.check(st, "sattn_prefill")
     return out
+
+
+def _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_causal, scale):
+    b, H, L, D = q_rot.shape
+    dev = check_cuda([q_rot, k_rot, v, select_gate, lengths], ["q_rot", "k_rot", "v", "select_gate", "lengths"])
+    for t, n in ((k_rot, "k_rot"), (v, "v")):
+        if tuple(t.shape) != (b, H, L, D):
+            raise ValueError(f"[{n}] expected shape {(b, H, L, D)}, got {tuple(t.shape)}")
+        if t.dtype != q_rot.dtype:
+            raise ValueError(f"[{n}] dtype {t.dtype} differs from q_rot's {q_rot.dtype}")
+    if tuple(select_gate.shape) != (b, H, L):
+        raise ValueError(f"[select_gate] expected shape {(b, H, L)}, got {tuple(select_gate.shape)}")
+    if lengths is not None and tuple(lengths.shape) != (b,):
+        raise ValueError(f"[lengths] expected shape {(b,)}, got {tuple(lengths.shape)}")
+    q_rot, k_rot, v = (_aligned16(to_contiguous(t)) for t in (q_rot, k_rot, v))
+    select_gate = to_contiguous(select_gate.to(q_rot.dtype))
+    lengths = None if lengths is None else to_contiguous(lengths.to(torch.int64))
+    p = _lib.SattnTrainParams()
+    p.batch, p.nheads, p.seqlen, p.head_dim = b, H, L, D
+    p.dtype = _lib.dtype_code(q_rot.dtype, "q_rot")
+    p.is_causal = 1 if is_causal else 0
+    p.scale = float(D ** -0.5 if scale is None else scale)
+    p.log_gate_penalty = float(log_gate_penalty)
+    p.q_rot, p.k_rot, p.v = _lib.ptr(q_rot), _lib.ptr(k_rot), _lib.ptr(v)
+    p.select_gate, p.lengths = _lib.ptr(select_gate), _lib.ptr(lengths)
+    keep = (q_rot, k_rot, v, select_gate, lengths)
+    return p, dev, keep
+
+
+def sattn_train_forward(q_rot, k_rot, v, select_gate, log_gate_penalty, lengths=None, is_causal=True, scale=None):
+    """Selective attention in training mode (C-ABI ``sattn_train_fwd``): the part of
+    ``SelectiveMHA.forward`` with ``self.training`` from the score matrix to ``attn_weight @ v``
+    (``modules/selective_attention.py:232-280``).
+
+    ``q_rot, k_rot, v`` ``(b, H, L, D)``; ``select_gate`` ``(b, H, L)`` (the sigmoid gate,
+    transposed as ``:204``); ``lengths`` ``(b,)`` or ``None``. Per head, the mean and std of the
+    valid scores (``:234-251``) scale the log-gates (``:259-268``; ``-inf`` past the length), and
+    the seq-mode gated softmax (``:125-144``) weights ``v``. Returns ``(out, lse, log_gate, stats)``:
+    ``out`` ``(b, H, L, D)`` in ``q_rot``'s dtype; fp32 ``lse`` and ``log_gate`` ``(b, H, L)``;
+    ``stats`` ``(H, 4)`` fp32 = mean, std, count of valid scores, and a slot the backward fills.
+    """
+    p, dev, keep = _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_causal, scale)
+    b, H, L, D = q_rot.shape
+    out = torch.empty(b, H, L, D, device=dev, dtype=q_rot.dtype)
+    lse = torch.empty(b, H, L, device=dev, dtype=torch.float32)
+    lg = torch.empty(b, H, L, device=dev, dtype=torch.float32)
+    stats = torch.empty(H, 4, device=dev, dtype=torch.float32)
+    L_ = _lib.lib()
+    ws = torch.empty(L_.sattn_train_workspace_size(byref(p)), device=dev, dtype=torch.uint8)
+    p.out, p.lse, p.log_gate, p.stats = _lib.ptr(out), _lib.ptr(lse), _lib.ptr(lg), _lib.ptr(stats)
+    p.workspace, p.workspace_bytes = _lib.ptr(ws), ws.numel()
+    _lib.check(L_.sattn_train_fwd(byref(p), _stream(dev)), "sattn_train_fwd")
+    del keep
+    return out, lse, lg, stats
+
+
+def sattn_train_backward(q_rot, k_rot, v, select_gate, out, lse, log_gate, stats, dout, log_gate_penalty,
+                         lengths=None, is_causal=True, scale=None):
+    """Backward of ``sattn_train_forward`` (C-ABI ``sattn_train_bwd``), the gradients torch's
+    autograd gives for ``modules/selective_attention.py:232-280`` including the path through
+    the score std. ``out, lse, log_gate, stats`` are the forward's outputs (``stats`` gets its
+    backward coefficient written). Returns ``(dq, dk, dv, dselect_gate)`` in ``q_rot``'s dtype.
+    """
+    p, dev, keep = _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_causal, scale)
+    dout = _aligned16(to_contiguous(dout.to(q_rot.dtype)))
+    if tuple(dout.shape) != tuple(q_rot.shape):
+        raise ValueError(f"[dout] expected shape {tuple(q_rot.shape)}, got {tuple(dout.shape)}")
+    dq, dk, dv = (torch.empty_like(t, memory_format=torch.contiguous_format) for t in (q_rot, q_rot, q_rot))
+    dgate = torch.empty(select_gate.shape, device=dev, dtype=q_rot.dtype)
+    L_ = _lib.lib()
+    ws = torch.empty(L_.sattn_train_workspace_size(byref(p)), device=dev, dtype=torch.uint8)
+    p.out, p.lse, p.log_gate, p.stats = _lib.ptr(out), _lib.ptr(lse), _lib.ptr(log_gate), _lib.ptr(stats)
+    p.workspace, p.workspace_bytes = _lib.ptr(ws), ws.numel()
+    st = L_.sattn_train_bwd(byref(p), _lib.ptr(dout), _lib.ptr(dq), _lib.ptr(dk), _lib.ptr(dv),
+                            _lib.ptr(dgate), _stream(dev))
+    _lib.check(st, "sattn_train_bwd")
+    del keep
+    return dq, dk, dv, dgate
