@@ -562,6 +562,7 @@ def run_ours(args, rank, world, local):
         if not args.no_sattn:
             line["sattn_decode"] = sattn_measure(args, dev, flush, hbm_peak)
             line["sattn_prefill"] = sattn_prefill_measure(args, dev, flush, peaks.get("bf16_tflops", 1590.0))
+            line["sattn_train"] = sattn_train_measure(args, dev, flush)
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
@@ -694,8 +695,10 @@ FFMA_NOMINAL_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12  # CUDA-core fp32 FMA, nomi
 def bwd_measure(args, cfg, inp, dev, flush):
     """SSD backward (row f1) on the bench workload's inputs: y_grad fp32 (the reference's
     y dtype) and h_last_grad, through ``kernels.ssd_scan_backward`` (the C-ABI
-    ``ssd_scan_bwd``). CUDA-core kernels: reported in TFLOP/s of the algorithmic fp32
-    FLOPs against the nominal FFMA rate, with the per-stage split from the C-ABI's events."""
+    ``ssd_scan_bwd``). For 16-bit u / B / C at headdim 64, dstate 128, chunk 256 (the bench
+    workload) the contractions run on tcgen05 with 16-bit operands; reported in TFLOP/s of
+    the algorithmic FLOPs, with the per-stage split from the C-ABI's events. The FFMA
+    fraction is kept for comparison with the CUDA-core path."""
     from selective_attention_b200 import kernels
 
     u, A, B, C, dr = inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"]
@@ -814,6 +817,45 @@ def sattn_prefill_measure(args, dev, flush, tc_peak):
         res[impl] = {"ms_per_step": ms, "tflops": tf, "peak_tflops": peak, "peak": peak_name, "frac": tf / peak,
                      "steps": steps}
     return res
+
+
+def sattn_train_measure(args, dev, flush):
+    """Selective attention in training mode (row f4, training): b 2, H 16, L 2048, head_dim 64,
+    causal, ragged lengths, bf16 inputs; one step = ``SelectiveAttnTrainFn`` forward + backward.
+    TFLOP/s of the algorithmic FLOPs over the valid causal pairs (forward: statistics
+    q k^T, attention q k^T and P v = 3 x 2 L^2 D / 2; backward as the reference's autograd runs
+    it: q k^T recompute, dO v^T, dv, dq, dk = 5 x 2 L^2 D / 2) against the nominal FFMA rate:
+    these kernels run on CUDA cores in fp32."""
+    import selective_attention_b200 as sab
+
+    b, H, L, D = 2, 16, 2048, 64
+    g = torch.Generator(device=dev).manual_seed(5)
+    q, k, v = (torch.randn(b, H, L, D, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+               for _ in range(3))
+    sel = torch.sigmoid(torch.randn(b, H, L, device=dev, generator=g) + 2.0).to(torch.bfloat16).requires_grad_(True)
+    lengths = torch.tensor([L, 3 * L // 4], device=dev)
+    dout = torch.randn(b, H, L, D, device=dev, generator=g).to(torch.bfloat16)
+
+    def fwd():
+        return sab.selective_attn_train(q, k, v, sel, lengths, 1.0, True)
+
+    def step():
+        out, _ = fwd()
+        out.backward(dout)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    steps = max(5, min(args.steps, 20))
+    per = time_steps(step, steps, flush, torch.cuda.current_stream(dev))
+    per_f = time_steps(fwd, steps, flush, torch.cuda.current_stream(dev))
+    ms, ms_f = statistics.median(per), statistics.median(per_f)
+    flops = 8 * b * H * L * L * D
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"config": "b2 H16 L2048 D64 bf16 causal, lengths (2048, 1536)", "ms_per_step": ms,
+            "fwd_ms": ms_f, "bwd_ms": ms - ms_f, "alg_flops": flops, "tflops": tf,
+            "ffma_nominal_tflops": FFMA_NOMINAL_TFLOPS, "frac_of_nominal_ffma": tf / FFMA_NOMINAL_TFLOPS,
+            "steps": steps, "timing": "median of per-step CUDA events, L2 flushed between steps"}
 
 
 def ssu_measure(args, dev, flush, hbm_peak, world):
