@@ -562,7 +562,7 @@ def run_ours(args, rank, world, local):
         if not args.no_sattn:
             line["sattn_decode"] = sattn_measure(args, dev, flush, hbm_peak)
             line["sattn_prefill"] = sattn_prefill_measure(args, dev, flush, peaks.get("bf16_tflops", 1590.0))
-            line["sattn_train"] = sattn_train_measure(args, dev, flush)
+            line["sattn_train"] = sattn_train_measure(args, dev, flush, peaks.get("bf16_tflops", 1590.0))
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
@@ -819,13 +819,14 @@ def sattn_prefill_measure(args, dev, flush, tc_peak):
     return res
 
 
-def sattn_train_measure(args, dev, flush):
+def sattn_train_measure(args, dev, flush, tc_peak):
     """Selective attention in training mode (row f4, training): b 2, H 16, L 2048, head_dim 64,
-    causal, ragged lengths, bf16 inputs; one step = ``SelectiveAttnTrainFn`` forward + backward.
-    TFLOP/s of the algorithmic FLOPs over the valid causal pairs (forward: statistics
-    q k^T, attention q k^T and P v = 3 x 2 L^2 D / 2; backward as the reference's autograd runs
-    it: q k^T recompute, dO v^T, dv, dq, dk = 5 x 2 L^2 D / 2) against the nominal FFMA rate:
-    these kernels run on CUDA cores in fp32."""
+    causal, ragged lengths, bf16 inputs; one step = ``SelectiveAttnTrainFn`` forward + backward
+    (tcgen05 kernels for this shape). TFLOP/s of the algorithmic FLOPs over the causal pairs
+    (forward: statistics q k^T, attention q k^T and P v = 3 x 2 L^2 D / 2; backward as the
+    reference's autograd runs it: q k^T, dO v^T, dv, dq, dk = 5 x 2 L^2 D / 2) against the
+    measured bf16 dense peak, and the CUDA-core path (``impl="simt"``) against the nominal FFMA
+    rate."""
     import selective_attention_b200 as sab
 
     b, H, L, D = 2, 16, 2048, 64
@@ -836,26 +837,29 @@ def sattn_train_measure(args, dev, flush):
     lengths = torch.tensor([L, 3 * L // 4], device=dev)
     dout = torch.randn(b, H, L, D, device=dev, generator=g).to(torch.bfloat16)
 
-    def fwd():
-        return sab.selective_attn_train(q, k, v, sel, lengths, 1.0, True)
-
-    def step():
-        out, _ = fwd()
-        out.backward(dout)
-
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    steps = max(5, min(args.steps, 20))
-    per = time_steps(step, steps, flush, torch.cuda.current_stream(dev))
-    per_f = time_steps(fwd, steps, flush, torch.cuda.current_stream(dev))
-    ms, ms_f = statistics.median(per), statistics.median(per_f)
     flops = 8 * b * H * L * L * D
-    tf = flops / (ms * 1e-3) / 1e12
-    return {"config": "b2 H16 L2048 D64 bf16 causal, lengths (2048, 1536)", "ms_per_step": ms,
-            "fwd_ms": ms_f, "bwd_ms": ms - ms_f, "alg_flops": flops, "tflops": tf,
-            "ffma_nominal_tflops": FFMA_NOMINAL_TFLOPS, "frac_of_nominal_ffma": tf / FFMA_NOMINAL_TFLOPS,
-            "steps": steps, "timing": "median of per-step CUDA events, L2 flushed between steps"}
+    res = {"config": "b2 H16 L2048 D64 bf16 causal, lengths (2048, 1536)", "alg_flops": flops,
+           "timing": "median of per-step CUDA events, L2 flushed between steps"}
+    for impl, peak, peak_name in (("tc", tc_peak, "bf16 dense, measured"),
+                                  ("simt", FFMA_NOMINAL_TFLOPS, "fp32 FFMA, nominal")):
+        def fwd():
+            return sab.selective_attn_train(q, k, v, sel, lengths, 1.0, True, impl=impl)
+
+        def step():
+            out, _ = fwd()
+            out.backward(dout)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        steps = max(5, min(args.steps, 20))
+        per = time_steps(step, steps, flush, torch.cuda.current_stream(dev))
+        per_f = time_steps(fwd, steps, flush, torch.cuda.current_stream(dev))
+        ms, ms_f = statistics.median(per), statistics.median(per_f)
+        tf = flops / (ms * 1e-3) / 1e12
+        res[impl] = {"ms_per_step": ms, "fwd_ms": ms_f, "bwd_ms": ms - ms_f, "tflops": tf, "peak_tflops": peak,
+                     "peak": peak_name, "frac": tf / peak, "steps": steps}
+    return res
 
 
 def ssu_measure(args, dev, flush, hbm_peak, world):

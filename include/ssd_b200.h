@@ -329,7 +329,9 @@ int sattn_prefill_fwd(const void* q_rot, const void* k_rot, const void* v, const
  *                             backward fills in
  * The backward takes dout (b, H, L, D) and writes dq, dk, dv (b, H, L, D) and
  * dselect_gate (b, H, L), all in dtype, including the path through std (the gates are
- * scaled by it). head_dim D in {16, 32, 64, 128}; CUDA cores, fp32 arithmetic. Both
+ * scaled by it). head_dim D in {16, 32, 64, 128}. impl: SSD_IMPL_AUTO runs 16-bit inputs
+ * with head_dim 64 on tcgen05 (16-bit products, fp32 accumulation and softmax) and the rest
+ * on CUDA cores in fp32; SSD_IMPL_TC requires the former, SSD_IMPL_SIMT forces the latter. Both
  * calls use p->workspace (>= sattn_train_workspace_size(p)); the backward needs the
  * forward's out, lse, log_gate and stats unchanged.
  */
@@ -337,6 +339,7 @@ typedef struct sattn_train_params {
   int64_t batch, nheads, seqlen, head_dim;
   int32_t dtype;
   int32_t is_causal;
+  int32_t impl; /* SSD_IMPL_AUTO / SSD_IMPL_TC (16-bit, head_dim 64: tcgen05) / SSD_IMPL_SIMT */
   float scale;
   float log_gate_penalty;
   const void* q_rot;

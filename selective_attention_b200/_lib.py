@@ -86,7 +86,8 @@ class SattnTrainParams(ctypes.Structure):
 
     _fields_ = [
         ("batch", c_int64), ("nheads", c_int64), ("seqlen", c_int64), ("head_dim", c_int64),
-        ("dtype", c_int32), ("is_causal", c_int32), ("scale", c_float), ("log_gate_penalty", c_float),
+        ("dtype", c_int32), ("is_causal", c_int32), ("impl", c_int32), ("scale", c_float),
+        ("log_gate_penalty", c_float),
         ("q_rot", c_void_p), ("k_rot", c_void_p), ("v", c_void_p), ("select_gate", c_void_p), ("lengths", c_void_p),
         ("out", c_void_p), ("lse", c_void_p), ("log_gate", c_void_p), ("stats", c_void_p),
         ("workspace", c_void_p), ("workspace_bytes", c_size_t),

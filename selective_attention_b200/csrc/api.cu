@@ -558,6 +558,9 @@ int train_args(const sattn_train_params* p, SattnTrainArgs* a, size_t* need) {
   a->D = (int)p->head_dim;
   a->dtype = p->dtype;
   a->causal = p->is_causal ? 1 : 0;
+  const bool tc_ok = sattn_train_tc_supported((int)p->head_dim, p->dtype);
+  if (p->impl == SSD_IMPL_TC && !tc_ok) return SSD_ERR_INVALID_ARGUMENT;
+  a->use_tc = p->impl != SSD_IMPL_SIMT && tc_ok;
   a->scale = p->scale;
   a->penalty = p->log_gate_penalty;
   a->q = p->q_rot;

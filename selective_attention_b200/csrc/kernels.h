@@ -80,10 +80,15 @@ bool sattn_prefill_tc_supported(int D, int dtype);
 cudaError_t launch_sattn_prefill(const void* q, const void* k, const void* v, const float* lg, void* out, int b, int H,
                                  int L, int D, float scale, int dtype, int use_tc, cudaStream_t s);
 unsigned int fetch_error_sattn(cudaStream_t s);
+// The pipelined tensor-core attention (16-bit, head_dim 64) with the row log-sum-exp written
+// (lse may be null) and causal or bidirectional key ranges; used by the training forward.
+cudaError_t launch_sattn_attn_fa(const void* q, const void* k, const void* v, const float* lg, void* out, float* lse,
+                                 int b, int H, int L, float scale, int dtype, int causal, cudaStream_t s);
 
 // sattn_train.cu (training-mode selective attention and its backward; CUDA cores)
 struct SattnTrainArgs {
   int B, H, L, D, dtype, causal;
+  int use_tc;  // tcgen05 kernels (16-bit inputs, head_dim 64)
   float scale, penalty;
   const void* q;
   const void* k;
@@ -95,11 +100,12 @@ struct SattnTrainArgs {
   float* lg;
   float* stats;
   // workspace
-  double* part;  // (B, H, L / 64, 2) per query tile: sum and sum of squares of the valid scores
+  double* part;  // (B, H, L / 64, 2) per query tile (128 rows on tensor cores): sum, sum of squares
   float* Di;     // (B, H, L) dout . out
   float* dlg;    // (B, H, L) gradient of the log-gates
 };
 bool sattn_train_supported(int D);
+bool sattn_train_tc_supported(int D, int dtype);
 cudaError_t launch_sattn_train_fwd(const SattnTrainArgs& a, cudaStream_t s);
 cudaError_t launch_sattn_train_bwd(const SattnTrainArgs& a, const void* dout, void* dq, void* dk, void* dv,
                                    void* dgate, cudaStream_t s);

@@ -318,6 +318,7 @@ constexpr int kKBlk = kTK * 128;   // bytes of one 64-column block of a K or V t
 constexpr size_t kTcSmem = 104 * 1024;  // at most two CTAs (2 x 256 TMEM columns) per SM
 constexpr int kTcThreads = 256;          // two threads per query row
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleLog2 = 8.0f * kLog2e;  // rescale O when a row max grows by more than e^8
 
 // rows x D 16-bit tile -> shared memory, 64-column blocks of 128-byte swizzled rows.
@@ -670,7 +671,8 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
                                                                           const __grid_constant__ CUtensorMap tm_k,
                                                                           const __grid_constant__ CUtensorMap tm_v,
                                                                           const float* __restrict__ lg,
-                                                                          T* __restrict__ out, int L, float scale) {
+                                                                          T* __restrict__ out, int L, float scale,
+                                                                          float* __restrict__ lse, int causal) {
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int NS = kFaStages;
   extern __shared__ uint8_t smraw[];
@@ -692,8 +694,9 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
   const int bh = blockIdx.x;
   const int t = (int)gridDim.y - 1 - (int)blockIdx.y;  // pairs with the most key tiles first
   const int q0A = 256 * t, q0B = q0A + 128;
-  const int nkA = q0A < L ? min(q0A + 127, L - 1) / 128 + 1 : 0;
-  const int nkB = q0B < L ? min(q0B + 127, L - 1) / 128 + 1 : 0;
+  const int nkv = (L + 127) / 128;  // every key tile (bidirectional attention)
+  const int nkA = q0A < L ? (causal ? min(q0A + 127, L - 1) / 128 + 1 : nkv) : 0;
+  const int nkB = q0B < L ? (causal ? min(q0B + 127, L - 1) / 128 + 1 : nkv) : 0;
   const int nk = max(nkA, nkB);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
@@ -873,7 +876,8 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
       float mp[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) mp[q] = -INFINITY;
-      if (k0 + 127 < q0 && k0 + 128 <= L) {  // every key before every query of the tile: all gated
+      // tiles are 128-aligned: a key tile holds none of the queries' own keys unless k0 == q0
+      if ((causal ? k0 < q0 : k0 != q0) && k0 + 128 <= L) {  // every key of the tile is gated
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -894,11 +898,11 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
             mp[q + 3] = fmaxf(mp[q + 3], x3);
           }
       } else {
-        // diagonal or tail tile: keys past the query or past L drop out, the query's own
-        // key is ungated
+        // diagonal or tail tile: keys past L (and, causal, past the query) drop out, the
+        // query's own key is ungated
         const float* g = sG(s);
-        const int gate_end = min(qi, L);      // keys below this are gated
-        const bool own = qi < L && qi >= k0;  // the query's own key is in this tile
+        const int gate_end = causal ? min(qi, L) : L;  // keys below this are gated (but qi)
+        const bool own = qi < L && qi >= k0 && qi < k0 + 128;  // the query's own key is in this tile
 #pragma unroll
         for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -975,6 +979,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
       tmem_ld32(tmem + tl + T_O + 64 * w + 32, o[1]);
       tmem_wait_ld();
       const float inv = 1.0f / lsum;
+      if (lse && qi < L) lse[(long long)bh * L + qi] = (m_used + __log2f(lsum)) * kLn2;  // natural log-sum-exp
       if (qi < L) {
         uint4* op = reinterpret_cast<uint4*>(out + ((long long)bh * L + qi) * 64);
 #pragma unroll
@@ -999,7 +1004,7 @@ __global__ void __launch_bounds__(kFaThreads, 1) sattn_prefill_fa_kernel(const _
 
 template <typename T>
 cudaError_t prefill_fa_t(const void* q, const void* k, const void* v, const float* lg, void* out, int b, int H, int L,
-                         float scale, cudaStream_t s) {
+                         float scale, cudaStream_t s, float* lse = nullptr, int causal = 1) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   const long long bhn = (long long)b * H, npairs = ((long long)L + 255) / 256;
   if (bhn > 0x7fffffffll || npairs > 65535) return cudaErrorInvalidValue;
@@ -1012,10 +1017,17 @@ cudaError_t prefill_fa_t(const void* q, const void* k, const void* v, const floa
                                        (int)kFaSmem);
   if (e != cudaSuccess) return e;
   dim3 grid((unsigned)bhn, (unsigned)npairs);
-  sattn_prefill_fa_kernel<T><<<grid, kFaThreads, kFaSmem, s>>>(mq, mk, mv, lg, (T*)out, L, scale);
+  sattn_prefill_fa_kernel<T><<<grid, kFaThreads, kFaSmem, s>>>(mq, mk, mv, lg, (T*)out, L, scale, lse, causal);
   return cudaGetLastError();
 }
 }  // namespace
+
+cudaError_t launch_sattn_attn_fa(const void* q, const void* k, const void* v, const float* lg, void* out, float* lse,
+                                 int b, int H, int L, float scale, int dtype, int causal, cudaStream_t s) {
+  if (dtype == SSD_BF16) return prefill_fa_t<__nv_bfloat16>(q, k, v, lg, out, b, H, L, scale, s, lse, causal);
+  if (dtype == SSD_F16) return prefill_fa_t<__half>(q, k, v, lg, out, b, H, L, scale, s, lse, causal);
+  return cudaErrorInvalidValue;
+}
 
 bool sattn_decode_supported(int D) { return D == 8 || D == 16 || D == 32 || D == 64 || D == 128 || D == 256; }
 

@@ -1,4 +1,4 @@
-// sattn_train.cu - training-mode selective attention and its backward, on CUDA cores.
+// sattn_train.cu - training-mode selective attention and its backward.
 //
 // SelectiveMHA.forward with self.training (modules/selective_attention.py:232-280):
 //   S[i,j]   = scale q_i . k_j, causal (j <= i) or not                       (_build_attn_matrix :89-99)
@@ -13,7 +13,8 @@
 //   dS_total = dS + c (S - mean) on valid scores,  c = dstd / (count std)  (d std / d S = (S - mean) / (count std))
 //   dq_i = scale sum_j dS_total[i,j] k_j,  dk_j = scale sum_i dS_total[i,j] q_i,  dv_j = sum_i P[i,j] dO_i
 //
-// Kernels (all 64 x 64 tiles, 256 threads, fp32 arithmetic on any input type):
+// CUDA-core kernels (64 x 64 tiles, 256 threads, fp32 arithmetic on any input type); 16-bit
+// inputs with head_dim 64 take the tensor-core versions further below:
 //   stats      per (query tile, head, row): sums of the valid scores and of their squares
 //   stats_fin  per head: mean, std, count (fp64 sums)
 //   gate       lg = log(g) std penalty, -inf past the length
@@ -25,12 +26,20 @@
 //   dq         per query tile: dq with dS_total
 #include <math.h>
 
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "sattn_tiles.cuh"
+#include "sm100.cuh"
+#include "tmap.cuh"
 
 namespace ssdb200 {
 namespace {
+
+using namespace sm100;
 
 constexpr int kLDT = kPT + 4;  // fp32 64 x 64 score tiles
 
@@ -105,7 +114,8 @@ __device__ __forceinline__ bool stat_valid(int qi, int kj, int len, int causal) 
   return qi < len && kj < len && (!causal || kj <= qi);
 }
 
-template <typename V>
+// Sum over a CTA of NW warps (red: NW slots of shared memory); every thread gets the total.
+template <typename V, int NW = 8>
 __device__ __forceinline__ V block_sum256(V v, V* red) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
@@ -115,7 +125,7 @@ __device__ __forceinline__ V block_sum256(V v, V* red) {
   __syncthreads();
   V t = 0;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) t += red[i];
+  for (int i = 0; i < NW; ++i) t += red[i];
   return t;
 }
 
@@ -570,11 +580,411 @@ cudaError_t train_bwd_t(const SattnTrainArgs& a, const void* dout, void* dq, voi
   return cudaGetLastError();
 }
 
+
+// ============================================================================ tensor cores
+// 16-bit inputs with head_dim 64: the same passes on tcgen05, 128 x 128 tiles moved by TMA
+// (128-byte swizzle), products in TMEM, thread = TMEM lane = row of the CTA's own tile.
+//   stats_tc  S = Q K^T per key tile, the valid scores' sums from the TMEM rows
+//   (forward attention: the pipelined prefill kernel with lse, sattn.cu)
+//   bwd_tc    MODE 0 (per key tile): S^T = K Q^T, dP^T = V dO^T -> P^T, dS^T; dv += P^T dO
+//             (TS form, P^T from TMEM), dlg from the rows; MODE 1: dk += dS_total^T Q;
+//             MODE 2 (per query tile): S = Q K^T, dP = dO V^T -> dS_total; dq += dS_total K
+// Every wait is bounded; a CTA that gives up records a site code and skips its remaining
+// work (its MMAs and copies in flight are waited for, bounded, before TMEM is released).
+constexpr unsigned int kSiteTrTma = 0x331, kSiteTrMma = 0x332;
+constexpr int kTrTile = 128 * 128;  // bytes of a 128-row x 64-column 16-bit tile
+
+constexpr size_t kStSmem = 1024 + 3 * kTrTile + 64;
+
+template <typename T>
+__global__ void __launch_bounds__(128) sattn_train_stats_tc_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                                   const __grid_constant__ CUtensorMap tm_k,
+                                                                   const int64_t* __restrict__ lengths, int H, int L,
+                                                                   float scale, int causal, double* part) {
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  extern __shared__ uint8_t smraw[];
+  uint8_t* base = align1024_shared(smraw);
+  uint8_t* sQ = base;
+  auto sK = [&](int st) { return base + kTrTile * (1 + st); };
+  __shared__ uint64_t bars[5];  // Q, K[2], S[2]
+  __shared__ uint32_t tslot[1];
+  __shared__ double red[8];
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int qt = blockIdx.y, bh = blockIdx.x;
+  const int b = bh / H;
+  const int len = row_len(lengths, b, L);
+  const int q0 = 128 * qt, tid = threadIdx.x, warp = tid >> 5;
+  float s1 = 0.f, s2 = 0.f;
+  const int nk = q0 >= len ? 0 : (causal ? min(q0 + 127, len - 1) / 128 + 1 : (len + 127) / 128);
+  if (nk > 0) {
+    if (tid == 0) {
+      prefetch_tmap(&tm_q);
+      prefetch_tmap(&tm_k);
+      for (int i = 0; i < 5; ++i) mbar_init(bar(i), 1);
+      fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint32_t tl = (uint32_t)(warp * 32) << 16;
+    constexpr uint32_t ID = idesc_f16(128, 128, BF16, false, false);
+    int k_iss[2] = {0, 0}, k_wt[2] = {0, 0}, s_iss[2] = {0, 0}, s_wt[2] = {0, 0};  // thread 0's books
+    bool ok = true;
+    auto issue_mma = [&](int j) -> bool {  // thread 0: S_(j % 2) = Q K_j^T once K_j has landed
+      const int st = j & 1;
+      if (!mbar_wait(bar(1 + st), k_wt[st] & 1, kSiteTrTma)) return false;
+      ++k_wt[st];
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        umma_f16(tmem + 128 * st, sdesc_sw128(smem_u32(sQ) + 32 * ks, 16, 1024),
+                 sdesc_sw128(smem_u32(sK(st)) + 32 * ks, 16, 1024), ID, ks > 0 ? 1u : 0u);
+      umma_commit(bar(3 + st));
+      ++s_iss[st];
+      return true;
+    };
+    if (tid == 0) {
+      mbar_expect_tx(bar(0), (uint32_t)kTrTile);
+      tma_load_3d(smem_u32(sQ), &tm_q, 0, q0, bh, bar(0));
+      for (int j = 0; j < 2 && j < nk; ++j) {
+        mbar_expect_tx(bar(1 + j), (uint32_t)kTrTile);
+        tma_load_3d(smem_u32(sK(j)), &tm_k, 0, 128 * j, bh, bar(1 + j));
+        ++k_iss[j];
+      }
+      ok = mbar_wait(bar(0), 0, kSiteTrTma) && issue_mma(0);
+    }
+    ok = __syncthreads_and(ok) != 0;
+    const int qi = q0 + tid;
+    for (int j = 0; j < nk && ok; ++j) {
+      const int st = j & 1;
+      if (tid == 0 && j + 1 < nk) ok = issue_mma(j + 1);
+      const bool got = mbar_wait(bar(3 + st), (j >> 1) & 1, kSiteTrMma);
+      if (tid == 0 && got) {
+        ++s_wt[st];
+        if (j + 2 < nk) {  // K stage st is free once S_j is complete
+          mbar_expect_tx(bar(1 + st), (uint32_t)kTrTile);
+          tma_load_3d(smem_u32(sK(st)), &tm_k, 0, 128 * (j + 2), bh, bar(1 + st));
+          ++k_iss[st];
+        }
+      }
+      ok = __syncthreads_and(ok && got) != 0;
+      if (!ok) break;
+      tc_fence_after();
+      const int k0 = 128 * j;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + tl + 128 * st + 32 * c, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          if (stat_valid(qi, k0 + 32 * c + e, len, causal)) {
+            const float x = __uint_as_float(v[e]) * scale;
+            s1 += x;
+            s2 = fmaf(x, x, s2);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncthreads();  // S_(j % 2) read before S_(j + 2) overwrites it
+    }
+    if (tid == 0) {  // nothing may still be in flight when TMEM and the CTA go away (bounded)
+      for (int st = 0; st < 2; ++st) {
+        while (s_wt[st] < s_iss[st] && mbar_wait(bar(3 + st), s_wt[st] & 1, kSiteTrMma)) ++s_wt[st];
+        while (k_wt[st] < k_iss[st] && mbar_wait(bar(1 + st), k_wt[st] & 1, kSiteTrTma)) ++k_wt[st];
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 256);
+  }
+  const double t1 = block_sum256<double, 4>((double)s1, red);
+  const double t2 = block_sum256<double, 4>((double)s2, red);
+  if (tid == 0) {
+    const long long idx = ((long long)bh * gridDim.y + qt) * 2;
+    part[idx] = t1;
+    part[idx + 1] = t2;
+  }
+}
+
+constexpr int kBtThreads = 256;
+constexpr size_t kBtSmem = 1024 + 6 * kTrTile + 64;
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(kBtThreads, 1) sattn_train_bwd_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+    const float* __restrict__ lg, const float* __restrict__ lse, const float* __restrict__ Di,
+    const float* __restrict__ stats, const int64_t* __restrict__ lengths, int H, int L, float scale, int causal,
+    T* __restrict__ outg, float* __restrict__ dlg) {
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr bool KEYS = MODE < 2;  // the CTA's own tile is a key tile
+  extern __shared__ uint8_t smraw[];
+  uint8_t* base = align1024_shared(smraw);
+  uint8_t* own1 = base;            // K (key-major) or Q
+  uint8_t* own2 = base + kTrTile;  // V or dO
+  auto oth1 = [&](int st) { return base + kTrTile * (2 + 2 * st); };  // Q or K
+  auto oth2 = [&](int st) { return base + kTrTile * (3 + 2 * st); };  // dO or V
+  __shared__ float colA[2][128], colB[2][128];  // per stage: lse, D_i of the queries (keys: log-gates)
+  __shared__ float red[2][128];
+  __shared__ uint64_t bars[4];  // own, other[2], mma
+  __shared__ uint32_t tslot[1];
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int bh = blockIdx.x, own = blockIdx.y;
+  const int b = bh / H, h = bh - b * H;
+  const int len = row_len(lengths, b, L);
+  const int nt = (L + 127) / 128;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = (warp & 3) * 32 + lane, hc = warp >> 2;
+  const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;
+  const int o0 = 128 * own, o = o0 + r;
+  const int t_begin = KEYS ? (causal ? own : 0) : 0;
+  const int t_end = KEYS ? nt : (causal ? own + 1 : nt);
+  const int cnt = t_end - t_begin;
+  const float mean = stats[h * 4], c_st = stats[h * 4 + 3];
+  const long long rowbase = (long long)bh * L;
+  // this thread's row values
+  const float g_row = KEYS && o < L ? lg[rowbase + o] : -INFINITY;
+  const float lse_row = !KEYS && o < L ? lse[rowbase + o] : 0.f;
+  const float di_row = !KEYS && o < L ? Di[rowbase + o] : 0.f;
+  auto load_cols = [&](int st, int t) {  // per-column values of other tile t (threads < 128)
+    if (tid < 128) {
+      const int x = 128 * t + tid;
+      if (KEYS) {
+        colA[st][tid] = x < L ? lse[rowbase + x] : 0.f;
+        colB[st][tid] = x < L ? Di[rowbase + x] : 0.f;
+      } else {
+        colA[st][tid] = x < L ? lg[rowbase + x] : -INFINITY;
+      }
+    }
+  };
+  if (tid == 0) {
+    prefetch_tmap(&tm_q);
+    prefetch_tmap(&tm_k);
+    prefetch_tmap(&tm_v);
+    prefetch_tmap(&tm_do);
+    for (int i = 0; i < 4; ++i) mbar_init(bar(i), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 512);
+  load_cols(0, t_begin);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  constexpr uint32_t T_S = 0, T_DP = 128, T_W = 256, T_ACC = 320;
+  constexpr uint32_t ID_SS = idesc_f16(128, 128, BF16, false, false);
+  constexpr uint32_t ID_ACC = idesc_f16(128, 64, BF16, false, true);
+  const CUtensorMap* m_own1 = KEYS ? &tm_k : &tm_q;
+  const CUtensorMap* m_own2 = KEYS ? &tm_v : &tm_do;
+  const CUtensorMap* m_oth1 = KEYS ? &tm_q : &tm_k;
+  const CUtensorMap* m_oth2 = KEYS ? &tm_do : &tm_v;
+  int ld_iss[2] = {0, 0}, ld_wt[2] = {0, 0}, mma_iss = 0, mma_wt = 0;  // thread 0's books
+  if (tid == 0) {
+    mbar_expect_tx(bar(0), 2u * kTrTile);
+    tma_load_3d(smem_u32(own1), m_own1, 0, o0, bh, bar(0));
+    tma_load_3d(smem_u32(own2), m_own2, 0, o0, bh, bar(0));
+    mbar_expect_tx(bar(1), 2u * kTrTile);
+    tma_load_3d(smem_u32(oth1(0)), m_oth1, 0, 128 * t_begin, bh, bar(1));
+    tma_load_3d(smem_u32(oth2(0)), m_oth2, 0, 128 * t_begin, bh, bar(1));
+    ++ld_iss[0];
+  }
+  bool ok = __syncthreads_and(mbar_wait(bar(0), 0, kSiteTrTma)) != 0;
+  float dl = 0.f;
+  for (int u = 0; u < cnt && ok; ++u) {
+    const int st = u & 1, t = t_begin + u, x0 = 128 * t;
+    if (u + 1 < cnt) {  // prefetch the next other tile into the stage MMA3(u - 1) released
+      if (tid == 0) {
+        const int sn = st ^ 1;
+        mbar_expect_tx(bar(1 + sn), 2u * kTrTile);
+        tma_load_3d(smem_u32(oth1(sn)), m_oth1, 0, x0 + 128, bh, bar(1 + sn));
+        tma_load_3d(smem_u32(oth2(sn)), m_oth2, 0, x0 + 128, bh, bar(1 + sn));
+        ++ld_iss[sn];
+      }
+      load_cols(st ^ 1, t + 1);
+    }
+    bool got = mbar_wait(bar(1 + st), (u >> 1) & 1, kSiteTrTma);
+    if (tid == 0 && got) ++ld_wt[st];
+    ok = __syncthreads_and(got) != 0;
+    if (!ok) break;
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        umma_f16(tmem + T_S, sdesc_sw128(smem_u32(own1) + 32 * ks, 16, 1024),
+                 sdesc_sw128(smem_u32(oth1(st)) + 32 * ks, 16, 1024), ID_SS, ks > 0 ? 1u : 0u);
+        umma_f16(tmem + T_DP, sdesc_sw128(smem_u32(own2) + 32 * ks, 16, 1024),
+                 sdesc_sw128(smem_u32(oth2(st)) + 32 * ks, 16, 1024), ID_SS, ks > 0 ? 1u : 0u);
+      }
+      umma_commit(bar(3));
+      ++mma_iss;
+    }
+    got = mbar_wait(bar(3), mma_wt & 1, kSiteTrMma);
+    if (got) ++mma_wt;  // the same count in every thread while nothing fails
+    ok = __syncthreads_and(got) != 0;
+    if (!ok) break;
+    tc_fence_after();
+    // P or dS for this thread's 64 columns, into TMEM as 16-bit pairs
+#pragma unroll 1
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c0 = 64 * hc + 32 * cc;
+      uint32_t sv[32], pv[32];
+      tmem_ld32(tmem + tl + T_S + c0, sv);
+      tmem_ld32(tmem + tl + T_DP + c0, pv);
+      tmem_wait_ld();
+      uint32_t pk[16];
+#pragma unroll
+      for (int e = 0; e < 32; e += 2) {
+        float w2[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int c = c0 + e + q, x = x0 + c;
+          const int kj = KEYS ? o : x, qi = KEYS ? x : o;
+          const float s = __uint_as_float(sv[e + q]) * scale;
+          const float g = KEYS ? g_row : colA[st][c];
+          const float lq = KEYS ? colA[st][c] : lse_row;
+          const float dq = KEYS ? colB[st][c] : di_row;
+          const float lgt = logit(s, qi, kj, g, L, causal);
+          const float p = lgt == -INFINITY ? 0.f : __expf(lgt - lq);
+          const float dsm = p * (__uint_as_float(pv[e + q]) - dq);
+          if (MODE == 0) {
+            if (kj != qi) dl += dsm;
+            w2[q] = p;
+          } else {
+            w2[q] = dsm + (stat_valid(qi, kj, len, causal) ? c_st * (s - mean) : 0.f);
+          }
+        }
+        pk[e >> 1] = pack2<T>(w2[0], w2[1]);
+      }
+      tmem_st16(tmem + tl + T_W + (uint32_t)(c0 >> 1), pk);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t b3 = smem_u32(MODE == 0 ? oth2(st) : oth1(st));
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks)
+        umma_f16_ts(tmem + T_ACC, tmem + T_W + 8 * ks, sdesc_sw128(b3 + 2048 * ks, 16, 1024), ID_ACC,
+                    (u > 0 || ks > 0) ? 1u : 0u);
+      umma_commit(bar(3));
+      ++mma_iss;
+    }
+    got = mbar_wait(bar(3), mma_wt & 1, kSiteTrMma);  // T_W and the stage are free afterwards
+    if (got) ++mma_wt;
+    ok = __syncthreads_and(got) != 0;
+    tc_fence_after();
+  }
+  if (ok) {
+    uint32_t av[32];
+    tmem_ld32(tmem + tl + T_ACC + 32 * hc, av);
+    tmem_wait_ld();
+    if (o < L) {
+      const float mul = MODE == 0 ? 1.f : scale;
+      uint4* dst = reinterpret_cast<uint4*>(outg + (rowbase + o) * 64 + 32 * hc);
+#pragma unroll
+      for (int e = 0; e < 32; e += 8)
+        dst[e >> 3] = make_uint4(pack2<T>(__uint_as_float(av[e]) * mul, __uint_as_float(av[e + 1]) * mul),
+                                 pack2<T>(__uint_as_float(av[e + 2]) * mul, __uint_as_float(av[e + 3]) * mul),
+                                 pack2<T>(__uint_as_float(av[e + 4]) * mul, __uint_as_float(av[e + 5]) * mul),
+                                 pack2<T>(__uint_as_float(av[e + 6]) * mul, __uint_as_float(av[e + 7]) * mul));
+    }
+    if (MODE == 0) {
+      red[hc][r] = dl;
+      __syncthreads();
+      if (hc == 0 && o < L) dlg[rowbase + o] = red[0][r] + red[1][r];
+    }
+  } else if (tid == 0) {  // let what is in flight land before TMEM and the CTA go away (bounded)
+    while (mma_wt < mma_iss && mbar_wait(bar(3), mma_wt & 1, kSiteTrMma)) ++mma_wt;
+    for (int st = 0; st < 2; ++st)
+      while (ld_wt[st] < ld_iss[st] && mbar_wait(bar(1 + st), ld_wt[st] & 1, kSiteTrTma)) ++ld_wt[st];
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+bool train_maps(CUtensorMap* m, const void* p, bool bf16, int L, long long bhn) {
+  return make_map_3d(m, p, bf16, 64, (uint64_t)L, (uint64_t)bhn, 64, 128, 1);
+}
+
+template <typename T>
+cudaError_t train_fwd_tc_t(const SattnTrainArgs& a, cudaStream_t s) {
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  const long long bhn = (long long)a.B * a.H;
+  const int nt = (a.L + 127) / 128;
+  CUtensorMap mq, mk;
+  if (!train_maps(&mq, a.q, bf16, a.L, bhn) || !train_maps(&mk, a.k, bf16, a.L, bhn)) return cudaErrorInvalidValue;
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(sattn_train_stats_tc_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kStSmem)))
+    return e;
+  sattn_train_stats_tc_kernel<T><<<dim3((unsigned)bhn, (unsigned)nt), 128, kStSmem, s>>>(mq, mk, a.lengths, a.H, a.L,
+                                                                                         a.scale, a.causal, a.part);
+  if ((e = cudaGetLastError())) return e;
+  sattn_train_stats_fin_kernel<<<(unsigned)a.H, 256, 0, s>>>(a.part, a.lengths, a.B, a.H, a.L, nt, a.causal, a.stats);
+  if ((e = cudaGetLastError())) return e;
+  const long long n = bhn * a.L;
+  sattn_train_gate_kernel<T><<<(unsigned)((n + 255) / 256), 256, 0, s>>>((const T*)a.gate, a.lengths, a.stats, a.H,
+                                                                         a.L, n, a.penalty, a.lg);
+  if ((e = cudaGetLastError())) return e;
+  return launch_sattn_attn_fa(a.q, a.k, a.v, a.lg, a.out, a.lse, a.B, a.H, a.L, a.scale, a.dtype, a.causal, s);
+}
+
+template <typename T>
+cudaError_t train_bwd_tc_t(const SattnTrainArgs& a, const void* dout, void* dq, void* dk, void* dv, void* dgate,
+                           cudaStream_t s) {
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  const long long bhn = (long long)a.B * a.H;
+  const int nt = (a.L + 127) / 128;
+  CUtensorMap mq, mk, mv, mo;
+  if (!train_maps(&mq, a.q, bf16, a.L, bhn) || !train_maps(&mk, a.k, bf16, a.L, bhn) ||
+      !train_maps(&mv, a.v, bf16, a.L, bhn) || !train_maps(&mo, dout, bf16, a.L, bhn))
+    return cudaErrorInvalidValue;
+  cudaError_t e;
+  if ((e = cudaFuncSetAttribute(sattn_train_bwd_tc_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kBtSmem)) ||
+      (e = cudaFuncSetAttribute(sattn_train_bwd_tc_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kBtSmem)) ||
+      (e = cudaFuncSetAttribute(sattn_train_bwd_tc_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kBtSmem)))
+    return e;
+  const long long rows = bhn * a.L;
+  sattn_train_rowdot_kernel<T><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>((const T*)dout, (const T*)a.out, rows, 64,
+                                                                          a.Di);
+  if ((e = cudaGetLastError())) return e;
+  const dim3 grid((unsigned)bhn, (unsigned)nt);
+  sattn_train_bwd_tc_kernel<T, 0><<<grid, kBtThreads, kBtSmem, s>>>(mq, mk, mv, mo, a.lg, a.lse, a.Di, a.stats,
+                                                                    a.lengths, a.H, a.L, a.scale, a.causal, (T*)dv,
+                                                                    a.dlg);
+  if ((e = cudaGetLastError())) return e;
+  sattn_train_bwd_fin_kernel<T><<<(unsigned)a.H, 256, 0, s>>>((const T*)a.gate, a.lengths, a.dlg, a.B, a.H, a.L,
+                                                              a.penalty, a.stats, (T*)dgate);
+  if ((e = cudaGetLastError())) return e;
+  sattn_train_bwd_tc_kernel<T, 1><<<grid, kBtThreads, kBtSmem, s>>>(mq, mk, mv, mo, a.lg, a.lse, a.Di, a.stats,
+                                                                    a.lengths, a.H, a.L, a.scale, a.causal, (T*)dk,
+                                                                    nullptr);
+  if ((e = cudaGetLastError())) return e;
+  sattn_train_bwd_tc_kernel<T, 2><<<grid, kBtThreads, kBtSmem, s>>>(mq, mk, mv, mo, a.lg, a.lse, a.Di, a.stats,
+                                                                    a.lengths, a.H, a.L, a.scale, a.causal, (T*)dq,
+                                                                    nullptr);
+  return cudaGetLastError();
+}
 }  // namespace
 
 bool sattn_train_supported(int D) { return D == 16 || D == 32 || D == 64 || D == 128; }
 
+bool sattn_train_tc_supported(int D, int dtype) { return D == 64 && dtype != SSD_F32; }
+
 cudaError_t launch_sattn_train_fwd(const SattnTrainArgs& a, cudaStream_t s) {
+  if (a.use_tc) {
+    if (!sattn_train_tc_supported(a.D, a.dtype) || (long long)a.B * a.H > 0x7fffffffll || (a.L + 127) / 128 > 65535)
+      return cudaErrorInvalidValue;
+    return a.dtype == SSD_BF16 ? train_fwd_tc_t<__nv_bfloat16>(a, s) : train_fwd_tc_t<__half>(a, s);
+  }
   switch (a.dtype) {
     case SSD_F32: return train_fwd_t<float>(a, s);
     case SSD_BF16: return train_fwd_t<__nv_bfloat16>(a, s);
@@ -585,6 +995,12 @@ cudaError_t launch_sattn_train_fwd(const SattnTrainArgs& a, cudaStream_t s) {
 
 cudaError_t launch_sattn_train_bwd(const SattnTrainArgs& a, const void* dout, void* dq, void* dk, void* dv,
                                    void* dgate, cudaStream_t s) {
+  if (a.use_tc) {
+    if (!sattn_train_tc_supported(a.D, a.dtype) || (long long)a.B * a.H > 0x7fffffffll || (a.L + 127) / 128 > 65535)
+      return cudaErrorInvalidValue;
+    return a.dtype == SSD_BF16 ? train_bwd_tc_t<__nv_bfloat16>(a, dout, dq, dk, dv, dgate, s)
+                               : train_bwd_tc_t<__half>(a, dout, dq, dk, dv, dgate, s);
+  }
   switch (a.dtype) {
     case SSD_F32: return train_bwd_t<float>(a, dout, dq, dk, dv, dgate, s);
     case SSD_BF16: return train_bwd_t<__nv_bfloat16>(a, dout, dq, dk, dv, dgate, s);

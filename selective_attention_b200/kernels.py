@@ -505,7 +505,7 @@ def sattn_prefill(q_rot, k_rot, v, log_gate, scale=None, out=None, impl: str = "
     return out
 
 
-def _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_causal, scale):
+def _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_causal, scale, impl):
     b, H, L, D = q_rot.shape
     dev = check_cuda([q_rot, k_rot, v, select_gate, lengths], ["q_rot", "k_rot", "v", "select_gate", "lengths"])
     for t, n in ((k_rot, "k_rot"), (v, "v")):
@@ -524,6 +524,7 @@ def _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_ca
     p.batch, p.nheads, p.seqlen, p.head_dim = b, H, L, D
     p.dtype = _lib.dtype_code(q_rot.dtype, "q_rot")
     p.is_causal = 1 if is_causal else 0
+    p.impl = _lib.IMPLS[impl]
     p.scale = float(D ** -0.5 if scale is None else scale)
     p.log_gate_penalty = float(log_gate_penalty)
     p.q_rot, p.k_rot, p.v = _lib.ptr(q_rot), _lib.ptr(k_rot), _lib.ptr(v)
@@ -532,7 +533,8 @@ def _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_ca
     return p, dev, keep
 
 
-def sattn_train_forward(q_rot, k_rot, v, select_gate, log_gate_penalty, lengths=None, is_causal=True, scale=None):
+def sattn_train_forward(q_rot, k_rot, v, select_gate, log_gate_penalty, lengths=None, is_causal=True, scale=None,
+                        impl: str = "auto"):
     """Selective attention in training mode (C-ABI ``sattn_train_fwd``): the part of
     ``SelectiveMHA.forward`` with ``self.training`` from the score matrix to ``attn_weight @ v``
     (``modules/selective_attention.py:232-280``).
@@ -543,8 +545,9 @@ def sattn_train_forward(q_rot, k_rot, v, select_gate, log_gate_penalty, lengths=
     the seq-mode gated softmax (``:125-144``) weights ``v``. Returns ``(out, lse, log_gate, stats)``:
     ``out`` ``(b, H, L, D)`` in ``q_rot``'s dtype; fp32 ``lse`` and ``log_gate`` ``(b, H, L)``;
     ``stats`` ``(H, 4)`` fp32 = mean, std, count of valid scores, and a slot the backward fills.
+    ``impl``: ``"auto"`` (tensor cores for 16-bit inputs with ``D`` 64), ``"tc"`` or ``"simt"``.
     """
-    p, dev, keep = _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_causal, scale)
+    p, dev, keep = _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_causal, scale, impl)
     b, H, L, D = q_rot.shape
     out = torch.empty(b, H, L, D, device=dev, dtype=q_rot.dtype)
     lse = torch.empty(b, H, L, device=dev, dtype=torch.float32)
@@ -560,13 +563,14 @@ def sattn_train_forward(q_rot, k_rot, v, select_gate, log_gate_penalty, lengths=
 
 
 def sattn_train_backward(q_rot, k_rot, v, select_gate, out, lse, log_gate, stats, dout, log_gate_penalty,
-                         lengths=None, is_causal=True, scale=None):
+                         lengths=None, is_causal=True, scale=None, impl: str = "auto"):
     """Backward of ``sattn_train_forward`` (C-ABI ``sattn_train_bwd``), the gradients torch's
     autograd gives for ``modules/selective_attention.py:232-280`` including the path through
     the score std. ``out, lse, log_gate, stats`` are the forward's outputs (``stats`` gets its
     backward coefficient written). Returns ``(dq, dk, dv, dselect_gate)`` in ``q_rot``'s dtype.
+    ``impl`` as for the forward (both calls must take the same path: the statistics tiles differ).
     """
-    p, dev, keep = _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_causal, scale)
+    p, dev, keep = _train_params(q_rot, k_rot, v, select_gate, lengths, log_gate_penalty, is_causal, scale, impl)
     dout = _aligned16(to_contiguous(dout.to(q_rot.dtype)))
     if tuple(dout.shape) != tuple(q_rot.shape):
         raise ValueError(f"[dout] expected shape {tuple(q_rot.shape)}, got {tuple(dout.shape)}")

@@ -162,3 +162,41 @@ def test_rejects_unsupported_head_dim():
     q = torch.randn(1, 1, 64, 48, device="cuda")
     with pytest.raises(ValueError):
         kernels.sattn_train_forward(q, q, q, torch.rand(1, 1, 64, device="cuda"), 1.0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_tensor_core_path_matches_oracle(causal, dtype):
+    """16-bit inputs with head_dim 64 run on tcgen05 (impl "tc"): b 2, H 3, L 300 (three
+    128-token tiles, the last partial), ragged lengths, against the oracle in fp32 on the
+    same rounded inputs. Probabilities and dS enter the products in 16 bits."""
+    import selective_attention_b200 as sab
+
+    gen = torch.Generator().manual_seed(31 + causal)
+    b, H, L, D = 2, 3, 300, 64
+    q, k, v = (torch.randn(b, H, L, D, generator=gen).to(dtype) for _ in range(3))
+    sel = torch.sigmoid(torch.randn(b, H, L, generator=gen) + 1.0).to(dtype)
+    dout = torch.randn(b, H, L, D, generator=gen).to(dtype)
+    lengths = torch.tensor([300, 190])
+    g = {"q_rot": q, "k_rot": k, "v": v, "select_gate": sel, "lengths": lengths, "log_gate_penalty": 1.0,
+         "is_causal": causal, "scale": D ** -0.5, "dout": dout}
+    ref_out, ref_std, ref_grads = _oracle_with_grads(g, torch.float32)
+    leaves = {n: g[n].cuda().requires_grad_(True) for n in GRADS}
+    out, std = sab.selective_attn_train(leaves["q_rot"], leaves["k_rot"], leaves["v"], leaves["select_gate"],
+                                        lengths.cuda(), 1.0, causal, impl="tc")
+    out.backward(dout.cuda())
+    sab.check_device_error()
+    assert_bf16_close(out.detach().float().cpu(), ref_out, "out")
+    assert_fp32_close(std.cpu(), ref_std, "std")
+    for n in GRADS:
+        assert_bf16_close(leaves[n].grad.float().cpu(), ref_grads[n], f"d{n}")
+
+
+@pytest.mark.gpu
+def test_tensor_core_path_rejects_fp32():
+    from selective_attention_b200 import kernels
+
+    q = torch.randn(1, 1, 128, 64, device="cuda")
+    with pytest.raises(ValueError):
+        kernels.sattn_train_forward(q, q, q, torch.rand(1, 1, 128, device="cuda"), 1.0, impl="tc")
