@@ -551,6 +551,8 @@ int train_args(const sattn_train_params* p, SattnTrainArgs* a, size_t* need) {
   a->part = reinterpret_cast<double*>(take(B * H * nt * 2 * sizeof(double)));
   a->Di = reinterpret_cast<float*>(take(B * H * L * sizeof(float)));
   a->dlg = reinterpret_cast<float*>(take(B * H * L * sizeof(float)));
+  a->dkb = reinterpret_cast<float*>(take(B * H * L * (size_t)p->head_dim * sizeof(float)));
+  a->gk = reinterpret_cast<float*>(take(B * H * L * (size_t)p->head_dim * sizeof(float)));
   *need = off;
   a->B = (int)B;
   a->H = (int)H;

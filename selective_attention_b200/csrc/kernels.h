@@ -103,6 +103,8 @@ struct SattnTrainArgs {
   double* part;  // (B, H, L / 64, 2) per query tile (128 rows on tensor cores): sum, sum of squares
   float* Di;     // (B, H, L) dout . out
   float* dlg;    // (B, H, L) gradient of the log-gates
+  float* dkb;    // (B, H, L, D) tensor-core path: the softmax part of dk (fp32)
+  float* gk;     // (B, H, L, D) tensor-core path: sum_i (S - mean) q_i over the valid scores
 };
 bool sattn_train_supported(int D);
 bool sattn_train_tc_supported(int D, int dtype);

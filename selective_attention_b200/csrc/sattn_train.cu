@@ -586,8 +586,10 @@ cudaError_t train_bwd_t(const SattnTrainArgs& a, const void* dout, void* dq, voi
 // (128-byte swizzle), products in TMEM, thread = TMEM lane = row of the CTA's own tile.
 //   stats_tc  S = Q K^T per key tile, the valid scores' sums from the TMEM rows
 //   (forward attention: the pipelined prefill kernel with lse, sattn.cu)
-//   bwd_tc    MODE 0 (per key tile): S^T = K Q^T, dP^T = V dO^T -> P^T, dS^T; dv += P^T dO
-//             (TS form, P^T from TMEM), dlg from the rows; MODE 1: dk += dS_total^T Q;
+//   bwd_tc    MODE 0 (per key tile): S^T = K Q^T, dP^T = V dO^T -> P^T, dS^T (softmax part)
+//             and the centred valid scores (S - mean)^T; dv += P^T dO, dk_s += dS^T Q,
+//             g += (S - mean)^T Q (TS form, the 16-bit operands from TMEM), dlg from the rows;
+//             dk = scale (dk_s + c g) once c is known (combine kernel);
 //             MODE 2 (per query tile): S = Q K^T, dP = dO V^T -> dS_total; dq += dS_total K
 // Every wait is bounded; a CTA that gives up records a site code and skips its remaining
 // work (its MMAs and copies in flight are waited for, bounded, before TMEM is released).
@@ -718,9 +720,9 @@ __global__ void __launch_bounds__(kBtThreads, 1) sattn_train_bwd_tc_kernel(
     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
     const float* __restrict__ lg, const float* __restrict__ lse, const float* __restrict__ Di,
     const float* __restrict__ stats, const int64_t* __restrict__ lengths, int H, int L, float scale, int causal,
-    T* __restrict__ outg, float* __restrict__ dlg) {
+    T* __restrict__ outg, float* __restrict__ dlg, float* __restrict__ dkb, float* __restrict__ gk) {
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr bool KEYS = MODE < 2;  // the CTA's own tile is a key tile
+  constexpr bool KEYS = MODE == 0;  // the CTA's own tile is a key tile
   extern __shared__ uint8_t smraw[];
   uint8_t* base = align1024_shared(smraw);
   uint8_t* own1 = base;            // K (key-major) or Q
@@ -732,10 +734,11 @@ __global__ void __launch_bounds__(kBtThreads, 1) sattn_train_bwd_tc_kernel(
   __shared__ uint64_t bars[4];  // own, other[2], mma
   __shared__ uint32_t tslot[1];
   auto bar = [&](int i) { return smem_u32(&bars[i]); };
-  const int bh = blockIdx.x, own = blockIdx.y;
+  const int nt = (L + 127) / 128;
+  // causal: the tiles with the most partners first (key tile 0, query tile nt - 1)
+  const int bh = blockIdx.x, own = KEYS || !causal ? (int)blockIdx.y : nt - 1 - (int)blockIdx.y;
   const int b = bh / H, h = bh - b * H;
   const int len = row_len(lengths, b, L);
-  const int nt = (L + 127) / 128;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = (warp & 3) * 32 + lane, hc = warp >> 2;
   const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;
@@ -774,7 +777,8 @@ __global__ void __launch_bounds__(kBtThreads, 1) sattn_train_bwd_tc_kernel(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  constexpr uint32_t T_S = 0, T_DP = 128, T_W = 256, T_ACC = 320;
+  // MODE 0: dv at T_ACC, the dk parts at T_DK, T_G; MODE 2: dS_total at T_W, dq at T_ACC
+  constexpr uint32_t T_S = 0, T_DP = 128, T_W = 256, T_ACC = MODE == 0 ? 256 : 320, T_DK = 320, T_G = 384;
   constexpr uint32_t ID_SS = idesc_f16(128, 128, BF16, false, false);
   constexpr uint32_t ID_ACC = idesc_f16(128, 64, BF16, false, true);
   const CUtensorMap* m_own1 = KEYS ? &tm_k : &tm_q;
@@ -826,7 +830,10 @@ __global__ void __launch_bounds__(kBtThreads, 1) sattn_train_bwd_tc_kernel(
     ok = __syncthreads_and(got) != 0;
     if (!ok) break;
     tc_fence_after();
-    // P or dS for this thread's 64 columns, into TMEM as 16-bit pairs
+    // this thread's 64 columns, as 16-bit pairs into TMEM. MODE 0 writes three operands over
+    // the S / dP columns it has already read (P and dS into its S half, the centred scores
+    // into its dP half: chunk cc of half hc lands at S + 64 hc + 32 cc, dP + 64 hc + 16 cc);
+    // MODE 2 writes dS_total into T_W.
 #pragma unroll 1
     for (int cc = 0; cc < 2; ++cc) {
       const int c0 = 64 * hc + 32 * cc;
@@ -834,10 +841,10 @@ __global__ void __launch_bounds__(kBtThreads, 1) sattn_train_bwd_tc_kernel(
       tmem_ld32(tmem + tl + T_S + c0, sv);
       tmem_ld32(tmem + tl + T_DP + c0, pv);
       tmem_wait_ld();
-      uint32_t pk[16];
+      uint32_t pk[16], pd[16], pg[16];
 #pragma unroll
       for (int e = 0; e < 32; e += 2) {
-        float w2[2];
+        float wp[2], wd[2], wg[2];
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           const int c = c0 + e + q, x = x0 + c;
@@ -849,31 +856,58 @@ __global__ void __launch_bounds__(kBtThreads, 1) sattn_train_bwd_tc_kernel(
           const float lgt = logit(s, qi, kj, g, L, causal);
           const float p = lgt == -INFINITY ? 0.f : __expf(lgt - lq);
           const float dsm = p * (__uint_as_float(pv[e + q]) - dq);
+          const bool valid = stat_valid(qi, kj, len, causal);
           if (MODE == 0) {
             if (kj != qi) dl += dsm;
-            w2[q] = p;
+            wp[q] = p;
+            wd[q] = dsm;
+            wg[q] = valid ? s - mean : 0.f;
           } else {
-            w2[q] = dsm + (stat_valid(qi, kj, len, causal) ? c_st * (s - mean) : 0.f);
+            wp[q] = dsm + (valid ? c_st * (s - mean) : 0.f);
           }
         }
-        pk[e >> 1] = pack2<T>(w2[0], w2[1]);
+        pk[e >> 1] = pack2<T>(wp[0], wp[1]);
+        if (MODE == 0) {
+          pd[e >> 1] = pack2<T>(wd[0], wd[1]);
+          pg[e >> 1] = pack2<T>(wg[0], wg[1]);
+        }
       }
-      tmem_st16(tmem + tl + T_W + (uint32_t)(c0 >> 1), pk);
+      if (MODE == 0) {
+        tmem_st16(tmem + tl + T_S + (uint32_t)c0, pk);
+        tmem_st16(tmem + tl + T_S + (uint32_t)c0 + 16, pd);
+        tmem_st16(tmem + tl + T_DP + (uint32_t)(64 * hc + 16 * cc), pg);
+      } else {
+        tmem_st16(tmem + tl + T_W + (uint32_t)(c0 >> 1), pk);
+      }
     }
     tmem_wait_st();
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t b3 = smem_u32(MODE == 0 ? oth2(st) : oth1(st));
+      if (MODE == 0) {
+        // K step ks covers other columns 16 ks .. 16 ks + 15: half ks / 4, chunk (ks / 2) % 2
+        const uint32_t bo = smem_u32(oth2(st)), bq = smem_u32(oth1(st));
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks)
-        umma_f16_ts(tmem + T_ACC, tmem + T_W + 8 * ks, sdesc_sw128(b3 + 2048 * ks, 16, 1024), ID_ACC,
-                    (u > 0 || ks > 0) ? 1u : 0u);
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t hh = ks >> 2, cq = (ks >> 1) & 1, sub = ks & 1;
+          const uint32_t aP = T_S + 64 * hh + 32 * cq + 8 * sub, aG = T_DP + 64 * hh + 16 * cq + 8 * sub;
+          const uint32_t acc = (u > 0 || ks > 0) ? 1u : 0u;
+          umma_f16_ts(tmem + T_ACC, tmem + aP, sdesc_sw128(bo + 2048 * ks, 16, 1024), ID_ACC, acc);
+          umma_f16_ts(tmem + T_DK, tmem + aP + 16, sdesc_sw128(bq + 2048 * ks, 16, 1024), ID_ACC, acc);
+          umma_f16_ts(tmem + T_G, tmem + aG, sdesc_sw128(bq + 2048 * ks, 16, 1024), ID_ACC, acc);
+        }
+      } else {
+        const uint32_t b3 = smem_u32(oth1(st));
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          umma_f16_ts(tmem + T_ACC, tmem + T_W + 8 * ks, sdesc_sw128(b3 + 2048 * ks, 16, 1024), ID_ACC,
+                      (u > 0 || ks > 0) ? 1u : 0u);
+      }
       umma_commit(bar(3));
       ++mma_iss;
     }
-    got = mbar_wait(bar(3), mma_wt & 1, kSiteTrMma);  // T_W and the stage are free afterwards
+    got = mbar_wait(bar(3), mma_wt & 1, kSiteTrMma);  // TMEM operands and the stage are free afterwards
     if (got) ++mma_wt;
     ok = __syncthreads_and(got) != 0;
     tc_fence_after();
@@ -893,6 +927,20 @@ __global__ void __launch_bounds__(kBtThreads, 1) sattn_train_bwd_tc_kernel(
                                  pack2<T>(__uint_as_float(av[e + 6]) * mul, __uint_as_float(av[e + 7]) * mul));
     }
     if (MODE == 0) {
+      // dk's two fp32 parts (the softmax term and the statistics one, whose coefficient the
+      // next kernel computes), then dlg
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        tmem_ld32(tmem + tl + (part ? T_G : T_DK) + 32 * hc, av);
+        tmem_wait_ld();
+        if (o < L) {
+          float4* dst = reinterpret_cast<float4*>((part ? gk : dkb) + (rowbase + o) * 64 + 32 * hc);
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            dst[e >> 2] = make_float4(__uint_as_float(av[e]), __uint_as_float(av[e + 1]), __uint_as_float(av[e + 2]),
+                                      __uint_as_float(av[e + 3]));
+        }
+      }
       red[hc][r] = dl;
       __syncthreads();
       if (hc == 0 && o < L) dlg[rowbase + o] = red[0][r] + red[1][r];
@@ -905,6 +953,23 @@ __global__ void __launch_bounds__(kBtThreads, 1) sattn_train_bwd_tc_kernel(
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// dk = scale (dk_s + c g) per element (head_dim 64; four elements a thread).
+template <typename T>
+__global__ void __launch_bounds__(256) sattn_train_dk_combine_kernel(const float* __restrict__ dkb,
+                                                                     const float* __restrict__ gk,
+                                                                     const float* __restrict__ stats, int H, int L,
+                                                                     long long n4, float scale, T* __restrict__ dk) {
+  const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+  if (i >= n4) return;
+  const int h = (int)((i / (16ll * L)) % H);
+  const float c = stats[h * 4 + 3];
+  const float4 a = reinterpret_cast<const float4*>(dkb)[i];
+  const float4 g = reinterpret_cast<const float4*>(gk)[i];
+  const uint32_t lo = pack2<T>(scale * fmaf(c, g.x, a.x), scale * fmaf(c, g.y, a.y));
+  const uint32_t hi = pack2<T>(scale * fmaf(c, g.z, a.z), scale * fmaf(c, g.w, a.w));
+  reinterpret_cast<uint2*>(dk)[i] = make_uint2(lo, hi);
 }
 
 bool train_maps(CUtensorMap* m, const void* p, bool bf16, int L, long long bhn) {
@@ -947,8 +1012,6 @@ cudaError_t train_bwd_tc_t(const SattnTrainArgs& a, const void* dout, void* dq, 
   cudaError_t e;
   if ((e = cudaFuncSetAttribute(sattn_train_bwd_tc_kernel<T, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)kBtSmem)) ||
-      (e = cudaFuncSetAttribute(sattn_train_bwd_tc_kernel<T, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)kBtSmem)) ||
       (e = cudaFuncSetAttribute(sattn_train_bwd_tc_kernel<T, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 (int)kBtSmem)))
     return e;
@@ -959,18 +1022,18 @@ cudaError_t train_bwd_tc_t(const SattnTrainArgs& a, const void* dout, void* dq, 
   const dim3 grid((unsigned)bhn, (unsigned)nt);
   sattn_train_bwd_tc_kernel<T, 0><<<grid, kBtThreads, kBtSmem, s>>>(mq, mk, mv, mo, a.lg, a.lse, a.Di, a.stats,
                                                                     a.lengths, a.H, a.L, a.scale, a.causal, (T*)dv,
-                                                                    a.dlg);
+                                                                    a.dlg, a.dkb, a.gk);
   if ((e = cudaGetLastError())) return e;
   sattn_train_bwd_fin_kernel<T><<<(unsigned)a.H, 256, 0, s>>>((const T*)a.gate, a.lengths, a.dlg, a.B, a.H, a.L,
                                                               a.penalty, a.stats, (T*)dgate);
   if ((e = cudaGetLastError())) return e;
-  sattn_train_bwd_tc_kernel<T, 1><<<grid, kBtThreads, kBtSmem, s>>>(mq, mk, mv, mo, a.lg, a.lse, a.Di, a.stats,
-                                                                    a.lengths, a.H, a.L, a.scale, a.causal, (T*)dk,
-                                                                    nullptr);
+  const long long n4 = rows * 16;  // float4 groups of dk
+  sattn_train_dk_combine_kernel<T><<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(a.dkb, a.gk, a.stats, a.H, a.L, n4,
+                                                                                a.scale, (T*)dk);
   if ((e = cudaGetLastError())) return e;
   sattn_train_bwd_tc_kernel<T, 2><<<grid, kBtThreads, kBtSmem, s>>>(mq, mk, mv, mo, a.lg, a.lse, a.Di, a.stats,
                                                                     a.lengths, a.H, a.L, a.scale, a.causal, (T*)dq,
-                                                                    nullptr);
+                                                                    nullptr, nullptr, nullptr);
   return cudaGetLastError();
 }
 }  // namespace
