@@ -300,6 +300,9 @@ size_t carve_bwd(const Geometry& g, uint8_t* base, BwdArgs* a, ChunkEntry** tabl
   w.A_part = take(nk * H * 4);
   w.bias_part = take(nk * H * 4);
   w.rows4 = take(4 * nk * H * cs * 4);
+  w.prev16 = reinterpret_cast<uint16_t*>(take(nk * H * PN * 2));
+  w.hg16 = reinterpret_cast<uint16_t*>(take(nk * H * PN * 2));
+  w.y16 = reinterpret_cast<uint16_t*>(take((size_t)g.T * H * g.P * 2));
   ChunkEntry* t = nullptr;
   int2* r = nullptr;
   int* c = nullptr;

@@ -57,16 +57,21 @@ struct BwdArgs {
   // workspace
   float *dt, *cum, *states, *hg, *CB, *CBg, *accS, *gC, *dl_part, *A_part, *bias_part;
   float* rows4;  // (4, chunks, H, cs): ddt, gB, row and column decay sums of the tensor-core intra kernel
+  // tensor-core path: 16-bit copies (the inputs' type) of prev and hg (chunks, H, P, N) and,
+  // when y_grad is fp32, of y_grad (b, L, H, P)
+  uint16_t *prev16, *hg16, *y16;
   cudaEvent_t ev[6];
 };
 bool bwd_supported(int P, int N, int cs);
 size_t bwd_dl_slices(int P, int N);
 cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a);
-// ssd_bwd_tc.cu (state-side products on tcgen05: 16-bit u / B / C, P 64, N 128, chunk 256)
+// ssd_bwd_tc.cu (the backward contractions on tcgen05: 16-bit u / B / C, P 64, N 128, chunk 256)
 bool bwd_state_grad_tc_supported(int x_dtype, int y_dtype, int P, int N, int cs);
-cudaError_t launch_bwd_state_grad_tc(const LaunchCtx& c, const BwdArgs& a);
 cudaError_t launch_bwd_chunk_states_tc(const LaunchCtx& c, const BwdArgs& a);  // same shapes
 cudaError_t launch_bwd_intra_tc(const LaunchCtx& c, const BwdArgs& a);         // same shapes; fills rows4
+// per (chunk, group, half) over the group's heads: B_grad / C_grad summed in TMEM (needs prev16,
+// hg16 from the state pass and, for fp32 y_grad, y16 from the recompute)
+cudaError_t launch_bwd_state_grad_grp_tc(const LaunchCtx& c, const BwdArgs& a);
 unsigned int fetch_error_bwd_tc(cudaStream_t s);
 
 // sattn.cu (selective-attention decode step; head_dim 8..256, a power of two)

@@ -269,10 +269,20 @@ __global__ void __launch_bounds__(256, 2) bwd_chunk_states_kernel(
 //   dlast_c = sum(prev_c * g) * exp(cl_c)   (per-warp partials, summed by bwd_intra)
 //   hg[c] <- g;  g = exp(cl_c) g + hg_intra[c];   h_init_grad = g after chunk 0.
 // ===========================================================================
+// With prev16 / hg16 set (the tensor-core path), the chunk-initial states and the state
+// gradients are also written rounded to the inputs' 16-bit type (x16: SSD_BF16 or SSD_F16),
+// as the operands the state-side products load by TMA.
+__device__ __forceinline__ void store4_16(uint16_t* dst, float4 v, int x16) {
+  const uint2 w = x16 == SSD_BF16 ? make_uint2(pack2<__nv_bfloat16>(v.x, v.y), pack2<__nv_bfloat16>(v.z, v.w))
+                                  : make_uint2(pack2<__half>(v.x, v.y), pack2<__half>(v.z, v.w));
+  *reinterpret_cast<uint2*>(dst) = w;
+}
+
 __global__ void __launch_bounds__(256) bwd_state_pass_kernel(
     float* __restrict__ states, float* __restrict__ hg, const float* __restrict__ cum,
     const float* __restrict__ h_init, const float* __restrict__ h_last_grad, float* __restrict__ h_init_grad,
-    float* __restrict__ dl_part, ChunkMap cm, int H, int PN) {
+    float* __restrict__ dl_part, ChunkMap cm, int H, int PN, uint16_t* __restrict__ prev16,
+    uint16_t* __restrict__ hg16, int x16) {
   const int row = blockIdx.z, h = blockIdx.y;
   const int nparts = gridDim.x * 8, part = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int e0 = (blockIdx.x * 256 + threadIdx.x) * 4;
@@ -297,7 +307,10 @@ __global__ void __launch_bounds__(256) bwd_state_pass_kernel(
     const float4 sv = nxt;
     if (act && c + 1 < count) nxt = *reinterpret_cast<const float4*>(at(states, c + 1));
     const float sc = scale(c);
-    if (act) *reinterpret_cast<float4*>(at(states, c)) = prev;
+    if (act) {
+      *reinterpret_cast<float4*>(at(states, c)) = prev;
+      if (prev16) store4_16(prev16 + (at(states, c) - states), prev, x16);
+    }
     prev.x = fmaf(sc, prev.x, sv.x);
     prev.y = fmaf(sc, prev.y, sv.y);
     prev.z = fmaf(sc, prev.z, sv.z);
@@ -320,7 +333,10 @@ __global__ void __launch_bounds__(256) bwd_state_pass_kernel(
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
     if ((threadIdx.x & 31) == 0) dl_part[((long long)(first + c) * H + h) * nparts + part] = d * sc;
-    if (act) *reinterpret_cast<float4*>(at(hg, c)) = gr;
+    if (act) {
+      *reinterpret_cast<float4*>(at(hg, c)) = gr;
+      if (hg16) store4_16(hg16 + (at(hg, c) - hg), gr, x16);
+    }
     gr.x = fmaf(sc, gr.x, hgi.x);
     gr.y = fmaf(sc, gr.y, hgi.y);
     gr.z = fmaf(sc, gr.z, hgi.z);
@@ -1027,7 +1043,8 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
   if (a.ev[1]) cudaEventRecord(a.ev[1], c.stream);
   const int nsl = (int)bwd_dl_slices(P, N);  // per-warp partials of the decay_last gradient
   bwd_state_pass_kernel<<<dim3((unsigned)(nsl / 8), (unsigned)H, (unsigned)c.nrows), 256, 0, c.stream>>>(
-      a.states, a.hg, a.cum, a.h_init, a.h_last_grad, a.h_init_grad, a.dl_part, c.cm, H, PN);
+      a.states, a.hg, a.cum, a.h_init, a.h_last_grad, a.h_init_grad, a.dl_part, c.cm, H, PN, tc ? a.prev16 : nullptr,
+      tc ? a.hg16 : nullptr, a.x_dtype);
   if ((e = cudaGetLastError())) return e;
   const int nt = (cs + 63) / 64;
   bwd_cb_kernel<<<dim3((unsigned)(nt * (nt + 1) / 2), (unsigned)G, (unsigned)nk), 256, kSmemCB, c.stream>>>(
@@ -1035,7 +1052,7 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
   if ((e = cudaGetLastError())) return e;
   if (a.ev[2]) cudaEventRecord(a.ev[2], c.stream);
   if (tc) {
-    if ((e = launch_bwd_state_grad_tc(c, a))) return e;
+    if ((e = launch_bwd_state_grad_grp_tc(c, a))) return e;
   } else {
     bwd_state_grad_kernel<<<gkh, 256, kSmemStateGrad, c.stream>>>(
         a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, a.accS, a.B_grad, a.C_grad, a.gC, c.cm, H, G, P, N,

@@ -1,21 +1,10 @@
-// ssd_bwd_tc.cu - the state-side products of the SSD backward on tcgen05 tensor cores
-// (16-bit u / B / C, headdim 64, dstate 128, chunk 256).
-//
-// Per (chunk, head), with scale_l = exp(min(cum_last - cum_l, 0)), w_l = scale_l dt_l and
-// e_l = exp(cum_l) (all zero at or past the row's length), the same products as
-// bwd_state_grad_kernel in ssd_bwd.cu (backward_kernel.py:255-262, :402-415, :522-538):
-//   accS[l,p]     = scale_l sum_n B[l,n] hg[p,n]   (stored [chunk, head][p / 4][l][4])
-//   B_grad[l,:]  += w_l     sum_p u[l,p] hg[p,:]
-//   C_grad[l,:]  += e_l     sum_p y_grad[l,p] prev[p,:]
-//   gC[l]         = sum_n (that C_grad row) C[l,n]
-// The chunk's hg and prev (fp32 state gradients / states) and, when it is fp32, y_grad are
-// rounded to the input's 16-bit type in shared memory; u and B arrive by TMA. Products
-// accumulate in fp32 in TMEM (accS 64 columns, the B_grad / C_grad row block 128 columns,
-// one after the other), the row factors are applied in the epilogue, where thread = row
-// l = TMEM lane, and B_grad / C_grad are summed over the group's heads with 16-byte fp32
-// atomics as in the CUDA-core kernel. One CTA of 4 warps per (chunk, head), two halves of
-// 128 rows; 99 KB of shared memory and 256 TMEM columns, two CTAs per SM. Every mbarrier
-// wait is bounded; a CTA that gives up records a site code and skips its remaining work.
+// ssd_bwd_tc.cu - the SSD backward's contractions on tcgen05 tensor cores (16-bit u / B / C,
+// headdim 64, dstate 128, chunk 256): the chunk-state recompute, the state-side products and
+// the intra-chunk products; the CUDA-core kernels in ssd_bwd.cu do the scans and the rest.
+// Operands arrive by TMA (128-byte swizzle) or are rounded to 16 bits in shared memory,
+// products accumulate in fp32 in TMEM, and the epilogues read rows with thread = row = TMEM
+// lane. Every mbarrier wait is bounded; a CTA that gives up records a site code, lets what it
+// has in flight land (bounded) and skips its remaining work.
 #include <cudaTypedefs.h>
 
 #include <type_traits>
@@ -32,13 +21,6 @@ using namespace sm100;
 namespace {
 
 constexpr unsigned int kSiteBwdTcTma = 0x121, kSiteBwdTcMma = 0x122;
-constexpr int kBgThreads = 128;
-// hg16 [2 n-blocks][64 p][128 B] | prev16 (same) | B [2 n-blocks][128 l][128 B] | u [128 l][128 B]
-// | y_grad [128 l][128 B] | row factors [3][256] | barriers, TMEM slot
-constexpr int kBgOffHg = 0, kBgOffPv = 16384, kBgOffB = 32768, kBgOffU = 65536, kBgOffY = 81920,
-              kBgOffF = 98304, kBgOffBar = kBgOffF + 3 * 1024;
-constexpr size_t kBgSmem = 1024 + kBgOffBar + 64;
-
 // 8 elements of a 16-byte chunk times w (fp32 products, one rounding to 16 bits).
 template <typename T16>
 __device__ __forceinline__ uint4 scaled8(uint4 a, float w) {
@@ -50,266 +32,6 @@ __device__ __forceinline__ uint4 scaled8(uint4 a, float w) {
   f = unpack2<T16>(a.w); v.w = pack2<T16>(f.x * w, f.y * w);
   return v;
 }
-
-template <bool BF16>
-__device__ __forceinline__ uint32_t pack2f(float a, float b) {
-  return pack2<typename std::conditional<BF16, __nv_bfloat16, __half>::type>(a, b);
-}
-
-// Rounds a (64 x 128) fp32 state block [p][n] (n contiguous) to 16 bits into the 128-byte
-// swizzled layout [n / 64][p][n % 64]: K-major over n for one MMA and MN-major over n for
-// the other.
-template <bool BF16>
-__device__ __forceinline__ void stage_state16(uint8_t* dst, const float* __restrict__ src) {
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int q = threadIdx.x + kBgThreads * i;  // 1024 chunks of 8 elements
-    const int p = q >> 4, n0 = (q & 15) * 8;
-    const float4 a = __ldg(reinterpret_cast<const float4*>(src + p * 128 + n0));
-    const float4 b = __ldg(reinterpret_cast<const float4*>(src + p * 128 + n0 + 4));
-    const uint4 v = make_uint4(pack2f<BF16>(a.x, a.y), pack2f<BF16>(a.z, a.w), pack2f<BF16>(b.x, b.y),
-                               pack2f<BF16>(b.z, b.w));
-    *reinterpret_cast<uint4*>(dst + (n0 >> 6) * 8192 + sw128_off((uint32_t)p, (uint32_t)((n0 & 63) >> 3))) = v;
-  }
-}
-
-template <bool BF16, typename YT>
-__global__ void __launch_bounds__(kBgThreads, 2) bwd_state_grad_tc_kernel(
-    const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_u,
-    const __grid_constant__ CUtensorMap tm_y, const void* __restrict__ Cm, const YT* __restrict__ yg,
-    const float* __restrict__ dt, const float* __restrict__ cum, const float* __restrict__ prev,
-    const float* __restrict__ hg, float* __restrict__ accS_out, float* __restrict__ Bgrad,
-    float* __restrict__ Cgrad, float* __restrict__ gC_out, ChunkMap cm, int H, int G) {
-  using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  constexpr bool kY16 = sizeof(YT) == 2;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = align1024_shared(smem_raw);
-  uint8_t* sHg = sm + kBgOffHg;
-  uint8_t* sPv = sm + kBgOffPv;
-  uint8_t* sB = sm + kBgOffB;
-  uint8_t* sU = sm + kBgOffU;
-  uint8_t* sY = sm + kBgOffY;
-  float* sS = reinterpret_cast<float*>(sm + kBgOffF);
-  float* wS = sS + 256;
-  float* eS = wS + 256;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kBgOffBar);  // TMA, MMA
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
-  const uint32_t bar_tma = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
-
-  const int h = blockIdx.x, k = blockIdx.y;
-  ChunkInfo ci;
-  if (!chunk_info(cm, k, ci)) return;
-  const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5;
-  const long long kh = (long long)k * H + h;
-  const int vl = ci.vlim;
-  if (tid == 0) {
-    prefetch_tmap(&tm_b);
-    prefetch_tmap(&tm_u);
-    if (kY16) prefetch_tmap(&tm_y);
-    mbar_init(bar_tma, 1);
-    mbar_init(bar_mma, 1);
-    fence_mbar_init();
-  }
-  if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
-  stage_state16<BF16>(sHg, hg + kh * 8192);
-  stage_state16<BF16>(sPv, prev + kh * 8192);
-  {
-    const float clast = cum[kh * 256 + 255];
-    for (int i = tid; i < 256; i += kBgThreads) {
-      const float c = cum[kh * 256 + i];
-      const float sc = i < vl ? __expf(fminf(clast - c, 0.f)) : 0.f;
-      sS[i] = sc;
-      wS[i] = sc * dt[kh * 256 + i];
-      eS[i] = i < vl ? __expf(c) : 0.f;
-    }
-  }
-  fence_proxy_async_smem();  // the 16-bit states are operands of the MMAs
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
-  const uint32_t tl = (uint32_t)(warp * 32) << 16;
-  constexpr uint32_t T_ACC = 0, T_G = 128;
-  constexpr uint32_t ID_S = idesc_f16(128, 64, BF16, false, false);   // accS: K = n
-  constexpr uint32_t ID_G = idesc_f16(128, 128, BF16, false, true);   // B_grad / C_grad: K = p, N = n MN-major
-  int uses_tma = 0, uses_mma = 0;
-  bool ok = true;
-  const int r = tid;  // row of the half = TMEM lane
-
-  for (int m = 0; m < 2 && ok; ++m) {
-    const int l0 = 128 * m;
-    if (l0 >= ci.lim) break;
-    const int t0 = (int)(ci.tok0 + l0);
-    if (tid == 0) {
-      mbar_expect_tx(bar_tma, 32768u + 16384u + (kY16 ? 16384u : 0u));
-      tma_load_3d(smem_u32(sB), &tm_b, 0, g, t0, bar_tma);
-      tma_load_3d(smem_u32(sB + 16384), &tm_b, 64, g, t0, bar_tma);
-      tma_load_3d(smem_u32(sU), &tm_u, 0, h, t0, bar_tma);
-      if (kY16) tma_load_3d(smem_u32(sY), &tm_y, 0, h, t0, bar_tma);
-    }
-    if (!kY16) {
-      // y_grad rows (fp32) rounded to 16 bits, K-major over p; rows past the length are 0
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int q = tid + kBgThreads * i;  // 1024 chunks of 8 elements
-        const int row = q >> 3, c8 = q & 7, l = l0 + row;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (l < vl) {
-          const float* s = reinterpret_cast<const float*>(yg) + ((ci.tok0 + l) * H + h) * 64 + c8 * 8;
-          const float4 a = __ldg(reinterpret_cast<const float4*>(s));
-          const float4 b = __ldg(reinterpret_cast<const float4*>(s + 4));
-          v = make_uint4(pack2f<BF16>(a.x, a.y), pack2f<BF16>(a.z, a.w), pack2f<BF16>(b.x, b.y),
-                         pack2f<BF16>(b.z, b.w));
-        }
-        *reinterpret_cast<uint4*>(sY + sw128_off((uint32_t)row, (uint32_t)c8)) = v;
-      }
-    }
-    const bool landed = mbar_wait(bar_tma, uses_tma & 1, kSiteBwdTcTma);
-    ++uses_tma;
-    if (landed && vl - l0 < 128) {
-      // rows at or past the length: zeros in every operand (their row factors are 0,
-      // but the data there need not be finite)
-      const int z0 = max(vl - l0, 0);
-      for (int q = tid; q < (128 - z0) * 8; q += kBgThreads) {
-        const int row = z0 + (q >> 3);
-        const uint32_t off = (uint32_t)row * 128u + (uint32_t)(q & 7) * 16u;
-        const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(sB + off) = zero;
-        *reinterpret_cast<uint4*>(sB + 16384 + off) = zero;
-        *reinterpret_cast<uint4*>(sU + off) = zero;
-        *reinterpret_cast<uint4*>(sY + off) = zero;
-      }
-    }
-    fence_proxy_async_smem();
-    ok = __syncthreads_and(landed) != 0;
-    if (!ok) break;
-    if (tid == 0) {
-      tc_fence_after();
-      // accS = B hg^T: A = B rows (K = n in two 64-blocks), B = hg16 (N = p, K = n)
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
-        umma_f16(tmem + T_ACC, sdesc_sw128(smem_u32(sB) + hf * 16384 + kk, 16, 1024),
-                 sdesc_sw128(smem_u32(sHg) + hf * 8192 + kk, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
-      }
-      // B_grad rows = u hg: A = u rows (K = p), B = hg16 as N = n MN-major (64-blocks 8 KB apart)
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma_f16(tmem + T_G, sdesc_sw128(smem_u32(sU) + ks * 32, 16, 1024),
-                 sdesc_sw128(smem_u32(sHg) + ks * 2048, 8192, 1024), ID_G, ks > 0 ? 1u : 0u);
-      umma_commit(bar_mma);
-    }
-    ok = __syncthreads_and(mbar_wait(bar_mma, uses_mma & 1, kSiteBwdTcMma)) != 0;
-    ++uses_mma;
-    tc_fence_after();
-    if (!ok) break;
-    const int l = l0 + r;
-    {
-      // accS row l (64 columns) times scale_l, stored as [p / 4][l][4] per (chunk, head) so
-      // that the lanes' 16-byte stores (and the intra kernel's loads) are contiguous
-      float4* o = reinterpret_cast<float4*>(accS_out) + kh * 16 * 256 + l;
-      const float sc = sS[l];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + tl + T_ACC + 32 * c, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; e += 4)
-          o[(8 * c + e / 4) * 256] =
-              make_float4(__uint_as_float(v[e]) * sc, __uint_as_float(v[e + 1]) * sc, __uint_as_float(v[e + 2]) * sc,
-                          __uint_as_float(v[e + 3]) * sc);
-      }
-      // B_grad row l (128 columns) times w_l, summed over the group's heads
-      const float wl = wS[l];
-      float* bgr = Bgrad + ((ci.tok0 + l) * G + g) * 128;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + tl + T_G + 32 * c, v);
-        tmem_wait_ld();
-        if (l < vl) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            atomicAdd(reinterpret_cast<float4*>(bgr + 32 * c + e),
-                      make_float4(__uint_as_float(v[e]) * wl, __uint_as_float(v[e + 1]) * wl,
-                                  __uint_as_float(v[e + 2]) * wl, __uint_as_float(v[e + 3]) * wl));
-        }
-      }
-    }
-    // C_grad rows = y_grad prev into the same TMEM columns, once every thread has read them
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks)
-        umma_f16(tmem + T_G, sdesc_sw128(smem_u32(sY) + ks * 32, 16, 1024),
-                 sdesc_sw128(smem_u32(sPv) + ks * 2048, 8192, 1024), ID_G, ks > 0 ? 1u : 0u);
-      umma_commit(bar_mma);
-    }
-    ok = __syncthreads_and(mbar_wait(bar_mma, uses_mma & 1, kSiteBwdTcMma)) != 0;
-    ++uses_mma;
-    tc_fence_after();
-    if (!ok) break;
-    {
-      const float el = eS[l];
-      float* cgr = Cgrad + ((ci.tok0 + l) * G + g) * 128;
-      const uint16_t* crow = reinterpret_cast<const uint16_t*>(Cm) + ((ci.tok0 + l) * G + g) * 128;
-      float gsum = 0.f;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + tl + T_G + 32 * c, v);
-        tmem_wait_ld();
-        if (l < vl) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 8) {
-            const uint4 c8 = __ldg(reinterpret_cast<const uint4*>(crow + 32 * c + e));
-            const uint32_t cw[4] = {c8.x, c8.y, c8.z, c8.w};
-            float x[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) x[q] = __uint_as_float(v[e + q]) * el;
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float2 cf = unpack2<T16>(cw[q]);
-              gsum = fmaf(x[2 * q], cf.x, fmaf(x[2 * q + 1], cf.y, gsum));
-            }
-            atomicAdd(reinterpret_cast<float4*>(cgr + 32 * c + e), make_float4(x[0], x[1], x[2], x[3]));
-            atomicAdd(reinterpret_cast<float4*>(cgr + 32 * c + e + 4), make_float4(x[4], x[5], x[6], x[7]));
-          }
-        }
-      }
-      gC_out[kh * 256 + l] = l < vl ? gsum : 0.f;
-    }
-    tc_fence_before();
-    __syncthreads();
-  }
-  if (!ok && tid == 0) {
-    // let an MMA still in flight land before TMEM is released (bounded)
-    if (uses_mma > 0) mbar_wait(bar_mma, (uses_mma - 1) & 1, kSiteBwdTcMma);
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 256);
-}
-
-template <bool BF16, typename YT>
-cudaError_t launch_typed(const LaunchCtx& c, const BwdArgs& a) {
-  CUtensorMap mb, mu, my;
-  if (!make_map_3d(&mb, a.B, BF16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128) ||
-      !make_map_3d(&mu, a.u, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
-      !make_map_3d(&my, sizeof(YT) == 2 ? a.y_grad : a.u, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128))
-    return cudaErrorInvalidValue;
-  auto kern = bwd_state_grad_tc_kernel<BF16, YT>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBgSmem);
-  if (e != cudaSuccess) return e;
-  kern<<<dim3((unsigned)c.H, (unsigned)c.nchunks_max), kBgThreads, kBgSmem, c.stream>>>(
-      mb, mu, my, a.C, reinterpret_cast<const YT*>(a.y_grad), a.dt, a.cum, a.states, a.hg, a.accS, a.B_grad,
-      a.C_grad, a.gC, c.cm, c.H, c.G);
-  return cudaGetLastError();
-}
-
 
 // ---------------------------------------------------------------------------
 // Chunk states and intra-chunk state gradients (ssd_bwd.cu bwd_chunk_states_kernel's
@@ -330,7 +52,7 @@ __global__ void __launch_bounds__(kCsThreads) bwd_chunk_states_tc_kernel(
     const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_b,
     const __grid_constant__ CUtensorMap tm_y, const __grid_constant__ CUtensorMap tm_c, const YT* __restrict__ yg,
     const float* __restrict__ dt, const float* __restrict__ cum, float* __restrict__ states, float* __restrict__ hg,
-    ChunkMap cm, int H, int G) {
+    ChunkMap cm, int H, int G, uint16_t* __restrict__ y16out) {
   using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   constexpr bool kY16 = sizeof(YT) == 2;
   extern __shared__ uint8_t smem_raw[];
@@ -389,12 +111,18 @@ __global__ void __launch_bounds__(kCsThreads) bwd_chunk_states_tc_kernel(
         const int q = tid + kCsThreads * i, row = q >> 3, c8 = q & 7, l = 128 * ph + row;
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         const float w = sW[l];
-        if (w != 0.f) {
-          const float* src = reinterpret_cast<const float*>(yg) + ((ci.tok0 + l) * H + h) * 64 + c8 * 8;
+        // every row below the length is read: the 16-bit copy needs it even where e_l = 0
+        if (l < vl && (w != 0.f || y16out)) {
+          const long long off = ((ci.tok0 + l) * H + h) * 64 + c8 * 8;
+          const float* src = reinterpret_cast<const float*>(yg) + off;
           const float4 a = __ldg(reinterpret_cast<const float4*>(src));
           const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
-          v = make_uint4(pack2<T16>(a.x * w, a.y * w), pack2<T16>(a.z * w, a.w * w), pack2<T16>(b.x * w, b.y * w),
-                         pack2<T16>(b.z * w, b.w * w));
+          if (w != 0.f)
+            v = make_uint4(pack2<T16>(a.x * w, a.y * w), pack2<T16>(a.z * w, a.w * w), pack2<T16>(b.x * w, b.y * w),
+                           pack2<T16>(b.z * w, b.w * w));
+          if (y16out)  // the rows rounded, unscaled, for the later kernels' TMA loads
+            *reinterpret_cast<uint4*>(y16out + off) = make_uint4(pack2<T16>(a.x, a.y), pack2<T16>(a.z, a.w),
+                                                                 pack2<T16>(b.x, b.y), pack2<T16>(b.z, b.w));
         }
         *reinterpret_cast<uint4*>(sX + sw128_off((uint32_t)row, (uint32_t)c8)) = v;
       }
@@ -459,7 +187,8 @@ cudaError_t launch_states_typed(const LaunchCtx& c, const BwdArgs& a) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCsSmem);
   if (e != cudaSuccess) return e;
   kern<<<dim3((unsigned)c.H, (unsigned)c.nchunks_max, 2u), kCsThreads, kCsSmem, c.stream>>>(
-      mu, mb, my, mc, reinterpret_cast<const YT*>(a.y_grad), a.dt, a.cum, a.states, a.hg, c.cm, c.H, c.G);
+      mu, mb, my, mc, reinterpret_cast<const YT*>(a.y_grad), a.dt, a.cum, a.states, a.hg, c.cm, c.H, c.G,
+      sizeof(YT) == 2 ? nullptr : a.y16);
   return cudaGetLastError();
 }
 
@@ -784,6 +513,244 @@ cudaError_t launch_intra_typed(const LaunchCtx& c, const BwdArgs& a) {
       c.cm, c.H, c.G, plane);
   return cudaGetLastError();
 }
+
+// ---------------------------------------------------------------------------
+// State-side products per (chunk, group, 128-row half), looping over the group's heads, so
+// that B_grad and C_grad sum over the heads inside TMEM (no atomics):
+//   accS_h[l,p] = scale_l sum_n B[l,n] hg_h[p,n]              (stored per head, blocked)
+//   Q_h[l,p]    = sum_n C[l,n] prev_h[p,n];  gC_h[l] = sum_p (e_l y_h[l,p]) Q_h[l,p]
+//   B_grad[l,:] = sum_h sum_p (w_l u_h[l,p]) hg_h[p,:]       (TMEM, over the heads)
+//   C_grad[l,:] = sum_h sum_p (e_l y_h[l,p]) prev_h[p,:]
+// with w_l = scale_l dt_l and e_l = exp(cum_l) of head h (0 at or past the length). The
+// 16-bit prev / hg (from the state pass) and u, y_grad rows arrive by TMA in a two-stage ring
+// over the heads; u and y_grad rows are scaled in place (16-bit products), B and C rows stay.
+// 8 warps: warps w and w + 4 share TMEM lane quadrant w % 4 and split the columns.
+// ---------------------------------------------------------------------------
+constexpr int kSgThreads = 256;
+constexpr int kSgStage = 65536;  // hg16 | prev16 (2 n-blocks x 64 p x 128 B each) | u | y (128 rows x 128 B)
+constexpr size_t kSgSmem = 1024 + 65536 + 2 * kSgStage;
+
+template <bool BF16>
+__global__ void __launch_bounds__(kSgThreads, 1) bwd_state_grad_grp_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_c,
+    const __grid_constant__ CUtensorMap tm_u, const __grid_constant__ CUtensorMap tm_y,
+    const __grid_constant__ CUtensorMap tm_hg, const __grid_constant__ CUtensorMap tm_pv, const float* __restrict__ dt,
+    const float* __restrict__ cum, float* __restrict__ accS_out, float* __restrict__ Bgrad,
+    float* __restrict__ Cgrad, float* __restrict__ gC_out, ChunkMap cm, int H, int G) {
+  using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024_shared(smem_raw);
+  uint8_t* sB = sm;          // [2 n-blocks][128 rows][128 B]
+  uint8_t* sC = sm + 32768;  // same
+  auto sHg = [&](int st) { return sm + 65536 + kSgStage * st; };
+  auto sPv = [&](int st) { return sHg(st) + 16384; };
+  auto sU = [&](int st) { return sHg(st) + 32768; };
+  auto sY = [&](int st) { return sHg(st) + 49152; };
+  __shared__ float sS[2][128], wS[2][128], eS[2][128], gcp[2][128];
+  __shared__ uint64_t bars[4];  // B / C, stage[2], mma
+  __shared__ uint32_t tslot[1];
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+  const int m = blockIdx.x, g = blockIdx.y, k = blockIdx.z;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int l0 = 128 * m;
+  if (l0 >= ci.lim) return;
+  const int HG = H / G, vl = ci.vlim;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = (warp & 3) * 32 + lane, hc = warp >> 2, l = l0 + r;
+  const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;
+  const int t0 = (int)(ci.tok0 + l0);
+  auto factors = [&](int st, int j) {  // row factors of head g HG + j (threads < 128)
+    if (tid < 128) {
+      const long long kh = (long long)k * H + g * HG + j;
+      const int li = l0 + tid;
+      const float c = cum[kh * 256 + li], clast = cum[kh * 256 + 255];
+      const float sc = li < vl ? __expf(fminf(clast - c, 0.f)) : 0.f;
+      sS[st][tid] = sc;
+      wS[st][tid] = sc * dt[kh * 256 + li];
+      eS[st][tid] = li < vl ? __expf(c) : 0.f;
+    }
+  };
+  int ld_iss[2] = {0, 0}, ld_wt[2] = {0, 0}, mma_iss = 0, mma_wt = 0;  // thread 0's books
+  auto load_stage = [&](int st, int j) {  // thread 0
+    const int h = g * HG + j, kh = k * H + h;
+    mbar_expect_tx(bar(1 + st), (uint32_t)kSgStage);
+    tma_load_3d(smem_u32(sHg(st)), &tm_hg, 0, 0, kh, bar(1 + st));
+    tma_load_3d(smem_u32(sHg(st)) + 8192, &tm_hg, 64, 0, kh, bar(1 + st));
+    tma_load_3d(smem_u32(sPv(st)), &tm_pv, 0, 0, kh, bar(1 + st));
+    tma_load_3d(smem_u32(sPv(st)) + 8192, &tm_pv, 64, 0, kh, bar(1 + st));
+    tma_load_3d(smem_u32(sU(st)), &tm_u, 0, h, t0, bar(1 + st));
+    tma_load_3d(smem_u32(sY(st)), &tm_y, 0, h, t0, bar(1 + st));
+    ++ld_iss[st];
+  };
+  if (tid == 0) {
+    prefetch_tmap(&tm_b);
+    prefetch_tmap(&tm_c);
+    prefetch_tmap(&tm_u);
+    prefetch_tmap(&tm_y);
+    prefetch_tmap(&tm_hg);
+    prefetch_tmap(&tm_pv);
+    for (int i = 0; i < 4; ++i) mbar_init(bar(i), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 512);
+  factors(0, 0);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  constexpr uint32_t T_S = 0, T_Q = 64, T_BG = 128, T_CG = 256;
+  constexpr uint32_t ID_S = idesc_f16(128, 64, BF16, false, false);  // K = n
+  constexpr uint32_t ID_G = idesc_f16(128, 128, BF16, false, true);  // K = p, N = n MN-major
+  if (tid == 0) {
+    mbar_expect_tx(bar(0), 65536u);
+    tma_load_3d(smem_u32(sB), &tm_b, 0, g, t0, bar(0));
+    tma_load_3d(smem_u32(sB) + 16384, &tm_b, 64, g, t0, bar(0));
+    tma_load_3d(smem_u32(sC), &tm_c, 0, g, t0, bar(0));
+    tma_load_3d(smem_u32(sC) + 16384, &tm_c, 64, g, t0, bar(0));
+    load_stage(0, 0);
+  }
+  bool ok = mbar_wait(bar(0), 0, kSiteBwdTcTma);
+  if (ok && vl - l0 < 128) {  // B / C rows at or past the length: zeros
+    for (int q = tid; q < (128 - max(vl - l0, 0)) * 8; q += kSgThreads) {
+      const uint32_t off = (uint32_t)(max(vl - l0, 0) + (q >> 3)) * 128u + (uint32_t)(q & 7) * 16u;
+      const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(sB + off) = z;
+      *reinterpret_cast<uint4*>(sB + 16384 + off) = z;
+      *reinterpret_cast<uint4*>(sC + off) = z;
+      *reinterpret_cast<uint4*>(sC + 16384 + off) = z;
+    }
+  }
+  ok = __syncthreads_and(ok) != 0;
+  for (int j = 0; j < HG && ok; ++j) {
+    const int st = j & 1;
+    const long long kh = (long long)k * H + g * HG + j;
+    if (j + 1 < HG) {  // the next head's stage: its previous user's MMAs completed last iteration
+      if (tid == 0) load_stage(st ^ 1, j + 1);
+      factors(st ^ 1, j + 1);
+    }
+    bool got = mbar_wait(bar(1 + st), (j >> 1) & 1, kSiteBwdTcTma);
+    if (tid == 0 && got) ++ld_wt[st];
+    ok = __syncthreads_and(got) != 0;
+    if (!ok) break;
+    // u rows times w_l and y_grad rows times e_l, in place (rows past the length become 0)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + kSgThreads * i, row = q >> 3;
+      uint4* pu = reinterpret_cast<uint4*>(sU(st) + q * 16);
+      uint4* py = reinterpret_cast<uint4*>(sY(st) + q * 16);
+      const float w = wS[st][row], e = eS[st][row];
+      *pu = w == 0.f ? make_uint4(0u, 0u, 0u, 0u) : scaled8<T16>(*pu, w);
+      *py = e == 0.f ? make_uint4(0u, 0u, 0u, 0u) : scaled8<T16>(*py, e);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t hf = ks >> 2, kk = (ks & 3) * 32;
+        umma_f16(tmem + T_S, sdesc_sw128(smem_u32(sB) + hf * 16384 + kk, 16, 1024),
+                 sdesc_sw128(smem_u32(sHg(st)) + hf * 8192 + kk, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
+        umma_f16(tmem + T_Q, sdesc_sw128(smem_u32(sC) + hf * 16384 + kk, 16, 1024),
+                 sdesc_sw128(smem_u32(sPv(st)) + hf * 8192 + kk, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
+      }
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t acc = (j > 0 || ks > 0) ? 1u : 0u;
+        umma_f16(tmem + T_BG, sdesc_sw128(smem_u32(sU(st)) + ks * 32, 16, 1024),
+                 sdesc_sw128(smem_u32(sHg(st)) + ks * 2048, 8192, 1024), ID_G, acc);
+        umma_f16(tmem + T_CG, sdesc_sw128(smem_u32(sY(st)) + ks * 32, 16, 1024),
+                 sdesc_sw128(smem_u32(sPv(st)) + ks * 2048, 8192, 1024), ID_G, acc);
+      }
+      umma_commit(bar(3));
+      ++mma_iss;
+    }
+    got = mbar_wait(bar(3), mma_wt & 1, kSiteBwdTcMma);
+    if (got) ++mma_wt;
+    ok = __syncthreads_and(got) != 0;
+    if (!ok) break;
+    tc_fence_after();
+    {
+      // accS row l, this thread's 32 columns p, times scale_l, stored blocked [p / 4][l][4]
+      uint32_t v[32];
+      tmem_ld32(tmem + tl + T_S + 32 * hc, v);
+      tmem_wait_ld();
+      const float sc = sS[st][r];
+      float4* o = reinterpret_cast<float4*>(accS_out) + (kh * 16 + 8 * hc) * 256 + l;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4)
+        o[(e >> 2) * 256] = make_float4(__uint_as_float(v[e]) * sc, __uint_as_float(v[e + 1]) * sc,
+                                        __uint_as_float(v[e + 2]) * sc, __uint_as_float(v[e + 3]) * sc);
+      // gC partial: the scaled y_grad row (shared memory) against Q's row
+      tmem_ld32(tmem + tl + T_Q + 32 * hc, v);
+      tmem_wait_ld();
+      float acc = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        const uint4 y8 = *reinterpret_cast<const uint4*>(sY(st) + sw128_off((uint32_t)r, (uint32_t)(4 * hc + c8)));
+        const uint32_t yw[4] = {y8.x, y8.y, y8.z, y8.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 yf = unpack2<T16>(yw[q]);
+          acc = fmaf(yf.x, __uint_as_float(v[8 * c8 + 2 * q]), fmaf(yf.y, __uint_as_float(v[8 * c8 + 2 * q + 1]), acc));
+        }
+      }
+      gcp[hc][r] = acc;
+    }
+    tc_fence_before();
+    __syncthreads();  // T_S / T_Q read before the next head's products, partials complete
+    if (hc == 0) gC_out[kh * 256 + l] = l < vl ? gcp[0][r] + gcp[1][r] : 0.f;
+  }
+  if (ok) {
+    // B_grad / C_grad rows of this half: 64 of the 128 columns per thread, plain stores
+    tc_fence_after();
+#pragma unroll 1
+    for (int part = 0; part < 2; ++part) {
+      float* dst = (part ? Cgrad : Bgrad) + ((ci.tok0 + l) * G + g) * 128 + 64 * hc;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + tl + (part ? T_CG : T_BG) + 64 * hc + 32 * c, v);
+        tmem_wait_ld();
+        if (l < ci.lim) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            *reinterpret_cast<float4*>(dst + 32 * c + e) =
+                make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]), __uint_as_float(v[e + 2]),
+                            __uint_as_float(v[e + 3]));
+        }
+      }
+    }
+  } else if (tid == 0) {  // let what is in flight land before TMEM and the CTA go away (bounded)
+    while (mma_wt < mma_iss && mbar_wait(bar(3), mma_wt & 1, kSiteBwdTcMma)) ++mma_wt;
+    for (int st = 0; st < 2; ++st)
+      while (ld_wt[st] < ld_iss[st] && mbar_wait(bar(1 + st), ld_wt[st] & 1, kSiteBwdTcTma)) ++ld_wt[st];
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+template <bool BF16>
+cudaError_t launch_grp_typed(const LaunchCtx& c, const BwdArgs& a, const void* y16) {
+  CUtensorMap mb, mc, mu, my, mh, mp;
+  const uint64_t nkh = (uint64_t)c.nchunks_max * (uint64_t)c.H;
+  if (!make_map_3d(&mb, a.B, BF16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&mc, a.C, BF16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&mu, a.u, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&my, y16, BF16, 64, (uint64_t)c.H, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&mh, a.hg16, BF16, 128, 64, nkh, 64, 64, 1) ||
+      !make_map_3d(&mp, a.prev16, BF16, 128, 64, nkh, 64, 64, 1))
+    return cudaErrorInvalidValue;
+  auto kern = bwd_state_grad_grp_tc_kernel<BF16>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSgSmem);
+  if (e != cudaSuccess) return e;
+  kern<<<dim3(2u, (unsigned)c.G, (unsigned)c.nchunks_max), kSgThreads, kSgSmem, c.stream>>>(
+      mb, mc, mu, my, mh, mp, a.dt, a.cum, a.accS, a.B_grad, a.C_grad, a.gC, c.cm, c.H, c.G);
+  return cudaGetLastError();
+}
 }  // namespace
 
 bool bwd_state_grad_tc_supported(int x_dtype, int y_dtype, int P, int N, int cs) {
@@ -791,15 +758,6 @@ bool bwd_state_grad_tc_supported(int x_dtype, int y_dtype, int P, int N, int cs)
   return x16 && (y_dtype == SSD_F32 || y_dtype == x_dtype) && P == 64 && N == 128 && cs == 256;
 }
 
-cudaError_t launch_bwd_state_grad_tc(const LaunchCtx& c, const BwdArgs& a) {
-  if (c.nchunks_max > 65535 || c.H > 65535) return cudaErrorInvalidValue;
-  if (a.x_dtype == SSD_BF16) {
-    if (a.y_dtype == SSD_F32) return launch_typed<true, float>(c, a);
-    return launch_typed<true, __nv_bfloat16>(c, a);
-  }
-  if (a.y_dtype == SSD_F32) return launch_typed<false, float>(c, a);
-  return launch_typed<false, __half>(c, a);
-}
 
 cudaError_t launch_bwd_chunk_states_tc(const LaunchCtx& c, const BwdArgs& a) {
   if (c.nchunks_max > 65535 || c.H > 65535) return cudaErrorInvalidValue;
@@ -811,14 +769,18 @@ cudaError_t launch_bwd_chunk_states_tc(const LaunchCtx& c, const BwdArgs& a) {
   return launch_states_typed<false, __half>(c, a);
 }
 
+cudaError_t launch_bwd_state_grad_grp_tc(const LaunchCtx& c, const BwdArgs& a) {
+  if (c.nchunks_max > 65535 || c.G > 65535) return cudaErrorInvalidValue;
+  const void* y16 = a.y_dtype == SSD_F32 ? (const void*)a.y16 : a.y_grad;  // y16: written by the recompute
+  return a.x_dtype == SSD_BF16 ? launch_grp_typed<true>(c, a, y16) : launch_grp_typed<false>(c, a, y16);
+}
+
 cudaError_t launch_bwd_intra_tc(const LaunchCtx& c, const BwdArgs& a) {
   if (c.nchunks_max > 65535 || c.H > 65535) return cudaErrorInvalidValue;
-  if (a.x_dtype == SSD_BF16) {
-    if (a.y_dtype == SSD_F32) return launch_intra_typed<true, float>(c, a);
-    return launch_intra_typed<true, __nv_bfloat16>(c, a);
-  }
-  if (a.y_dtype == SSD_F32) return launch_intra_typed<false, float>(c, a);
-  return launch_intra_typed<false, __half>(c, a);
+  BwdArgs b = a;
+  if (a.y_dtype == SSD_F32) b.y_grad = a.y16;  // the 16-bit copy the recompute wrote
+  if (a.x_dtype == SSD_BF16) return launch_intra_typed<true, __nv_bfloat16>(c, b);
+  return launch_intra_typed<false, __half>(c, b);
 }
 
 SSDB200_DEFINE_ERROR_FETCH(fetch_error_bwd_tc)
