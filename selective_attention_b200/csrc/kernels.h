@@ -72,6 +72,8 @@ cudaError_t launch_bwd_intra_tc(const LaunchCtx& c, const BwdArgs& a);         /
 // per (chunk, group, half) over the group's heads: B_grad / C_grad summed in TMEM (needs prev16,
 // hg16 from the state pass and, for fp32 y_grad, y16 from the recompute)
 cudaError_t launch_bwd_state_grad_grp_tc(const LaunchCtx& c, const BwdArgs& a);
+cudaError_t launch_bwd_cb_tc(const LaunchCtx& c, const BwdArgs& a);   // CB = C B^T, lower 128-row blocks
+cudaError_t launch_bwd_bmm_tc(const LaunchCtx& c, const BwdArgs& a);  // CB_grad products into B_grad / C_grad
 unsigned int fetch_error_bwd_tc(cudaStream_t s);
 
 // sattn.cu (selective-attention decode step; head_dim 8..256, a power of two)

@@ -1047,9 +1047,13 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
       tc ? a.hg16 : nullptr, a.x_dtype);
   if ((e = cudaGetLastError())) return e;
   const int nt = (cs + 63) / 64;
-  bwd_cb_kernel<<<dim3((unsigned)(nt * (nt + 1) / 2), (unsigned)G, (unsigned)nk), 256, kSmemCB, c.stream>>>(
-      a.B, a.C, a.CB, c.cm, G, N, a.x_dtype);
-  if ((e = cudaGetLastError())) return e;
+  if (tc) {
+    if ((e = launch_bwd_cb_tc(c, a))) return e;
+  } else {
+    bwd_cb_kernel<<<dim3((unsigned)(nt * (nt + 1) / 2), (unsigned)G, (unsigned)nk), 256, kSmemCB, c.stream>>>(
+        a.B, a.C, a.CB, c.cm, G, N, a.x_dtype);
+    if ((e = cudaGetLastError())) return e;
+  }
   if (a.ev[2]) cudaEventRecord(a.ev[2], c.stream);
   if (tc) {
     if ((e = launch_bwd_state_grad_grp_tc(c, a))) return e;
@@ -1073,9 +1077,13 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
   }
   if ((e = cudaGetLastError())) return e;
   if (a.ev[4]) cudaEventRecord(a.ev[4], c.stream);
-  bwd_bmm_kernel<<<dim3((unsigned)(2 * nt), (unsigned)G, (unsigned)nk), 256, 0, c.stream>>>(
-      a.B, a.C, a.CBg, a.B_grad, a.C_grad, c.cm, G, N, a.x_dtype);
-  if ((e = cudaGetLastError())) return e;
+  if (tc) {
+    if ((e = launch_bwd_bmm_tc(c, a))) return e;
+  } else {
+    bwd_bmm_kernel<<<dim3((unsigned)(2 * nt), (unsigned)G, (unsigned)nk), 256, 0, c.stream>>>(
+        a.B, a.C, a.CBg, a.B_grad, a.C_grad, c.cm, G, N, a.x_dtype);
+    if ((e = cudaGetLastError())) return e;
+  }
   bwd_param_reduce_kernel<<<(unsigned)H, 256, 0, c.stream>>>(a.A_part, a.bias_part, a.A_grad, a.delta_bias_grad,
                                                              nk, H);
   return cudaGetLastError();

@@ -751,6 +751,254 @@ cudaError_t launch_grp_typed(const LaunchCtx& c, const BwdArgs& a, const void* y
       mb, mc, mu, my, mh, mp, a.dt, a.cum, a.accS, a.B_grad, a.C_grad, a.gC, c.cm, c.H, c.G);
   return cudaGetLastError();
 }
+
+// ---------------------------------------------------------------------------
+// CB = C B^T and the bmm backward on tcgen05 (ssd_bwd.cu bwd_cb_kernel / bwd_bmm_kernel;
+// forward_kernel.py:270-328, backward_kernel.py:686-780), per (chunk, group, 128-row block m):
+//   cb:  CB[l,s] = sum_n C[l,n] B[s,n] for l in block m, s in blocks 0..m      (K = n)
+//   bmm product 0: C_grad[l,:] += sum_{s <= l} CB_grad[l,s] B[s,:]           (K = s)
+//   bmm product 1: B_grad[s,:] += sum_{l >= s} CB_grad[l,s] C[l,:]           (K = l)
+// B / C rows arrive by TMA (rows at or past the length zeroed in shared memory); CB_grad
+// (fp32, the group's heads summed) is rounded to 16 bits into the A operand, K-major for
+// product 0 and MN-major (rows read as columns) for product 1. The bmm rows are added to the
+// gradients read-modify-write (each row belongs to one CTA).
+// ---------------------------------------------------------------------------
+constexpr int kBmThreads = 256;
+constexpr size_t kBmSmem = 1024 + 65536;
+constexpr size_t kCbSmem = 1024 + 3 * 32768;
+
+// Zeros rows [from, 128) of a [2 n-blocks][128 rows][128 B] tile.
+__device__ __forceinline__ void zero_rows_tile(uint8_t* t, int from) {
+  from = max(from, 0);
+  for (int q = threadIdx.x; q < (128 - from) * 8; q += blockDim.x) {
+    const uint32_t off = (uint32_t)(from + (q >> 3)) * 128u + (uint32_t)(q & 7) * 16u;
+    *reinterpret_cast<uint4*>(t + off) = make_uint4(0u, 0u, 0u, 0u);
+    *reinterpret_cast<uint4*>(t + 16384 + off) = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kBmThreads) bwd_cb_tc_kernel(const __grid_constant__ CUtensorMap tm_b,
+                                                               const __grid_constant__ CUtensorMap tm_c,
+                                                               float* __restrict__ CB, ChunkMap cm, int G) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024_shared(smem_raw);
+  uint8_t* sC = sm;  // C rows of block m; then B rows of blocks 0 and 1
+  auto sBr = [&](int j) { return sm + 32768 * (1 + j); };
+  __shared__ uint64_t bars[2];
+  __shared__ uint32_t tslot[1];
+  const uint32_t bar_tma = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
+  const int m = blockIdx.x, g = blockIdx.y, k = blockIdx.z;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int vl = ci.vlim, r0 = 128 * m;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = (warp & 3) * 32 + lane, hc = warp >> 2;
+  const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;
+  if (tid == 0) {
+    prefetch_tmap(&tm_b);
+    prefetch_tmap(&tm_c);
+    mbar_init(bar_tma, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  if (tid == 0) {
+    mbar_expect_tx(bar_tma, 32768u * (uint32_t)(m + 2));
+    const int t0 = (int)ci.tok0;
+    tma_load_3d(smem_u32(sC), &tm_c, 0, g, t0 + r0, bar_tma);
+    tma_load_3d(smem_u32(sC) + 16384, &tm_c, 64, g, t0 + r0, bar_tma);
+    for (int j = 0; j <= m; ++j) {
+      tma_load_3d(smem_u32(sBr(j)), &tm_b, 0, g, t0 + 128 * j, bar_tma);
+      tma_load_3d(smem_u32(sBr(j)) + 16384, &tm_b, 64, g, t0 + 128 * j, bar_tma);
+    }
+  }
+  bool ok = mbar_wait(bar_tma, 0, kSiteBwdTcTma);
+  if (ok) {
+    zero_rows_tile(sC, vl - r0);
+    for (int j = 0; j <= m; ++j) zero_rows_tile(sBr(j), vl - 128 * j);
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  ok = __syncthreads_and(ok) != 0;
+  if (ok && tid == 0) {
+    tc_fence_after();
+    constexpr uint32_t ID = idesc_f16(128, 128, BF16, false, false);
+    for (int j = 0; j <= m; ++j)
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t off = (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u;
+        umma_f16(tmem + 128 * j, sdesc_sw128(smem_u32(sC) + off, 16, 1024), sdesc_sw128(smem_u32(sBr(j)) + off, 16, 1024),
+                 ID, ks > 0 ? 1u : 0u);
+      }
+    umma_commit(bar_mma);
+  }
+  if (ok) ok = __syncthreads_and(mbar_wait(bar_mma, 0, kSiteBwdTcMma)) != 0;
+  if (ok) {
+    tc_fence_after();
+    // row l = r0 + r: this thread's half of the 128 (m + 1) columns, fp32
+    const int ncol = 64 * (m + 1);
+    float* dst = CB + ((long long)k * G + g) * 65536 + (long long)(r0 + r) * 256 + ncol * hc;
+#pragma unroll 1
+    for (int c = 0; c < ncol; c += 32) {
+      uint32_t v[32];
+      tmem_ld32(tmem + tl + (uint32_t)(ncol * hc + c), v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int e = 0; e < 32; e += 4)
+        *reinterpret_cast<float4*>(dst + c + e) = make_float4(__uint_as_float(v[e]), __uint_as_float(v[e + 1]),
+                                                              __uint_as_float(v[e + 2]), __uint_as_float(v[e + 3]));
+    }
+  } else if (tid == 0) {
+    mbar_wait(bar_mma, 0, kSiteBwdTcMma);  // an MMA that was issued lands before TMEM goes (bounded)
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kBmThreads) bwd_bmm_tc_kernel(const __grid_constant__ CUtensorMap tm_b,
+                                                                const __grid_constant__ CUtensorMap tm_c,
+                                                                const float* __restrict__ CBg, float* __restrict__ Bgrad,
+                                                                float* __restrict__ Cgrad, ChunkMap cm, int G) {
+  using T16 = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024_shared(smem_raw);
+  uint8_t* sA = sm;          // 16-bit CB_grad block [2 64-blocks][128 rows][128 B]
+  uint8_t* sX = sm + 32768;  // B or C rows [2 n-blocks][128 rows][128 B]
+  __shared__ uint64_t bars[2];
+  __shared__ uint32_t tslot[1];
+  const uint32_t bar_tma = smem_u32(&bars[0]), bar_mma = smem_u32(&bars[1]);
+  const int prod = blockIdx.x >> 1, m = blockIdx.x & 1, g = blockIdx.y, k = blockIdx.z;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int vl = ci.vlim, r0 = 128 * m;
+  if (r0 >= vl) return;  // rows at or past the length receive nothing
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = (warp & 3) * 32 + lane, hc = warp >> 2;
+  const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;
+  const CUtensorMap* mx = prod == 0 ? &tm_b : &tm_c;
+  const float* cbg = CBg + ((long long)k * G + g) * 65536;
+  if (tid == 0) {
+    prefetch_tmap(mx);
+    mbar_init(bar_tma, 1);
+    mbar_init(bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t ID = prod == 0 ? idesc_f16(128, 128, BF16, false, true) : idesc_f16(128, 128, BF16, true, true);
+  // source blocks: product 0 s-blocks 0..m, product 1 l-blocks m..1 (below the length)
+  const int jb = prod == 0 ? 0 : m, je = prod == 0 ? m : 1;
+  bool ok = true;
+  int uses = 0;
+  for (int j = jb; j <= je && ok; ++j) {
+    if (128 * j >= vl) break;
+    if (tid == 0) {
+      mbar_expect_tx(bar_tma, 32768u);
+      tma_load_3d(smem_u32(sX), mx, 0, g, (int)ci.tok0 + 128 * j, bar_tma);
+      tma_load_3d(smem_u32(sX) + 16384, mx, 64, g, (int)ci.tok0 + 128 * j, bar_tma);
+    }
+    // A: product 0 rows l = r0 + i, columns s = 128 j + c (K-major); product 1 CB_grad rows
+    // l = 128 j + i read as the K index, columns s = r0 + c as M (MN-major): one layout,
+    // [c / 64][i][c % 64], swizzled
+#pragma unroll 2
+    for (int i0 = 0; i0 < 8; i0 += 4) {
+      float4 va[4], vb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int q = tid + kBmThreads * (i0 + i), row = q >> 4, c8 = q & 15;
+        const float* src = prod == 0 ? cbg + (long long)(r0 + row) * 256 + 128 * j + 8 * c8
+                                     : cbg + (long long)(128 * j + row) * 256 + r0 + 8 * c8;
+        va[i] = __ldg(reinterpret_cast<const float4*>(src));
+        vb[i] = __ldg(reinterpret_cast<const float4*>(src + 4));
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int q = tid + kBmThreads * (i0 + i), row = q >> 4, c8 = q & 15;
+        *reinterpret_cast<uint4*>(sA + (c8 >> 3) * 16384 + sw128_off((uint32_t)row, (uint32_t)(c8 & 7))) =
+            make_uint4(pack2<T16>(va[i].x, va[i].y), pack2<T16>(va[i].z, va[i].w), pack2<T16>(vb[i].x, vb[i].y),
+                       pack2<T16>(vb[i].z, vb[i].w));
+      }
+    }
+    bool got = mbar_wait(bar_tma, uses & 1, kSiteBwdTcTma);
+    if (got) zero_rows_tile(sX, vl - 128 * j);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    ok = __syncthreads_and(got) != 0;
+    if (!ok) break;
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t ad = prod == 0
+                                ? sdesc_sw128(smem_u32(sA) + (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u, 16, 1024)
+                                : sdesc_sw128(smem_u32(sA) + (uint32_t)ks * 2048u, 16384, 1024);
+        umma_f16(tmem, ad, sdesc_sw128(smem_u32(sX) + (uint32_t)ks * 2048u, 16384, 1024), ID,
+                 (j > jb || ks > 0) ? 1u : 0u);
+      }
+      umma_commit(bar_mma);
+    }
+    ok = __syncthreads_and(mbar_wait(bar_mma, uses & 1, kSiteBwdTcMma)) != 0;  // sA, sX reused
+    ++uses;
+    tc_fence_after();
+  }
+  if (ok && uses > 0) {
+    const int row = r0 + r;
+    float* out = (prod == 0 ? Cgrad : Bgrad) + ((ci.tok0 + row) * G + g) * 128 + 64 * hc;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      uint32_t v[32];
+      tmem_ld32(tmem + tl + (uint32_t)(64 * hc + 32 * c), v);
+      tmem_wait_ld();
+      if (row < ci.lim) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 4) {
+          float4 o = *reinterpret_cast<float4*>(out + 32 * c + e);
+          o.x += __uint_as_float(v[e]);
+          o.y += __uint_as_float(v[e + 1]);
+          o.z += __uint_as_float(v[e + 2]);
+          o.w += __uint_as_float(v[e + 3]);
+          *reinterpret_cast<float4*>(out + 32 * c + e) = o;
+        }
+      }
+    }
+  } else if (!ok && tid == 0 && uses > 0) {
+    mbar_wait(bar_mma, (uses - 1) & 1, kSiteBwdTcMma);  // bounded
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+template <bool BF16>
+cudaError_t launch_cb_bmm_typed(const LaunchCtx& c, const BwdArgs& a, bool bmm) {
+  CUtensorMap mb, mc;
+  if (!make_map_3d(&mb, a.B, BF16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128) ||
+      !make_map_3d(&mc, a.C, BF16, 128, (uint64_t)c.G, (uint64_t)c.T, 64, 1, 128))
+    return cudaErrorInvalidValue;
+  cudaError_t e;
+  if (bmm) {
+    if ((e = cudaFuncSetAttribute(bwd_bmm_tc_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBmSmem)))
+      return e;
+    bwd_bmm_tc_kernel<BF16><<<dim3(4u, (unsigned)c.G, (unsigned)c.nchunks_max), kBmThreads, kBmSmem, c.stream>>>(
+        mb, mc, a.CBg, a.B_grad, a.C_grad, c.cm, c.G);
+  } else {
+    if ((e = cudaFuncSetAttribute(bwd_cb_tc_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCbSmem)))
+      return e;
+    bwd_cb_tc_kernel<BF16><<<dim3(2u, (unsigned)c.G, (unsigned)c.nchunks_max), kBmThreads, kCbSmem, c.stream>>>(
+        mb, mc, a.CB, c.cm, c.G);
+  }
+  return cudaGetLastError();
+}
 }  // namespace
 
 bool bwd_state_grad_tc_supported(int x_dtype, int y_dtype, int P, int N, int cs) {
@@ -773,6 +1021,16 @@ cudaError_t launch_bwd_state_grad_grp_tc(const LaunchCtx& c, const BwdArgs& a) {
   if (c.nchunks_max > 65535 || c.G > 65535) return cudaErrorInvalidValue;
   const void* y16 = a.y_dtype == SSD_F32 ? (const void*)a.y16 : a.y_grad;  // y16: written by the recompute
   return a.x_dtype == SSD_BF16 ? launch_grp_typed<true>(c, a, y16) : launch_grp_typed<false>(c, a, y16);
+}
+
+cudaError_t launch_bwd_cb_tc(const LaunchCtx& c, const BwdArgs& a) {
+  if (c.nchunks_max > 65535 || c.G > 65535) return cudaErrorInvalidValue;
+  return a.x_dtype == SSD_BF16 ? launch_cb_bmm_typed<true>(c, a, false) : launch_cb_bmm_typed<false>(c, a, false);
+}
+
+cudaError_t launch_bwd_bmm_tc(const LaunchCtx& c, const BwdArgs& a) {
+  if (c.nchunks_max > 65535 || c.G > 65535) return cudaErrorInvalidValue;
+  return a.x_dtype == SSD_BF16 ? launch_cb_bmm_typed<true>(c, a, true) : launch_cb_bmm_typed<false>(c, a, true);
 }
 
 cudaError_t launch_bwd_intra_tc(const LaunchCtx& c, const BwdArgs& a) {
