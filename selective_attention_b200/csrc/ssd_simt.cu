@@ -359,6 +359,219 @@ __global__ void __launch_bounds__(256) simt_chunk_scan_kernel(
   }
 }
 
+
+// ===========================================================================
+// Tiled CUDA-core versions (P <= 64 and N <= 256, both multiples of 4): 64 x 64 output
+// tiles per CTA, operand tiles staged in shared memory as fp32, 4 x 4 outputs per thread
+// (rows tr + 16 i, columns 4 tc + j) from 16-byte shared-memory loads.
+// ===========================================================================
+constexpr int kTT = 64;       // output tile
+constexpr int kTK = 32;       // reduction slice
+constexpr int kTLD = kTK + 4; // [row][k] tiles
+constexpr int kTLP = kTT + 4; // [k][col] tiles
+
+__device__ __forceinline__ float c4(const float4& v, int e) { return e == 0 ? v.x : (e == 1 ? v.y : (e == 2 ? v.z : v.w)); }
+
+// acc[i][j] += sum_k A[ar + 16 i][k] * Bt[k][4 bc + j]; A is [row][k] (kTLD), Bt is [k][col] (kTLP).
+__device__ __forceinline__ void mma_rk_kc(float (&acc)[4][4], const float* A, const float* Bt, int ar, int bc,
+                                          int kn) {
+  for (int k = 0; k < kn; k += 4) {
+    float4 a[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = *reinterpret_cast<const float4*>(A + (ar + 16 * i) * kTLD + k);
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const float4 b = *reinterpret_cast<const float4*>(Bt + (k + kk) * kTLP + 4 * bc);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float x = c4(a[i], kk);
+        acc[i][0] = fmaf(x, b.x, acc[i][0]);
+        acc[i][1] = fmaf(x, b.y, acc[i][1]);
+        acc[i][2] = fmaf(x, b.z, acc[i][2]);
+        acc[i][3] = fmaf(x, b.w, acc[i][3]);
+      }
+    }
+  }
+}
+
+// chunk_scan (forward_kernel.py:350-455 + the D / z epilogue of modules/ssm.py:145-150):
+// CTA = (64-row tile of the chunk, head, chunk), all P columns.
+//   y = exp(cum_l) C_l . prev + sum_{s <= l, s < lim} CB[l,s] exp(min(cum_l - cum_s, 0)) dt_s u_s
+template <typename T, typename YT>
+__global__ void __launch_bounds__(256) simt_chunk_scan_tiled_kernel(
+    const T* __restrict__ u, const float* __restrict__ dt, const float* __restrict__ cum,
+    const T* __restrict__ Cm, const float* __restrict__ prev, const float* __restrict__ CB,
+    const float* __restrict__ D, const T* __restrict__ z, YT* __restrict__ y, ChunkMap cm, int H, int G,
+    int P, int N) {
+  __shared__ __align__(16) float As[kTT * kTLD];  // C rows [l][n] | M [l][s]
+  __shared__ __align__(16) float Bs[kTK * kTLP];  // prev^T [n][p] | u [s][p]
+  __shared__ float cml[kTT];
+  const int k = blockIdx.z, h = blockIdx.y, l0 = blockIdx.x * kTT;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  if (l0 >= ci.lim) return;
+  const int cs = cm.cs, g = h / (H / G), lim = ci.lim;
+  const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  const float* dtk = dt + ((long long)k * H + h) * cs;
+  const float* cmk = cum + ((long long)k * H + h) * cs;
+  const float* hp = prev + ((long long)k * H + h) * (long long)P * N;
+  const float* cbk = CB + ((long long)k * G + g) * cs * cs;
+  if (tid < kTT) cml[tid] = l0 + tid < cs ? cmk[l0 + tid] : 0.f;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  // C . prev^T over slices of 32 states
+  for (int n0 = 0; n0 < N; n0 += kTK) {
+    __syncthreads();
+    for (int idx = tid; idx < kTT * kTK; idx += 256) {
+      const int r = idx >> 5, c = idx & 31, l = l0 + r, n = n0 + c;
+      As[r * kTLD + c] = (l < lim && n < N) ? Ld<T>::f(Cm + ((ci.tok0 + l) * G + g) * (long long)N + n) : 0.f;
+    }
+    for (int idx = tid; idx < kTK * kTT; idx += 256) {
+      const int p = idx >> 5, c = idx & 31, n = n0 + c;  // prev^T: Bs[n][p], prev rows read along n
+      Bs[c * kTLP + p] = (p < P && n < N) ? hp[(long long)p * N + n] : 0.f;
+    }
+    __syncthreads();
+    mma_rk_kc(acc, As, Bs, tr, tc, kTK);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float e = expf(cml[tr + 16 * i]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] *= e;
+  }
+  // intra-chunk term over source slices of 32 tokens up to the tile's last row
+  const int send = min(l0 + kTT, lim);
+  for (int s0 = 0; s0 < send; s0 += kTK) {
+    __syncthreads();
+    for (int idx = tid; idx < kTT * kTK; idx += 256) {
+      const int r = idx >> 5, c = idx & 31, l = l0 + r, sidx = s0 + c;
+      float m = 0.f;
+      if (l < lim && sidx <= l) m = cbk[(long long)l * cs + sidx] * expf(fminf(cml[r] - cmk[sidx], 0.f)) * dtk[sidx];
+      As[r * kTLD + c] = m;
+    }
+    for (int idx = tid; idx < kTK * kTT; idx += 256) {
+      const int r = idx >> 6, p = idx & 63, sidx = s0 + r;
+      Bs[r * kTLP + p] = (sidx < lim && p < P) ? Ld<T>::f(u + ((ci.tok0 + sidx) * H + h) * (long long)P + p) : 0.f;
+    }
+    __syncthreads();
+    mma_rk_kc(acc, As, Bs, tr, tc, kTK);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int l = l0 + tr + 16 * i;
+    if (l >= lim) continue;
+    const long long tok = ci.tok0 + l;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int p = 4 * tc + j;
+      if (p >= P) continue;
+      const long long yo = (tok * H + h) * (long long)P + p;
+      float v = acc[i][j];
+      if (D) v = fmaf(D[h * P + p], Ld<T>::f(u + yo), v);
+      if (z) v *= silu(Ld<T>::f(z + yo));
+      y[yo] = from_f32<YT>(v);
+    }
+  }
+}
+
+// bmm_chunk (forward_kernel.py:270-328): CTA = (64 x 64 tile of CB, group, chunk);
+// CB[l,s] = sum_n C[l,n] B[s,n] for l, s < lim, zero outside.
+template <typename T>
+__global__ void __launch_bounds__(256) simt_bmm_chunk_tiled_kernel(const T* __restrict__ Bm, const T* __restrict__ Cm,
+                                                                   float* __restrict__ CB, ChunkMap cm, int G, int N) {
+  __shared__ __align__(16) float As[kTT * kTLD];  // C rows [l][n]
+  __shared__ __align__(16) float Bs[kTK * kTLP];  // B^T [n][s]
+  const int k = blockIdx.z, g = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int cs = cm.cs, nt = (cs + kTT - 1) / kTT;
+  const int l0 = (blockIdx.x / nt) * kTT, s0 = (blockIdx.x % nt) * kTT, lim = ci.lim;
+  const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  if (l0 < lim && s0 < lim) {
+    for (int n0 = 0; n0 < N; n0 += kTK) {
+      __syncthreads();
+      for (int idx = tid; idx < kTT * kTK; idx += 256) {
+        const int r = idx >> 5, c = idx & 31, n = n0 + c;
+        As[r * kTLD + c] = (l0 + r < lim && n < N) ? Ld<T>::f(Cm + ((ci.tok0 + l0 + r) * G + g) * (long long)N + n) : 0.f;
+        Bs[c * kTLP + r] = (s0 + r < lim && n < N) ? Ld<T>::f(Bm + ((ci.tok0 + s0 + r) * G + g) * (long long)N + n) : 0.f;
+      }
+      __syncthreads();
+      mma_rk_kc(acc, As, Bs, tr, tc, kTK);
+    }
+  }
+  float* out = CB + ((long long)k * G + g) * cs * cs;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int l = l0 + tr + 16 * i;
+    if (l >= cs) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int sidx = s0 + 4 * tc + j;
+      if (sidx < cs) out[(long long)l * cs + sidx] = (l < lim && sidx < lim) ? acc[i][j] : 0.f;
+    }
+  }
+}
+
+// chunk_state (forward_kernel.py:107-185): CTA = (64-state-column tile, head, chunk);
+// states[p,n] = sum_l u[l,p] exp(min(cum_last - cum_l, 0)) dt_l B[l,n] over l < lim.
+template <typename T>
+__global__ void __launch_bounds__(256) simt_chunk_state_tiled_kernel(
+    const T* __restrict__ u, const T* __restrict__ Bm, const float* __restrict__ dt,
+    const float* __restrict__ cum, float* __restrict__ states, ChunkMap cm, int H, int G, int P, int N) {
+  __shared__ __align__(16) float As[kTT * kTLD];  // (u w)^T [p][l]
+  __shared__ __align__(16) float Bs[kTK * kTLP];  // B [l][n]
+  const int k = blockIdx.z, h = blockIdx.y, n0 = blockIdx.x * kTT;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int cs = cm.cs, g = h / (H / G), lim = ci.lim;
+  const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  const float* dtk = dt + ((long long)k * H + h) * cs;
+  const float* cmk = cum + ((long long)k * H + h) * cs;
+  const float clast = cmk[cs - 1];
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int t0 = 0; t0 < lim; t0 += kTK) {
+    __syncthreads();
+    for (int idx = tid; idx < kTK * kTT; idx += 256) {
+      const int r = idx >> 6, c = idx & 63, l = t0 + r;  // token r, column c
+      float xv = 0.f, bv = 0.f;
+      if (l < lim) {
+        if (c < P)
+          xv = Ld<T>::f(u + ((ci.tok0 + l) * H + h) * (long long)P + c) * (expf(fminf(clast - cmk[l], 0.f)) * dtk[l]);
+        if (n0 + c < N) bv = Ld<T>::f(Bm + ((ci.tok0 + l) * G + g) * (long long)N + n0 + c);
+      }
+      As[c * kTLD + r] = xv;
+      Bs[r * kTLP + c] = bv;
+    }
+    __syncthreads();
+    mma_rk_kc(acc, As, Bs, tr, tc, kTK);
+  }
+  float* out = states + ((long long)k * H + h) * (long long)P * N;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int p = tr + 16 * i;
+    if (p >= P) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + 4 * tc + j;
+      if (n < N) out[(long long)p * N + n] = acc[i][j];
+    }
+  }
+}
+
+inline bool simt_tiled_ok(int P, int N) { return P <= 64 && N <= 256; }
+
 // ===========================================================================
 // Host launchers
 // ===========================================================================
@@ -415,6 +628,12 @@ template <typename T>
 static cudaError_t simt_state_t(const LaunchCtx& c, const void* u, const void* B, const float* dt,
                                 const float* cum, float* states) {
   const int PN = c.P * c.N;
+  if (simt_tiled_ok(c.P, c.N)) {
+    simt_chunk_state_tiled_kernel<T><<<dim3((unsigned)((c.N + kTT - 1) / kTT), (unsigned)c.H, (unsigned)c.nchunks_max),
+                                       256, 0, c.stream>>>((const T*)u, (const T*)B, dt, cum, states, c.cm, c.H, c.G,
+                                                           c.P, c.N);
+    return cudaGetLastError();
+  }
   dim3 grid((unsigned)((PN + 4095) / 4096), (unsigned)c.H, (unsigned)c.nchunks_max);
   size_t sm = (size_t)32 * (c.P + c.N) * sizeof(float);
   if (sm > 48 * 1024) {
@@ -439,6 +658,12 @@ cudaError_t launch_simt_chunk_state(const LaunchCtx& c, int x_dtype, const void*
 
 template <typename T>
 static cudaError_t simt_bmm_t(const LaunchCtx& c, const void* B, const void* C, float* CB) {
+  if (simt_tiled_ok(c.P, c.N)) {
+    const int nt = (c.cs + kTT - 1) / kTT;
+    simt_bmm_chunk_tiled_kernel<T><<<dim3((unsigned)(nt * nt), (unsigned)c.G, (unsigned)c.nchunks_max), 256, 0,
+                                     c.stream>>>((const T*)B, (const T*)C, CB, c.cm, c.G, c.N);
+    return cudaGetLastError();
+  }
   dim3 grid((unsigned)((c.cs * c.cs + 4095) / 4096), (unsigned)c.G, (unsigned)c.nchunks_max);
   simt_bmm_chunk_kernel<T><<<grid, 256, 0, c.stream>>>((const T*)B, (const T*)C, CB, c.cm, c.G, c.N);
   return cudaGetLastError();
@@ -456,6 +681,13 @@ cudaError_t launch_simt_bmm_chunk(const LaunchCtx& c, int x_dtype, const void* B
 template <typename T, typename YT>
 static cudaError_t simt_scan_t(const LaunchCtx& c, const void* u, const float* dt, const float* cum, const void* C,
                                const float* prev, const float* CB, const float* D, const void* z, void* y) {
+  if (simt_tiled_ok(c.P, c.N)) {
+    simt_chunk_scan_tiled_kernel<T, YT><<<dim3((unsigned)((c.cs + kTT - 1) / kTT), (unsigned)c.H,
+                                               (unsigned)c.nchunks_max),
+                                          256, 0, c.stream>>>((const T*)u, dt, cum, (const T*)C, prev, CB, D,
+                                                              (const T*)z, (YT*)y, c.cm, c.H, c.G, c.P, c.N);
+    return cudaGetLastError();
+  }
   dim3 grid((unsigned)((c.cs * c.P + 4095) / 4096), (unsigned)c.H, (unsigned)c.nchunks_max);
   simt_chunk_scan_kernel<T, YT><<<grid, 256, 0, c.stream>>>((const T*)u, dt, cum, (const T*)C, prev, CB, D,
                                                             (const T*)z, (YT*)y, c.cm, c.H, c.G, c.P, c.N);
