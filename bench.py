@@ -380,7 +380,9 @@ def measure_ssd(run, args, world, flush, hbm_peak, peak_src, global_tokens, step
         stages[n_] = {"us": ms_ * 1e3, "alg_bytes": by, "gbs": gbs, "frac": (gbs / hbm_peak) if gbs else None}
     dom = max(stages, key=lambda k: stages[k]["us"])
     roof = {"kernel": dom, "bound": "hbm", "achieved": stages[dom]["gbs"], "peak": hbm_peak, "unit": "GB/s",
-            "frac": stages[dom]["frac"], "traffic": _traffic_from_profiles(dom, cfg.name, T, H),
+            "frac": stages[dom]["frac"],
+            # the committed captures are of the tensor-core chain; the CUDA-core chain has none
+            "traffic": _traffic_from_profiles(dom, cfg.name, T, H) if tc else None,
             "peak_source": peak_src, "alg_bytes_per_launch": stages[dom]["alg_bytes"],
             "us_per_launch": stages[dom]["us"]}
     from selective_attention_b200 import workloads
