@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--no-sattn", action="store_true", help="skip the selective-attention decode measurement")
     ap.add_argument("--no-c4", action="store_true", help="skip the config-c4 (head-group split) measurement")
     ap.add_argument("--no-extra", action="store_true", help="skip the one-GPU c2 and fp32 measurements")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="skip timing the reference's own Triton SSD on the GPU (secondary comparison)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     return ap.parse_args()
 
@@ -565,6 +567,8 @@ def run_ours(args, rank, world, local):
             line["sattn_decode"] = sattn_measure(args, dev, flush, hbm_peak)
             line["sattn_prefill"] = sattn_prefill_measure(args, dev, flush, peaks.get("bf16_tflops", 1590.0))
             line["sattn_train"] = sattn_train_measure(args, dev, flush, peaks.get("bf16_tflops", 1590.0))
+        if not args.no_ref_gpu:
+            line["reference_gpu"] = ref_gpu_measure(args, dev, flush)
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_baseline(cfg, args.cpu_seconds)
     if rank == 0:
@@ -861,6 +865,74 @@ def sattn_train_measure(args, dev, flush, tc_peak):
         tf = flops / (ms * 1e-3) / 1e12
         res[impl] = {"ms_per_step": ms, "fwd_ms": ms_f, "bwd_ms": ms - ms_f, "tflops": tf, "peak_tflops": peak,
                      "peak": peak_name, "frac": tf / peak, "steps": steps}
+    return res
+
+
+def ref_gpu_measure(args, dev, flush):
+    """Secondary comparison on this GPU: the reference's own Triton SSD (``SSDScanFn`` of the
+    package ``baseline/install_reference.sh`` installs into ``baseline/_ref``; ``ops/ssd_scan.py``
+    over ``triton_kernels/ssd_scan``) at config 1's shape in fp32, its operand type, forward
+    and forward + backward, beside this library's ``SSDScanFn`` on the same fp32 inputs (the
+    CUDA-core chain) and on bf16 inputs (tensor cores). No D / z (the reference op has none).
+    The reference runs its stock code path; Triton compiles and autotunes it on first use,
+    outside the timed steps."""
+    import selective_attention_b200 as sab
+    from selective_attention_b200 import workloads
+
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "selective_attention")):
+        return {"unavailable": "reference package not installed in baseline/_ref"}
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    try:
+        from selective_attention.ops import SSDScanFn as RefSSD
+    except Exception as e:  # noqa: BLE001 - recorded, not raised: the entry is optional
+        return {"unavailable": f"reference import failed: {e!r}"[:300]}
+    cfg = workloads.SSDConfig(**{**workloads.CONFIGS["c1"].__dict__, "dtype": "f32", "D": False, "z": False})
+    inp = workloads.make_ssd_inputs(cfg, seed=7, device=dev, gen_device="cuda")
+    b, L = cfg.batch, cfg.seqlen
+    length = torch.full((b,), L, dtype=torch.long, device=dev)
+    g = torch.Generator(device=dev).manual_seed(8)
+    res = {"config": "c1 shape (8x2048 H24 P64 N128 G1 cs256), no D / z; fp32 unless noted",
+           "timing": "median of per-step CUDA events, L2 flushed between steps"}
+    steps = max(3, min(args.steps, 10))
+    stream = torch.cuda.current_stream(dev)
+
+    def run(name, op, dtype):
+        leaves = [inp[k].to(dtype) if k in ("u", "B", "C") else inp[k] for k in ("u", "A", "B", "C", "delta_raw")]
+        bias = inp.get("delta_bias")
+        yg = torch.randn(inp["u"].shape, device=dev, generator=g)
+
+        def fwd():
+            with torch.no_grad():
+                return op.apply(*leaves, bias, None, length, cfg.chunk)
+
+        def fwd_bwd():
+            xs = [t.detach().requires_grad_(True) for t in leaves]
+            y, h = op.apply(*xs, bias, None, length, cfg.chunk)
+            torch.autograd.backward([y], [yg.to(y.dtype)])
+
+        try:
+            for f in (fwd, fwd_bwd):
+                f()
+            torch.cuda.synchronize()
+            tf = statistics.median(time_steps(fwd, steps, flush, stream))
+            tb = statistics.median(time_steps(fwd_bwd, steps, flush, stream))
+            res[name] = {"fwd_ms": tf, "fwd_bwd_ms": tb, "tokens_per_s_fwd": b * L / (tf * 1e-3)}
+        except Exception as e:  # noqa: BLE001 - recorded, the other lines still run
+            res[name] = {"error": f"{e!r}"[:300]}
+
+    run("reference_triton_fp32", RefSSD, torch.float32)
+    run("ours_fp32", sab.SSDScanFn, torch.float32)
+    run("ours_bf16", sab.SSDScanFn, torch.bfloat16)
+    r, o = res.get("reference_triton_fp32", {}), res.get("ours_bf16", {})
+    if "fwd_ms" in r and "fwd_ms" in o:
+        res["speedup_bf16_vs_reference_fwd"] = r["fwd_ms"] / o["fwd_ms"]
+        res["speedup_bf16_vs_reference_fwd_bwd"] = r["fwd_bwd_ms"] / o["fwd_bwd_ms"]
+    if "fwd_ms" in r and "fwd_ms" in res.get("ours_fp32", {}):
+        res["speedup_fp32_vs_reference_fwd"] = r["fwd_ms"] / res["ours_fp32"]["fwd_ms"]
+    del inp
+    torch.cuda.empty_cache()
     return res
 
 
