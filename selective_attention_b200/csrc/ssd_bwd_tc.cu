@@ -105,25 +105,30 @@ __global__ void __launch_bounds__(kCsThreads) bwd_chunk_states_tc_kernel(
       if (x_tma) tma_load_3d(smem_u32(sX), from_y ? &tm_y : &tm_u, 0, h, t0, bar_tma);
     }
     if (from_y && !kY16) {
-      // fp32 y_grad rows times e_l, rounded to 16 bits into the swizzled tile
+      // fp32 y_grad rows times e_l, rounded to 16 bits into the swizzled tile. Every row below
+      // the length is read (the 16-bit copy needs it even where e_l = 0); the 16 loads are
+      // issued before any is used, rows at or past the length reading the last valid row.
+      float4 ya[8], yb[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int q = tid + kCsThreads * i, row = q >> 3, c8 = q & 7, l = 128 * ph + row;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        const int lr = l < vl ? l : vl - 1;  // vl > 128 ph here
+        const float* src = reinterpret_cast<const float*>(yg) + ((ci.tok0 + lr) * H + h) * 64 + c8 * 8;
+        ya[i] = __ldg(reinterpret_cast<const float4*>(src));
+        yb[i] = __ldg(reinterpret_cast<const float4*>(src + 4));
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = tid + kCsThreads * i, row = q >> 3, c8 = q & 7, l = 128 * ph + row;
         const float w = sW[l];
-        // every row below the length is read: the 16-bit copy needs it even where e_l = 0
-        if (l < vl && (w != 0.f || y16out)) {
-          const long long off = ((ci.tok0 + l) * H + h) * 64 + c8 * 8;
-          const float* src = reinterpret_cast<const float*>(yg) + off;
-          const float4 a = __ldg(reinterpret_cast<const float4*>(src));
-          const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
-          if (w != 0.f)
-            v = make_uint4(pack2<T16>(a.x * w, a.y * w), pack2<T16>(a.z * w, a.w * w), pack2<T16>(b.x * w, b.y * w),
-                           pack2<T16>(b.z * w, b.w * w));
-          if (y16out)  // the rows rounded, unscaled, for the later kernels' TMA loads
-            *reinterpret_cast<uint4*>(y16out + off) = make_uint4(pack2<T16>(a.x, a.y), pack2<T16>(a.z, a.w),
-                                                                 pack2<T16>(b.x, b.y), pack2<T16>(b.z, b.w));
-        }
+        const float4 a = ya[i], b = yb[i];
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (w != 0.f)
+          v = make_uint4(pack2<T16>(a.x * w, a.y * w), pack2<T16>(a.z * w, a.w * w), pack2<T16>(b.x * w, b.y * w),
+                         pack2<T16>(b.z * w, b.w * w));
+        if (y16out && l < vl)  // the rows rounded, unscaled, for the later kernels' TMA loads
+          *reinterpret_cast<uint4*>(y16out + ((ci.tok0 + l) * H + h) * 64 + c8 * 8) =
+              make_uint4(pack2<T16>(a.x, a.y), pack2<T16>(a.z, a.w), pack2<T16>(b.x, b.y), pack2<T16>(b.z, b.w));
         *reinterpret_cast<uint4*>(sX + sw128_off((uint32_t)row, (uint32_t)c8)) = v;
       }
     }
