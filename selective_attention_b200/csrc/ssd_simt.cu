@@ -425,13 +425,21 @@ __global__ void __launch_bounds__(256) simt_chunk_scan_tiled_kernel(
   // C . prev^T over slices of 32 states
   for (int n0 = 0; n0 < N; n0 += kTK) {
     __syncthreads();
-    for (int idx = tid; idx < kTT * kTK; idx += 256) {
-      const int r = idx >> 5, c = idx & 31, l = l0 + r, n = n0 + c;
-      As[r * kTLD + c] = (l < lim && n < N) ? Ld<T>::f(Cm + ((ci.tok0 + l) * G + g) * (long long)N + n) : 0.f;
+    // all loads of the slice issued before any store (indices clamped into range, values masked)
+    float cv[8], pv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + 256 * i, r = idx >> 5, c = idx & 31;
+      const int l = min(l0 + r, lim - 1), n = min(n0 + c, N - 1), p = min(r, P - 1);
+      cv[i] = Ld<T>::f(Cm + ((ci.tok0 + l) * G + g) * (long long)N + n);
+      pv[i] = hp[(long long)p * N + n];  // prev^T: Bs[n][p], prev rows read along n
     }
-    for (int idx = tid; idx < kTK * kTT; idx += 256) {
-      const int p = idx >> 5, c = idx & 31, n = n0 + c;  // prev^T: Bs[n][p], prev rows read along n
-      Bs[c * kTLP + p] = (p < P && n < N) ? hp[(long long)p * N + n] : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + 256 * i, r = idx >> 5, c = idx & 31;
+      const bool nok = n0 + c < N;
+      As[r * kTLD + c] = (l0 + r < lim && nok) ? cv[i] : 0.f;
+      Bs[c * kTLP + r] = (r < P && nok) ? pv[i] : 0.f;
     }
     __syncthreads();
     mma_rk_kc(acc, As, Bs, tr, tc, kTK);
@@ -446,15 +454,23 @@ __global__ void __launch_bounds__(256) simt_chunk_scan_tiled_kernel(
   const int send = min(l0 + kTT, lim);
   for (int s0 = 0; s0 < send; s0 += kTK) {
     __syncthreads();
-    for (int idx = tid; idx < kTT * kTK; idx += 256) {
-      const int r = idx >> 5, c = idx & 31, l = l0 + r, sidx = s0 + c;
-      float m = 0.f;
-      if (l < lim && sidx <= l) m = cbk[(long long)l * cs + sidx] * expf(fminf(cml[r] - cmk[sidx], 0.f)) * dtk[sidx];
-      As[r * kTLD + c] = m;
+    float mv[8], cs8[8], dt8[8], uv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + 256 * i, r = idx >> 5, c = idx & 31;
+      const int l = min(l0 + r, lim - 1), sidx = min(s0 + c, lim - 1);
+      mv[i] = cbk[(long long)l * cs + sidx];
+      cs8[i] = cmk[sidx];
+      dt8[i] = dtk[sidx];
+      const int ur = min(s0 + (idx >> 6), lim - 1), up = min(idx & 63, P - 1);
+      uv[i] = Ld<T>::f(u + ((ci.tok0 + ur) * H + h) * (long long)P + up);
     }
-    for (int idx = tid; idx < kTK * kTT; idx += 256) {
-      const int r = idx >> 6, p = idx & 63, sidx = s0 + r;
-      Bs[r * kTLP + p] = (sidx < lim && p < P) ? Ld<T>::f(u + ((ci.tok0 + sidx) * H + h) * (long long)P + p) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + 256 * i, r = idx >> 5, c = idx & 31, l = l0 + r, sidx = s0 + c;
+      As[r * kTLD + c] = (l < lim && sidx <= l) ? mv[i] * expf(fminf(cml[r] - cs8[i], 0.f)) * dt8[i] : 0.f;
+      const int ur = idx >> 6, up = idx & 63;
+      Bs[ur * kTLP + up] = (s0 + ur < lim && up < P) ? uv[i] : 0.f;
     }
     __syncthreads();
     mma_rk_kc(acc, As, Bs, tr, tc, kTK);
@@ -498,10 +514,19 @@ __global__ void __launch_bounds__(256) simt_bmm_chunk_tiled_kernel(const T* __re
   if (l0 < lim && s0 < lim) {
     for (int n0 = 0; n0 < N; n0 += kTK) {
       __syncthreads();
-      for (int idx = tid; idx < kTT * kTK; idx += 256) {
-        const int r = idx >> 5, c = idx & 31, n = n0 + c;
-        As[r * kTLD + c] = (l0 + r < lim && n < N) ? Ld<T>::f(Cm + ((ci.tok0 + l0 + r) * G + g) * (long long)N + n) : 0.f;
-        Bs[c * kTLP + r] = (s0 + r < lim && n < N) ? Ld<T>::f(Bm + ((ci.tok0 + s0 + r) * G + g) * (long long)N + n) : 0.f;
+      float cv[8], bv[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int idx = tid + 256 * i, r = idx >> 5, c = idx & 31, n = min(n0 + c, N - 1);
+        cv[i] = Ld<T>::f(Cm + ((ci.tok0 + min(l0 + r, lim - 1)) * G + g) * (long long)N + n);
+        bv[i] = Ld<T>::f(Bm + ((ci.tok0 + min(s0 + r, lim - 1)) * G + g) * (long long)N + n);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int idx = tid + 256 * i, r = idx >> 5, c = idx & 31;
+        const bool nok = n0 + c < N;
+        As[r * kTLD + c] = (l0 + r < lim && nok) ? cv[i] : 0.f;
+        Bs[c * kTLP + r] = (s0 + r < lim && nok) ? bv[i] : 0.f;
       }
       __syncthreads();
       mma_rk_kc(acc, As, Bs, tr, tc, kTK);
@@ -543,16 +568,22 @@ __global__ void __launch_bounds__(256) simt_chunk_state_tiled_kernel(
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
   for (int t0 = 0; t0 < lim; t0 += kTK) {
     __syncthreads();
-    for (int idx = tid; idx < kTK * kTT; idx += 256) {
-      const int r = idx >> 6, c = idx & 63, l = t0 + r;  // token r, column c
-      float xv = 0.f, bv = 0.f;
-      if (l < lim) {
-        if (c < P)
-          xv = Ld<T>::f(u + ((ci.tok0 + l) * H + h) * (long long)P + c) * (expf(fminf(clast - cmk[l], 0.f)) * dtk[l]);
-        if (n0 + c < N) bv = Ld<T>::f(Bm + ((ci.tok0 + l) * G + g) * (long long)N + n0 + c);
-      }
-      As[c * kTLD + r] = xv;
-      Bs[r * kTLP + c] = bv;
+    float xv[8], bv[8], c8[8], d8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + 256 * i, r = idx >> 6, c = idx & 63;  // token r, column c
+      const int l = min(t0 + r, lim - 1);
+      xv[i] = Ld<T>::f(u + ((ci.tok0 + l) * H + h) * (long long)P + min(c, P - 1));
+      bv[i] = Ld<T>::f(Bm + ((ci.tok0 + l) * G + g) * (long long)N + min(n0 + c, N - 1));
+      c8[i] = cmk[l];
+      d8[i] = dtk[l];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int idx = tid + 256 * i, r = idx >> 6, c = idx & 63;
+      const bool lok = t0 + r < lim;
+      As[c * kTLD + r] = (lok && c < P) ? xv[i] * (expf(fminf(clast - c8[i], 0.f)) * d8[i]) : 0.f;
+      Bs[r * kTLP + c] = (lok && n0 + c < N) ? bv[i] : 0.f;
     }
     __syncthreads();
     mma_rk_kc(acc, As, Bs, tr, tc, kTK);
