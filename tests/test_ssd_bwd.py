@@ -150,7 +150,7 @@ def make_inputs(seed, b, L, H, P, N, G, dtype, *, h_init=False, bias=False):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_kernel_matches_oracle_c1_heads(dtype):
     """config-1 head shape (P64 N128 cs256) over 4 chunks, a ragged row, 6 heads in 2 groups."""
     from selective_attention_b200 import kernels
