@@ -200,3 +200,27 @@ def test_tensor_core_path_rejects_fp32():
     q = torch.randn(1, 1, 128, 64, device="cuda")
     with pytest.raises(ValueError):
         kernels.sattn_train_forward(q, q, q, torch.rand(1, 1, 128, device="cuda"), 1.0, impl="tc")
+
+
+@pytest.mark.gpu
+def test_tensor_core_path_short_sequence():
+    """L = 100 (one partial 128-token tile; TMA boxes reach past the end), bidirectional."""
+    import selective_attention_b200 as sab
+
+    gen = torch.Generator().manual_seed(41)
+    b, H, L, D = 1, 2, 100, 64
+    q, k, v = (torch.randn(b, H, L, D, generator=gen).bfloat16() for _ in range(3))
+    sel = torch.sigmoid(torch.randn(b, H, L, generator=gen) + 1.0).bfloat16()
+    dout = torch.randn(b, H, L, D, generator=gen).bfloat16()
+    g = {"q_rot": q, "k_rot": k, "v": v, "select_gate": sel, "lengths": None, "log_gate_penalty": 1.0,
+         "is_causal": False, "scale": D ** -0.5, "dout": dout}
+    ref_out, ref_std, ref_grads = _oracle_with_grads(g, torch.float32)
+    leaves = {n: g[n].cuda().requires_grad_(True) for n in GRADS}
+    out, std = sab.selective_attn_train(leaves["q_rot"], leaves["k_rot"], leaves["v"], leaves["select_gate"],
+                                        None, 1.0, False, impl="tc")
+    out.backward(dout.cuda())
+    sab.check_device_error()
+    assert_bf16_close(out.detach().float().cpu(), ref_out, "out")
+    assert_fp32_close(std.cpu(), ref_std, "std")
+    for n in GRADS:
+        assert_bf16_close(leaves[n].grad.float().cpu(), ref_grads[n], f"d{n}")
