@@ -301,7 +301,7 @@ class SSDRun:
         self.tc = kernels.uses_tensor_cores(p)
         self.path = kernels.scan_path(p)
         self.kernel_impl = kernel_impl
-        self.launches = {"tc_fused": 2, "tc_staged": 3, "simt": 5}[self.path] + (1 if cu is not None else 0)
+        self.launches = {"tc_fused": 2, "tc_staged": 3, "simt": 5, "tc_split": 5}[self.path] + (1 if cu is not None else 0)
 
     def step(self, events=None):
         from selective_attention_b200 import kernels
@@ -349,7 +349,8 @@ def measure_ssd(run, args, world, flush, hbm_peak, peak_src, global_tokens, step
     stage_ms = [statistics.median(r[j] for r in st) for j in range(5)]
     sab.check_device_error(dev)
 
-    cfg, tc, path, nseq = run.cfg, run.tc, run.path, run.nseq
+    cfg, path, nseq = run.cfg, run.path, run.nseq
+    tc = path in ("tc_fused", "tc_staged")  # the 16-bit chain: cumsum and bmm fused into neighbours
     b, L, H, P, N, G = run.shape
     T = b * L
     sx = run.inp["u"].element_size()
@@ -395,7 +396,7 @@ def measure_ssd(run, args, world, flush, hbm_peak, peak_src, global_tokens, step
              "frac_of_fused_roof": fused_min / (ms_step / 1e3) / 1e9 / hbm_peak}
     return {"value": global_tokens / (ms_step / 1e3), "unit": "tokens/s", "ms_per_step": ms_step, "steps": steps,
             "path": {"tc_fused": "tcgen05, chunk_state+state_passing fused", "tc_staged": "tcgen05",
-                     "simt": "cuda-core"}[path],
+                     "simt": "cuda-core", "tc_split": "tcgen05, split-bf16 products of fp32"}[path],
             "roofline": roof, "stages": stages, "whole_step": whole, "launches_per_step": run.launches}
 
 
@@ -499,7 +500,8 @@ def c2_measure(args, dev, flush, hbm_peak, peak_src):
 
 def fp32_measure(args, dev, flush, hbm_peak, peak_src):
     """Config c1's shape in fp32 (the reference's own precision: its SSD takes fp32
-    operands only) on one GPU: fp32 u, B, C, z in and y out, on the CUDA-core chain."""
+    operands only) on one GPU: fp32 u, B, C, z in and y out, on the default fp32 chain
+    (tensor cores with split-bf16 products; ``--kernel-impl simt`` does not change it)."""
     from selective_attention_b200 import workloads
 
     cfg = workloads.SSDConfig(**{**workloads.CONFIGS["c1"].__dict__, "dtype": "f32"})
@@ -507,6 +509,12 @@ def fp32_measure(args, dev, flush, hbm_peak, peak_src):
     run = SSDRun(cfg, inp, "auto", dev)
     res = measure_ssd(run, args, 1, flush, hbm_peak, peak_src, cfg.tokens, max(5, min(args.steps, 50)))
     res.update(workload=_workload_name(cfg), n_gpus=1, dtype="f32")
+    del run
+    # the CUDA-core chain on the same inputs (fp32 FFMA products), for comparison
+    run = SSDRun(cfg, inp, "simt", dev)
+    simt = measure_ssd(run, args, 1, flush, hbm_peak, peak_src, cfg.tokens, 5)
+    res["cuda_core_chain"] = {"ms_per_step": simt["ms_per_step"], "value": simt["value"], "path": simt["path"],
+                              "stages_us": {k: v["us"] for k, v in simt["stages"].items()}}
     del run, inp
     torch.cuda.empty_cache()
     return res

@@ -67,7 +67,8 @@ typedef enum { SSD_F32 = 0, SSD_BF16 = 1, SSD_F16 = 2 } ssd_dtype_t;
 typedef enum {
   SSD_IMPL_AUTO = 0,   /* tensor-core path when the shape/dtype allow it, else CUDA-core path;
                           on the tensor-core path chunk_state and state_passing are fused when
-                          there are at least SSD_FUSED_MIN_CHAINS (row, head) chains */
+                          there are at least SSD_FUSED_MIN_CHAINS (row, head) chains; fp32
+                          inputs with fp32 output take the split-bf16 tensor-core chain */
   SSD_IMPL_TC = 1,     /* tcgen05 + TMA kernels (bf16/fp16, headdim 64, dstate 128, chunk 256),
                           chunk_state and state_passing fused (one CTA per (row, head) chain) */
   SSD_IMPL_SIMT = 2,   /* CUDA-core FFMA kernels (any dtype; fp32-exact accumulation) */
@@ -144,12 +145,16 @@ const char* ssd_b200_status_string(int status);
  */
 int ssd_b200_device_error(void* stream);
 
-/* Whether `p` would take the tensor-core path under SSD_IMPL_AUTO (1) or not (0). */
+/* Whether ssd_scan_fwd runs `p` on tensor cores (1: the 16-bit chains, or the split-bf16
+ * chain of fp32 inputs) or on CUDA cores (0). */
 int ssd_scan_uses_tensor_cores(const ssd_params* p);
 
 /* The kernel chain ssd_scan_fwd runs for `p` (its impl field included): 0 CUDA-core
  * stages, 1 tensor-core stages with chunk_state and state_passing as separate launches,
- * 2 tensor-core with chunk_state and state_passing fused; -1 for an invalid geometry.
+ * 2 tensor-core with chunk_state and state_passing fused, 3 fp32 inputs and output on
+ * tensor cores with split-bf16 products (hi = bf16(x), lo = bf16(x - hi); three products
+ * per pair; chunk_state, bmm_chunk and chunk_scan; taken under SSD_IMPL_AUTO at headdim 64,
+ * dstate 128, chunk 256 when u, B and C are 16-byte aligned); -1 for an invalid geometry.
  * No reference counterpart (host-side query). */
 int ssd_scan_path(const ssd_params* p);
 

@@ -19,7 +19,7 @@ BUILD_DIR = os.path.join(ROOT, "_build")
 LIB_NAME = "libssd_b200.so"
 LIB_PATH = os.path.join(PKG_DIR, LIB_NAME)
 
-SOURCES = ["api.cu", "ssd_simt.cu", "ssd_tc.cu", "ssd_bwd.cu", "ssd_bwd_tc.cu", "ssu.cu", "ssm_conv.cu", "sattn.cu", "sattn_train.cu", "noalloc.cu"]
+SOURCES = ["api.cu", "ssd_simt.cu", "ssd_tc.cu", "ssd_split.cu", "ssd_bwd.cu", "ssd_bwd_tc.cu", "ssu.cu", "ssm_conv.cu", "sattn.cu", "sattn_train.cu", "noalloc.cu"]
 HEADERS = ["common.cuh", "sm100.cuh", "tmap.cuh", "sattn_tiles.cuh", "kernels.h"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

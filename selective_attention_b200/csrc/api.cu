@@ -64,6 +64,15 @@ bool use_tc(const ssd_params* p, const Geometry& g) {
   return tc_supported(p->x_dtype, g.P, g.N, g.cs);
 }
 
+// fp32 inputs and output at P 64, N 128, cs 256 under AUTO: chunk_state, bmm_chunk and
+// chunk_scan on tcgen05 with split-bf16 products (ssd_split.cu); SSD_IMPL_SIMT keeps the
+// CUDA-core kernels. u, B, C, D, z and y are accessed with 16-byte loads and stores.
+bool use_split(const ssd_params* p, const Geometry& g) {
+  return p->impl == SSD_IMPL_AUTO && split_supported(p->x_dtype, p->y_dtype, g.P, g.N, g.cs) &&
+         aligned16(p->u) && aligned16(p->B) && aligned16(p->C) && aligned16(p->y) &&
+         (!p->D || aligned16(p->D)) && (!p->z || aligned16(p->z));
+}
+
 // Tensor-core path with chunk_state and state_passing fused (one CTA per (row, head)
 // chain): always under SSD_IMPL_TC, under AUTO when there are enough chains to fill
 // the GPU.
@@ -78,6 +87,8 @@ struct Workspace {
   float* states;
   void* prev16;
   float* CB;
+  void* CBs;  // split-bf16 chain: chunk_scan's operand tiles (masked CB, then the C rows)
+  void* Cs;
   ChunkEntry* table;
   int2* rows;
   int* count;
@@ -97,13 +108,16 @@ Workspace carve(const ssd_params* p, const Geometry& g, bool tc, bool fused, uin
   w.cum = (float*)take(nk * g.H * g.cs * sizeof(float));
   if (!fused) w.states = (float*)take(nk * g.H * (size_t)g.P * g.N * sizeof(float));
   if (tc) w.prev16 = take(nk * g.H * (size_t)g.P * g.N * 2);
-  else w.CB = (float*)take(nk * g.G * (size_t)g.cs * g.cs * sizeof(float));
+  else if (use_split(p, g)) {
+    const size_t per = split_operand_bytes_per_chunk_group();  // 6 CB tiles + 4 C tiles
+    w.CBs = take(nk * g.G * per * 6 / 10);
+    w.Cs = take(nk * g.G * per * 4 / 10);
+  } else w.CB = (float*)take(nk * g.G * (size_t)g.cs * g.cs * sizeof(float));
   if (g.packed) {
     w.table = (ChunkEntry*)take(nk * sizeof(ChunkEntry));
     w.rows = (int2*)take((size_t)g.nrows * sizeof(int2));
     w.count = (int*)take(sizeof(int));
   }
-  (void)p;
   w.bytes = off;
   return w;
 }
@@ -174,19 +188,21 @@ int ssd_b200_device_error(void* stream) {
   const unsigned int c = fetch_error_ssu(s);
   const unsigned int d = fetch_error_sattn(s);
   const unsigned int e = fetch_error_bwd_tc(s);
-  return (int)(a ? a : (b ? b : (c ? c : (d ? d : e))));
+  const unsigned int f = fetch_error_split(s);
+  return (int)(a ? a : (b ? b : (c ? c : (d ? d : (e ? e : f)))));
 }
 
 int ssd_scan_uses_tensor_cores(const ssd_params* p) {
   Geometry g;
   if (geometry(p, g) != SSD_OK) return 0;
-  return use_tc(p, g) ? 1 : 0;
+  return (use_tc(p, g) || use_split(p, g)) ? 1 : 0;
 }
 
 int ssd_scan_path(const ssd_params* p) {
   Geometry g;
   if (geometry(p, g) != SSD_OK) return -1;
   if (use_fused(p, g)) return 2;
+  if (use_split(p, g)) return 3;
   return use_tc(p, g) ? 1 : 0;
 }
 
@@ -260,15 +276,24 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
     if ((st = cuda_status(launch_chunk_cumsum(c, p->dt_dtype, p->A, p->delta_raw, p->delta_bias, w.dt, w.cum))))
       return st;
     record(p, 1, s);
-    if ((st = cuda_status(launch_simt_chunk_state(c, p->x_dtype, p->u, p->B, w.dt, w.cum, w.states)))) return st;
+    const bool split = use_split(p, g);
+    const float *u32 = static_cast<const float*>(p->u), *B32 = static_cast<const float*>(p->B),
+                *C32 = static_cast<const float*>(p->C);
+    if ((st = cuda_status(split ? launch_split_chunk_state(c, u32, B32, w.dt, w.cum, w.states)
+                                : launch_simt_chunk_state(c, p->x_dtype, p->u, p->B, w.dt, w.cum, w.states))))
+      return st;
     record(p, 2, s);
     if ((st = cuda_status(launch_state_passing(c, w.states, nullptr, SSD_F32, w.cum, p->h_init, p->h_last))))
       return st;
     record(p, 3, s);
-    if ((st = cuda_status(launch_simt_bmm_chunk(c, p->x_dtype, p->B, p->C, w.CB)))) return st;
+    if ((st = cuda_status(split ? launch_split_bmm(c, B32, C32, w.CBs, w.Cs)
+                                : launch_simt_bmm_chunk(c, p->x_dtype, p->B, p->C, w.CB))))
+      return st;
     record(p, 4, s);
-    if ((st = cuda_status(launch_simt_chunk_scan(c, p->x_dtype, p->y_dtype, p->u, w.dt, w.cum, p->C, w.states,
-                                                 w.CB, p->D, p->z, p->y))))
+    if ((st = cuda_status(split ? launch_split_chunk_scan(c, u32, w.dt, w.cum, w.Cs, w.states, w.CBs, p->D,
+                                                          static_cast<const float*>(p->z), static_cast<float*>(p->y))
+                                : launch_simt_chunk_scan(c, p->x_dtype, p->y_dtype, p->u, w.dt, w.cum, p->C,
+                                                         w.states, w.CB, p->D, p->z, p->y))))
       return st;
     record(p, 5, s);
   }

@@ -135,6 +135,20 @@ cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, c
                                  const float* D, const void* z, void* y, int* tmap_status);
 unsigned int fetch_error_tc(cudaStream_t s);
 
+// ssd_split.cu (tcgen05 with split-bf16 products for fp32 inputs and outputs, P = 64, N = 128,
+// cs = 256): chunk_state into fp32 states; bmm_chunk writes chunk_scan's A operands (masked
+// CB and the C rows, split into bf16 hi / lo, swizzled) per (chunk, group); chunk_scan reads
+// them with bulk copies, beside the fp32 states that state_passing turned into prev.
+bool split_supported(int x_dtype, int y_dtype, int P, int N, int cs);
+size_t split_operand_bytes_per_chunk_group();
+cudaError_t launch_split_chunk_state(const LaunchCtx& c, const float* u, const float* B, const float* dt,
+                                     const float* cum, float* states);
+cudaError_t launch_split_bmm(const LaunchCtx& c, const float* B, const float* C, void* CBs, void* Cs);
+cudaError_t launch_split_chunk_scan(const LaunchCtx& c, const float* u, const float* dt, const float* cum,
+                                    const void* Cs, const float* prev, const void* CBs, const float* D,
+                                    const float* z, float* y);
+unsigned int fetch_error_split(cudaStream_t s);
+
 // ssu.cu
 cudaError_t launch_ssm_conv_prefill(const void* hbc, long long row_stride, const float* w, const float* bias,
                                     void* x, void* Bo, void* Co, void* ctx, const int64_t* lengths, int b, int L,

@@ -1,0 +1,616 @@
+// ssd_split.cu - the SSD forward for fp32 inputs on tcgen05 tensor cores with split-bf16
+// products (headdim 64, dstate 128, chunk 256).
+//
+// Every fp32 operand x is split into two bf16 parts, hi = bf16(x) and lo = bf16(x - hi),
+// which together carry 16 significant bits; a product a b is taken as
+//   a_hi b_hi + a_hi b_lo + a_lo b_hi
+// (three kind::f16 MMAs into one fp32 TMEM accumulator; the dropped a_lo b_lo term and the
+// rounding of the parts are each about 2^-18 of |a b|). The reference's tl.dot runs fp32
+// operands as TF32 (10-bit mantissas); the three-product split keeps the fp32 chain's
+// rel 1e-4 agreement. The stages are those of the CUDA-core chain with its fp32 cumsum and
+// state passing (ssd_scan/forward_kernel.py:107-185, :270-328, :350-455):
+//   chunk_state  S[p,n]  = sum_l u[l,p] w_l B[l,n],  w_l = exp(min(cum_last - cum_l, 0)) dt_l
+//   bmm_chunk    CB[l,s] = sum_n C[l,n] B[s,n]
+//   chunk_scan   y[l,p]  = exp(cum_l) sum_n C[l,n] prev[p,n]
+//                        + sum_{s <= l} CB[l,s] exp(min(cum_l - cum_s, 0)) dt_s u[s,p]  (+ D u, * silu z)
+// Operands are staged by CUDA cores: fp32 loads (all of a step's loads issued before its
+// stores), the split, and 16-byte stores into the 128-byte-swizzled layout
+// [column / 64][row][column % 64], which one descriptor reads as a K-major operand and
+// another as an MN-major one. Two stages alternate, so the staging of step i + 1 overlaps
+// the MMAs of step i; one thread issues the MMAs. Every mbarrier wait is bounded; a CTA
+// whose wait gives up records a site code and writes nothing.
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace ssdb200 {
+
+using namespace sm100;
+
+namespace {
+
+constexpr unsigned int kSiteSplitState = 0x141;
+constexpr unsigned int kSiteSplitBmm = 0x142;
+constexpr unsigned int kSiteSplitScan = 0x143;
+constexpr int kSplitThreads = 256;
+
+// 8 consecutive fp32 values -> one 16-byte chunk of hi parts and one of lo parts.
+__device__ __forceinline__ void store_split8(uint8_t* hi, uint8_t* lo, uint32_t off, const float (&v)[8]) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    h[q] = pack2<__nv_bfloat16>(v[2 * q], v[2 * q + 1]);
+    const float2 hf = unpack2<__nv_bfloat16>(h[q]);
+    l[q] = pack2<__nv_bfloat16>(v[2 * q] - hf.x, v[2 * q + 1] - hf.y);
+  }
+  *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+  *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+__device__ __forceinline__ void load8(const float* src, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(src));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(src + 4));
+  v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+
+// The three split products of one 16-deep K step into `d`.
+__device__ __forceinline__ void mma3(uint32_t d, uint64_t ah, uint64_t al, uint64_t bh, uint64_t bl, uint32_t id,
+                                     uint32_t acc) {
+  umma_f16(d, ah, bh, id, acc);
+  umma_f16(d, ah, bl, id, 1u);
+  umma_f16(d, al, bh, id, 1u);
+}
+
+// Commit books of the two stage barriers: commits issued per barrier, so a wait can name
+// the phase it needs and the exit path can wait for the last one of each.
+struct StageBooks {
+  int n[2] = {0, 0};
+};
+
+// Wait (bounded, every thread) until stage b's MMAs of commit number `c` (1-based) are done.
+__device__ __forceinline__ bool wait_commit(uint32_t bar, int c, unsigned int site) {
+  return c <= 0 || mbar_wait(bar, (uint32_t)(c - 1) & 1u, site);
+}
+
+// ---------------------------------------------------------------------------- chunk_state
+// CTA = (head, chunk), 256 threads. Steps of 64 tokens: A = B rows as an MN-major
+// operand (M = 128 dstate, two 64-wide blocks 8 KB apart), B operand = the rows u w
+// (N = 64 headdim, MN-major), K = 64 tokens. Warp w reads TMEM lanes 32 (w % 4) (dstate n)
+// and columns 32 (w / 4) (headdim p) and writes states[p][n] (n contiguous).
+constexpr int kSsStage = 2 * 16384 + 2 * 8192;  // B hi | B lo | (u w) hi | (u w) lo
+constexpr size_t kSsSmem = 1024 + 2 * kSsStage;
+
+__global__ void __launch_bounds__(kSplitThreads, 2) split_chunk_state_kernel(
+    const float* __restrict__ u, const float* __restrict__ Bm, const float* __restrict__ dt,
+    const float* __restrict__ cum, float* __restrict__ states, ChunkMap cm, int H, int G) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024_shared(smem_raw);
+  __shared__ float sW[256];
+  __shared__ uint64_t bars[2];
+  __shared__ uint32_t tslot[1];
+  const int h = blockIdx.x, k = blockIdx.y;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long kh = (long long)k * H + h;
+  const int lim = ci.lim;
+  float bv[4][8], uv[2][8];
+  auto load_step = [&](int st) {
+    const int t0 = 64 * st;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // B rows: 64 tokens x 16 chunks of 8 states
+      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
+      load8(Bm + ((ci.tok0 + min(t0 + r, lim - 1)) * G + g) * 128 + 8 * c8, bv[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {  // u rows: 64 tokens x 8 chunks of 8 headdim columns
+      const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+      load8(u + ((ci.tok0 + min(t0 + r, lim - 1)) * H + h) * 64 + 8 * c8, uv[i]);
+    }
+  };
+  load_step(0);  // in flight during the set-up
+  if (tid == 0) {
+    mbar_init(smem_u32(&bars[0]), 1);
+    mbar_init(smem_u32(&bars[1]), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 64);
+  if (tid < lim) {
+    // L2 prefetch (128-byte lines) of the chunk's B rows and this head's u rows
+    const float* br = Bm + ((ci.tok0 + tid) * G + g) * 128;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) asm volatile("prefetch.global.L2 [%0];" ::"l"(br + 32 * j));
+    const float* ur = u + ((ci.tok0 + tid) * H + h) * 64;
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ur));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(ur + 32));
+  }
+  {
+    const float clast = cum[kh * 256 + 255];
+    const float cl = cum[kh * 256 + tid], dl = dt[kh * 256 + tid];
+    sW[tid] = tid < lim ? expf(fminf(clast - cl, 0.f)) * dl : 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  constexpr uint32_t ID = idesc_f16(128, 64, true, /*a_mn=*/true, /*b_mn=*/true);
+  const int nsteps = (lim + 63) >> 6;
+  StageBooks bk;
+  bool ok = true;
+  for (int st = 0; st < nsteps; ++st) {
+    const int b = st & 1, t0 = 64 * st;
+    uint8_t* bH = sm + b * kSsStage;
+    uint8_t* bL = bH + 16384;
+    uint8_t* xH = bH + 32768;
+    uint8_t* xL = bH + 40960;
+    // this stage was last read by the MMAs of step st - 2
+    ok = __syncthreads_and(ok && wait_commit(smem_u32(&bars[b]), bk.n[b], kSiteSplitState)) != 0;
+    if (!ok) break;
+    tc_fence_after();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
+      if (t0 + r >= lim) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bv[i][e] = 0.f;
+      }
+      store_split8(bH, bL, (uint32_t)(c8 >> 3) * 8192u + sw128_off((uint32_t)r, (uint32_t)(c8 & 7)), bv[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+      const float w = sW[t0 + r];  // 0 past lim
+#pragma unroll
+      for (int e = 0; e < 8; ++e) uv[i][e] *= w;
+      store_split8(xH, xL, sw128_off((uint32_t)r, (uint32_t)c8), uv[i]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t bh = smem_u32(bH), bl = smem_u32(bL), xh = smem_u32(xH), xl = smem_u32(xL);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma3(tmem, sdesc_sw128(bh + ks * 2048, 8192, 1024), sdesc_sw128(bl + ks * 2048, 8192, 1024),
+             sdesc_sw128(xh + ks * 2048, 16, 1024), sdesc_sw128(xl + ks * 2048, 16, 1024), ID,
+             (st > 0 || ks > 0) ? 1u : 0u);
+      umma_commit(smem_u32(&bars[b]));
+    }
+    ++bk.n[b];
+    if (st + 1 < nsteps) load_step(st + 1);
+  }
+  // the last commit of each stage barrier (all MMAs are done once both have arrived)
+  const bool done = wait_commit(smem_u32(&bars[0]), bk.n[0], kSiteSplitState) &&
+                    wait_commit(smem_u32(&bars[1]), bk.n[1], kSiteSplitState);
+  tc_fence_after();
+  if (__syncthreads_and(ok && done)) {
+    const int n = (warp & 3) * 32 + lane, p0 = 32 * (warp >> 2);
+    float* out = states + kh * 8192;
+    uint32_t v[32];
+    tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)p0, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) out[(p0 + j) * 128 + n] = __uint_as_float(v[j]);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 64);
+}
+
+// Operand tiles that bmm_chunk writes for chunk_scan: [128 rows][64 columns] of bf16 hi parts
+// in the 128-byte-swizzled K-major layout (16 KB), then the lo parts (16 KB).
+//   CBs per (chunk, group): 6 tiles, half m = 0: source blocks 0, 1; half m = 1: blocks 0..3
+//   Cs  per (chunk, group): 2 halves x 2 dstate blocks
+constexpr int kSplitTile = 32768;
+
+// ---------------------------------------------------------------------------- bmm_chunk
+// CTA = (128 x 128 tile (rows l, columns s) of the lower block triangle, group, chunk),
+// 256 threads, two K steps of 64 states: A = C rows, B operand = B rows, both K-major.
+// Rows or columns at or past lim are zero. The tile above the diagonal block is not
+// written: chunk_scan below reads CB only where s <= l.
+constexpr int kBmStage = 4 * 16384;  // C hi | C lo | B hi | B lo
+constexpr size_t kBmSmem = 1024 + kBmStage;
+
+__global__ void __launch_bounds__(kSplitThreads, 2) split_bmm_kernel(const float* __restrict__ Bm,
+                                                                    const float* __restrict__ Cm,
+                                                                    uint8_t* __restrict__ CBs,
+                                                                    uint8_t* __restrict__ Cs, ChunkMap cm, int G) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024_shared(smem_raw);
+  __shared__ uint64_t bars[1];
+  __shared__ uint32_t tslot[1];
+  const int t = blockIdx.x, g = blockIdx.y, k = blockIdx.z;
+  const int tl = t > 0 ? 1 : 0, ts = t > 1 ? 1 : 0;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int lim = ci.lim;
+  if (128 * tl >= lim) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t bar = smem_u32(&bars[0]);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  constexpr uint32_t ID = idesc_f16(128, 128, true, false, false);
+  uint8_t* cH = sm;
+  uint8_t* cL = sm + 16384;
+  uint8_t* bH = sm + 32768;
+  uint8_t* bL = sm + 49152;
+  // the C rows of half tl as chunk_scan's Yoff operand tiles (written by the ts = 0 CTA)
+  uint8_t* cdst = Cs + (((size_t)k * G + g) * 2 + tl) * (2 * kSplitTile);
+  float cv[4][8], bv[4][8];
+  auto load_step = [&](int st) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {  // 128 rows x 8 chunks of 8 states
+      const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+      load8(Cm + ((ci.tok0 + min(128 * tl + r, lim - 1)) * G + g) * 128 + 64 * st + 8 * c8, cv[i]);
+      load8(Bm + ((ci.tok0 + min(128 * ts + r, lim - 1)) * G + g) * 128 + 64 * st + 8 * c8, bv[i]);
+    }
+  };
+  load_step(0);
+  bool ok = true;
+  int commits = 0;
+  for (int st = 0; st < 2; ++st) {
+    ok = __syncthreads_and(ok && wait_commit(bar, commits, kSiteSplitBmm)) != 0;
+    if (!ok) break;
+    tc_fence_after();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+      if (128 * tl + r >= lim) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) cv[i][e] = 0.f;
+      }
+      if (128 * ts + r >= lim) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bv[i][e] = 0.f;
+      }
+      const uint32_t off = sw128_off((uint32_t)r, (uint32_t)c8);
+      store_split8(cH, cL, off, cv[i]);
+      store_split8(bH, bL, off, bv[i]);
+      if (ts == 0) store_split8(cdst + st * kSplitTile, cdst + st * kSplitTile + 16384, off, cv[i]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t ch = smem_u32(cH), cl = smem_u32(cL), bh = smem_u32(bH), bl = smem_u32(bL);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma3(tmem, sdesc_sw128(ch + ks * 32, 16, 1024), sdesc_sw128(cl + ks * 32, 16, 1024),
+             sdesc_sw128(bh + ks * 32, 16, 1024), sdesc_sw128(bl + ks * 32, 16, 1024), ID,
+             (st > 0 || ks > 0) ? 1u : 0u);
+      umma_commit(bar);
+    }
+    ++commits;
+    if (st == 0) load_step(1);
+  }
+  const bool done = wait_commit(bar, commits, kSiteSplitBmm);
+  tc_fence_after();
+  if (__syncthreads_and(ok && done)) {
+    // thread = row r (TMEM lane); warps 4..7 take the tile's second 64-column block. The
+    // block leaves as chunk_scan's A operand tile: masked to s <= l < lim, split into hi and
+    // lo, in the 128-byte-swizzled K-major layout a bulk copy lands as is.
+    const int r = (warp & 3) * 32 + lane, cb = warp >> 2, l = 128 * tl + r;
+    uint8_t* dst = CBs + (((size_t)k * G + g) * 6 + (tl ? 2 : 0) + 2 * ts + cb) * kSplitTile;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(64 * cb + 32 * hf), v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int s = 128 * ts + 64 * cb + 32 * hf + 8 * q + e;
+          f[e] = (s <= l && l < lim) ? __uint_as_float(v[8 * q + e]) : 0.f;
+        }
+        store_split8(dst, dst + 16384, sw128_off((uint32_t)r, (uint32_t)(4 * hf + q)), f);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+// ---------------------------------------------------------------------------- chunk_scan
+// CTA = (half m of the chunk: rows l in [128 m, 128 m + 128), head, chunk): 8 converter
+// warps and one copy warp. Steps of K = 64, all with A = 128 rows x 64 (K-major) and
+// B = 64 x 64:
+//   steps 0, 1   Yoff += C[l, n-block] prev[p, n-block]^T           (prev K-major)
+//   steps 2...   Yin  += M[l, s-block] u[s-block, p]                 (u MN-major)
+// with M[l,s] = CB[l,s] exp(min(cum_l - cum_s, 0)) dt_s for s <= l < lim, else 0, over the
+// source blocks s < min(128 m + 128, lim). The A tiles (C rows, masked CB) arrive split and
+// swizzled from bmm_chunk, one bulk copy each, issued by the copy warp as soon as the MMAs
+// two steps back have released the stage; the converter warps split the B rows. When cum is
+// non-increasing over the chunk (the min(., 0) clamp is then inert) and falls by at most
+// kScFacMax over the half, the decay is factored at the half's first row l0:
+//   exp(cum_l - cum_s) = exp(cum_l - cum_l0) * exp(cum_l0 - cum_s),
+// the column factor times dt_s scales the u rows (B = w_s u_s, so A is CB itself), and the
+// row factor multiplies the row's Yin in the epilogue (a common factor of every term of the
+// row's sum, so the fp32 accumulation loses nothing; both factors stay inside fp32's range).
+// Other halves rebuild each CB tile in place element by element. The epilogue (thread =
+// TMEM lane = row, warps 4..7 the second half of the columns) forms exp(cum_l) Yoff +
+// rowf_l Yin in shared memory; then a coalesced pass adds D u and the z gate and writes y.
+constexpr int kScThreads = kSplitThreads + 32;     // 8 converter warps + the copy warp
+constexpr int kScStage = kSplitTile + 2 * 8192;    // A hi | A lo | B hi | B lo
+constexpr size_t kScSmem = 1024 + 2 * kScStage;
+constexpr int kScYld = 68;         // row stride (floats) of the epilogue's Y tile (16-byte rows)
+constexpr float kScFacMax = 80.f;  // largest decay over a half for the factored form (e^80 < FLT_MAX)
+
+__global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
+    const float* __restrict__ u, const float* __restrict__ dt, const float* __restrict__ cum,
+    const uint8_t* __restrict__ Cs, const float* __restrict__ prev, const uint8_t* __restrict__ CBs,
+    const float* __restrict__ D, const float* __restrict__ z, float* __restrict__ y, ChunkMap cm, int H, int G) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024_shared(smem_raw);
+  __shared__ __align__(16) float sCum[256], sDt[256], sW[256];
+  __shared__ uint64_t bars[4];  // MMAs of the stage done [2], A tile of the stage landed [2]
+  __shared__ uint32_t tslot[1];
+  const int m = blockIdx.x, h = blockIdx.y, k = blockIdx.z;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int lim = ci.lim, l0 = 128 * m;
+  if (l0 >= lim) return;
+  const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool conv = tid < kSplitThreads;
+  const long long kh = (long long)k * H + h;
+  const float* pk = prev + kh * 8192;
+  const int send = min(l0 + 128, lim);  // source tokens s < send
+  const int nsteps = 2 + ((send + 63) >> 6);
+  auto bar_mma = [&](int b) { return smem_u32(&bars[b]); };
+  auto bar_a = [&](int b) { return smem_u32(&bars[2 + b]); };
+  float bv[2][8];
+  // B rows of step st: prev rows p (steps 0, 1) or u rows 64 (st - 2) + r; 64 rows x 8 chunks of 8
+  auto load_b = [&](int st) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+      if (st < 2) load8(pk + r * 128 + 64 * st + 8 * c8, bv[i]);
+      else load8(u + ((ci.tok0 + min(64 * (st - 2) + r, lim - 1)) * H + h) * 64 + 8 * c8, bv[i]);
+    }
+  };
+  if (conv) load_b(0);  // in flight during the set-up
+  if (tid == 0) {
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 128);
+  float c_t = 0.f;
+  if (conv) {
+    // L2 prefetch (128-byte lines) of the epilogue's u and z rows and of the steps' u rows
+    const int row = tid >> 1, hb = tid & 1, l = l0 + row;
+    if (l < lim) {
+      const long long o = ((ci.tok0 + l) * H + h) * 64 + 32 * hb;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(u + o));
+      if (z) asm volatile("prefetch.global.L2 [%0];" ::"l"(z + o));
+    }
+    if (m == 1 && row < lim)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(u + ((ci.tok0 + row) * H + h) * 64 + 32 * hb));
+    c_t = cum[kh * 256 + tid];
+    sCum[tid] = c_t;
+    sDt[tid] = dt[kh * 256 + tid];
+  }
+  __syncthreads();
+  const bool nonincr = !conv || tid == 0 || tid >= lim || c_t <= sCum[tid - 1];
+  const bool fac = __syncthreads_and(nonincr) && sCum[l0] - sCum[send - 1] <= kScFacMax;
+  if (conv) sW[tid] = (fac && tid < send) ? expf(sCum[l0] - c_t) * sDt[tid] : 0.f;
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  bool fin = true;
+  float4 ue[8], ze[8];
+  const int c4 = tid & 15, rb = tid >> 4;
+  if (!conv) {
+    // ---- copy warp: A tile of step st into stage st & 1 once the MMAs of step st - 2 are done
+    if (lane == 0) {
+      const uint8_t* cs = Cs + (((size_t)k * G + g) * 2 + m) * (2 * kSplitTile);
+      const uint8_t* cbs = CBs + (((size_t)k * G + g) * 6 + (m ? 2 : 0)) * kSplitTile;
+      int issued = 0;
+      for (int st = 0; st < nsteps; ++st) {
+        const int b = st & 1;
+        if (st >= 2 && !mbar_wait(bar_mma(b), (uint32_t)((st - 2) >> 1) & 1u, kSiteSplitScan)) break;
+        const uint8_t* src = st < 2 ? cs + st * kSplitTile : cbs + (st - 2) * kSplitTile;
+        mbar_expect_tx(bar_a(b), (uint32_t)kSplitTile);
+        bulk_load(smem_u32(sm + b * kScStage), src, (uint32_t)kSplitTile, bar_a(b));
+        ++issued;
+      }
+      // no copy may still be in flight when the CTA exits
+      for (int d = 1; d <= 2 && d <= issued; ++d) {
+        const int st = issued - d;
+        mbar_wait(bar_a(st & 1), (uint32_t)(st >> 1) & 1u, kSiteSplitScan);
+      }
+    }
+    __syncwarp();
+  } else {
+    constexpr uint32_t ID_OFF = idesc_f16(128, 64, true, false, false);
+    constexpr uint32_t ID_IN = idesc_f16(128, 64, true, false, /*b_mn=*/true);
+    StageBooks bk;
+    bool ok = true;
+    for (int st = 0; st < nsteps; ++st) {
+      const int b = st & 1, s0 = 64 * (st - 2);
+      uint8_t* aH = sm + b * kScStage;
+      uint8_t* aL = aH + 16384;
+      uint8_t* xH = aH + kSplitTile;
+      uint8_t* xL = xH + 8192;
+      // the B half of stage b was last read by the MMAs of step st - 2
+      ok = named_bar_and(1, kSplitThreads, ok && wait_commit(bar_mma(b), bk.n[b], kSiteSplitScan));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+        if (st >= 2) {
+          // u rows past lim are zero; under the factored decay a row carries w_s
+          const float w = s0 + r >= lim ? 0.f : (fac ? sW[s0 + r] : 1.f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) bv[i][e] *= w;
+        }
+        store_split8(xH, xL, sw128_off((uint32_t)r, (uint32_t)c8), bv[i]);
+      }
+      if (st + 1 < nsteps) load_b(st + 1);
+      const bool landed = mbar_wait(bar_a(b), (uint32_t)(st >> 1) & 1u, kSiteSplitScan);
+      if (landed && !fac && st >= 2) {
+        // element-by-element decay: A = CB exp(min(cum_l - cum_s, 0)) dt_s, rebuilt in place
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+          const uint32_t off = sw128_off((uint32_t)r, (uint32_t)c8);
+          const uint4 hv = *reinterpret_cast<const uint4*>(aH + off);
+          const uint4 lv = *reinterpret_cast<const uint4*>(aL + off);
+          const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, lw[4] = {lv.x, lv.y, lv.z, lv.w};
+          const float cl = sCum[l0 + r];
+          float f[8];
+#pragma unroll
+          for (int e2 = 0; e2 < 4; ++e2) {
+            const float2 a = unpack2<__nv_bfloat16>(hw[e2]), c = unpack2<__nv_bfloat16>(lw[e2]);
+            const int sa = s0 + 8 * c8 + 2 * e2;
+            f[2 * e2] = (a.x + c.x) * expf(fminf(cl - sCum[sa], 0.f)) * sDt[sa];
+            f[2 * e2 + 1] = (a.y + c.y) * expf(fminf(cl - sCum[sa + 1], 0.f)) * sDt[sa + 1];
+          }
+          store_split8(aH, aL, off, f);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      ok = named_bar_and(1, kSplitThreads, ok && landed);
+      if (!ok) break;
+      if (tid == 0) {
+        tc_fence_after();
+        const uint32_t ah = smem_u32(aH), al = smem_u32(aL), xh = smem_u32(xH), xl = smem_u32(xL);
+        if (st < 2) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            mma3(tmem, sdesc_sw128(ah + ks * 32, 16, 1024), sdesc_sw128(al + ks * 32, 16, 1024),
+                 sdesc_sw128(xh + ks * 32, 16, 1024), sdesc_sw128(xl + ks * 32, 16, 1024), ID_OFF,
+                 (st > 0 || ks > 0) ? 1u : 0u);
+        } else {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            mma3(tmem + 64, sdesc_sw128(ah + ks * 32, 16, 1024), sdesc_sw128(al + ks * 32, 16, 1024),
+                 sdesc_sw128(xh + ks * 2048, 16, 1024), sdesc_sw128(xl + ks * 2048, 16, 1024), ID_IN,
+                 (st > 2 || ks > 0) ? 1u : 0u);
+        }
+        umma_commit(bar_mma(b));
+      }
+      ++bk.n[b];
+    }
+    // The epilogue's u (D term) and z rows, loaded while the last MMAs run: thread (rb, c4)
+    // takes 16-byte column piece c4 of rows rb + 16 i (rows clamped; stores skip rows past lim).
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const long long o = ((ci.tok0 + min(l0 + rb + 16 * i, lim - 1)) * H + h) * 64 + 4 * c4;
+      ue[i] = D ? __ldg(reinterpret_cast<const float4*>(u + o)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      ze[i] = z ? __ldg(reinterpret_cast<const float4*>(z + o)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    fin = ok && wait_commit(bar_mma(0), bk.n[0], kSiteSplitScan) &&
+          wait_commit(bar_mma(1), bk.n[1], kSiteSplitScan);
+  }
+  tc_fence_after();
+  const bool all_ok = __syncthreads_and(fin) != 0;
+  if (all_ok && conv) {
+    // Y tile [128 rows][64 columns] (row stride kScYld) over the stages, which the MMAs no longer read
+    float* sY = reinterpret_cast<float*>(sm);
+    const int r = (warp & 3) * 32 + lane, c0 = 32 * (warp >> 2);
+    const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;
+    const float el = expf(sCum[l0 + r]);
+    const float rowf = fac ? expf(sCum[l0 + r] - sCum[l0]) : 1.f;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      uint32_t vo[16], vi[16];
+      tmem_ld16(tmem + tl + (uint32_t)(c0 + 16 * hf), vo);
+      tmem_ld16(tmem + tl + 64u + (uint32_t)(c0 + 16 * hf), vi);
+      tmem_wait_ld();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float4 o4;
+        o4.x = fmaf(el, __uint_as_float(vo[4 * q]), rowf * __uint_as_float(vi[4 * q]));
+        o4.y = fmaf(el, __uint_as_float(vo[4 * q + 1]), rowf * __uint_as_float(vi[4 * q + 1]));
+        o4.z = fmaf(el, __uint_as_float(vo[4 * q + 2]), rowf * __uint_as_float(vi[4 * q + 2]));
+        o4.w = fmaf(el, __uint_as_float(vo[4 * q + 3]), rowf * __uint_as_float(vi[4 * q + 3]));
+        *reinterpret_cast<float4*>(sY + r * kScYld + c0 + 16 * hf + 4 * q) = o4;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+  if (!all_ok || !conv) return;
+  const float* sY = reinterpret_cast<const float*>(sm);
+  const float4 d4 = D ? __ldg(reinterpret_cast<const float4*>(D + h * 64 + 4 * c4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = rb + 16 * i, l = l0 + r;
+    if (l >= lim) break;
+    float4 v = *reinterpret_cast<const float4*>(sY + r * kScYld + 4 * c4);
+    if (D) {
+      v.x = fmaf(d4.x, ue[i].x, v.x);
+      v.y = fmaf(d4.y, ue[i].y, v.y);
+      v.z = fmaf(d4.z, ue[i].z, v.z);
+      v.w = fmaf(d4.w, ue[i].w, v.w);
+    }
+    if (z) {
+      v.x *= silu(ze[i].x);
+      v.y *= silu(ze[i].y);
+      v.z *= silu(ze[i].z);
+      v.w *= silu(ze[i].w);
+    }
+    *reinterpret_cast<float4*>(y + ((ci.tok0 + l) * H + h) * 64 + 4 * c4) = v;
+  }
+}
+
+}  // namespace
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+bool split_supported(int x_dtype, int y_dtype, int P, int N, int cs) {
+  return x_dtype == SSD_F32 && y_dtype == SSD_F32 && P == 64 && N == 128 && cs == 256;
+}
+
+cudaError_t launch_split_chunk_state(const LaunchCtx& c, const float* u, const float* B, const float* dt,
+                                     const float* cum, float* states) {
+  cudaError_t e = cudaFuncSetAttribute(split_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kSsSmem);
+  if (e != cudaSuccess) return e;
+  split_chunk_state_kernel<<<dim3((unsigned)c.H, (unsigned)c.nchunks_max), kSplitThreads, kSsSmem, c.stream>>>(
+      u, B, dt, cum, states, c.cm, c.H, c.G);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_bmm(const LaunchCtx& c, const float* B, const float* C, void* CBs, void* Cs) {
+  cudaError_t e =
+      cudaFuncSetAttribute(split_bmm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBmSmem);
+  if (e != cudaSuccess) return e;
+  split_bmm_kernel<<<dim3(3u, (unsigned)c.G, (unsigned)c.nchunks_max), kSplitThreads, kBmSmem, c.stream>>>(
+      B, C, static_cast<uint8_t*>(CBs), static_cast<uint8_t*>(Cs), c.cm, c.G);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_chunk_scan(const LaunchCtx& c, const float* u, const float* dt, const float* cum,
+                                    const void* Cs, const float* prev, const void* CBs, const float* D,
+                                    const float* z, float* y) {
+  cudaError_t e = cudaFuncSetAttribute(split_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kScSmem);
+  if (e != cudaSuccess) return e;
+  split_chunk_scan_kernel<<<dim3(2u, (unsigned)c.H, (unsigned)c.nchunks_max), kScThreads, kScSmem, c.stream>>>(
+      u, dt, cum, static_cast<const uint8_t*>(Cs), prev, static_cast<const uint8_t*>(CBs), D, z, y, c.cm, c.H,
+      c.G);
+  return cudaGetLastError();
+}
+
+size_t split_operand_bytes_per_chunk_group() { return (size_t)(6 + 4) * kSplitTile; }
+
+SSDB200_DEFINE_ERROR_FETCH(fetch_error_split)
+
+}  // namespace ssdb200

@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
   bool pend_tma = true, pend_mma = false;
   int cur_mma_bar = 2;
   for (int ph = 0; ph < (two_phases ? 2 : 1); ++ph) {
-    bool w_ok = mbar_wait(bar[ph], 0, kSiteStateTma);
+    bool w_ok = mbar_wait_sleep(bar[ph], 0, kSiteStateTma);
     if (w_ok) {
       // x rows scaled by w_l in place (rows past `lim` have w = 0 and become exact zeros).
       for (int q = tid; q < 1024; q += 128) {
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
     if (ph == 0 && two_phases) {
       // The second phase reuses the buffers: wait for this phase's MMAs first.
       if (tid == 0) {
-        if (mbar_wait(bar[2], 0, kSiteStateMma)) {
+        if (mbar_wait_sleep(bar[2], 0, kSiteStateMma)) {
           mbar_expect_tx(bar[1], 49152u);
           tma_load_3d(smem_u32(sX), &tm_x, 0, h, t0 + 128, bar[1]);
           tma_load_3d(smem_u32(sB), &tm_b, 0, g, t0 + 128, bar[1]);
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
     }
   }
   bool mma_ok = false;
-  if (ok) mma_ok = mbar_wait(bar[cur_mma_bar], 0, kSiteStateMma);
+  if (ok) mma_ok = mbar_wait_sleep(bar[cur_mma_bar], 0, kSiteStateMma);
   tc_fence_after();
   if (ok && __syncthreads_and(mma_ok)) {
     const int n = warp * 32 + lane;
@@ -268,8 +268,8 @@ __global__ void __launch_bounds__(128) tc_chunk_state_kernel(
     }
   } else if (tid == 0) {
     // Let in-flight copies / MMAs land (bounded) before the CTA exits.
-    if (pend_tma) mbar_wait(bar[two_phases ? 1 : 0], 0, kSiteStateTma);
-    if (pend_mma) mbar_wait(bar[cur_mma_bar], 0, kSiteStateMma);
+    if (pend_tma) mbar_wait_sleep(bar[two_phases ? 1 : 0], 0, kSiteStateTma);
+    if (pend_mma) mbar_wait_sleep(bar[cur_mma_bar], 0, kSiteStateMma);
   }
   tc_fence_before();
   __syncthreads();
@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
   // the abort flag, so the others leave at their next check or bounded wait.
   bool wfail = false;
   auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
-    if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
+    if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait_sleep(b, parity, site));
     return !wfail;
   };
 
@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         const int nst = (ci.lim + 127) >> 7, t0 = (int)ci.tok0;
         for (int s = 0; s < nst; ++s, ++r) {
           const int slot = r % NST;
-          if (r >= NST && !mbar_wait(bar(EMPTY + slot), ((r / NST) - 1) & 1, kSiteSpMma)) {
+          if (r >= NST && !mbar_wait_sleep(bar(EMPTY + slot), ((r / NST) - 1) & 1, kSiteSpMma)) {
             fail = true;
             break;
           }
@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       // No copy may still be in flight when the CTA exits.
       for (int d = 1; d <= NST && d <= r; ++d) {
         const int rr = r - d;
-        mbar_wait(bar(FULL + rr % NST), (rr / NST) & 1, kSiteSpTma);
+        mbar_wait_sleep(bar(FULL + rr % NST), (rr / NST) & 1, kSiteSpTma);
       }
     }
     __syncwarp();
@@ -447,13 +447,13 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
         const int nst = (ci.lim + 127) >> 7;
         const uint32_t acc = tmem + 128 * (k % NA);
         // the fold of chunk k - 2 must have read this accumulator
-        if (k >= NA && !mbar_wait(bar(ACC_FREE + k % NA), ((k - NA) / NA) & 1, kSiteSpFold)) {
+        if (k >= NA && !mbar_wait_sleep(bar(ACC_FREE + k % NA), ((k - NA) / NA) & 1, kSiteSpFold)) {
           fail = true;
           break;
         }
         for (int s = 0; s < nst; ++s, ++r) {
           const int slot = r % NST;
-          if (!mbar_wait(bar(SCALED + slot), (r / NST) & 1, kSiteSpScaled)) {
+          if (!mbar_wait_sleep(bar(SCALED + slot), (r / NST) & 1, kSiteSpScaled)) {
             fail = true;
             break;
           }
@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(kSpThreads, 1) tc_state_pass_kernel(
       }
       if (fail) *s_abort = 1;
       // All MMAs must be complete before TMEM is released.
-      if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, kSiteSpMma);
+      if (last_bar >= 0) mbar_wait_sleep(bar(last_bar), last_par, kSiteSpMma);
     }
     __syncwarp();
   } else if (warp < 6) {
@@ -855,7 +855,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       // [128, 256) that the first half does not use.)
       auto load_z = [&]() -> bool {
         const int s = zpend % NS;
-        if (!mbar_wait(bar(YOFF0 + s), (zpend / NS) & 1, kSiteScanMma2)) return false;
+        if (!mbar_wait_sleep(bar(YOFF0 + s), (zpend / NS) & 1, kSiteScanMma2)) return false;
         mbar_expect_tx(bar(Z_FULL0 + s), 16384u);
         tma_load_3d(smem_u32(hstage(s) + 32768), &tm_z, 0, zh, zt, bar(Z_FULL0 + s));
         ++zc;
@@ -869,8 +869,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         const int t0 = (int)ci.tok0, S = 128 * (si.m + 1);
         // C free once the previous item's last MMA3 completed; the B buffer once the
         // previous MMA1 did.
-        if ((I > 0 && !mbar_wait(bar(C_FREE), (I - 1) & 1, kSiteScanMma1)) ||
-            (Bc > 0 && !mbar_wait(bar(B_FREE), (Bc - 1) & 1, kSiteScanMma1))) {
+        if ((I > 0 && !mbar_wait_sleep(bar(C_FREE), (I - 1) & 1, kSiteScanMma1)) ||
+            (Bc > 0 && !mbar_wait_sleep(bar(B_FREE), (Bc - 1) & 1, kSiteScanMma1))) {
           fail = true;
           break;
         }
@@ -888,8 +888,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           const int h = si.h0 + i, hs = Hc % NS;
           // The stage is free once the epilogue of the head NS back copied what it
           // needs and that head's MMAs completed.
-          if (Hc >= NS && (!mbar_wait(bar(STAGE_FREE0 + hs), ((Hc - NS) / NS) & 1, kSiteScanEpi) ||
-                           !mbar_wait(bar(STAGE_MMA0 + hs), ((Hc - NS) / NS) & 1, kSiteScanMma2))) {
+          if (Hc >= NS && (!mbar_wait_sleep(bar(STAGE_FREE0 + hs), ((Hc - NS) / NS) & 1, kSiteScanEpi) ||
+                           !mbar_wait_sleep(bar(STAGE_MMA0 + hs), ((Hc - NS) / NS) & 1, kSiteScanMma2))) {
             fail = true;
             break;
           }
@@ -920,7 +920,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           }
           if (i == 0 && si.m == 1) {
             // B rows of block 1 once MMA1 of block 0 has read the buffer
-            if (!mbar_wait(bar(B_FREE), (Bc - 1) & 1, kSiteScanMma1)) {
+            if (!mbar_wait_sleep(bar(B_FREE), (Bc - 1) & 1, kSiteScanMma1)) {
               fail = true;
               break;
             }
@@ -937,15 +937,15 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       if (!fail && !*s_abort && zpend >= 0 && !load_z()) fail = true;
       if (fail) *s_abort = 1;
       // No copy may still be in flight when the CTA exits.
-      if (I > 0) mbar_wait(bar(ITEM_FULL), (I - 1) & 1, kSiteScanTma);
-      if (Bj > 0) mbar_wait(bar(BJ_FULL), (Bj - 1) & 1, kSiteScanTma);
+      if (I > 0) mbar_wait_sleep(bar(ITEM_FULL), (I - 1) & 1, kSiteScanTma);
+      if (Bj > 0) mbar_wait_sleep(bar(BJ_FULL), (Bj - 1) & 1, kSiteScanTma);
       for (int d = 1; d <= NS && d <= Hc; ++d) {
         const int hc = Hc - d;
-        mbar_wait(bar(HEAD_FULL0 + hc % NS), (hc / NS) & 1, kSiteScanTma);
+        mbar_wait_sleep(bar(HEAD_FULL0 + hc % NS), (hc / NS) & 1, kSiteScanTma);
       }
       for (int d = 1; d <= NS && d <= zc; ++d) {
         const int hc = zc - d;
-        mbar_wait(bar(Z_FULL0 + hc % NS), (hc / NS) & 1, kSiteScanTma);
+        mbar_wait_sleep(bar(Z_FULL0 + hc % NS), (hc / NS) & 1, kSiteScanTma);
       }
     }
     __syncwarp();
@@ -962,7 +962,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         ScanItem si;
         ChunkInfo ci;
         if (!scan_item(cm, it, G, hpg, HB, si, ci)) continue;
-        if (!mbar_wait(bar(ITEM_FULL), I & 1, kSiteScanTma)) {
+        if (!mbar_wait_sleep(bar(ITEM_FULL), I & 1, kSiteScanTma)) {
           fail = true;
           break;
         }
@@ -971,9 +971,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           // The landing zone is Y buffer 1: free once the epilogue of the last head
           // that used it loaded it, and once the previous CB_j landing was converted.
           const int y1 = Hc / 2;  // heads so far that used Y buffer 1 (odd head counters)
-          if ((y1 > 0 && !mbar_wait(bar(YFREE1), (y1 - 1) & 1, kSiteScanEpi)) ||
-              (Sc > 0 && !mbar_wait(bar(CBS_FREE), (Sc - 1) & 1, kSiteScanConv)) ||
-              (j == 1 && !mbar_wait(bar(BJ_FULL), Bj & 1, kSiteScanTma))) {
+          if ((y1 > 0 && !mbar_wait_sleep(bar(YFREE1), (y1 - 1) & 1, kSiteScanEpi)) ||
+              (Sc > 0 && !mbar_wait_sleep(bar(CBS_FREE), (Sc - 1) & 1, kSiteScanConv)) ||
+              (j == 1 && !mbar_wait_sleep(bar(BJ_FULL), Bj & 1, kSiteScanTma))) {
             fail = true;
             break;
           }
@@ -992,14 +992,14 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
         }
         if (fail) break;
         // Head MMAs may write Y buffer 1 only after the last landing was converted.
-        if (!mbar_wait(bar(CBS_FREE), (Sc - 1) & 1, kSiteScanConv)) {
+        if (!mbar_wait_sleep(bar(CBS_FREE), (Sc - 1) & 1, kSiteScanConv)) {
           fail = true;
           break;
         }
         for (int i = 0; i < si.nh && !fail; ++i) {
           const int hs = Hc % NS, yb = Hc & 1;
-          if (!mbar_wait(bar(HEAD_FULL0 + hs), (Hc / NS) & 1, kSiteScanTma) ||
-              (Hc >= 2 && !mbar_wait(bar(YFREE0 + yb), ((Hc - 2) >> 1) & 1, kSiteScanEpi))) {
+          if (!mbar_wait_sleep(bar(HEAD_FULL0 + hs), (Hc / NS) & 1, kSiteScanTma) ||
+              (Hc >= 2 && !mbar_wait_sleep(bar(YFREE0 + yb), ((Hc - 2) >> 1) & 1, kSiteScanEpi))) {
             fail = true;
             break;
           }
@@ -1015,7 +1015,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
           if (i == si.nh - 1) umma_commit(bar(C_FREE));
           for (int j = 0; j <= si.m; ++j) {
             const int mb = Jc & 1;
-            if (!mbar_wait(bar(MFULL0 + mb), (Jc >> 1) & 1, kSiteScanConv)) {
+            if (!mbar_wait_sleep(bar(MFULL0 + mb), (Jc >> 1) & 1, kSiteScanConv)) {
               fail = true;
               break;
             }
@@ -1038,8 +1038,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
       }
       if (fail) *s_abort = 1;
       // All MMAs must be complete before TMEM is released.
-      if (last_bar >= 0) mbar_wait(bar(last_bar), last_par, kSiteScanMma2);
-      else if (Sc > 0) mbar_wait(bar(CBS_FULL), (Sc - 1) & 1, kSiteScanMma1);
+      if (last_bar >= 0) mbar_wait_sleep(bar(last_bar), last_par, kSiteScanMma2);
+      else if (Sc > 0) mbar_wait_sleep(bar(CBS_FULL), (Sc - 1) & 1, kSiteScanMma1);
     }
     __syncwarp();
   } else if (warp < 10) {
@@ -1053,7 +1053,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     int I = 0, Hc = 0, Jc = 0, Sc = 0;
     bool fail = false, wfail = false;
     auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
-      if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
+      if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait_sleep(b, parity, site));
       return !wfail;
     };
     for (int jt = 0, it = scan_item_of(0); it < n_items && !fail; it = scan_item_of(++jt)) {
@@ -1201,7 +1201,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) tc_chunk_scan_kernel(
     int Hc = 0;
     bool fail = false, wfail = false;
     auto warp_wait = [&](uint32_t b, uint32_t parity, unsigned int site) {
-      if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait(b, parity, site));
+      if (!wfail) wfail = !__all_sync(0xffffffffu, mbar_wait_sleep(b, parity, site));
       return !wfail;
     };
     for (int jt = 0, it = scan_item_of(0); it < n_items && !fail; it = scan_item_of(++jt)) {

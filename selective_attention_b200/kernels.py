@@ -192,12 +192,13 @@ def uses_tensor_cores(params) -> bool:
     return bool(_lib.lib().ssd_scan_uses_tensor_cores(byref(params)))
 
 
-SCAN_PATHS = {0: "simt", 1: "tc_staged", 2: "tc_fused"}
+SCAN_PATHS = {0: "simt", 1: "tc_staged", 2: "tc_fused", 3: "tc_split"}
 
 
 def scan_path(params) -> str:
-    """Kernel chain of ``ssd_scan_fwd`` for these parameters: "simt", "tc_staged" or
-    "tc_fused" (chunk_state and state_passing in one kernel)."""
+    """Kernel chain of ``ssd_scan_fwd`` for these parameters: "simt", "tc_staged",
+    "tc_fused" (chunk_state and state_passing in one kernel) or "tc_split" (fp32 inputs:
+    chunk_state, bmm_chunk and chunk_scan on tensor cores with split-bf16 products)."""
     code = _lib.lib().ssd_scan_path(byref(params))
     if code < 0:
         raise ValueError("invalid SSD geometry")

@@ -23,12 +23,13 @@ INF = float("inf")
 
 
 # (dtype, batch, seqlen, heads, chain the default dispatch takes). 2 x 8 (row, head)
-# chains run the staged tensor-core chain (bf16) or the CUDA-core chain (fp32); 8 x 16 =
-# 128 chains reach the fused chain, whose state pass and chunk_scan overlap through a
-# dependent launch and read dt, cum and the 16-bit chunk states from the scratch array.
+# chains run the staged tensor-core chain (bf16) or the split-bf16 tensor-core chain (fp32,
+# fp32 states and CB in the scratch array); 8 x 16 = 128 chains reach the fused chain, whose
+# state pass and chunk_scan overlap through a dependent launch and read dt, cum and the
+# 16-bit chunk states from the scratch array.
 CASES = [
     (torch.bfloat16, 2, 700, 8, "tc_staged"),
-    (torch.float32, 2, 700, 8, "simt"),
+    (torch.float32, 2, 700, 8, "tc_split"),
     (torch.bfloat16, 8, 700, 16, "tc_fused"),
 ]
 
