@@ -881,7 +881,9 @@ def ref_gpu_measure(args, dev, flush):
     package ``baseline/install_reference.sh`` installs into ``baseline/_ref``; ``ops/ssd_scan.py``
     over ``triton_kernels/ssd_scan``) at config 1's shape in fp32, its operand type, forward
     and forward + backward, beside this library's ``SSDScanFn`` on the same fp32 inputs (the
-    CUDA-core chain) and on bf16 inputs (tensor cores). No D / z (the reference op has none).
+    split-bf16 tensor-core forward, and the CUDA-core chain with ``impl="simt"``; the fp32
+    backward runs on CUDA cores in both) and on bf16 inputs (tensor cores). No D / z (the
+    reference op has none).
     The reference runs its stock code path; Triton compiles and autotunes it on first use,
     outside the timed steps."""
     import selective_attention_b200 as sab
@@ -906,18 +908,18 @@ def ref_gpu_measure(args, dev, flush):
     steps = max(3, min(args.steps, 10))
     stream = torch.cuda.current_stream(dev)
 
-    def run(name, op, dtype):
+    def run(name, op, dtype, extra=()):
         leaves = [inp[k].to(dtype) if k in ("u", "B", "C") else inp[k] for k in ("u", "A", "B", "C", "delta_raw")]
         bias = inp.get("delta_bias")
         yg = torch.randn(inp["u"].shape, device=dev, generator=g)
 
         def fwd():
             with torch.no_grad():
-                return op.apply(*leaves, bias, None, length, cfg.chunk)
+                return op.apply(*leaves, bias, None, length, cfg.chunk, *extra)
 
         def fwd_bwd():
             xs = [t.detach().requires_grad_(True) for t in leaves]
-            y, h = op.apply(*xs, bias, None, length, cfg.chunk)
+            y, h = op.apply(*xs, bias, None, length, cfg.chunk, *extra)
             torch.autograd.backward([y], [yg.to(y.dtype)])
 
         try:
@@ -932,6 +934,7 @@ def ref_gpu_measure(args, dev, flush):
 
     run("reference_triton_fp32", RefSSD, torch.float32)
     run("ours_fp32", sab.SSDScanFn, torch.float32)
+    run("ours_fp32_cuda_core", sab.SSDScanFn, torch.float32, (True, (0.0, INF), True, None, None, None, "simt"))
     run("ours_bf16", sab.SSDScanFn, torch.bfloat16)
     r, o = res.get("reference_triton_fp32", {}), res.get("ours_bf16", {})
     if "fwd_ms" in r and "fwd_ms" in o:
@@ -939,6 +942,7 @@ def ref_gpu_measure(args, dev, flush):
         res["speedup_bf16_vs_reference_fwd_bwd"] = r["fwd_bwd_ms"] / o["fwd_bwd_ms"]
     if "fwd_ms" in r and "fwd_ms" in res.get("ours_fp32", {}):
         res["speedup_fp32_vs_reference_fwd"] = r["fwd_ms"] / res["ours_fp32"]["fwd_ms"]
+        res["speedup_fp32_vs_reference_fwd_bwd"] = r["fwd_bwd_ms"] / res["ours_fp32"]["fwd_bwd_ms"]
     del inp
     torch.cuda.empty_cache()
     return res

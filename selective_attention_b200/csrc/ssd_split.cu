@@ -323,15 +323,15 @@ __global__ void __launch_bounds__(kSplitThreads, 2) split_bmm_kernel(const float
 }
 
 // ---------------------------------------------------------------------------- chunk_scan
-// CTA = (half m of the chunk: rows l in [128 m, 128 m + 128), head, chunk): 8 converter
-// warps and one copy warp. Steps of K = 64, all with A = 128 rows x 64 (K-major) and
-// B = 64 x 64:
+// CTA = (half m of the chunk: rows l in [128 m, 128 m + 128), head, chunk), 256 threads.
+// Steps of K = 64, all with A = 128 rows x 64 (K-major) and B = 64 x 64:
 //   steps 0, 1   Yoff += C[l, n-block] prev[p, n-block]^T           (prev K-major)
 //   steps 2...   Yin  += M[l, s-block] u[s-block, p]                 (u MN-major)
 // with M[l,s] = CB[l,s] exp(min(cum_l - cum_s, 0)) dt_s for s <= l < lim, else 0, over the
 // source blocks s < min(128 m + 128, lim). The A tiles (C rows, masked CB) arrive split and
-// swizzled from bmm_chunk, one bulk copy each, issued by the copy warp as soon as the MMAs
-// two steps back have released the stage; the converter warps split the B rows. When cum is
+// swizzled from bmm_chunk, one bulk copy each: steps 0 and 1 at the start, step st + 1 as
+// soon as thread 0 has issued step st's MMAs and step st - 1's are done; every thread splits
+// the B rows, loaded two steps ahead into one of two register sets. When cum is
 // non-increasing over the chunk (the min(., 0) clamp is then inert) and falls by at most
 // kScFacMax over the half, the decay is factored at the half's first row l0:
 //   exp(cum_l - cum_s) = exp(cum_l - cum_l0) * exp(cum_l0 - cum_s),
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kSplitThreads, 2) split_bmm_kernel(const float
 // Other halves rebuild each CB tile in place element by element. The epilogue (thread =
 // TMEM lane = row, warps 4..7 the second half of the columns) forms exp(cum_l) Yoff +
 // rowf_l Yin in shared memory; then a coalesced pass adds D u and the z gate and writes y.
-constexpr int kScThreads = kSplitThreads + 32;     // 8 converter warps + the copy warp
+constexpr int kScThreads = kSplitThreads;
 constexpr int kScStage = kSplitTile + 2 * 8192;    // A hi | A lo | B hi | B lo
 constexpr size_t kScSmem = 1024 + 2 * kScStage;
 constexpr int kScYld = 68;         // row stride (floats) of the epilogue's Y tile (16-byte rows)
@@ -362,31 +362,40 @@ __global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
   const int lim = ci.lim, l0 = 128 * m;
   if (l0 >= lim) return;
   const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const bool conv = tid < kSplitThreads;
   const long long kh = (long long)k * H + h;
   const float* pk = prev + kh * 8192;
   const int send = min(l0 + 128, lim);  // source tokens s < send
   const int nsteps = 2 + ((send + 63) >> 6);
   auto bar_mma = [&](int b) { return smem_u32(&bars[b]); };
   auto bar_a = [&](int b) { return smem_u32(&bars[2 + b]); };
-  float bv[2][8];
   // B rows of step st: prev rows p (steps 0, 1) or u rows 64 (st - 2) + r; 64 rows x 8 chunks of 8
-  auto load_b = [&](int st) {
+  float bv0[2][8], bv1[2][8];
+  auto load_b = [&](int st, float (&dst)[2][8]) {
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
-      if (st < 2) load8(pk + r * 128 + 64 * st + 8 * c8, bv[i]);
-      else load8(u + ((ci.tok0 + min(64 * (st - 2) + r, lim - 1)) * H + h) * 64 + 8 * c8, bv[i]);
+      if (st < 2) load8(pk + r * 128 + 64 * st + 8 * c8, dst[i]);
+      else load8(u + ((ci.tok0 + min(64 * (st - 2) + r, lim - 1)) * H + h) * 64 + 8 * c8, dst[i]);
     }
   };
-  if (conv) load_b(0);  // in flight during the set-up
+  load_b(0, bv0);  // in flight during the set-up
+  load_b(1, bv1);
+  const uint8_t* cs = Cs + (((size_t)k * G + g) * 2 + m) * (2 * kSplitTile);
+  const uint8_t* cbs = CBs + (((size_t)k * G + g) * 6 + (m ? 2 : 0)) * kSplitTile;
+  auto a_src = [&](int st) { return st < 2 ? cs + st * kSplitTile : cbs + (st - 2) * kSplitTile; };
   if (tid == 0) {
+    // the barriers, and the A tiles of steps 0 and 1 started at once
     for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars[i]), 1);
     fence_mbar_init();
+    for (int st = 0; st < 2; ++st) {
+      mbar_expect_tx(bar_a(st), (uint32_t)kSplitTile);
+      bulk_load(smem_u32(sm + st * kScStage), a_src(st), (uint32_t)kSplitTile, bar_a(st));
+    }
   }
+  int a_issued = 2;  // A tiles started (thread 0's count)
   if (warp == 0) tmem_alloc(smem_u32(tslot), 128);
-  float c_t = 0.f;
-  if (conv) {
+  float c_t;
+  {
     // L2 prefetch (128-byte lines) of the epilogue's u and z rows and of the steps' u rows
     const int row = tid >> 1, hb = tid & 1, l = l0 + row;
     if (l < lim) {
@@ -401,9 +410,9 @@ __global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
     sDt[tid] = dt[kh * 256 + tid];
   }
   __syncthreads();
-  const bool nonincr = !conv || tid == 0 || tid >= lim || c_t <= sCum[tid - 1];
+  const bool nonincr = tid == 0 || tid >= lim || c_t <= sCum[tid - 1];
   const bool fac = __syncthreads_and(nonincr) && sCum[l0] - sCum[send - 1] <= kScFacMax;
-  if (conv) sW[tid] = (fac && tid < send) ? expf(sCum[l0] - c_t) * sDt[tid] : 0.f;
+  sW[tid] = (fac && tid < send) ? expf(sCum[l0] - c_t) * sDt[tid] : 0.f;
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -411,41 +420,21 @@ __global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
   bool fin = true;
   float4 ue[8], ze[8];
   const int c4 = tid & 15, rb = tid >> 4;
-  if (!conv) {
-    // ---- copy warp: A tile of step st into stage st & 1 once the MMAs of step st - 2 are done
-    if (lane == 0) {
-      const uint8_t* cs = Cs + (((size_t)k * G + g) * 2 + m) * (2 * kSplitTile);
-      const uint8_t* cbs = CBs + (((size_t)k * G + g) * 6 + (m ? 2 : 0)) * kSplitTile;
-      int issued = 0;
-      for (int st = 0; st < nsteps; ++st) {
-        const int b = st & 1;
-        if (st >= 2 && !mbar_wait(bar_mma(b), (uint32_t)((st - 2) >> 1) & 1u, kSiteSplitScan)) break;
-        const uint8_t* src = st < 2 ? cs + st * kSplitTile : cbs + (st - 2) * kSplitTile;
-        mbar_expect_tx(bar_a(b), (uint32_t)kSplitTile);
-        bulk_load(smem_u32(sm + b * kScStage), src, (uint32_t)kSplitTile, bar_a(b));
-        ++issued;
-      }
-      // no copy may still be in flight when the CTA exits
-      for (int d = 1; d <= 2 && d <= issued; ++d) {
-        const int st = issued - d;
-        mbar_wait(bar_a(st & 1), (uint32_t)(st >> 1) & 1u, kSiteSplitScan);
-      }
-    }
-    __syncwarp();
-  } else {
+  {
     constexpr uint32_t ID_OFF = idesc_f16(128, 64, true, false, false);
     constexpr uint32_t ID_IN = idesc_f16(128, 64, true, false, /*b_mn=*/true);
-    StageBooks bk;
+    int committed = 0;  // steps whose MMAs were issued and committed (stage st & 1 holds st >> 1 before step st)
     bool ok = true;
-    for (int st = 0; st < nsteps; ++st) {
-      const int b = st & 1, s0 = 64 * (st - 2);
+    // step st on stage b = st & 1 (a literal at each call) with its B rows in `cur`
+    auto step = [&](const int st, const int b, float (&cur)[2][8]) {
+      const int s0 = 64 * (st - 2);
       uint8_t* aH = sm + b * kScStage;
       uint8_t* aL = aH + 16384;
       uint8_t* xH = aH + kSplitTile;
       uint8_t* xL = xH + 8192;
       // the B half of stage b was last read by the MMAs of step st - 2
-      ok = named_bar_and(1, kSplitThreads, ok && wait_commit(bar_mma(b), bk.n[b], kSiteSplitScan));
-      if (!ok) break;
+      ok = named_bar_and(1, kSplitThreads, ok && wait_commit(bar_mma(b), st >> 1, kSiteSplitScan));
+      if (!ok) return;
       tc_fence_after();
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
@@ -454,11 +443,11 @@ __global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
           // u rows past lim are zero; under the factored decay a row carries w_s
           const float w = s0 + r >= lim ? 0.f : (fac ? sW[s0 + r] : 1.f);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) bv[i][e] *= w;
+          for (int e = 0; e < 8; ++e) cur[i][e] *= w;
         }
-        store_split8(xH, xL, sw128_off((uint32_t)r, (uint32_t)c8), bv[i]);
+        store_split8(xH, xL, sw128_off((uint32_t)r, (uint32_t)c8), cur[i]);
       }
-      if (st + 1 < nsteps) load_b(st + 1);
+      if (st + 2 < nsteps) load_b(st + 2, cur);
       const bool landed = mbar_wait(bar_a(b), (uint32_t)(st >> 1) & 1u, kSiteSplitScan);
       if (landed && !fac && st >= 2) {
         // element-by-element decay: A = CB exp(min(cum_l - cum_s, 0)) dt_s, rebuilt in place
@@ -484,7 +473,7 @@ __global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
       fence_proxy_async_smem();
       tc_fence_before();
       ok = named_bar_and(1, kSplitThreads, ok && landed);
-      if (!ok) break;
+      if (!ok) return;
       if (tid == 0) {
         tc_fence_after();
         const uint32_t ah = smem_u32(aH), al = smem_u32(aL), xh = smem_u32(xH), xl = smem_u32(xL);
@@ -502,8 +491,21 @@ __global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
                  (st > 2 || ks > 0) ? 1u : 0u);
         }
         umma_commit(bar_mma(b));
+        // the A tile of step st + 1 goes into the stage that step st - 1 used, once its MMAs are done
+        if (st + 1 < nsteps && st + 1 >= 2) {
+          const int nb = (st + 1) & 1;
+          if (mbar_wait(bar_mma(nb), (uint32_t)((st - 1) >> 1) & 1u, kSiteSplitScan)) {
+            mbar_expect_tx(bar_a(nb), (uint32_t)kSplitTile);
+            bulk_load(smem_u32(sm + nb * kScStage), a_src(st + 1), (uint32_t)kSplitTile, bar_a(nb));
+            a_issued = st + 2;
+          }
+        }
       }
-      ++bk.n[b];
+      ++committed;
+    };
+    for (int st = 0; st < nsteps && ok; st += 2) {
+      step(st, 0, bv0);
+      if (st + 1 < nsteps && ok) step(st + 1, 1, bv1);
     }
     // The epilogue's u (D term) and z rows, loaded while the last MMAs run: thread (rb, c4)
     // takes 16-byte column piece c4 of rows rb + 16 i (rows clamped; stores skip rows past lim).
@@ -513,12 +515,13 @@ __global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
       ue[i] = D ? __ldg(reinterpret_cast<const float4*>(u + o)) : make_float4(0.f, 0.f, 0.f, 0.f);
       ze[i] = z ? __ldg(reinterpret_cast<const float4*>(z + o)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    fin = ok && wait_commit(bar_mma(0), bk.n[0], kSiteSplitScan) &&
-          wait_commit(bar_mma(1), bk.n[1], kSiteSplitScan);
+    const bool drained = wait_commit(bar_mma(0), (committed + 1) >> 1, kSiteSplitScan) &&
+                         wait_commit(bar_mma(1), committed >> 1, kSiteSplitScan);
+    fin = ok && drained;
   }
   tc_fence_after();
   const bool all_ok = __syncthreads_and(fin) != 0;
-  if (all_ok && conv) {
+  if (all_ok) {
     // Y tile [128 rows][64 columns] (row stride kScYld) over the stages, which the MMAs no longer read
     float* sY = reinterpret_cast<float*>(sm);
     const int r = (warp & 3) * 32 + lane, c0 = 32 * (warp >> 2);
@@ -545,7 +548,12 @@ __global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 128);
-  if (!all_ok || !conv) return;
+  if (tid == 0 && !all_ok) {
+    // after a failed wait no A copy may still be in flight when the CTA exits (bounded)
+    for (int st = max(0, a_issued - 2); st < a_issued; ++st)
+      mbar_wait(bar_a(st & 1), (uint32_t)(st >> 1) & 1u, kSiteSplitScan);
+  }
+  if (!all_ok) return;
   const float* sY = reinterpret_cast<const float*>(sm);
   const float4 d4 = D ? __ldg(reinterpret_cast<const float4*>(D + h * 64 + 4 * c4)) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
