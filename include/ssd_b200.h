@@ -129,9 +129,9 @@ typedef struct ssd_params {
   void* workspace;
   size_t workspace_bytes;
   /* Optional cudaEvent_t handles recorded on the stream by ssd_scan_fwd: [0] before
-     the first stage, then after chunk_cumsum [1], chunk_state [2], state_passing [3],
-     bmm_chunk [4] (same point as [3] when bmm is fused) and chunk_scan [5]. NULL
-     entries are skipped. */
+     the first stage, then after chunk_cumsum [1] (on the split-bf16 chain also after the
+     split of B for chunk_state), chunk_state [2], state_passing [3], bmm_chunk [4] (same
+     point as [3] when bmm is fused) and chunk_scan [5]. NULL entries are skipped. */
   void* events[6];
 } ssd_params;
 

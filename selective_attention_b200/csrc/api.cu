@@ -87,7 +87,8 @@ struct Workspace {
   float* states;
   void* prev16;
   float* CB;
-  void* CBs;  // split-bf16 chain: chunk_scan's operand tiles (masked CB, then the C rows)
+  void* Bs;   // split-bf16 chain: operand tiles of chunk_state (B rows) and chunk_scan
+  void* CBs;  // (masked CB, C rows)
   void* Cs;
   ChunkEntry* table;
   int2* rows;
@@ -109,9 +110,10 @@ Workspace carve(const ssd_params* p, const Geometry& g, bool tc, bool fused, uin
   if (!fused) w.states = (float*)take(nk * g.H * (size_t)g.P * g.N * sizeof(float));
   if (tc) w.prev16 = take(nk * g.H * (size_t)g.P * g.N * 2);
   else if (use_split(p, g)) {
-    const size_t per = split_operand_bytes_per_chunk_group();  // 6 CB tiles + 4 C tiles
-    w.CBs = take(nk * g.G * per * 6 / 10);
-    w.Cs = take(nk * g.G * per * 4 / 10);
+    const size_t tile = split_operand_bytes_per_chunk_group() / 14;  // 4 B + 6 CB + 4 C tiles
+    w.Bs = take(nk * g.G * 4 * tile);
+    w.CBs = take(nk * g.G * 6 * tile);
+    w.Cs = take(nk * g.G * 4 * tile);
   } else w.CB = (float*)take(nk * g.G * (size_t)g.cs * g.cs * sizeof(float));
   if (g.packed) {
     w.table = (ChunkEntry*)take(nk * sizeof(ChunkEntry));
@@ -273,13 +275,15 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
     if ((st = cuda_status(e))) return st;
     record(p, 5, s);
   } else {
-    if ((st = cuda_status(launch_chunk_cumsum(c, p->dt_dtype, p->A, p->delta_raw, p->delta_bias, w.dt, w.cum))))
-      return st;
-    record(p, 1, s);
     const bool split = use_split(p, g);
     const float *u32 = static_cast<const float*>(p->u), *B32 = static_cast<const float*>(p->B),
                 *C32 = static_cast<const float*>(p->C);
-    if ((st = cuda_status(split ? launch_split_chunk_state(c, u32, B32, w.dt, w.cum, w.states)
+    if ((st = cuda_status(launch_chunk_cumsum(c, p->dt_dtype, p->A, p->delta_raw, p->delta_bias, w.dt, w.cum))))
+      return st;
+    // split chain: chunk_state's B tiles are written here too (inside events [0, 1])
+    if (split && (st = cuda_status(launch_split_b(c, B32, w.Bs)))) return st;
+    record(p, 1, s);
+    if ((st = cuda_status(split ? launch_split_chunk_state(c, u32, w.Bs, w.dt, w.cum, w.states)
                                 : launch_simt_chunk_state(c, p->x_dtype, p->u, p->B, w.dt, w.cum, w.states))))
       return st;
     record(p, 2, s);

@@ -136,12 +136,13 @@ cudaError_t launch_tc_chunk_scan(const LaunchCtx& c, int x_dtype, int y_dtype, c
 unsigned int fetch_error_tc(cudaStream_t s);
 
 // ssd_split.cu (tcgen05 with split-bf16 products for fp32 inputs and outputs, P = 64, N = 128,
-// cs = 256): chunk_state into fp32 states; bmm_chunk writes chunk_scan's A operands (masked
-// CB and the C rows, split into bf16 hi / lo, swizzled) per (chunk, group); chunk_scan reads
-// them with bulk copies, beside the fp32 states that state_passing turned into prev.
+// cs = 256). Operand tiles per (chunk, group), split into bf16 hi / lo and swizzled, read with
+// bulk copies: split_b writes chunk_state's B tiles (4), bmm_chunk chunk_scan's masked CB (6)
+// and C (4) tiles. chunk_state writes fp32 states, which state_passing turns into prev.
 bool split_supported(int x_dtype, int y_dtype, int P, int N, int cs);
-size_t split_operand_bytes_per_chunk_group();
-cudaError_t launch_split_chunk_state(const LaunchCtx& c, const float* u, const float* B, const float* dt,
+size_t split_operand_bytes_per_chunk_group();  // Bs + CBs + Cs
+cudaError_t launch_split_b(const LaunchCtx& c, const float* B, void* Bs);
+cudaError_t launch_split_chunk_state(const LaunchCtx& c, const float* u, const void* Bs, const float* dt,
                                      const float* cum, float* states);
 cudaError_t launch_split_bmm(const LaunchCtx& c, const float* B, const float* C, void* CBs, void* Cs);
 cudaError_t launch_split_chunk_scan(const LaunchCtx& c, const float* u, const float* dt, const float* cum,

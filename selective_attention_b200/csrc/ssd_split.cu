@@ -72,21 +72,60 @@ __device__ __forceinline__ bool wait_commit(uint32_t bar, int c, unsigned int si
   return c <= 0 || mbar_wait(bar, (uint32_t)(c - 1) & 1u, site);
 }
 
+// Operand tiles written once per (chunk, group) and read with bulk copies: 32 KB each, the bf16
+// hi parts (16 KB) then the lo parts (16 KB), in the 128-byte-swizzled layout.
+//   Bs  per (chunk, group): 4 tiles, one per 64-token step of chunk_state: the step's B rows as
+//       an MN-major operand, [dstate block (2)][64 tokens][64 states], split_b_kernel
+//   CBs per (chunk, group): 6 tiles [128 rows][64 source tokens], K-major: half m = 0: source
+//       blocks 0, 1; half m = 1: blocks 0..3 (masked CB), bmm_chunk
+//   Cs  per (chunk, group): 2 halves x 2 dstate blocks [128 rows][64 states], K-major, bmm_chunk
+constexpr int kSplitTile = 32768;
+
+// ---------------------------------------------------------------------------- B tiles
+// CTA = (64-token step, group, chunk): the step's B rows (rows at or past lim zero), split.
+__global__ void __launch_bounds__(kSplitThreads) split_b_kernel(const float* __restrict__ Bm,
+                                                                uint8_t* __restrict__ Bs, ChunkMap cm, int G) {
+  const int st = blockIdx.x, g = blockIdx.y, k = blockIdx.z;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int lim = ci.lim, t0 = 64 * st;
+  if (t0 >= lim) return;
+  const int tid = threadIdx.x;
+  uint8_t* dst = Bs + (((size_t)k * G + g) * 4 + st) * kSplitTile;
+  float v[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // 64 tokens x 16 chunks of 8 states
+    const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
+    load8(Bm + ((ci.tok0 + min(t0 + r, lim - 1)) * G + g) * 128 + 8 * c8, v[i]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
+    if (t0 + r >= lim) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+    }
+    store_split8(dst, dst + 16384, (uint32_t)(c8 >> 3) * 8192u + sw128_off((uint32_t)r, (uint32_t)(c8 & 7)), v[i]);
+  }
+}
+
 // ---------------------------------------------------------------------------- chunk_state
-// CTA = (head, chunk), 256 threads. Steps of 64 tokens: A = B rows as an MN-major
-// operand (M = 128 dstate, two 64-wide blocks 8 KB apart), B operand = the rows u w
-// (N = 64 headdim, MN-major), K = 64 tokens. Warp w reads TMEM lanes 32 (w % 4) (dstate n)
-// and columns 32 (w / 4) (headdim p) and writes states[p][n] (n contiguous).
-constexpr int kSsStage = 2 * 16384 + 2 * 8192;  // B hi | B lo | (u w) hi | (u w) lo
+// CTA = (head, chunk), 256 threads. Steps of 64 tokens: A = the step's B tile (MN-major,
+// M = 128 dstate in two 64-wide blocks 8 KB apart), landed by a bulk copy (steps 0 and 1 at
+// the start, step st + 1 once thread 0 has issued step st's MMAs and step st - 1's are done);
+// B operand = the rows u w (N = 64 headdim, MN-major), split by every thread from registers
+// loaded two steps ahead; K = 64 tokens. Warp w reads TMEM lanes 32 (w % 4) (dstate n) and
+// columns 32 (w / 4) (headdim p) and writes states[p][n] (n contiguous).
+constexpr int kSsStage = kSplitTile + 2 * 8192;  // B tile hi | lo | (u w) hi | (u w) lo
 constexpr size_t kSsSmem = 1024 + 2 * kSsStage;
 
 __global__ void __launch_bounds__(kSplitThreads, 2) split_chunk_state_kernel(
-    const float* __restrict__ u, const float* __restrict__ Bm, const float* __restrict__ dt,
+    const float* __restrict__ u, const uint8_t* __restrict__ Bs, const float* __restrict__ dt,
     const float* __restrict__ cum, float* __restrict__ states, ChunkMap cm, int H, int G) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024_shared(smem_raw);
   __shared__ float sW[256];
-  __shared__ uint64_t bars[2];
+  __shared__ uint64_t bars[4];  // MMAs of the stage done [2], B tile of the stage landed [2]
   __shared__ uint32_t tslot[1];
   const int h = blockIdx.x, k = blockIdx.y;
   ChunkInfo ci;
@@ -94,36 +133,32 @@ __global__ void __launch_bounds__(kSplitThreads, 2) split_chunk_state_kernel(
   const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long kh = (long long)k * H + h;
   const int lim = ci.lim;
-  float bv[4][8], uv[2][8];
-  auto load_step = [&](int st) {
-    const int t0 = 64 * st;
+  const int nsteps = (lim + 63) >> 6;
+  auto bar_mma = [&](int b) { return smem_u32(&bars[b]); };
+  auto bar_a = [&](int b) { return smem_u32(&bars[2 + b]); };
+  const uint8_t* bsrc = Bs + ((size_t)k * G + g) * 4 * kSplitTile;
+  // u rows of step st: 64 tokens x 8 chunks of 8 headdim columns
+  float uv0[2][8], uv1[2][8];
+  auto load_u = [&](int st, float (&dst)[2][8]) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {  // B rows: 64 tokens x 16 chunks of 8 states
-      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
-      load8(Bm + ((ci.tok0 + min(t0 + r, lim - 1)) * G + g) * 128 + 8 * c8, bv[i]);
-    }
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {  // u rows: 64 tokens x 8 chunks of 8 headdim columns
+    for (int i = 0; i < 2; ++i) {
       const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
-      load8(u + ((ci.tok0 + min(t0 + r, lim - 1)) * H + h) * 64 + 8 * c8, uv[i]);
+      load8(u + ((ci.tok0 + min(64 * st + r, lim - 1)) * H + h) * 64 + 8 * c8, dst[i]);
     }
   };
-  load_step(0);  // in flight during the set-up
+  load_u(0, uv0);  // in flight during the set-up
+  if (nsteps > 1) load_u(1, uv1);
+  int a_issued = 0;  // B tiles started (thread 0's count)
   if (tid == 0) {
-    mbar_init(smem_u32(&bars[0]), 1);
-    mbar_init(smem_u32(&bars[1]), 1);
+    for (int i = 0; i < 4; ++i) mbar_init(smem_u32(&bars[i]), 1);
     fence_mbar_init();
+    for (; a_issued < 2 && a_issued < nsteps; ++a_issued) {
+      mbar_expect_tx(bar_a(a_issued), (uint32_t)kSplitTile);
+      bulk_load(smem_u32(sm + a_issued * kSsStage), bsrc + a_issued * kSplitTile, (uint32_t)kSplitTile,
+                bar_a(a_issued));
+    }
   }
   if (warp == 0) tmem_alloc(smem_u32(tslot), 64);
-  if (tid < lim) {
-    // L2 prefetch (128-byte lines) of the chunk's B rows and this head's u rows
-    const float* br = Bm + ((ci.tok0 + tid) * G + g) * 128;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) asm volatile("prefetch.global.L2 [%0];" ::"l"(br + 32 * j));
-    const float* ur = u + ((ci.tok0 + tid) * H + h) * 64;
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(ur));
-    asm volatile("prefetch.global.L2 [%0];" ::"l"(ur + 32));
-  }
   {
     const float clast = cum[kh * 256 + 255];
     const float cl = cum[kh * 256 + tid], dl = dt[kh * 256 + tid];
@@ -134,57 +169,64 @@ __global__ void __launch_bounds__(kSplitThreads, 2) split_chunk_state_kernel(
   tc_fence_after();
   const uint32_t tmem = *tslot;
   constexpr uint32_t ID = idesc_f16(128, 64, true, /*a_mn=*/true, /*b_mn=*/true);
-  const int nsteps = (lim + 63) >> 6;
-  StageBooks bk;
+  int committed = 0;  // steps whose MMAs were issued and committed
   bool ok = true;
-  for (int st = 0; st < nsteps; ++st) {
-    const int b = st & 1, t0 = 64 * st;
-    uint8_t* bH = sm + b * kSsStage;
-    uint8_t* bL = bH + 16384;
-    uint8_t* xH = bH + 32768;
-    uint8_t* xL = bH + 40960;
-    // this stage was last read by the MMAs of step st - 2
-    ok = __syncthreads_and(ok && wait_commit(smem_u32(&bars[b]), bk.n[b], kSiteSplitState)) != 0;
-    if (!ok) break;
+  // step st on stage b = st & 1 (a literal at each call) with its u rows in `cur`
+  auto step = [&](const int st, const int b, float (&cur)[2][8]) {
+    uint8_t* aH = sm + b * kSsStage;
+    uint8_t* aL = aH + 16384;
+    uint8_t* xH = aH + kSplitTile;
+    uint8_t* xL = xH + 8192;
+    // the (u w) half of stage b was last read by the MMAs of step st - 2
+    ok = __syncthreads_and(ok && wait_commit(bar_mma(b), st >> 1, kSiteSplitState)) != 0;
+    if (!ok) return;
     tc_fence_after();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
-      if (t0 + r >= lim) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) bv[i][e] = 0.f;
-      }
-      store_split8(bH, bL, (uint32_t)(c8 >> 3) * 8192u + sw128_off((uint32_t)r, (uint32_t)(c8 & 7)), bv[i]);
-    }
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
       const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
-      const float w = sW[t0 + r];  // 0 past lim
+      const float w = sW[64 * st + r];  // 0 past lim
 #pragma unroll
-      for (int e = 0; e < 8; ++e) uv[i][e] *= w;
-      store_split8(xH, xL, sw128_off((uint32_t)r, (uint32_t)c8), uv[i]);
+      for (int e = 0; e < 8; ++e) cur[i][e] *= w;
+      store_split8(xH, xL, sw128_off((uint32_t)r, (uint32_t)c8), cur[i]);
     }
+    if (st + 2 < nsteps) load_u(st + 2, cur);
+    const bool landed = mbar_wait(bar_a(b), (uint32_t)(st >> 1) & 1u, kSiteSplitState);
     fence_proxy_async_smem();
     tc_fence_before();
-    __syncthreads();
+    ok = __syncthreads_and(ok && landed) != 0;
+    if (!ok) return;
     if (tid == 0) {
       tc_fence_after();
-      const uint32_t bh = smem_u32(bH), bl = smem_u32(bL), xh = smem_u32(xH), xl = smem_u32(xL);
+      const uint32_t bh = smem_u32(aH), bl = smem_u32(aL), xh = smem_u32(xH), xl = smem_u32(xL);
 #pragma unroll
       for (int ks = 0; ks < 4; ++ks)
         mma3(tmem, sdesc_sw128(bh + ks * 2048, 8192, 1024), sdesc_sw128(bl + ks * 2048, 8192, 1024),
              sdesc_sw128(xh + ks * 2048, 16, 1024), sdesc_sw128(xl + ks * 2048, 16, 1024), ID,
              (st > 0 || ks > 0) ? 1u : 0u);
-      umma_commit(smem_u32(&bars[b]));
+      umma_commit(bar_mma(b));
+      // the B tile of step st + 1 goes into the stage step st - 1 used, once its MMAs are done
+      if (st + 1 < nsteps && st + 1 >= 2) {
+        const int nb = (st + 1) & 1;
+        if (mbar_wait(bar_mma(nb), (uint32_t)((st - 1) >> 1) & 1u, kSiteSplitState)) {
+          mbar_expect_tx(bar_a(nb), (uint32_t)kSplitTile);
+          bulk_load(smem_u32(sm + nb * kSsStage), bsrc + (st + 1) * kSplitTile, (uint32_t)kSplitTile,
+                    bar_a(nb));
+          a_issued = st + 2;
+        }
+      }
     }
-    ++bk.n[b];
-    if (st + 1 < nsteps) load_step(st + 1);
+    ++committed;
+  };
+  for (int st = 0; st < nsteps && ok; st += 2) {
+    step(st, 0, uv0);
+    if (st + 1 < nsteps && ok) step(st + 1, 1, uv1);
   }
   // the last commit of each stage barrier (all MMAs are done once both have arrived)
-  const bool done = wait_commit(smem_u32(&bars[0]), bk.n[0], kSiteSplitState) &&
-                    wait_commit(smem_u32(&bars[1]), bk.n[1], kSiteSplitState);
+  const bool done = wait_commit(bar_mma(0), (committed + 1) >> 1, kSiteSplitState) &&
+                    wait_commit(bar_mma(1), committed >> 1, kSiteSplitState);
   tc_fence_after();
-  if (__syncthreads_and(ok && done)) {
+  const bool all_ok = __syncthreads_and(ok && done) != 0;
+  if (all_ok) {
     const int n = (warp & 3) * 32 + lane, p0 = 32 * (warp >> 2);
     float* out = states + kh * 8192;
     uint32_t v[32];
@@ -192,17 +234,15 @@ __global__ void __launch_bounds__(kSplitThreads, 2) split_chunk_state_kernel(
     tmem_wait_ld();
 #pragma unroll
     for (int j = 0; j < 32; ++j) out[(p0 + j) * 128 + n] = __uint_as_float(v[j]);
+  } else if (tid == 0) {
+    // after a failed wait no B copy may still be in flight when the CTA exits (bounded)
+    for (int st = max(0, a_issued - 2); st < a_issued; ++st)
+      mbar_wait(bar_a(st & 1), (uint32_t)(st >> 1) & 1u, kSiteSplitState);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 64);
 }
-
-// Operand tiles that bmm_chunk writes for chunk_scan: [128 rows][64 columns] of bf16 hi parts
-// in the 128-byte-swizzled K-major layout (16 KB), then the lo parts (16 KB).
-//   CBs per (chunk, group): 6 tiles, half m = 0: source blocks 0, 1; half m = 1: blocks 0..3
-//   Cs  per (chunk, group): 2 halves x 2 dstate blocks
-constexpr int kSplitTile = 32768;
 
 // ---------------------------------------------------------------------------- bmm_chunk
 // CTA = (128 x 128 tile (rows l, columns s) of the lower block triangle, group, chunk),
@@ -586,13 +626,19 @@ bool split_supported(int x_dtype, int y_dtype, int P, int N, int cs) {
   return x_dtype == SSD_F32 && y_dtype == SSD_F32 && P == 64 && N == 128 && cs == 256;
 }
 
-cudaError_t launch_split_chunk_state(const LaunchCtx& c, const float* u, const float* B, const float* dt,
+cudaError_t launch_split_b(const LaunchCtx& c, const float* B, void* Bs) {
+  split_b_kernel<<<dim3(4u, (unsigned)c.G, (unsigned)c.nchunks_max), kSplitThreads, 0, c.stream>>>(
+      B, static_cast<uint8_t*>(Bs), c.cm, c.G);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_chunk_state(const LaunchCtx& c, const float* u, const void* Bs, const float* dt,
                                      const float* cum, float* states) {
   cudaError_t e = cudaFuncSetAttribute(split_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSsSmem);
   if (e != cudaSuccess) return e;
   split_chunk_state_kernel<<<dim3((unsigned)c.H, (unsigned)c.nchunks_max), kSplitThreads, kSsSmem, c.stream>>>(
-      u, B, dt, cum, states, c.cm, c.H, c.G);
+      u, static_cast<const uint8_t*>(Bs), dt, cum, states, c.cm, c.H, c.G);
   return cudaGetLastError();
 }
 
@@ -617,7 +663,7 @@ cudaError_t launch_split_chunk_scan(const LaunchCtx& c, const float* u, const fl
   return cudaGetLastError();
 }
 
-size_t split_operand_bytes_per_chunk_group() { return (size_t)(6 + 4) * kSplitTile; }
+size_t split_operand_bytes_per_chunk_group() { return (size_t)(6 + 4 + 4) * kSplitTile; }
 
 SSDB200_DEFINE_ERROR_FETCH(fetch_error_split)
 

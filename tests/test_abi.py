@@ -105,14 +105,15 @@ def test_workspace_and_dispatch_queries_are_host_only():
     simt = _params(impl=2)
     assert L.ssd_scan_uses_tensor_cores(ctypes.byref(simt)) == 0
     # fp32 in and out: the split-bf16 tensor-core chain under AUTO (fp32 states, and per
-    # (chunk, group) chunk_scan's ten 32 KB operand tiles: six of masked CB, four of C rows),
+    # (chunk, group) fourteen 32 KB operand tiles: four of B rows for chunk_state, six of
+    # masked CB and four of C rows for chunk_scan),
     # the CUDA-core chain under SIMT (fp32 states and the fp32 CB)
     f32 = _params(x_dtype=0, y_dtype=0)
     assert L.ssd_scan_uses_tensor_cores(ctypes.byref(f32)) == 1
     assert L.ssd_scan_path(ctypes.byref(f32)) == 3
     assert L.ssd_scan_path(ctypes.byref(_params(x_dtype=0, y_dtype=0, impl=2))) == 0
     base32 = 2 * nk * H * 256 * 4 + nk * H * 64 * 128 * 4
-    assert L.ssd_scan_fwd_workspace_size(ctypes.byref(f32)) == base32 + nk * 10 * 32768
+    assert L.ssd_scan_fwd_workspace_size(ctypes.byref(f32)) == base32 + nk * 14 * 32768
     assert L.ssd_scan_fwd_workspace_size(ctypes.byref(_params(x_dtype=0, y_dtype=0, impl=2))) == \
         base32 + nk * 256 * 256 * 4
 
