@@ -99,6 +99,32 @@ def test_split_packed_varlen_vs_oracle():
         assert_fp32_close(h[s:s + 1], hs, f"split seq {s} h_last")
 
 
+def test_split_groups_vs_oracle():
+    """Several groups with an odd number of heads each (H6 over G2: B / C rows and the operand
+    tiles are per (chunk, group)), h_init and a ragged row."""
+    inp = _inputs(seed=13, batch=2, seqlen=600, nheads=6, ngroups=2, h_init=True)
+    length = torch.tensor([600, 389])
+    y, h = _run(inp, "auto", length=length, h_init=inp["h_init"])
+    y_ref, h_ref = _oracle(inp, length=length, h_init=inp["h_init"])
+    assert_fp32_close(y, y_ref, "split groups y")
+    assert_fp32_close(h, h_ref, "split groups h_last")
+
+
+def test_split_without_gate_returns_fp32_scan_output():
+    """No D / z: y is the plain scan output (the reference contract, fp32)."""
+    import selective_attention_b200 as sab
+
+    inp = _inputs(seed=17, batch=1, seqlen=512, nheads=4, D=False, z=False)
+    y, h = sab.SSDScanFn.apply(dev(inp["u"]), dev(inp["A"]), dev(inp["B"]), dev(inp["C"]), dev(inp["delta_raw"]),
+                               None, None, None, 256)
+    sab.check_device_error()
+    y_ref, h_ref = ssd_ref.ssd_scan_forward(inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"], None, None,
+                                            None, 256)
+    assert y.dtype == torch.float32
+    assert_fp32_close(y, y_ref, "split y (no gate)")
+    assert_fp32_close(h, h_ref, "split h_last (no gate)")
+
+
 def test_split_and_simt_agree_and_repeat_bit_identically():
     inp = _inputs(seed=9, batch=2, seqlen=1024, nheads=8)
     y1, h1 = _run(inp, "auto")
