@@ -29,14 +29,16 @@ __global__ void __launch_bounds__(256) chunk_cumsum_kernel(
   const int E = (cs + 31) >> 5;  // tokens per lane (<= 8)
   const float a = A[h];
   const float bias = delta_bias ? delta_bias[h] : 0.f;
-  float dv[8], vals[8];
+  float dv[8], vals[8], raw[8];
   float run = 0.f;
+  // all eight loads issued before any is used (indices clamped into the chunk, values masked)
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    raw[e] = Ld<DT>::f(delta_raw + (ci.tok0 + min(lane * E + e, max(ci.vlim - 1, 0))) * (long long)H + h);
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
     const int t = lane * E + e;
-    float v = 0.f;
-    if (e < E && t < ci.vlim)
-      v = dt_transform(Ld<DT>::f(delta_raw + (ci.tok0 + t) * (long long)H + h) + bias, use_sp, dmin, dmax);
+    const float v = (e < E && t < ci.vlim) ? dt_transform(raw[e] + bias, use_sp, dmin, dmax) : 0.f;
     dv[e] = v;
     run += v * a;
     vals[e] = run;
