@@ -332,6 +332,11 @@ size_t carve_bwd(const Geometry& g, uint8_t* base, BwdArgs* a, ChunkEntry** tabl
   w.prev16 = reinterpret_cast<uint16_t*>(take(nk * H * PN * 2));
   w.hg16 = reinterpret_cast<uint16_t*>(take(nk * H * PN * 2));
   w.y16 = reinterpret_cast<uint16_t*>(take((size_t)g.T * H * g.P * 2));
+  if (split_supported(SSD_F32, SSD_F32, g.P, g.N, g.cs)) {  // used when the inputs are fp32
+    const size_t tiles = nk * g.G * (split_operand_bytes_per_chunk_group() / 14) * 4;
+    w.Bs_split = take(tiles);
+    w.Cs_split = take(tiles);
+  }
   ChunkEntry* t = nullptr;
   int2* r = nullptr;
   int* c = nullptr;

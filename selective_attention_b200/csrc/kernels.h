@@ -60,6 +60,9 @@ struct BwdArgs {
   // tensor-core path: 16-bit copies (the inputs' type) of prev and hg (chunks, H, P, N) and,
   // when y_grad is fp32, of y_grad (b, L, H, P)
   uint16_t *prev16, *hg16, *y16;
+  // fp32 inputs at P 64, N 128, cs 256: B and C split into the bf16 hi / lo tiles of the
+  // split-bf16 chunk_state (ssd_split.cu), which recomputes the chunk states and HG
+  void *Bs_split, *Cs_split;
   cudaEvent_t ev[6];
 };
 bool bwd_supported(int P, int N, int cs);
@@ -142,8 +145,10 @@ unsigned int fetch_error_tc(cudaStream_t s);
 bool split_supported(int x_dtype, int y_dtype, int P, int N, int cs);
 size_t split_operand_bytes_per_chunk_group();  // Bs + CBs + Cs
 cudaError_t launch_split_b(const LaunchCtx& c, const float* B, void* Bs);
+// mode 0: chunk states (the forward); mode 1: the backward's intra-chunk state gradient from
+// y_grad (in place of u) and the C tiles (in place of B)
 cudaError_t launch_split_chunk_state(const LaunchCtx& c, const float* u, const void* Bs, const float* dt,
-                                     const float* cum, float* states);
+                                     const float* cum, float* states, int mode = 0);
 cudaError_t launch_split_bmm(const LaunchCtx& c, const float* B, const float* C, void* CBs, void* Cs);
 cudaError_t launch_split_chunk_scan(const LaunchCtx& c, const float* u, const float* dt, const float* cum,
                                     const void* Cs, const float* prev, const void* CBs, const float* D,

@@ -1035,6 +1035,17 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
   const bool tc = bwd_state_grad_tc_supported(a.x_dtype, a.y_dtype, P, N, cs);
   if (tc) {
     if ((e = launch_bwd_chunk_states_tc(c, a))) return e;
+  } else if (a.Bs_split && a.Cs_split && split_supported(a.x_dtype, a.y_dtype, P, N, cs) &&
+             ((reinterpret_cast<uintptr_t>(a.u) | reinterpret_cast<uintptr_t>(a.B) |
+               reinterpret_cast<uintptr_t>(a.C) | reinterpret_cast<uintptr_t>(a.y_grad)) & 15u) == 0) {
+    // fp32 inputs: the chunk states and HG on tcgen05 with split-bf16 products (the forward's
+    // chunk_state kernel; B and C split once per (chunk, group))
+    const float *u32 = static_cast<const float*>(a.u), *B32 = static_cast<const float*>(a.B),
+                *C32 = static_cast<const float*>(a.C), *y32 = static_cast<const float*>(a.y_grad);
+    if ((e = launch_split_b(c, B32, a.Bs_split)) || (e = launch_split_b(c, C32, a.Cs_split)) ||
+        (e = launch_split_chunk_state(c, u32, a.Bs_split, a.dt, a.cum, a.states, 0)) ||
+        (e = launch_split_chunk_state(c, y32, a.Cs_split, a.dt, a.cum, a.hg, 1)))
+      return e;
   } else {
     bwd_chunk_states_kernel<<<dim3((unsigned)H, (unsigned)nk, 2u), 256, kSmemStates, c.stream>>>(
         a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, c.cm, H, G, P, N, a.x_dtype, a.y_dtype);

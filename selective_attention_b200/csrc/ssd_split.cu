@@ -115,13 +115,15 @@ __global__ void __launch_bounds__(kSplitThreads) split_b_kernel(const float* __r
 // the start, step st + 1 once thread 0 has issued step st's MMAs and step st - 1's are done);
 // B operand = the rows u w (N = 64 headdim, MN-major), split by every thread from registers
 // loaded two steps ahead; K = 64 tokens. Warp w reads TMEM lanes 32 (w % 4) (dstate n) and
-// columns 32 (w / 4) (headdim p) and writes states[p][n] (n contiguous).
+// columns 32 (w / 4) (headdim p) and writes states[p][n] (n contiguous). mode 1 is the
+// backward's intra-chunk state gradient HG[p,n] = sum_{l < length} y_grad[l,p] exp(cum_l) C[l,n]
+// (backward_kernel.py:23-93): y_grad rows in place of u, C tiles in place of B, weights exp(cum_l).
 constexpr int kSsStage = kSplitTile + 2 * 8192;  // B tile hi | lo | (u w) hi | (u w) lo
 constexpr size_t kSsSmem = 1024 + 2 * kSsStage;
 
 __global__ void __launch_bounds__(kSplitThreads, 2) split_chunk_state_kernel(
     const float* __restrict__ u, const uint8_t* __restrict__ Bs, const float* __restrict__ dt,
-    const float* __restrict__ cum, float* __restrict__ states, ChunkMap cm, int H, int G) {
+    const float* __restrict__ cum, float* __restrict__ states, ChunkMap cm, int H, int G, int mode) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024_shared(smem_raw);
   __shared__ float sW[256];
@@ -162,7 +164,8 @@ __global__ void __launch_bounds__(kSplitThreads, 2) split_chunk_state_kernel(
   {
     const float clast = cum[kh * 256 + 255];
     const float cl = cum[kh * 256 + tid], dl = dt[kh * 256 + tid];
-    sW[tid] = tid < lim ? expf(fminf(clast - cl, 0.f)) * dl : 0.f;
+    if (mode == 0) sW[tid] = tid < lim ? expf(fminf(clast - cl, 0.f)) * dl : 0.f;
+    else sW[tid] = tid < ci.vlim ? expf(cl) : 0.f;  // backward: y_grad rows past the length ignored
   }
   tc_fence_before();
   __syncthreads();
@@ -633,12 +636,12 @@ cudaError_t launch_split_b(const LaunchCtx& c, const float* B, void* Bs) {
 }
 
 cudaError_t launch_split_chunk_state(const LaunchCtx& c, const float* u, const void* Bs, const float* dt,
-                                     const float* cum, float* states) {
+                                     const float* cum, float* states, int mode) {
   cudaError_t e = cudaFuncSetAttribute(split_chunk_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)kSsSmem);
   if (e != cudaSuccess) return e;
   split_chunk_state_kernel<<<dim3((unsigned)c.H, (unsigned)c.nchunks_max), kSplitThreads, kSsSmem, c.stream>>>(
-      u, static_cast<const uint8_t*>(Bs), dt, cum, states, c.cm, c.H, c.G);
+      u, static_cast<const uint8_t*>(Bs), dt, cum, states, c.cm, c.H, c.G, mode);
   return cudaGetLastError();
 }
 
