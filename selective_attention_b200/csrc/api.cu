@@ -68,7 +68,8 @@ bool use_tc(const ssd_params* p, const Geometry& g) {
 // chunk_scan on tcgen05 with split-bf16 products (ssd_split.cu); SSD_IMPL_SIMT keeps the
 // CUDA-core kernels. u, B, C, D, z and y are accessed with 16-byte loads and stores.
 bool use_split(const ssd_params* p, const Geometry& g) {
-  return p->impl == SSD_IMPL_AUTO && split_supported(p->x_dtype, p->y_dtype, g.P, g.N, g.cs) &&
+  // grids of (.., chunk) with the chunk index in a y / z grid dimension (at most 65535)
+  return p->impl == SSD_IMPL_AUTO && split_supported(p->x_dtype, p->y_dtype, g.P, g.N, g.cs) && g.nchunks <= 65535 &&
          aligned16(p->u) && aligned16(p->B) && aligned16(p->C) && aligned16(p->y) &&
          (!p->D || aligned16(p->D)) && (!p->z || aligned16(p->z));
 }
