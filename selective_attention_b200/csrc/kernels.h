@@ -153,6 +153,11 @@ cudaError_t launch_split_bmm(const LaunchCtx& c, const float* B, const float* C,
 cudaError_t launch_split_chunk_scan(const LaunchCtx& c, const float* u, const float* dt, const float* cum,
                                     const void* Cs, const float* prev, const void* CBs, const float* D,
                                     const float* z, float* y);
+// The backward's state-side products for fp32 inputs (accS, B_grad / C_grad group sums by
+// atomics, gC), as bwd_state_grad_kernel computes them
+cudaError_t launch_split_state_grad(const LaunchCtx& c, const float* u, const float* B, const float* C,
+                                    const float* y_grad, const float* dt, const float* cum, const float* prev,
+                                    const float* hg, float* accS, float* B_grad, float* C_grad, float* gC);
 unsigned int fetch_error_split(cudaStream_t s);
 
 // ssu.cu

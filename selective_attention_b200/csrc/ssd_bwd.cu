@@ -1033,11 +1033,14 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
   const dim3 gkh((unsigned)H, (unsigned)nk);
   // grid x = head: the heads of one chunk run side by side and share its B, C, CB in L2
   const bool tc = bwd_state_grad_tc_supported(a.x_dtype, a.y_dtype, P, N, cs);
+  // fp32 inputs at P 64, N 128, cs 256: the recompute and the state-side products on tcgen05
+  // with split-bf16 products (ssd_split.cu); 16-byte loads of u, B, C and y_grad
+  const bool split32 = !tc && a.Bs_split && a.Cs_split && split_supported(a.x_dtype, a.y_dtype, P, N, cs) &&
+                       ((reinterpret_cast<uintptr_t>(a.u) | reinterpret_cast<uintptr_t>(a.B) |
+                         reinterpret_cast<uintptr_t>(a.C) | reinterpret_cast<uintptr_t>(a.y_grad)) & 15u) == 0;
   if (tc) {
     if ((e = launch_bwd_chunk_states_tc(c, a))) return e;
-  } else if (a.Bs_split && a.Cs_split && split_supported(a.x_dtype, a.y_dtype, P, N, cs) &&
-             ((reinterpret_cast<uintptr_t>(a.u) | reinterpret_cast<uintptr_t>(a.B) |
-               reinterpret_cast<uintptr_t>(a.C) | reinterpret_cast<uintptr_t>(a.y_grad)) & 15u) == 0) {
+  } else if (split32) {
     // fp32 inputs: the chunk states and HG on tcgen05 with split-bf16 products (the forward's
     // chunk_state kernel; B and C split once per (chunk, group))
     const float *u32 = static_cast<const float*>(a.u), *B32 = static_cast<const float*>(a.B),
@@ -1068,6 +1071,11 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
   if (a.ev[2]) cudaEventRecord(a.ev[2], c.stream);
   if (tc) {
     if ((e = launch_bwd_state_grad_grp_tc(c, a))) return e;
+  } else if (split32) {
+    if ((e = launch_split_state_grad(c, static_cast<const float*>(a.u), static_cast<const float*>(a.B),
+                                     static_cast<const float*>(a.C), static_cast<const float*>(a.y_grad), a.dt,
+                                     a.cum, a.states, a.hg, a.accS, a.B_grad, a.C_grad, a.gC)))
+      return e;
   } else {
     bwd_state_grad_kernel<<<gkh, 256, kSmemStateGrad, c.stream>>>(
         a.u, a.B, a.C, a.y_grad, a.dt, a.cum, a.states, a.hg, a.accS, a.B_grad, a.C_grad, a.gC, c.cm, H, G, P, N,
