@@ -337,6 +337,7 @@ size_t carve_bwd(const Geometry& g, uint8_t* base, BwdArgs* a, ChunkEntry** tabl
     const size_t tiles = nk * g.G * (split_operand_bytes_per_chunk_group() / 14) * 4;
     w.Bs_split = take(tiles);
     w.Cs_split = take(tiles);
+    w.accY = take(nk * H * cs * g.P * 4);
   }
   ChunkEntry* t = nullptr;
   int2* r = nullptr;

@@ -63,6 +63,7 @@ struct BwdArgs {
   // fp32 inputs at P 64, N 128, cs 256: B and C split into the bf16 hi / lo tiles of the
   // split-bf16 chunk_state (ssd_split.cu), which recomputes the chunk states and HG
   void *Bs_split, *Cs_split;
+  float* accY;  // (chunks, H, cs, P): the intra-chunk product from split_bwd_accy
   cudaEvent_t ev[6];
 };
 bool bwd_supported(int P, int N, int cs);
@@ -158,6 +159,10 @@ cudaError_t launch_split_chunk_scan(const LaunchCtx& c, const float* u, const fl
 cudaError_t launch_split_state_grad(const LaunchCtx& c, const float* u, const float* B, const float* C,
                                     const float* y_grad, const float* dt, const float* cum, const float* prev,
                                     const float* hg, float* accS, float* B_grad, float* C_grad, float* gC);
+// The backward's intra-chunk product accY for fp32 inputs (from the fp32 CB of bwd_cb), which
+// the CUDA-core intra kernel then takes in place of computing it
+cudaError_t launch_split_bwd_accy(const LaunchCtx& c, const float* CB, const float* y_grad, const float* cum,
+                                  float* accY);
 unsigned int fetch_error_split(cudaStream_t s);
 
 // ssu.cu

@@ -651,7 +651,8 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
     const void* __restrict__ u, const void* __restrict__ yg, const void* __restrict__ delta_raw,
     const float* __restrict__ A, const float* __restrict__ delta_bias, const float* __restrict__ dt,
     const float* __restrict__ cum, const float* __restrict__ CB, const float* __restrict__ accS,
-    const float* __restrict__ gC, const float* __restrict__ dl_part, int nsl, float* __restrict__ CBg,
+    const float* __restrict__ gC, const float* __restrict__ accY_in, const float* __restrict__ dl_part, int nsl,
+    float* __restrict__ CBg,
     void* __restrict__ u_grad, void* __restrict__ draw_grad, float* __restrict__ A_part,
     float* __restrict__ bias_part, ChunkMap cm, int H, int G, int P, int xdt, int ydt, int ddt_dtype, int use_sp,
     float dmin, float dmax) {
@@ -694,13 +695,23 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
   const bool pvalid = p0 < P;
 
   for (int l0 = 0; l0 < ci.lim; l0 += kIR) {
-    // accY: rows l = l0 + tl + 32 i, columns p0 .. p0 + 3
+    // accY: rows l = l0 + tl + 32 i, columns p0 .. p0 + 3 (given, or computed here)
     float aY[2][4];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) aY[i][j] = 0.f;
-    for (int s0 = l0; s0 < vl; s0 += kIB) {
+    if (accY_in && pvalid) {
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int l = l0 + tl + 32 * i;
+        if (l < vl) {
+          const float4 y4 = *reinterpret_cast<const float4*>(accY_in + (kh * cs + l) * P + p0);
+          aY[i][0] = y4.x, aY[i][1] = y4.y, aY[i][2] = y4.z, aY[i][3] = y4.w;
+        }
+      }
+    }
+    for (int s0 = l0; !accY_in && s0 < vl; s0 += kIB) {
       __syncthreads();
       {
         // CB rows s = s0 + c (c < kIB), columns l0 + r4 .. + 3: four 16-byte loads per thread
@@ -1089,8 +1100,11 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
                                               a.dl_part, nsl, a.delta_raw_grad, a.A_part, a.bias_part, c.cm, H,
                                               a.dt_dtype, c.use_sp, c.dmin, c.dmax);
   } else {
+    if (split32 && (e = launch_split_bwd_accy(c, a.CB, static_cast<const float*>(a.y_grad), a.cum, a.accY)))
+      return e;
     bwd_intra_kernel<<<gkh, kIT, kSmemIntra, c.stream>>>(
-        a.u, a.y_grad, a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, a.dl_part, nsl, a.CBg,
+        a.u, a.y_grad, a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, split32 ? a.accY : nullptr,
+        a.dl_part, nsl, a.CBg,
         a.u_grad, a.delta_raw_grad, a.A_part, a.bias_part, c.cm, H, G, P, a.x_dtype, a.y_dtype, a.dt_dtype,
         c.use_sp, c.dmin, c.dmax);
   }

@@ -807,6 +807,135 @@ __global__ void __launch_bounds__(kSplitThreads, 1) split_state_grad_kernel(
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
+// ---------------------------------------------------------------------------- backward accY
+// The backward's intra-chunk product for fp32 inputs (backward_kernel.py:272-293),
+//   accY[l,p] = sum_{l <= s < length} CB[s,l] exp(min(cum_s - cum_l, 0)) y_grad[s,p],
+// per (half m: rows l in [128 m, 128 m + 128), head, chunk), 256 threads; the CUDA-core intra
+// kernel then takes it in place of its own accY. Steps of 64 source tokens s >= 128 m: A = the
+// decay-weighted CB transposed, [l][s], staged MN-major from CB's rows s (l contiguous: two
+// 64-wide l blocks 8 KB apart), B operand = the y_grad rows s (MN-major); both split by every
+// thread from fp32 loads issued one step ahead; two stages alternate.
+constexpr int kAyStage = 2 * 16384 + 2 * 8192;  // A hi | A lo | y hi | y lo
+constexpr size_t kAySmem = 1024 + 2 * kAyStage;
+
+__global__ void __launch_bounds__(kSplitThreads, 2) split_bwd_accy_kernel(
+    const float* __restrict__ CB, const float* __restrict__ yg, const float* __restrict__ cum,
+    float* __restrict__ accY_out, ChunkMap cm, int H, int G) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024_shared(smem_raw);
+  __shared__ float sC[256];
+  __shared__ uint64_t bars[2];
+  __shared__ uint32_t tslot[1];
+  const int m = blockIdx.x, h = blockIdx.y, k = blockIdx.z;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int lim = ci.lim, vl = ci.vlim, l0 = 128 * m;
+  if (l0 >= lim) return;
+  const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long kh = (long long)k * H + h;
+  const float* cbk = CB + ((long long)k * G + g) * 65536;
+  const int s_beg = l0, nsteps = vl > s_beg ? (vl - s_beg + 63) >> 6 : 0;
+  float av[4][8], yv[2][8];
+  // step st: CB rows s = s_beg + 64 st + r (64 rows x 16 chunks of 8 l), y_grad rows s
+  auto load_step = [&](int st) {
+    const int s0 = s_beg + 64 * st;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
+      load8(cbk + (long long)min(s0 + r, 255) * 256 + l0 + 8 * c8, av[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+      load8(yg + ((ci.tok0 + min(s0 + r, lim - 1)) * H + h) * 64 + 8 * c8, yv[i]);
+    }
+  };
+  if (nsteps > 0) load_step(0);
+  if (tid == 0) {
+    mbar_init(smem_u32(&bars[0]), 1);
+    mbar_init(smem_u32(&bars[1]), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 64);
+  sC[tid] = cum[kh * 256 + tid];
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  constexpr uint32_t ID = idesc_f16(128, 64, true, /*a_mn=*/true, /*b_mn=*/true);
+  bool ok = true;
+  int committed = 0;
+  for (int st = 0; st < nsteps; ++st) {
+    const int b = st & 1, s0 = s_beg + 64 * st;
+    uint8_t* aH = sm + b * kAyStage;
+    uint8_t* aL = aH + 16384;
+    uint8_t* xH = aH + 32768;
+    uint8_t* xL = aH + 40960;
+    // this stage was last read by the MMAs of step st - 2
+    ok = __syncthreads_and(ok && wait_commit(smem_u32(&bars[b]), st >> 1, kSiteSplitState)) != 0;
+    if (!ok) break;
+    tc_fence_after();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15, s = s0 + r;
+      const float cs_ = sC[min(s, 255)];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int l = l0 + 8 * c8 + e;
+        av[i][e] = (s >= l && s < vl && l < vl) ? av[i][e] * expf(fminf(cs_ - sC[l], 0.f)) : 0.f;
+      }
+      store_split8(aH, aL, (uint32_t)(c8 >> 3) * 8192u + sw128_off((uint32_t)r, (uint32_t)(c8 & 7)), av[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+      if (s0 + r >= vl) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) yv[i][e] = 0.f;
+      }
+      store_split8(xH, xL, sw128_off((uint32_t)r, (uint32_t)c8), yv[i]);
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t ah = smem_u32(aH), al = smem_u32(aL), xh = smem_u32(xH), xl = smem_u32(xL);
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        mma3(tmem, sdesc_sw128(ah + ks * 2048, 8192, 1024), sdesc_sw128(al + ks * 2048, 8192, 1024),
+             sdesc_sw128(xh + ks * 2048, 16, 1024), sdesc_sw128(xl + ks * 2048, 16, 1024), ID,
+             (st > 0 || ks > 0) ? 1u : 0u);
+      umma_commit(smem_u32(&bars[b]));
+    }
+    ++committed;
+    if (st + 1 < nsteps) load_step(st + 1);
+  }
+  // step (committed - 1)'s commit completes after every earlier MMA of the CTA
+  const bool done = committed == 0 ||
+                    wait_commit(smem_u32(&bars[(committed - 1) & 1]), ((committed - 1) >> 1) + 1, kSiteSplitState);
+  tc_fence_after();
+  if (__syncthreads_and(ok && done)) {
+    const int r = (warp & 3) * 32 + lane, c0 = 32 * (warp >> 2);
+    float4* o = reinterpret_cast<float4*>(accY_out + (kh * 256 + l0 + r) * 64 + c0);
+    if (committed == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)c0, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        o[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]), __uint_as_float(v[4 * j + 2]),
+                           __uint_as_float(v[4 * j + 3]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 64);
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -863,6 +992,16 @@ cudaError_t launch_split_state_grad(const LaunchCtx& c, const float* u, const fl
   if (e != cudaSuccess) return e;
   split_state_grad_kernel<<<dim3(2u, (unsigned)c.H, (unsigned)c.nchunks_max), kSplitThreads, kSgSmem, c.stream>>>(
       u, B, C, y_grad, dt, cum, prev, hg, accS, B_grad, C_grad, gC, c.cm, c.H, c.G);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_bwd_accy(const LaunchCtx& c, const float* CB, const float* y_grad, const float* cum,
+                                  float* accY) {
+  cudaError_t e = cudaFuncSetAttribute(split_bwd_accy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)kAySmem);
+  if (e != cudaSuccess) return e;
+  split_bwd_accy_kernel<<<dim3(2u, (unsigned)c.H, (unsigned)c.nchunks_max), kSplitThreads, kAySmem, c.stream>>>(
+      CB, y_grad, cum, accY, c.cm, c.H, c.G);
   return cudaGetLastError();
 }
 
