@@ -881,8 +881,8 @@ def ref_gpu_measure(args, dev, flush):
     package ``baseline/install_reference.sh`` installs into ``baseline/_ref``; ``ops/ssd_scan.py``
     over ``triton_kernels/ssd_scan``) at config 1's shape in fp32, its operand type, forward
     and forward + backward, beside this library's ``SSDScanFn`` on the same fp32 inputs (the
-    split-bf16 tensor-core forward, and the CUDA-core chain with ``impl="simt"``; the fp32
-    backward runs on CUDA cores in both) and on bf16 inputs (tensor cores). No D / z (the
+    split-bf16 tensor-core forward, and the CUDA-core forward with ``impl="simt"``; the backward
+    is the same in both: split-bf16 tcgen05 stages and CUDA-core stages for fp32) and on bf16 inputs (tensor cores). No D / z (the
     reference op has none).
     The reference runs its stock code path; Triton compiles and autotunes it on first use,
     outside the timed steps."""
