@@ -630,21 +630,28 @@ __global__ void __launch_bounds__(kScThreads, 2) split_chunk_scan_kernel(
 //   C_grad[l,:]  += e_l sum_p y_grad[l,p] prev[p,:]    A = y_grad rows, prev MN-major
 //   gC[l]         = sum_n (that C_grad row) C[l,n]
 // hg and prev hold [p][n] rows: one split tile [n block][64 p][64 n] serves as the K-major
-// operand of accS and as the MN-major one of B_grad / C_grad. Every operand is split once into
-// shared memory, the MMAs (split-bf16, three per K step) run at once into TMEM columns
-// accS [0, 64), B_grad [64, 192), C_grad [192, 320), and thread = TMEM lane = row scales the
-// rows; B_grad / C_grad rows are summed over the group's heads by 16-byte atomics in L2, as the
-// CUDA-core kernel does.
-constexpr size_t kSgSmem = 1024 + 6 * 32768;  // B rows 64 KB | u rows 32 | y rows 32 | hg 32 | prev 32
+// operand of accS and as the MN-major one of B_grad / C_grad. A CTA splits its operands into
+// shared memory, runs its product's MMAs (split-bf16, three per K step) into TMEM, and thread =
+// TMEM lane = row scales the rows; B_grad / C_grad rows are summed over the group's heads by
+// 16-byte atomics in L2, as the CUDA-core kernel does.
+// One launch per product (MODE 0: accS, 1: B_grad, 2: C_grad and gC), so that each CTA holds
+// only its own operands and several CTAs share an SM.
+template <int MODE>
+struct SgCfg {
+  static constexpr size_t kSmem = 1024 + (MODE == 0 ? 3 : 2) * 32768;  // A rows (64 or 32 KB) | hg or prev 32 KB
+  static constexpr uint32_t kCols = MODE == 0 ? 64 : 128;
+  static constexpr int kMinBlocks = MODE == 0 ? 2 : 3;
+};
 
-__global__ void __launch_bounds__(kSplitThreads, 1) split_state_grad_kernel(
+template <int MODE>
+__global__ void __launch_bounds__(kSplitThreads, SgCfg<MODE>::kMinBlocks) split_state_grad_kernel(
     const float* __restrict__ u, const float* __restrict__ Bm, const float* __restrict__ Cm,
     const float* __restrict__ yg, const float* __restrict__ dt, const float* __restrict__ cum,
     const float* __restrict__ prev, const float* __restrict__ hg, float* __restrict__ accS_out,
     float* __restrict__ Bgrad, float* __restrict__ Cgrad, float* __restrict__ gC_out, ChunkMap cm, int H, int G) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = align1024_shared(smem_raw);
-  __shared__ float sS[128], sWt[128], sE[128], sG[128];
+  __shared__ float sF[128], sG[128];  // the row factor (s_l, w_l or e_l) | gC partial sums
   __shared__ uint64_t bars[1];
   __shared__ uint32_t tslot[1];
   const int m = blockIdx.x, h = blockIdx.y, k = blockIdx.z;
@@ -654,69 +661,42 @@ __global__ void __launch_bounds__(kSplitThreads, 1) split_state_grad_kernel(
   if (l0 >= lim) return;
   const int g = h / (H / G), tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long kh = (long long)k * H + h;
-  uint8_t* aH = sm;            // B rows: [n block (2)][128 rows][128 B], hi then lo (64 KB)
-  uint8_t* aL = sm + 32768;
-  uint8_t* uH = sm + 65536;    // u rows [128][64 p], hi then lo
-  uint8_t* uL = sm + 81920;
-  uint8_t* yH = sm + 98304;    // y_grad rows
-  uint8_t* yL = sm + 114688;
-  uint8_t* hH = sm + 131072;   // hg [n block (2)][64 p][64 n], hi then lo
-  uint8_t* hL = sm + 147456;
-  uint8_t* pH = sm + 163840;   // prev, same layout
-  uint8_t* pL = sm + 180224;
+  constexpr uint32_t AB = MODE == 0 ? 65536u : 32768u;  // bytes of the A rows (hi then lo)
+  uint8_t* aH = sm;  // MODE 0: B rows [n block (2)][128 rows][128 B]; else u / y_grad rows [128][64 p]
+  uint8_t* aL = sm + AB / 2;
+  uint8_t* hH = sm + AB;  // hg (MODE 0, 1) or prev (MODE 2): [n block (2)][64 p][64 n], hi then lo
+  uint8_t* hL = sm + AB + 16384;
   const uint32_t bar = smem_u32(&bars[0]);
   if (tid == 0) {
     mbar_init(bar, 1);
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(smem_u32(tslot), 512);
+  if (warp == 0) tmem_alloc(smem_u32(tslot), SgCfg<MODE>::kCols);
   if (tid < 128) {
     const int l = l0 + tid;
     const float clast = cum[kh * 256 + 255], cl = cum[kh * 256 + l];
-    const float s = l < vl ? expf(fminf(clast - cl, 0.f)) : 0.f;
-    sS[tid] = s;
-    sWt[tid] = s * dt[kh * 256 + l];
-    sE[tid] = l < vl ? expf(cl) : 0.f;
+    const float s_l = l < vl ? expf(fminf(clast - cl, 0.f)) : 0.f;
+    sF[tid] = MODE == 0 ? s_l : (MODE == 1 ? s_l * dt[kh * 256 + l] : (l < vl ? expf(cl) : 0.f));
     sG[tid] = 0.f;
   }
   // operands, split; each batch's four loads issued before its stores
   float v[4][8];
-  const float* hgk = hg + kh * 8192;
-  const float* pvk = prev + kh * 8192;
+  if (MODE == 0) {
 #pragma unroll 1
-  for (int bt = 0; bt < 2; ++bt) {  // B rows: 128 x 16 chunks of 8 states
+    for (int bt = 0; bt < 2; ++bt) {  // B rows: 128 x 16 chunks of 8 states
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int q = tid + kSplitThreads * (4 * bt + i), r = q >> 4, c8 = q & 15;
-      load8(Bm + ((ci.tok0 + min(l0 + r, lim - 1)) * G + g) * 128 + 8 * c8, v[i]);
-    }
+      for (int i = 0; i < 4; ++i) {
+        const int q = tid + kSplitThreads * (4 * bt + i), r = q >> 4, c8 = q & 15;
+        load8(Bm + ((ci.tok0 + min(l0 + r, lim - 1)) * G + g) * 128 + 8 * c8, v[i]);
+      }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int q = tid + kSplitThreads * (4 * bt + i), r = q >> 4, c8 = q & 15;
-      store_split8(aH, aL, (uint32_t)(c8 >> 3) * 16384u + sw128_off((uint32_t)r, (uint32_t)(c8 & 7)), v[i]);
+      for (int i = 0; i < 4; ++i) {
+        const int q = tid + kSplitThreads * (4 * bt + i), r = q >> 4, c8 = q & 15;
+        store_split8(aH, aL, (uint32_t)(c8 >> 3) * 16384u + sw128_off((uint32_t)r, (uint32_t)(c8 & 7)), v[i]);
+      }
     }
-  }
-#pragma unroll 1
-  for (int which = 0; which < 2; ++which) {  // hg, prev: 64 p x 16 chunks of 8 states
-    const float* src = which ? pvk : hgk;
-    uint8_t* dh = which ? pH : hH;
-    uint8_t* dl = which ? pL : hL;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
-      load8(src + r * 128 + 8 * c8, v[i]);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
-      store_split8(dh, dl, (uint32_t)(c8 >> 3) * 8192u + sw128_off((uint32_t)r, (uint32_t)(c8 & 7)), v[i]);
-    }
-  }
-#pragma unroll 1
-  for (int which = 0; which < 2; ++which) {  // u, y_grad rows: 128 x 8 chunks of 8 headdim columns
-    const float* src = which ? yg : u;
-    uint8_t* dh = which ? yH : uH;
-    uint8_t* dl = which ? yL : uL;
+  } else {
+    const float* src = MODE == 1 ? u : yg;  // 128 rows x 8 chunks of 8 headdim columns
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
@@ -725,7 +705,20 @@ __global__ void __launch_bounds__(kSplitThreads, 1) split_state_grad_kernel(
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
-      store_split8(dh, dl, sw128_off((uint32_t)r, (uint32_t)c8), v[i]);
+      store_split8(aH, aL, sw128_off((uint32_t)r, (uint32_t)c8), v[i]);
+    }
+  }
+  {
+    const float* src = (MODE == 2 ? prev : hg) + kh * 8192;  // 64 p x 16 chunks of 8 states
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
+      load8(src + r * 128 + 8 * c8, v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 4, c8 = q & 15;
+      store_split8(hH, hL, (uint32_t)(c8 >> 3) * 8192u + sw128_off((uint32_t)r, (uint32_t)(c8 & 7)), v[i]);
     }
   }
   fence_proxy_async_smem();
@@ -734,26 +727,23 @@ __global__ void __launch_bounds__(kSplitThreads, 1) split_state_grad_kernel(
   tc_fence_after();
   const uint32_t tmem = *tslot;
   if (tid == 0) {
-    constexpr uint32_t ID_S = idesc_f16(128, 64, true, false, false);
-    constexpr uint32_t ID_G = idesc_f16(128, 128, true, false, /*b_mn=*/true);
-    const uint32_t ah = smem_u32(aH), al = smem_u32(aL), uh = smem_u32(uH), ul = smem_u32(uL);
-    const uint32_t yh = smem_u32(yH), yl = smem_u32(yL), hh = smem_u32(hH), hl = smem_u32(hL);
-    const uint32_t ph = smem_u32(pH), pl = smem_u32(pL);
+    const uint32_t ah = smem_u32(aH), al = smem_u32(aL), hh = smem_u32(hH), hl = smem_u32(hL);
+    if (MODE == 0) {
+      constexpr uint32_t ID_S = idesc_f16(128, 64, true, false, false);
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {  // accS: K = 128 states in two blocks
-      const uint32_t ka = (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u;
-      const uint32_t kb = (uint32_t)(ks >> 2) * 8192u + (uint32_t)(ks & 3) * 32u;
-      mma3(tmem, sdesc_sw128(ah + ka, 16, 1024), sdesc_sw128(al + ka, 16, 1024), sdesc_sw128(hh + kb, 16, 1024),
-           sdesc_sw128(hl + kb, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
-    }
+      for (int ks = 0; ks < 8; ++ks) {  // K = 128 states in two blocks
+        const uint32_t ka = (uint32_t)(ks >> 2) * 16384u + (uint32_t)(ks & 3) * 32u;
+        const uint32_t kb = (uint32_t)(ks >> 2) * 8192u + (uint32_t)(ks & 3) * 32u;
+        mma3(tmem, sdesc_sw128(ah + ka, 16, 1024), sdesc_sw128(al + ka, 16, 1024), sdesc_sw128(hh + kb, 16, 1024),
+             sdesc_sw128(hl + kb, 16, 1024), ID_S, ks > 0 ? 1u : 0u);
+      }
+    } else {
+      constexpr uint32_t ID_G = idesc_f16(128, 128, true, false, /*b_mn=*/true);
 #pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {  // B_grad, C_grad: K = 64 headdim, N = 128 states
-      mma3(tmem + 64, sdesc_sw128(uh + ks * 32, 16, 1024), sdesc_sw128(ul + ks * 32, 16, 1024),
-           sdesc_sw128(hh + ks * 2048, 8192, 1024), sdesc_sw128(hl + ks * 2048, 8192, 1024), ID_G,
-           ks > 0 ? 1u : 0u);
-      mma3(tmem + 192, sdesc_sw128(yh + ks * 32, 16, 1024), sdesc_sw128(yl + ks * 32, 16, 1024),
-           sdesc_sw128(ph + ks * 2048, 8192, 1024), sdesc_sw128(pl + ks * 2048, 8192, 1024), ID_G,
-           ks > 0 ? 1u : 0u);
+      for (int ks = 0; ks < 4; ++ks)  // K = 64 headdim, N = 128 states
+        mma3(tmem, sdesc_sw128(ah + ks * 32, 16, 1024), sdesc_sw128(al + ks * 32, 16, 1024),
+             sdesc_sw128(hh + ks * 2048, 8192, 1024), sdesc_sw128(hl + ks * 2048, 8192, 1024), ID_G,
+             ks > 0 ? 1u : 0u);
     }
     umma_commit(bar);
   }
@@ -762,49 +752,45 @@ __global__ void __launch_bounds__(kSplitThreads, 1) split_state_grad_kernel(
   if (__syncthreads_and(done)) {
     const int r = (warp & 3) * 32 + lane, hc = warp >> 2, l = l0 + r;
     const uint32_t tl = (uint32_t)((warp & 3) * 32) << 16;
-    const bool valid = l < vl;
-    {
+    const float f = sF[r];
+    if (MODE == 0) {
       uint32_t a[32];
       tmem_ld32(tmem + tl + (uint32_t)(32 * hc), a);
       tmem_wait_ld();
-      const float s = sS[r];
       float4* o = reinterpret_cast<float4*>(accS_out + (kh * 256 + l) * 64 + 32 * hc);
 #pragma unroll
       for (int j = 0; j < 8; ++j)
-        o[j] = make_float4(s * __uint_as_float(a[4 * j]), s * __uint_as_float(a[4 * j + 1]),
-                           s * __uint_as_float(a[4 * j + 2]), s * __uint_as_float(a[4 * j + 3]));
-    }
-    const long long row = ((ci.tok0 + l) * G + g) * 128 + 64 * hc;
-    float gsum = 0.f;
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      const float f = which ? sE[r] : sWt[r];
-      float* dst = which ? Cgrad : Bgrad;
+        o[j] = make_float4(f * __uint_as_float(a[4 * j]), f * __uint_as_float(a[4 * j + 1]),
+                           f * __uint_as_float(a[4 * j + 2]), f * __uint_as_float(a[4 * j + 3]));
+    } else {
+      const long long row = ((ci.tok0 + l) * G + g) * 128 + 64 * hc;
+      float* dst = MODE == 1 ? Bgrad : Cgrad;
+      float gsum = 0.f;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t a[32];
-        tmem_ld32(tmem + tl + (uint32_t)(64 + 128 * which + 64 * hc + 32 * half), a);
+        tmem_ld32(tmem + tl + (uint32_t)(64 * hc + 32 * half), a);
         tmem_wait_ld();
-        if (valid) {
+        if (l < vl) {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float4 q = make_float4(f * __uint_as_float(a[4 * j]), f * __uint_as_float(a[4 * j + 1]),
                                          f * __uint_as_float(a[4 * j + 2]), f * __uint_as_float(a[4 * j + 3]));
             atomicAdd(reinterpret_cast<float4*>(dst + row + 32 * half + 4 * j), q);
-            if (which) {
+            if (MODE == 2) {
               const float4 c = __ldg(reinterpret_cast<const float4*>(Cm + row + 32 * half + 4 * j));
               gsum = fmaf(q.x, c.x, fmaf(q.y, c.y, fmaf(q.z, c.z, fmaf(q.w, c.w, gsum))));
             }
           }
         }
       }
+      if (MODE == 2) atomicAdd(&sG[r], gsum);
     }
-    atomicAdd(&sG[r], gsum);
   }
   tc_fence_before();
   __syncthreads();
-  if (tid < 128) gC_out[kh * 256 + l0 + tid] = l0 + tid < vl ? sG[tid] : 0.f;
-  if (warp == 0) tmem_dealloc(tmem, 512);
+  if (MODE == 2 && tid < 128) gC_out[kh * 256 + l0 + tid] = l0 + tid < vl ? sG[tid] : 0.f;
+  if (warp == 0) tmem_dealloc(tmem, SgCfg<MODE>::kCols);
 }
 
 // ---------------------------------------------------------------------------- backward accY
@@ -984,15 +970,26 @@ cudaError_t launch_split_chunk_scan(const LaunchCtx& c, const float* u, const fl
 
 size_t split_operand_bytes_per_chunk_group() { return (size_t)(6 + 4 + 4) * kSplitTile; }
 
+template <int MODE>
+static cudaError_t split_state_grad_mode(const LaunchCtx& c, const float* u, const float* B, const float* C,
+                                        const float* y_grad, const float* dt, const float* cum, const float* prev,
+                                        const float* hg, float* accS, float* B_grad, float* C_grad, float* gC) {
+  auto kern = split_state_grad_kernel<MODE>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SgCfg<MODE>::kSmem);
+  if (e != cudaSuccess) return e;
+  kern<<<dim3(2u, (unsigned)c.H, (unsigned)c.nchunks_max), kSplitThreads, SgCfg<MODE>::kSmem, c.stream>>>(
+      u, B, C, y_grad, dt, cum, prev, hg, accS, B_grad, C_grad, gC, c.cm, c.H, c.G);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_split_state_grad(const LaunchCtx& c, const float* u, const float* B, const float* C,
                                     const float* y_grad, const float* dt, const float* cum, const float* prev,
                                     const float* hg, float* accS, float* B_grad, float* C_grad, float* gC) {
-  cudaError_t e = cudaFuncSetAttribute(split_state_grad_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kSgSmem);
-  if (e != cudaSuccess) return e;
-  split_state_grad_kernel<<<dim3(2u, (unsigned)c.H, (unsigned)c.nchunks_max), kSplitThreads, kSgSmem, c.stream>>>(
-      u, B, C, y_grad, dt, cum, prev, hg, accS, B_grad, C_grad, gC, c.cm, c.H, c.G);
-  return cudaGetLastError();
+  cudaError_t e;
+  if ((e = split_state_grad_mode<0>(c, u, B, C, y_grad, dt, cum, prev, hg, accS, B_grad, C_grad, gC)) ||
+      (e = split_state_grad_mode<1>(c, u, B, C, y_grad, dt, cum, prev, hg, accS, B_grad, C_grad, gC)))
+    return e;
+  return split_state_grad_mode<2>(c, u, B, C, y_grad, dt, cum, prev, hg, accS, B_grad, C_grad, gC);
 }
 
 cudaError_t launch_split_bwd_accy(const LaunchCtx& c, const float* CB, const float* y_grad, const float* cum,
