@@ -233,6 +233,8 @@ typedef struct ssd_bwd_params {
   float* h_init_grad;
 } ssd_bwd_params;
 
+/* Bytes of device workspace ssd_scan_bwd needs for p's geometry and x_dtype (fp32 inputs at
+ * headdim 64, dstate 128, chunk 256 add the buffers of the tensor-core fp32 path). */
 size_t ssd_scan_bwd_workspace_size(const ssd_params* p);
 int ssd_scan_bwd(const ssd_params* p, const ssd_bwd_params* g, void* stream);
 

@@ -308,7 +308,10 @@ int ssd_scan_fwd(const ssd_params* p, void* stream) {
 // ------------------------------------------------------------- backward
 namespace {
 
-size_t carve_bwd(const Geometry& g, uint8_t* base, BwdArgs* a, ChunkEntry** table, int2** rows, int** count) {
+// x32: fp32 u / B / C, whose backward (at the split path's shape) also needs the split operand
+// tiles, accY and G = y_grad u^T
+size_t carve_bwd(const Geometry& g, bool x32, uint8_t* base, BwdArgs* a, ChunkEntry** table, int2** rows,
+                 int** count) {
   size_t off = 0;
   auto take = [&](size_t n) {
     uint8_t* ptr = base ? base + off : nullptr;
@@ -333,11 +336,12 @@ size_t carve_bwd(const Geometry& g, uint8_t* base, BwdArgs* a, ChunkEntry** tabl
   w.prev16 = reinterpret_cast<uint16_t*>(take(nk * H * PN * 2));
   w.hg16 = reinterpret_cast<uint16_t*>(take(nk * H * PN * 2));
   w.y16 = reinterpret_cast<uint16_t*>(take((size_t)g.T * H * g.P * 2));
-  if (split_supported(SSD_F32, SSD_F32, g.P, g.N, g.cs)) {  // used when the inputs are fp32
+  if (x32 && split_supported(SSD_F32, SSD_F32, g.P, g.N, g.cs)) {
     const size_t tiles = nk * g.G * (split_operand_bytes_per_chunk_group() / 14) * 4;
     w.Bs_split = take(tiles);
     w.Cs_split = take(tiles);
     w.accY = take(nk * H * cs * g.P * 4);
+    w.Gyu = take(nk * H * cs * cs * 4);
   }
   ChunkEntry* t = nullptr;
   int2* r = nullptr;
@@ -358,7 +362,7 @@ size_t carve_bwd(const Geometry& g, uint8_t* base, BwdArgs* a, ChunkEntry** tabl
 extern "C" size_t ssd_scan_bwd_workspace_size(const ssd_params* p) {
   Geometry g;
   if (geometry(p, g) != SSD_OK || !bwd_supported(g.P, g.N, g.cs)) return 0;
-  return carve_bwd(g, nullptr, nullptr, nullptr, nullptr, nullptr);
+  return carve_bwd(g, p->x_dtype == SSD_F32, nullptr, nullptr, nullptr, nullptr, nullptr);
 }
 
 extern "C" int ssd_scan_bwd(const ssd_params* p, const ssd_bwd_params* gr, void* stream) {
@@ -381,7 +385,7 @@ extern "C" int ssd_scan_bwd(const ssd_params* p, const ssd_bwd_params* gr, void*
   ChunkEntry* table;
   int2* rows;
   int* count;
-  const size_t need = carve_bwd(g, reinterpret_cast<uint8_t*>(p->workspace), &a, &table, &rows, &count);
+  const size_t need = carve_bwd(g, p->x_dtype == SSD_F32, reinterpret_cast<uint8_t*>(p->workspace), &a, &table, &rows, &count);
   if (p->workspace_bytes < need) return SSD_ERR_WORKSPACE_TOO_SMALL;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   Workspace w{};

@@ -64,6 +64,7 @@ struct BwdArgs {
   // split-bf16 chunk_state (ssd_split.cu), which recomputes the chunk states and HG
   void *Bs_split, *Cs_split;
   float* accY;  // (chunks, H, cs, P): the intra-chunk product from split_bwd_accy
+  float* Gyu;   // (chunks, H, cs, cs): y_grad u^T from split_bwd_g (lower blocks)
   cudaEvent_t ev[6];
 };
 bool bwd_supported(int P, int N, int cs);
@@ -159,10 +160,13 @@ cudaError_t launch_split_chunk_scan(const LaunchCtx& c, const float* u, const fl
 cudaError_t launch_split_state_grad(const LaunchCtx& c, const float* u, const float* B, const float* C,
                                     const float* y_grad, const float* dt, const float* cum, const float* prev,
                                     const float* hg, float* accS, float* B_grad, float* C_grad, float* gC);
-// The backward's intra-chunk product accY for fp32 inputs (from the fp32 CB of bwd_cb), which
-// the CUDA-core intra kernel then takes in place of computing it
+// The backward's intra-chunk product accY for fp32 inputs (from the fp32 CB of bwd_cb), for
+// bwd_intra_split
 cudaError_t launch_split_bwd_accy(const LaunchCtx& c, const float* CB, const float* y_grad, const float* cum,
                                   float* accY);
+// G = y_grad u^T per (chunk, head) for fp32 inputs, the lower 128 x 128 blocks, as fp32 rows
+// [chunk][head][256][256] for bwd_intra_split
+cudaError_t launch_split_bwd_g(const LaunchCtx& c, const float* u, const float* y_grad, float* G);
 unsigned int fetch_error_split(cudaStream_t s);
 
 // ssu.cu

@@ -651,7 +651,7 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
     const void* __restrict__ u, const void* __restrict__ yg, const void* __restrict__ delta_raw,
     const float* __restrict__ A, const float* __restrict__ delta_bias, const float* __restrict__ dt,
     const float* __restrict__ cum, const float* __restrict__ CB, const float* __restrict__ accS,
-    const float* __restrict__ gC, const float* __restrict__ accY_in, const float* __restrict__ dl_part, int nsl,
+    const float* __restrict__ gC, const float* __restrict__ dl_part, int nsl,
     float* __restrict__ CBg,
     void* __restrict__ u_grad, void* __restrict__ draw_grad, float* __restrict__ A_part,
     float* __restrict__ bias_part, ChunkMap cm, int H, int G, int P, int xdt, int ydt, int ddt_dtype, int use_sp,
@@ -695,23 +695,13 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
   const bool pvalid = p0 < P;
 
   for (int l0 = 0; l0 < ci.lim; l0 += kIR) {
-    // accY: rows l = l0 + tl + 32 i, columns p0 .. p0 + 3 (given, or computed here)
+    // accY: rows l = l0 + tl + 32 i, columns p0 .. p0 + 3
     float aY[2][4];
 #pragma unroll
     for (int i = 0; i < 2; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) aY[i][j] = 0.f;
-    if (accY_in && pvalid) {
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int l = l0 + tl + 32 * i;
-        if (l < vl) {
-          const float4 y4 = *reinterpret_cast<const float4*>(accY_in + (kh * cs + l) * P + p0);
-          aY[i][0] = y4.x, aY[i][1] = y4.y, aY[i][2] = y4.z, aY[i][3] = y4.w;
-        }
-      }
-    }
-    for (int s0 = l0; !accY_in && s0 < vl; s0 += kIB) {
+    for (int s0 = l0; s0 < vl; s0 += kIB) {
       __syncthreads();
       {
         // CB rows s = s0 + c (c < kIB), columns l0 + r4 .. + 3: four 16-byte loads per thread
@@ -860,6 +850,103 @@ __global__ void __launch_bounds__(kIT, 1) bwd_intra_kernel(
 
   // dt backward, one token per thread
   dt_backward<kIT>(cols, rows, gBs, ddts, revc, tmp, gC, dl_part, nsl, delta_raw, A, delta_bias, draw_grad, A_part,
+                   bias_part, ci, kh, h, H, cs, vl, ddt_dtype, use_sp, dmin, dmax);
+}
+
+// bwd_intra_split: the intra-chunk step for fp32 inputs at headdim 64, chunk 256, after the
+// tensor-core products (ssd_split.cu): accY (split_bwd_accy) and G = y_grad u^T
+// (split_bwd_g, lower 128 x 128 blocks) arrive in global memory, so this kernel keeps no
+// operand rows in shared memory and runs several CTAs per SM. Per (head, chunk), 256 threads,
+// 16 per row (4 headdim columns / 4 source tokens each):
+//   acc = accS + accY: u_grad = acc dt_l, ddt[l] = sum_p acc u, gB[l] = dt_l sum_p accS u
+//   CB_grad[l,s] += G[l,s] dt_s exp(min(cum_l - cum_s, 0))  (s <= l < length), 16-byte L2 atomics
+//   w = that term * CB[l,s] (s < l): rows[l] = sum_s w, cols[s] = sum_l w
+// then the dt backward (backward_kernel.py:296-314, :417-421, :632-659, :847-895).
+__global__ void __launch_bounds__(256) bwd_intra_split_kernel(
+    const float* __restrict__ u, const void* __restrict__ delta_raw, const float* __restrict__ A,
+    const float* __restrict__ delta_bias, const float* __restrict__ dt, const float* __restrict__ cum,
+    const float* __restrict__ CB, const float* __restrict__ accS, const float* __restrict__ gC,
+    const float* __restrict__ accY, const float* __restrict__ Gyu, const float* __restrict__ dl_part, int nsl,
+    float* __restrict__ CBg, float* __restrict__ u_grad, void* __restrict__ draw_grad, float* __restrict__ A_part,
+    float* __restrict__ bias_part, ChunkMap cm, int H, int G, int ddt_dtype, int use_sp, float dmin, float dmax) {
+  constexpr int cs = 256, P = 64;
+  __shared__ float dts[cs], cms[cs], rows[cs], cols[cs], ddts[cs], gBs[cs], revc[cs], tmp[16];
+  const int h = blockIdx.x, k = blockIdx.y, tid = threadIdx.x;
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) {
+    if (tid == 0) {
+      A_part[(long long)k * H + h] = 0.f;
+      bias_part[(long long)k * H + h] = 0.f;
+    }
+    return;
+  }
+  const int g = h / (H / G), vl = ci.vlim, lim = ci.lim;
+  const long long kh = (long long)k * H + h;
+  const long long kg = ((long long)k * G + g) * cs * cs;
+  dts[tid] = dt[kh * cs + tid];
+  cms[tid] = cum[kh * cs + tid];
+  cols[tid] = 0.f;
+  __syncthreads();
+  const int grp = tid >> 4, tq = tid & 15;
+  // per-row products: rows l = grp + 16 m, columns 4 tq .. 4 tq + 3
+#pragma unroll 4
+  for (int m = 0; m < 16; ++m) {
+    const int l = grp + 16 * m;
+    float dpart = 0.f, bpart = 0.f;
+    if (l < vl) {
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(accS + (kh * cs + l) * P) + tq);
+      const float4 y4 = __ldg(reinterpret_cast<const float4*>(accY + (kh * cs + l) * P) + tq);
+      const float4 u4 = __ldg(reinterpret_cast<const float4*>(u + ((ci.tok0 + l) * H + h) * P) + tq);
+      const float4 acc = make_float4(s4.x + y4.x, s4.y + y4.y, s4.z + y4.z, s4.w + y4.w);
+      dpart = dot4(acc, u4, 0.f);
+      bpart = dot4(s4, u4, 0.f);
+      const float d = dts[l];
+      reinterpret_cast<float4*>(u_grad + ((ci.tok0 + l) * H + h) * P)[tq] =
+          make_float4(acc.x * d, acc.y * d, acc.z * d, acc.w * d);
+    } else if (l < lim) {
+      reinterpret_cast<float4*>(u_grad + ((ci.tok0 + l) * H + h) * P)[tq] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    dpart = half_warp_sum(dpart);
+    bpart = half_warp_sum(bpart);
+    if (tq == 0) {
+      ddts[l] = dpart;
+      gBs[l] = bpart * dts[l];
+    }
+  }
+  // CB_grad and the decay sums: rows l = grp + 16 m, source tokens s0 + 4 tq .. + 3 in
+  // 64-token steps; a warp's two rows step to the larger row so that the sums stay uniform.
+#pragma unroll 1
+  for (int m = 0; m < 16; ++m) {
+    const int l = grp + 16 * m, lw = ((tid >> 5) << 1) + 1 + 16 * m;
+    const float cl = cms[l];
+    const float* gr = Gyu + (kh * cs + l) * cs;
+    const float* cbr = CB + kg + (long long)l * cs;
+    float* cgr = CBg + kg + (long long)l * cs;
+    float rsum = 0.f;
+    for (int s0 = 0; s0 <= min(lw, vl - 1); s0 += 64) {
+      const int s = s0 + 4 * tq;
+      if (l < vl && s <= l) {
+        const float4 gv = __ldg(reinterpret_cast<const float4*>(gr + s));
+        const float4 cb = __ldg(reinterpret_cast<const float4*>(cbr + s));
+        float c[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int se = s + e;
+          c[e] = se <= l ? comp(gv, e) * dts[se] * expf(fminf(cl - cms[se], 0.f)) : 0.f;
+          if (se < l) {
+            const float w = c[e] * comp(cb, e);
+            rsum += w;
+            atomicAdd(&cols[se], w);
+          }
+        }
+        atomicAdd(reinterpret_cast<float4*>(cgr + s), make_float4(c[0], c[1], c[2], c[3]));
+      }
+    }
+    rsum = half_warp_sum(rsum);
+    if (tq == 0) rows[l] = rsum;
+  }
+  __syncthreads();
+  dt_backward<256>(cols, rows, gBs, ddts, revc, tmp, gC, dl_part, nsl, delta_raw, A, delta_bias, draw_grad, A_part,
                    bias_part, ci, kh, h, H, cs, vl, ddt_dtype, use_sp, dmin, dmax);
 }
 
@@ -1099,12 +1186,18 @@ cudaError_t launch_ssd_bwd(const LaunchCtx& c, const BwdArgs& a) {
     bwd_dt_kernel<<<gkh, 256, 0, c.stream>>>(a.rows4, (long long)nk * H * cs, a.delta_raw, a.A, a.delta_bias, a.gC,
                                               a.dl_part, nsl, a.delta_raw_grad, a.A_part, a.bias_part, c.cm, H,
                                               a.dt_dtype, c.use_sp, c.dmin, c.dmax);
-  } else {
-    if (split32 && (e = launch_split_bwd_accy(c, a.CB, static_cast<const float*>(a.y_grad), a.cum, a.accY)))
+  } else if (split32) {
+    if ((e = launch_split_bwd_accy(c, a.CB, static_cast<const float*>(a.y_grad), a.cum, a.accY)) ||
+        (e = launch_split_bwd_g(c, static_cast<const float*>(a.u), static_cast<const float*>(a.y_grad), a.Gyu)))
       return e;
+    bwd_intra_split_kernel<<<gkh, 256, 0, c.stream>>>(
+        static_cast<const float*>(a.u), a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, a.accY,
+        a.Gyu, a.dl_part, nsl, a.CBg, static_cast<float*>(a.u_grad), a.delta_raw_grad, a.A_part, a.bias_part, c.cm,
+        H, G, a.dt_dtype, c.use_sp, c.dmin, c.dmax);
+  } else {
     bwd_intra_kernel<<<gkh, kIT, kSmemIntra, c.stream>>>(
-        a.u, a.y_grad, a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, split32 ? a.accY : nullptr,
-        a.dl_part, nsl, a.CBg,
+        a.u, a.y_grad, a.delta_raw, a.A, a.delta_bias, a.dt, a.cum, a.CB, a.accS, a.gC, a.dl_part, nsl,
+        a.CBg,
         a.u_grad, a.delta_raw_grad, a.A_part, a.bias_part, c.cm, H, G, P, a.x_dtype, a.y_dtype, a.dt_dtype,
         c.use_sp, c.dmin, c.dmax);
   }

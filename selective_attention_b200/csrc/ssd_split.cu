@@ -796,8 +796,8 @@ __global__ void __launch_bounds__(kSplitThreads, SgCfg<MODE>::kMinBlocks) split_
 // ---------------------------------------------------------------------------- backward accY
 // The backward's intra-chunk product for fp32 inputs (backward_kernel.py:272-293),
 //   accY[l,p] = sum_{l <= s < length} CB[s,l] exp(min(cum_s - cum_l, 0)) y_grad[s,p],
-// per (half m: rows l in [128 m, 128 m + 128), head, chunk), 256 threads; the CUDA-core intra
-// kernel then takes it in place of its own accY. Steps of 64 source tokens s >= 128 m: A = the
+// per (half m: rows l in [128 m, 128 m + 128), head, chunk), 256 threads, for the fp32 intra
+// kernel (ssd_bwd.cu bwd_intra_split). Steps of 64 source tokens s >= 128 m: A = the
 // decay-weighted CB transposed, [l][s], staged MN-major from CB's rows s (l contiguous: two
 // 64-wide l blocks 8 KB apart), B operand = the y_grad rows s (MN-major); both split by every
 // thread from fp32 loads issued one step ahead; two stages alternate.
@@ -922,6 +922,93 @@ __global__ void __launch_bounds__(kSplitThreads, 2) split_bwd_accy_kernel(
   if (warp == 0) tmem_dealloc(tmem, 64);
 }
 
+// ---------------------------------------------------------------------------- backward G
+// G[l,s] = sum_p y_grad[l,p] u[s,p] for fp32 inputs (the product behind CB_grad,
+// backward_kernel.py:632-659), per (128 x 128 block of the lower block triangle, head, chunk):
+// y_grad rows (A) and u rows (B operand), both K-major, split; G leaves as fp32 rows for the
+// fp32 intra kernel (ssd_bwd.cu bwd_intra_split), which applies the decay, the atomics and
+// the decay sums.
+constexpr size_t kBgSmem = 1024 + 2 * 32768;  // y rows hi | lo, u rows hi | lo
+
+__global__ void __launch_bounds__(kSplitThreads, 3) split_bwd_g_kernel(const float* __restrict__ u,
+                                                                      const float* __restrict__ yg,
+                                                                      float* __restrict__ Gout, ChunkMap cm, int H) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = align1024_shared(smem_raw);
+  __shared__ uint64_t bars[1];
+  __shared__ uint32_t tslot[1];
+  const int t = blockIdx.x, h = blockIdx.y, k = blockIdx.z;
+  const int lb = t > 0 ? 1 : 0, sb = t > 1 ? 1 : 0;  // (0, 0), (1, 0), (1, 1)
+  ChunkInfo ci;
+  if (!chunk_info(cm, k, ci)) return;
+  const int lim = ci.lim;
+  if (128 * lb >= lim) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long kh = (long long)k * H + h;
+  uint8_t* yH = sm;
+  uint8_t* yL = sm + 16384;
+  uint8_t* uH = sm + 32768;
+  uint8_t* uL = sm + 49152;
+  const uint32_t bar = smem_u32(&bars[0]);
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(smem_u32(tslot), 128);
+  float v[4][8];
+#pragma unroll 1
+  for (int which = 0; which < 2; ++which) {  // y_grad rows of block lb, u rows of block sb: 128 x 8 chunks
+    const float* src = which ? u : yg;
+    const int r0 = 128 * (which ? sb : lb);
+    uint8_t* dh = which ? uH : yH;
+    uint8_t* dl = which ? uL : yL;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+      load8(src + ((ci.tok0 + min(r0 + r, lim - 1)) * H + h) * 64 + 8 * c8, v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int q = tid + kSplitThreads * i, r = q >> 3, c8 = q & 7;
+      store_split8(dh, dl, sw128_off((uint32_t)r, (uint32_t)c8), v[i]);
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  if (tid == 0) {
+    constexpr uint32_t ID = idesc_f16(128, 128, true, false, false);
+    const uint32_t yh = smem_u32(yH), yl = smem_u32(yL), uh = smem_u32(uH), ul = smem_u32(uL);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+      mma3(tmem, sdesc_sw128(yh + ks * 32, 16, 1024), sdesc_sw128(yl + ks * 32, 16, 1024),
+           sdesc_sw128(uh + ks * 32, 16, 1024), sdesc_sw128(ul + ks * 32, 16, 1024), ID, ks > 0 ? 1u : 0u);
+    umma_commit(bar);
+  }
+  const bool done = mbar_wait(bar, 0u, kSiteSplitState);
+  tc_fence_after();
+  if (__syncthreads_and(done)) {
+    const int r = (warp & 3) * 32 + lane, c0 = 64 * (warp >> 2);
+    float* out = Gout + (kh * 256 + 128 * lb + r) * 256 + 128 * sb + c0;
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      uint32_t a[32];
+      tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(c0 + 32 * hf), a);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        reinterpret_cast<float4*>(out + 32 * hf)[j] = make_float4(
+            __uint_as_float(a[4 * j]), __uint_as_float(a[4 * j + 1]), __uint_as_float(a[4 * j + 2]),
+            __uint_as_float(a[4 * j + 3]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -999,6 +1086,15 @@ cudaError_t launch_split_bwd_accy(const LaunchCtx& c, const float* CB, const flo
   if (e != cudaSuccess) return e;
   split_bwd_accy_kernel<<<dim3(2u, (unsigned)c.H, (unsigned)c.nchunks_max), kSplitThreads, kAySmem, c.stream>>>(
       CB, y_grad, cum, accY, c.cm, c.H, c.G);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_bwd_g(const LaunchCtx& c, const float* u, const float* y_grad, float* G) {
+  cudaError_t e =
+      cudaFuncSetAttribute(split_bwd_g_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBgSmem);
+  if (e != cudaSuccess) return e;
+  split_bwd_g_kernel<<<dim3(3u, (unsigned)c.H, (unsigned)c.nchunks_max), kSplitThreads, kBgSmem, c.stream>>>(
+      u, y_grad, G, c.cm, c.H);
   return cudaGetLastError();
 }
 
