@@ -501,7 +501,8 @@ def c2_measure(args, dev, flush, hbm_peak, peak_src):
 def fp32_measure(args, dev, flush, hbm_peak, peak_src):
     """Config c1's shape in fp32 (the reference's own precision: its SSD takes fp32
     operands only) on one GPU: fp32 u, B, C, z in and y out, on the default fp32 chain
-    (tensor cores with split-bf16 products; ``--kernel-impl simt`` does not change it)."""
+    (tensor cores with split-bf16 products; ``--kernel-impl simt`` does not change it), and
+    the backward on the same inputs unless ``--no-bwd``."""
     from selective_attention_b200 import workloads
 
     cfg = workloads.SSDConfig(**{**workloads.CONFIGS["c1"].__dict__, "dtype": "f32"})
@@ -515,7 +516,11 @@ def fp32_measure(args, dev, flush, hbm_peak, peak_src):
     simt = measure_ssd(run, args, 1, flush, hbm_peak, peak_src, cfg.tokens, 5)
     res["cuda_core_chain"] = {"ms_per_step": simt["ms_per_step"], "value": simt["value"], "path": simt["path"],
                               "stages_us": {k: v["us"] for k, v in simt["stages"].items()}}
-    del run, inp
+    del run
+    if not args.no_bwd:
+        # the backward on the same fp32 inputs (split-bf16 tcgen05 products, CUDA-core rest)
+        res["bwd"] = bwd_measure(args, cfg, inp, dev, flush)
+    del inp
     torch.cuda.empty_cache()
     return res
 
@@ -711,8 +716,9 @@ def bwd_measure(args, cfg, inp, dev, flush):
     y dtype) and h_last_grad, through ``kernels.ssd_scan_backward`` (the C-ABI
     ``ssd_scan_bwd``). For 16-bit u / B / C at headdim 64, dstate 128, chunk 256 (the bench
     workload) the contractions run on tcgen05 with 16-bit operands; reported in TFLOP/s of
-    the algorithmic FLOPs, with the per-stage split from the C-ABI's events. The FFMA
-    fraction is kept for comparison with the CUDA-core path."""
+    the algorithmic FLOPs, with the per-stage split from the C-ABI's events; fp32 u / B / C
+    at that shape run them on tcgen05 with split-bf16 products. The FFMA fraction is kept for
+    comparison with the CUDA-core path."""
     from selective_attention_b200 import kernels
 
     u, A, B, C, dr = inp["u"], inp["A"], inp["B"], inp["C"], inp["delta_raw"]

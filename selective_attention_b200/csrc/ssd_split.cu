@@ -990,18 +990,29 @@ __global__ void __launch_bounds__(kSplitThreads, 3) split_bwd_g_kernel(const flo
   const bool done = mbar_wait(bar, 0u, kSiteSplitState);
   tc_fence_after();
   if (__syncthreads_and(done)) {
+    // the tile goes through shared memory (the operands are consumed): [128 rows][32 float4],
+    // float4 index ^ (row & 7) so that both the row-per-thread writes and the row-per-warp
+    // reads are free of bank conflicts; then each warp stores whole 512-byte rows
     const int r = (warp & 3) * 32 + lane, c0 = 64 * (warp >> 2);
-    float* out = Gout + (kh * 256 + 128 * lb + r) * 256 + 128 * sb + c0;
+    float4* st = reinterpret_cast<float4*>(sm);
 #pragma unroll
     for (int hf = 0; hf < 2; ++hf) {
       uint32_t a[32];
       tmem_ld32(tmem + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(c0 + 32 * hf), a);
       tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        reinterpret_cast<float4*>(out + 32 * hf)[j] = make_float4(
-            __uint_as_float(a[4 * j]), __uint_as_float(a[4 * j + 1]), __uint_as_float(a[4 * j + 2]),
-            __uint_as_float(a[4 * j + 3]));
+      for (int j = 0; j < 8; ++j) {
+        const int c4 = (c0 >> 2) + 8 * hf + j;
+        st[r * 32 + (c4 ^ (r & 7))] = make_float4(__uint_as_float(a[4 * j]), __uint_as_float(a[4 * j + 1]),
+                                                  __uint_as_float(a[4 * j + 2]), __uint_as_float(a[4 * j + 3]));
+      }
+    }
+    __syncthreads();
+    float* out = Gout + (kh * 256 + 128 * lb) * 256 + 128 * sb;
+#pragma unroll 4
+    for (int it = 0; it < 16; ++it) {
+      const int row = 8 * it + warp;
+      reinterpret_cast<float4*>(out + (long long)row * 256)[lane] = st[row * 32 + (lane ^ (row & 7))];
     }
   }
   tc_fence_before();
