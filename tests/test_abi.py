@@ -132,6 +132,13 @@ def test_entry_points_reject_bad_arguments_without_launching():
     assert L.ssd_scan_bwd(ctypes.byref(p), ctypes.byref(g), None) == _lib.SSD_ERR_INVALID_ARGUMENT
     assert L.ssd_scan_bwd_workspace_size(ctypes.byref(_params(headdim=128))) == 0  # outside the backward's shapes
     assert L.ssd_scan_bwd_workspace_size(ctypes.byref(_params())) > 0
+    # fp32 u / B / C at headdim 64, dstate 128, chunk 256 add the split path's backward
+    # buffers: B and C operand tiles (four 32 KB tiles per chunk and group each), accY
+    # (chunk, head, 256, 64) and G = y_grad u^T (chunk, head, 256, 256), all fp32
+    nk, H = 8 * 8, 24
+    extra = 2 * nk * 4 * 32768 + nk * H * 256 * 64 * 4 + nk * H * 256 * 256 * 4
+    assert L.ssd_scan_bwd_workspace_size(ctypes.byref(_params(x_dtype=0, y_dtype=0))) == \
+        L.ssd_scan_bwd_workspace_size(ctypes.byref(_params())) + extra
     assert L.sattn_decode_step(*([None] * 7), 0, 16, None, 1, 1, 64, 0.125, 0, None) == _lib.SSD_ERR_INVALID_ARGUMENT
     assert L.sattn_prefill_fwd(*([None] * 5), 1, 1, 16, 64, 0.125, 0, 0, None) == _lib.SSD_ERR_INVALID_ARGUMENT
     for s in range(7):
