@@ -83,6 +83,18 @@ def test_golden_equals_autograd_of_the_forward():
         assert_fp32_close(leaves[k].grad, g[k + "_grad"], f"autograd {k}")
 
 
+@pytest.mark.parametrize("case", BWD_CASES)
+def test_golden_bias_grad_is_the_token_sum_of_raw_grad(case):
+    """The bias enters as raw + bias, so the reference's delta_bias_grad is the sum over tokens
+    of its delta_raw_grad: the identity the fp32 bias-gradient tolerance rests on."""
+    g = load_golden(case)
+    db = g.get("delta_bias_grad")
+    if db is None:
+        pytest.skip("no delta_bias in this case")
+    dr = g["delta_raw_grad"].double().reshape(-1, db.numel())
+    assert ((dr.sum(0) - db.double()).abs() <= 1e-6 * dr.abs().sum(0) + 1e-12).all()
+
+
 def test_oracle_ignores_y_grad_past_length():
     """The reference masks every backward stage at ``length``: y_grad there changes nothing."""
     g = load_golden("ssd_bwd_ragged_fp32")
